@@ -1,0 +1,321 @@
+"""Python binding of libmoe_b200.so -- the B200 MoE FFN layer.
+
+A thin ctypes view of the C ABI declared in ``include/moe_b200.h``; every
+call goes to the CUDA kernels in that library.  There is no CPU fallback:
+importing this module without the built library raises, and so does using a
+layer on a machine without a B200.
+
+Also holds the host-side data formats either side of the layer: synthetic
+layer weights (seeded), and the ``model.bin`` format of the reference's
+ModelLoader (src/model_loader.cu:14-50) for tensors named as PhiMoE loads
+them (src/layer.cu:73-77).
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Optional, Sequence
+
+import numpy as np
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libmoe_b200.so"
+
+MOE_OK = 0
+STATUS_NAMES = {0: "MOE_OK", -1: "MOE_ERR_INVALID", -2: "MOE_ERR_UNSUPPORTED", -3: "MOE_ERR_CUDA",
+                -4: "MOE_ERR_OOM", -5: "MOE_ERR_IO", -6: "MOE_ERR_TIMEOUT", -7: "MOE_ERR_NCCL"}
+ROUTER_PHI_QUANTISED = 0
+ROUTER_SOFTMAX_TOPK = 1
+PREC_FP32 = 0
+PREC_BF16 = 1
+
+# Every symbol include/moe_b200.h declares.
+EXPORTED_SYMBOLS = (
+    "moe_abi_version", "moe_last_error", "moe_config_init", "moe_create",
+    "moe_create_from_model_bin", "moe_destroy", "moe_get_config", "moe_device_bytes",
+    "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
+    "moe_expert_counts", "moe_dispatch_layout",
+)
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class MoeConfig(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_int32), ("d_ff", ctypes.c_int32),
+                ("num_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("router_policy", ctypes.c_int32), ("precision", ctypes.c_int32),
+                ("router_quantum", ctypes.c_float), ("router_tie_eps", ctypes.c_float),
+                ("decode_max_tokens", ctypes.c_int32), ("device", ctypes.c_int32),
+                ("max_tokens", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5)]
+
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+class MoeWeightsHost(ctypes.Structure):
+    _fields_ = [("router_weight", _f32p), ("router_bias", _f32p),
+                ("w1", ctypes.POINTER(_f32p)), ("w3", ctypes.POINTER(_f32p)),
+                ("w2", ctypes.POINTER(_f32p))]
+
+
+_lib = None
+
+
+def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
+    """Load libmoe_b200.so; raises if it has not been built."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(f"{p} is not built; run accelerating-moe-inference_b200/build.py")
+    L = ctypes.CDLL(str(p))
+    vp = ctypes.c_void_p
+    L.moe_abi_version.restype = ctypes.c_int
+    L.moe_last_error.restype = ctypes.c_char_p
+    L.moe_config_init.argtypes = [ctypes.POINTER(MoeConfig)]
+    L.moe_create.argtypes = [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeightsHost),
+                             ctypes.POINTER(vp)]
+    L.moe_create_from_model_bin.argtypes = [ctypes.POINTER(MoeConfig), ctypes.c_char_p,
+                                            ctypes.c_int, ctypes.POINTER(vp)]
+    L.moe_destroy.argtypes = [vp]
+    L.moe_get_config.argtypes = [vp, ctypes.POINTER(MoeConfig)]
+    L.moe_device_bytes.argtypes = [vp]
+    L.moe_device_bytes.restype = ctypes.c_size_t
+    L.moe_set_decode_max_tokens.argtypes = [vp, ctypes.c_int32]
+    L.moe_forward_device.argtypes = [vp, vp, vp, ctypes.c_int32, vp]
+    L.moe_forward_host.argtypes = [vp, _f32p, _f32p, ctypes.c_int32]
+    L.moe_route_device.argtypes = [vp, vp, ctypes.c_int32, vp, vp, vp, vp]
+    L.moe_expert_counts.argtypes = [vp, _i32p]
+    L.moe_dispatch_layout.argtypes = [vp, _i32p, _f32p, ctypes.c_int32, _i32p, _i32p]
+    if path is None:
+        _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != MOE_OK:
+        raise MoeError(rc, load_library().moe_last_error().decode())
+
+
+def default_config(**kw) -> MoeConfig:
+    cfg = MoeConfig()
+    load_library().moe_config_init(ctypes.byref(cfg))
+    for k, v in kw.items():
+        if not hasattr(cfg, k):
+            raise TypeError(f"unknown MoeConfig field {k}")
+        setattr(cfg, k, v)
+    return cfg
+
+
+# ------------------------------------------------------------------ weights
+@dataclass
+class LayerWeights:
+    """One MoE layer's fp32 weights in nn.Linear layout (src/layer.cu:28-30)."""
+    wg: np.ndarray                      # [E][d]
+    w1: list                            # E x [ff][d]   gate
+    w3: list                            # E x [ff][d]   up
+    w2: list                            # E x [d][ff]   down
+    router_bias: Optional[np.ndarray] = None  # [E]
+
+    @property
+    def E(self) -> int:
+        return self.wg.shape[0]
+
+    @property
+    def d(self) -> int:
+        return self.wg.shape[1]
+
+    @property
+    def ff(self) -> int:
+        return self.w1[0].shape[0]
+
+
+def synthetic_layer(seed: int, d: int, ff: int, E: int, std: float = 0.02,
+                    router_std: Optional[float] = None,
+                    router_bias: Optional[np.ndarray] = None) -> LayerWeights:
+    """Seeded N(0, std) weights (numpy PCG64), drawn in a fixed order:
+    router, then per expert w1, w3, w2."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    rs = std if router_std is None else router_std
+
+    def normal(shape, s):
+        return (g.standard_normal(shape, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+    wg = normal((E, d), rs)
+    w1, w3, w2 = [], [], []
+    for _ in range(E):
+        w1.append(normal((ff, d), std))
+        w3.append(normal((ff, d), std))
+        w2.append(normal((d, ff), std))
+    bias = None if router_bias is None else np.ascontiguousarray(router_bias, np.float32)
+    return LayerWeights(wg, w1, w3, w2, bias)
+
+
+def synthetic_tokens(seed: int, T: int, d: int) -> np.ndarray:
+    """Seeded N(0, 1) activations [T][d] (numpy PCG64, stream offset by 0x5eed)."""
+    g = np.random.Generator(np.random.PCG64([seed, 0x5EED]))
+    return g.standard_normal((T, d), dtype=np.float32)
+
+
+def zipf_router_bias(E: int) -> np.ndarray:
+    """Per-expert router bias 0.5 * ln(1 / rank), rank = 1..E (Zipf-like skew)."""
+    r = np.arange(1, E + 1, dtype=np.float64)
+    return (0.5 * np.log(1.0 / r)).astype(np.float32)
+
+
+def write_model_bin(path, layers: Sequence[LayerWeights]) -> None:
+    """Write layers in the ModelLoader format (src/model_loader.cu:14-30):
+    u32 count; per entry u32 name_len, name, u32 ndim, u32 dims[ndim],
+    u64 offset, u64 bytes; then the fp32 payloads."""
+    entries = []
+    for li, L in enumerate(layers):
+        base = f"model.layers.{li}.block_sparse_moe"
+        entries.append((f"{base}.gate.weight", L.wg))
+        if L.router_bias is not None:
+            entries.append((f"{base}.gate.bias", L.router_bias))
+        for e in range(L.E):
+            entries.append((f"{base}.experts.{e}.w1.weight", L.w1[e]))
+            entries.append((f"{base}.experts.{e}.w2.weight", L.w2[e]))
+            entries.append((f"{base}.experts.{e}.w3.weight", L.w3[e]))
+    header = bytearray(struct.pack("<I", len(entries)))
+    # First pass: header size, so payload offsets are known.
+    metas = []
+    for name, arr in entries:
+        nb = name.encode()
+        metas.append((nb, arr.shape, arr.nbytes))
+    hsize = 4 + sum(4 + len(nb) + 4 + 4 * len(sh) + 16 for nb, sh, _ in metas)
+    off = hsize
+    for (nb, sh, nbytes) in metas:
+        header += struct.pack("<I", len(nb)) + nb + struct.pack("<I", len(sh))
+        header += struct.pack(f"<{len(sh)}I", *sh)
+        header += struct.pack("<QQ", off, nbytes)
+        off += nbytes
+    assert len(header) == hsize
+    with open(path, "wb") as f:
+        f.write(header)
+        for _, arr in entries:
+            f.write(np.ascontiguousarray(arr, np.float32).tobytes())
+
+
+# ------------------------------------------------------------------ layer
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(_f32p)
+
+
+class MoeLayer:
+    """Owns one MoeHandle.  Weights are uploaded once at construction."""
+
+    def __init__(self, weights: Optional[LayerWeights] = None, *, top_k: int = 2,
+                 policy: int = ROUTER_SOFTMAX_TOPK, precision: int = PREC_FP32, device: int = 0,
+                 max_tokens: int = 0, decode_max_tokens: Optional[int] = None,
+                 model_bin: Optional[str] = None, layer_idx: int = 0, **cfg_kw):
+        L = load_library()
+        cfg = default_config(top_k=top_k, router_policy=policy, precision=precision,
+                             device=device, max_tokens=max_tokens, **cfg_kw)
+        if decode_max_tokens is not None:
+            cfg.decode_max_tokens = decode_max_tokens
+        h = ctypes.c_void_p()
+        if model_bin is not None:
+            cfg.d_model = cfg_kw.get("d_model", 0)
+            cfg.d_ff = cfg_kw.get("d_ff", 0)
+            cfg.num_experts = cfg_kw.get("num_experts", 0)
+            _check(L.moe_create_from_model_bin(ctypes.byref(cfg), str(model_bin).encode(),
+                                               layer_idx, ctypes.byref(h)))
+        else:
+            w = weights
+            cfg.d_model, cfg.d_ff, cfg.num_experts = w.d, w.ff, w.E
+            keep = [np.ascontiguousarray(a, np.float32) for a in (w.wg, *w.w1, *w.w3, *w.w2)]
+            E = w.E
+            wg, w1, w3, w2 = keep[0], keep[1:1 + E], keep[1 + E:1 + 2 * E], keep[1 + 2 * E:]
+            P = _f32p * E
+            pw1, pw3, pw2 = P(*map(_fp, w1)), P(*map(_fp, w3)), P(*map(_fp, w2))
+            bias = None
+            if w.router_bias is not None:
+                bias = np.ascontiguousarray(w.router_bias, np.float32)
+            hw = MoeWeightsHost(_fp(wg), None if bias is None else _fp(bias), pw1, pw3, pw2)
+            _check(L.moe_create(ctypes.byref(cfg), ctypes.byref(hw), ctypes.byref(h)))
+        self._h = h
+        self.cfg = MoeConfig()
+        _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
+
+    # -- properties
+    @property
+    def d(self):
+        return self.cfg.d_model
+
+    @property
+    def E(self):
+        return self.cfg.num_experts
+
+    @property
+    def k(self):
+        return self.cfg.top_k
+
+    def device_bytes(self) -> int:
+        return load_library().moe_device_bytes(self._h)
+
+    def set_decode_max_tokens(self, n: int):
+        _check(load_library().moe_set_decode_max_tokens(self._h, n))
+
+    # -- compute
+    def forward_host(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        T, d = x.shape
+        if d != self.d:
+            raise ValueError(f"x has {d} columns, layer expects {self.d}")
+        y = np.empty_like(x)
+        _check(load_library().moe_forward_host(self._h, _fp(x), _fp(y), T))
+        return y
+
+    def forward_device(self, x_ptr: int, y_ptr: int, T: int, stream: int = 0):
+        _check(load_library().moe_forward_device(self._h, ctypes.c_void_p(x_ptr),
+                                                 ctypes.c_void_p(y_ptr), T,
+                                                 ctypes.c_void_p(stream)))
+
+    def route_device(self, x_ptr: int, T: int, logits_ptr: int, idx_ptr: int, w_ptr: int,
+                     stream: int = 0):
+        _check(load_library().moe_route_device(self._h, ctypes.c_void_p(x_ptr), T,
+                                               ctypes.c_void_p(logits_ptr),
+                                               ctypes.c_void_p(idx_ptr), ctypes.c_void_p(w_ptr),
+                                               ctypes.c_void_p(stream)))
+
+    def expert_counts(self) -> np.ndarray:
+        c = np.zeros(self.E, np.int32)
+        _check(load_library().moe_expert_counts(self._h, c.ctypes.data_as(_i32p)))
+        return c
+
+    def dispatch_layout(self, rows_cap: int):
+        tok = np.zeros(rows_cap, np.int32)
+        wt = np.zeros(rows_cap, np.float32)
+        rows = ctypes.c_int32()
+        eoff = np.zeros(self.E + 1, np.int32)
+        _check(load_library().moe_dispatch_layout(self._h, tok.ctypes.data_as(_i32p), _fp(wt),
+                                                  rows_cap, ctypes.byref(rows),
+                                                  eoff.ctypes.data_as(_i32p)))
+        n = rows.value
+        return tok[:n], wt[:n], eoff
+
+    def close(self):
+        if self._h:
+            load_library().moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()

@@ -1,0 +1,580 @@
+// C ABI of libmoe_b200.so (declared in include/moe_b200.h): layer handles,
+// weight upload, workspace management and the forward orchestration.
+//
+// forward on device buffers, all on the caller's stream, no host sync:
+//   router_kernel -> dispatch_scan -> dispatch_permute -> memset(y)
+//   -> gate/up grouped GEMM (SwiGLU epilogue) -> down grouped GEMM (combine
+//   epilogue)
+// or, for T <= decode_max_tokens, router -> scan -> the weight-streaming
+// decode kernels.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "moe_internal.h"
+
+namespace moe {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define MOE_CUDA(call)                                            \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);       \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+bool load_encode(std::string* err) {
+    if (g_encode) return true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        *err = "cuTensorMapEncodeTiled is not available from the driver";
+        return false;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return true;
+}
+
+void free_ptr(void* p) {
+    if (p) cudaFree(p);
+}
+
+template <typename T>
+cudaError_t dalloc(T** p, size_t bytes, size_t* counter) {
+    *p = nullptr;
+    if (bytes == 0) bytes = 256;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes);
+    if (e == cudaSuccess && counter) *counter += bytes;
+    return e;
+}
+
+void free_workspace(Workspace& W) {
+    free_ptr(W.logits); free_ptr(W.idx); free_ptr(W.wts); free_ptr(W.blockhist);
+    free_ptr(W.counts); free_ptr(W.eoff); free_ptr(W.mtiles); free_ptr(W.num_mtiles);
+    free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.a_hi); free_ptr(W.a_lo);
+    free_ptr(W.h_hi); free_ptr(W.h_lo); free_ptr(W.x_stage); free_ptr(W.y_stage);
+    free_ptr(W.dev_err);
+    W = Workspace{};
+}
+
+int ensure_workspace(Layer& L, int T) {
+    Workspace& W = L.ws;
+    if (T <= W.cap_T && W.dev_err) return MOE_OK;
+    // Grow-only.  Work queued on the previous buffers must finish first.
+    if (W.dev_err) MOE_CUDA(cudaDeviceSynchronize());
+    const int capT = std::max({T, W.cap_T + W.cap_T / 2, 64});
+    free_workspace(W);
+    const size_t k = L.k, E = L.E;
+    const int nblk = (capT + kRouteTokens - 1) / kRouteTokens;
+    const int cap_mtiles = (int)((size_t)capT * k / kTileM) + L.E + 1;
+    const size_t cap_rows = (size_t)cap_mtiles * kTileM;
+    const size_t eb = elem_bytes(L);
+    const bool tf = three_pass(L);
+    size_t bytes = 0;
+    MOE_CUDA(dalloc(&W.logits, sizeof(float) * capT * E, &bytes));
+    MOE_CUDA(dalloc(&W.idx, sizeof(int) * capT * k, &bytes));
+    MOE_CUDA(dalloc(&W.wts, sizeof(float) * capT * k, &bytes));
+    MOE_CUDA(dalloc(&W.blockhist, sizeof(int) * nblk * E, &bytes));
+    MOE_CUDA(dalloc(&W.counts, sizeof(int) * E, &bytes));
+    MOE_CUDA(dalloc(&W.eoff, sizeof(int) * (E + 1), &bytes));
+    MOE_CUDA(dalloc(&W.mtiles, sizeof(MTile) * cap_mtiles, &bytes));
+    MOE_CUDA(dalloc(&W.num_mtiles, sizeof(int), &bytes));
+    MOE_CUDA(dalloc(&W.row_token, sizeof(int) * cap_rows, &bytes));
+    MOE_CUDA(dalloc(&W.row_weight, sizeof(float) * cap_rows, &bytes));
+    MOE_CUDA(dalloc(&W.a_hi, eb * cap_rows * L.d, &bytes));
+    MOE_CUDA(dalloc(&W.h_hi, eb * cap_rows * L.ffp, &bytes));
+    if (tf) {
+        MOE_CUDA(dalloc(&W.a_lo, 4 * cap_rows * L.d, &bytes));
+        MOE_CUDA(dalloc(&W.h_lo, 4 * cap_rows * L.ffp, &bytes));
+    }
+    MOE_CUDA(dalloc(&W.dev_err, sizeof(int), &bytes));
+    MOE_CUDA(cudaMemset(W.dev_err, 0, sizeof(int)));
+    MOE_CUDA(cudaMemset(W.num_mtiles, 0, sizeof(int)));
+    W.cap_T = capT;
+    W.cap_rows = (int)cap_rows;
+    W.cap_mtiles = cap_mtiles;
+    W.bytes = bytes;
+    const bool bf = !tf;
+    const uint32_t box_k = tf ? 32 : 64;
+    std::string err;
+    if (!make_tmap_2d(&W.tm_a_hi, W.a_hi, bf, L.d, cap_rows, box_k, kTileM, &err) ||
+        !make_tmap_2d(&W.tm_h_hi, W.h_hi, bf, L.ffp, cap_rows, box_k, kTileM, &err))
+        return fail(MOE_ERR_CUDA, err);
+    if (tf) {
+        if (!make_tmap_2d(&W.tm_a_lo, W.a_lo, false, L.d, cap_rows, box_k, kTileM, &err) ||
+            !make_tmap_2d(&W.tm_h_lo, W.h_lo, false, L.ffp, cap_rows, box_k, kTileM, &err))
+            return fail(MOE_ERR_CUDA, err);
+    } else {
+        W.tm_a_lo = W.tm_a_hi;
+        W.tm_h_lo = W.tm_h_hi;
+    }
+    return MOE_OK;
+}
+
+int ensure_stage(Layer& L, int T) {
+    int rc = ensure_workspace(L, T);
+    if (rc) return rc;
+    Workspace& W = L.ws;
+    if (!W.x_stage) {
+        MOE_CUDA(dalloc(&W.x_stage, sizeof(float) * (size_t)W.cap_T * L.d, &W.bytes));
+        MOE_CUDA(dalloc(&W.y_stage, sizeof(float) * (size_t)W.cap_T * L.d, &W.bytes));
+    }
+    return MOE_OK;
+}
+
+int validate_config(const MoeConfig& c) {
+    if (c.d_model <= 0 || c.d_model % 64 != 0)
+        return fail(MOE_ERR_UNSUPPORTED, "d_model must be a positive multiple of 64");
+    if (c.d_ff <= 0) return fail(MOE_ERR_INVALID, "d_ff must be positive");
+    if (c.num_experts < 1 || c.num_experts > kMaxExperts)
+        return fail(MOE_ERR_UNSUPPORTED, "num_experts must be in 1..256");
+    if (c.top_k < 1 || c.top_k > kMaxTopK || c.top_k > c.num_experts)
+        return fail(MOE_ERR_INVALID, "top_k must be in 1..min(8, num_experts)");
+    if (c.router_policy != MOE_ROUTER_PHI_QUANTISED && c.router_policy != MOE_ROUTER_SOFTMAX_TOPK)
+        return fail(MOE_ERR_INVALID, "unknown router_policy");
+    if (c.router_policy == MOE_ROUTER_PHI_QUANTISED && (c.top_k != 2 || c.num_experts < 2))
+        return fail(MOE_ERR_INVALID, "the PHI_QUANTISED router selects exactly 2 experts");
+    if (c.router_policy == MOE_ROUTER_PHI_QUANTISED && !(c.router_quantum > 0.0f))
+        return fail(MOE_ERR_INVALID, "router_quantum must be positive");
+    if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16)
+        return fail(MOE_ERR_INVALID, "unknown precision");
+    if (c.decode_max_tokens < 0) return fail(MOE_ERR_INVALID, "decode_max_tokens < 0");
+    if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
+    return MOE_OK;
+}
+
+int check_device_errors(Layer& L) {
+    int flag = 0;
+    if (!L.ws.dev_err) return MOE_OK;
+    MOE_CUDA(cudaMemcpy(&flag, L.ws.dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        cudaMemset(L.ws.dev_err, 0, sizeof(int));
+        char buf[128];
+        std::snprintf(buf, sizeof buf, "a device-side wait timed out (flags 0x%x)", flag);
+        return fail(MOE_ERR_TIMEOUT, buf);
+    }
+    return MOE_OK;
+}
+
+int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+    int rc = ensure_workspace(L, T);
+    if (rc) return rc;
+    Workspace& W = L.ws;
+    L.last_stream = s;
+    L.last_T = T;
+    MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s));
+    MOE_CUDA(launch_dispatch_scan(L, T, s));
+    if (T <= L.cfg.decode_max_tokens) {
+        MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
+        MOE_CUDA(launch_decode(L, x, T, y, s));
+        return MOE_OK;
+    }
+    MOE_CUDA(launch_dispatch_permute(L, x, T, s));
+    MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
+    MOE_CUDA(launch_expert_gemms(L, T, y, s));
+    return MOE_OK;
+}
+
+// ------------------------------------------------------------ model.bin
+struct BinEntry {
+    std::vector<uint64_t> shape;
+    uint64_t offset = 0, bytes = 0;
+};
+
+// The index format of ModelLoader (src/model_loader.cu:14-30): u32 count; per
+// entry u32 name_len, name bytes, u32 ndim, u32 dims[ndim], u64 offset,
+// u64 bytes; payloads are fp32.
+int read_index(const std::string& path, std::unordered_map<std::string, BinEntry>* out) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return fail(MOE_ERR_IO, "cannot open model: " + path);
+    auto rd32 = [&](uint32_t* v) { return bool(f.read(reinterpret_cast<char*>(v), 4)); };
+    auto rd64 = [&](uint64_t* v) { return bool(f.read(reinterpret_cast<char*>(v), 8)); };
+    uint32_t count = 0;
+    if (!rd32(&count)) return fail(MOE_ERR_IO, "truncated model.bin");
+    for (uint32_t i = 0; i < count; ++i) {
+        uint32_t nl = 0, nd = 0;
+        if (!rd32(&nl) || nl > (1u << 20)) return fail(MOE_ERR_IO, "truncated model.bin");
+        std::string name(nl, '\0');
+        if (!f.read(name.data(), nl) || !rd32(&nd) || nd > 8)
+            return fail(MOE_ERR_IO, "truncated model.bin");
+        BinEntry e;
+        e.shape.resize(nd);
+        for (uint32_t j = 0; j < nd; ++j) {
+            uint32_t v;
+            if (!rd32(&v)) return fail(MOE_ERR_IO, "truncated model.bin");
+            e.shape[j] = v;
+        }
+        if (!rd64(&e.offset) || !rd64(&e.bytes)) return fail(MOE_ERR_IO, "truncated model.bin");
+        (*out)[name] = std::move(e);
+    }
+    return MOE_OK;
+}
+
+int load_tensor(const std::string& path, const std::unordered_map<std::string, BinEntry>& idx,
+                const std::string& name, std::vector<float>* out, std::vector<uint64_t>* shape) {
+    auto it = idx.find(name);
+    if (it == idx.end()) return fail(MOE_ERR_IO, "missing tensor: " + name);
+    uint64_t n = 1;
+    for (uint64_t dd : it->second.shape) n *= dd;
+    if (it->second.bytes != n * sizeof(float))
+        return fail(MOE_ERR_IO, "tensor is not float32: " + name);
+    out->resize(n);
+    std::ifstream f(path, std::ios::binary);
+    if (!f) return fail(MOE_ERR_IO, "cannot reopen model: " + path);
+    f.seekg(static_cast<std::streamoff>(it->second.offset));
+    if (!f.read(reinterpret_cast<char*>(out->data()), static_cast<std::streamsize>(n * 4)))
+        return fail(MOE_ERR_IO, "truncated tensor: " + name);
+    if (shape) *shape = it->second.shape;
+    return MOE_OK;
+}
+
+}  // namespace
+
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
+                  uint32_t box_inner, uint32_t box_outer, std::string* err) {
+    if (!load_encode(err)) return false;
+    const size_t es = bf16 ? 2 : 4;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * es};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[160];
+        std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu map",
+                      (int)r, (unsigned long long)outer, (unsigned long long)inner);
+        *err = buf;
+        return false;
+    }
+    return true;
+}
+
+}  // namespace moe
+
+using moe::Layer;
+struct MoeHandle {
+    Layer L;
+    cudaStream_t own_stream = nullptr;
+};
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+const char* moe_last_error(void) { return moe::g_last_error.c_str(); }
+
+void moe_config_init(MoeConfig* c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->d_model = 4096;
+    c->d_ff = 448;
+    c->num_experts = 16;
+    c->top_k = 2;
+    c->router_policy = MOE_ROUTER_PHI_QUANTISED;
+    c->precision = MOE_PREC_FP32;
+    c->router_quantum = 1.0e-3f;
+    c->router_tie_eps = 2.0e-2f;
+    c->decode_max_tokens = 0;
+    c->device = 0;
+    c->max_tokens = 0;
+}
+
+int moe_create(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
+    using namespace moe;
+    if (!cfg || !w || !out) return fail(MOE_ERR_INVALID, "null argument");
+    *out = nullptr;
+    int rc = validate_config(*cfg);
+    if (rc) return rc;
+    if (!w->router_weight || !w->w1 || !w->w2 || !w->w3)
+        return fail(MOE_ERR_INVALID, "missing weight pointers");
+    for (int e = 0; e < cfg->num_experts; ++e)
+        if (!w->w1[e] || !w->w2[e] || !w->w3[e]) return fail(MOE_ERR_INVALID, "null expert weight");
+    int ndev = 0;
+    MOE_CUDA(cudaGetDeviceCount(&ndev));
+    if (cfg->device < 0 || cfg->device >= ndev) return fail(MOE_ERR_INVALID, "no such device");
+    DeviceGuard guard(cfg->device);
+    int major = 0, minor = 0;
+    MOE_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, cfg->device));
+    MOE_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, cfg->device));
+    if (major != 10 || minor != 0)
+        return fail(MOE_ERR_UNSUPPORTED, "libmoe_b200 is built for sm_100a (B200) only");
+
+    std::unique_ptr<MoeHandle> h(new MoeHandle());
+    Layer& L = h->L;
+    L.cfg = *cfg;
+    L.d = cfg->d_model;
+    L.ff = cfg->d_ff;
+    L.ffp = (cfg->d_ff + kFfBlock - 1) / kFfBlock * kFfBlock;
+    L.E = cfg->num_experts;
+    L.k = cfg->top_k;
+    MOE_CUDA(cudaDeviceGetAttribute(&L.sm_count, cudaDevAttrMultiProcessorCount, cfg->device));
+    MOE_CUDA(cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking));
+    cudaStream_t s = h->own_stream;
+
+    const size_t d = L.d, E = L.E, ffp = L.ffp, ff = L.ff;
+    const bool tf = three_pass(L);
+    const size_t eb = elem_bytes(L);
+    size_t& wb = L.weight_bytes;
+    auto cleanup_and_fail = [&](int code) {
+        moe_destroy(h.release());
+        return code;
+    };
+#define MOE_CUDA_C(call)                                                 \
+    do {                                                                 \
+        cudaError_t e_ = (call);                                         \
+        if (e_ != cudaSuccess) return cleanup_and_fail(cuda_fail(e_, #call)); \
+    } while (0)
+    MOE_CUDA_C(dalloc(&L.wg, sizeof(float) * E * d, &wb));
+    MOE_CUDA_C(cudaMemcpy(L.wg, w->router_weight, sizeof(float) * E * d, cudaMemcpyHostToDevice));
+    if (w->router_bias) {
+        MOE_CUDA_C(dalloc(&L.bias, sizeof(float) * E, &wb));
+        MOE_CUDA_C(cudaMemcpy(L.bias, w->router_bias, sizeof(float) * E, cudaMemcpyHostToDevice));
+    }
+    MOE_CUDA_C(dalloc(&L.w13_hi, eb * E * 2 * ffp * d, &wb));
+    MOE_CUDA_C(dalloc(&L.w2_hi, eb * E * d * ffp, &wb));
+    if (tf) {
+        MOE_CUDA_C(dalloc(&L.w13_lo, 4 * E * 2 * ffp * d, &wb));
+        MOE_CUDA_C(dalloc(&L.w2_lo, 4 * E * d * ffp, &wb));
+        MOE_CUDA_C(dalloc(&L.w13_f32, 4 * E * 2 * ffp * d, &wb));
+        MOE_CUDA_C(dalloc(&L.w2_f32, 4 * E * d * ffp, &wb));
+    }
+    float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr;
+    MOE_CUDA_C(dalloc(&st1, sizeof(float) * ff * d, nullptr));
+    MOE_CUDA_C(dalloc(&st3, sizeof(float) * ff * d, nullptr));
+    MOE_CUDA_C(dalloc(&st2, sizeof(float) * ff * d, nullptr));
+    for (int e = 0; e < L.E; ++e) {
+        MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
+        MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
+        MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
+        MOE_CUDA_C(convert_gateup(L, e, st1, st3, s));
+        MOE_CUDA_C(convert_down(L, e, st2, s));
+        MOE_CUDA_C(cudaStreamSynchronize(s));
+    }
+    cudaFree(st1);
+    cudaFree(st3);
+    cudaFree(st2);
+    const uint32_t box_k = tf ? 32 : 64;
+    std::string err;
+    const bool bf = !tf;
+    if (!make_tmap_2d(&L.tm_w13_hi, L.w13_hi, bf, d, E * 2 * ffp, box_k, kTileN, &err) ||
+        !make_tmap_2d(&L.tm_w2_hi, L.w2_hi, bf, ffp, E * d, box_k, kTileN, &err))
+        return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
+    if (tf) {
+        if (!make_tmap_2d(&L.tm_w13_lo, L.w13_lo, false, d, E * 2 * ffp, box_k, kTileN, &err) ||
+            !make_tmap_2d(&L.tm_w2_lo, L.w2_lo, false, ffp, E * d, box_k, kTileN, &err))
+            return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
+    } else {
+        L.tm_w13_lo = L.tm_w13_hi;
+        L.tm_w2_lo = L.tm_w2_hi;
+    }
+    rc = ensure_workspace(L, std::max(cfg->max_tokens, 1));
+    if (rc) return cleanup_and_fail(rc);
+#undef MOE_CUDA_C
+    *out = h.release();
+    return MOE_OK;
+}
+
+int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int layer_idx,
+                              MoeHandle** out) {
+    using namespace moe;
+    if (!cfg_in || !path || !out) return fail(MOE_ERR_INVALID, "null argument");
+    std::unordered_map<std::string, BinEntry> index;
+    int rc = read_index(path, &index);
+    if (rc) return rc;
+    MoeConfig cfg = *cfg_in;
+    const std::string base = "model.layers." + std::to_string(layer_idx) + ".block_sparse_moe";
+    std::vector<float> gate;
+    std::vector<uint64_t> gshape;
+    rc = load_tensor(path, index, base + ".gate.weight", &gate, &gshape);
+    if (rc) return rc;
+    if (gshape.size() != 2) return fail(MOE_ERR_IO, "router weight is not 2-D");
+    if (cfg.num_experts == 0) cfg.num_experts = (int)gshape[0];
+    if (cfg.d_model == 0) cfg.d_model = (int)gshape[1];
+    if ((int)gshape[0] != cfg.num_experts || (int)gshape[1] != cfg.d_model)
+        return fail(MOE_ERR_INVALID, "router weight shape does not match the config");
+    std::vector<std::vector<float>> w1(cfg.num_experts), w2(cfg.num_experts), w3(cfg.num_experts);
+    for (int e = 0; e < cfg.num_experts; ++e) {
+        const std::string pre = base + ".experts." + std::to_string(e);
+        std::vector<uint64_t> s1, s2, s3;
+        if ((rc = load_tensor(path, index, pre + ".w1.weight", &w1[e], &s1)) ||
+            (rc = load_tensor(path, index, pre + ".w2.weight", &w2[e], &s2)) ||
+            (rc = load_tensor(path, index, pre + ".w3.weight", &w3[e], &s3)))
+            return rc;
+        if (s1.size() != 2 || s2.size() != 2 || s3.size() != 2)
+            return fail(MOE_ERR_IO, "expert weight is not 2-D");
+        if (cfg.d_ff == 0) cfg.d_ff = (int)s1[0];
+        if ((int)s1[0] != cfg.d_ff || (int)s1[1] != cfg.d_model || s3 != s1 ||
+            (int)s2[0] != cfg.d_model || (int)s2[1] != cfg.d_ff)
+            return fail(MOE_ERR_INVALID, "expert weight shapes do not match the config");
+    }
+    std::vector<const float*> p1(cfg.num_experts), p2(cfg.num_experts), p3(cfg.num_experts);
+    for (int e = 0; e < cfg.num_experts; ++e) {
+        p1[e] = w1[e].data();
+        p2[e] = w2[e].data();
+        p3[e] = w3[e].data();
+    }
+    std::vector<float> bias;
+    MoeWeightsHost wh{};
+    wh.router_weight = gate.data();
+    if (index.count(base + ".gate.bias")) {
+        rc = load_tensor(path, index, base + ".gate.bias", &bias, nullptr);
+        if (rc) return rc;
+        if ((int)bias.size() != cfg.num_experts) return fail(MOE_ERR_IO, "router bias shape");
+        wh.router_bias = bias.data();
+    }
+    wh.w1 = p1.data();
+    wh.w2 = p2.data();
+    wh.w3 = p3.data();
+    return moe_create(&cfg, &wh, out);
+}
+
+void moe_destroy(MoeHandle* h) {
+    if (!h) return;
+    moe::DeviceGuard guard(h->L.cfg.device);
+    cudaDeviceSynchronize();
+    Layer& L = h->L;
+    moe::free_workspace(L.ws);
+    moe::free_ptr(L.wg); moe::free_ptr(L.bias); moe::free_ptr(L.w13_hi); moe::free_ptr(L.w13_lo);
+    moe::free_ptr(L.w2_hi); moe::free_ptr(L.w2_lo); moe::free_ptr(L.w13_f32); moe::free_ptr(L.w2_f32);
+    if (h->own_stream) cudaStreamDestroy(h->own_stream);
+    delete h;
+}
+
+int moe_get_config(const MoeHandle* h, MoeConfig* cfg) {
+    if (!h || !cfg) return moe::fail(MOE_ERR_INVALID, "null argument");
+    *cfg = h->L.cfg;
+    return MOE_OK;
+}
+
+size_t moe_device_bytes(const MoeHandle* h) {
+    return h ? h->L.weight_bytes + h->L.ws.bytes : 0;
+}
+
+int moe_set_decode_max_tokens(MoeHandle* h, int32_t n) {
+    if (!h || n < 0) return moe::fail(MOE_ERR_INVALID, "bad argument");
+    h->L.cfg.decode_max_tokens = n;
+    return MOE_OK;
+}
+
+int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
+    if (T == 0) return MOE_OK;
+    if (!x || !y) return fail(MOE_ERR_INVALID, "null x or y");
+    if (x == y) return fail(MOE_ERR_INVALID, "y must not alias x");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15)
+        return fail(MOE_ERR_INVALID, "x and y must be 16-byte aligned");
+    DeviceGuard guard(h->L.cfg.device);
+    return forward_impl(h->L, x, y, T, static_cast<cudaStream_t>(stream));
+}
+
+int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
+    if (T == 0) return MOE_OK;
+    if (!x || !y) return fail(MOE_ERR_INVALID, "null x or y");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    int rc = ensure_stage(L, T);
+    if (rc) return rc;
+    cudaStream_t s = h->own_stream;
+    const size_t bytes = sizeof(float) * (size_t)T * L.d;
+    MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage, x, bytes, cudaMemcpyHostToDevice, s));
+    rc = forward_impl(L, L.ws.x_stage, L.ws.y_stage, T, s);
+    if (rc) return rc;
+    MOE_CUDA(cudaMemcpyAsync(y, L.ws.y_stage, bytes, cudaMemcpyDeviceToHost, s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    return check_device_errors(L);
+}
+
+int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
+                     float* weights, void* stream) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
+    if (T == 0) return MOE_OK;
+    if (!x || !idx || !weights) return fail(MOE_ERR_INVALID, "null argument");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    int rc = ensure_workspace(L, T);
+    if (rc) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    L.last_stream = s;
+    L.last_T = T;
+    MOE_CUDA(launch_router(L, x, T, logits, idx, weights, L.ws.blockhist, s));
+    // The scan reads the histogram the router just wrote, so counts and the
+    // layout queries below describe this call.
+    MOE_CUDA(launch_dispatch_scan(L, T, s));
+    return MOE_OK;
+}
+
+int moe_expert_counts(MoeHandle* h, int32_t* counts) {
+    using namespace moe;
+    if (!h || !counts) return fail(MOE_ERR_INVALID, "null argument");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    MOE_CUDA(cudaStreamSynchronize(L.last_stream));
+    MOE_CUDA(cudaMemcpy(counts, L.ws.counts, sizeof(int) * L.E, cudaMemcpyDeviceToHost));
+    return check_device_errors(L);
+}
+
+int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int32_t rows_cap,
+                        int32_t* rows_out, int32_t* expert_offsets) {
+    using namespace moe;
+    if (!h || !rows_out) return fail(MOE_ERR_INVALID, "null argument");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    MOE_CUDA(cudaStreamSynchronize(L.last_stream));
+    std::vector<int> eoff(L.E + 1);
+    MOE_CUDA(cudaMemcpy(eoff.data(), L.ws.eoff, sizeof(int) * (L.E + 1), cudaMemcpyDeviceToHost));
+    const int rows = eoff[L.E];
+    *rows_out = rows;
+    if (expert_offsets) std::copy(eoff.begin(), eoff.end(), expert_offsets);
+    if (rows > rows_cap) return fail(MOE_ERR_INVALID, "rows_cap is smaller than the packed rows");
+    if (row_token)
+        MOE_CUDA(cudaMemcpy(row_token, L.ws.row_token, sizeof(int) * rows, cudaMemcpyDeviceToHost));
+    if (row_weight)
+        MOE_CUDA(cudaMemcpy(row_weight, L.ws.row_weight, sizeof(float) * rows,
+                            cudaMemcpyDeviceToHost));
+    return check_device_errors(L);
+}
+
+}  // extern "C"

@@ -1,0 +1,404 @@
+// Grouped expert GEMMs on tcgen05 tensor cores.
+//
+// gate/up:  H[r, j] = silu(A[r] . w1[e, j]) * (A[r] . w3[e, j])
+//           A = packed activations (rows grouped by expert), B = w13[e], the
+//           row-interleaved gate/up weights: one 128 x 256 tile gives the gate
+//           and up values of the same 128 intermediate columns, so SwiGLU is
+//           applied in the epilogue straight out of TMEM.  Replaces
+//           gemm_grouped<true,true> (src/model.cu:618-643) and
+//           PhiMLP::forward's w1/w3/silu/mul (src/layer.cu:32-41).
+// down:     y[token(r)] += weight(r) * (H[r] . w2[e])
+//           The weighted un-permute/combine is the epilogue: each row's
+//           fp32 result is scaled by its routing weight and added into the
+//           token's output row with a vector reduction.  Replaces
+//           gemm_grouped_combine<1,2> (src/model.cu:645-667, 417-449) and the
+//           combine loop src/layer.cu:100-101.  With top-2 the two adds into a
+//           zeroed row commute, so y is deterministic; with k > 2 the order
+//           of the k adds is not fixed.
+//
+// One persistent CTA per SM, 6 warps:
+//   warp 0      TMA producer (one thread): A and B K-blocks into a ring of
+//               shared-memory stages, completion on a per-stage mbarrier.
+//   warp 1      MMA issuer (one thread) and TMEM owner: tcgen05.mma
+//               128 x 256 x (32 bytes of K) per instruction into one of two
+//               256-column fp32 accumulators in TMEM; tcgen05.commit releases
+//               smem stages and hands finished accumulators to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, one row per thread.
+// Precision: BF16 (kind::f16, 64 bf16 per 128-byte K-block, 4 stages) or
+// FP32 as 3xTF32 (kind::tf32 on hi/lo planes: hi*hi + hi*lo + lo*hi, 32 fp32
+// per K-block, 2 stages).  Both use 128-byte-swizzled K-major tiles.
+#include <cuda_bf16.h>
+
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace moe {
+namespace {
+
+enum Epi { kEpiGateUp = 0, kEpiDown = 1 };
+
+struct GemmParams {
+    const MTile* mtiles;
+    const int* num_mtiles;
+    int n_tiles;       // N tiles per expert
+    int k_blocks;      // K / (elements per 128-byte block)
+    int b_rows_per_expert;
+    // gate/up epilogue
+    void* h_hi;
+    void* h_lo;
+    int ldh;           // padded d_ff
+    // down epilogue
+    const int* row_token;
+    const float* row_weight;
+    float* y;
+    int d;
+    int* err;
+};
+
+constexpr int kThreads = 192;
+constexpr int kABytes = kTileM * 128;   // one A plane per stage: 128 rows x 128 B
+constexpr int kBBytes = kTileN * 128;   // one B plane per stage: 256 rows x 128 B
+constexpr int kAccCols = kTileN;        // fp32 columns per accumulator
+constexpr int kTmemCols = 2 * kAccCols;
+
+template <bool kTf32x3>
+struct Cfg {
+    static constexpr int kPlanes = kTf32x3 ? 2 : 1;
+    static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
+    static constexpr int kStages = kTf32x3 ? 2 : 4;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+    static constexpr uint32_t kIdesc = mma_idesc(kTf32x3 ? 2u : 1u, kTileM, kTileN);
+};
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+template <bool kTf32x3, int kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
+                   const __grid_constant__ CUtensorMap tmA_lo,
+                   const __grid_constant__ CUtensorMap tmB_hi,
+                   const __grid_constant__ CUtensorMap tmB_lo, const GemmParams p) {
+    using C = Cfg<kTf32x3>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* tfull = empty + C::kStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA_hi);
+        tma_prefetch_desc(&tmB_hi);
+        if constexpr (kTf32x3) {
+            tma_prefetch_desc(&tmA_lo);
+            tma_prefetch_desc(&tmB_lo);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int m_tiles = *p.num_mtiles;
+    const int total = m_tiles * p.n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const int mt = t % m_tiles;
+                const int nt = t / m_tiles;
+                const MTile tile = p.mtiles[mt];
+                const int brow = tile.expert * p.b_rows_per_expert + nt * kTileN;
+                constexpr int kElems = kTf32x3 ? 32 : 64;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, kDevErrTimeoutProducer)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t* sbase = smem + stage * C::kStageBytes;
+                    mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+                    const int kx = kb * kElems;
+                    tma_load_2d(sbase, &tmA_hi, &full[stage], kx, tile.row0);
+                    if constexpr (kTf32x3) {
+                        tma_load_2d(sbase + kABytes, &tmA_lo, &full[stage], kx, tile.row0);
+                        tma_load_2d(sbase + 2 * kABytes, &tmB_hi, &full[stage], kx, brow);
+                        tma_load_2d(sbase + 2 * kABytes + kBBytes, &tmB_lo, &full[stage], kx, brow);
+                    } else {
+                        tma_load_2d(sbase + kABytes, &tmB_hi, &full[stage], kx, brow);
+                    }
+                    ++issued;
+                    if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (*abort_flag) {
+                // Let every load already issued land before the CTA leaves.
+                const int pending = issued < C::kStages ? issued : C::kStages;
+                int s = stage;
+                uint32_t ph = phase;
+                for (int i = 0; i < pending; ++i) {
+                    if (--s < 0) { s = C::kStages - 1; ph ^= 1u; }
+                    mbar_wait(&full[s], ph, p.err, kDevErrTimeoutDrain);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err, kDevErrTimeoutMma)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                bool ok = true;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, p.err, kDevErrTimeoutMma)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = smem_u32(smem + stage * C::kStageBytes);
+                    const uint64_t a_hi = smem_desc_sw128(sbase);
+                    uint64_t a_lo = 0, b_hi, b_lo = 0;
+                    if constexpr (kTf32x3) {
+                        a_lo = smem_desc_sw128(sbase + kABytes);
+                        b_hi = smem_desc_sw128(sbase + 2 * kABytes);
+                        b_lo = smem_desc_sw128(sbase + 2 * kABytes + kBBytes);
+                    } else {
+                        b_hi = smem_desc_sw128(sbase + kABytes);
+                    }
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        // 32 bytes of K per instruction: +2 in the >>4 address field.
+                        const uint64_t off = static_cast<uint64_t>(ks * 2);
+                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        if constexpr (kTf32x3) {
+                            tc_mma<true>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
+                            tc_mma<true>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
+                            tc_mma<true>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
+                        } else {
+                            tc_mma<false>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, accum);
+                        }
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+            // Every MMA issued by this thread has completed once `done` fires.
+            tc_commit(done);
+            mbar_wait(done, 0, p.err, kDevErrTimeoutDrain);
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const int q = warp & 3;            // TMEM lane quarter this warp may read
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x) {
+            // Exit decisions are warp-uniform: tcgen05.ld below is .sync.aligned.
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            const int mt = t % m_tiles;
+            const int nt = t / m_tiles;
+            const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err, kDevErrTimeoutEpilogue);
+            if (!__all_sync(0xffffffffu, ready)) {
+                if (lane == 0) *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const MTile tile = p.mtiles[mt];
+            const bool valid = row_in_tile < tile.rows;
+            const size_t prow = static_cast<size_t>(tile.row0 + row_in_tile);
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * kAccCols);
+            if constexpr (kEpi == kEpiGateUp) {
+#pragma unroll 1
+                for (int c = 0; c < kTileN / 2; c += 32) {
+                    uint32_t g[32], u[32];
+                    tmem_ld32(tbase + c, g);
+                    tmem_ld32(tbase + kTileN / 2 + c, u);
+                    tmem_ld_wait();
+                    const int col = nt * (kTileN / 2) + c;
+                    if (valid) {
+                        if constexpr (kTf32x3) {
+                            float4* dh = reinterpret_cast<float4*>(
+                                static_cast<float*>(p.h_hi) + prow * p.ldh + col);
+                            float4* dl = reinterpret_cast<float4*>(
+                                static_cast<float*>(p.h_lo) + prow * p.ldh + col);
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                float4 hv, lv;
+                                float h0 = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                                float h1 = silu_f(__uint_as_float(g[j + 1])) * __uint_as_float(u[j + 1]);
+                                float h2 = silu_f(__uint_as_float(g[j + 2])) * __uint_as_float(u[j + 2]);
+                                float h3 = silu_f(__uint_as_float(g[j + 3])) * __uint_as_float(u[j + 3]);
+                                hv.x = to_tf32(h0); lv.x = to_tf32(h0 - hv.x);
+                                hv.y = to_tf32(h1); lv.y = to_tf32(h1 - hv.y);
+                                hv.z = to_tf32(h2); lv.z = to_tf32(h2 - hv.z);
+                                hv.w = to_tf32(h3); lv.w = to_tf32(h3 - hv.w);
+                                dh[j / 4] = hv;
+                                dl[j / 4] = lv;
+                            }
+                        } else {
+                            uint4* dst = reinterpret_cast<uint4*>(
+                                static_cast<__nv_bfloat16*>(p.h_hi) + prow * p.ldh + col);
+#pragma unroll
+                            for (int j = 0; j < 32; j += 8) {
+                                uint32_t w4[4];
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    const float a = silu_f(__uint_as_float(g[j + 2 * i])) *
+                                                    __uint_as_float(u[j + 2 * i]);
+                                    const float b = silu_f(__uint_as_float(g[j + 2 * i + 1])) *
+                                                    __uint_as_float(u[j + 2 * i + 1]);
+                                    __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+                                    w4[i] = *reinterpret_cast<uint32_t*>(&v2);
+                                }
+                                dst[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                            }
+                        }
+                    }
+                }
+            } else {
+                int tok = 0;
+                float wgt = 0.0f;
+                if (valid) {
+                    tok = p.row_token[prow];
+                    wgt = p.row_weight[prow];
+                }
+#pragma unroll 1
+                for (int c = 0; c < kTileN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + c, v);
+                    tmem_ld_wait();
+                    const int col = nt * kTileN + c;
+                    if (valid && col < p.d) {
+                        float* dst = p.y + static_cast<size_t>(tok) * p.d + col;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 o;
+                            o.x = wgt * __uint_as_float(v[j]);
+                            o.y = wgt * __uint_as_float(v[j + 1]);
+                            o.z = wgt * __uint_as_float(v[j + 2]);
+                            o.w = wgt * __uint_as_float(v[j + 3]);
+                            atomicAdd(reinterpret_cast<float4*>(dst + j), o);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+template <bool kTf32x3, int kEpi>
+cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                       const CUtensorMap& b_hi, const CUtensorMap& b_lo, const GemmParams& p,
+                       int grid, cudaStream_t s) {
+    using C = Cfg<kTf32x3>;
+    auto kern = expert_gemm_kernel<kTf32x3, kEpi>;
+    cudaError_t err =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    kern<<<grid, kThreads, C::kSmemBytes, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_expert_gemms(const Layer& L, int T, float* y, cudaStream_t s) {
+    const Workspace& W = L.ws;
+    const bool tf = three_pass(L);
+    const int elems = tf ? 32 : 64;
+    const int max_mtiles = (T * L.k + kTileM - 1) / kTileM + L.E;
+
+    GemmParams g{};
+    g.mtiles = W.mtiles;
+    g.num_mtiles = W.num_mtiles;
+    g.err = W.dev_err;
+    g.row_token = W.row_token;
+    g.row_weight = W.row_weight;
+    g.y = y;
+    g.d = L.d;
+    g.h_hi = W.h_hi;
+    g.h_lo = W.h_lo;
+    g.ldh = L.ffp;
+
+    // gate/up: N = 2 * ffp per expert, K = d.
+    GemmParams gu = g;
+    gu.n_tiles = 2 * L.ffp / kTileN;
+    gu.k_blocks = L.d / elems;
+    gu.b_rows_per_expert = 2 * L.ffp;
+    int grid = max_mtiles * gu.n_tiles;
+    if (grid > L.sm_count) grid = L.sm_count;
+    cudaError_t err;
+    if (tf)
+        err = launch_one<true, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi, L.tm_w13_lo, gu,
+                                          grid, s);
+    else
+        err = launch_one<false, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi, L.tm_w13_hi,
+                                           gu, grid, s);
+    if (err != cudaSuccess) return err;
+
+    // down: N = d per expert, K = ffp.
+    GemmParams dn = g;
+    dn.n_tiles = (L.d + kTileN - 1) / kTileN;
+    dn.k_blocks = L.ffp / elems;
+    dn.b_rows_per_expert = L.d;
+    grid = max_mtiles * dn.n_tiles;
+    if (grid > L.sm_count) grid = L.sm_count;
+    if (tf)
+        err = launch_one<true, kEpiDown>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo, dn,
+                                        grid, s);
+    else
+        err = launch_one<false, kEpiDown>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi, dn,
+                                         grid, s);
+    return err;
+}
+
+}  // namespace moe

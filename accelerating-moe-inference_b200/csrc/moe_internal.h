@@ -1,0 +1,119 @@
+// Internal declarations shared by the translation units of libmoe_b200.so.
+//
+// HBM layout of one layer (all row-major, 256-byte aligned allocations):
+//   router    wg [E][d] fp32, bias [E] fp32
+//   gate/up   w13 [E][2*ffp][d]: per 128-row block b of the padded d_ff
+//             (ffp = d_ff rounded up to 128), rows [256b, 256b+128) are
+//             w1 rows [128b, 128b+128) and rows [256b+128, 256b+256) are the
+//             matching w3 rows, so one 256-wide MMA tile holds the gate and
+//             up halves of the same 128 intermediate columns.  Padding rows
+//             are zero.
+//   down      w2 [E][d][ffp], padding columns zero.
+//   BF16 precision stores these once in bf16.  FP32 precision stores a tf32
+//   "hi" plane and an fp32 "lo" plane (w = hi + lo exactly, hi has its low 13
+//   mantissa bits clear) for the 3xTF32 tensor-core path, plus the plain fp32
+//   weights for the decode path.
+// Workspace per forward (capacity grows, never shrinks):
+//   logits [T][E], idx/wts [T][k], blockhist [nblk][E], counts [E],
+//   eoff [E+1] (packed-row offset of each expert, multiples of 128),
+//   mtiles [max_mtiles] (expert, first row, valid rows) and their number,
+//   row_token/row_weight [rows] (packed row -> token, combine weight),
+//   A [rows][d] and H [rows][ffp] activation planes (bf16, or tf32 hi + lo).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "moe_b200.h"
+
+namespace moe {
+
+constexpr int kRouteTokens = 32;   // tokens per router / dispatch block
+constexpr int kTileM = 128;        // GEMM tile rows (= expert block alignment)
+constexpr int kTileN = 256;        // GEMM tile columns
+constexpr int kFfBlock = 128;      // d_ff padding granule (half of kTileN)
+constexpr int kMaxExperts = 256;
+constexpr int kMaxTopK = 8;
+
+struct MTile {
+    int expert;
+    int row0;   // first packed row
+    int rows;   // valid rows (<= kTileM)
+    int pad;
+};
+
+struct Workspace {
+    int cap_T = 0;
+    int cap_rows = 0;
+    int cap_mtiles = 0;
+    float* logits = nullptr;
+    int* idx = nullptr;
+    float* wts = nullptr;
+    int* blockhist = nullptr;
+    int* counts = nullptr;
+    int* eoff = nullptr;
+    MTile* mtiles = nullptr;
+    int* num_mtiles = nullptr;
+    int* row_token = nullptr;
+    float* row_weight = nullptr;
+    void* a_hi = nullptr;
+    void* a_lo = nullptr;
+    void* h_hi = nullptr;
+    void* h_lo = nullptr;
+    float* x_stage = nullptr;   // host-API staging, [cap_T][d]
+    float* y_stage = nullptr;
+    int* dev_err = nullptr;     // device-side error flags (timeouts)
+    CUtensorMap tm_a_hi, tm_a_lo, tm_h_hi, tm_h_lo;
+    size_t bytes = 0;
+};
+
+struct Layer {
+    MoeConfig cfg{};
+    int d = 0, ff = 0, ffp = 0, E = 0, k = 0;
+    int sm_count = 148;
+    float* wg = nullptr;
+    float* bias = nullptr;
+    void* w13_hi = nullptr;
+    void* w13_lo = nullptr;
+    void* w2_hi = nullptr;
+    void* w2_lo = nullptr;
+    float* w13_f32 = nullptr;
+    float* w2_f32 = nullptr;
+    CUtensorMap tm_w13_hi, tm_w13_lo, tm_w2_hi, tm_w2_lo;
+    Workspace ws;
+    size_t weight_bytes = 0;
+    cudaStream_t last_stream = nullptr;
+    int last_T = 0;
+};
+
+// ------------------------------------------------------------ launchers
+// route.cu
+cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
+                          float* wts, int* blockhist, cudaStream_t s);
+cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
+cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s);
+
+// expert_gemm.cu
+cudaError_t launch_expert_gemms(const Layer& L, int T, float* y, cudaStream_t s);
+cudaError_t expert_gemm_setup(int device);
+
+// decode.cu
+cudaError_t launch_decode(const Layer& L, const float* x, int T, float* y, cudaStream_t s);
+
+// weights.cu
+cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const float* w3_dev,
+                           cudaStream_t s);
+cudaError_t convert_down(const Layer& L, int e, const float* w2_dev, cudaStream_t s);
+
+// tensor maps (capi.cpp)
+bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
+                  uint64_t outer, uint32_t box_inner, uint32_t box_outer, std::string* err);
+
+inline size_t elem_bytes(const Layer& L) { return L.cfg.precision == MOE_PREC_BF16 ? 2 : 4; }
+inline bool three_pass(const Layer& L) { return L.cfg.precision == MOE_PREC_FP32; }
+
+}  // namespace moe

@@ -1,0 +1,388 @@
+// Router and dispatch kernels.
+//
+//   router_kernel     logits = x . wg^T (+ bias), one fp32 fused-multiply-add
+//                     chain per (token, expert), k ascending -- the exact
+//                     arithmetic of the reference's matmul_transposed as its
+//                     Makefile builds it (src/tensor.cu:136-148, contracted to
+//                     FMA under -O3 -march=native) and of its device gate GEMM
+//                     (src/model.cu:505-616).  Then top-k selection per token
+//                     (PHI policy src/layer.cu:47-70 / src/model.cu:878-904, or
+//                     softmax top-k with a warp-shuffle argmax), the combine
+//                     weights, and the block's per-expert histogram
+//                     (src/model.cu:921-942).
+//   dispatch_scan     per-expert exclusive scan over blocks, expert offsets
+//                     padded to 128 rows, the GEMM m-tile list
+//                     (src/model.cu:953-1003).
+//   dispatch_permute  stable placement (ascending token order within each
+//                     expert, as assignments[e] in src/layer.cu:86-91 and
+//                     route_place src/model.cu:1009-1030) fused with the row
+//                     gather and the conversion of x into the GEMM operand
+//                     format (bf16, or tf32 hi + lo planes).
+#include <cuda_bf16.h>
+
+#include <cfloat>
+#include <climits>
+#include <cmath>
+
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kRouterThreads = 256;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    const uint32_t s = smem_u32(smem);
+    const int n = pred ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Softmax ordering key: NaN sorts below every number (as -inf).
+__device__ __forceinline__ float route_key(float v) { return v != v ? -INFINITY : v; }
+
+// Thread layout: el = tid % 8 is the expert lane, tt = tid / 8 the token
+// (0..31).  Thread (tt, el) owns the chains of experts el, el + 8, ...,
+// el + 8 (EJ - 1) for token tt.  Per 4-wide k step a warp reads 4 distinct x
+// rows and 8 distinct weight rows out of shared memory.
+template <int EJ, int KC>
+__global__ void __launch_bounds__(kRouterThreads)
+router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
+              const float* __restrict__ bias, int T, int d, int E, int k, int policy,
+              float quantum, float tie_eps, float* __restrict__ logits_out,
+              int* __restrict__ idx_out, float* __restrict__ w_out,
+              int* __restrict__ blockhist) {
+    constexpr int kStages = 3;
+    constexpr int kLd = KC + 4;              // padded row stride (floats)
+    constexpr int kXs = kRouteTokens * kLd;  // x floats per stage
+    constexpr int kWs = 8 * EJ * kLd;        // wg floats per stage
+    extern __shared__ __align__(16) float rsm[];
+    float* xs = rsm;                       // [kStages][32][kLd]
+    float* ws = rsm + kStages * kXs;       // [kStages][8*EJ][kLd]
+    float* lg = ws + kStages * kWs;        // [32][E + 1]
+    int* hist = reinterpret_cast<int*>(lg + kRouteTokens * (E + 1));
+
+    const int tid = threadIdx.x;
+    const int el = tid & 7;
+    const int tt = tid >> 3;
+    const int t0 = blockIdx.x * kRouteTokens;
+    const int n_tok = min(kRouteTokens, T - t0);
+    const int nchunks = d / KC;
+
+    // Stage loader: x chunk is 32 rows x KC floats, wg chunk E rows x KC.
+    auto load_chunk = [&](int chunk, int stage) {
+        const int kbase = chunk * KC;
+        constexpr int kXv = kRouteTokens * KC / 4;  // float4 per x chunk
+        for (int v = tid; v < kXv; v += kRouterThreads) {
+            const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
+            const bool ok = r < n_tok;
+            const float* src = x + (size_t)(ok ? t0 + r : 0) * d + kbase + c;
+            cp_async16(xs + stage * kXs + r * kLd + c, src, ok);
+        }
+        const int wv = E * KC / 4;
+        for (int v = tid; v < wv; v += kRouterThreads) {
+            const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
+            cp_async16(ws + stage * kWs + r * kLd + c, wg + (size_t)r * d + kbase + c, true);
+        }
+    };
+
+    float acc[EJ];
+#pragma unroll
+    for (int j = 0; j < EJ; ++j) acc[j] = 0.0f;
+
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < nchunks) load_chunk(s, s);
+        cp_async_commit();
+    }
+    for (int c = 0; c < nchunks; ++c) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        // Refill the stage consumed in the previous iteration.
+        const int nxt = c + kStages - 1;
+        if (nxt < nchunks) load_chunk(nxt, nxt % kStages);
+        cp_async_commit();
+        const int st = c % kStages;
+        const float* xr = xs + st * kXs + tt * kLd;
+        const float* wr = ws + st * kWs;
+#pragma unroll 4
+        for (int kk = 0; kk < KC; kk += 4) {
+            const float4 xv = *reinterpret_cast<const float4*>(xr + kk);
+#pragma unroll
+            for (int j = 0; j < EJ; ++j) {
+                const int e = el + 8 * j;
+                if (e < E) {
+                    const float4 wv = *reinterpret_cast<const float4*>(wr + e * kLd + kk);
+                    acc[j] = __fmaf_rn(xv.x, wv.x, acc[j]);
+                    acc[j] = __fmaf_rn(xv.y, wv.y, acc[j]);
+                    acc[j] = __fmaf_rn(xv.z, wv.z, acc[j]);
+                    acc[j] = __fmaf_rn(xv.w, wv.w, acc[j]);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+
+    for (int e = tid; e < E; e += kRouterThreads) hist[e] = 0;
+#pragma unroll
+    for (int j = 0; j < EJ; ++j) {
+        const int e = el + 8 * j;
+        if (e < E) {
+            float v = acc[j];
+            if (bias) v = __fadd_rn(v, bias[e]);
+            lg[tt * (E + 1) + e] = v;
+            if (logits_out && tt < n_tok) logits_out[(size_t)(t0 + tt) * E + e] = v;
+        }
+    }
+    __syncthreads();
+
+    // Selection: warp w handles tokens 4w .. 4w+3.
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int q = 0; q < 4; ++q) {
+        const int tk = warp * 4 + q;
+        if (tk >= n_tok) break;
+        const float* l = lg + tk * (E + 1);
+        int sel[kMaxTopK];
+        float wsel[kMaxTopK];
+        if (policy == MOE_ROUTER_PHI_QUANTISED) {
+            // src/layer.cu:47-70: quantise, then two hysteresis scans.  The
+            // scan is order-dependent, so one lane runs it serially.
+            if (lane == 0) {
+                for (int s = 0; s < 2; ++s) {
+                    const int excluded = s == 0 ? -1 : sel[0];
+                    int best = -1;
+                    float best_value = -INFINITY;
+                    for (int e = 0; e < E; ++e) {
+                        if (e == excluded) continue;
+                        const float score = l[e];
+                        const float rounded =
+                            floorf(__fadd_rn(__fdiv_rn(fabsf(score), quantum), 0.5f)) * quantum;
+                        const float v = score < 0.0f ? -rounded : rounded;
+                        if (best < 0 || v > __fadd_rn(best_value, tie_eps)) {
+                            best = e;
+                            best_value = v;
+                        }
+                    }
+                    sel[s] = best;
+                    wsel[s] = 0.5f;
+                }
+            }
+        } else {
+            // Softmax top-k: k rounds of a warp-wide argmax over
+            // (key, index), larger key first, exact ties to the lower index.
+            unsigned taken = 0;  // bit i: expert lane + 32 i already chosen
+            for (int s = 0; s < k; ++s) {
+                float bk = -INFINITY;
+                int bi = INT_MAX;
+                for (int i = 0, e = lane; e < E; ++i, e += 32) {
+                    if (taken & (1u << i)) continue;
+                    const float kv = route_key(l[e]);
+                    if (bi == INT_MAX || kv > bk) { bk = kv; bi = e; }
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) {
+                    const float ok = __shfl_xor_sync(0xffffffffu, bk, off);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                    if (ok > bk || (ok == bk && oi < bi)) { bk = ok; bi = oi; }
+                }
+                if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+                sel[s] = bi;
+            }
+            if (lane == 0) {
+                const double m = (double)l[sel[0]];
+                double p[kMaxTopK], sum = 0.0;
+                for (int s = 0; s < k; ++s) { p[s] = exp((double)l[sel[s]] - m); sum += p[s]; }
+                for (int s = 0; s < k; ++s) wsel[s] = (float)(p[s] / sum);
+            }
+        }
+        if (lane == 0) {
+            const int t = t0 + tk;
+            for (int s = 0; s < k; ++s) {
+                idx_out[(size_t)t * k + s] = sel[s];
+                w_out[(size_t)t * k + s] = wsel[s];
+                atomicAdd(&hist[sel[s]], 1);
+            }
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouterThreads) blockhist[(size_t)blockIdx.x * E + e] = hist[e];
+}
+
+// One block, one thread per expert.  blockhist becomes each block's base
+// row inside its expert's run; counts, padded offsets and the m-tile list
+// follow.  Padding rows of every expert block get token -1.
+__global__ void __launch_bounds__(kMaxExperts)
+dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restrict__ counts,
+                     int* __restrict__ eoff, MTile* __restrict__ mtiles,
+                     int* __restrict__ num_mtiles, int* __restrict__ row_token,
+                     float* __restrict__ row_weight) {
+    __shared__ int s_cnt[kMaxExperts];
+    __shared__ int s_off[kMaxExperts + 1];
+    const int e = threadIdx.x;
+    if (e < E) {
+        int run = 0;
+        for (int b = 0; b < nblk; ++b) {
+            const int c = blockhist[(size_t)b * E + e];
+            blockhist[(size_t)b * E + e] = run;
+            run += c;
+        }
+        s_cnt[e] = run;
+        counts[e] = run;
+    }
+    __syncthreads();
+    if (e == 0) {
+        int off = 0, nm = 0;
+        for (int x = 0; x < E; ++x) {
+            s_off[x] = off;
+            eoff[x] = off;
+            const int c = s_cnt[x];
+            for (int r = 0; r < c; r += kTileM) {
+                MTile mt;
+                mt.expert = x;
+                mt.row0 = off + r;
+                mt.rows = min(kTileM, c - r);
+                mt.pad = 0;
+                mtiles[nm++] = mt;
+            }
+            off += (c + kTileM - 1) / kTileM * kTileM;
+        }
+        s_off[E] = off;
+        eoff[E] = off;
+        *num_mtiles = nm;
+    }
+    __syncthreads();
+    if (e < E) {
+        for (int r = s_off[e] + s_cnt[e]; r < s_off[e + 1]; ++r) {
+            row_token[r] = -1;
+            row_weight[r] = 0.0f;
+        }
+    }
+}
+
+template <int kMode>  // 0: bf16 plane, 1: tf32 hi + lo planes
+__global__ void __launch_bounds__(256)
+dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
+                        const int* __restrict__ idx, const float* __restrict__ wts,
+                        const int* __restrict__ blockbase, const int* __restrict__ eoff,
+                        int* __restrict__ row_token, float* __restrict__ row_weight,
+                        void* __restrict__ a_hi, void* __restrict__ a_lo) {
+    __shared__ unsigned s_mask[kMaxExperts];
+    __shared__ int s_base[kMaxExperts];
+    __shared__ int s_dest[kRouteTokens * kMaxTopK];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * kRouteTokens;
+    const int n_tok = min(kRouteTokens, T - t0);
+    for (int e = tid; e < E; e += blockDim.x) {
+        s_mask[e] = 0u;
+        s_base[e] = eoff[e] + blockbase[(size_t)blockIdx.x * E + e];
+    }
+    __syncthreads();
+    const int n_ent = n_tok * k;
+    int my_e = -1, my_t = 0;
+    if (tid < n_ent) {
+        my_t = tid / k;
+        my_e = idx[(size_t)(t0 + my_t) * k + (tid % k)];
+        atomicOr(&s_mask[my_e], 1u << my_t);
+    }
+    __syncthreads();
+    if (tid < n_ent) {
+        const int rank = __popc(s_mask[my_e] & ((1u << my_t) - 1u));
+        const int pos = s_base[my_e] + rank;
+        s_dest[tid] = pos;
+        row_token[pos] = t0 + my_t;
+        row_weight[pos] = wts[(size_t)(t0 + my_t) * k + (tid % k)];
+    }
+    __syncthreads();
+    const int nv = d / 4;
+    for (int t = 0; t < n_tok; ++t) {
+        const float4* src = reinterpret_cast<const float4*>(x + (size_t)(t0 + t) * d);
+        for (int v = tid; v < nv; v += blockDim.x) {
+            const float4 f = src[v];
+            if constexpr (kMode == 0) {
+                __nv_bfloat162 lo2 = __floats2bfloat162_rn(f.x, f.y);
+                __nv_bfloat162 hi2 = __floats2bfloat162_rn(f.z, f.w);
+                uint2 packed;
+                packed.x = *reinterpret_cast<uint32_t*>(&lo2);
+                packed.y = *reinterpret_cast<uint32_t*>(&hi2);
+                for (int s = 0; s < k; ++s) {
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
+                }
+            } else {
+                float4 h, l;
+                h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+                h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+                h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+                h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+                for (int s = 0; s < k; ++s) {
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<float4*>(a_hi)[row * nv + v] = h;
+                    reinterpret_cast<float4*>(a_lo)[row * nv + v] = l;
+                }
+            }
+        }
+    }
+}
+
+template <int EJ, int KC>
+cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
+                            float* wts, int* blockhist, cudaStream_t s) {
+    const int E = L.E;
+    const size_t smem = sizeof(float) * (3 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4)) +
+                                         kRouteTokens * (E + 1)) +
+                        sizeof(int) * E;
+    auto kern = router_kernel<EJ, KC>;
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess) return err;
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
+    kern<<<nblk, kRouterThreads, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
+                                            L.cfg.router_policy, L.cfg.router_quantum,
+                                            L.cfg.router_tie_eps, logits, idx, wts, blockhist);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
+                          float* wts, int* blockhist, cudaStream_t s) {
+    const int ej = (L.E + 7) / 8;
+    if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s);
+    if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s);
+    if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s);
+    if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s);
+    if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s);
+    return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s);
+}
+
+cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
+    const Workspace& W = L.ws;
+    dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(W.blockhist, nblk, L.E, W.counts, W.eoff,
+                                                  W.mtiles, W.num_mtiles, W.row_token,
+                                                  W.row_weight);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s) {
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
+    const Workspace& W = L.ws;
+    if (three_pass(L))
+        dispatch_permute_kernel<1><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, W.a_lo);
+    else
+        dispatch_permute_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, W.a_lo);
+    return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,163 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, the B200 (sm_100a) MoE FFN layer.
+ *
+ * This is the drop-in boundary for the MoE hot path of
+ * songsnim/accelerating-MoE-inference.  Each entry point names the reference
+ * interface it replaces.  Plain pointers and sizes only: device pointers are
+ * CUDA device addresses, streams are cudaStream_t passed as void*.
+ *
+ * Conventions (mirroring the reference's, include/layer.h:29-36):
+ *   - x and y are fp32, row-major [T][d_model].
+ *   - Expert weights are nn.Linear layout: w1 (gate) and w3 (up) are
+ *     [d_ff][d_model], w2 (down) is [d_model][d_ff]; the router weight is
+ *     [num_experts][d_model] (src/layer.cu:28-30, 73-77).
+ *   - Every function returns MOE_OK (0) or a negative MoeStatus; the message
+ *     of the last failure on the calling thread is moe_last_error().  The
+ *     reference throws std::invalid_argument / std::runtime_error for the
+ *     same conditions (src/tensor.cu:138, src/model_loader.cu:34-42); the C++
+ *     layer in include/layer.h rethrows them that way.
+ *   - A handle owns its device weights and workspace.  One handle serves one
+ *     stream at a time; calls on one handle must not overlap.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+typedef enum MoeStatus {
+    MOE_OK = 0,
+    MOE_ERR_INVALID = -1,     /* bad argument or shape */
+    MOE_ERR_UNSUPPORTED = -2, /* valid but not supported by this build */
+    MOE_ERR_CUDA = -3,        /* a CUDA runtime/driver call failed */
+    MOE_ERR_OOM = -4,         /* device or pinned allocation failed */
+    MOE_ERR_IO = -5,          /* model.bin missing, truncated or malformed */
+    MOE_ERR_TIMEOUT = -6,     /* a bounded device-side wait ran out */
+    MOE_ERR_NCCL = -7         /* expert-parallel exchange failed */
+} MoeStatus;
+
+/* Routing policy.
+ * PHI_QUANTISED: the reference's router, src/layer.cu:47-70 (scores
+ *   quantised to router_quantum, top-2 with router_tie_eps hysteresis, lower
+ *   index wins, weights 0.5/0.5).  Requires top_k == 2.
+ * SOFTMAX_TOPK: softmax over experts, top-k by logit (exact ties go to the
+ *   lower expert index), the k weights renormalised to sum to 1. */
+typedef enum MoeRouterPolicy {
+    MOE_ROUTER_PHI_QUANTISED = 0,
+    MOE_ROUTER_SOFTMAX_TOPK = 1
+} MoeRouterPolicy;
+
+/* Expert-FFN arithmetic.  The router is always exact fp32 (a k-ascending
+ * fused-multiply-add chain, bit-identical to src/tensor.cu:136-148 as the
+ * reference's Makefile builds it).
+ * FP32: fp32-faithful.  Prefill runs 3xTF32 on tcgen05 tensor cores
+ *   (hi*hi + hi*lo + lo*hi into an fp32 TMEM accumulator); decode streams the
+ *   fp32 weights through CUDA cores.  Relative L2 error vs the reference
+ *   <= 1e-3.
+ * BF16: weights and activations rounded to bf16 (RNE), fp32 accumulation.
+ *   Relative L2 error vs the reference <= 2e-2. */
+typedef enum MoePrecision {
+    MOE_PREC_FP32 = 0,
+    MOE_PREC_BF16 = 1
+} MoePrecision;
+
+typedef struct MoeConfig {
+    int32_t d_model;        /* hidden size; multiple of 64 */
+    int32_t d_ff;           /* expert intermediate size (any; padded internally) */
+    int32_t num_experts;    /* 1..256 */
+    int32_t top_k;          /* 1..min(8, num_experts) */
+    int32_t router_policy;  /* MoeRouterPolicy */
+    int32_t precision;      /* MoePrecision */
+    float router_quantum;   /* PHI policy score quantum (reference 1e-3, include/config.h:22) */
+    float router_tie_eps;   /* PHI policy tie margin (reference 2e-2, include/config.h:23) */
+    int32_t decode_max_tokens; /* T <= this takes the weight-streaming decode kernels
+                                  (0: never; default 16) */
+    int32_t device;         /* CUDA device ordinal the handle lives on */
+    int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
+    int32_t reserved[5];
+} MoeConfig;
+
+/* Host fp32 weights of one layer (the tensors PhiMoE loads by name,
+ * src/layer.cu:73-77: block_sparse_moe.gate.weight and
+ * block_sparse_moe.experts.{e}.w{1,2,3}.weight). */
+typedef struct MoeWeightsHost {
+    const float* router_weight;      /* [E][d] */
+    const float* router_bias;        /* [E] or NULL (added after the dot product) */
+    const float* const* w1;          /* E pointers, each [d_ff][d] */
+    const float* const* w3;          /* E pointers, each [d_ff][d] */
+    const float* const* w2;          /* E pointers, each [d][d_ff] */
+} MoeWeightsHost;
+
+typedef struct MoeHandle MoeHandle;
+
+/* Library ABI version (MOE_B200_ABI_VERSION). */
+int moe_abi_version(void);
+
+/* Message of the last failure on this thread ("" if none). */
+const char* moe_last_error(void);
+
+/* Fill *cfg with defaults: the reference's Phi-tiny-MoE constants
+ * (include/config.h:8-23: d 4096, d_ff 448, 16 experts, top-2, PHI policy,
+ * quantum 1e-3, tie-eps 2e-2), FP32 precision, device 0. */
+void moe_config_init(MoeConfig* cfg);
+
+/* Build a layer from host weights.  Replaces the weight upload of
+ * PhiMoE::PhiMoE (src/layer.cu:72-78) and DeviceMoE::DeviceMoE
+ * (src/model.cu:1491-1513). */
+int moe_create(const MoeConfig* cfg, const MoeWeightsHost* weights, MoeHandle** out);
+
+/* Build a layer straight from a model.bin (ModelLoader format,
+ * src/model_loader.cu:14-50), layer `layer_idx`.  Zero d_model / d_ff /
+ * num_experts in *cfg are inferred from the file. */
+int moe_create_from_model_bin(const MoeConfig* cfg, const char* path, int layer_idx,
+                              MoeHandle** out);
+
+void moe_destroy(MoeHandle* h);
+
+int moe_get_config(const MoeHandle* h, MoeConfig* cfg);
+
+/* Device bytes held by the handle (weights + workspace). */
+size_t moe_device_bytes(const MoeHandle* h);
+
+/* Change the decode threshold (MoeConfig.decode_max_tokens) of a handle. */
+int moe_set_decode_max_tokens(MoeHandle* h, int32_t max_tokens);
+
+/* y[T][d] = MoE(x[T][d]) on device buffers, enqueued on `stream`; no host
+ * synchronisation.  Replaces the device MoE segment src/model.cu:1976-2019
+ * (gemm_gate -> route_count/scan/place -> gemm_grouped ->
+ * gemm_grouped_combine).  y must not alias x.  T == 0 is a no-op. */
+int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream);
+
+/* The same on host buffers (copies in, computes, copies out, synchronises).
+ * Replaces PhiMoE::forward(const Tensor& x, Tensor& y) (src/layer.cu:80-103). */
+int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T);
+
+/* Router only, device buffers: logits [T][E] (may be NULL), expert indices
+ * and weights [T][top_k] in selection order.  Replaces the router GEMM and
+ * route (src/layer.cu:84-91; src/model.cu:505-616, 878-942). */
+int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
+                     float* weights, void* stream);
+
+/* Per-expert row counts [E] of the last forward or route on this handle
+ * (synchronises the handle's last stream).  The dispatch histogram of
+ * src/model.cu:921-1003. */
+int moe_expert_counts(MoeHandle* h, int32_t* counts);
+
+/* Dispatch layout of the last forward (synchronises): for each packed row
+ * (rows are grouped by expert, each expert's block starting on a multiple of
+ * 128 rows) the source token (-1 for padding rows) and its combine weight.
+ * `rows_cap` is the capacity of the two arrays; *rows_out receives the number
+ * of packed rows.  Replaces route_place's index (src/model.cu:1009-1030). */
+int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int32_t rows_cap,
+                        int32_t* rows_out, int32_t* expert_offsets /* [E+1] or NULL */);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

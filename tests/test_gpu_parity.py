@@ -1,0 +1,171 @@
+"""CUDA path vs the CPU oracle, through the C ABI (needs a B200).
+
+Tolerances (north star): router logits and expert indices bit-exact; combine
+weights within 1 fp32 ulp (the softmax weights use double exp on both sides);
+output relative L2 <= 1e-3 in FP32 (3xTF32) precision and <= 2e-2 in BF16.
+"""
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN_DIR, load_oracle, load_pkg, ref_elementwise_failures, rel_l2
+
+sys.path.insert(0, str(GOLDEN_DIR))
+from cases import CASES, case_inputs  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+oracle = load_oracle()
+TOL = {0: 1e-3, 1: 2e-2}   # precision -> rel-L2 bound
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def route_on_gpu(pkg, layer_gpu, x):
+    import torch
+    T = x.shape[0]
+    xd = torch.from_numpy(x).cuda()
+    lg = torch.empty((T, layer_gpu.E), dtype=torch.float32, device="cuda")
+    idx = torch.empty((T, layer_gpu.k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, layer_gpu.k), dtype=torch.float32, device="cuda")
+    layer_gpu.route_device(xd.data_ptr(), T, lg.data_ptr(), idx.data_ptr(), w.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return lg.cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy()
+
+
+def policies(name):
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    out = []
+    if "phi_y" in g:
+        out.append(("phi", 0))
+    out.append(("soft", 1))
+    return out
+
+
+CASE_POL = [(n, tag, pol) for n in sorted(CASES) for (tag, pol) in policies(n)]
+
+
+@pytest.mark.parametrize("name,tag,policy", CASE_POL)
+def test_router_matches_golden(name, tag, policy):
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, name)
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    with pkg.MoeLayer(layer, top_k=CASES[name]["k"], policy=policy) as m:
+        lg, idx, w = route_on_gpu(pkg, m, x)
+    assert np.array_equal(bits(lg), bits(g[f"{tag}_logits"])), "router logits differ"
+    assert np.array_equal(idx, g[f"{tag}_idx"]), "expert indices differ"
+    ulp = np.abs(bits(w).astype(np.int64) - bits(g[f"{tag}_w"]).astype(np.int64))
+    assert ulp.max() <= 1
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("name,tag,policy", CASE_POL)
+def test_forward_matches_golden(name, tag, policy, precision):
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, name)
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    y_ref = g[f"{tag}_y"]
+    with pkg.MoeLayer(layer, top_k=CASES[name]["k"], policy=policy, precision=precision) as m:
+        y = m.forward_host(x)
+        y2 = m.forward_host(x)
+    err = rel_l2(y, y_ref)
+    assert np.isfinite(y).all()
+    assert err <= TOL[precision], f"rel-L2 {err:.3e}"
+    if precision == 0:
+        assert ref_elementwise_failures(y, y_ref) == 0
+    if CASES[name]["k"] <= 2:
+        assert np.array_equal(bits(y), bits(y2)), "top-2 forward is not deterministic"
+
+
+def test_dispatch_layout_is_stable_and_aligned():
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, "c1")
+    g = np.load(GOLDEN_DIR / "c1.npz")
+    idx = g["soft_idx"]
+    with pkg.MoeLayer(layer, top_k=2, policy=1) as m:
+        m.forward_host(x)
+        counts = m.expert_counts()
+        tok, wt, eoff = m.dispatch_layout(rows_cap=4096)
+    T, E = x.shape[0], layer.E
+    assert counts.sum() == T * 2
+    assert np.array_equal(counts, np.bincount(idx.ravel(), minlength=E))
+    assert (eoff % 128 == 0).all() and eoff[0] == 0
+    for e in range(E):
+        blk = tok[eoff[e]:eoff[e + 1]]
+        valid = blk[: counts[e]]
+        # assignments[e] in ascending token order (src/layer.cu:86-91)
+        expect = np.nonzero((idx == e).any(1))[0]
+        assert np.array_equal(valid, expect)
+        assert (blk[counts[e]:] == -1).all()
+        ws = wt[eoff[e]:eoff[e] + counts[e]]
+        slot = np.argmax(idx[expect] == e, axis=1)
+        assert np.array_equal(bits(ws), bits(g["soft_w"][expect, slot]))
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("T", [1, 2, 33, 129, 300])
+def test_ragged_token_counts(T, precision, orc):
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(21, 256, 320, 8)
+    x = pkg.synthetic_tokens(21, T, 256)
+    y_ref, idx_ref, *_ = orc.moe_forward(x, layer, 2, oracle.POLICY_SOFTMAX)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision) as m:
+        y = m.forward_host(x)
+    assert rel_l2(y, y_ref) <= TOL[precision]
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_skewed_routing_and_empty_experts(precision, orc):
+    """A router bias sends every token to experts 3 and 5: their blocks span
+    several 128-row tiles and the other experts get no rows at all."""
+    pkg = load_pkg()
+    bias = np.zeros(8, np.float32)
+    bias[3] = bias[5] = 100.0
+    layer = pkg.synthetic_layer(22, 128, 256, 8, router_bias=bias)
+    x = pkg.synthetic_tokens(22, 700, 128)
+    y_ref, idx_ref, *_ = orc.moe_forward(x, layer, 2, oracle.POLICY_SOFTMAX)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision) as m:
+        y = m.forward_host(x)
+        counts = m.expert_counts()
+    assert counts[3] == counts[5] == 700 and counts.sum() == 1400
+    assert rel_l2(y, y_ref) <= TOL[precision]
+
+
+def test_permutation_equivariance_bit_exact():
+    """Each token's output depends only on its own row: permuting the tokens
+    permutes the outputs bit for bit (top-2, so the combine is order-free)."""
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(23, 512, 768, 8)
+    x = pkg.synthetic_tokens(23, 1000, 512)
+    perm = np.random.default_rng(0).permutation(1000)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=1) as m:
+        y = m.forward_host(x)
+        yp = m.forward_host(x[perm])
+    assert np.array_equal(bits(yp), bits(y[perm]))
+
+
+def test_model_bin_path_matches_in_memory_path(tmp_path):
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, "phi16")
+    pkg.write_model_bin(tmp_path / "m.bin", [layer])
+    with pkg.MoeLayer(layer, top_k=2, policy=0) as a, \
+            pkg.MoeLayer(model_bin=str(tmp_path / "m.bin"), top_k=2, policy=0) as b:
+        assert np.array_equal(bits(a.forward_host(x)), bits(b.forward_host(x)))
+
+
+def test_forward_device_on_torch_stream():
+    import torch
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, "c1")
+    g = np.load(GOLDEN_DIR / "c1.npz")
+    with pkg.MoeLayer(layer, top_k=2, policy=0) as m:
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.full_like(xd, float("nan"))
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            m.forward_device(xd.data_ptr(), yd.data_ptr(), x.shape[0], s.cuda_stream)
+        s.synchronize()
+        assert rel_l2(yd.cpu().numpy(), g["phi_y"]) <= 1e-3
