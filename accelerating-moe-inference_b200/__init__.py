@@ -33,11 +33,12 @@ PREC_BF16 = 1
 
 # Every symbol include/moe_b200.h declares.
 EXPORTED_SYMBOLS = (
-    "moe_abi_version", "moe_last_error", "moe_config_init", "moe_create",
+    "moe_abi_version", "moe_last_error", "moe_config_init", "moe_create", "moe_create_from_device",
     "moe_create_from_model_bin", "moe_destroy", "moe_get_config", "moe_device_bytes",
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
-    "moe_expert_counts", "moe_dispatch_layout",
+    "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
 )
+PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
 
 
 class MoeError(RuntimeError):
@@ -83,6 +84,8 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_config_init.argtypes = [ctypes.POINTER(MoeConfig)]
     L.moe_create.argtypes = [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeightsHost),
                              ctypes.POINTER(vp)]
+    L.moe_create_from_device.argtypes = [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeightsHost),
+                                         ctypes.POINTER(vp)]
     L.moe_create_from_model_bin.argtypes = [ctypes.POINTER(MoeConfig), ctypes.c_char_p,
                                             ctypes.c_int, ctypes.POINTER(vp)]
     L.moe_destroy.argtypes = [vp]
@@ -95,6 +98,8 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_route_device.argtypes = [vp, vp, ctypes.c_int32, vp, vp, vp, vp]
     L.moe_expert_counts.argtypes = [vp, _i32p]
     L.moe_dispatch_layout.argtypes = [vp, _i32p, _f32p, ctypes.c_int32, _i32p, _i32p]
+    L.moe_profile_enable.argtypes = [vp, ctypes.c_int]
+    L.moe_profile_read.argtypes = [vp, _f32p, ctypes.c_int32]
     if path is None:
         _lib = L
     return L
@@ -246,6 +251,33 @@ class MoeLayer:
         self.cfg = MoeConfig()
         _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
 
+    @classmethod
+    def from_device_pointers(cls, d: int, ff: int, E: int, wg_ptr: int, w1_ptrs, w3_ptrs,
+                             w2_ptrs, bias_ptr: Optional[int] = None, *, top_k: int = 2,
+                             policy: int = ROUTER_SOFTMAX_TOPK, precision: int = PREC_FP32,
+                             device: int = 0, max_tokens: int = 0,
+                             decode_max_tokens: Optional[int] = None, **cfg_kw) -> "MoeLayer":
+        """Build from fp32 weights already on `device` (moe_create_from_device);
+        pointers are integer device addresses in the same layouts as LayerWeights."""
+        L = load_library()
+        cfg = default_config(d_model=d, d_ff=ff, num_experts=E, top_k=top_k,
+                             router_policy=policy, precision=precision, device=device,
+                             max_tokens=max_tokens, **cfg_kw)
+        if decode_max_tokens is not None:
+            cfg.decode_max_tokens = decode_max_tokens
+        P = _f32p * E
+        cast = lambda v: ctypes.cast(ctypes.c_void_p(v), _f32p)  # noqa: E731
+        hw = MoeWeightsHost(cast(wg_ptr), cast(bias_ptr) if bias_ptr else None,
+                            P(*map(cast, w1_ptrs)), P(*map(cast, w3_ptrs)),
+                            P(*map(cast, w2_ptrs)))
+        h = ctypes.c_void_p()
+        _check(L.moe_create_from_device(ctypes.byref(cfg), ctypes.byref(hw), ctypes.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.cfg = MoeConfig()
+        _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
+        return self
+
     # -- properties
     @property
     def d(self):
@@ -302,6 +334,17 @@ class MoeLayer:
                                                   eoff.ctypes.data_as(_i32p)))
         n = rows.value
         return tok[:n], wt[:n], eoff
+
+    def profile(self, enable: bool = True):
+        _check(load_library().moe_profile_enable(self._h, int(enable)))
+
+    def stage_ms(self) -> np.ndarray:
+        """Per-stage device milliseconds of the last forward (see PROFILE_STAGES)."""
+        out = np.zeros(len(PROFILE_STAGES), np.float32)
+        rc = load_library().moe_profile_read(self._h, _fp(out), len(out))
+        if rc < 0:
+            _check(rc)
+        return out
 
     def close(self):
         if self._h:

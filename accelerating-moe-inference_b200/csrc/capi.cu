@@ -195,16 +195,25 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     Workspace& W = L.ws;
     L.last_stream = s;
     L.last_T = T;
+    for (bool& r : L.prof_ran) r = false;
+    MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
+    prof_mark(L, 0, s);
     MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s));
+    prof_mark(L, 1, s);
     MOE_CUDA(launch_dispatch_scan(L, T, s));
+    prof_mark(L, 2, s);
     if (T <= L.cfg.decode_max_tokens) {
-        MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
-        MOE_CUDA(launch_decode(L, x, T, y, s));
+        MOE_CUDA(launch_decode(L, x, T, y, s));  // marks stage 3 between its kernels
+        prof_mark(L, 4, s);
+        if (L.profile) L.prof_ran[4] = false;
         return MOE_OK;
     }
     MOE_CUDA(launch_dispatch_permute(L, x, T, s));
-    MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
-    MOE_CUDA(launch_expert_gemms(L, T, y, s));
+    prof_mark(L, 3, s);
+    MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/false));
+    prof_mark(L, 4, s);
+    MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/true));
+    prof_mark(L, kProfileStages, s);
     return MOE_OK;
 }
 
@@ -315,8 +324,29 @@ void moe_config_init(MoeConfig* c) {
     c->max_tokens = 0;
 }
 
+}  // extern "C"
+
+namespace moe {
+namespace {
+int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, MoeHandle** out);
+}
+}  // namespace moe
+
+extern "C" {
+
 int moe_create(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
-    using namespace moe;
+    return moe::create_impl(cfg, w, false, out);
+}
+
+int moe_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
+    return moe::create_impl(cfg, w, true, out);
+}
+
+}  // extern "C"
+
+namespace moe {
+namespace {
+int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, MoeHandle** out) {
     if (!cfg || !w || !out) return fail(MOE_ERR_INVALID, "null argument");
     *out = nullptr;
     int rc = validate_config(*cfg);
@@ -360,11 +390,12 @@ int moe_create(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
         cudaError_t e_ = (call);                                         \
         if (e_ != cudaSuccess) return cleanup_and_fail(cuda_fail(e_, #call)); \
     } while (0)
+    const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     MOE_CUDA_C(dalloc(&L.wg, sizeof(float) * E * d, &wb));
-    MOE_CUDA_C(cudaMemcpy(L.wg, w->router_weight, sizeof(float) * E * d, cudaMemcpyHostToDevice));
+    MOE_CUDA_C(cudaMemcpy(L.wg, w->router_weight, sizeof(float) * E * d, kind));
     if (w->router_bias) {
         MOE_CUDA_C(dalloc(&L.bias, sizeof(float) * E, &wb));
-        MOE_CUDA_C(cudaMemcpy(L.bias, w->router_bias, sizeof(float) * E, cudaMemcpyHostToDevice));
+        MOE_CUDA_C(cudaMemcpy(L.bias, w->router_bias, sizeof(float) * E, kind));
     }
     MOE_CUDA_C(dalloc(&L.w13_hi, eb * E * 2 * ffp * d, &wb));
     MOE_CUDA_C(dalloc(&L.w2_hi, eb * E * d * ffp, &wb));
@@ -374,21 +405,31 @@ int moe_create(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
         MOE_CUDA_C(dalloc(&L.w13_f32, 4 * E * 2 * ffp * d, &wb));
         MOE_CUDA_C(dalloc(&L.w2_f32, 4 * E * d * ffp, &wb));
     }
-    float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr;
-    MOE_CUDA_C(dalloc(&st1, sizeof(float) * ff * d, nullptr));
-    MOE_CUDA_C(dalloc(&st3, sizeof(float) * ff * d, nullptr));
-    MOE_CUDA_C(dalloc(&st2, sizeof(float) * ff * d, nullptr));
-    for (int e = 0; e < L.E; ++e) {
-        MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
-        MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
-        MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e], sizeof(float) * ff * d, cudaMemcpyHostToDevice, s));
-        MOE_CUDA_C(convert_gateup(L, e, st1, st3, s));
-        MOE_CUDA_C(convert_down(L, e, st2, s));
+    if (device_ptrs) {
+        // The caller's device copies serve directly as the converters' input.
+        MOE_CUDA_C(cudaDeviceSynchronize());
+        for (int e = 0; e < L.E; ++e) {
+            MOE_CUDA_C(convert_gateup(L, e, w->w1[e], w->w3[e], s));
+            MOE_CUDA_C(convert_down(L, e, w->w2[e], s));
+        }
         MOE_CUDA_C(cudaStreamSynchronize(s));
+    } else {
+        float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr;
+        MOE_CUDA_C(dalloc(&st1, sizeof(float) * ff * d, nullptr));
+        MOE_CUDA_C(dalloc(&st3, sizeof(float) * ff * d, nullptr));
+        MOE_CUDA_C(dalloc(&st2, sizeof(float) * ff * d, nullptr));
+        for (int e = 0; e < L.E; ++e) {
+            MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(convert_gateup(L, e, st1, st3, s));
+            MOE_CUDA_C(convert_down(L, e, st2, s));
+            MOE_CUDA_C(cudaStreamSynchronize(s));
+        }
+        cudaFree(st1);
+        cudaFree(st3);
+        cudaFree(st2);
     }
-    cudaFree(st1);
-    cudaFree(st3);
-    cudaFree(st2);
     const uint32_t box_k = tf ? 32 : 64;
     std::string err;
     const bool bf = !tf;
@@ -409,6 +450,10 @@ int moe_create(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHandle** out) {
     *out = h.release();
     return MOE_OK;
 }
+}  // namespace
+}  // namespace moe
+
+extern "C" {
 
 int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int layer_idx,
                               MoeHandle** out) {
@@ -472,6 +517,8 @@ void moe_destroy(MoeHandle* h) {
     moe::free_workspace(L.ws);
     moe::free_ptr(L.wg); moe::free_ptr(L.bias); moe::free_ptr(L.w13_hi); moe::free_ptr(L.w13_lo);
     moe::free_ptr(L.w2_hi); moe::free_ptr(L.w2_lo); moe::free_ptr(L.w13_f32); moe::free_ptr(L.w2_f32);
+    for (cudaEvent_t& e : L.prof_ev)
+        if (e) cudaEventDestroy(e);
     if (h->own_stream) cudaStreamDestroy(h->own_stream);
     delete h;
 }
@@ -490,6 +537,34 @@ int moe_set_decode_max_tokens(MoeHandle* h, int32_t n) {
     if (!h || n < 0) return moe::fail(MOE_ERR_INVALID, "bad argument");
     h->L.cfg.decode_max_tokens = n;
     return MOE_OK;
+}
+
+int moe_profile_enable(MoeHandle* h, int enable) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    if (enable && !L.prof_ev[0])
+        for (cudaEvent_t& e : L.prof_ev) MOE_CUDA(cudaEventCreate(&e));
+    L.profile = enable != 0;
+    return MOE_OK;
+}
+
+int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n) {
+    using namespace moe;
+    if (!h || !stage_ms || n < 0) return fail(MOE_ERR_INVALID, "bad argument");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    if (!L.prof_ev[0]) return fail(MOE_ERR_INVALID, "profiling was never enabled");
+    int last = -1;
+    for (int i = 0; i < kProfileStages; ++i)
+        if (L.prof_ran[i]) last = i;
+    if (last >= 0) MOE_CUDA(cudaEventSynchronize(L.prof_ev[last + 1]));
+    for (int i = 0; i < n && i < kProfileStages; ++i) {
+        stage_ms[i] = 0.0f;
+        if (L.prof_ran[i]) MOE_CUDA(cudaEventElapsedTime(&stage_ms[i], L.prof_ev[i], L.prof_ev[i + 1]));
+    }
+    return kProfileStages;
 }
 
 int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream) {

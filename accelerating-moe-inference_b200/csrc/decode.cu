@@ -4,7 +4,7 @@
 
 namespace moe {
 
-cudaError_t launch_decode(const Layer&, const float*, int, float*, cudaStream_t) {
+cudaError_t launch_decode(Layer&, const float*, int, float*, cudaStream_t) {
     return cudaErrorNotSupported;
 }
 

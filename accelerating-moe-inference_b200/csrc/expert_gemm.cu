@@ -351,7 +351,7 @@ cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMa
 
 }  // namespace
 
-cudaError_t launch_expert_gemms(const Layer& L, int T, float* y, cudaStream_t s) {
+cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down) {
     const Workspace& W = L.ws;
     const bool tf = three_pass(L);
     const int elems = tf ? 32 : 64;
@@ -368,37 +368,31 @@ cudaError_t launch_expert_gemms(const Layer& L, int T, float* y, cudaStream_t s)
     g.h_hi = W.h_hi;
     g.h_lo = W.h_lo;
     g.ldh = L.ffp;
-
-    // gate/up: N = 2 * ffp per expert, K = d.
-    GemmParams gu = g;
-    gu.n_tiles = 2 * L.ffp / kTileN;
-    gu.k_blocks = L.d / elems;
-    gu.b_rows_per_expert = 2 * L.ffp;
-    int grid = max_mtiles * gu.n_tiles;
+    if (!down) {
+        // gate/up: N = 2 * ffp per expert, K = d.
+        g.n_tiles = 2 * L.ffp / kTileN;
+        g.k_blocks = L.d / elems;
+        g.b_rows_per_expert = 2 * L.ffp;
+    } else {
+        // down: N = d per expert, K = ffp.
+        g.n_tiles = (L.d + kTileN - 1) / kTileN;
+        g.k_blocks = L.ffp / elems;
+        g.b_rows_per_expert = L.d;
+    }
+    int grid = max_mtiles * g.n_tiles;
     if (grid > L.sm_count) grid = L.sm_count;
-    cudaError_t err;
+    if (!down) {
+        if (tf)
+            return launch_one<true, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi, L.tm_w13_lo,
+                                                g, grid, s);
+        return launch_one<false, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi, L.tm_w13_hi, g,
+                                             grid, s);
+    }
     if (tf)
-        err = launch_one<true, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi, L.tm_w13_lo, gu,
-                                          grid, s);
-    else
-        err = launch_one<false, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi, L.tm_w13_hi,
-                                           gu, grid, s);
-    if (err != cudaSuccess) return err;
-
-    // down: N = d per expert, K = ffp.
-    GemmParams dn = g;
-    dn.n_tiles = (L.d + kTileN - 1) / kTileN;
-    dn.k_blocks = L.ffp / elems;
-    dn.b_rows_per_expert = L.d;
-    grid = max_mtiles * dn.n_tiles;
-    if (grid > L.sm_count) grid = L.sm_count;
-    if (tf)
-        err = launch_one<true, kEpiDown>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo, dn,
-                                        grid, s);
-    else
-        err = launch_one<false, kEpiDown>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi, dn,
-                                         grid, s);
-    return err;
+        return launch_one<true, kEpiDown>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo, g, grid,
+                                          s);
+    return launch_one<false, kEpiDown>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi, g, grid,
+                                       s);
 }
 
 }  // namespace moe

@@ -38,6 +38,7 @@ constexpr int kTileN = 256;        // GEMM tile columns
 constexpr int kFfBlock = 128;      // d_ff padding granule (half of kTileN)
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
+constexpr int kProfileStages = 5;
 
 struct MTile {
     int expert;
@@ -88,7 +89,18 @@ struct Layer {
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;
     int last_T = 0;
+    // Stage timers (moe_profile_enable): event i marks the start of stage i,
+    // event kProfileStages the end of the last one.
+    bool profile = false;
+    cudaEvent_t prof_ev[kProfileStages + 1] = {};
+    bool prof_ran[kProfileStages] = {};
 };
+
+// Record the boundary before stage `i` (no-op unless profiling).
+inline void prof_mark(Layer& L, int i, cudaStream_t s) {
+    if (L.profile) cudaEventRecord(L.prof_ev[i], s);
+    if (L.profile && i < kProfileStages) L.prof_ran[i] = true;
+}
 
 // ------------------------------------------------------------ launchers
 // route.cu
@@ -98,11 +110,12 @@ cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s);
 
 // expert_gemm.cu
-cudaError_t launch_expert_gemms(const Layer& L, int T, float* y, cudaStream_t s);
-cudaError_t expert_gemm_setup(int device);
+// down == false: gate/up GEMM with the SwiGLU epilogue into H;
+// down == true:  down GEMM with the weighted-combine epilogue into y.
+cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down);
 
 // decode.cu
-cudaError_t launch_decode(const Layer& L, const float* x, int T, float* y, cudaStream_t s);
+cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s);
 
 // weights.cu
 cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const float* w3_dev,

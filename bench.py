@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""MoE-layer benchmark on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--precision bf16|fp32] [--workload c2]
+
+Workload: a Mixtral-shaped MoE FFN layer in prefill,
+T=4096 tokens per GPU, d_model=4096, d_ff=14336, 8 experts, top-2 softmax
+routing, SwiGLU experts, fp32 weights N(0, 0.02) (seed 1) and N(0, 1)
+activations -- synthetic, drawn on the GPU by a seeded torch generator.
+
+One step = one forward of the layer over the step's T tokens: router,
+dispatch (histogram / scan / permute), gate/up grouped GEMM with the SwiGLU
+epilogue, down grouped GEMM with the weighted-combine epilogue.
+
+  value       tokens/s over all ranks, x resident in HBM, CUDA events around
+              each step on the launching stream; L2 is flushed (256 MiB
+              write) between steps, outside the events.
+  e2e         tokens/s through moe_forward_host (the reference-facing
+              host-buffer call): pinned host x -> device -> layer -> host y,
+              timed around the synchronous call.
+  roofline    the gate/up GEMM (2/3 of the layer's FLOPs): algorithmic FLOPs
+              4*T*k*d*ff per launch / its live CUDA-event duration, against
+              the measured dense bf16 peak in MEASURED_PEAKS.json.
+  cpu_baseline  the reference's own PhiMoE::forward (src/layer.cu:80-103,
+              compiled from its sources into oracle/_ref) on this host's
+              cores, on a bounded sample of the same layer.
+
+N > 1 (torchrun): token-sharded replicas -- every rank holds all experts and
+its own T tokens (weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "MoE-layer tokens/s at 1–8 B200; expert-GEMM % of TC peak; decode HBM GB/s"
+WORKLOADS = {
+    "c2": dict(workload="c2-mixtral-moe-prefill", T=4096, d=4096, ff=14336, E=8, k=2, seed=1),
+}
+KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
+FLUSH_BYTES = 256 << 20
+
+
+def _pkg():
+    import importlib.util
+    name = "moe_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "accelerating-moe-inference_b200" / "__init__.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def _traffic_from_profile(workload: str, precision: str):
+    """dram bytes per launch of the gate/up GEMM from the committed ncu summary."""
+    f = ROOT / "profiles" / f"expert_gemm_gateup_{workload}_{precision}.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.f = tempfile.TemporaryFile(mode="w+")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9 or (self.uuid and c[0] != self.uuid):
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = float(c[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cpu_reference_tokens_per_s(host_layer, x_host, threads: int):
+    """Time the reference's own PhiMoE::forward on a bounded token sample.
+    Returns (tokens/s, kind, tokens in the sample, threads used)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle  # checker / baseline only
+    pkg = _pkg()
+    E = host_layer.E
+    if oracle.Reference.available(E):
+        ref = oracle.Reference(E)
+        cores = ref.set_threads(threads)
+        fd = os.memfd_create("moe_model_bin", 0)
+        path = f"/proc/self/fd/{fd}"
+        try:
+            pkg.write_model_bin(path, [host_layer])
+            ref.load(path, 0)
+        finally:
+            os.close(fd)
+        run = ref.forward
+        kind = "reference"
+    else:
+        orc = oracle.Oracle()
+        cores = threads
+        run = lambda xs: orc.moe_forward(xs, host_layer, 2, oracle.POLICY_PHI, nthreads=threads)[0]  # noqa: E731
+        kind = "port"
+        ref = None
+    # The reference parallelises each expert's matmul over its rows, so the
+    # sample carries ~4 tokens per core (about one row per core per expert
+    # at top-2 of 8); the per-token work is fixed, so its time is bounded.
+    n = int(min(len(x_host), max(8, 4 * cores)))
+    t = time.perf_counter()
+    run(x_host[:n])
+    dt = time.perf_counter() - t
+    if ref is not None:
+        ref.close()
+    return n / dt, kind, n, cores
+
+
+def reference_arm(args, wl):
+    """bench.py --impl reference: the reference's own CPU MoE layer (rank 0)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    pkg = _pkg()
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    g = torch.Generator().manual_seed(wl["seed"])
+    d, ff, E = wl["d"], wl["ff"], wl["E"]
+    std = 0.02
+    mk = lambda *s: (torch.randn(*s, generator=g) * std).numpy()  # noqa: E731
+    layer = pkg.LayerWeights(mk(E, d), [mk(ff, d) for _ in range(E)],
+                             [mk(ff, d) for _ in range(E)], [mk(d, ff) for _ in range(E)])
+    x = torch.randn(wl["T"], d, generator=g).numpy()
+    threads = len(os.sched_getaffinity(0))
+    if not oracle.Reference.available(E):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref was not built (reference sources absent at build time)"}))
+        return 0
+    ref = oracle.Reference(E)
+    cores = ref.set_threads(threads)
+    fd = os.memfd_create("moe_model_bin", 0)
+    try:
+        pkg.write_model_bin(f"/proc/self/fd/{fd}", [layer])
+        ref.load(f"/proc/self/fd/{fd}", 0)
+    finally:
+        os.close(fd)
+    # Size each step so the whole run stays within ~3 minutes.
+    n0 = max(1, min(wl["T"], cores))
+    t = time.perf_counter()
+    ref.forward(x[:n0])
+    rate = n0 / (time.perf_counter() - t)
+    per_step = 150.0 / max(1, args.steps + args.warmup)
+    n = int(max(1, min(wl["T"], rate * per_step)))
+    for _ in range(args.warmup):
+        ref.forward(x[:n])
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        ref.forward(x[:n])
+        times.append(time.perf_counter() - t)
+    ref.close()
+    ms = 1e3 * sum(times) / len(times)
+    value = n / (ms / 1e3)
+    sample = (f"{n} of the workload's {wl['T']} tokens per step through the reference's "
+              f"PhiMoE::forward (its quantised top-2 router; same per-token work)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded torch CPU generator, N(0,0.02) weights, N(0,1) x)",
+        "config": {k: wl[k] for k in ("workload", "T", "d", "ff", "E", "k", "seed")},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return reference_arm(args, wl)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    pkg = _pkg()
+    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
+    T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
+
+    # ---- synthetic layer, drawn on the device (same weights on every rank)
+    gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
+    dev = torch.device("cuda", local)
+    rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
+    wg = rnd(E, d)
+    w1 = [rnd(ff, d) for _ in range(E)]
+    w3 = [rnd(ff, d) for _ in range(E)]
+    w2 = [rnd(d, ff) for _ in range(E)]
+    layer = pkg.MoeLayer.from_device_pointers(
+        d, ff, E, wg.data_ptr(), [t.data_ptr() for t in w1], [t.data_ptr() for t in w3],
+        [t.data_ptr() for t in w2], top_k=k, policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec,
+        device=local, max_tokens=T)
+    host_layer = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_layer = pkg.LayerWeights(wg.cpu().numpy(), [t.cpu().numpy() for t in w1],
+                                      [t.cpu().numpy() for t in w3], [t.cpu().numpy() for t in w2])
+    del w1, w3, w2
+    torch.cuda.empty_cache()
+    xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
+    x = torch.randn(T, d, generator=xgen, device=dev)
+    y = torch.empty_like(x)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    layer.profile(True)
+
+    def step():
+        layer.forward_device(x.data_ptr(), y.data_ptr(), T, sp)
+
+    for _ in range(args.warmup):
+        step()
+        flush.zero_()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    stage_sum = np.zeros(len(pkg.PROFILE_STAGES))
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+        stage_sum += layer.stage_ms()
+        flush.zero_()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+
+    # ---- e2e through the host-buffer C-ABI call (pinned buffers)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    xn, yn = xh.numpy(), yh.numpy()
+    import ctypes
+    lib = pkg.load_library()
+    fp = ctypes.POINTER(ctypes.c_float)
+    xp, yp = xn.ctypes.data_as(fp), yn.ctypes.data_as(fp)
+    for _ in range(args.warmup):
+        pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
+    e2e_steps = max(3, args.steps // 2)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    clocks = sampler.stop()
+    ok_y = bool(torch.isfinite(torch.from_numpy(yn)).all())
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_s = float(t[0]), float(t[1])
+    ms = total_ms / args.steps
+    value = world * T / (ms / 1e3)
+    e2e = world * T / e2e_s
+
+    if rank == 0:
+        hbm, bf16_peak, bf16_sust, src = _peaks()
+        st = stage_sum / args.steps
+        gu_ms, dn_ms = st[3], st[4]
+        gu_flops = 4.0 * T * k * d * ff
+        dn_flops = 2.0 * T * k * d * ff
+        achieved = gu_flops / (gu_ms / 1e3) / 1e12
+        traffic = _traffic_from_profile(wl["workload"], args.precision)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
+            "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
+            "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
+                       "experts": E, "top_k": k, "router": "softmax_topk_renorm",
+                       "precision": args.precision, "seed": wl["seed"],
+                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "parallelism": f"dp{world} (token-sharded replicas, all experts per GPU)"},
+            "roofline": {"kernel": "gate/up grouped GEMM (tcgen05, SwiGLU epilogue)",
+                         "bound": "tensor", "achieved": achieved, "peak": bf16_peak,
+                         "unit": "TFLOP/s", "frac": achieved / bf16_peak,
+                         "traffic": traffic, "peak_source": f"{src} bf16 dense (burst)"},
+            "expert_gemm": {"tflops": (gu_flops + dn_flops) / ((gu_ms + dn_ms) / 1e3) / 1e12,
+                            "frac_of_bf16_peak": (gu_flops + dn_flops) / ((gu_ms + dn_ms) / 1e3)
+                            / 1e12 / bf16_peak},
+            "stages_ms": {n: float(v) for n, v in zip(pkg.PROFILE_STAGES, st)},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * d * 4,
+                    "d2h_bytes_per_step": T * d * 4,
+                    "how": "moe_forward_host on pinned host buffers, host clock around the "
+                           "synchronous call"},
+            "gpu_launches": KERNELS_PER_FORWARD * args.steps,
+            "clocks": clocks,
+            "output_finite": ok_y,
+        }
+        if host_layer is not None:
+            xs = x[: min(T, 1024)].cpu().numpy()
+            tps, kind, n, cores = cpu_reference_tokens_per_s(host_layer, xs,
+                                                             len(os.sched_getaffinity(0)))
+            line["cpu_baseline"] = {
+                "value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+                "sample": f"{n} tokens of this layer through PhiMoE::forward (fp32, "
+                          f"its quantised top-2 router), {cores} OpenMP threads"}
+        print(json.dumps(line))
+    layer.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -112,6 +112,12 @@ void moe_config_init(MoeConfig* cfg);
  * (src/model.cu:1491-1513). */
 int moe_create(const MoeConfig* cfg, const MoeWeightsHost* weights, MoeHandle** out);
 
+/* The same, with every pointer in *weights a device address on cfg->device
+ * (for callers whose weights are already resident, e.g. generated or loaded
+ * on the GPU).  The handle keeps its own converted copies; the caller's
+ * buffers may be freed afterwards. */
+int moe_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* weights, MoeHandle** out);
+
 /* Build a layer straight from a model.bin (ModelLoader format,
  * src/model_loader.cu:14-50), layer `layer_idx`.  Zero d_model / d_ff /
  * num_experts in *cfg are inferred from the file. */
@@ -156,6 +162,18 @@ int moe_expert_counts(MoeHandle* h, int32_t* counts);
  * of packed rows.  Replaces route_place's index (src/model.cu:1009-1030). */
 int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int32_t rows_cap,
                         int32_t* rows_out, int32_t* expert_offsets /* [E+1] or NULL */);
+
+/* Per-stage device timers, the counterpart of the reference's APS_PROFILE
+ * stage timers (src/model.cu:1584-1622, 2052-2058).  When enabled, forward
+ * records a CUDA event on its stream at each stage boundary (no host
+ * synchronisation).  moe_profile_read synchronises on the last event and
+ * writes the milliseconds of each stage of the last forward:
+ *   [0] router  [1] dispatch scan  [2] dispatch permute (or decode gate/up)
+ *   [3] gate/up grouped GEMM (or decode down)  [4] down grouped GEMM
+ * Stages a forward did not run read 0.  Returns the number of stages (5). */
+#define MOE_PROFILE_STAGES 5
+int moe_profile_enable(MoeHandle* h, int enable);
+int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n);
 
 #ifdef __cplusplus
 }
