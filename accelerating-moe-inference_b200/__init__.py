@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "moe_create_from_model_bin", "moe_destroy", "moe_get_config", "moe_device_bytes",
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
     "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
+    "moe_dispatch_noalloc",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
 
@@ -100,6 +101,8 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_dispatch_layout.argtypes = [vp, _i32p, _f32p, ctypes.c_int32, _i32p, _i32p]
     L.moe_profile_enable.argtypes = [vp, ctypes.c_int]
     L.moe_profile_read.argtypes = [vp, _f32p, ctypes.c_int32]
+    L.moe_dispatch_noalloc.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                       vp, vp, ctypes.c_int32, vp, vp, vp]
     if path is None:
         _lib = L
     return L

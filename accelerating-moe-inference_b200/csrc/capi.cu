@@ -272,6 +272,8 @@ int load_tensor(const std::string& path, const std::unordered_map<std::string, B
 
 }  // namespace
 
+int report_error(int code, const std::string& msg) { return fail(code, msg); }
+
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
                   uint32_t box_inner, uint32_t box_outer, std::string* err) {
     if (!load_encode(err)) return false;

@@ -122,6 +122,9 @@ cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const flo
                            cudaStream_t s);
 cudaError_t convert_down(const Layer& L, int e, const float* w2_dev, cudaStream_t s);
 
+// Record `msg` as this thread's moe_last_error() and return `code` (capi.cu).
+int report_error(int code, const std::string& msg);
+
 // tensor maps (capi.cpp)
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
                   uint64_t outer, uint32_t box_inner, uint32_t box_outer, std::string* err);

@@ -175,6 +175,34 @@ int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int
 int moe_profile_enable(MoeHandle* h, int enable);
 int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n);
 
+/* Dispatch that allocates nothing.  No counterpart in the reference: it
+ * exists for callers that cannot call cudaMalloc -- code running inside a
+ * stream capture that must not touch the allocator, frameworks that own all
+ * device memory through their own pool, latency-critical paths that cannot
+ * afford an allocation's implicit synchronisation.
+ *
+ * From routing decisions already on the device (idx / weights [T][top_k],
+ * e.g. from moe_route_device) it writes the same packed layout the forward
+ * path uses: expert blocks padded to multiples of 128 rows, tokens in
+ * ascending order inside each block, row_token = -1 and row_weight = 0 on
+ * padding rows, expert_offsets [E+1], counts [E].  All outputs are device
+ * buffers; rows_cap must be >= (T * top_k / 128 + num_experts + 1) * 128.
+ * Expert indices outside [0, num_experts) are not placed.
+ *
+ * Its only scratch is a fixed 1 MiB array in the library's device memory
+ * (MOE_NOALLOC_SCRATCH_BYTES, present on every GPU that loads the library
+ * until the process exits), so ceil(T / 32) * num_experts may not exceed
+ * 262144; larger calls are rejected with MOE_ERR_INVALID.  The first call on
+ * a device looks up that array's address, so make it before any stream
+ * capture starts.  All calls on a device share the array: calls whose GPU
+ * work can overlap race and must be serialised by the caller.  Enqueued on
+ * `stream` with no host synchronisation. */
+#define MOE_NOALLOC_SCRATCH_BYTES (1u << 20)
+int moe_dispatch_noalloc(const int32_t* idx, const float* weights, int32_t T,
+                         int32_t num_experts, int32_t top_k, int32_t* row_token,
+                         float* row_weight, int32_t rows_cap, int32_t* expert_offsets,
+                         int32_t* counts, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
