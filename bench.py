@@ -46,6 +46,10 @@ ROOT = Path(__file__).resolve().parent
 METRIC = "MoE-layer tokens/s at 1–8 B200; expert-GEMM % of TC peak; decode HBM GB/s"
 WORKLOADS = {
     "c2": dict(workload="c2-mixtral-moe-prefill", T=4096, d=4096, ff=14336, E=8, k=2, seed=1),
+    # Profiling case for ncu --set full: the C2 expert shapes (d 4096, d_ff
+    # 14336) with 2 experts, ~2 GB on the device (weights > L2).
+    "c2small": dict(workload="c2small-2expert-profile", T=2048, d=4096, ff=14336, E=2, k=2,
+                    seed=1),
 }
 KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
 FLUSH_BYTES = 256 << 20
