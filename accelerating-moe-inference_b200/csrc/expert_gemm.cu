@@ -73,6 +73,24 @@ struct Cfg {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
 
+// Tile order: expert by expert; inside an expert, n-tile major and m-tile
+// minor.  The CTAs running at once then share one expert's activation rows
+// (which stay in L2) and each weight tile is fetched from HBM once, by the
+// m-tiles of its expert running side by side.
+struct TileCoord {
+    int mt;
+    int nt;
+};
+__device__ __forceinline__ TileCoord decode_tile(const MTile* __restrict__ mtiles, int t,
+                                                 int n_tiles) {
+    const MTile& head = mtiles[t / n_tiles];
+    const int local = t - head.mstart * n_tiles;
+    TileCoord c;
+    c.nt = local / head.mcount;
+    c.mt = head.mstart + local % head.mcount;
+    return c;
+}
+
 template <bool kTf32x3, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
 expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
@@ -132,8 +150,8 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             uint32_t phase = 0;
             int issued = 0;
             for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-                const int mt = t % m_tiles;
-                const int nt = t / m_tiles;
+                const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+                const int mt = tc.mt, nt = tc.nt;
                 const MTile tile = p.mtiles[mt];
                 const int brow = tile.expert * p.b_rows_per_expert + nt * kTileN;
                 constexpr int kElems = kTf32x3 ? 32 : 64;
@@ -233,8 +251,8 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             // Exit decisions are warp-uniform: tcgen05.ld below is .sync.aligned.
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            const int mt = t % m_tiles;
-            const int nt = t / m_tiles;
+            const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+            const int mt = tc.mt, nt = tc.nt;
             const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err, kDevErrTimeoutEpilogue);
             if (!__all_sync(0xffffffffu, ready)) {
                 if (lane == 0) *abort_flag = 1;

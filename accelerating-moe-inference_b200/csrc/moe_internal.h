@@ -40,11 +40,15 @@ constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
 constexpr int kProfileStages = 5;
 
+// One 128-row slice of an expert's packed block.  m-tiles are listed expert
+// by expert; mstart / mcount locate the expert's own run in that list.
 struct MTile {
     int expert;
-    int row0;   // first packed row
-    int rows;   // valid rows (<= kTileM)
-    int pad;
+    int row0;    // first packed row
+    int rows;    // valid rows (<= kTileM)
+    int mstart;  // index of the expert's first m-tile
+    int mcount;  // m-tiles of this expert
+    int pad[3];
 };
 
 struct Workspace {

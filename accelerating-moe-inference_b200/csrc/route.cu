@@ -60,7 +60,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
               float quantum, float tie_eps, float* __restrict__ logits_out,
               int* __restrict__ idx_out, float* __restrict__ w_out,
               int* __restrict__ blockhist) {
-    constexpr int kStages = 3;
+    constexpr int kStages = 4;
     constexpr int kLd = KC + 4;              // padded row stride (floats)
     constexpr int kXs = kRouteTokens * kLd;  // x floats per stage
     constexpr int kWs = 8 * EJ * kLd;        // wg floats per stage
@@ -215,51 +215,87 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     for (int e = tid; e < E; e += kRouterThreads) blockhist[(size_t)blockIdx.x * E + e] = hist[e];
 }
 
-// One block, one thread per expert.  blockhist becomes each block's base
-// row inside its expert's run; counts, padded offsets and the m-tile list
-// follow.  Padding rows of every expert block get token -1.
-__global__ void __launch_bounds__(kMaxExperts)
+// One block of 32 warps.  Warp w scans experts w, w + 32, ... over the
+// blocks with warp shuffles, turning blockhist into each block's base row
+// inside its expert's run; warp 0 then scans the experts' padded sizes into
+// offsets; finally every warp writes its experts' m-tiles and marks their
+// padding rows (token -1, weight 0).
+constexpr int kScanThreads = 1024;
+
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += n;
+    }
+    return v;
+}
+
+__global__ void __launch_bounds__(kScanThreads)
 dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restrict__ counts,
                      int* __restrict__ eoff, MTile* __restrict__ mtiles,
                      int* __restrict__ num_mtiles, int* __restrict__ row_token,
                      float* __restrict__ row_weight) {
     __shared__ int s_cnt[kMaxExperts];
     __shared__ int s_off[kMaxExperts + 1];
-    const int e = threadIdx.x;
-    if (e < E) {
-        int run = 0;
-        for (int b = 0; b < nblk; ++b) {
-            const int c = blockhist[(size_t)b * E + e];
-            blockhist[(size_t)b * E + e] = run;
-            run += c;
+    __shared__ int s_mst[kMaxExperts + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kWarps = kScanThreads / 32;
+    for (int e = warp; e < E; e += kWarps) {
+        int carry = 0;
+        for (int b0 = 0; b0 < nblk; b0 += 32) {
+            const int b = b0 + lane;
+            const int c = b < nblk ? blockhist[(size_t)b * E + e] : 0;
+            const int incl = warp_inclusive_scan(c, lane);
+            if (b < nblk) blockhist[(size_t)b * E + e] = carry + incl - c;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        s_cnt[e] = run;
-        counts[e] = run;
+        if (lane == 0) {
+            s_cnt[e] = carry;
+            counts[e] = carry;
+        }
     }
     __syncthreads();
-    if (e == 0) {
-        int off = 0, nm = 0;
-        for (int x = 0; x < E; ++x) {
-            s_off[x] = off;
-            eoff[x] = off;
-            const int c = s_cnt[x];
-            for (int r = 0; r < c; r += kTileM) {
-                MTile mt;
-                mt.expert = x;
-                mt.row0 = off + r;
-                mt.rows = min(kTileM, c - r);
-                mt.pad = 0;
-                mtiles[nm++] = mt;
+    if (warp == 0) {
+        int run_off = 0, run_m = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < E ? s_cnt[e] : 0;
+            const int mc = (c + kTileM - 1) / kTileM;
+            const int pc = mc * kTileM;
+            const int ipc = warp_inclusive_scan(pc, lane);
+            const int imc = warp_inclusive_scan(mc, lane);
+            if (e < E) {
+                s_off[e] = run_off + ipc - pc;
+                s_mst[e] = run_m + imc - mc;
+                eoff[e] = s_off[e];
             }
-            off += (c + kTileM - 1) / kTileM * kTileM;
+            run_off += __shfl_sync(0xffffffffu, ipc, 31);
+            run_m += __shfl_sync(0xffffffffu, imc, 31);
         }
-        s_off[E] = off;
-        eoff[E] = off;
-        *num_mtiles = nm;
+        if (lane == 0) {
+            s_off[E] = run_off;
+            s_mst[E] = run_m;
+            eoff[E] = run_off;
+            *num_mtiles = run_m;
+        }
     }
     __syncthreads();
-    if (e < E) {
-        for (int r = s_off[e] + s_cnt[e]; r < s_off[e + 1]; ++r) {
+    for (int e = warp; e < E; e += kWarps) {
+        const int c = s_cnt[e];
+        const int mst = s_mst[e];
+        const int mc = s_mst[e + 1] - mst;
+        for (int i = lane; i < mc; i += 32) {
+            MTile mt;
+            mt.expert = e;
+            mt.row0 = s_off[e] + i * kTileM;
+            mt.rows = min(kTileM, c - i * kTileM);
+            mt.mstart = mst;
+            mt.mcount = mc;
+            mt.pad[0] = mt.pad[1] = mt.pad[2] = 0;
+            mtiles[mst + i] = mt;
+        }
+        for (int r = s_off[e] + c + lane; r < s_off[e + 1]; r += 32) {
             row_token[r] = -1;
             row_weight[r] = 0.0f;
         }
@@ -301,13 +337,23 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
     }
     __syncthreads();
     const int nv = d / 4;
-    for (int t = 0; t < n_tok; ++t) {
-        const float4* src = reinterpret_cast<const float4*>(x + (size_t)(t0 + t) * d);
-        for (int v = tid; v < nv; v += blockDim.x) {
-            const float4 f = src[v];
+    const int total = n_tok * nv;
+    constexpr int kUnroll = 4;
+    for (int base = tid; base < total; base += kUnroll * 256) {
+        float4 f[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int i = base + u * 256;
+            if (i < total) f[u] = reinterpret_cast<const float4*>(x + (size_t)t0 * d)[i];
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int i = base + u * 256;
+            if (i >= total) break;
+            const int t = i / nv, v = i % nv;
             if constexpr (kMode == 0) {
-                __nv_bfloat162 lo2 = __floats2bfloat162_rn(f.x, f.y);
-                __nv_bfloat162 hi2 = __floats2bfloat162_rn(f.z, f.w);
+                __nv_bfloat162 lo2 = __floats2bfloat162_rn(f[u].x, f[u].y);
+                __nv_bfloat162 hi2 = __floats2bfloat162_rn(f[u].z, f[u].w);
                 uint2 packed;
                 packed.x = *reinterpret_cast<uint32_t*>(&lo2);
                 packed.y = *reinterpret_cast<uint32_t*>(&hi2);
@@ -317,10 +363,10 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                 }
             } else {
                 float4 h, l;
-                h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
-                h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
-                h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
-                h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+                h.x = to_tf32(f[u].x); l.x = to_tf32(f[u].x - h.x);
+                h.y = to_tf32(f[u].y); l.y = to_tf32(f[u].y - h.y);
+                h.z = to_tf32(f[u].z); l.z = to_tf32(f[u].z - h.z);
+                h.w = to_tf32(f[u].w); l.w = to_tf32(f[u].w - h.w);
                 for (int s = 0; s < k; ++s) {
                     const size_t row = (size_t)s_dest[t * k + s];
                     reinterpret_cast<float4*>(a_hi)[row * nv + v] = h;
@@ -335,7 +381,7 @@ template <int EJ, int KC>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
                             float* wts, int* blockhist, cudaStream_t s) {
     const int E = L.E;
-    const size_t smem = sizeof(float) * (3 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4)) +
+    const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4)) +
                                          kRouteTokens * (E + 1)) +
                         sizeof(int) * E;
     auto kern = router_kernel<EJ, KC>;
@@ -365,7 +411,7 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
     const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     const Workspace& W = L.ws;
-    dispatch_scan_kernel<<<1, kMaxExperts, 0, s>>>(W.blockhist, nblk, L.E, W.counts, W.eoff,
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(W.blockhist, nblk, L.E, W.counts, W.eoff,
                                                   W.mtiles, W.num_mtiles, W.row_token,
                                                   W.row_weight);
     return cudaGetLastError();
