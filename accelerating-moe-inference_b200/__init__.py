@@ -37,7 +37,7 @@ EXPORTED_SYMBOLS = (
     "moe_create_from_model_bin", "moe_destroy", "moe_get_config", "moe_device_bytes",
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
     "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
-    "moe_dispatch_noalloc",
+    "moe_dispatch_noalloc", "moe_route_host", "moe_host_alloc", "moe_host_free",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
 
@@ -101,6 +101,9 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_dispatch_layout.argtypes = [vp, _i32p, _f32p, ctypes.c_int32, _i32p, _i32p]
     L.moe_profile_enable.argtypes = [vp, ctypes.c_int]
     L.moe_profile_read.argtypes = [vp, _f32p, ctypes.c_int32]
+    L.moe_route_host.argtypes = [vp, _f32p, ctypes.c_int32, _f32p, _i32p, _f32p]
+    L.moe_host_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.moe_host_free.argtypes = [vp]
     L.moe_dispatch_noalloc.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        vp, vp, ctypes.c_int32, vp, vp, vp]
     if path is None:
@@ -321,6 +324,17 @@ class MoeLayer:
                                                ctypes.c_void_p(logits_ptr),
                                                ctypes.c_void_p(idx_ptr), ctypes.c_void_p(w_ptr),
                                                ctypes.c_void_p(stream)))
+
+    def route_host(self, x: np.ndarray):
+        """(logits [T][E], idx [T][k], weights [T][k]) of host x."""
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        lg = np.empty((T, self.E), np.float32)
+        idx = np.empty((T, self.k), np.int32)
+        w = np.empty((T, self.k), np.float32)
+        _check(load_library().moe_route_host(self._h, _fp(x), T, _fp(lg),
+                                             idx.ctypes.data_as(_i32p), _fp(w)))
+        return lg, idx, w
 
     def expert_counts(self) -> np.ndarray:
         c = np.zeros(self.E, np.int32)

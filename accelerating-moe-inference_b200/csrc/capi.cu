@@ -86,7 +86,7 @@ void free_workspace(Workspace& W) {
     free_ptr(W.counts); free_ptr(W.eoff); free_ptr(W.mtiles); free_ptr(W.num_mtiles);
     free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.a_hi); free_ptr(W.a_lo);
     free_ptr(W.h_hi); free_ptr(W.h_lo); free_ptr(W.x_stage); free_ptr(W.y_stage);
-    free_ptr(W.dev_err);
+    free_ptr(W.dev_err); free_ptr(W.h_dec); free_ptr(W.dec_counter);
     W = Workspace{};
 }
 
@@ -120,6 +120,9 @@ int ensure_workspace(Layer& L, int T) {
         MOE_CUDA(dalloc(&W.a_lo, 4 * cap_rows * L.d, &bytes));
         MOE_CUDA(dalloc(&W.h_lo, 4 * cap_rows * L.ffp, &bytes));
     }
+    MOE_CUDA(dalloc(&W.h_dec, sizeof(float) * (size_t)decode_max_supported_tokens() * k * L.ffp,
+                    &bytes));
+    MOE_CUDA(dalloc(&W.dec_counter, 2 * sizeof(int), &bytes));
     MOE_CUDA(dalloc(&W.dev_err, sizeof(int), &bytes));
     MOE_CUDA(cudaMemset(W.dev_err, 0, sizeof(int)));
     MOE_CUDA(cudaMemset(W.num_mtiles, 0, sizeof(int)));
@@ -171,7 +174,8 @@ int validate_config(const MoeConfig& c) {
         return fail(MOE_ERR_INVALID, "router_quantum must be positive");
     if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16)
         return fail(MOE_ERR_INVALID, "unknown precision");
-    if (c.decode_max_tokens < 0) return fail(MOE_ERR_INVALID, "decode_max_tokens < 0");
+    if (c.decode_max_tokens < 0 || c.decode_max_tokens > decode_max_supported_tokens())
+        return fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
     if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
     return MOE_OK;
 }
@@ -203,9 +207,8 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     MOE_CUDA(launch_dispatch_scan(L, T, s));
     prof_mark(L, 2, s);
     if (T <= L.cfg.decode_max_tokens) {
-        MOE_CUDA(launch_decode(L, x, T, y, s));  // marks stage 3 between its kernels
-        prof_mark(L, 4, s);
-        if (L.profile) L.prof_ran[4] = false;
+        MOE_CUDA(launch_decode(L, x, T, y, s));  // marks stages 3 and 4 between its kernels
+        prof_mark(L, kProfileStages, s);
         return MOE_OK;
     }
     MOE_CUDA(launch_dispatch_permute(L, x, T, s));
@@ -321,7 +324,7 @@ void moe_config_init(MoeConfig* c) {
     c->precision = MOE_PREC_FP32;
     c->router_quantum = 1.0e-3f;
     c->router_tie_eps = 2.0e-2f;
-    c->decode_max_tokens = 0;
+    c->decode_max_tokens = 16;
     c->device = 0;
     c->max_tokens = 0;
 }
@@ -536,7 +539,8 @@ size_t moe_device_bytes(const MoeHandle* h) {
 }
 
 int moe_set_decode_max_tokens(MoeHandle* h, int32_t n) {
-    if (!h || n < 0) return moe::fail(MOE_ERR_INVALID, "bad argument");
+    if (!h || n < 0 || n > moe::decode_max_supported_tokens())
+        return moe::fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
     h->L.cfg.decode_max_tokens = n;
     return MOE_OK;
 }
@@ -620,6 +624,50 @@ int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int
     // The scan reads the histogram the router just wrote, so counts and the
     // layout queries below describe this call.
     MOE_CUDA(launch_dispatch_scan(L, T, s));
+    return MOE_OK;
+}
+
+int moe_route_host(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
+                   float* weights) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
+    if (T == 0) return MOE_OK;
+    if (!x || !idx || !weights) return fail(MOE_ERR_INVALID, "null argument");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    int rc = ensure_stage(L, T);
+    if (rc) return rc;
+    cudaStream_t s = h->own_stream;
+    Workspace& W = L.ws;
+    MOE_CUDA(cudaMemcpyAsync(W.x_stage, x, sizeof(float) * (size_t)T * L.d, cudaMemcpyHostToDevice, s));
+    L.last_stream = s;
+    L.last_T = T;
+    MOE_CUDA(launch_router(L, W.x_stage, T, W.logits, W.idx, W.wts, W.blockhist, s));
+    MOE_CUDA(launch_dispatch_scan(L, T, s));
+    if (logits)
+        MOE_CUDA(cudaMemcpyAsync(logits, W.logits, sizeof(float) * (size_t)T * L.E,
+                                 cudaMemcpyDeviceToHost, s));
+    MOE_CUDA(cudaMemcpyAsync(idx, W.idx, sizeof(int) * (size_t)T * L.k, cudaMemcpyDeviceToHost, s));
+    MOE_CUDA(cudaMemcpyAsync(weights, W.wts, sizeof(float) * (size_t)T * L.k,
+                             cudaMemcpyDeviceToHost, s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+    return check_device_errors(L);
+}
+
+int moe_host_alloc(size_t bytes, void** out) {
+    using namespace moe;
+    if (!out) return fail(MOE_ERR_INVALID, "null argument");
+    *out = nullptr;
+    cudaError_t e = cudaHostAlloc(out, bytes ? bytes : 1, cudaHostAllocDefault);
+    if (e != cudaSuccess) return fail(MOE_ERR_OOM, std::string("cudaHostAlloc: ") + cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+int moe_host_free(void* p) {
+    using namespace moe;
+    if (!p) return MOE_OK;
+    MOE_CUDA(cudaFreeHost(p));
     return MOE_OK;
 }
 

@@ -1,0 +1,151 @@
+// MoE layer classes of the drop-in (include/layer.h) over the C ABI.
+#include "layer.h"
+
+#include <stdexcept>
+#include <string>
+
+namespace {
+
+[[noreturn]] void throw_status(int rc, const char* what) {
+    const std::string msg = std::string(what) + ": " + moe_last_error();
+    if (rc == MOE_ERR_INVALID) throw std::invalid_argument(msg);
+    throw std::runtime_error(msg);
+}
+
+std::shared_ptr<MoeHandle> make_handle(const MoeConfig& cfg, const Tensor& gate,
+                                       const Tensor* bias, const std::vector<Tensor>& w1,
+                                       const std::vector<Tensor>& w3,
+                                       const std::vector<Tensor>& w2) {
+    std::vector<const float*> p1, p2, p3;
+    for (std::size_t e = 0; e < w1.size(); ++e) {
+        p1.push_back(w1[e].data());
+        p2.push_back(w2[e].data());
+        p3.push_back(w3[e].data());
+    }
+    MoeWeightsHost w{};
+    w.router_weight = gate.data();
+    w.router_bias = bias ? bias->data() : nullptr;
+    w.w1 = p1.data();
+    w.w2 = p2.data();
+    w.w3 = p3.data();
+    MoeHandle* h = nullptr;
+    const int rc = moe_create(&cfg, &w, &h);
+    if (rc != MOE_OK) throw_status(rc, "moe_create");
+    return std::shared_ptr<MoeHandle>(h, moe_destroy);
+}
+
+void check_2d(const Tensor& x, std::size_t d) {
+    if (x.ndim() != 2 || x.size(1) != d) throw std::invalid_argument("MoE input shape");
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- Linear
+Linear::Linear(const ModelLoader& loader, const std::string& weight, const std::string& bias)
+    : weight_(loader.load(weight)) {
+    if (!bias.empty() && loader.has(bias)) bias_ = loader.load(bias);
+}
+
+void Linear::forward(const Tensor& x, Tensor& y) const {
+    const std::size_t in = x.size(x.ndim() - 1), rows = x.size() / in;
+    Tensor flat = x;
+    flat.reshape({rows, in});
+    y = Tensor({rows, weight_.size(0)});
+    tensor_ops::matmul_transposed(flat, weight_, y);
+    if (bias_.size()) tensor_ops::add_bias_inplace(y, bias_);
+}
+
+// ---------------------------------------------------------------- PhiMLP
+// One expert is a layer with a single expert, top-1 softmax routing and an
+// all-zero router: every token goes to expert 0 with weight exactly 1.
+PhiMLP::PhiMLP(const ModelLoader& loader, const std::string& prefix, int precision, int device) {
+    std::vector<Tensor> w1, w2, w3;
+    w1.push_back(loader.load(prefix + ".w1.weight"));
+    w2.push_back(loader.load(prefix + ".w2.weight"));
+    w3.push_back(loader.load(prefix + ".w3.weight"));
+    d_ = w1[0].size(1);
+    MoeConfig cfg;
+    moe_config_init(&cfg);
+    cfg.d_model = static_cast<int32_t>(d_);
+    cfg.d_ff = static_cast<int32_t>(w1[0].size(0));
+    cfg.num_experts = 1;
+    cfg.top_k = 1;
+    cfg.router_policy = MOE_ROUTER_SOFTMAX_TOPK;
+    cfg.precision = precision;
+    cfg.device = device;
+    Tensor gate({1, d_});
+    h_ = make_handle(cfg, gate, nullptr, w1, w3, w2);
+}
+
+void PhiMLP::forward(const Tensor& x, Tensor& y) const {
+    const std::size_t rows = x.size() / x.size(x.ndim() - 1);
+    if (x.size(x.ndim() - 1) != d_) throw std::invalid_argument("PhiMLP input shape");
+    Tensor out(x.shape());
+    const int rc = moe_forward_host(h_.get(), x.data(), out.data(), static_cast<int32_t>(rows));
+    if (rc != MOE_OK) throw_status(rc, "PhiMLP::forward");
+    y = std::move(out);
+}
+
+// ---------------------------------------------------------------- PhiMoE
+namespace {
+MoeConfig reference_config() {
+    MoeConfig c;
+    moe_config_init(&c);
+    c.d_model = c.d_ff = c.num_experts = 0;  // taken from the file
+    return c;
+}
+}  // namespace
+
+PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx)
+    : PhiMoE(loader, layer_idx, reference_config()) {}
+
+PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg_in) {
+    const std::string base = "model.layers." + std::to_string(layer_idx) + ".block_sparse_moe";
+    Tensor gate = loader.load(base + ".gate.weight");
+    if (gate.ndim() != 2) throw std::runtime_error("router weight is not 2-D: " + base);
+    MoeConfig cfg = cfg_in;
+    if (cfg.num_experts == 0) {
+        int e = 0;
+        while (loader.has(base + ".experts." + std::to_string(e) + ".w1.weight")) ++e;
+        cfg.num_experts = e;
+    }
+    if (cfg.d_model == 0) cfg.d_model = static_cast<int32_t>(gate.size(1));
+    std::vector<Tensor> w1, w2, w3;
+    for (int e = 0; e < cfg.num_experts; ++e) {
+        const std::string pre = base + ".experts." + std::to_string(e);
+        w1.push_back(loader.load(pre + ".w1.weight"));
+        w2.push_back(loader.load(pre + ".w2.weight"));
+        w3.push_back(loader.load(pre + ".w3.weight"));
+    }
+    if (cfg.d_ff == 0 && !w1.empty()) cfg.d_ff = static_cast<int32_t>(w1[0].size(0));
+    Tensor bias;
+    const bool has_bias = loader.has(base + ".gate.bias");
+    if (has_bias) bias = loader.load(base + ".gate.bias");
+    h_ = make_handle(cfg, gate, has_bias ? &bias : nullptr, w1, w3, w2);
+    moe_get_config(h_.get(), &cfg_);
+}
+
+void PhiMoE::forward(const Tensor& x, Tensor& y) const {
+    check_2d(x, static_cast<std::size_t>(cfg_.d_model));
+    Tensor out({x.size(0), x.size(1)});
+    const int rc = moe_forward_host(h_.get(), x.data(), out.data(), static_cast<int32_t>(x.size(0)));
+    if (rc != MOE_OK) throw_status(rc, "PhiMoE::forward");
+    y = std::move(out);
+}
+
+void PhiMoE::forward_device(const float* x_dev, float* y_dev, std::size_t rows, void* stream) const {
+    const int rc = moe_forward_device(h_.get(), x_dev, y_dev, static_cast<int32_t>(rows), stream);
+    if (rc != MOE_OK) throw_status(rc, "PhiMoE::forward_device");
+}
+
+void PhiMoE::route(const Tensor& x, std::vector<std::pair<int, float>>& routes) const {
+    check_2d(x, static_cast<std::size_t>(cfg_.d_model));
+    const std::size_t rows = x.size(0), k = static_cast<std::size_t>(cfg_.top_k);
+    std::vector<int32_t> idx(rows * k);
+    std::vector<float> w(rows * k);
+    const int rc = moe_route_host(h_.get(), x.data(), static_cast<int32_t>(rows), nullptr,
+                                  idx.data(), w.data());
+    if (rc != MOE_OK) throw_status(rc, "PhiMoE::route");
+    routes.clear();
+    for (std::size_t i = 0; i < rows * k; ++i) routes.emplace_back(idx[i], w[i]);
+}

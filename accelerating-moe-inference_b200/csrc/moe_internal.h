@@ -72,6 +72,8 @@ struct Workspace {
     float* x_stage = nullptr;   // host-API staging, [cap_T][d]
     float* y_stage = nullptr;
     int* dev_err = nullptr;     // device-side error flags (timeouts)
+    float* h_dec = nullptr;     // decode-path H, fp32 [64 * k][ffp]
+    int* dec_counter = nullptr; // decode-path work counters [2]
     CUtensorMap tm_a_hi, tm_a_lo, tm_h_hi, tm_h_lo;
     size_t bytes = 0;
 };
@@ -112,14 +114,18 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
                           float* wts, int* blockhist, cudaStream_t s);
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s);
+// The same placement with the rows copied in the decode kernels' format:
+// fp32 as is (FP32 precision) or bf16 (BF16 precision).
+cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s);
 
 // expert_gemm.cu
 // down == false: gate/up GEMM with the SwiGLU epilogue into H;
 // down == true:  down GEMM with the weighted-combine epilogue into y.
 cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down);
 
-// decode.cu
+// decode.cu: T <= decode_max_supported_tokens() (64)
 cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s);
+int decode_max_supported_tokens();
 
 // weights.cu
 cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const float* w3_dev,

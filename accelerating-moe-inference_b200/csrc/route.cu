@@ -112,7 +112,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         const int st = c % kStages;
         const float* xr = xs + st * kXs + tt * kLd;
         const float* wr = ws + st * kWs;
-#pragma unroll 4
+#pragma unroll 8
         for (int kk = 0; kk < KC; kk += 4) {
             const float4 xv = *reinterpret_cast<const float4*>(xr + kk);
 #pragma unroll
@@ -302,7 +302,7 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restri
     }
 }
 
-template <int kMode>  // 0: bf16 plane, 1: tf32 hi + lo planes
+template <int kMode>  // 0: bf16 plane, 1: tf32 hi + lo planes, 2: fp32 as is (decode)
 __global__ void __launch_bounds__(256)
 dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                         const int* __restrict__ idx, const float* __restrict__ wts,
@@ -361,6 +361,11 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                     const size_t row = (size_t)s_dest[t * k + s];
                     reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
                 }
+            } else if constexpr (kMode == 2) {
+                for (int s = 0; s < k; ++s) {
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<float4*>(a_hi)[row * nv + v] = f[u];
+                }
             } else {
                 float4 h, l;
                 h.x = to_tf32(f[u].x); l.x = to_tf32(f[u].x - h.x);
@@ -399,7 +404,20 @@ cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits
 
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
                           float* wts, int* blockhist, cudaStream_t s) {
+    // K chunk per pipeline stage: as wide as shared memory allows, so each
+    // SM keeps 100-200 KB of x / wg loads in flight (the dot-product chains
+    // themselves are serial and cannot be split).
     const int ej = (L.E + 7) / 8;
+    if (L.d % 256 == 0) {
+        if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s);
+    }
+    if (L.d % 128 == 0) {
+        if (ej <= 1) return launch_router_t<1, 128>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 2) return launch_router_t<2, 128>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 4) return launch_router_t<4, 128>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 8) return launch_router_t<8, 128>(L, x, T, logits, idx, wts, blockhist, s);
+    }
     if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s);
     if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s);
     if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s);
@@ -414,6 +432,20 @@ cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
     dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(W.blockhist, nblk, L.E, W.counts, W.eoff,
                                                   W.mtiles, W.num_mtiles, W.row_token,
                                                   W.row_weight);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s) {
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
+    const Workspace& W = L.ws;
+    if (three_pass(L))
+        dispatch_permute_kernel<2><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, W.a_lo);
+    else
+        dispatch_permute_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, W.a_lo);
     return cudaGetLastError();
 }
 

@@ -52,6 +52,7 @@ WORKLOADS = {
                     seed=1),
 }
 KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
+DECODE_T = (1, 8, 32, 64)
 FLUSH_BYTES = 256 << 20
 
 
@@ -234,6 +235,9 @@ def main():
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--decode-max-tokens", type=int, default=None,
+                    help="override the handle's decode threshold (0..64)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -268,7 +272,7 @@ def main():
     layer = pkg.MoeLayer.from_device_pointers(
         d, ff, E, wg.data_ptr(), [t.data_ptr() for t in w1], [t.data_ptr() for t in w3],
         [t.data_ptr() for t in w2], top_k=k, policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec,
-        device=local, max_tokens=T)
+        device=local, max_tokens=T, decode_max_tokens=args.decode_max_tokens)
     host_layer = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host_layer = pkg.LayerWeights(wg.cpu().numpy(), [t.cpu().numpy() for t in w1],
@@ -311,6 +315,41 @@ def main():
     if world > 1:
         dist.barrier()
     total_ms = sum(a.elapsed_time(b) for a, b in ev)
+
+    # ---- decode: the same layer at T in DECODE_T, HBM GB/s
+    decode = {}
+    if not args.no_decode:
+        hbm = _peaks()[0]
+        dec_T = [t for t in DECODE_T if t <= T]
+        for td in dec_T:
+            xt = x[:td]
+            yt = y[:td]
+            for _ in range(args.warmup):
+                layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)
+                flush.zero_()
+            torch.cuda.synchronize()
+            tot, n = 0.0, max(5, args.steps)
+            st_d = np.zeros(len(pkg.PROFILE_STAGES))
+            for _ in range(n):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)
+                b.record(stream)
+                st_d += layer.stage_ms()
+                flush.zero_()
+                b.synchronize()
+                tot += a.elapsed_time(b)
+            ms_d = tot / n
+            active = int((layer.expert_counts() > 0).sum())
+            wbytes = 2 if args.precision == "bf16" else 4
+            alg = active * 3 * d * ff * wbytes + E * d * 4 + 2 * td * d * 4
+            gbs = alg / (ms_d / 1e3) / 1e9
+            path = "decode kernels" if td <= layer.cfg.decode_max_tokens else "grouped GEMM"
+            decode[str(td)] = {"ms": ms_d, "tokens_per_s": td / (ms_d / 1e3),
+                               "experts_streamed": active, "algorithmic_bytes": alg,
+                               "hbm_gbs": gbs, "frac_of_hbm": gbs / hbm, "path": path,
+                               "stages_ms": {nm: float(v) / n
+                                             for nm, v in zip(pkg.PROFILE_STAGES, st_d)}}
 
     # ---- e2e through the host-buffer C-ABI call (pinned buffers)
     xh = x.cpu().pin_memory()
@@ -371,6 +410,8 @@ def main():
                     "d2h_bytes_per_step": T * d * 4,
                     "how": "moe_forward_host on pinned host buffers, host clock around the "
                            "synchronous call"},
+            "decode": {"hbm_peak_gbs": _peaks()[0], "by_T": decode,
+                       "bytes": "routed experts x 3 x d x d_ff x weight bytes + router + x/y"},
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clocks,
             "output_finite": ok_y,

@@ -1,0 +1,76 @@
+// layer.h -- the MoE layer classes of the drop-in, over libmoe_b200.so.
+//
+// Mirrors the reference's include/layer.h:11-36 (songsnim/accelerating-MoE-
+// inference) for the MoE hot path:
+//   Linear   y = x W^T (+ b)                    host, reference arithmetic
+//   PhiMLP   SwiGLU expert, src/layer.cu:32-45  on the GPU (a 1-expert layer)
+//   PhiMoE   router + experts + combine,        on the GPU
+//            src/layer.cu:80-103
+// Constructors take the same (ModelLoader, index / prefix) arguments and load
+// the same tensor names; forward(const Tensor& x, Tensor& y) allocates y like
+// the reference does.  Errors keep the reference's exception types:
+// std::invalid_argument for shape mismatches, std::runtime_error for I/O and
+// device failures (carrying moe_last_error()).
+//
+// PhiAttention and PhiDecoderLayer (attention, layer norm) are not part of
+// this library's path and are not declared here.
+//
+// Layers share their device handle between copies; a handle runs one forward
+// at a time, so copies must not run forward concurrently.
+#pragma once
+
+#include "model_loader.h"
+#include "moe_b200.h"
+#include "tensor.h"
+
+#include <cstddef>
+#include <memory>
+#include <string>
+#include <utility>
+#include <vector>
+
+class Linear {
+public:
+    Linear() = default;
+    Linear(const ModelLoader& loader, const std::string& weight, const std::string& bias = "");
+    void forward(const Tensor& x, Tensor& y) const;
+
+private:
+    Tensor weight_;
+    Tensor bias_;
+};
+
+class PhiMLP {
+public:
+    PhiMLP(const ModelLoader& loader, const std::string& prefix, int precision = MOE_PREC_FP32,
+           int device = 0);
+    void forward(const Tensor& x, Tensor& y) const;
+
+private:
+    std::shared_ptr<MoeHandle> h_;
+    std::size_t d_ = 0;
+};
+
+class PhiMoE {
+public:
+    // The reference's configuration: its quantised top-2 router
+    // (include/config.h:13-23), expert count and sizes taken from the file,
+    // fp32-faithful expert arithmetic.
+    PhiMoE(const ModelLoader& loader, std::size_t layer_idx);
+    // Any configuration; zero d_model / d_ff / num_experts come from the file.
+    PhiMoE(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg);
+
+    void forward(const Tensor& x, Tensor& y) const;
+    // Device-resident variant for an engine that keeps activations on the GPU
+    // (the reference's DeviceMoE segment, src/model.cu:1976-2019).
+    void forward_device(const float* x_dev, float* y_dev, std::size_t rows,
+                        void* stream = nullptr) const;
+    // Expert indices / weights [rows][top_k] of x (host), in selection order.
+    void route(const Tensor& x, std::vector<std::pair<int, float>>& routes) const;
+
+    const MoeConfig& config() const { return cfg_; }
+
+private:
+    std::shared_ptr<MoeHandle> h_;
+    MoeConfig cfg_{};
+};

@@ -77,7 +77,7 @@ typedef struct MoeConfig {
     float router_quantum;   /* PHI policy score quantum (reference 1e-3, include/config.h:22) */
     float router_tie_eps;   /* PHI policy tie margin (reference 2e-2, include/config.h:23) */
     int32_t decode_max_tokens; /* T <= this takes the weight-streaming decode kernels
-                                  (0: never; default 16) */
+                                  (0..64; 0: never; default 16) */
     int32_t device;         /* CUDA device ordinal the handle lives on */
     int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
     int32_t reserved[5];
@@ -150,6 +150,18 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T);
 int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
                      float* weights, void* stream);
 
+/* Router only, host buffers (copies x in, synchronises): logits [T][E] (may
+ * be NULL), expert indices and weights [T][top_k].  The host-side view of
+ * PhiMoE::route (src/layer.cu:47-70) over a whole batch. */
+int moe_route_host(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
+                   float* weights);
+
+/* Page-locked host memory for host-side tensors (the reference's
+ * Tensor::Alloc::Pinned, src/tensor.cu:11-29), so moe_forward_host's copies
+ * run at full link speed.  Free with moe_host_free. */
+int moe_host_alloc(size_t bytes, void** out);
+int moe_host_free(void* p);
+
 /* Per-expert row counts [E] of the last forward or route on this handle
  * (synchronises the handle's last stream).  The dispatch histogram of
  * src/model.cu:921-1003. */
@@ -168,8 +180,9 @@ int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int
  * records a CUDA event on its stream at each stage boundary (no host
  * synchronisation).  moe_profile_read synchronises on the last event and
  * writes the milliseconds of each stage of the last forward:
- *   [0] router  [1] dispatch scan  [2] dispatch permute (or decode gate/up)
- *   [3] gate/up grouped GEMM (or decode down)  [4] down grouped GEMM
+ *   [0] router  [1] dispatch scan  [2] dispatch permute
+ *   [3] gate/up grouped GEMM (decode path: decode gate/up kernel)
+ *   [4] down grouped GEMM (decode path: decode down kernel)
  * Stages a forward did not run read 0.  Returns the number of stages (5). */
 #define MOE_PROFILE_STAGES 5
 int moe_profile_enable(MoeHandle* h, int enable);

@@ -1,0 +1,141 @@
+// Drives the drop-in C++ layer the way the reference's code uses its own
+// classes (include/layer.h, include/model_loader.h, include/tensor.h):
+//
+//   test_phimoe errors <dir>                       exception types, no GPU
+//   test_phimoe forward <model.bin> <x.bin> <T> <d> <out_prefix>
+//       PhiMoE(loader, 0).forward(x, y)  -> <out_prefix>.moe.bin
+//       PhiMLP(loader, "...experts.0")   -> <out_prefix>.mlp.bin
+//       PhiMoE::route                    -> <out_prefix>.route.bin (int idx, float w)
+//       a wrong-width input must throw std::invalid_argument
+#include "layer.h"
+#include "model_loader.h"
+#include "tensor.h"
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+static int failures = 0;
+#define CHECK(cond, msg)                                  \
+    do {                                                  \
+        if (!(cond)) {                                    \
+            std::fprintf(stderr, "FAIL: %s\n", msg);      \
+            ++failures;                                   \
+        }                                                 \
+    } while (0)
+
+template <typename Ex, typename F>
+static bool throws(F f, const char* needle) {
+    try {
+        f();
+    } catch (const Ex& e) {
+        return std::strstr(e.what(), needle) != nullptr;
+    } catch (...) {
+        return false;
+    }
+    return false;
+}
+
+static void write_file(const std::string& p, const void* data, size_t n) {
+    std::ofstream f(p, std::ios::binary);
+    f.write(static_cast<const char*>(data), static_cast<std::streamsize>(n));
+}
+
+static int errors(const std::string& dir) {
+    CHECK(throws<std::runtime_error>([&] { ModelLoader l(dir + "/does_not_exist.bin"); },
+                                     "cannot open model"),
+          "missing file");
+    {
+        const std::string p = dir + "/trunc.bin";
+        const unsigned char bytes[6] = {3, 0, 0, 0, 9, 0};
+        write_file(p, bytes, sizeof bytes);
+        CHECK(throws<std::runtime_error>([&] { ModelLoader l(p); }, "truncated model.bin"),
+              "truncated index");
+    }
+    {
+        const std::string p = dir + "/empty.bin";
+        const unsigned char zero[4] = {0, 0, 0, 0};
+        write_file(p, zero, sizeof zero);
+        ModelLoader l(p);
+        CHECK(!l.has("x"), "has() on an empty index");
+        CHECK(throws<std::runtime_error>([&] { l.load("model.layers.0.block_sparse_moe.gate.weight"); },
+                                         "missing tensor"),
+              "missing tensor");
+        CHECK(throws<std::runtime_error>([&] { PhiMoE m(l, 0); }, "missing tensor"),
+              "PhiMoE on a file without the layer");
+    }
+    Tensor t({2, 3});
+    CHECK(throws<std::out_of_range>([&] { t.at(2, 0); }, "Tensor index"), "at() bounds");
+    CHECK(throws<std::invalid_argument>([&] { t.at(1); }, "rank"), "at() rank");
+    CHECK(throws<std::invalid_argument>([&] { t.reshape({4, 2}); }, "reshape"), "reshape size");
+    Tensor a({2, 4}), b({3, 4}), c({2, 3});
+    for (size_t i = 0; i < a.size(); ++i) a[i] = 0.5f * float(i);
+    for (size_t i = 0; i < b.size(); ++i) b[i] = 0.25f * float(i) - 1.0f;
+    tensor_ops::matmul_transposed(a, b, c);
+    CHECK(c.at(1, 2) == 0.5f * (4 * 1.0f + 5 * 1.25f + 6 * 1.5f + 7 * 1.75f), "matmul_transposed");
+    Tensor bad({2, 5});
+    CHECK(throws<std::invalid_argument>([&] { tensor_ops::matmul_transposed(bad, b, c); },
+                                        "matmul_transposed shape"),
+          "matmul shape");
+    std::printf("%s\n", failures ? "errors: FAILED" : "errors: ok");
+    return failures ? 1 : 0;
+}
+
+static int forward(const std::string& model, const std::string& xpath, size_t T, size_t d,
+                   const std::string& out) {
+    ModelLoader loader(model);
+    PhiMoE moe(loader, 0);
+    Tensor x({T, d});
+    {
+        std::ifstream f(xpath, std::ios::binary);
+        f.read(reinterpret_cast<char*>(x.data()), static_cast<std::streamsize>(T * d * 4));
+        if (!f) throw std::runtime_error("cannot read x");
+    }
+    Tensor y;
+    moe.forward(x, y);
+    CHECK(y.ndim() == 2 && y.size(0) == T && y.size(1) == d, "PhiMoE output shape");
+    write_file(out + ".moe.bin", y.data(), y.size() * 4);
+
+    PhiMLP mlp(loader, "model.layers.0.block_sparse_moe.experts.0");
+    Tensor ym;
+    mlp.forward(x, ym);
+    write_file(out + ".mlp.bin", ym.data(), ym.size() * 4);
+
+    std::vector<std::pair<int, float>> routes;
+    moe.route(x, routes);
+    std::vector<int> idx;
+    std::vector<float> w;
+    for (auto& r : routes) {
+        idx.push_back(r.first);
+        w.push_back(r.second);
+    }
+    write_file(out + ".route_idx.bin", idx.data(), idx.size() * 4);
+    write_file(out + ".route_w.bin", w.data(), w.size() * 4);
+
+    Tensor wrong({T, d + 64});
+    CHECK(throws<std::invalid_argument>([&] { Tensor yy; moe.forward(wrong, yy); }, "shape"),
+          "wrong width input");
+    Tensor pinned({T, d}, Tensor::Alloc::Pinned);
+    std::memcpy(pinned.data(), x.data(), T * d * 4);
+    Tensor yp;
+    moe.forward(pinned, yp);
+    CHECK(std::memcmp(yp.data(), y.data(), T * d * 4) == 0, "pinned input gives the same y");
+    std::printf("%s\n", failures ? "forward: FAILED" : "forward: ok");
+    return failures ? 1 : 0;
+}
+
+int main(int argc, char** argv) {
+    try {
+        if (argc >= 3 && std::string(argv[1]) == "errors") return errors(argv[2]);
+        if (argc >= 7 && std::string(argv[1]) == "forward")
+            return forward(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "uncaught: %s\n", e.what());
+        return 2;
+    }
+    std::fprintf(stderr, "usage: test_phimoe errors <dir> | forward <model> <x> <T> <d> <out>\n");
+    return 2;
+}

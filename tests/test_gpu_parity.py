@@ -169,3 +169,42 @@ def test_forward_device_on_torch_stream():
             m.forward_device(xd.data_ptr(), yd.data_ptr(), x.shape[0], s.cuda_stream)
         s.synchronize()
         assert rel_l2(yd.cpu().numpy(), g["phi_y"]) <= 1e-3
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("T", [1, 2, 5, 8, 16, 33, 64])
+def test_decode_path_matches_oracle(T, precision, orc):
+    """The weight-streaming decode kernels (T <= decode_max_tokens)."""
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(31, 512, 448, 8)   # d_ff 448: padded K chunk
+    x = pkg.synthetic_tokens(31, T, 512)
+    y_ref, *_ = orc.moe_forward(x, layer, 2, oracle.POLICY_SOFTMAX)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision,
+                      decode_max_tokens=64) as m:
+        y = m.forward_host(x)
+    assert rel_l2(y, y_ref) <= TOL[precision]
+    if precision == 0:
+        assert ref_elementwise_failures(y, y_ref) == 0
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_decode_and_prefill_paths_agree(precision):
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, "c5mini")      # 64 experts, top-8, router bias
+    with pkg.MoeLayer(layer, top_k=8, policy=1, precision=precision,
+                      decode_max_tokens=64) as m:
+        y_dec = m.forward_host(x)
+        m.set_decode_max_tokens(0)
+        y_pre = m.forward_host(x)
+    g = np.load(GOLDEN_DIR / "c5mini.npz")
+    assert rel_l2(y_dec, g["soft_y"]) <= TOL[precision]
+    assert rel_l2(y_pre, g["soft_y"]) <= TOL[precision]
+    assert rel_l2(y_dec, y_pre) <= TOL[precision]
+
+
+def test_decode_threshold_bounds():
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(1, 64, 64, 4)
+    with pkg.MoeLayer(layer, top_k=2, policy=1) as m:
+        with pytest.raises(pkg.MoeError):
+            m.set_decode_max_tokens(65)
