@@ -80,15 +80,15 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     // Stage loader: x chunk is 32 rows x KC floats, wg chunk E rows x KC.
     auto load_chunk = [&](int chunk, int stage) {
         const int kbase = chunk * KC;
-        constexpr int kXv = kRouteTokens * KC / 4;  // float4 per x chunk
-        for (int v = tid; v < kXv; v += kRouterThreads) {
+        const int kXv = (blockDim.x / 8) * KC / 4;   // float4 per x chunk (tokens this CTA runs)
+        for (int v = tid; v < kXv; v += blockDim.x) {
             const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
             const bool ok = r < n_tok;
             const float* src = x + (size_t)(ok ? t0 + r : 0) * d + kbase + c;
             cp_async16(xs + stage * kXs + r * kLd + c, src, ok);
         }
         const int wv = E * KC / 4;
-        for (int v = tid; v < wv; v += kRouterThreads) {
+        for (int v = tid; v < wv; v += blockDim.x) {
             const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
             cp_async16(ws + stage * kWs + r * kLd + c, wg + (size_t)r * d + kbase + c, true);
         }
@@ -111,26 +111,56 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         cp_async_commit();
         const int st = c % kStages;
         const float* xr = xs + st * kXs + tt * kLd;
-        const float* wr = ws + st * kWs;
-#pragma unroll 8
-        for (int kk = 0; kk < KC; kk += 4) {
-            const float4 xv = *reinterpret_cast<const float4*>(xr + kk);
+        const float* wr = ws + st * kWs + el * kLd;
+        // Fully unrolled over the chunk, every shared-memory offset an
+        // immediate, and the operands of the next 16-wide group loaded while
+        // the current group's FMAs run (the chain itself cannot overlap).
+        // Lanes whose expert index is past E run chains on unused rows that
+        // are never stored.
+        float4 xa[4], wa[EJ][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xa[q] = *reinterpret_cast<const float4*>(xr + 4 * q);
+#pragma unroll
+        for (int j = 0; j < EJ; ++j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                wa[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + 4 * q);
+#pragma unroll
+        for (int kk = 0; kk < KC; kk += 16) {
+            float4 xb[4], wb[EJ][4];
+            if (kk + 16 < KC) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    xb[q] = *reinterpret_cast<const float4*>(xr + kk + 16 + 4 * q);
+#pragma unroll
+                for (int j = 0; j < EJ; ++j)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        wb[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 16 + 4 * q);
+            }
 #pragma unroll
             for (int j = 0; j < EJ; ++j) {
-                const int e = el + 8 * j;
-                if (e < E) {
-                    const float4 wv = *reinterpret_cast<const float4*>(wr + e * kLd + kk);
-                    acc[j] = __fmaf_rn(xv.x, wv.x, acc[j]);
-                    acc[j] = __fmaf_rn(xv.y, wv.y, acc[j]);
-                    acc[j] = __fmaf_rn(xv.z, wv.z, acc[j]);
-                    acc[j] = __fmaf_rn(xv.w, wv.w, acc[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    acc[j] = __fmaf_rn(xa[q].x, wa[j][q].x, acc[j]);
+                    acc[j] = __fmaf_rn(xa[q].y, wa[j][q].y, acc[j]);
+                    acc[j] = __fmaf_rn(xa[q].z, wa[j][q].z, acc[j]);
+                    acc[j] = __fmaf_rn(xa[q].w, wa[j][q].w, acc[j]);
                 }
+            }
+            if (kk + 16 < KC) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) xa[q] = xb[q];
+#pragma unroll
+                for (int j = 0; j < EJ; ++j)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) wa[j][q] = wb[j][q];
             }
         }
     }
     cp_async_wait<0>();
 
-    for (int e = tid; e < E; e += kRouterThreads) hist[e] = 0;
+    for (int e = tid; e < E; e += blockDim.x) hist[e] = 0;
 #pragma unroll
     for (int j = 0; j < EJ; ++j) {
         const int e = el + 8 * j;
@@ -212,7 +242,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         }
     }
     __syncthreads();
-    for (int e = tid; e < E; e += kRouterThreads) blockhist[(size_t)blockIdx.x * E + e] = hist[e];
+    for (int e = tid; e < E; e += blockDim.x) blockhist[(size_t)blockIdx.x * E + e] = hist[e];
 }
 
 // One block of 32 warps.  Warp w scans experts w, w + 32, ... over the
@@ -332,25 +362,32 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
         const int rank = __popc(s_mask[my_e] & ((1u << my_t) - 1u));
         const int pos = s_base[my_e] + rank;
         s_dest[tid] = pos;
-        row_token[pos] = t0 + my_t;
-        row_weight[pos] = wts[(size_t)(t0 + my_t) * k + (tid % k)];
+        if (blockIdx.y == 0) {
+            row_token[pos] = t0 + my_t;
+            row_weight[pos] = wts[(size_t)(t0 + my_t) * k + (tid % k)];
+        }
     }
     __syncthreads();
+    // This CTA copies columns [c0, c1) (in float4 units) of its block's rows.
     const int nv = d / 4;
-    const int total = n_tok * nv;
-    constexpr int kUnroll = 4;
+    const int per = (nv + gridDim.y - 1) / gridDim.y;
+    const int c0 = blockIdx.y * per, c1 = min(nv, c0 + per);
+    const int width = max(0, c1 - c0);
+    const int total = n_tok * width;
+    constexpr int kUnroll = 8;
     for (int base = tid; base < total; base += kUnroll * 256) {
         float4 f[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int i = base + u * 256;
-            if (i < total) f[u] = reinterpret_cast<const float4*>(x + (size_t)t0 * d)[i];
+            if (i < total)
+                f[u] = reinterpret_cast<const float4*>(x + (size_t)(t0 + i / width) * d)[c0 + i % width];
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
             const int i = base + u * 256;
             if (i >= total) break;
-            const int t = i / nv, v = i % nv;
+            const int t = i / width, v = c0 + i % width;
             if constexpr (kMode == 0) {
                 __nv_bfloat162 lo2 = __floats2bfloat162_rn(f[u].x, f[u].y);
                 __nv_bfloat162 hi2 = __floats2bfloat162_rn(f[u].z, f[u].w);
@@ -382,6 +419,16 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
     }
 }
 
+// Token blocks x column splits: enough CTAs (about 4 per SM) to keep tens of
+// MB of row loads in flight.
+dim3 permute_grid(const Layer& L, int T) {
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
+    int splits = (4 * L.sm_count + nblk - 1) / nblk;
+    const int max_splits = max(1, L.d / 4 / 256);   // at least 256 float4 columns per CTA
+    splits = max(1, min(splits, max_splits));
+    return dim3(nblk, splits);
+}
+
 template <int EJ, int KC>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
                             float* wts, int* blockhist, cudaStream_t s) {
@@ -394,7 +441,11 @@ cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits
                                            (int)smem);
     if (err != cudaSuccess) return err;
     const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
-    kern<<<nblk, kRouterThreads, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
+    // A single block of fewer than 32 tokens runs only the warps it needs
+    // (8 threads per token, whole warps): at decode sizes the dependent FMA
+    // chain is the critical path and idle warps would only take issue slots.
+    const int tok = T < kRouteTokens ? (T + 3) / 4 * 4 : kRouteTokens;
+    kern<<<nblk, 8 * tok, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
                                             L.cfg.router_policy, L.cfg.router_quantum,
                                             L.cfg.router_tie_eps, logits, idx, wts, blockhist);
     return cudaGetLastError();
@@ -436,28 +487,28 @@ cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
 }
 
 cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s) {
-    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     const Workspace& W = L.ws;
+    const dim3 grid = permute_grid(L, T);
     if (three_pass(L))
-        dispatch_permute_kernel<2><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     else
-        dispatch_permute_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     return cudaGetLastError();
 }
 
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s) {
-    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     const Workspace& W = L.ws;
+    const dim3 grid = permute_grid(L, T);
     if (three_pass(L))
-        dispatch_permute_kernel<1><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     else
-        dispatch_permute_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     return cudaGetLastError();
