@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
     "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
     "moe_dispatch_noalloc", "moe_route_host", "moe_host_alloc", "moe_host_free",
+    "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
 
@@ -104,6 +105,13 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_route_host.argtypes = [vp, _f32p, ctypes.c_int32, _f32p, _i32p, _f32p]
     L.moe_host_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
     L.moe_host_free.argtypes = [vp]
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    L.moe_ep_plan.argtypes = [_i32p, _i32p, ctypes.c_int32, ctypes.c_int32, i64p, i64p, i64p, i64p]
+    L.moe_ep_unique_id.argtypes = [vp]
+    L.moe_ep_create.argtypes = [ctypes.POINTER(MoeConfig), ctypes.POINTER(MoeWeightsHost),
+                                ctypes.c_int, ctypes.c_int, vp, ctypes.POINTER(vp)]
+    L.moe_ep_create_from_device.argtypes = L.moe_ep_create.argtypes
+    L.moe_ep_forward_device.argtypes = [vp, vp, vp, ctypes.c_int32, vp]
     L.moe_dispatch_noalloc.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        vp, vp, ctypes.c_int32, vp, vp, vp]
     if path is None:
@@ -114,6 +122,25 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
 def _check(rc: int):
     if rc != MOE_OK:
         raise MoeError(rc, load_library().moe_last_error().decode())
+
+
+def ep_plan(counts: np.ndarray, counts_in: np.ndarray, world: int, e_local: int):
+    """moe_ep_plan: (send_rows, send_off, recv_rows, recv_off) of one exchange."""
+    c = np.ascontiguousarray(counts, np.int32)
+    ci = np.ascontiguousarray(counts_in, np.int32)
+    out = [np.zeros(world, np.int64), np.zeros(world + 1, np.int64),
+           np.zeros(world, np.int64), np.zeros(world + 1, np.int64)]
+    p64 = lambda a: a.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))  # noqa: E731
+    _check(load_library().moe_ep_plan(c.ctypes.data_as(_i32p), ci.ctypes.data_as(_i32p), world,
+                                      e_local, *map(p64, out)))
+    return tuple(out)
+
+
+def ep_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (rank 0 of an expert-parallel group)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(load_library().moe_ep_unique_id(buf))
+    return buf.raw
 
 
 def default_config(**kw) -> MoeConfig:
@@ -283,6 +310,46 @@ class MoeLayer:
         self.cfg = MoeConfig()
         _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
         return self
+
+    @classmethod
+    def expert_parallel(cls, rank: int, world: int, nccl_id: bytes, *, d: int, ff: int, E: int,
+                        wg, w1, w3, w2, bias=None, device_pointers: bool = False, top_k: int = 2,
+                        policy: int = ROUTER_SOFTMAX_TOPK, precision: int = PREC_FP32,
+                        device: int = 0, max_tokens: int = 0, **cfg_kw) -> "MoeLayer":
+        """Collective: this rank's member of an expert-parallel group
+        (moe_ep_create / moe_ep_create_from_device).  Weights are numpy arrays
+        (host) or integer device addresses (device_pointers=True) for all E
+        experts; only this rank's slice is read."""
+        L = load_library()
+        cfg = default_config(d_model=d, d_ff=ff, num_experts=E, top_k=top_k, router_policy=policy,
+                             precision=precision, device=device, max_tokens=max_tokens, **cfg_kw)
+        P = _f32p * E
+        if device_pointers:
+            cast = lambda v: ctypes.cast(ctypes.c_void_p(v), _f32p)  # noqa: E731
+            keep = None
+        else:
+            keep = [np.ascontiguousarray(a, np.float32) for a in [wg, *w1, *w3, *w2]
+                    + ([bias] if bias is not None else [])]
+            wg, w1, w3, w2 = keep[0], keep[1:1 + E], keep[1 + E:1 + 2 * E], keep[1 + 2 * E:1 + 3 * E]
+            if bias is not None:
+                bias = keep[-1]
+            cast = _fp
+        hw = MoeWeightsHost(cast(wg), cast(bias) if bias is not None else None,
+                            P(*map(cast, w1)), P(*map(cast, w3)), P(*map(cast, w2)))
+        idbuf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+        h = ctypes.c_void_p()
+        fn = L.moe_ep_create_from_device if device_pointers else L.moe_ep_create
+        _check(fn(ctypes.byref(cfg), ctypes.byref(hw), rank, world, idbuf, ctypes.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.cfg = MoeConfig()
+        _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
+        return self
+
+    def ep_forward_device(self, x_ptr: int, y_ptr: int, T: int, stream: int = 0):
+        _check(load_library().moe_ep_forward_device(self._h, ctypes.c_void_p(x_ptr),
+                                                    ctypes.c_void_p(y_ptr), T,
+                                                    ctypes.c_void_p(stream)))
 
     # -- properties
     @property

@@ -90,6 +90,8 @@ void free_workspace(Workspace& W) {
     W = Workspace{};
 }
 
+}  // namespace
+
 int ensure_workspace(Layer& L, int T) {
     Workspace& W = L.ws;
     if (T <= W.cap_T && W.dev_err) return MOE_OK;
@@ -97,7 +99,7 @@ int ensure_workspace(Layer& L, int T) {
     if (W.dev_err) MOE_CUDA(cudaDeviceSynchronize());
     const int capT = std::max({T, W.cap_T + W.cap_T / 2, 64});
     free_workspace(W);
-    const size_t k = L.k, E = L.E;
+    const size_t k = L.k, E = L.E_route > L.E ? L.E_route : L.E;
     const int nblk = (capT + kRouteTokens - 1) / kRouteTokens;
     const int cap_mtiles = (int)((size_t)capT * k / kTileM) + L.E + 1;
     const size_t cap_rows = (size_t)cap_mtiles * kTileM;
@@ -146,6 +148,8 @@ int ensure_workspace(Layer& L, int T) {
     }
     return MOE_OK;
 }
+
+namespace {
 
 int ensure_stage(Layer& L, int T) {
     int rc = ensure_workspace(L, T);
@@ -302,10 +306,6 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
 }  // namespace moe
 
 using moe::Layer;
-struct MoeHandle {
-    Layer L;
-    cudaStream_t own_stream = nullptr;
-};
 
 extern "C" {
 
@@ -352,13 +352,23 @@ int moe_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* w, MoeHan
 namespace moe {
 namespace {
 int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, MoeHandle** out) {
+    return create_slice(cfg, w, device_ptrs, 0, cfg ? cfg->num_experts : 0, out);
+}
+}  // namespace
+
+// Build a handle that routes over cfg->num_experts experts and holds experts
+// [e_first, e_first + e_count) (all of them unless expert-parallel).
+int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, int e_first,
+                 int e_count, MoeHandle** out) {
     if (!cfg || !w || !out) return fail(MOE_ERR_INVALID, "null argument");
     *out = nullptr;
     int rc = validate_config(*cfg);
     if (rc) return rc;
     if (!w->router_weight || !w->w1 || !w->w2 || !w->w3)
         return fail(MOE_ERR_INVALID, "missing weight pointers");
-    for (int e = 0; e < cfg->num_experts; ++e)
+    if (e_first < 0 || e_count < 1 || e_first + e_count > cfg->num_experts)
+        return fail(MOE_ERR_INVALID, "bad expert slice");
+    for (int e = e_first; e < e_first + e_count; ++e)
         if (!w->w1[e] || !w->w2[e] || !w->w3[e]) return fail(MOE_ERR_INVALID, "null expert weight");
     int ndev = 0;
     MOE_CUDA(cudaGetDeviceCount(&ndev));
@@ -376,7 +386,9 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
     L.d = cfg->d_model;
     L.ff = cfg->d_ff;
     L.ffp = (cfg->d_ff + kFfBlock - 1) / kFfBlock * kFfBlock;
-    L.E = cfg->num_experts;
+    L.E = e_count;
+    L.E_route = cfg->num_experts;
+    L.e_first = e_first;
     L.k = cfg->top_k;
     MOE_CUDA(cudaDeviceGetAttribute(&L.sm_count, cudaDevAttrMultiProcessorCount, cfg->device));
     MOE_CUDA(cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking));
@@ -396,11 +408,12 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
         if (e_ != cudaSuccess) return cleanup_and_fail(cuda_fail(e_, #call)); \
     } while (0)
     const cudaMemcpyKind kind = device_ptrs ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    MOE_CUDA_C(dalloc(&L.wg, sizeof(float) * E * d, &wb));
-    MOE_CUDA_C(cudaMemcpy(L.wg, w->router_weight, sizeof(float) * E * d, kind));
+    const size_t Er = L.E_route;
+    MOE_CUDA_C(dalloc(&L.wg, sizeof(float) * Er * d, &wb));
+    MOE_CUDA_C(cudaMemcpy(L.wg, w->router_weight, sizeof(float) * Er * d, kind));
     if (w->router_bias) {
-        MOE_CUDA_C(dalloc(&L.bias, sizeof(float) * E, &wb));
-        MOE_CUDA_C(cudaMemcpy(L.bias, w->router_bias, sizeof(float) * E, kind));
+        MOE_CUDA_C(dalloc(&L.bias, sizeof(float) * Er, &wb));
+        MOE_CUDA_C(cudaMemcpy(L.bias, w->router_bias, sizeof(float) * Er, kind));
     }
     MOE_CUDA_C(dalloc(&L.w13_hi, eb * E * 2 * ffp * d, &wb));
     MOE_CUDA_C(dalloc(&L.w2_hi, eb * E * d * ffp, &wb));
@@ -414,8 +427,8 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
         // The caller's device copies serve directly as the converters' input.
         MOE_CUDA_C(cudaDeviceSynchronize());
         for (int e = 0; e < L.E; ++e) {
-            MOE_CUDA_C(convert_gateup(L, e, w->w1[e], w->w3[e], s));
-            MOE_CUDA_C(convert_down(L, e, w->w2[e], s));
+            MOE_CUDA_C(convert_gateup(L, e, w->w1[e_first + e], w->w3[e_first + e], s));
+            MOE_CUDA_C(convert_down(L, e, w->w2[e_first + e], s));
         }
         MOE_CUDA_C(cudaStreamSynchronize(s));
     } else {
@@ -424,9 +437,9 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
         MOE_CUDA_C(dalloc(&st3, sizeof(float) * ff * d, nullptr));
         MOE_CUDA_C(dalloc(&st2, sizeof(float) * ff * d, nullptr));
         for (int e = 0; e < L.E; ++e) {
-            MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e], sizeof(float) * ff * d, kind, s));
-            MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e], sizeof(float) * ff * d, kind, s));
-            MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e_first + e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e_first + e], sizeof(float) * ff * d, kind, s));
+            MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e_first + e], sizeof(float) * ff * d, kind, s));
             MOE_CUDA_C(convert_gateup(L, e, st1, st3, s));
             MOE_CUDA_C(convert_down(L, e, st2, s));
             MOE_CUDA_C(cudaStreamSynchronize(s));
@@ -455,7 +468,6 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
     *out = h.release();
     return MOE_OK;
 }
-}  // namespace
 }  // namespace moe
 
 extern "C" {
@@ -519,6 +531,7 @@ void moe_destroy(MoeHandle* h) {
     moe::DeviceGuard guard(h->L.cfg.device);
     cudaDeviceSynchronize();
     Layer& L = h->L;
+    if (L.ep) moe::ep_destroy(L);
     moe::free_workspace(L.ws);
     moe::free_ptr(L.wg); moe::free_ptr(L.bias); moe::free_ptr(L.w13_hi); moe::free_ptr(L.w13_lo);
     moe::free_ptr(L.w2_hi); moe::free_ptr(L.w2_lo); moe::free_ptr(L.w13_f32); moe::free_ptr(L.w2_f32);

@@ -1,0 +1,452 @@
+// Expert parallelism: one process and one B200 per rank, experts split
+// contiguously across the ranks, NCCL point-to-point over NVLink for the
+// dispatch and combine exchanges.  The reference has no multi-GPU path; this
+// is the layer's scale-out.
+//
+// Forward on rank r with T local tokens (every rank runs it collectively):
+//   1. router over all E experts (router weights are replicated);
+//   2. compact dispatch (granule 1): rows sorted by global expert, then token,
+//      so the rows for rank j are one contiguous run; fp32 rows in FP32
+//      precision, bf16 rows in BF16 precision;
+//   3. counts exchange: each rank sends rank j its E/G per-expert counts for
+//      j's experts; one small device-to-host copy gives the split sizes;
+//   4. payload exchange (grouped ncclSend / ncclRecv, self included);
+//   5. the received [source][local expert][token] rows are arranged into the
+//      grouped GEMM's expert blocks: the same scan kernel as the local
+//      dispatch, run on the [source][local expert] count matrix, gives each
+//      (source, expert) run its place; an arrange kernel converts the rows
+//      (bf16, or tf32 hi + lo);
+//   6. gate/up GEMM, then the down GEMM storing each row's fp32 result at the
+//      row it arrived in;
+//   7. return exchange (the reverse splits), so each rank gets its own rows
+//      back in its compact dispatch order;
+//   8. combine: y[token] += routing weight * returned row.
+#include <cuda_bf16.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace moe {
+
+// ------------------------------------------------------------------ NCCL
+// Loaded at first use, so the library itself does not depend on NCCL being
+// installed.  In a process that already loaded NCCL (e.g. through PyTorch),
+// dlopen returns that same library.
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+namespace {
+
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+bool load_nccl(std::string* err) {
+    std::lock_guard<std::mutex> lock(g_nccl_mu);
+    if (g_nccl.ok) return true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        *err = std::string("cannot load NCCL: ") + dlerror();
+        return false;
+    }
+#define MOE_SYM(field, name)                                                   \
+    g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(h, name));  \
+    if (!g_nccl.field) {                                                       \
+        *err = std::string("NCCL symbol missing: ") + name;                   \
+        return false;                                                          \
+    }
+    MOE_SYM(GetUniqueId, "ncclGetUniqueId")
+    MOE_SYM(CommInitRank, "ncclCommInitRank")
+    MOE_SYM(CommDestroy, "ncclCommDestroy")
+    MOE_SYM(Send, "ncclSend")
+    MOE_SYM(Recv, "ncclRecv")
+    MOE_SYM(GroupStart, "ncclGroupStart")
+    MOE_SYM(GroupEnd, "ncclGroupEnd")
+    MOE_SYM(GetErrorString, "ncclGetErrorString")
+#undef MOE_SYM
+    g_nccl.ok = true;
+    return true;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+    return report_error(MOE_ERR_NCCL, std::string(what) + ": " +
+                                          (g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "?"));
+}
+
+}  // namespace
+
+struct EpState {
+    int rank = 0, world = 1;
+    int e_local = 0;            // experts per rank
+    ncclComm_t comm = nullptr;
+    int cap_T = 0;              // local tokens the buffers hold
+    size_t row_bytes = 0;       // bytes of one dispatched row
+    void* send_rows = nullptr;  // [T*k][d] compact, expert-sorted
+    int* send_tok = nullptr;    // compact row -> local token
+    float* send_w = nullptr;    // compact row -> routing weight
+    int* send_eoff = nullptr;   // [E+1] compact offsets
+    void* recv_rows = nullptr;  // [G*T*k][d]
+    float* ret_send = nullptr;  // [G*T*k][d] fp32 results, by arrival row
+    float* ret_recv = nullptr;  // [T*k][d] fp32 results, by compact row
+    int* cnt_recv = nullptr;    // [G][E_local] device
+    int* cnt_scan = nullptr;    // [G][E_local] device (scan in place)
+    int* h_counts = nullptr;    // pinned [E]
+    int* h_cnt_recv = nullptr;  // pinned [G][E_local]
+};
+
+namespace {
+
+void ep_free_buffers(EpState& S) {
+    for (void* p : {S.send_rows, (void*)S.send_tok, (void*)S.send_w, (void*)S.send_eoff,
+                    S.recv_rows, (void*)S.ret_send, (void*)S.ret_recv, (void*)S.cnt_recv,
+                    (void*)S.cnt_scan})
+        if (p) cudaFree(p);
+    if (S.h_counts) cudaFreeHost(S.h_counts);
+    if (S.h_cnt_recv) cudaFreeHost(S.h_cnt_recv);
+    S.send_rows = S.recv_rows = nullptr;
+    S.send_tok = S.send_eoff = S.cnt_recv = S.cnt_scan = S.h_counts = S.h_cnt_recv = nullptr;
+    S.send_w = S.ret_send = S.ret_recv = nullptr;
+    S.cap_T = 0;
+}
+
+int ep_ensure(Layer& L, int T) {
+    EpState& S = *L.ep;
+    if (T <= S.cap_T) return MOE_OK;
+    cudaDeviceSynchronize();
+    ep_free_buffers(S);
+    const int capT = T > 64 ? T : 64;
+    const size_t rows_local = (size_t)capT * L.k;
+    const size_t rows_recv = rows_local * S.world;
+    S.row_bytes = (size_t)L.d * elem_bytes(L);
+    cudaError_t e = cudaSuccess;
+    auto A = [&](void** p, size_t b) {
+        if (e == cudaSuccess) e = cudaMalloc(p, b ? b : 256);
+    };
+    A(&S.send_rows, rows_local * S.row_bytes);
+    A((void**)&S.send_tok, rows_local * sizeof(int));
+    A((void**)&S.send_w, rows_local * sizeof(float));
+    A((void**)&S.send_eoff, (L.E_route + 1) * sizeof(int));
+    A(&S.recv_rows, rows_recv * S.row_bytes);
+    A((void**)&S.ret_send, rows_recv * L.d * sizeof(float));
+    A((void**)&S.ret_recv, rows_local * L.d * sizeof(float));
+    A((void**)&S.cnt_recv, (size_t)S.world * S.e_local * sizeof(int));
+    A((void**)&S.cnt_scan, (size_t)S.world * S.e_local * sizeof(int));
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&S.h_counts, L.E_route * sizeof(int), 0);
+    if (e == cudaSuccess)
+        e = cudaHostAlloc((void**)&S.h_cnt_recv, (size_t)S.world * S.e_local * sizeof(int), 0);
+    if (e != cudaSuccess) {
+        ep_free_buffers(S);
+        return report_error(MOE_ERR_OOM, std::string("expert-parallel buffers: ") +
+                                             cudaGetErrorString(e));
+    }
+    S.cap_T = capT;
+    // The receiving side runs the grouped GEMMs on up to world * T tokens' rows.
+    return ensure_workspace(L, capT * S.world);
+}
+
+// One warp per received row: find its (source, local expert) run, place it in
+// the expert's GEMM block and convert it to the operand format.
+template <bool kTf32x3>
+__global__ void __launch_bounds__(256)
+ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
+                  const int* __restrict__ cnt, const int* __restrict__ base,
+                  const int* __restrict__ eoff, int* __restrict__ row_token,
+                  float* __restrict__ row_weight, void* __restrict__ a_hi,
+                  void* __restrict__ a_lo) {
+    extern __shared__ int sm[];
+    int* src_off = sm;              // [G + 1] first arrival row of each source
+    int* run_off = sm + G + 1;      // [G][El + 1] offsets inside each source
+    if (threadIdx.x == 0) {
+        int off = 0;
+        for (int s = 0; s < G; ++s) {
+            src_off[s] = off;
+            int r = 0;
+            for (int e = 0; e < El; ++e) {
+                run_off[s * (El + 1) + e] = r;
+                r += cnt[s * El + e];
+            }
+            run_off[s * (El + 1) + El] = r;
+            off += r;
+        }
+        src_off[G] = off;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i = blockIdx.x * 8 + warp;
+    if (i >= rows) return;
+    int s = 0;
+    while (s + 1 < G && src_off[s + 1] <= i) ++s;
+    const int q = i - src_off[s];
+    int e = 0;
+    while (e + 1 < El && run_off[s * (El + 1) + e + 1] <= q) ++e;
+    const int prow = eoff[e] + base[s * El + e] + (q - run_off[s * (El + 1) + e]);
+    if (lane == 0) {
+        row_token[prow] = i;
+        row_weight[prow] = 1.0f;
+    }
+    if constexpr (kTf32x3) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + (size_t)i * d);
+        float4* hi = reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow * d);
+        float4* lo = reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow * d);
+        for (int v = lane; v < d / 4; v += 32) {
+            const float4 f = src[v];
+            float4 h, l;
+            h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+            h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+            h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+            h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+            hi[v] = h;
+            lo[v] = l;
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + (size_t)i * d);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow * d);
+        for (int v = lane; v < d / 8; v += 32) dst[v] = src[v];
+    }
+}
+
+// y[token] += weight * returned row, one compact row per warp.
+__global__ void __launch_bounds__(256)
+ep_combine_kernel(const float* __restrict__ ret, int rows, int d, const int* __restrict__ tok,
+                  const float* __restrict__ w, float* __restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = blockIdx.x * 8 + warp;
+    if (j >= rows) return;
+    const float wt = w[j];
+    const float4* src = reinterpret_cast<const float4*>(ret + (size_t)j * d);
+    float* dst = y + (size_t)tok[j] * d;
+    for (int v = lane; v < d / 4; v += 32) {
+        const float4 r = src[v];
+        atomicAdd(reinterpret_cast<float4*>(dst) + v,
+                  make_float4(wt * r.x, wt * r.y, wt * r.z, wt * r.w));
+    }
+}
+
+int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+    EpState& S = *L.ep;
+    int rc = ep_ensure(L, T);
+    if (rc) return rc;
+    Workspace& W = L.ws;
+    const int G = S.world, El = S.e_local, Eg = L.E_route;
+    const ncclDataType_t dt = three_pass(L) ? ncclFloat32 : ncclBfloat16;
+    const size_t d = L.d;
+    auto cuda_err = [](cudaError_t e, const char* what) {
+        return report_error(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    cudaError_t ce;
+    ncclResult_t nr;
+
+    // 1-2: route and pack locally (compact, expert-sorted).
+    if (T > 0) {
+        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s)) != cudaSuccess)
+            return cuda_err(ce, "router");
+        if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
+                                      W.counts, S.send_eoff, nullptr, nullptr, nullptr, nullptr,
+                                      s)) != cudaSuccess)
+            return cuda_err(ce, "dispatch scan");
+        if ((ce = launch_dispatch_permute_to(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w,
+                                             S.send_rows, s)) != cudaSuccess)
+            return cuda_err(ce, "dispatch permute");
+    } else {
+        if ((ce = cudaMemsetAsync(W.counts, 0, Eg * sizeof(int), s)) != cudaSuccess)
+            return cuda_err(ce, "counts");
+    }
+    // 3: counts exchange.
+    if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
+    for (int j = 0; j < G; ++j) {
+        g_nccl.Send(W.counts + j * El, El, ncclInt32, j, S.comm, s);
+        g_nccl.Recv(S.cnt_recv + j * El, El, ncclInt32, j, S.comm, s);
+    }
+    if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "counts exchange");
+    if ((ce = cudaMemcpyAsync(S.h_counts, W.counts, Eg * sizeof(int), cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+        (ce = cudaMemcpyAsync(S.h_cnt_recv, S.cnt_recv, (size_t)G * El * sizeof(int),
+                              cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
+        (ce = cudaMemcpyAsync(S.cnt_scan, S.cnt_recv, (size_t)G * El * sizeof(int),
+                              cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+        return cuda_err(ce, "counts copy");
+    if ((ce = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_err(ce, "counts sync");
+    std::vector<int64_t> send_rows(G), send_off(G + 1), recv_rows(G), recv_off(G + 1);
+    if ((rc = moe_ep_plan(S.h_counts, S.h_cnt_recv, G, El, send_rows.data(), send_off.data(),
+                          recv_rows.data(), recv_off.data())) != MOE_OK)
+        return rc;
+    const int R = (int)recv_off[G];
+    const size_t rb = S.row_bytes;
+    // 4: payload exchange.
+    if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
+    for (int j = 0; j < G; ++j) {
+        if (send_rows[j])
+            g_nccl.Send(static_cast<char*>(S.send_rows) + send_off[j] * rb, send_rows[j] * d, dt, j,
+                        S.comm, s);
+        if (recv_rows[j])
+            g_nccl.Recv(static_cast<char*>(S.recv_rows) + recv_off[j] * rb, recv_rows[j] * d, dt, j,
+                        S.comm, s);
+    }
+    if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "dispatch exchange");
+    // 5-6: arrange and run the local experts.
+    if (R > 0) {
+        if ((ce = launch_scan_generic(S.cnt_scan, G, El, kTileM, W.counts, W.eoff, W.mtiles,
+                                      W.num_mtiles, W.row_token, W.row_weight, s)) != cudaSuccess)
+            return cuda_err(ce, "arrival scan");
+        const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
+        const int grid = (R + 7) / 8;
+        if (three_pass(L))
+            ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, S.cnt_recv,
+                                                            S.cnt_scan, W.eoff, W.row_token,
+                                                            W.row_weight, W.a_hi, W.a_lo);
+        else
+            ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, S.cnt_recv,
+                                                             S.cnt_scan, W.eoff, W.row_token,
+                                                             W.row_weight, W.a_hi, W.a_lo);
+        if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
+        if ((ce = launch_expert_gemm_rows(L, R, nullptr, s, 0)) != cudaSuccess)
+            return cuda_err(ce, "gate/up GEMM");
+        if ((ce = launch_expert_gemm_rows(L, R, S.ret_send, s, 2)) != cudaSuccess)
+            return cuda_err(ce, "down GEMM");
+    }
+    // 7: return exchange.
+    if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
+    for (int j = 0; j < G; ++j) {
+        if (recv_rows[j])
+            g_nccl.Send(S.ret_send + recv_off[j] * d, recv_rows[j] * d, ncclFloat32, j, S.comm, s);
+        if (send_rows[j])
+            g_nccl.Recv(S.ret_recv + send_off[j] * d, send_rows[j] * d, ncclFloat32, j, S.comm, s);
+    }
+    if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "combine exchange");
+    // 8: weighted combine into y.
+    if (T > 0) {
+        if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * d, s)) != cudaSuccess)
+            return cuda_err(ce, "y memset");
+        const int rows = T * L.k;
+        ep_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok, S.send_w,
+                                                         y);
+        if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
+    }
+    return MOE_OK;
+}
+
+struct DeviceGuardEp {
+    int prev = -1;
+    explicit DeviceGuardEp(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuardEp() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+void ep_destroy(Layer& L) {
+    if (!L.ep) return;
+    ep_free_buffers(*L.ep);
+    if (L.ep->comm && g_nccl.ok) g_nccl.CommDestroy(L.ep->comm);
+    delete L.ep;
+    L.ep = nullptr;
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_ep_plan(const int32_t* counts, const int32_t* counts_in, int32_t world, int32_t e_local,
+                int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off) {
+    if (!counts || !counts_in || !send_rows || !send_off || !recv_rows || !recv_off || world < 1 ||
+        e_local < 1)
+        return moe::report_error(MOE_ERR_INVALID, "moe_ep_plan: bad argument");
+    send_off[0] = recv_off[0] = 0;
+    for (int j = 0; j < world; ++j) {
+        int64_t a = 0, b = 0;
+        for (int e = 0; e < e_local; ++e) {
+            if (counts[j * e_local + e] < 0 || counts_in[j * e_local + e] < 0)
+                return moe::report_error(MOE_ERR_INVALID, "moe_ep_plan: negative count");
+            a += counts[j * e_local + e];
+            b += counts_in[j * e_local + e];
+        }
+        send_rows[j] = a;
+        recv_rows[j] = b;
+        send_off[j + 1] = send_off[j] + a;
+        recv_off[j + 1] = recv_off[j] + b;
+    }
+    return MOE_OK;
+}
+
+int moe_ep_unique_id(void* id_out) {
+    std::string err;
+    if (!id_out) return moe::report_error(MOE_ERR_INVALID, "null argument");
+    if (!moe::load_nccl(&err)) return moe::report_error(MOE_ERR_NCCL, err);
+    ncclUniqueId id;
+    ncclResult_t r = moe::g_nccl.GetUniqueId(&id);
+    if (r != ncclSuccess) return moe::nccl_fail(r, "ncclGetUniqueId");
+    std::memcpy(id_out, &id, sizeof id);
+    return MOE_OK;
+}
+
+static int ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, int rank,
+                     int world, const void* nccl_id, MoeHandle** out) {
+    using namespace moe;
+    std::string err;
+    if (!cfg || !w || !nccl_id || !out) return report_error(MOE_ERR_INVALID, "null argument");
+    if (world < 1 || rank < 0 || rank >= world) return report_error(MOE_ERR_INVALID, "bad rank");
+    if (cfg->num_experts % world != 0)
+        return report_error(MOE_ERR_INVALID, "num_experts must be a multiple of the group size");
+    if (!load_nccl(&err)) return report_error(MOE_ERR_NCCL, err);
+    const int El = cfg->num_experts / world;
+    MoeHandle* h = nullptr;
+    int rc = create_slice(cfg, w, device_ptrs, rank * El, El, &h);
+    if (rc) return rc;
+    DeviceGuardEp guard(cfg->device);
+    auto* S = new EpState();
+    S->rank = rank;
+    S->world = world;
+    S->e_local = El;
+    h->L.ep = S;
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    ncclResult_t r = g_nccl.CommInitRank(&S->comm, world, id, rank);
+    if (r != ncclSuccess) {
+        rc = nccl_fail(r, "ncclCommInitRank");
+        S->comm = nullptr;
+        moe_destroy(h);
+        return rc;
+    }
+    *out = h;
+    return MOE_OK;
+}
+
+int moe_ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, int rank, int world,
+                  const void* nccl_id, MoeHandle** out) {
+    return ep_create(cfg, w, false, rank, world, nccl_id, out);
+}
+
+int moe_ep_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* w, int rank, int world,
+                              const void* nccl_id, MoeHandle** out) {
+    return ep_create(cfg, w, true, rank, world, nccl_id, out);
+}
+
+int moe_ep_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream) {
+    using namespace moe;
+    if (!h || !h->L.ep) return report_error(MOE_ERR_INVALID, "not an expert-parallel handle");
+    if (T < 0) return report_error(MOE_ERR_INVALID, "T < 0");
+    if (T > 0 && (!x || !y)) return report_error(MOE_ERR_INVALID, "null x or y");
+    DeviceGuardEp guard(h->L.cfg.device);
+    return ep_forward(h->L, x, y, T, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -35,7 +35,7 @@
 namespace moe {
 namespace {
 
-enum Epi { kEpiGateUp = 0, kEpiDown = 1 };
+enum Epi { kEpiGateUp = 0, kEpiDown = 1, kEpiDownStore = 2 };
 
 struct GemmParams {
     const MTile* mtiles;
@@ -50,7 +50,7 @@ struct GemmParams {
     // down epilogue
     const int* row_token;
     const float* row_weight;
-    float* y;
+    float* y;          // Down: [T][d] accumulated; DownStore: [rows][d], row row_token[prow]
     int d;
     int* err;
 };
@@ -312,6 +312,24 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                         }
                     }
                 }
+            } else if constexpr (kEpi == kEpiDownStore) {
+                // Expert parallelism: each row's fp32 result goes back to the
+                // rank that sent it, at the row it arrived in.
+                const int dst = valid ? p.row_token[prow] : 0;
+#pragma unroll 1
+                for (int c = 0; c < kTileN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + c, v);
+                    tmem_ld_wait();
+                    const int col = nt * kTileN + c;
+                    if (valid && col < p.d) {
+                        float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                     __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    }
+                }
             } else {
                 int tok = 0;
                 float wgt = 0.0f;
@@ -370,10 +388,16 @@ cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMa
 }  // namespace
 
 cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down) {
+    return launch_expert_gemm_rows(L, T * L.k, y, s, down ? 1 : 0);
+}
+
+cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
+                                    int mode) {
+    const bool down = mode != 0;
     const Workspace& W = L.ws;
     const bool tf = three_pass(L);
     const int elems = tf ? 32 : 64;
-    const int max_mtiles = (T * L.k + kTileM - 1) / kTileM + L.E;
+    const int max_mtiles = (routed_rows + kTileM - 1) / kTileM + L.E;
 
     GemmParams g{};
     g.mtiles = W.mtiles;
@@ -405,6 +429,13 @@ cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, 
                                                 g, grid, s);
         return launch_one<false, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi, L.tm_w13_hi, g,
                                              grid, s);
+    }
+    if (mode == 2) {
+        if (tf)
+            return launch_one<true, kEpiDownStore>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo,
+                                                   g, grid, s);
+        return launch_one<false, kEpiDownStore>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi,
+                                                g, grid, s);
     }
     if (tf)
         return launch_one<true, kEpiDown>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo, g, grid,

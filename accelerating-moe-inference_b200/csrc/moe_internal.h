@@ -78,9 +78,17 @@ struct Workspace {
     size_t bytes = 0;
 };
 
+struct EpState;  // expert-parallel group (ep.cu)
+
 struct Layer {
     MoeConfig cfg{};
     int d = 0, ff = 0, ffp = 0, E = 0, k = 0;
+    // Experts the router scores.  Equal to E except under expert parallelism,
+    // where E is the number of experts this rank holds and E_route the global
+    // count; the rank's experts are [e_first, e_first + E).
+    int E_route = 0;
+    int e_first = 0;
+    EpState* ep = nullptr;
     int sm_count = 148;
     float* wg = nullptr;
     float* bias = nullptr;
@@ -117,11 +125,24 @@ cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaS
 // The same placement with the rows copied in the decode kernels' format:
 // fp32 as is (FP32 precision) or bf16 (BF16 precision).
 cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s);
+// Placement into explicit outputs, routing over E experts with offsets eoff.
+cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
+                                       const int* eoff, int* row_token, float* row_weight,
+                                       void* rows, cudaStream_t s);
+// The scan on any [nblk][E] count matrix, expert blocks rounded to `granule`
+// rows; mtiles == nullptr gives a compact layout with no tiles or padding.
+cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
+                                MTile* mtiles, int* num_mtiles, int* row_token,
+                                float* row_weight, cudaStream_t s);
 
 // expert_gemm.cu
 // down == false: gate/up GEMM with the SwiGLU epilogue into H;
 // down == true:  down GEMM with the weighted-combine epilogue into y.
 cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down);
+// The same over `routed_rows` packed rows; mode 0 gate/up, 1 down with the
+// combine epilogue, 2 down storing each row's result at y[row_token[row]].
+cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
+                                    int mode);
 
 // decode.cu: T <= decode_max_supported_tokens() (64)
 cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s);
@@ -134,10 +155,26 @@ cudaError_t convert_down(const Layer& L, int e, const float* w2_dev, cudaStream_
 
 // Record `msg` as this thread's moe_last_error() and return `code` (capi.cu).
 int report_error(int code, const std::string& msg);
+// Grow the workspace to T tokens (capi.cu).
+int ensure_workspace(Layer& L, int T);
+// Handle construction for experts [e_first, e_first + e_count) (capi.cu).
+int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, int e_first,
+                 int e_count, MoeHandle** out);
+// Expert-parallel teardown (ep.cu).
+void ep_destroy(Layer& L);
 
 // tensor maps (capi.cpp)
 bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
                   uint64_t outer, uint32_t box_inner, uint32_t box_outer, std::string* err);
+
+}  // namespace moe
+
+struct MoeHandle {
+    moe::Layer L;
+    cudaStream_t own_stream = nullptr;
+};
+
+namespace moe {
 
 inline size_t elem_bytes(const Layer& L) { return L.cfg.precision == MOE_PREC_BF16 ? 2 : 4; }
 inline bool three_pass(const Layer& L) { return L.cfg.precision == MOE_PREC_FP32; }

@@ -262,8 +262,8 @@ __device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
 }
 
 __global__ void __launch_bounds__(kScanThreads)
-dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restrict__ counts,
-                     int* __restrict__ eoff, MTile* __restrict__ mtiles,
+dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
+                     int* __restrict__ counts, int* __restrict__ eoff, MTile* __restrict__ mtiles,
                      int* __restrict__ num_mtiles, int* __restrict__ row_token,
                      float* __restrict__ row_weight) {
     __shared__ int s_cnt[kMaxExperts];
@@ -292,7 +292,7 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restri
             const int e = e0 + lane;
             const int c = e < E ? s_cnt[e] : 0;
             const int mc = (c + kTileM - 1) / kTileM;
-            const int pc = mc * kTileM;
+            const int pc = (c + granule - 1) / granule * granule;
             const int ipc = warp_inclusive_scan(pc, lane);
             const int imc = warp_inclusive_scan(mc, lane);
             if (e < E) {
@@ -307,10 +307,11 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int* __restri
             s_off[E] = run_off;
             s_mst[E] = run_m;
             eoff[E] = run_off;
-            *num_mtiles = run_m;
+            if (num_mtiles) *num_mtiles = run_m;
         }
     }
     __syncthreads();
+    if (!mtiles) return;   // compact layout (granule 1): no GEMM tiles, no padding rows
     for (int e = warp; e < E; e += kWarps) {
         const int c = s_cnt[e];
         const int mst = s_mst[e];
@@ -432,7 +433,7 @@ dim3 permute_grid(const Layer& L, int T) {
 template <int EJ, int KC>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
                             float* wts, int* blockhist, cudaStream_t s) {
-    const int E = L.E;
+    const int E = L.E_route;
     const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4)) +
                                          kRouteTokens * (E + 1)) +
                         sizeof(int) * E;
@@ -458,7 +459,7 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
     // K chunk per pipeline stage: as wide as shared memory allows, so each
     // SM keeps 100-200 KB of x / wg loads in flight (the dot-product chains
     // themselves are serial and cannot be split).
-    const int ej = (L.E + 7) / 8;
+    const int ej = (L.E_route + 7) / 8;
     if (L.d % 256 == 0) {
         if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s);
         if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s);
@@ -480,23 +481,39 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
     const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     const Workspace& W = L.ws;
-    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(W.blockhist, nblk, L.E, W.counts, W.eoff,
-                                                  W.mtiles, W.num_mtiles, W.row_token,
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(W.blockhist, nblk, L.E_route, kTileM, W.counts,
+                                                  W.eoff, W.mtiles, W.num_mtiles, W.row_token,
                                                   W.row_weight);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
+                                MTile* mtiles, int* num_mtiles, int* row_token,
+                                float* row_weight, cudaStream_t s) {
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(hist, nblk, E, granule, counts, eoff, mtiles,
+                                                  num_mtiles, row_token, row_weight);
     return cudaGetLastError();
 }
 
 cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s) {
     const Workspace& W = L.ws;
+    return launch_dispatch_permute_to(L, x, T, L.E_route, W.eoff, W.row_token, W.row_weight,
+                                      W.a_hi, s);
+}
+
+cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
+                                       const int* eoff, int* row_token, float* row_weight,
+                                       void* rows, cudaStream_t s) {
+    const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
     if (three_pass(L))
-        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo);
+        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
+                                                        W.blockhist, eoff, row_token,
+                                                        row_weight, rows, nullptr);
     else
-        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo);
+        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
+                                                        W.blockhist, eoff, row_token,
+                                                        row_weight, rows, nullptr);
     return cudaGetLastError();
 }
 
@@ -504,11 +521,11 @@ cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaS
     const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
     if (three_pass(L))
-        dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     else
-        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E, L.k, W.idx, W.wts,
+        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
                                                         W.row_weight, W.a_hi, W.a_lo);
     return cudaGetLastError();

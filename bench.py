@@ -26,8 +26,9 @@ epilogue, down grouped GEMM with the weighted-combine epilogue.
               compiled from its sources into oracle/_ref) on this host's
               cores, on a bounded sample of the same layer.
 
-N > 1 (torchrun): token-sharded replicas -- every rank holds all experts and
-its own T tokens (weak scaling, no data-path collective).
+N > 1 (torchrun): expert parallel -- each rank holds E/N experts and its own
+T tokens; dispatch and combine are NCCL send/recv exchanges over NVLink
+(weak scaling).  --parallelism dp runs token-sharded replicas instead.
 """
 from __future__ import annotations
 
@@ -226,6 +227,116 @@ def reference_arm(args, wl):
     return 0
 
 
+def run_ep(args, wl, pkg, world, rank, local):
+    """N > 1, expert parallel: each rank holds E/N experts and its own T
+    tokens; dispatch and combine are NCCL exchanges over NVLink (weak scaling:
+    tokens per GPU fixed)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
+    if E % world:
+        raise SystemExit(f"{E} experts do not split over {world} GPUs")
+    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
+    dev = torch.device("cuda", local)
+    obj = [pkg.ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
+    rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
+    wg = rnd(E, d)
+    w1, w3, w2 = [], [], []
+    El = E // world
+    for e in range(E):
+        mine = rank * El <= e < (rank + 1) * El
+        a, b, c = rnd(ff, d), rnd(ff, d), rnd(d, ff)   # every rank draws the same stream
+        w1.append(a if mine else None)
+        w3.append(b if mine else None)
+        w2.append(c if mine else None)
+        if not mine:
+            del a, b, c
+    ptr = lambda t: t.data_ptr() if t is not None else wg.data_ptr()  # noqa: E731
+    layer = pkg.MoeLayer.expert_parallel(
+        rank, world, obj[0], d=d, ff=ff, E=E, wg=wg.data_ptr(), w1=[ptr(t) for t in w1],
+        w3=[ptr(t) for t in w3], w2=[ptr(t) for t in w2], device_pointers=True, top_k=k,
+        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec, device=local, max_tokens=T)
+    del w1, w3, w2
+    torch.cuda.empty_cache()
+    xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
+    x = torch.randn(T, d, generator=xgen, device=dev)
+    y = torch.empty_like(x)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    step = lambda: layer.ep_forward_device(x.data_ptr(), y.data_ptr(), T, sp)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+        flush.zero_()
+    torch.cuda.synchronize()
+    dist.barrier()
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    dist.barrier()
+    total = 0.0
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        flush.zero_()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    torch.cuda.synchronize()
+    dist.barrier()
+    # e2e: pinned host x in, y out, copies inside the timed region.
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    e2e_n = max(3, args.steps // 2)
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_n):
+        x.copy_(xh, non_blocking=True)
+        step()
+        yh.copy_(y, non_blocking=True)
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = a.elapsed_time(b) / e2e_n
+    clocks = sampler.stop()
+    t = torch.tensor([total, e2e_ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0]) / args.steps
+    e2e_ms = float(t[1])
+    if rank == 0:
+        hbm, bf16_peak, _, src = _peaks()
+        flops = 6.0 * T * k * d * ff          # expert FLOPs per rank (average routed rows)
+        achieved = flops / (ms / 1e3) / 1e12
+        print(json.dumps({
+            "metric": METRIC, "value": world * T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
+            "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
+            "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
+                       "experts": E, "top_k": k, "router": "softmax_topk_renorm",
+                       "precision": args.precision, "seed": wl["seed"],
+                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU, "
+                                      "NCCL send/recv dispatch and combine)"},
+            "roofline": {"kernel": "whole expert-parallel step (exchanges included)",
+                         "bound": "tensor", "achieved": achieved, "peak": bf16_peak,
+                         "unit": "TFLOP/s", "frac": achieved / bf16_peak, "traffic": None,
+                         "peak_source": f"{src} bf16 dense (burst)"},
+            "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
+                    "how": "pinned host x -> device -> moe_ep_forward_device -> pinned host y, "
+                           "CUDA events, max over ranks"},
+            "gpu_launches": 7 * args.steps,
+            "clocks": clocks,
+        }))
+    layer.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -236,6 +347,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--parallelism", choices=["ep", "dp"], default="ep",
+                    help="N > 1: expert parallel (default) or token-sharded replicas")
     ap.add_argument("--decode-max-tokens", type=int, default=None,
                     help="override the handle's decode threshold (0..64)")
     args = ap.parse_args()
@@ -258,6 +371,11 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     pkg = _pkg()
+    if world > 1 and args.parallelism == "ep":
+        rc = run_ep(args, wl, pkg, world, rank, local)
+        dist.barrier()
+        dist.destroy_process_group()
+        return rc
     prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
     T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
 

@@ -188,6 +188,43 @@ int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int
 int moe_profile_enable(MoeHandle* h, int enable);
 int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n);
 
+/* ---------------------------------------------------------------------
+ * Expert parallelism (no counterpart in the reference, which runs on one
+ * GPU): one process and one GPU per rank, experts split contiguously
+ * (rank r holds experts [r*E/G, (r+1)*E/G)), router weights replicated,
+ * NCCL point-to-point exchanges over NVLink for dispatch and combine.
+ * NCCL is loaded at run time (libnccl.so.2); MOE_ERR_NCCL if it is absent.
+ * --------------------------------------------------------------------- */
+
+/* The exchange plan of one forward, host only (no GPU needed): from this
+ * rank's routed rows per global expert `counts` [world * e_local] and the
+ * rows each source sends it for its local experts `counts_in`
+ * [world][e_local], the rows sent to / received from each rank and their
+ * offsets in the (expert-sorted) send and (source-major) receive buffers.
+ * send_off / recv_off have world + 1 entries. */
+int moe_ep_plan(const int32_t* counts, const int32_t* counts_in, int32_t world, int32_t e_local,
+                int64_t* send_rows, int64_t* send_off, int64_t* recv_rows, int64_t* recv_off);
+
+/* 128-byte NCCL unique id for a new group: rank 0 calls this and hands the
+ * bytes to every rank by its own means (a store, a broadcast, a file). */
+int moe_ep_unique_id(void* id_out);
+
+/* Collective over the group: every rank calls it with the same global
+ * config (num_experts a multiple of `world`) and the same id.  `weights`
+ * holds pointers for all E experts; only this rank's slice is read (host
+ * pointers here, device pointers on cfg->device for the _from_device
+ * variant). */
+int moe_ep_create(const MoeConfig* cfg, const MoeWeightsHost* weights, int rank, int world,
+                  const void* nccl_id, MoeHandle** out);
+int moe_ep_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* weights, int rank,
+                              int world, const void* nccl_id, MoeHandle** out);
+
+/* Collective forward: each rank passes its own T local tokens (T may differ
+ * between ranks, and may be 0) and gets its own y.  Synchronises the stream
+ * once, after the counts exchange, to size the payload exchange.
+ * moe_destroy releases the group's communicator. */
+int moe_ep_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream);
+
 /* Dispatch that allocates nothing.  No counterpart in the reference: it
  * exists for callers that cannot call cudaMalloc -- code running inside a
  * stream capture that must not touch the allocator, frameworks that own all
