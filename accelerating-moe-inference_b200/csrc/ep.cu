@@ -16,8 +16,8 @@
 //      dispatch, run on the [source][local expert] count matrix, gives each
 //      (source, expert) run its place; an arrange kernel converts the rows
 //      (bf16, or tf32 hi + lo);
-//   6. gate/up GEMM, then the down GEMM storing each row's fp32 result at the
-//      row it arrived in;
+//   6. gate/up GEMM, then the down GEMM storing each row's result (fp32, or
+//      bf16 in BF16 precision) at the row it arrived in;
 //   7. return exchange (the reverse splits), so each rank gets its own rows
 //      back in its compact dispatch order;
 //   8. combine: y[token] += routing weight * returned row.
@@ -102,8 +102,8 @@ struct EpState {
     float* send_w = nullptr;    // compact row -> routing weight
     int* send_eoff = nullptr;   // [E+1] compact offsets
     void* recv_rows = nullptr;  // [G*T*k][d]
-    float* ret_send = nullptr;  // [G*T*k][d] fp32 results, by arrival row
-    float* ret_recv = nullptr;  // [T*k][d] fp32 results, by compact row
+    float* ret_send = nullptr;  // [G*T*k][d] results (dispatch element type), by arrival row
+    float* ret_recv = nullptr;  // [T*k][d] results, by compact row
     int* cnt_recv = nullptr;    // [G][E_local] device
     int* cnt_scan = nullptr;    // [G][E_local] device (scan in place)
     int* h_counts = nullptr;    // pinned [E]
@@ -221,18 +221,27 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
     }
 }
 
-// y[token] += weight * returned row, one compact row per warp.
+// y[token] += weight * returned row, one compact row per warp.  Returned rows
+// are fp32 (FP32 precision) or bf16 (BF16 precision).
+template <bool kF32>
 __global__ void __launch_bounds__(256)
-ep_combine_kernel(const float* __restrict__ ret, int rows, int d, const int* __restrict__ tok,
+ep_combine_kernel(const void* __restrict__ ret, int rows, int d, const int* __restrict__ tok,
                   const float* __restrict__ w, float* __restrict__ y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = blockIdx.x * 8 + warp;
     if (j >= rows) return;
     const float wt = w[j];
-    const float4* src = reinterpret_cast<const float4*>(ret + (size_t)j * d);
     float* dst = y + (size_t)tok[j] * d;
     for (int v = lane; v < d / 4; v += 32) {
-        const float4 r = src[v];
+        float4 r;
+        if constexpr (kF32) {
+            r = reinterpret_cast<const float4*>(static_cast<const float*>(ret) + (size_t)j * d)[v];
+        } else {
+            const uint2 u = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(ret) +
+                                                          (size_t)j * d)[v];
+            r = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                            __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+        }
         atomicAdd(reinterpret_cast<float4*>(dst) + v,
                   make_float4(wt * r.x, wt * r.y, wt * r.z, wt * r.w));
     }
@@ -319,13 +328,15 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         if ((ce = launch_expert_gemm_rows(L, R, S.ret_send, s, 2)) != cudaSuccess)
             return cuda_err(ce, "down GEMM");
     }
-    // 7: return exchange.
+    // 7: return exchange (same element type as the dispatch).
     if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
     for (int j = 0; j < G; ++j) {
         if (recv_rows[j])
-            g_nccl.Send(S.ret_send + recv_off[j] * d, recv_rows[j] * d, ncclFloat32, j, S.comm, s);
+            g_nccl.Send(reinterpret_cast<char*>(S.ret_send) + recv_off[j] * rb, recv_rows[j] * d, dt,
+                        j, S.comm, s);
         if (send_rows[j])
-            g_nccl.Recv(S.ret_recv + send_off[j] * d, send_rows[j] * d, ncclFloat32, j, S.comm, s);
+            g_nccl.Recv(reinterpret_cast<char*>(S.ret_recv) + send_off[j] * rb, send_rows[j] * d, dt,
+                        j, S.comm, s);
     }
     if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "combine exchange");
     // 8: weighted combine into y.
@@ -333,8 +344,12 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * d, s)) != cudaSuccess)
             return cuda_err(ce, "y memset");
         const int rows = T * L.k;
-        ep_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok, S.send_w,
-                                                         y);
+        if (three_pass(L))
+            ep_combine_kernel<true><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
+                                                                   S.send_w, y);
+        else
+            ep_combine_kernel<false><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
+                                                                    S.send_w, y);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
     return MOE_OK;

@@ -313,8 +313,9 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     }
                 }
             } else if constexpr (kEpi == kEpiDownStore) {
-                // Expert parallelism: each row's fp32 result goes back to the
-                // rank that sent it, at the row it arrived in.
+                // Expert parallelism: each row's result goes back to the rank
+                // that sent it, at the row it arrived in -- fp32 in FP32
+                // precision, bf16 in BF16 precision (half the return bytes).
                 const int dst = valid ? p.row_token[prow] : 0;
 #pragma unroll 1
                 for (int c = 0; c < kTileN; c += 32) {
@@ -323,11 +324,27 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     tmem_ld_wait();
                     const int col = nt * kTileN + c;
                     if (valid && col < p.d) {
-                        float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
+                        if constexpr (kTf32x3) {
+                            float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                     __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                            for (int j = 0; j < 32; j += 4)
+                                out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                         __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                        } else {
+                            uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.y) +
+                                                                  static_cast<size_t>(dst) * p.d + col);
+#pragma unroll
+                            for (int j = 0; j < 32; j += 8) {
+                                uint32_t w4[4];
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[j + 2 * i]),
+                                                                              __uint_as_float(v[j + 2 * i + 1]));
+                                    w4[i] = *reinterpret_cast<uint32_t*>(&b2);
+                                }
+                                out[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                            }
+                        }
                     }
                 }
             } else {

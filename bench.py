@@ -365,6 +365,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # Rank 0's stdout carries exactly one JSON line: keep NCCL's banner off it.
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
