@@ -87,7 +87,7 @@ def _traffic_from_profile(workload: str, precision: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms."""
     Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -97,7 +97,7 @@ class ClockSampler:
         self.f = tempfile.TemporaryFile(mode="w+")
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
