@@ -30,6 +30,8 @@ ROUTER_PHI_QUANTISED = 0
 ROUTER_SOFTMAX_TOPK = 1
 PREC_FP32 = 0
 PREC_BF16 = 1
+GEMM_CTA_PAIR = 0
+GEMM_SINGLE_CTA = 1
 
 # Every symbol include/moe_b200.h declares.
 EXPORTED_SYMBOLS = (
@@ -55,7 +57,8 @@ class MoeConfig(ctypes.Structure):
                 ("router_policy", ctypes.c_int32), ("precision", ctypes.c_int32),
                 ("router_quantum", ctypes.c_float), ("router_tie_eps", ctypes.c_float),
                 ("decode_max_tokens", ctypes.c_int32), ("device", ctypes.c_int32),
-                ("max_tokens", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5)]
+                ("max_tokens", ctypes.c_int32), ("gemm_variant", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 4)]
 
 
 _f32p = ctypes.POINTER(ctypes.c_float)

@@ -84,6 +84,7 @@ cudaError_t dalloc(T** p, size_t bytes, size_t* counter) {
 void free_workspace(Workspace& W) {
     free_ptr(W.logits); free_ptr(W.idx); free_ptr(W.wts); free_ptr(W.blockhist);
     free_ptr(W.counts); free_ptr(W.eoff); free_ptr(W.mtiles); free_ptr(W.num_mtiles);
+    free_ptr(W.ptiles); free_ptr(W.num_ptiles);
     free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.a_hi); free_ptr(W.a_lo);
     free_ptr(W.h_hi); free_ptr(W.h_lo); free_ptr(W.x_stage); free_ptr(W.y_stage);
     free_ptr(W.dev_err); free_ptr(W.h_dec); free_ptr(W.dec_counter);
@@ -114,6 +115,8 @@ int ensure_workspace(Layer& L, int T) {
     MOE_CUDA(dalloc(&W.eoff, sizeof(int) * (E + 1), &bytes));
     MOE_CUDA(dalloc(&W.mtiles, sizeof(MTile) * cap_mtiles, &bytes));
     MOE_CUDA(dalloc(&W.num_mtiles, sizeof(int), &bytes));
+    MOE_CUDA(dalloc(&W.ptiles, sizeof(MTile) * cap_mtiles, &bytes));
+    MOE_CUDA(dalloc(&W.num_ptiles, sizeof(int), &bytes));
     MOE_CUDA(dalloc(&W.row_token, sizeof(int) * cap_rows, &bytes));
     MOE_CUDA(dalloc(&W.row_weight, sizeof(float) * cap_rows, &bytes));
     MOE_CUDA(dalloc(&W.a_hi, eb * cap_rows * L.d, &bytes));
@@ -128,6 +131,7 @@ int ensure_workspace(Layer& L, int T) {
     MOE_CUDA(dalloc(&W.dev_err, sizeof(int), &bytes));
     MOE_CUDA(cudaMemset(W.dev_err, 0, sizeof(int)));
     MOE_CUDA(cudaMemset(W.num_mtiles, 0, sizeof(int)));
+    MOE_CUDA(cudaMemset(W.num_ptiles, 0, sizeof(int)));
     W.cap_T = capT;
     W.cap_rows = (int)cap_rows;
     W.cap_mtiles = cap_mtiles;
@@ -181,6 +185,8 @@ int validate_config(const MoeConfig& c) {
     if (c.decode_max_tokens < 0 || c.decode_max_tokens > decode_max_supported_tokens())
         return fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
     if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
+    if (c.gemm_variant != MOE_GEMM_CTA_PAIR && c.gemm_variant != MOE_GEMM_SINGLE_CTA)
+        return fail(MOE_ERR_INVALID, "unknown gemm_variant");
     return MOE_OK;
 }
 
@@ -462,6 +468,18 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
         L.tm_w13_lo = L.tm_w13_hi;
         L.tm_w2_lo = L.tm_w2_hi;
     }
+    if (!make_tmap_2d(&L.tm_w13_hi2, L.w13_hi, bf, d, E * 2 * ffp, box_k, kTileN / 2, &err) ||
+        !make_tmap_2d(&L.tm_w2_hi2, L.w2_hi, bf, ffp, E * d, box_k, kTileN / 2, &err))
+        return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
+    if (tf) {
+        if (!make_tmap_2d(&L.tm_w13_lo2, L.w13_lo, false, d, E * 2 * ffp, box_k, kTileN / 2, &err) ||
+            !make_tmap_2d(&L.tm_w2_lo2, L.w2_lo, false, ffp, E * d, box_k, kTileN / 2, &err))
+            return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
+    } else {
+        L.tm_w13_lo2 = L.tm_w13_hi2;
+        L.tm_w2_lo2 = L.tm_w2_hi2;
+    }
+    L.pair_gemm = cfg->gemm_variant == MOE_GEMM_CTA_PAIR;
     rc = ensure_workspace(L, std::max(cfg->max_tokens, 1));
     if (rc) return cleanup_and_fail(rc);
 #undef MOE_CUDA_C

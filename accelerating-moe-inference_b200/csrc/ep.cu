@@ -267,7 +267,7 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
             return cuda_err(ce, "router");
         if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
                                       W.counts, S.send_eoff, nullptr, nullptr, nullptr, nullptr,
-                                      s)) != cudaSuccess)
+                                      nullptr, nullptr, s)) != cudaSuccess)
             return cuda_err(ce, "dispatch scan");
         if ((ce = launch_dispatch_permute_to(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w,
                                              S.send_rows, s)) != cudaSuccess)
@@ -310,7 +310,8 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 5-6: arrange and run the local experts.
     if (R > 0) {
         if ((ce = launch_scan_generic(S.cnt_scan, G, El, kTileM, W.counts, W.eoff, W.mtiles,
-                                      W.num_mtiles, W.row_token, W.row_weight, s)) != cudaSuccess)
+                                      W.num_mtiles, W.ptiles, W.num_ptiles, W.row_token,
+                                      W.row_weight, s)) != cudaSuccess)
             return cuda_err(ce, "arrival scan");
         const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
         const int grid = (R + 7) / 8;

@@ -91,6 +91,124 @@ __device__ __forceinline__ TileCoord decode_tile(const MTile* __restrict__ mtile
     return c;
 }
 
+// One accumulator tile out of TMEM for the calling warp's 32 rows: lane i
+// holds row (lane quarter base + i); `valid` rows are written.  tcgen05.ld is
+// warp-collective, so every lane runs the loads.
+template <bool kTf32x3, int kEpi>
+__device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbase, bool valid,
+                                              size_t prow, int nt) {
+    if constexpr (kEpi == kEpiGateUp) {
+#pragma unroll 1
+        for (int c = 0; c < kTileN / 2; c += 32) {
+            uint32_t g[32], u[32];
+            tmem_ld32(tbase + c, g);
+            tmem_ld32(tbase + kTileN / 2 + c, u);
+            tmem_ld_wait();
+            const int col = nt * (kTileN / 2) + c;
+            if (valid) {
+                if constexpr (kTf32x3) {
+                    float4* dh = reinterpret_cast<float4*>(
+                        static_cast<float*>(p.h_hi) + prow * p.ldh + col);
+                    float4* dl = reinterpret_cast<float4*>(
+                        static_cast<float*>(p.h_lo) + prow * p.ldh + col);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 hv, lv;
+                        float h0 = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                        float h1 = silu_f(__uint_as_float(g[j + 1])) * __uint_as_float(u[j + 1]);
+                        float h2 = silu_f(__uint_as_float(g[j + 2])) * __uint_as_float(u[j + 2]);
+                        float h3 = silu_f(__uint_as_float(g[j + 3])) * __uint_as_float(u[j + 3]);
+                        hv.x = to_tf32(h0); lv.x = to_tf32(h0 - hv.x);
+                        hv.y = to_tf32(h1); lv.y = to_tf32(h1 - hv.y);
+                        hv.z = to_tf32(h2); lv.z = to_tf32(h2 - hv.z);
+                        hv.w = to_tf32(h3); lv.w = to_tf32(h3 - hv.w);
+                        dh[j / 4] = hv;
+                        dl[j / 4] = lv;
+                    }
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(
+                        static_cast<__nv_bfloat16*>(p.h_hi) + prow * p.ldh + col);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float a = silu_f(__uint_as_float(g[j + 2 * i])) *
+                                            __uint_as_float(u[j + 2 * i]);
+                            const float b = silu_f(__uint_as_float(g[j + 2 * i + 1])) *
+                                            __uint_as_float(u[j + 2 * i + 1]);
+                            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+                            w4[i] = *reinterpret_cast<uint32_t*>(&v2);
+                        }
+                        dst[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+            }
+        }
+    } else if constexpr (kEpi == kEpiDownStore) {
+        // Expert parallelism: each row's result goes back to the rank
+        // that sent it, at the row it arrived in -- fp32 in FP32
+        // precision, bf16 in BF16 precision (half the return bytes).
+        const int dst = valid ? p.row_token[prow] : 0;
+#pragma unroll 1
+        for (int c = 0; c < kTileN; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c, v);
+            tmem_ld_wait();
+            const int col = nt * kTileN + c;
+            if (valid && col < p.d) {
+                if constexpr (kTf32x3) {
+                    float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                 __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                } else {
+                    uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.y) +
+                                                          static_cast<size_t>(dst) * p.d + col);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        uint32_t w4[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[j + 2 * i]),
+                                                                      __uint_as_float(v[j + 2 * i + 1]));
+                            w4[i] = *reinterpret_cast<uint32_t*>(&b2);
+                        }
+                        out[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+            }
+        }
+    } else {
+        int tok = 0;
+        float wgt = 0.0f;
+        if (valid) {
+            tok = p.row_token[prow];
+            wgt = p.row_weight[prow];
+        }
+#pragma unroll 1
+        for (int c = 0; c < kTileN; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c, v);
+            tmem_ld_wait();
+            const int col = nt * kTileN + c;
+            if (valid && col < p.d) {
+                float* dst = p.y + static_cast<size_t>(tok) * p.d + col;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 o;
+                    o.x = wgt * __uint_as_float(v[j]);
+                    o.y = wgt * __uint_as_float(v[j + 1]);
+                    o.z = wgt * __uint_as_float(v[j + 2]);
+                    o.w = wgt * __uint_as_float(v[j + 3]);
+                    atomicAdd(reinterpret_cast<float4*>(dst + j), o);
+                }
+            }
+        }
+    }
+}
+
 template <bool kTf32x3, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
 expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
@@ -264,116 +382,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             const size_t prow = static_cast<size_t>(tile.row0 + row_in_tile);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kAccCols);
-            if constexpr (kEpi == kEpiGateUp) {
-#pragma unroll 1
-                for (int c = 0; c < kTileN / 2; c += 32) {
-                    uint32_t g[32], u[32];
-                    tmem_ld32(tbase + c, g);
-                    tmem_ld32(tbase + kTileN / 2 + c, u);
-                    tmem_ld_wait();
-                    const int col = nt * (kTileN / 2) + c;
-                    if (valid) {
-                        if constexpr (kTf32x3) {
-                            float4* dh = reinterpret_cast<float4*>(
-                                static_cast<float*>(p.h_hi) + prow * p.ldh + col);
-                            float4* dl = reinterpret_cast<float4*>(
-                                static_cast<float*>(p.h_lo) + prow * p.ldh + col);
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                float4 hv, lv;
-                                float h0 = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-                                float h1 = silu_f(__uint_as_float(g[j + 1])) * __uint_as_float(u[j + 1]);
-                                float h2 = silu_f(__uint_as_float(g[j + 2])) * __uint_as_float(u[j + 2]);
-                                float h3 = silu_f(__uint_as_float(g[j + 3])) * __uint_as_float(u[j + 3]);
-                                hv.x = to_tf32(h0); lv.x = to_tf32(h0 - hv.x);
-                                hv.y = to_tf32(h1); lv.y = to_tf32(h1 - hv.y);
-                                hv.z = to_tf32(h2); lv.z = to_tf32(h2 - hv.z);
-                                hv.w = to_tf32(h3); lv.w = to_tf32(h3 - hv.w);
-                                dh[j / 4] = hv;
-                                dl[j / 4] = lv;
-                            }
-                        } else {
-                            uint4* dst = reinterpret_cast<uint4*>(
-                                static_cast<__nv_bfloat16*>(p.h_hi) + prow * p.ldh + col);
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint32_t w4[4];
-#pragma unroll
-                                for (int i = 0; i < 4; ++i) {
-                                    const float a = silu_f(__uint_as_float(g[j + 2 * i])) *
-                                                    __uint_as_float(u[j + 2 * i]);
-                                    const float b = silu_f(__uint_as_float(g[j + 2 * i + 1])) *
-                                                    __uint_as_float(u[j + 2 * i + 1]);
-                                    __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
-                                    w4[i] = *reinterpret_cast<uint32_t*>(&v2);
-                                }
-                                dst[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                            }
-                        }
-                    }
-                }
-            } else if constexpr (kEpi == kEpiDownStore) {
-                // Expert parallelism: each row's result goes back to the rank
-                // that sent it, at the row it arrived in -- fp32 in FP32
-                // precision, bf16 in BF16 precision (half the return bytes).
-                const int dst = valid ? p.row_token[prow] : 0;
-#pragma unroll 1
-                for (int c = 0; c < kTileN; c += 32) {
-                    uint32_t v[32];
-                    tmem_ld32(tbase + c, v);
-                    tmem_ld_wait();
-                    const int col = nt * kTileN + c;
-                    if (valid && col < p.d) {
-                        if constexpr (kTf32x3) {
-                            float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4)
-                                out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                         __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-                        } else {
-                            uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.y) +
-                                                                  static_cast<size_t>(dst) * p.d + col);
-#pragma unroll
-                            for (int j = 0; j < 32; j += 8) {
-                                uint32_t w4[4];
-#pragma unroll
-                                for (int i = 0; i < 4; ++i) {
-                                    __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[j + 2 * i]),
-                                                                              __uint_as_float(v[j + 2 * i + 1]));
-                                    w4[i] = *reinterpret_cast<uint32_t*>(&b2);
-                                }
-                                out[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-                            }
-                        }
-                    }
-                }
-            } else {
-                int tok = 0;
-                float wgt = 0.0f;
-                if (valid) {
-                    tok = p.row_token[prow];
-                    wgt = p.row_weight[prow];
-                }
-#pragma unroll 1
-                for (int c = 0; c < kTileN; c += 32) {
-                    uint32_t v[32];
-                    tmem_ld32(tbase + c, v);
-                    tmem_ld_wait();
-                    const int col = nt * kTileN + c;
-                    if (valid && col < p.d) {
-                        float* dst = p.y + static_cast<size_t>(tok) * p.d + col;
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 o;
-                            o.x = wgt * __uint_as_float(v[j]);
-                            o.y = wgt * __uint_as_float(v[j + 1]);
-                            o.z = wgt * __uint_as_float(v[j + 2]);
-                            o.w = wgt * __uint_as_float(v[j + 3]);
-                            atomicAdd(reinterpret_cast<float4*>(dst + j), o);
-                        }
-                    }
-                }
-            }
+            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, nt);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -387,6 +396,245 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }
+}
+
+// ------------------------------------------------------------ CTA-pair GEMM
+// The same grouped GEMM on 256 x 256 tiles computed by a 2-CTA cluster with
+// tcgen05.mma.cta_group::2: each CTA loads 128 rows of A and 128 rows (half
+// the N tile) of B into its own shared memory, the leader CTA issues the MMAs
+// (which read both CTAs' operands) and each CTA's TMEM holds its 128 rows x
+// 256 columns of the accumulator.  Per SM this halves the B traffic from L2
+// and shared memory.  Barrier protocol:
+//   full[s]    leader only; its producer arms it with both CTAs' bytes, both
+//              CTAs' TMA loads complete on it (cluster address of rank 0);
+//   empty[s]   both CTAs; the leader's commit arrives on both;
+//   tfull[a]   both CTAs; the leader's commit arrives on both;
+//   tempty[a]  leader only; 4 epilogue warps x 2 CTAs arrive.
+template <bool kTf32x3>
+struct PairCfg {
+    static constexpr int kPlanes = kTf32x3 ? 2 : 1;
+    static constexpr int kHalfA = kTileM * 128;          // 128 rows of A
+    static constexpr int kHalfB = (kTileN / 2) * 128;    // 128 rows of B
+    static constexpr int kStageBytes = kPlanes * (kHalfA + kHalfB);
+    static constexpr int kStages = kTf32x3 ? 3 : 6;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
+    static constexpr uint32_t kIdesc = mma_idesc(kTf32x3 ? 2u : 1u, 2 * kTileM, kTileN);
+};
+
+template <bool kTf32x3, int kEpi>
+__global__ void __launch_bounds__(kThreads, 1)
+expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
+                        const __grid_constant__ CUtensorMap tmA_lo,
+                        const __grid_constant__ CUtensorMap tmB_hi,
+                        const __grid_constant__ CUtensorMap tmB_lo, const GemmParams p) {
+    using C = PairCfg<kTf32x3>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    uint64_t* empty = full + C::kStages;
+    uint64_t* tfull = empty + C::kStages;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* done = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t crank = cluster_ctarank();
+    const bool leader = crank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 8);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA_hi);
+        tma_prefetch_desc(&tmB_hi);
+        if constexpr (kTf32x3) {
+            tma_prefetch_desc(&tmA_lo);
+            tma_prefetch_desc(&tmB_lo);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();                     // barriers of both CTAs initialised
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int p_tiles = *p.num_mtiles;  // pair tiles (num_ptiles)
+    const int total = p_tiles * p.n_tiles;
+    const int cid = blockIdx.x >> 1;
+    const int nclusters = gridDim.x >> 1;
+    const uint32_t full0 = mapa_shared(&full[0], 0);     // leader's full[0]
+    const uint32_t tempty0 = mapa_shared(&tempty[0], 0); // leader's tempty[0]
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            constexpr int kElems = kTf32x3 ? 32 : 64;
+            for (int t = cid; t < total && !*abort_flag; t += nclusters) {
+                const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+                const MTile tile = p.mtiles[tc.mt];
+                const int arow = tile.row0 + (int)crank * kTileM;
+                const int brow = tile.expert * p.b_rows_per_expert + tc.nt * kTileN +
+                                 (int)crank * (kTileN / 2);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, kDevErrTimeoutProducer)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t* sbase = smem + stage * C::kStageBytes;
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
+                    const uint32_t fb = full0 + stage * 8;
+                    const int kx = kb * kElems;
+                    tma_load_2d_pair(sbase, &tmA_hi, fb, kx, arow);
+                    if constexpr (kTf32x3) {
+                        tma_load_2d_pair(sbase + C::kHalfA, &tmA_lo, fb, kx, arow);
+                        tma_load_2d_pair(sbase + 2 * C::kHalfA, &tmB_hi, fb, kx, brow);
+                        tma_load_2d_pair(sbase + 2 * C::kHalfA + C::kHalfB, &tmB_lo, fb, kx, brow);
+                    } else {
+                        tma_load_2d_pair(sbase + C::kHalfA, &tmB_hi, fb, kx, brow);
+                    }
+                    ++issued;
+                    if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (*abort_flag && leader) {
+                const int pending = issued < C::kStages ? issued : C::kStages;
+                int s = stage;
+                uint32_t ph = phase;
+                for (int i = 0; i < pending; ++i) {
+                    if (--s < 0) { s = C::kStages - 1; ph ^= 1u; }
+                    mbar_wait(&full[s], ph, p.err, kDevErrTimeoutDrain);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int t = cid; t < total && !*abort_flag; t += nclusters) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err, kDevErrTimeoutMma)) {
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                bool ok = true;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, p.err, kDevErrTimeoutMma)) {
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = smem_u32(smem + stage * C::kStageBytes);
+                    const uint64_t a_hi = smem_desc_sw128(sbase);
+                    uint64_t a_lo = 0, b_hi, b_lo = 0;
+                    if constexpr (kTf32x3) {
+                        a_lo = smem_desc_sw128(sbase + C::kHalfA);
+                        b_hi = smem_desc_sw128(sbase + 2 * C::kHalfA);
+                        b_lo = smem_desc_sw128(sbase + 2 * C::kHalfA + C::kHalfB);
+                    } else {
+                        b_hi = smem_desc_sw128(sbase + C::kHalfA);
+                    }
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint64_t off = static_cast<uint64_t>(ks * 2);
+                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        if constexpr (kTf32x3) {
+                            tc_mma_pair<true>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
+                            tc_mma_pair<true>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
+                            tc_mma_pair<true>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
+                        } else {
+                            tc_mma_pair<false>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, accum);
+                        }
+                    }
+                    tc_commit_pair(&empty[stage], 0x3);
+                    if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                tc_commit_pair(&tfull[acc], 0x3);
+                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+            tc_commit_pair(done, 0x1);
+            mbar_wait(done, 0, p.err, kDevErrTimeoutDrain);
+        }
+    } else {
+        const int q = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = cid; t < total; t += nclusters) {
+            if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+            const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+            const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err, kDevErrTimeoutEpilogue);
+            if (!__all_sync(0xffffffffu, ready)) {
+                if (lane == 0) *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const MTile tile = p.mtiles[tc.mt];
+            const int half_rows = crank == 0 ? tile.rows : tile.pad[0];
+            const bool valid = row_in_tile < half_rows;
+            const size_t prow = static_cast<size_t>(tile.row0 + (int)crank * kTileM + row_in_tile);
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                   static_cast<uint32_t>(acc * kAccCols);
+            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, tc.nt);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                     // the leader's MMAs (which read both CTAs) are done
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
+template <bool kTf32x3, int kEpi>
+cudaError_t launch_pair(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                        const CUtensorMap& b_lo, const GemmParams& p, int clusters,
+                        cudaStream_t s) {
+    using C = PairCfg<kTf32x3>;
+    auto kern = expert_gemm_pair_kernel<kTf32x3, kEpi>;
+    cudaError_t err =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a_hi, a_lo, b_hi, b_lo, p);
 }
 
 template <bool kTf32x3, int kEpi>
@@ -437,6 +685,33 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         g.n_tiles = (L.d + kTileN - 1) / kTileN;
         g.k_blocks = L.ffp / elems;
         g.b_rows_per_expert = L.d;
+    }
+    if (L.pair_gemm) {
+        // CTA-pair tiles: 256 rows x 256 columns per 2-SM cluster.
+        GemmParams gp = g;
+        gp.mtiles = W.ptiles;
+        gp.num_mtiles = W.num_ptiles;
+        int clusters = ((routed_rows + 2 * kTileM - 1) / (2 * kTileM) + L.E) * g.n_tiles;
+        if (clusters > L.sm_count / 2) clusters = L.sm_count / 2;
+        if (!down) {
+            if (tf)
+                return launch_pair<true, kEpiGateUp>(W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi2, L.tm_w13_lo2,
+                                                     gp, clusters, s);
+            return launch_pair<false, kEpiGateUp>(W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi2, L.tm_w13_hi2,
+                                                  gp, clusters, s);
+        }
+        if (mode == 2) {
+            if (tf)
+                return launch_pair<true, kEpiDownStore>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2,
+                                                        L.tm_w2_lo2, gp, clusters, s);
+            return launch_pair<false, kEpiDownStore>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2,
+                                                     gp, clusters, s);
+        }
+        if (tf)
+            return launch_pair<true, kEpiDown>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2, L.tm_w2_lo2, gp,
+                                               clusters, s);
+        return launch_pair<false, kEpiDown>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2, gp,
+                                            clusters, s);
     }
     int grid = max_mtiles * g.n_tiles;
     if (grid > L.sm_count) grid = L.sm_count;

@@ -41,7 +41,9 @@ constexpr int kMaxTopK = 8;
 constexpr int kProfileStages = 5;
 
 // One 128-row slice of an expert's packed block.  m-tiles are listed expert
-// by expert; mstart / mcount locate the expert's own run in that list.
+// by expert; mstart / mcount locate the expert's own run in that list.  The
+// pair list (CTA-pair GEMM) uses the same struct for 256-row slices: rows is
+// the first half's valid rows and pad[0] the second half's.
 struct MTile {
     int expert;
     int row0;    // first packed row
@@ -63,6 +65,8 @@ struct Workspace {
     int* eoff = nullptr;
     MTile* mtiles = nullptr;
     int* num_mtiles = nullptr;
+    MTile* ptiles = nullptr;    // 256-row pair tiles (two m-tiles of one expert)
+    int* num_ptiles = nullptr;
     int* row_token = nullptr;
     float* row_weight = nullptr;
     void* a_hi = nullptr;
@@ -99,6 +103,10 @@ struct Layer {
     float* w13_f32 = nullptr;
     float* w2_f32 = nullptr;
     CUtensorMap tm_w13_hi, tm_w13_lo, tm_w2_hi, tm_w2_lo;
+    // The same weights in 128-row boxes: each CTA of a pair loads half of the
+    // 256-wide N tile.
+    CUtensorMap tm_w13_hi2, tm_w13_lo2, tm_w2_hi2, tm_w2_lo2;
+    bool pair_gemm = false;     // 2-CTA (cta_group::2) 256 x 256 tiles
     Workspace ws;
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;
@@ -132,8 +140,8 @@ cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, in
 // The scan on any [nblk][E] count matrix, expert blocks rounded to `granule`
 // rows; mtiles == nullptr gives a compact layout with no tiles or padding.
 cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
-                                MTile* mtiles, int* num_mtiles, int* row_token,
-                                float* row_weight, cudaStream_t s);
+                                MTile* mtiles, int* num_mtiles, MTile* ptiles, int* num_ptiles,
+                                int* row_token, float* row_weight, cudaStream_t s);
 
 // expert_gemm.cu
 // down == false: gate/up GEMM with the SwiGLU epilogue into H;

@@ -264,11 +264,13 @@ __device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
 __global__ void __launch_bounds__(kScanThreads)
 dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
                      int* __restrict__ counts, int* __restrict__ eoff, MTile* __restrict__ mtiles,
-                     int* __restrict__ num_mtiles, int* __restrict__ row_token,
+                     int* __restrict__ num_mtiles, MTile* __restrict__ ptiles,
+                     int* __restrict__ num_ptiles, int* __restrict__ row_token,
                      float* __restrict__ row_weight) {
     __shared__ int s_cnt[kMaxExperts];
     __shared__ int s_off[kMaxExperts + 1];
     __shared__ int s_mst[kMaxExperts + 1];
+    __shared__ int s_pst[kMaxExperts + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kWarps = kScanThreads / 32;
     for (int e = warp; e < E; e += kWarps) {
@@ -287,27 +289,33 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
     }
     __syncthreads();
     if (warp == 0) {
-        int run_off = 0, run_m = 0;
+        int run_off = 0, run_m = 0, run_p = 0;
         for (int e0 = 0; e0 < E; e0 += 32) {
             const int e = e0 + lane;
             const int c = e < E ? s_cnt[e] : 0;
             const int mc = (c + kTileM - 1) / kTileM;
+            const int qc = (mc + 1) / 2;                  // 256-row pair tiles
             const int pc = (c + granule - 1) / granule * granule;
             const int ipc = warp_inclusive_scan(pc, lane);
             const int imc = warp_inclusive_scan(mc, lane);
+            const int iqc = warp_inclusive_scan(qc, lane);
             if (e < E) {
                 s_off[e] = run_off + ipc - pc;
                 s_mst[e] = run_m + imc - mc;
+                s_pst[e] = run_p + iqc - qc;
                 eoff[e] = s_off[e];
             }
             run_off += __shfl_sync(0xffffffffu, ipc, 31);
             run_m += __shfl_sync(0xffffffffu, imc, 31);
+            run_p += __shfl_sync(0xffffffffu, iqc, 31);
         }
         if (lane == 0) {
             s_off[E] = run_off;
             s_mst[E] = run_m;
+            s_pst[E] = run_p;
             eoff[E] = run_off;
             if (num_mtiles) *num_mtiles = run_m;
+            if (num_ptiles) *num_ptiles = run_p;
         }
     }
     __syncthreads();
@@ -325,6 +333,21 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
             mt.mcount = mc;
             mt.pad[0] = mt.pad[1] = mt.pad[2] = 0;
             mtiles[mst + i] = mt;
+        }
+        if (ptiles) {
+            const int pst = s_pst[e];
+            const int pc = s_pst[e + 1] - pst;
+            for (int i = lane; i < pc; i += 32) {
+                MTile pt;
+                pt.expert = e;
+                pt.row0 = s_off[e] + 2 * i * kTileM;
+                pt.rows = min(kTileM, c - 2 * i * kTileM);
+                pt.mstart = pst;
+                pt.mcount = pc;
+                pt.pad[0] = max(0, min(kTileM, c - (2 * i + 1) * kTileM));   // second half
+                pt.pad[1] = pt.pad[2] = 0;
+                ptiles[pst + i] = pt;
+            }
         }
         for (int r = s_off[e] + c + lane; r < s_off[e + 1]; r += 32) {
             row_token[r] = -1;
@@ -482,16 +505,17 @@ cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
     const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     const Workspace& W = L.ws;
     dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(W.blockhist, nblk, L.E_route, kTileM, W.counts,
-                                                  W.eoff, W.mtiles, W.num_mtiles, W.row_token,
-                                                  W.row_weight);
+                                                  W.eoff, W.mtiles, W.num_mtiles, W.ptiles,
+                                                  W.num_ptiles, W.row_token, W.row_weight);
     return cudaGetLastError();
 }
 
 cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
-                                MTile* mtiles, int* num_mtiles, int* row_token,
-                                float* row_weight, cudaStream_t s) {
+                                MTile* mtiles, int* num_mtiles, MTile* ptiles, int* num_ptiles,
+                                int* row_token, float* row_weight, cudaStream_t s) {
     dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(hist, nblk, E, granule, counts, eoff, mtiles,
-                                                  num_mtiles, row_token, row_weight);
+                                                  num_mtiles, ptiles, num_ptiles, row_token,
+                                                  row_weight);
     return cudaGetLastError();
 }
 

@@ -67,6 +67,15 @@ typedef enum MoePrecision {
     MOE_PREC_BF16 = 1
 } MoePrecision;
 
+/* Tiling of the tcgen05 grouped expert GEMMs.
+ * CTA_PAIR: 256 x 256 tiles on 2-CTA clusters (tcgen05 cta_group::2), each SM
+ *   loading half of every weight tile.
+ * SINGLE_CTA: 128 x 256 tiles, one CTA per SM. */
+typedef enum MoeGemmVariant {
+    MOE_GEMM_CTA_PAIR = 0,
+    MOE_GEMM_SINGLE_CTA = 1
+} MoeGemmVariant;
+
 typedef struct MoeConfig {
     int32_t d_model;        /* hidden size; multiple of 64 */
     int32_t d_ff;           /* expert intermediate size (any; padded internally) */
@@ -80,7 +89,8 @@ typedef struct MoeConfig {
                                   (0..64; 0: never; default 16) */
     int32_t device;         /* CUDA device ordinal the handle lives on */
     int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
-    int32_t reserved[5];
+    int32_t gemm_variant;   /* MoeGemmVariant of the grouped expert GEMMs */
+    int32_t reserved[4];
 } MoeConfig;
 
 /* Host fp32 weights of one layer (the tensors PhiMoE loads by name,

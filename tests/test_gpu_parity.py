@@ -61,14 +61,19 @@ def test_router_matches_golden(name, tag, policy):
     assert ulp.max() <= 1
 
 
+GEMMS = pytest.mark.parametrize("gemm", [0, 1], ids=["ctapair", "single"])
+
+
+@GEMMS
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
 @pytest.mark.parametrize("name,tag,policy", CASE_POL)
-def test_forward_matches_golden(name, tag, policy, precision):
+def test_forward_matches_golden(name, tag, policy, precision, gemm):
     pkg = load_pkg()
     layer, x = case_inputs(pkg, name)
     g = np.load(GOLDEN_DIR / f"{name}.npz")
     y_ref = g[f"{tag}_y"]
-    with pkg.MoeLayer(layer, top_k=CASES[name]["k"], policy=policy, precision=precision) as m:
+    with pkg.MoeLayer(layer, top_k=CASES[name]["k"], policy=policy, precision=precision,
+                      gemm_variant=gemm) as m:
         y = m.forward_host(x)
         y2 = m.forward_host(x)
     err = rel_l2(y, y_ref)
@@ -117,8 +122,9 @@ def test_ragged_token_counts(T, precision, orc):
     assert rel_l2(y, y_ref) <= TOL[precision]
 
 
+@GEMMS
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
-def test_skewed_routing_and_empty_experts(precision, orc):
+def test_skewed_routing_and_empty_experts(precision, gemm, orc):
     """A router bias sends every token to experts 3 and 5: their blocks span
     several 128-row tiles and the other experts get no rows at all."""
     pkg = load_pkg()
@@ -127,21 +133,22 @@ def test_skewed_routing_and_empty_experts(precision, orc):
     layer = pkg.synthetic_layer(22, 128, 256, 8, router_bias=bias)
     x = pkg.synthetic_tokens(22, 700, 128)
     y_ref, idx_ref, *_ = orc.moe_forward(x, layer, 2, oracle.POLICY_SOFTMAX)
-    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision) as m:
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, gemm_variant=gemm) as m:
         y = m.forward_host(x)
         counts = m.expert_counts()
     assert counts[3] == counts[5] == 700 and counts.sum() == 1400
     assert rel_l2(y, y_ref) <= TOL[precision]
 
 
-def test_permutation_equivariance_bit_exact():
+@GEMMS
+def test_permutation_equivariance_bit_exact(gemm):
     """Each token's output depends only on its own row: permuting the tokens
     permutes the outputs bit for bit (top-2, so the combine is order-free)."""
     pkg = load_pkg()
     layer = pkg.synthetic_layer(23, 512, 768, 8)
     x = pkg.synthetic_tokens(23, 1000, 512)
     perm = np.random.default_rng(0).permutation(1000)
-    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=1) as m:
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=1, gemm_variant=gemm) as m:
         y = m.forward_host(x)
         yp = m.forward_host(x[perm])
     assert np.array_equal(bits(yp), bits(y[perm]))
@@ -208,3 +215,15 @@ def test_decode_threshold_bounds():
     with pkg.MoeLayer(layer, top_k=2, policy=1) as m:
         with pytest.raises(pkg.MoeError):
             m.set_decode_max_tokens(65)
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_gemm_variants_agree(precision):
+    """The CTA-pair and single-CTA GEMMs compute every output row with the
+    same K order, so their results are bit-identical (top-2)."""
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(24, 512, 640, 8)
+    x = pkg.synthetic_tokens(24, 777, 512)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, gemm_variant=0) as a, \
+            pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, gemm_variant=1) as b:
+        assert np.array_equal(bits(a.forward_host(x)), bits(b.forward_host(x)))
