@@ -30,8 +30,9 @@ ROUTER_PHI_QUANTISED = 0
 ROUTER_SOFTMAX_TOPK = 1
 PREC_FP32 = 0
 PREC_BF16 = 1
-GEMM_CTA_PAIR = 0
+GEMM_AUTO = 0
 GEMM_SINGLE_CTA = 1
+GEMM_CTA_PAIR = 2
 
 # Every symbol include/moe_b200.h declares.
 EXPORTED_SYMBOLS = (

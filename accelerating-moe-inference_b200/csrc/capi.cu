@@ -185,7 +185,7 @@ int validate_config(const MoeConfig& c) {
     if (c.decode_max_tokens < 0 || c.decode_max_tokens > decode_max_supported_tokens())
         return fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
     if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
-    if (c.gemm_variant != MOE_GEMM_CTA_PAIR && c.gemm_variant != MOE_GEMM_SINGLE_CTA)
+    if (c.gemm_variant < MOE_GEMM_AUTO || c.gemm_variant > MOE_GEMM_CTA_PAIR)
         return fail(MOE_ERR_INVALID, "unknown gemm_variant");
     return MOE_OK;
 }
@@ -214,7 +214,8 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     prof_mark(L, 0, s);
     MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s));
     prof_mark(L, 1, s);
-    MOE_CUDA(launch_dispatch_scan(L, T, s));
+    // A batch that fits one router block is scanned inside the permute kernel.
+    if (T > kRouteTokens) MOE_CUDA(launch_dispatch_scan(L, T, s));
     prof_mark(L, 2, s);
     if (T <= L.cfg.decode_max_tokens) {
         MOE_CUDA(launch_decode(L, x, T, y, s));  // marks stages 3 and 4 between its kernels
@@ -479,7 +480,7 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
         L.tm_w13_lo2 = L.tm_w13_hi2;
         L.tm_w2_lo2 = L.tm_w2_hi2;
     }
-    L.pair_gemm = cfg->gemm_variant == MOE_GEMM_CTA_PAIR;
+    L.gemm_variant = cfg->gemm_variant;
     rc = ensure_workspace(L, std::max(cfg->max_tokens, 1));
     if (rc) return cleanup_and_fail(rc);
 #undef MOE_CUDA_C

@@ -686,7 +686,13 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         g.k_blocks = L.ffp / elems;
         g.b_rows_per_expert = L.d;
     }
-    if (L.pair_gemm) {
+    // CTA-pair tiles pay off when experts have at least 256 routed rows on
+    // average; below that (decode-sized T) most of a 256-row tile would be
+    // padding and the 1-CTA tiles spread the weight stream over twice as many
+    // SMs.
+    const bool pair = L.gemm_variant == MOE_GEMM_CTA_PAIR ||
+                      (L.gemm_variant == MOE_GEMM_AUTO && routed_rows >= 2 * kTileM * L.E);
+    if (pair) {
         // CTA-pair tiles: 256 rows x 256 columns per 2-SM cluster.
         GemmParams gp = g;
         gp.mtiles = W.ptiles;

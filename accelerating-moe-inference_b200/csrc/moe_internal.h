@@ -106,7 +106,7 @@ struct Layer {
     // The same weights in 128-row boxes: each CTA of a pair loads half of the
     // 256-wide N tile.
     CUtensorMap tm_w13_hi2, tm_w13_lo2, tm_w2_hi2, tm_w2_lo2;
-    bool pair_gemm = false;     // 2-CTA (cta_group::2) 256 x 256 tiles
+    int gemm_variant = 0;       // MoeGemmVariant
     Workspace ws;
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;

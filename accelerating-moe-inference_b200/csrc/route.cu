@@ -32,6 +32,17 @@ namespace {
 
 constexpr int kRouterThreads = 256;
 
+// Outputs of the scan, handed to the permute kernel when it also does the
+// scan (single-block dispatch); all null otherwise.
+struct ScanOut {
+    int* counts = nullptr;
+    int* eoff = nullptr;
+    MTile* mtiles = nullptr;
+    int* num_mtiles = nullptr;
+    MTile* ptiles = nullptr;
+    int* num_ptiles = nullptr;
+};
+
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
     const uint32_t s = smem_u32(smem);
     const int n = pred ? 16 : 0;
@@ -113,49 +124,39 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         const float* xr = xs + st * kXs + tt * kLd;
         const float* wr = ws + st * kWs + el * kLd;
         // Fully unrolled over the chunk, every shared-memory offset an
-        // immediate, and the operands of the next 16-wide group loaded while
-        // the current group's FMAs run (the chain itself cannot overlap).
-        // Lanes whose expert index is past E run chains on unused rows that
-        // are never stored.
-        float4 xa[4], wa[EJ][4];
+        // immediate.  Two register sets alternate (ping-pong, no copies): the
+        // loads of the next 16-wide group are issued before the current
+        // group's dependent FMAs, which the loads then overlap.  Lanes whose
+        // expert index is past E run chains on unused rows that are never
+        // stored.
+        float4 xa[4], wa[EJ][4], xb[4], wb[EJ][4];
+        auto load_group = [&](float4 (&xv)[4], float4 (&wv)[EJ][4], int kk) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) xa[q] = *reinterpret_cast<const float4*>(xr + 4 * q);
+            for (int q = 0; q < 4; ++q) xv[q] = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
 #pragma unroll
-        for (int j = 0; j < EJ; ++j)
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-                wa[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + 4 * q);
-#pragma unroll
-        for (int kk = 0; kk < KC; kk += 16) {
-            float4 xb[4], wb[EJ][4];
-            if (kk + 16 < KC) {
+            for (int j = 0; j < EJ; ++j)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                    xb[q] = *reinterpret_cast<const float4*>(xr + kk + 16 + 4 * q);
+                    wv[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 4 * q);
+        };
+        auto chain_group = [&](const float4 (&xv)[4], const float4 (&wv)[EJ][4]) {
 #pragma unroll
-                for (int j = 0; j < EJ; ++j)
+            for (int q = 0; q < 4; ++q)
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        wb[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 16 + 4 * q);
-            }
-#pragma unroll
-            for (int j = 0; j < EJ; ++j) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc[j] = __fmaf_rn(xa[q].x, wa[j][q].x, acc[j]);
-                    acc[j] = __fmaf_rn(xa[q].y, wa[j][q].y, acc[j]);
-                    acc[j] = __fmaf_rn(xa[q].z, wa[j][q].z, acc[j]);
-                    acc[j] = __fmaf_rn(xa[q].w, wa[j][q].w, acc[j]);
+                for (int j = 0; j < EJ; ++j) {
+                    acc[j] = __fmaf_rn(xv[q].x, wv[j][q].x, acc[j]);
+                    acc[j] = __fmaf_rn(xv[q].y, wv[j][q].y, acc[j]);
+                    acc[j] = __fmaf_rn(xv[q].z, wv[j][q].z, acc[j]);
+                    acc[j] = __fmaf_rn(xv[q].w, wv[j][q].w, acc[j]);
                 }
-            }
-            if (kk + 16 < KC) {
+        };
+        load_group(xa, wa, 0);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) xa[q] = xb[q];
-#pragma unroll
-                for (int j = 0; j < EJ; ++j)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) wa[j][q] = wb[j][q];
-            }
+        for (int kk = 0; kk < KC; kk += 32) {
+            load_group(xb, wb, kk + 16);
+            chain_group(xa, wa);
+            if (kk + 32 < KC) load_group(xa, wa, kk + 32);
+            chain_group(xb, wb);
         }
     }
     cp_async_wait<0>();
@@ -356,22 +357,83 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
     }
 }
 
+// Tiles of one expert-block layout from per-expert counts held in shared
+// memory (single-block dispatch: T fits one 32-token router block, so the
+// block histogram is the whole count and the scan is a prefix over experts).
+// Called by every thread of the CTA; writes the layout only if `write`.
+__device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_off, bool write,
+                                    int* __restrict__ counts, int* __restrict__ eoff,
+                                    MTile* __restrict__ mtiles, int* __restrict__ num_mtiles,
+                                    MTile* __restrict__ ptiles, int* __restrict__ num_ptiles,
+                                    int* __restrict__ row_token, float* __restrict__ row_weight) {
+    if (threadIdx.x == 0) {
+        int off = 0, nm = 0, np = 0;
+        for (int e = 0; e < E; ++e) {
+            const int c = cnt[e];
+            s_off[e] = off;
+            if (write) {
+                counts[e] = c;
+                eoff[e] = off;
+                const int mc = (c + kTileM - 1) / kTileM;
+                const int qc = (mc + 1) / 2;
+                for (int i = 0; i < mc; ++i) {
+                    MTile mt;
+                    mt.expert = e; mt.row0 = off + i * kTileM; mt.rows = min(kTileM, c - i * kTileM);
+                    mt.mstart = nm; mt.mcount = mc; mt.pad[0] = mt.pad[1] = mt.pad[2] = 0;
+                    mtiles[nm + i] = mt;
+                }
+                for (int i = 0; i < qc; ++i) {
+                    MTile pt;
+                    pt.expert = e; pt.row0 = off + 2 * i * kTileM;
+                    pt.rows = min(kTileM, c - 2 * i * kTileM);
+                    pt.mstart = np; pt.mcount = qc;
+                    pt.pad[0] = max(0, min(kTileM, c - (2 * i + 1) * kTileM));
+                    pt.pad[1] = pt.pad[2] = 0;
+                    ptiles[np + i] = pt;
+                }
+                for (int r = off + c; r < off + mc * kTileM; ++r) {
+                    row_token[r] = -1;
+                    row_weight[r] = 0.0f;
+                }
+                nm += mc;
+                np += qc;
+            }
+            off += (c + kTileM - 1) / kTileM * kTileM;
+        }
+        s_off[E] = off;
+        if (write) {
+            eoff[E] = off;
+            *num_mtiles = nm;
+            *num_ptiles = np;
+        }
+    }
+    __syncthreads();
+}
+
 template <int kMode>  // 0: bf16 plane, 1: tf32 hi + lo planes, 2: fp32 as is (decode)
 __global__ void __launch_bounds__(256)
 dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                         const int* __restrict__ idx, const float* __restrict__ wts,
                         const int* __restrict__ blockbase, const int* __restrict__ eoff,
                         int* __restrict__ row_token, float* __restrict__ row_weight,
-                        void* __restrict__ a_hi, void* __restrict__ a_lo) {
+                        void* __restrict__ a_hi, void* __restrict__ a_lo, ScanOut so) {
     __shared__ unsigned s_mask[kMaxExperts];
-    __shared__ int s_base[kMaxExperts];
+    __shared__ int s_base[kMaxExperts + 1];
     __shared__ int s_dest[kRouteTokens * kMaxTopK];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kRouteTokens;
     const int n_tok = min(kRouteTokens, T - t0);
-    for (int e = tid; e < E; e += blockDim.x) {
-        s_mask[e] = 0u;
-        s_base[e] = eoff[e] + blockbase[(size_t)blockIdx.x * E + e];
+    if (so.counts) {
+        // Single-block dispatch: this kernel also does the scan.  blockbase
+        // holds the one block's histogram.
+        single_block_layout(blockbase, E, s_base, blockIdx.y == 0, so.counts, so.eoff, so.mtiles,
+                            so.num_mtiles, so.ptiles, so.num_ptiles, row_token, row_weight);
+        for (int e = tid; e < E; e += blockDim.x) s_mask[e] = 0u;
+    } else {
+        for (int e = tid; e < E; e += blockDim.x) {
+            s_mask[e] = 0u;
+            s_base[e] = eoff[e] + blockbase[(size_t)blockIdx.x * E + e];
+        }
     }
     __syncthreads();
     const int n_ent = n_tok * k;
@@ -442,6 +504,9 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
         }
     }
 }
+
+// T fits one router block: the permute kernel does the scan as well.
+bool single_block(int T) { return T <= kRouteTokens; }
 
 // Token blocks x column splits: enough CTAs (about 4 per SM) to keep tens of
 // MB of row loads in flight.
@@ -521,8 +586,21 @@ cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* co
 
 cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s) {
     const Workspace& W = L.ws;
-    return launch_dispatch_permute_to(L, x, T, L.E_route, W.eoff, W.row_token, W.row_weight,
-                                      W.a_hi, s);
+    const dim3 grid = permute_grid(L, T);
+    ScanOut so;
+    if (single_block(T)) {
+        so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
+        so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
+    }
+    if (three_pass(L))
+        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, nullptr, so);
+    else
+        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
+                                                        W.blockhist, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, nullptr, so);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
@@ -533,25 +611,30 @@ cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, in
     if (three_pass(L))
         dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr);
+                                                        row_weight, rows, nullptr, ScanOut{});
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr);
+                                                        row_weight, rows, nullptr, ScanOut{});
     return cudaGetLastError();
 }
 
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s) {
     const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
+    ScanOut so;
+    if (single_block(T)) {
+        so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
+        so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
+    }
     if (three_pass(L))
         dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo);
+                                                        W.row_weight, W.a_hi, W.a_lo, so);
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo);
+                                                        W.row_weight, W.a_hi, W.a_lo, so);
     return cudaGetLastError();
 }
 

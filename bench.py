@@ -78,7 +78,8 @@ def _peaks():
 
 
 def _gemm_variant(args, pkg):
-    return pkg.GEMM_SINGLE_CTA if args.gemm == "single" else pkg.GEMM_CTA_PAIR
+    return {"auto": pkg.GEMM_AUTO, "single": pkg.GEMM_SINGLE_CTA,
+            "ctapair": pkg.GEMM_CTA_PAIR}[args.gemm]
 
 
 def _traffic_from_profile(workload: str, precision: str):
@@ -352,8 +353,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
-    ap.add_argument("--gemm", choices=["ctapair", "single"], default="ctapair",
-                    help="grouped-GEMM tiling: 2-CTA 256x256 (default) or 1-CTA 128x256")
+    ap.add_argument("--gemm", choices=["auto", "ctapair", "single"], default="auto",
+                    help="grouped-GEMM tiling: auto (2-CTA 256x256 tiles for prefill, 1-CTA "
+                         "128x256 for decode-sized T), or force one")
     ap.add_argument("--parallelism", choices=["ep", "dp"], default="ep",
                     help="N > 1: expert parallel (default) or token-sharded replicas")
     ap.add_argument("--decode-max-tokens", type=int, default=None,

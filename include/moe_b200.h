@@ -68,12 +68,16 @@ typedef enum MoePrecision {
 } MoePrecision;
 
 /* Tiling of the tcgen05 grouped expert GEMMs.
+ * AUTO: CTA_PAIR when the experts average at least 256 routed rows (prefill),
+ *   SINGLE_CTA below that (decode-sized T, where most of a 256-row tile would
+ *   be padding).
+ * SINGLE_CTA: 128 x 256 tiles, one CTA per SM.
  * CTA_PAIR: 256 x 256 tiles on 2-CTA clusters (tcgen05 cta_group::2), each SM
- *   loading half of every weight tile.
- * SINGLE_CTA: 128 x 256 tiles, one CTA per SM. */
+ *   loading half of every weight tile, at every size. */
 typedef enum MoeGemmVariant {
-    MOE_GEMM_CTA_PAIR = 0,
-    MOE_GEMM_SINGLE_CTA = 1
+    MOE_GEMM_AUTO = 0,
+    MOE_GEMM_SINGLE_CTA = 1,
+    MOE_GEMM_CTA_PAIR = 2
 } MoeGemmVariant;
 
 typedef struct MoeConfig {
