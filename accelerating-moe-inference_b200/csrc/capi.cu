@@ -399,6 +399,12 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
     L.k = cfg->top_k;
     MOE_CUDA(cudaDeviceGetAttribute(&L.sm_count, cudaDevAttrMultiProcessorCount, cfg->device));
     MOE_CUDA(cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking));
+    MOE_CUDA(cudaStreamCreateWithFlags(&h->h2d_stream, cudaStreamNonBlocking));
+    MOE_CUDA(cudaStreamCreateWithFlags(&h->d2h_stream, cudaStreamNonBlocking));
+    for (int c = 0; c < MoeHandle::kMaxChunks; ++c) {
+        MOE_CUDA(cudaEventCreateWithFlags(&h->in_ev[c], cudaEventDisableTiming));
+        MOE_CUDA(cudaEventCreateWithFlags(&h->out_ev[c], cudaEventDisableTiming));
+    }
     cudaStream_t s = h->own_stream;
 
     const size_t d = L.d, E = L.E, ffp = L.ffp, ff = L.ff;
@@ -556,6 +562,12 @@ void moe_destroy(MoeHandle* h) {
     moe::free_ptr(L.w2_hi); moe::free_ptr(L.w2_lo); moe::free_ptr(L.w13_f32); moe::free_ptr(L.w2_f32);
     for (cudaEvent_t& e : L.prof_ev)
         if (e) cudaEventDestroy(e);
+    for (int c = 0; c < MoeHandle::kMaxChunks; ++c) {
+        if (h->in_ev[c]) cudaEventDestroy(h->in_ev[c]);
+        if (h->out_ev[c]) cudaEventDestroy(h->out_ev[c]);
+    }
+    if (h->h2d_stream) cudaStreamDestroy(h->h2d_stream);
+    if (h->d2h_stream) cudaStreamDestroy(h->d2h_stream);
     if (h->own_stream) cudaStreamDestroy(h->own_stream);
     delete h;
 }
@@ -629,11 +641,37 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
     int rc = ensure_stage(L, T);
     if (rc) return rc;
     cudaStream_t s = h->own_stream;
-    const size_t bytes = sizeof(float) * (size_t)T * L.d;
-    MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage, x, bytes, cudaMemcpyHostToDevice, s));
-    rc = forward_impl(L, L.ws.x_stage, L.ws.y_stage, T, s);
-    if (rc) return rc;
-    MOE_CUDA(cudaMemcpyAsync(y, L.ws.y_stage, bytes, cudaMemcpyDeviceToHost, s));
+    const size_t row = sizeof(float) * (size_t)L.d;
+    // Rows are independent, so large batches run as a pipeline of chunks: the
+    // copy-in of chunk c + 1 and the copy-out of chunk c - 1 overlap chunk c's
+    // compute (and each other: the link is full duplex).  Chunks stay at
+    // least 2048 tokens so the grouped GEMMs keep their weight reuse.
+    int nch = T / 2048;
+    if (nch > MoeHandle::kMaxChunks) nch = MoeHandle::kMaxChunks;
+    if (nch < 2 || !h->h2d_stream) nch = 1;
+    if (nch == 1) {
+        MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage, x, row * T, cudaMemcpyHostToDevice, s));
+        rc = forward_impl(L, L.ws.x_stage, L.ws.y_stage, T, s);
+        if (rc) return rc;
+        MOE_CUDA(cudaMemcpyAsync(y, L.ws.y_stage, row * T, cudaMemcpyDeviceToHost, s));
+        MOE_CUDA(cudaStreamSynchronize(s));
+        return check_device_errors(L);
+    }
+    int off = 0;
+    for (int c = 0; c < nch; ++c) {
+        const int n = (int)((long long)T * (c + 1) / nch) - off;
+        const size_t b = row * n, o = (size_t)off * L.d;
+        MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage + o, x + o, b, cudaMemcpyHostToDevice, h->h2d_stream));
+        MOE_CUDA(cudaEventRecord(h->in_ev[c], h->h2d_stream));
+        MOE_CUDA(cudaStreamWaitEvent(s, h->in_ev[c], 0));
+        rc = forward_impl(L, L.ws.x_stage + o, L.ws.y_stage + o, n, s);
+        if (rc) return rc;
+        MOE_CUDA(cudaEventRecord(h->out_ev[c], s));
+        MOE_CUDA(cudaStreamWaitEvent(h->d2h_stream, h->out_ev[c], 0));
+        MOE_CUDA(cudaMemcpyAsync(y + o, L.ws.y_stage + o, b, cudaMemcpyDeviceToHost, h->d2h_stream));
+        off += n;
+    }
+    MOE_CUDA(cudaStreamSynchronize(h->d2h_stream));
     MOE_CUDA(cudaStreamSynchronize(s));
     return check_device_errors(L);
 }

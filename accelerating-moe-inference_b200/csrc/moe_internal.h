@@ -179,7 +179,11 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner,
 
 struct MoeHandle {
     moe::Layer L;
-    cudaStream_t own_stream = nullptr;
+    cudaStream_t own_stream = nullptr;   // compute stream of the host-buffer API
+    // Copy streams and chunk events of the pipelined host-buffer forward.
+    cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
+    static constexpr int kMaxChunks = 4;
+    cudaEvent_t in_ev[kMaxChunks] = {}, out_ev[kMaxChunks] = {};
 };
 
 namespace moe {

@@ -155,7 +155,10 @@ int moe_set_decode_max_tokens(MoeHandle* h, int32_t max_tokens);
 int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream);
 
 /* The same on host buffers (copies in, computes, copies out, synchronises).
- * Replaces PhiMoE::forward(const Tensor& x, Tensor& y) (src/layer.cu:80-103). */
+ * Replaces PhiMoE::forward(const Tensor& x, Tensor& y) (src/layer.cu:80-103).
+ * Batches of 4096+ tokens run as a pipeline of up to 4 chunks (>= 2048 tokens
+ * each) so the host<->device copies overlap the compute; page-locked x and y
+ * (moe_host_alloc, Tensor::Alloc::Pinned) are needed for the overlap. */
 int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T);
 
 /* Router only, device buffers: logits [T][E] (may be NULL), expert indices
@@ -177,7 +180,8 @@ int moe_host_alloc(size_t bytes, void** out);
 int moe_host_free(void* p);
 
 /* Per-expert row counts [E] of the last forward or route on this handle
- * (synchronises the handle's last stream).  The dispatch histogram of
+ * (synchronises the handle's last stream; after a pipelined
+ * moe_forward_host, of its last chunk).  The dispatch histogram of
  * src/model.cu:921-1003. */
 int moe_expert_counts(MoeHandle* h, int32_t* counts);
 

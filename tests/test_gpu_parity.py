@@ -227,3 +227,21 @@ def test_gemm_variants_agree(precision):
     with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, gemm_variant=2) as a, \
             pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, gemm_variant=1) as b:
         assert np.array_equal(bits(a.forward_host(x)), bits(b.forward_host(x)))
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_pipelined_host_forward_matches_device_forward(precision):
+    """moe_forward_host splits 4096+ tokens into chunks whose copies overlap
+    the compute; rows are independent, so the result is the single device
+    call's, bit for bit (top-2)."""
+    import torch
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(25, 256, 384, 8)
+    x = pkg.synthetic_tokens(25, 6144, 256)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision) as m:
+        y_host = m.forward_host(x)
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty_like(xd)
+        m.forward_device(xd.data_ptr(), yd.data_ptr(), x.shape[0], 0)
+        torch.cuda.synchronize()
+    assert np.array_equal(bits(y_host), bits(yd.cpu().numpy()))
