@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
     "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
     "moe_dispatch_noalloc", "moe_route_host", "moe_host_alloc", "moe_host_free",
+    "moe_selftest_wait_timeout",
     "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
@@ -108,6 +109,7 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_profile_read.argtypes = [vp, _f32p, ctypes.c_int32]
     L.moe_route_host.argtypes = [vp, _f32p, ctypes.c_int32, _f32p, _i32p, _f32p]
     L.moe_host_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.moe_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int32]
     L.moe_host_free.argtypes = [vp]
     i64p = ctypes.POINTER(ctypes.c_int64)
     L.moe_ep_plan.argtypes = [_i32p, _i32p, ctypes.c_int32, ctypes.c_int32, i64p, i64p, i64p, i64p]

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "moe_internal.h"
+#include "ptx.cuh"
 
 namespace moe {
 namespace {
@@ -723,6 +724,29 @@ int moe_route_host(MoeHandle* h, const float* x, int32_t T, float* logits, int32
                              cudaMemcpyDeviceToHost, s));
     MOE_CUDA(cudaStreamSynchronize(s));
     return check_device_errors(L);
+}
+
+int moe_selftest_wait_timeout(int device, int32_t budget_us) {
+    using namespace moe;
+    if (budget_us < 1 || budget_us > 2000000) return fail(MOE_ERR_INVALID, "budget_us out of range");
+    int ndev = 0;
+    MOE_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(MOE_ERR_INVALID, "no such device");
+    DeviceGuard guard(device);
+    int* flag = nullptr;
+    MOE_CUDA(cudaMalloc(&flag, sizeof(int)));
+    MOE_CUDA(cudaMemset(flag, 0, sizeof(int)));
+    cudaError_t e = launch_selftest_wait(flag, (unsigned long long)budget_us * 1000ull);
+    int h_flag = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(flag);
+    if (e != cudaSuccess) return cuda_fail(e, "selftest kernel");
+    if (h_flag & kDevErrTimeoutSelftest) {
+        char buf[96];
+        std::snprintf(buf, sizeof buf, "a device-side wait timed out (flags 0x%x)", h_flag);
+        return fail(MOE_ERR_TIMEOUT, buf);
+    }
+    return fail(MOE_ERR_CUDA, "selftest: the wait that nothing completes did not time out");
 }
 
 int moe_host_alloc(size_t bytes, void** out) {

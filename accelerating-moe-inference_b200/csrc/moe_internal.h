@@ -157,6 +157,8 @@ cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_
 int decode_max_supported_tokens();
 
 // weights.cu
+// Runs one bounded mbarrier wait that nothing completes (timeout self-test).
+cudaError_t launch_selftest_wait(int* err, unsigned long long budget_ns);
 cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const float* w3_dev,
                            cudaStream_t s);
 cudaError_t convert_down(const Layer& L, int e, const float* w2_dev, cudaStream_t s);

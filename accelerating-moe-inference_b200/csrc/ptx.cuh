@@ -22,6 +22,7 @@ enum DeviceError : int {
     kDevErrTimeoutMma = 2,
     kDevErrTimeoutEpilogue = 4,
     kDevErrTimeoutDrain = 8,
+    kDevErrTimeoutSelftest = 16,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -72,14 +73,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// ORs `code` into *err) if it has not completed within kWaitBudgetNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// ORs `code` into *err) if it has not completed within `budget_ns`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          unsigned long long budget_ns = kWaitBudgetNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_timer_ns();
     while (true) {
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+        if (global_timer_ns() - t0 > budget_ns) {
             if (err) atomicOr(err, code);
             return false;
         }

@@ -62,7 +62,25 @@ __global__ void down_kernel(const float* __restrict__ w2, int ff, int ffp, int d
     }
 }
 
+// One thread waits, with the production bounded-wait routine, on an mbarrier
+// that nothing arrives on; the wait runs out and records the timeout flag.
+__global__ void selftest_wait_kernel(int* err, unsigned long long budget_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, err, kDevErrTimeoutSelftest, budget_ns);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_selftest_wait(int* err, unsigned long long budget_ns) {
+    selftest_wait_kernel<<<1, 32>>>(err, budget_ns);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return cudaDeviceSynchronize();
+}
 
 cudaError_t convert_gateup(const Layer& L, int e, const float* w1_dev, const float* w3_dev,
                            cudaStream_t s) {

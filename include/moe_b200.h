@@ -173,6 +173,17 @@ int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int
 int moe_route_host(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,
                    float* weights);
 
+/* Failure-detection self-test.  Every device-side wait in the kernels
+ * (mbarrier waits of the TMA / MMA / epilogue pipelines) is bounded in
+ * wall-clock time; when one runs out the kernel records an error flag, stops
+ * issuing work, drains what it issued and returns, and the host reports
+ * MOE_ERR_TIMEOUT.  This runs that same bounded wait on an mbarrier nothing
+ * ever completes, with a budget of budget_us microseconds, on `device`:
+ * it returns MOE_ERR_TIMEOUT when the timeout path works.  The device stays
+ * usable afterwards.  (No counterpart in the reference, whose kernels have no
+ * waits.) */
+int moe_selftest_wait_timeout(int device, int32_t budget_us);
+
 /* Page-locked host memory for host-side tensors (the reference's
  * Tensor::Alloc::Pinned, src/tensor.cu:11-29), so moe_forward_host's copies
  * run at full link speed.  Free with moe_host_free. */

@@ -245,3 +245,22 @@ def test_pipelined_host_forward_matches_device_forward(precision):
         m.forward_device(xd.data_ptr(), yd.data_ptr(), x.shape[0], 0)
         torch.cuda.synchronize()
     assert np.array_equal(bits(y_host), bits(yd.cpu().numpy()))
+
+
+def test_bounded_wait_times_out_and_device_stays_usable():
+    """The kernels' bounded-wait path: a wait that nothing completes runs out
+    after its budget and is reported as MOE_ERR_TIMEOUT; the context is still
+    usable for a normal forward afterwards."""
+    import time
+    pkg = load_pkg()
+    lib = pkg.load_library()
+    t0 = time.perf_counter()
+    rc = lib.moe_selftest_wait_timeout(0, 20000)   # 20 ms budget
+    dt = time.perf_counter() - t0
+    assert rc == -6, lib.moe_last_error().decode()
+    assert "timed out" in lib.moe_last_error().decode()
+    assert dt < 5.0
+    layer, x = case_inputs(pkg, "c1")
+    g = np.load(GOLDEN_DIR / "c1.npz")
+    with pkg.MoeLayer(layer, top_k=2, policy=0) as m:
+        assert rel_l2(m.forward_host(x), g["phi_y"]) <= 1e-3
