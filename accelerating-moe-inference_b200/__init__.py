@@ -41,7 +41,8 @@ EXPORTED_SYMBOLS = (
     "moe_set_decode_max_tokens", "moe_forward_device", "moe_forward_host", "moe_route_device",
     "moe_expert_counts", "moe_dispatch_layout", "moe_profile_enable", "moe_profile_read",
     "moe_dispatch_noalloc", "moe_route_host", "moe_host_alloc", "moe_host_free",
-    "moe_selftest_wait_timeout",
+    "moe_selftest_wait_timeout", "moe_set_post_norm", "moe_block_forward_device",
+    "moe_block_forward_host", "moe_layer_norm_device",
     "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
@@ -111,6 +112,11 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_host_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
     L.moe_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int32]
     L.moe_host_free.argtypes = [vp]
+    L.moe_set_post_norm.argtypes = [vp, _f32p, _f32p, ctypes.c_float]
+    L.moe_block_forward_device.argtypes = [vp, vp, vp, ctypes.c_int32, vp]
+    L.moe_block_forward_host.argtypes = [vp, _f32p, _f32p, ctypes.c_int32]
+    L.moe_layer_norm_device.argtypes = [vp, vp, vp, ctypes.c_float, ctypes.c_int32, ctypes.c_int32,
+                                        vp, vp]
     i64p = ctypes.POINTER(ctypes.c_int64)
     L.moe_ep_plan.argtypes = [_i32p, _i32p, ctypes.c_int32, ctypes.c_int32, i64p, i64p, i64p, i64p]
     L.moe_ep_unique_id.argtypes = [vp]
@@ -149,6 +155,14 @@ def ep_unique_id() -> bytes:
     return buf.raw
 
 
+def layer_norm_device(x_ptr: int, w_ptr: int, b_ptr: int, eps: float, rows: int, cols: int,
+                      y_ptr: int, stream: int = 0) -> None:
+    """tensor_ops::layer_norm (src/tensor.cu:174-189) on device buffers."""
+    vp = ctypes.c_void_p
+    _check(load_library().moe_layer_norm_device(vp(x_ptr), vp(w_ptr), vp(b_ptr), eps, rows, cols,
+                                                vp(y_ptr), vp(stream)))
+
+
 def default_config(**kw) -> MoeConfig:
     cfg = MoeConfig()
     load_library().moe_config_init(ctypes.byref(cfg))
@@ -168,6 +182,9 @@ class LayerWeights:
     w3: list                            # E x [ff][d]   up
     w2: list                            # E x [d][ff]   down
     router_bias: Optional[np.ndarray] = None  # [E]
+    # The decoder layer's post_attention_layernorm, [d] each (optional).
+    norm_weight: Optional[np.ndarray] = None
+    norm_bias: Optional[np.ndarray] = None
 
     @property
     def E(self) -> int:
@@ -215,12 +232,25 @@ def zipf_router_bias(E: int) -> np.ndarray:
     return (0.5 * np.log(1.0 / r)).astype(np.float32)
 
 
+def synthetic_post_norm(seed: int, d: int):
+    """Seeded post-attention LayerNorm weight ~ 1 + N(0, 0.1) and bias ~
+    N(0, 0.1), [d] each (numpy PCG64, stream offset by 0x4e4f)."""
+    g = np.random.Generator(np.random.PCG64([seed, 0x4E4F]))
+    w = (1.0 + 0.1 * g.standard_normal(d)).astype(np.float32)
+    b = (0.1 * g.standard_normal(d)).astype(np.float32)
+    return w, b
+
+
 def write_model_bin(path, layers: Sequence[LayerWeights]) -> None:
     """Write layers in the ModelLoader format (src/model_loader.cu:14-30):
     u32 count; per entry u32 name_len, name, u32 ndim, u32 dims[ndim],
     u64 offset, u64 bytes; then the fp32 payloads."""
     entries = []
     for li, L in enumerate(layers):
+        if L.norm_weight is not None:
+            pn = f"model.layers.{li}.post_attention_layernorm"
+            entries.append((f"{pn}.weight", L.norm_weight))
+            entries.append((f"{pn}.bias", L.norm_bias))
         base = f"model.layers.{li}.block_sparse_moe"
         entries.append((f"{base}.gate.weight", L.wg))
         if L.router_bias is not None:
@@ -289,6 +319,8 @@ class MoeLayer:
         self._h = h
         self.cfg = MoeConfig()
         _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
+        if weights is not None and weights.norm_weight is not None:
+            self.set_post_norm(weights.norm_weight, weights.norm_bias)
 
     @classmethod
     def from_device_pointers(cls, d: int, ff: int, E: int, wg_ptr: int, w1_ptrs, w3_ptrs,
@@ -390,6 +422,28 @@ class MoeLayer:
         _check(load_library().moe_forward_device(self._h, ctypes.c_void_p(x_ptr),
                                                  ctypes.c_void_p(y_ptr), T,
                                                  ctypes.c_void_p(stream)))
+
+    # -- the decoder layer's MoE half: y = attn + MoE(layer_norm(attn))
+    def set_post_norm(self, weight: np.ndarray, bias: np.ndarray, eps: float = 1e-5):
+        w = np.ascontiguousarray(weight, np.float32)
+        b = np.ascontiguousarray(bias, np.float32)
+        if w.shape != (self.d,) or b.shape != (self.d,):
+            raise ValueError(f"post-norm weight and bias must have shape ({self.d},)")
+        _check(load_library().moe_set_post_norm(self._h, _fp(w), _fp(b), eps))
+
+    def block_forward_host(self, attn: np.ndarray) -> np.ndarray:
+        attn = np.ascontiguousarray(attn, np.float32)
+        T, d = attn.shape
+        if d != self.d:
+            raise ValueError(f"attn has {d} columns, layer expects {self.d}")
+        y = np.empty_like(attn)
+        _check(load_library().moe_block_forward_host(self._h, _fp(attn), _fp(y), T))
+        return y
+
+    def block_forward_device(self, attn_ptr: int, y_ptr: int, T: int, stream: int = 0):
+        _check(load_library().moe_block_forward_device(self._h, ctypes.c_void_p(attn_ptr),
+                                                       ctypes.c_void_p(y_ptr), T,
+                                                       ctypes.c_void_p(stream)))
 
     def route_device(self, x_ptr: int, T: int, logits_ptr: int, idx_ptr: int, w_ptr: int,
                      stream: int = 0):

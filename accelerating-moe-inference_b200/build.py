@@ -75,7 +75,10 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
         host_hdrs = [INCLUDE / n for n in ("tensor.h", "model_loader.h", "layer.h", "moe_b200.h")
                      if (INCLUDE / n).exists()]
         if _newer(LAYER_LIB, host_srcs + host_hdrs + [LIB]):
-            _run([CXX, "-std=c++17", "-O2", "-fPIC", "-shared", "-fopenmp", "-Wall", "-I",
+            # No implicit contraction: the reference-order arithmetic (the
+            # router's FMA chain, layer_norm's unfused variance) is spelled out.
+            _run([CXX, "-std=c++17", "-O2", "-ffp-contract=off", "-fPIC", "-shared", "-fopenmp",
+                  "-Wall", "-I",
                   INCLUDE, *host_srcs, "-o", LAYER_LIB, f"-L{PKG}", "-lmoe_b200",
                   "-Wl,-rpath,$ORIGIN"], verbose)
     return LIB

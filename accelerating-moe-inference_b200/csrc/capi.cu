@@ -89,6 +89,7 @@ void free_workspace(Workspace& W) {
     free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.a_hi); free_ptr(W.a_lo);
     free_ptr(W.h_hi); free_ptr(W.h_lo); free_ptr(W.x_stage); free_ptr(W.y_stage);
     free_ptr(W.dev_err); free_ptr(W.h_dec); free_ptr(W.dec_counter);
+    free_ptr(W.row_mean); free_ptr(W.row_inv);
     W = Workspace{};
 }
 
@@ -129,6 +130,8 @@ int ensure_workspace(Layer& L, int T) {
     MOE_CUDA(dalloc(&W.h_dec, sizeof(float) * (size_t)decode_max_supported_tokens() * k * L.ffp,
                     &bytes));
     MOE_CUDA(dalloc(&W.dec_counter, 2 * sizeof(int), &bytes));
+    MOE_CUDA(dalloc(&W.row_mean, sizeof(float) * capT, &bytes));
+    MOE_CUDA(dalloc(&W.row_inv, sizeof(float) * capT, &bytes));
     MOE_CUDA(dalloc(&W.dev_err, sizeof(int), &bytes));
     MOE_CUDA(cudaMemset(W.dev_err, 0, sizeof(int)));
     MOE_CUDA(cudaMemset(W.num_mtiles, 0, sizeof(int)));
@@ -204,30 +207,43 @@ int check_device_errors(Layer& L) {
     return MOE_OK;
 }
 
-int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+// block: the decoder layer's MoE half -- x is the attention output, the
+// post-attention LayerNorm is applied on load and x is added after the
+// combine (stages: norm statistics count as router time, the residual as
+// down time).
+int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool block = false) {
     int rc = ensure_workspace(L, T);
     if (rc) return rc;
     Workspace& W = L.ws;
     L.last_stream = s;
     L.last_T = T;
     for (bool& r : L.prof_ran) r = false;
+    NormRef nr;
+    if (block) {
+        nr.mean = W.row_mean;
+        nr.inv = W.row_inv;
+        nr.w = L.norm_w;
+        nr.b = L.norm_b;
+    }
     MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
     prof_mark(L, 0, s);
-    MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s));
+    if (block)
+        MOE_CUDA(launch_row_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, W.dev_err, s));
+    MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, nr));
     prof_mark(L, 1, s);
     // A batch that fits one router block is scanned inside the permute kernel.
     if (T > kRouteTokens) MOE_CUDA(launch_dispatch_scan(L, T, s));
     prof_mark(L, 2, s);
     if (T <= L.cfg.decode_max_tokens) {
-        MOE_CUDA(launch_decode(L, x, T, y, s));  // marks stages 3 and 4 between its kernels
-        prof_mark(L, kProfileStages, s);
-        return MOE_OK;
+        MOE_CUDA(launch_decode(L, x, T, y, s, nr));  // marks stages 3 and 4 between its kernels
+    } else {
+        MOE_CUDA(launch_dispatch_permute(L, x, T, s, nr));
+        prof_mark(L, 3, s);
+        MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/false));
+        prof_mark(L, 4, s);
+        MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/true));
     }
-    MOE_CUDA(launch_dispatch_permute(L, x, T, s));
-    prof_mark(L, 3, s);
-    MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/false));
-    prof_mark(L, 4, s);
-    MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/true));
+    if (block) MOE_CUDA(launch_residual_add(L, y, x, (size_t)T * L.d, s));
     prof_mark(L, kProfileStages, s);
     return MOE_OK;
 }
@@ -549,7 +565,24 @@ int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int lay
     wh.w1 = p1.data();
     wh.w2 = p2.data();
     wh.w3 = p3.data();
-    return moe_create(&cfg, &wh, out);
+    // The decoder layer's post-attention LayerNorm, when the file has it.
+    const std::string pn = "model.layers." + std::to_string(layer_idx) + ".post_attention_layernorm";
+    std::vector<float> nw, nb;
+    if (index.count(pn + ".weight") && index.count(pn + ".bias")) {
+        if ((rc = load_tensor(path, index, pn + ".weight", &nw, nullptr)) ||
+            (rc = load_tensor(path, index, pn + ".bias", &nb, nullptr)))
+            return rc;
+        if ((int)nw.size() != cfg.d_model || (int)nb.size() != cfg.d_model)
+            return fail(MOE_ERR_IO, "post_attention_layernorm shape");
+    }
+    rc = moe_create(&cfg, &wh, out);
+    if (rc || nw.empty()) return rc;
+    rc = moe_set_post_norm(*out, nw.data(), nb.data(), 1.0e-5f);
+    if (rc) {
+        moe_destroy(*out);
+        *out = nullptr;
+    }
+    return rc;
 }
 
 void moe_destroy(MoeHandle* h) {
@@ -561,6 +594,7 @@ void moe_destroy(MoeHandle* h) {
     moe::free_workspace(L.ws);
     moe::free_ptr(L.wg); moe::free_ptr(L.bias); moe::free_ptr(L.w13_hi); moe::free_ptr(L.w13_lo);
     moe::free_ptr(L.w2_hi); moe::free_ptr(L.w2_lo); moe::free_ptr(L.w13_f32); moe::free_ptr(L.w2_f32);
+    moe::free_ptr(L.norm_w); moe::free_ptr(L.norm_b);
     for (cudaEvent_t& e : L.prof_ev)
         if (e) cudaEventDestroy(e);
     for (int c = 0; c < MoeHandle::kMaxChunks; ++c) {
@@ -631,9 +665,11 @@ int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* 
     return forward_impl(h->L, x, y, T, static_cast<cudaStream_t>(stream));
 }
 
-int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
-    using namespace moe;
-    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+}  // extern "C"
+
+namespace moe {
+namespace {
+int forward_host_impl(MoeHandle* h, const float* x, float* y, int32_t T, bool block) {
     if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
     if (T == 0) return MOE_OK;
     if (!x || !y) return fail(MOE_ERR_INVALID, "null x or y");
@@ -652,7 +688,7 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
     if (nch < 2 || !h->h2d_stream) nch = 1;
     if (nch == 1) {
         MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage, x, row * T, cudaMemcpyHostToDevice, s));
-        rc = forward_impl(L, L.ws.x_stage, L.ws.y_stage, T, s);
+        rc = forward_impl(L, L.ws.x_stage, L.ws.y_stage, T, s, block);
         if (rc) return rc;
         MOE_CUDA(cudaMemcpyAsync(y, L.ws.y_stage, row * T, cudaMemcpyDeviceToHost, s));
         MOE_CUDA(cudaStreamSynchronize(s));
@@ -665,7 +701,7 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
         MOE_CUDA(cudaMemcpyAsync(L.ws.x_stage + o, x + o, b, cudaMemcpyHostToDevice, h->h2d_stream));
         MOE_CUDA(cudaEventRecord(h->in_ev[c], h->h2d_stream));
         MOE_CUDA(cudaStreamWaitEvent(s, h->in_ev[c], 0));
-        rc = forward_impl(L, L.ws.x_stage + o, L.ws.y_stage + o, n, s);
+        rc = forward_impl(L, L.ws.x_stage + o, L.ws.y_stage + o, n, s, block);
         if (rc) return rc;
         MOE_CUDA(cudaEventRecord(h->out_ev[c], s));
         MOE_CUDA(cudaStreamWaitEvent(h->d2h_stream, h->out_ev[c], 0));
@@ -675,6 +711,78 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
     MOE_CUDA(cudaStreamSynchronize(h->d2h_stream));
     MOE_CUDA(cudaStreamSynchronize(s));
     return check_device_errors(L);
+}
+
+int check_block(const MoeHandle* h) {
+    if (!h->L.norm_w) return fail(MOE_ERR_INVALID, "no post-attention norm attached (moe_set_post_norm)");
+    return MOE_OK;
+}
+}  // namespace
+}  // namespace moe
+
+extern "C" {
+
+int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    return forward_host_impl(h, x, y, T, false);
+}
+
+int moe_block_forward_host(MoeHandle* h, const float* attn, float* y, int32_t T) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (int rc = check_block(h)) return rc;
+    return forward_host_impl(h, attn, y, T, true);
+}
+
+int moe_block_forward_device(MoeHandle* h, const float* attn, float* y, int32_t T, void* stream) {
+    using namespace moe;
+    if (!h) return fail(MOE_ERR_INVALID, "null handle");
+    if (int rc = check_block(h)) return rc;
+    if (T < 0) return fail(MOE_ERR_INVALID, "T < 0");
+    if (T == 0) return MOE_OK;
+    if (!attn || !y) return fail(MOE_ERR_INVALID, "null attn or y");
+    if (attn == y) return fail(MOE_ERR_INVALID, "y must not alias attn");
+    if ((reinterpret_cast<uintptr_t>(attn) | reinterpret_cast<uintptr_t>(y)) & 15)
+        return fail(MOE_ERR_INVALID, "attn and y must be 16-byte aligned");
+    DeviceGuard guard(h->L.cfg.device);
+    return forward_impl(h->L, attn, y, T, static_cast<cudaStream_t>(stream), true);
+}
+
+int moe_set_post_norm(MoeHandle* h, const float* weight, const float* bias, float eps) {
+    using namespace moe;
+    if (!h || !weight || !bias) return fail(MOE_ERR_INVALID, "null argument");
+    if (!(eps >= 0.0f)) return fail(MOE_ERR_INVALID, "eps must be >= 0");
+    if (!norm_supported(h->L.d))
+        return fail(MOE_ERR_UNSUPPORTED, "the fused LayerNorm needs d_model a multiple of 128");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    const size_t bytes = sizeof(float) * L.d;
+    if (!L.norm_w) {
+        MOE_CUDA(dalloc(&L.norm_w, bytes, &L.weight_bytes));
+        MOE_CUDA(dalloc(&L.norm_b, bytes, &L.weight_bytes));
+    }
+    MOE_CUDA(cudaDeviceSynchronize());   // no forward may still read the old values
+    MOE_CUDA(cudaMemcpy(L.norm_w, weight, bytes, cudaMemcpyHostToDevice));
+    MOE_CUDA(cudaMemcpy(L.norm_b, bias, bytes, cudaMemcpyHostToDevice));
+    L.norm_eps = eps;
+    return MOE_OK;
+}
+
+int moe_layer_norm_device(const float* x, const float* weight, const float* bias, float eps,
+                          int32_t rows, int32_t cols, float* y, void* stream) {
+    using namespace moe;
+    if (rows < 0 || !norm_supported(cols))
+        return fail(MOE_ERR_INVALID, "rows >= 0 and cols a positive multiple of 128 required");
+    if (rows == 0) return MOE_OK;
+    if (!x || !weight || !bias || !y) return fail(MOE_ERR_INVALID, "null argument");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+         reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(bias)) & 15)
+        return fail(MOE_ERR_INVALID, "pointers must be 16-byte aligned");
+    if (!(eps >= 0.0f)) return fail(MOE_ERR_INVALID, "eps must be >= 0");
+    MOE_CUDA(launch_layer_norm(x, rows, cols, eps, weight, bias, y,
+                               static_cast<cudaStream_t>(stream)));
+    return MOE_OK;
 }
 
 int moe_route_device(MoeHandle* h, const float* x, int32_t T, float* logits, int32_t* idx,

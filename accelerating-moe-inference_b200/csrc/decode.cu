@@ -295,10 +295,12 @@ cudaError_t launch_w(Layer& L, int T, float* y, cudaStream_t s, const WT* w13, c
 
 int decode_max_supported_tokens() { return kMaxDecodeTokens; }
 
-cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s) {
+cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
+                          const NormRef& nr) {
     if (T > kMaxDecodeTokens || !L.ws.h_dec) return cudaErrorInvalidValue;
-    // Pack the routed token rows (fp32 as is in FP32 precision, bf16 in BF16).
-    cudaError_t err = launch_dispatch_permute_raw(L, x, T, s);
+    // Pack the routed token rows (fp32 as is in FP32 precision, bf16 in BF16),
+    // normalised on the way when nr is active.
+    cudaError_t err = launch_dispatch_permute_raw(L, x, T, s, nr);
     if (err != cudaSuccess) return err;
     prof_mark(L, 3, s);
     if (L.cfg.precision == MOE_PREC_BF16)

@@ -99,7 +99,11 @@ MoeConfig reference_config() {
 PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx)
     : PhiMoE(loader, layer_idx, reference_config()) {}
 
-PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg_in) {
+namespace {
+
+// The MoE layer `layer_idx` of a model file (src/layer.cu:73-77 names).
+std::shared_ptr<MoeHandle> load_moe(const ModelLoader& loader, std::size_t layer_idx,
+                                    const MoeConfig& cfg_in) {
     const std::string base = "model.layers." + std::to_string(layer_idx) + ".block_sparse_moe";
     Tensor gate = loader.load(base + ".gate.weight");
     if (gate.ndim() != 2) throw std::runtime_error("router weight is not 2-D: " + base);
@@ -121,7 +125,13 @@ PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig
     Tensor bias;
     const bool has_bias = loader.has(base + ".gate.bias");
     if (has_bias) bias = loader.load(base + ".gate.bias");
-    h_ = make_handle(cfg, gate, has_bias ? &bias : nullptr, w1, w3, w2);
+    return make_handle(cfg, gate, has_bias ? &bias : nullptr, w1, w3, w2);
+}
+
+}  // namespace
+
+PhiMoE::PhiMoE(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg_in)
+    : h_(load_moe(loader, layer_idx, cfg_in)) {
     moe_get_config(h_.get(), &cfg_);
 }
 
@@ -148,4 +158,37 @@ void PhiMoE::route(const Tensor& x, std::vector<std::pair<int, float>>& routes) 
     if (rc != MOE_OK) throw_status(rc, "PhiMoE::route");
     routes.clear();
     for (std::size_t i = 0; i < rows * k; ++i) routes.emplace_back(idx[i], w[i]);
+}
+
+// ---------------------------------------------------------------- PhiMoEBlock
+PhiMoEBlock::PhiMoEBlock(const ModelLoader& loader, std::size_t layer_idx)
+    : PhiMoEBlock(loader, layer_idx, reference_config()) {}
+
+PhiMoEBlock::PhiMoEBlock(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg)
+    : h_(load_moe(loader, layer_idx, cfg)) {
+    moe_get_config(h_.get(), &cfg_);
+    const std::string pn =
+        "model.layers." + std::to_string(layer_idx) + ".post_attention_layernorm";
+    const Tensor w = loader.load(pn + ".weight");
+    const Tensor b = loader.load(pn + ".bias");
+    if (w.size() != static_cast<std::size_t>(cfg_.d_model) || b.size() != w.size())
+        throw std::runtime_error("post_attention_layernorm shape: " + pn);
+    const int rc = moe_set_post_norm(h_.get(), w.data(), b.data(), 1.0e-5f);
+    if (rc != MOE_OK) throw_status(rc, "moe_set_post_norm");
+}
+
+void PhiMoEBlock::forward(const Tensor& attn, Tensor& y) const {
+    check_2d(attn, static_cast<std::size_t>(cfg_.d_model));
+    Tensor out({attn.size(0), attn.size(1)});
+    const int rc = moe_block_forward_host(h_.get(), attn.data(), out.data(),
+                                          static_cast<int32_t>(attn.size(0)));
+    if (rc != MOE_OK) throw_status(rc, "PhiMoEBlock::forward");
+    y = std::move(out);
+}
+
+void PhiMoEBlock::forward_device(const float* attn_dev, float* y_dev, std::size_t rows,
+                                 void* stream) const {
+    const int rc = moe_block_forward_device(h_.get(), attn_dev, y_dev, static_cast<int32_t>(rows),
+                                            stream);
+    if (rc != MOE_OK) throw_status(rc, "PhiMoEBlock::forward_device");
 }

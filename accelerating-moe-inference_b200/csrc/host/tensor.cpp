@@ -146,6 +146,32 @@ void matmul_transposed(const Tensor& a, const Tensor& b, Tensor& c) {
         }
 }
 
+void layer_norm(const Tensor& x, const Tensor& weight, const Tensor& bias, float eps, Tensor& y) {
+    if (x.ndim() == 0) throw std::invalid_argument("layer norm shape");
+    const std::size_t h = x.size(x.ndim() - 1), rows = x.size() / h;
+    if (weight.size() != h || bias.size() != h || y.size() != x.size())
+        throw std::invalid_argument("layer norm shape");
+    const float* X = x.data();
+    const float* W = weight.data();
+    const float* B = bias.data();
+    float* Y = y.data();
+#pragma omp parallel for
+    for (long long r = 0; r < static_cast<long long>(rows); ++r) {
+        const float* xr = X + static_cast<std::size_t>(r) * h;
+        float* yr = Y + static_cast<std::size_t>(r) * h;
+        float mean = 0.0f;
+        for (std::size_t j = 0; j < h; ++j) mean += xr[j];
+        mean /= static_cast<float>(h);
+        float var = 0.0f;
+        for (std::size_t j = 0; j < h; ++j) {
+            const float dv = xr[j] - mean;
+            var += dv * dv;
+        }
+        const float inv = 1.0f / std::sqrt(var / static_cast<float>(h) + eps);
+        for (std::size_t j = 0; j < h; ++j) yr[j] = std::fma((xr[j] - mean) * inv, W[j], B[j]);
+    }
+}
+
 void add_inplace(Tensor& a, const Tensor& b) {
     if (a.size() != b.size()) throw std::invalid_argument("add shape");
     for (std::size_t i = 0; i < a.size(); ++i) a[i] += b[i];

@@ -76,10 +76,44 @@ struct Workspace {
     float* x_stage = nullptr;   // host-API staging, [cap_T][d]
     float* y_stage = nullptr;
     int* dev_err = nullptr;     // device-side error flags (timeouts)
+    float* row_mean = nullptr;  // post-attention LayerNorm statistics, [cap_T]
+    float* row_inv = nullptr;
     float* h_dec = nullptr;     // decode-path H, fp32 [64 * k][ffp]
     int* dec_counter = nullptr; // decode-path work counters [2]
     CUtensorMap tm_a_hi, tm_a_lo, tm_h_hi, tm_h_lo;
     size_t bytes = 0;
+};
+
+#ifdef __CUDACC__
+// Output expression of tensor_ops::layer_norm (src/tensor.cu:187) as GCC
+// contracts it: fma((x - mean) * inv, w, b), four columns at a time.
+__device__ __forceinline__ float4 layer_norm_out4(float4 x, float m, float iv, float4 w,
+                                                  float4 b) {
+    float4 o;
+    o.x = __fmaf_rn(__fmul_rn(__fsub_rn(x.x, m), iv), w.x, b.x);
+    o.y = __fmaf_rn(__fmul_rn(__fsub_rn(x.y, m), iv), w.y, b.y);
+    o.z = __fmaf_rn(__fmul_rn(__fsub_rn(x.z, m), iv), w.z, b.z);
+    o.w = __fmaf_rn(__fmul_rn(__fsub_rn(x.w, m), iv), w.w, b.w);
+    return o;
+}
+#endif
+
+// The LayerNorm applied on load (norm.cu): row t's mean and inverse standard
+// deviation from row_stats_kernel, and the norm's weight and bias.  Inactive
+// (mean == nullptr) for the plain MoE forward.
+struct NormRef {
+    const float* mean = nullptr;   // [T]
+    const float* inv = nullptr;    // [T]
+    const float* w = nullptr;      // [d]
+    const float* b = nullptr;      // [d]
+#ifdef __CUDACC__
+    // Columns 4v .. 4v+3 of row t, normalised.
+    __device__ __forceinline__ float4 apply4(float4 x, int t, int v) const {
+        return layer_norm_out4(x, __ldg(mean + t), __ldg(inv + t),
+                               __ldg(reinterpret_cast<const float4*>(w) + v),
+                               __ldg(reinterpret_cast<const float4*>(b) + v));
+    }
+#endif
 };
 
 struct EpState;  // expert-parallel group (ep.cu)
@@ -107,6 +141,10 @@ struct Layer {
     // 256-wide N tile.
     CUtensorMap tm_w13_hi2, tm_w13_lo2, tm_w2_hi2, tm_w2_lo2;
     int gemm_variant = 0;       // MoeGemmVariant
+    // Post-attention LayerNorm (moe_set_post_norm): weight and bias [d].
+    float* norm_w = nullptr;
+    float* norm_b = nullptr;
+    float norm_eps = 0.0f;
     Workspace ws;
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;
@@ -126,13 +164,16 @@ inline void prof_mark(Layer& L, int i, cudaStream_t s) {
 
 // ------------------------------------------------------------ launchers
 // route.cu
+// nr active: x is normalised on load (the post-attention LayerNorm).
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
-                          float* wts, int* blockhist, cudaStream_t s);
+                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr = {});
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
-cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s);
+cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s,
+                                    const NormRef& nr = {});
 // The same placement with the rows copied in the decode kernels' format:
 // fp32 as is (FP32 precision) or bf16 (BF16 precision).
-cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s);
+cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s,
+                                        const NormRef& nr = {});
 // Placement into explicit outputs, routing over E experts with offsets eoff.
 cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
                                        const int* eoff, int* row_token, float* row_weight,
@@ -153,8 +194,20 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
                                     int mode);
 
 // decode.cu: T <= decode_max_supported_tokens() (64)
-cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s);
+cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
+                          const NormRef& nr = {});
 int decode_max_supported_tokens();
+
+// norm.cu: per-row LayerNorm statistics, the whole LayerNorm into y (d a
+// multiple of 128: norm_supported), and y += r over n floats (n a multiple
+// of 4).  err collects timed-out waits (may be null).
+bool norm_supported(int d);
+cudaError_t launch_row_stats(const float* x, int T, int d, float eps, float* mean, float* inv,
+                             int* err, cudaStream_t s);
+cudaError_t launch_layer_norm(const float* x, int T, int d, float eps, const float* w,
+                              const float* b, float* y, cudaStream_t s);
+cudaError_t launch_residual_add(const Layer& L, float* y, const float* r, size_t n,
+                                cudaStream_t s);
 
 // weights.cu
 // Runs one bounded mbarrier wait that nothing completes (timeout self-test).

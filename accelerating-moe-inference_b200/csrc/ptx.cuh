@@ -23,6 +23,7 @@ enum DeviceError : int {
     kDevErrTimeoutEpilogue = 4,
     kDevErrTimeoutDrain = 8,
     kDevErrTimeoutSelftest = 16,
+    kDevErrTimeoutNorm = 32,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -89,6 +90,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ---------------------------------------------------------------- TMA
+// 1-D bulk copy of `bytes` from global memory into this CTA's shared memory,
+// completing on `bar` (both addresses 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

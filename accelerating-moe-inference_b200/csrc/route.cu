@@ -70,7 +70,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
               const float* __restrict__ bias, int T, int d, int E, int k, int policy,
               float quantum, float tie_eps, float* __restrict__ logits_out,
               int* __restrict__ idx_out, float* __restrict__ w_out,
-              int* __restrict__ blockhist) {
+              int* __restrict__ blockhist, NormRef nr) {
     constexpr int kStages = 4;
     constexpr int kLd = KC + 4;              // padded row stride (floats)
     constexpr int kXs = kRouteTokens * kLd;  // x floats per stage
@@ -78,7 +78,9 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     extern __shared__ __align__(16) float rsm[];
     float* xs = rsm;                       // [kStages][32][kLd]
     float* ws = rsm + kStages * kXs;       // [kStages][8*EJ][kLd]
-    float* lg = ws + kStages * kWs;        // [32][E + 1]
+    float* nws = ws + kStages * kWs;       // [kStages][2][KC] norm weight, bias chunks
+    float* nst = nws + kStages * 2 * KC;   // [2][32] norm mean, inverse std of the tokens
+    float* lg = nst + 2 * kRouteTokens;    // [32][E + 1]
     int* hist = reinterpret_cast<int*>(lg + kRouteTokens * (E + 1));
 
     const int tid = threadIdx.x;
@@ -87,6 +89,12 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     const int t0 = blockIdx.x * kRouteTokens;
     const int n_tok = min(kRouteTokens, T - t0);
     const int nchunks = d / KC;
+    if (nr.mean) {
+        for (int t = tid; t < n_tok; t += blockDim.x) {
+            nst[t] = nr.mean[t0 + t];
+            nst[kRouteTokens + t] = nr.inv[t0 + t];
+        }
+    }
 
     // Stage loader: x chunk is 32 rows x KC floats, wg chunk E rows x KC.
     auto load_chunk = [&](int chunk, int stage) {
@@ -102,6 +110,13 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         for (int v = tid; v < wv; v += blockDim.x) {
             const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
             cp_async16(ws + stage * kWs + r * kLd + c, wg + (size_t)r * d + kbase + c, true);
+        }
+        if (nr.mean) {
+            for (int v = tid; v < KC / 2; v += blockDim.x) {
+                const int c = (v % (KC / 4)) * 4;
+                const float* src = (v < KC / 4 ? nr.w : nr.b) + kbase + c;
+                cp_async16(nws + stage * 2 * KC + (v < KC / 4 ? 0 : KC) + c, src, true);
+            }
         }
     };
 
@@ -121,6 +136,23 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         if (nxt < nchunks) load_chunk(nxt, nxt % kStages);
         cp_async_commit();
         const int st = c % kStages;
+        if (nr.mean) {
+            // Post-attention LayerNorm: normalise the landed x chunk in place,
+            // once per element, before the chains read it (the norm's weight
+            // and bias chunk landed with it).
+            const int kXv = (blockDim.x / 8) * KC / 4;
+            const float* nw = nws + st * 2 * KC;
+            for (int v = tid; v < kXv; v += blockDim.x) {
+                const int r = v / (KC / 4), cc = (v % (KC / 4)) * 4;
+                if (r < n_tok) {
+                    float4* p = reinterpret_cast<float4*>(xs + st * kXs + r * kLd + cc);
+                    *p = layer_norm_out4(*p, nst[r], nst[kRouteTokens + r],
+                                         *reinterpret_cast<const float4*>(nw + cc),
+                                         *reinterpret_cast<const float4*>(nw + KC + cc));
+                }
+            }
+            __syncthreads();
+        }
         const float* xr = xs + st * kXs + tt * kLd;
         const float* wr = ws + st * kWs + el * kLd;
         // Fully unrolled over the chunk, every shared-memory offset an
@@ -416,13 +448,19 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                         const int* __restrict__ idx, const float* __restrict__ wts,
                         const int* __restrict__ blockbase, const int* __restrict__ eoff,
                         int* __restrict__ row_token, float* __restrict__ row_weight,
-                        void* __restrict__ a_hi, void* __restrict__ a_lo, ScanOut so) {
+                        void* __restrict__ a_hi, void* __restrict__ a_lo, ScanOut so,
+                        NormRef nr) {
     __shared__ unsigned s_mask[kMaxExperts];
     __shared__ int s_base[kMaxExperts + 1];
     __shared__ int s_dest[kRouteTokens * kMaxTopK];
+    __shared__ float s_nmean[kRouteTokens], s_ninv[kRouteTokens];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kRouteTokens;
     const int n_tok = min(kRouteTokens, T - t0);
+    if (nr.mean && tid < n_tok) {
+        s_nmean[tid] = nr.mean[t0 + tid];
+        s_ninv[tid] = nr.inv[t0 + tid];
+    }
     if (so.counts) {
         // Single-block dispatch: this kernel also does the scan.  blockbase
         // holds the one block's histogram.
@@ -461,13 +499,39 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
     const int width = max(0, c1 - c0);
     const int total = n_tok * width;
     constexpr int kUnroll = 8;
+    const float4* nw4 = reinterpret_cast<const float4*>(nr.w);
+    const float4* nb4 = reinterpret_cast<const float4*>(nr.b);
     for (int base = tid; base < total; base += kUnroll * 256) {
         float4 f[kUnroll];
+        if (nr.mean) {
+            // The post-attention LayerNorm's weight and bias columns are
+            // loaded in the same batch as the rows.
+            float4 wv[kUnroll], bv[kUnroll];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const int i = base + u * 256;
-            if (i < total)
-                f[u] = reinterpret_cast<const float4*>(x + (size_t)(t0 + i / width) * d)[c0 + i % width];
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * 256;
+                if (i < total) {
+                    const int v = c0 + i % width;
+                    f[u] = reinterpret_cast<const float4*>(x + (size_t)(t0 + i / width) * d)[v];
+                    wv[u] = __ldg(nw4 + v);
+                    bv[u] = __ldg(nb4 + v);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * 256;
+                if (i < total) {
+                    const int t = i / width;
+                    f[u] = layer_norm_out4(f[u], s_nmean[t], s_ninv[t], wv[u], bv[u]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * 256;
+                if (i < total)
+                    f[u] = reinterpret_cast<const float4*>(x + (size_t)(t0 + i / width) * d)[c0 + i % width];
+            }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
@@ -520,10 +584,10 @@ dim3 permute_grid(const Layer& L, int T) {
 
 template <int EJ, int KC>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
-                            float* wts, int* blockhist, cudaStream_t s) {
+                            float* wts, int* blockhist, cudaStream_t s, const NormRef& nr) {
     const int E = L.E_route;
-    const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4)) +
-                                         kRouteTokens * (E + 1)) +
+    const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4) + 2 * KC) +
+                                         2 * kRouteTokens + kRouteTokens * (E + 1)) +
                         sizeof(int) * E;
     auto kern = router_kernel<EJ, KC>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -536,34 +600,34 @@ cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits
     const int tok = T < kRouteTokens ? (T + 3) / 4 * 4 : kRouteTokens;
     kern<<<nblk, 8 * tok, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
                                             L.cfg.router_policy, L.cfg.router_quantum,
-                                            L.cfg.router_tie_eps, logits, idx, wts, blockhist);
+                                            L.cfg.router_tie_eps, logits, idx, wts, blockhist, nr);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
-                          float* wts, int* blockhist, cudaStream_t s) {
+                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr) {
     // K chunk per pipeline stage: as wide as shared memory allows, so each
     // SM keeps 100-200 KB of x / wg loads in flight (the dot-product chains
     // themselves are serial and cannot be split).
     const int ej = (L.E_route + 7) / 8;
     if (L.d % 256 == 0) {
-        if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s);
-        if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s, nr);
     }
     if (L.d % 128 == 0) {
-        if (ej <= 1) return launch_router_t<1, 128>(L, x, T, logits, idx, wts, blockhist, s);
-        if (ej <= 2) return launch_router_t<2, 128>(L, x, T, logits, idx, wts, blockhist, s);
-        if (ej <= 4) return launch_router_t<4, 128>(L, x, T, logits, idx, wts, blockhist, s);
-        if (ej <= 8) return launch_router_t<8, 128>(L, x, T, logits, idx, wts, blockhist, s);
+        if (ej <= 1) return launch_router_t<1, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 2) return launch_router_t<2, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 4) return launch_router_t<4, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 8) return launch_router_t<8, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
     }
-    if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s);
-    if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s);
-    if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s);
-    if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s);
-    if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s);
-    return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s);
+    if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
 }
 
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {
@@ -584,7 +648,8 @@ cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* co
     return cudaGetLastError();
 }
 
-cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s) {
+cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s,
+                                        const NormRef& nr) {
     const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
     ScanOut so;
@@ -595,11 +660,11 @@ cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, c
     if (three_pass(L))
         dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, nullptr, so);
+                                                        W.row_weight, W.a_hi, nullptr, so, nr);
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, nullptr, so);
+                                                        W.row_weight, W.a_hi, nullptr, so, nr);
     return cudaGetLastError();
 }
 
@@ -611,15 +676,16 @@ cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, in
     if (three_pass(L))
         dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, ScanOut{});
+                                                        row_weight, rows, nullptr, ScanOut{}, NormRef{});
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, ScanOut{});
+                                                        row_weight, rows, nullptr, ScanOut{}, NormRef{});
     return cudaGetLastError();
 }
 
-cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s) {
+cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s,
+                                    const NormRef& nr) {
     const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
     ScanOut so;
@@ -630,11 +696,11 @@ cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaS
     if (three_pass(L))
         dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo, so);
+                                                        W.row_weight, W.a_hi, W.a_lo, so, nr);
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo, so);
+                                                        W.row_weight, W.a_hi, W.a_lo, so, nr);
     return cudaGetLastError();
 }
 

@@ -358,6 +358,9 @@ def main():
                          "128x256 for decode-sized T), or force one")
     ap.add_argument("--parallelism", choices=["ep", "dp"], default="ep",
                     help="N > 1: expert parallel (default) or token-sharded replicas")
+    ap.add_argument("--no-block", action="store_true",
+                    help="skip the decoder-layer block section (post-attention LayerNorm + "
+                         "MoE + residual)")
     ap.add_argument("--decode-max-tokens", type=int, default=None,
                     help="override the handle's decode threshold (0..64)")
     args = ap.parse_args()
@@ -482,6 +485,48 @@ def main():
                                "stages_ms": {nm: float(v) / n
                                              for nm, v in zip(pkg.PROFILE_STAGES, st_d)}}
 
+    # ---- the decoder layer's MoE half: y = x + MoE(layer_norm(x)), the norm
+    # fused into the router and the dispatch permute, the residual after the
+    # combine; and the standalone bit-exact LayerNorm (read x, write y).
+    block = {}
+    if not args.no_block:
+        nw, nb = pkg.synthetic_post_norm(wl["seed"], d)
+        layer.set_post_norm(nw, nb)
+        wd, bd = torch.from_numpy(nw).to(dev), torch.from_numpy(nb).to(dev)
+        yb = torch.empty_like(x)
+
+        def timed(fn, n):
+            for _ in range(args.warmup):
+                fn()
+                flush.zero_()
+            torch.cuda.synchronize()
+            tot, st_b = 0.0, np.zeros(len(pkg.PROFILE_STAGES))
+            for _ in range(n):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                st_b += layer.stage_ms()
+                flush.zero_()
+                b.synchronize()
+                tot += a.elapsed_time(b)
+            return tot / n, st_b / n
+
+        nb_steps = max(5, args.steps // 2)
+        for tb in sorted({T, 1}):
+            ms_b, st_b = timed(lambda: layer.block_forward_device(x.data_ptr(), yb.data_ptr(), tb,
+                                                                  sp), nb_steps)
+            block[str(tb)] = {"ms": ms_b, "tokens_per_s": tb / (ms_b / 1e3),
+                              "stages_ms": {nm: float(v)
+                                            for nm, v in zip(pkg.PROFILE_STAGES, st_b)}}
+        block[str(T)]["overhead_ms_vs_moe_forward"] = block[str(T)]["ms"] - total_ms / args.steps
+        ms_ln, _ = timed(lambda: pkg.layer_norm_device(x.data_ptr(), wd.data_ptr(), bd.data_ptr(),
+                                                       1e-5, T, d, yb.data_ptr(), sp), nb_steps)
+        ln_bytes = 2 * T * d * 4
+        block["layer_norm_device"] = {"T": T, "ms": ms_ln, "algorithmic_bytes": ln_bytes,
+                                      "gbs": ln_bytes / (ms_ln / 1e3) / 1e9,
+                                      "frac_of_hbm": ln_bytes / (ms_ln / 1e3) / 1e9 / _peaks()[0]}
+
     # ---- e2e through the host-buffer C-ABI call (pinned buffers)
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -550,6 +595,10 @@ def main():
                            "synchronous call"},
             "decode": {"hbm_peak_gbs": _peaks()[0], "by_T": decode,
                        "bytes": "routed experts x 3 x d x d_ff x weight bytes + router + x/y"},
+            "block": {"by_T": block,
+                      "what": "moe_block_forward_device: y = x + MoE(layer_norm(x)) "
+                              "(PhiDecoderLayer's MoE half; norm statistics bit-exact with "
+                              "tensor_ops::layer_norm, applied inside router and permute)"},
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clocks,
             "output_finite": ok_y,

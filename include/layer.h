@@ -12,8 +12,11 @@
 // std::invalid_argument for shape mismatches, std::runtime_error for I/O and
 // device failures (carrying moe_last_error()).
 //
-// PhiAttention and PhiDecoderLayer (attention, layer norm) are not part of
-// this library's path and are not declared here.
+//   PhiMoEBlock  the MoE half of PhiDecoderLayer::forward (src/layer.cu:
+//            157-161): post-attention LayerNorm, PhiMoE, residual add, on the
+//            GPU with the norm fused into the MoE's input
+// PhiAttention and PhiDecoderLayer's attention half are not part of this
+// library's path and are not declared here.
 //
 // Layers share their device handle between copies; a handle runs one forward
 // at a time, so copies must not run forward concurrently.
@@ -67,6 +70,27 @@ public:
                         void* stream = nullptr) const;
     // Expert indices / weights [rows][top_k] of x (host), in selection order.
     void route(const Tensor& x, std::vector<std::pair<int, float>>& routes) const;
+
+    const MoeConfig& config() const { return cfg_; }
+
+private:
+    std::shared_ptr<MoeHandle> h_;
+    MoeConfig cfg_{};
+};
+
+// y = attn + PhiMoE(layer_norm(attn)) with the layer's
+// post_attention_layernorm.{weight,bias} and NORM_EPS 1e-5 (include/config.h:
+// 19).  In PhiDecoderLayer::forward this replaces
+//     layer_norm(attn, post_norm_weight_, post_norm_bias_, NORM_EPS, post);
+//     moe_.forward(post, ff);  add_inplace(ff, attn);  y = std::move(ff);
+class PhiMoEBlock {
+public:
+    PhiMoEBlock(const ModelLoader& loader, std::size_t layer_idx);
+    PhiMoEBlock(const ModelLoader& loader, std::size_t layer_idx, const MoeConfig& cfg);
+
+    void forward(const Tensor& attn, Tensor& y) const;
+    void forward_device(const float* attn_dev, float* y_dev, std::size_t rows,
+                        void* stream = nullptr) const;
 
     const MoeConfig& config() const { return cfg_; }
 

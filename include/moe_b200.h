@@ -161,6 +161,35 @@ int moe_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* 
  * (moe_host_alloc, Tensor::Alloc::Pinned) are needed for the overlap. */
 int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T);
 
+/* ---- The MoE half of the decoder layer (PhiDecoderLayer::forward,
+ * src/layer.cu:157-161):  y = attn + MoE(layer_norm(attn)).
+ *
+ * moe_set_post_norm attaches the layer's post_attention_layernorm weight and
+ * bias ([d_model] fp32, host pointers, copied) and eps (the reference uses
+ * NORM_EPS = 1e-5, include/config.h:19); it replaces the post_norm_weight_ /
+ * post_norm_bias_ members of PhiDecoderLayer (src/layer.cu:140-147).
+ * moe_create_from_model_bin attaches them by itself when the file holds
+ * model.layers.<i>.post_attention_layernorm.{weight,bias} (eps 1e-5).
+ *
+ * moe_block_forward_device / _host then run the norm's statistics with the
+ * reference's serial arithmetic (tensor_ops::layer_norm, src/tensor.cu:
+ * 174-189, bit for bit), apply the norm inside the router and the dispatch
+ * permute (the normalised activations are never stored), run the MoE, and
+ * add the residual after the combine: y = (sum of weighted expert outputs)
+ * + attn, in the reference's order.  MOE_ERR_INVALID if no norm is attached.
+ * y must not alias attn.  d_model must be a multiple of 128. */
+int moe_set_post_norm(MoeHandle* h, const float* weight, const float* bias, float eps);
+int moe_block_forward_device(MoeHandle* h, const float* attn, float* y, int32_t T, void* stream);
+int moe_block_forward_host(MoeHandle* h, const float* attn, float* y, int32_t T);
+
+/* tensor_ops::layer_norm (src/tensor.cu:174-189) on device buffers, bit for
+ * bit with the reference's host function: y[rows][cols] = layer_norm(x) with
+ * weight/bias [cols].  Needs no handle; runs on the current device, on
+ * `stream`.  cols a multiple of 128; all pointers 16-byte aligned; y may
+ * alias x. */
+int moe_layer_norm_device(const float* x, const float* weight, const float* bias, float eps,
+                          int32_t rows, int32_t cols, float* y, void* stream);
+
 /* Router only, device buffers: logits [T][E] (may be NULL), expert indices
  * and weights [T][top_k] in selection order.  Replaces the router GEMM and
  * route (src/layer.cu:84-91; src/model.cu:505-616, 878-942). */

@@ -70,4 +70,7 @@ void add_inplace(Tensor& a, const Tensor& b);
 void add_bias_inplace(Tensor& a, const Tensor& bias);
 void mul(const Tensor& a, const Tensor& b, Tensor& c);
 void silu(const Tensor& x, Tensor& y);
+// src/tensor.cu:174-189, with the reference build's arithmetic: serial
+// j-ascending sums, unfused variance terms, fused output expression.
+void layer_norm(const Tensor& x, const Tensor& weight, const Tensor& bias, float eps, Tensor& y);
 }

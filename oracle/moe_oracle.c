@@ -141,6 +141,26 @@ void oracle_route(const float* logits, int T, int E, int k, int policy,
     }
 }
 
+/* src/tensor.cu:174-189 tensor_ops::layer_norm. */
+void oracle_layer_norm(const float* x, const float* w, const float* b, float eps, int T, int d,
+                       float* y) {
+#pragma omp parallel for schedule(static)
+    for (long long r = 0; r < (long long)T; ++r) {
+        const float* xr = x + (size_t)r * d;
+        float* yr = y + (size_t)r * d;
+        float mean = 0.0f;
+        for (int j = 0; j < d; ++j) mean += xr[j];
+        mean /= (float)d;
+        float var = 0.0f;
+        for (int j = 0; j < d; ++j) {
+            const float dv = xr[j] - mean;
+            var += dv * dv;   /* not contracted in the reference build: rounded product */
+        }
+        const float inv = 1.0f / sqrtf(var / (float)d + eps);
+        for (int j = 0; j < d; ++j) yr[j] = fmaf((xr[j] - mean) * inv, w[j], b[j]);
+    }
+}
+
 /* src/layer.cu:32-45 PhiMLP::forward. */
 void oracle_expert_ffn(const float* X, int rows, int d, int ff,
                        const float* w1, const float* w3, const float* w2,

@@ -57,6 +57,14 @@ void oracle_expert_ffn(const float* X, int rows, int d, int ff,
                        const float* w1, const float* w3, const float* w2,
                        float* out, int nthreads);
 
+/* tensor_ops::layer_norm (src/tensor.cu:174-189) per row of x [T][d]:
+ * mean = serial sum / d; var = serial sum of rounded (x - mean)^2, / d;
+ * inv = 1 / sqrt(var + eps); y = fma((x - mean) * inv, w, b).  GCC contracts
+ * the output expression but leaves the variance accumulation unfused; both
+ * were established bit-exactly against the reference's compiled function. */
+void oracle_layer_norm(const float* x, const float* w, const float* b, float eps, int T, int d,
+                       float* y);
+
 /* Full layer.  w1[e], w3[e]: [ff][d]; w2[e]: [d][ff].  y is [T][d] and is
  * overwritten.  idx/w/logits outputs may be NULL.  If `sample` is non-NULL
  * only the n_sample listed tokens get their y rows computed (routing is still

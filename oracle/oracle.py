@@ -69,6 +69,16 @@ class Oracle:
                                          ctypes.c_float, _f32p, _f32p, PP, PP, PP, _i32p,
                                          ctypes.c_int, _f32p, _i32p, _f32p, _f32p, ctypes.c_int]
         L.oracle_moe_forward.restype = ctypes.c_int
+        L.oracle_layer_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_float, ctypes.c_int,
+                                        ctypes.c_int, _f32p]
+
+    def layer_norm(self, x, w, b, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        T, d = x.shape
+        y = np.empty_like(x)
+        self.lib.oracle_layer_norm(_fp(x), _fp(np.ascontiguousarray(w, np.float32)),
+                                   _fp(np.ascontiguousarray(b, np.float32)), eps, T, d, _fp(y))
+        return y
 
     def router_logits(self, x, wg, bias=None, nthreads=0):
         x = np.ascontiguousarray(x, np.float32)
@@ -127,6 +137,14 @@ class Oracle:
             raise ValueError("oracle_moe_forward rejected its arguments")
         return y, idx, w, logits
 
+    def block_forward(self, attn, layer, k, policy, norm_w, norm_b, eps=1e-5, nthreads=0):
+        """The decoder layer's MoE half (src/layer.cu:157-161): post =
+        layer_norm(attn); y = moe(post) + attn.  Returns (y, idx, post)."""
+        attn = np.ascontiguousarray(attn, np.float32)
+        post = self.layer_norm(attn, norm_w, norm_b, eps)
+        ff, idx, _, _ = self.moe_forward(post, layer, k, policy, nthreads=nthreads)
+        return ff + attn, idx, post
+
 
 class Reference:
     """The reference's own PhiMoE (compiled from its sources) for E experts."""
@@ -146,6 +164,8 @@ class Reference:
         L.ref_matmul_transposed.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
                                             ctypes.c_int]
         L.ref_last_error.restype = ctypes.c_char_p
+        L.ref_layer_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_float, ctypes.c_int,
+                                     ctypes.c_int, _f32p]
         L.ref_set_threads.argtypes = [ctypes.c_int]
         L.ref_set_threads.restype = ctypes.c_int
         self.E = L.ref_num_experts()
@@ -186,6 +206,16 @@ class Reference:
         if self.lib.ref_moe_route(self.h, _fp(x), T, d, _fp(logits), _ip(idx), _fp(w)) != 0:
             raise RuntimeError(self.lib.ref_last_error().decode())
         return logits, idx, w
+
+    def layer_norm(self, x, w, b, eps=1e-5):
+        x = np.ascontiguousarray(x, np.float32)
+        T, d = x.shape
+        y = np.empty_like(x)
+        if self.lib.ref_layer_norm(_fp(x), _fp(np.ascontiguousarray(w, np.float32)),
+                                   _fp(np.ascontiguousarray(b, np.float32)), eps, T, d,
+                                   _fp(y)) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return y
 
     def matmul_transposed(self, a, b):
         a = np.ascontiguousarray(a, np.float32)

@@ -120,6 +120,24 @@ int ref_moe_route(void* h, const float* x, int T, int d, float* logits, int* idx
     }
 }
 
+// tensor_ops::layer_norm on raw buffers (src/tensor.cu:174-189).
+int ref_layer_norm(const float* x, const float* w, const float* b, float eps, int T, int d,
+                   float* y) {
+    try {
+        Tensor xt({static_cast<std::size_t>(T), static_cast<std::size_t>(d)});
+        Tensor wt({static_cast<std::size_t>(d)}), bt({static_cast<std::size_t>(d)});
+        Tensor yt({static_cast<std::size_t>(T), static_cast<std::size_t>(d)});
+        std::memcpy(xt.data(), x, sizeof(float) * xt.size());
+        std::memcpy(wt.data(), w, sizeof(float) * wt.size());
+        std::memcpy(bt.data(), b, sizeof(float) * bt.size());
+        tensor_ops::layer_norm(xt, wt, bt, eps, yt);
+        std::memcpy(y, yt.data(), sizeof(float) * yt.size());
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
 // tensor_ops::matmul_transposed on raw buffers (src/tensor.cu:136-148).
 int ref_matmul_transposed(const float* a, const float* b, float* c, int m, int k, int n) {
     try {

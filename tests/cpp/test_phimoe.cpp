@@ -7,6 +7,10 @@
 //       PhiMLP(loader, "...experts.0")   -> <out_prefix>.mlp.bin
 //       PhiMoE::route                    -> <out_prefix>.route.bin (int idx, float w)
 //       a wrong-width input must throw std::invalid_argument
+//   test_phimoe layernorm <model.bin> <x.bin> <T> <d> <out_prefix>   no GPU
+//       tensor_ops::layer_norm with post_attention_layernorm -> <out_prefix>.ln.bin
+//   test_phimoe block <model.bin> <x.bin> <T> <d> <out_prefix>
+//       PhiMoEBlock(loader, 0).forward(attn, y)          -> <out_prefix>.block.bin
 #include "layer.h"
 #include "model_loader.h"
 #include "tensor.h"
@@ -127,11 +131,53 @@ static int forward(const std::string& model, const std::string& xpath, size_t T,
     return failures ? 1 : 0;
 }
 
+static Tensor read_x(const std::string& xpath, size_t T, size_t d) {
+    Tensor x({T, d});
+    std::ifstream f(xpath, std::ios::binary);
+    f.read(reinterpret_cast<char*>(x.data()), static_cast<std::streamsize>(T * d * 4));
+    if (!f) throw std::runtime_error("cannot read x");
+    return x;
+}
+
+static int layernorm(const std::string& model, const std::string& xpath, size_t T, size_t d,
+                     const std::string& out) {
+    ModelLoader loader(model);
+    const Tensor x = read_x(xpath, T, d);
+    const Tensor w = loader.load("model.layers.0.post_attention_layernorm.weight");
+    const Tensor b = loader.load("model.layers.0.post_attention_layernorm.bias");
+    Tensor y({T, d});
+    tensor_ops::layer_norm(x, w, b, 1.0e-5f, y);
+    write_file(out + ".ln.bin", y.data(), y.size() * 4);
+    Tensor bad({T, d + 1});
+    CHECK(throws<std::invalid_argument>([&] { tensor_ops::layer_norm(x, w, b, 1e-5f, bad); },
+                                        "layer norm shape"),
+          "layer_norm shape");
+    std::printf("%s\n", failures ? "layernorm: FAILED" : "layernorm: ok");
+    return failures ? 1 : 0;
+}
+
+static int block(const std::string& model, const std::string& xpath, size_t T, size_t d,
+                 const std::string& out) {
+    ModelLoader loader(model);
+    PhiMoEBlock blk(loader, 0);
+    const Tensor attn = read_x(xpath, T, d);
+    Tensor y;
+    blk.forward(attn, y);
+    CHECK(y.ndim() == 2 && y.size(0) == T && y.size(1) == d, "PhiMoEBlock output shape");
+    write_file(out + ".block.bin", y.data(), y.size() * 4);
+    std::printf("%s\n", failures ? "block: FAILED" : "block: ok");
+    return failures ? 1 : 0;
+}
+
 int main(int argc, char** argv) {
     try {
         if (argc >= 3 && std::string(argv[1]) == "errors") return errors(argv[2]);
         if (argc >= 7 && std::string(argv[1]) == "forward")
             return forward(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
+        if (argc >= 7 && std::string(argv[1]) == "layernorm")
+            return layernorm(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
+        if (argc >= 7 && std::string(argv[1]) == "block")
+            return block(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
     } catch (const std::exception& e) {
         std::fprintf(stderr, "uncaught: %s\n", e.what());
         return 2;

@@ -52,3 +52,35 @@ def test_phimoe_forward_matches_reference(test_bin, tmp_path):
     ym = np.fromfile(tmp_path / "out.mlp.bin", np.float32).reshape(T, d)
     ym_ref = oracle.Oracle().expert_ffn(x, layer.w1[0], layer.w3[0], layer.w2[0])
     assert rel_l2(ym, ym_ref) <= 1e-3             # PhiMLP::forward (src/layer.cu:32-45)
+
+
+def _block_model(pkg, tmp_path, name="c1"):
+    layer, x = case_inputs(pkg, name)
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    layer.norm_weight, layer.norm_bias = g["block_norm_w"], g["block_norm_b"]
+    model = tmp_path / "mb.bin"
+    pkg.write_model_bin(model, [layer])
+    xp = tmp_path / "x.bin"
+    x.tofile(xp)
+    return model, xp, x.shape, g
+
+
+def test_host_layer_norm_matches_reference_fixture(test_bin, tmp_path):
+    """tensor_ops::layer_norm of the drop-in (host) gives the reference's bits."""
+    model, xp, (T, d), g = _block_model(load_pkg(), tmp_path)
+    r = subprocess.run([str(test_bin), "layernorm", str(model), str(xp), str(T), str(d),
+                        str(tmp_path / "out")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    y = np.fromfile(tmp_path / "out.ln.bin", np.float32).reshape(T, d)
+    assert np.array_equal(y.view(np.uint32), g["block_post"].view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_phimoe_block_matches_reference(test_bin, tmp_path):
+    """PhiMoEBlock(loader, 0): layer_norm -> PhiMoE -> + attn of the reference."""
+    model, xp, (T, d), g = _block_model(load_pkg(), tmp_path)
+    r = subprocess.run([str(test_bin), "block", str(model), str(xp), str(T), str(d),
+                        str(tmp_path / "out")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    y = np.fromfile(tmp_path / "out.block.bin", np.float32).reshape(T, d)
+    assert rel_l2(y, g["block_phi_y"]) <= 1e-3

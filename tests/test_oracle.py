@@ -144,3 +144,31 @@ def test_empty_input(orc):
     x = np.zeros((0, 64), np.float32)
     y, idx, w, logits = orc.moe_forward(x, layer, 2, oracle.POLICY_PHI)
     assert y.shape == (0, 64)
+
+
+@need_ref8
+def test_layer_norm_matches_reference(orc):
+    """tensor_ops::layer_norm (src/tensor.cu:174-189), bit for bit."""
+    ref = oracle.Reference(8)
+    g = np.random.default_rng(9)
+    for (T, d) in [(1, 64), (7, 512), (33, 4096)]:
+        x = (g.standard_normal((T, d)) * 3 + 0.5).astype(np.float32)
+        w = g.standard_normal(d).astype(np.float32)
+        b = g.standard_normal(d).astype(np.float32)
+        assert np.array_equal(bits(orc.layer_norm(x, w, b, 1e-5)), bits(ref.layer_norm(x, w, b, 1e-5)))
+
+
+@pytest.mark.parametrize("name", [n for n in sorted(CASES)
+                                  if "block_phi_y" in np.load(GOLDEN_DIR / f"{n}.npz")])
+def test_block_fixture(name, orc):
+    """The decoder layer's MoE half (src/layer.cu:157-161) from the reference,
+    committed as a fixture: the restatement reproduces the normalised rows,
+    the expert indices and y bit for bit."""
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, name)
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    y, idx, post = orc.block_forward(x, layer, 2, oracle.POLICY_PHI, g["block_norm_w"],
+                                     g["block_norm_b"], 1e-5)
+    assert np.array_equal(bits(post), bits(g["block_post"]))
+    assert np.array_equal(idx, g["block_phi_idx"])
+    assert np.array_equal(bits(y), bits(g["block_phi_y"]))
