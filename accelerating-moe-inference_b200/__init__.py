@@ -30,6 +30,8 @@ ROUTER_PHI_QUANTISED = 0
 ROUTER_SOFTMAX_TOPK = 1
 PREC_FP32 = 0
 PREC_BF16 = 1
+# MoeConfig.decode_max_tokens: the measured decode-kernel threshold of the precision.
+DECODE_AUTO = -1
 GEMM_AUTO = 0
 GEMM_SINGLE_CTA = 1
 GEMM_CTA_PAIR = 2

@@ -170,6 +170,17 @@ int ensure_stage(Layer& L, int T) {
     return MOE_OK;
 }
 
+}  // namespace
+
+// The decode-kernel threshold MOE_DECODE_AUTO resolves to, from the measured
+// crossover with the grouped GEMMs on B200 (C2 weights): in BF16 the grouped
+// GEMMs stream as fast as the decode kernels from T = 2 on and faster from
+// T = 4; in FP32 the decode kernels read 4 bytes per weight against the
+// 3xTF32 GEMMs' 8 and stay ahead up to about T = 14.
+int auto_decode_max_tokens(int precision) { return precision == MOE_PREC_BF16 ? 1 : 14; }
+
+namespace {
+
 int validate_config(const MoeConfig& c) {
     if (c.d_model <= 0 || c.d_model % 64 != 0)
         return fail(MOE_ERR_UNSUPPORTED, "d_model must be a positive multiple of 64");
@@ -186,8 +197,8 @@ int validate_config(const MoeConfig& c) {
         return fail(MOE_ERR_INVALID, "router_quantum must be positive");
     if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16)
         return fail(MOE_ERR_INVALID, "unknown precision");
-    if (c.decode_max_tokens < 0 || c.decode_max_tokens > decode_max_supported_tokens())
-        return fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
+    if (c.decode_max_tokens < -1 || c.decode_max_tokens > decode_max_supported_tokens())
+        return fail(MOE_ERR_INVALID, "decode_max_tokens must be in -1..64");
     if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
     if (c.gemm_variant < MOE_GEMM_AUTO || c.gemm_variant > MOE_GEMM_CTA_PAIR)
         return fail(MOE_ERR_INVALID, "unknown gemm_variant");
@@ -348,7 +359,7 @@ void moe_config_init(MoeConfig* c) {
     c->precision = MOE_PREC_FP32;
     c->router_quantum = 1.0e-3f;
     c->router_tie_eps = 2.0e-2f;
-    c->decode_max_tokens = 16;
+    c->decode_max_tokens = MOE_DECODE_AUTO;
     c->device = 0;
     c->max_tokens = 0;
 }
@@ -407,6 +418,7 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
     std::unique_ptr<MoeHandle> h(new MoeHandle());
     Layer& L = h->L;
     L.cfg = *cfg;
+    if (L.cfg.decode_max_tokens < 0) L.cfg.decode_max_tokens = auto_decode_max_tokens(cfg->precision);
     L.d = cfg->d_model;
     L.ff = cfg->d_ff;
     L.ffp = (cfg->d_ff + kFfBlock - 1) / kFfBlock * kFfBlock;
@@ -618,9 +630,9 @@ size_t moe_device_bytes(const MoeHandle* h) {
 }
 
 int moe_set_decode_max_tokens(MoeHandle* h, int32_t n) {
-    if (!h || n < 0 || n > moe::decode_max_supported_tokens())
-        return moe::fail(MOE_ERR_INVALID, "decode_max_tokens must be in 0..64");
-    h->L.cfg.decode_max_tokens = n;
+    if (!h || n < -1 || n > moe::decode_max_supported_tokens())
+        return moe::fail(MOE_ERR_INVALID, "decode_max_tokens must be in -1..64");
+    h->L.cfg.decode_max_tokens = n < 0 ? moe::auto_decode_max_tokens(h->L.cfg.precision) : n;
     return MOE_OK;
 }
 

@@ -29,6 +29,8 @@
 // per K-block, 2 stages).  Both use 128-byte-swizzled K-major tiles.
 #include <cuda_bf16.h>
 
+#include <algorithm>
+
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -42,6 +44,8 @@ struct GemmParams {
     const int* num_mtiles;
     int n_tiles;       // N tiles per expert
     int k_blocks;      // K / (elements per 128-byte block)
+    int k_splits;      // K splits per tile (down with the adding epilogue only; else 1)
+    int kb_per;        // K blocks per split; k_splits = ceil(k_blocks / kb_per), none empty
     int b_rows_per_expert;
     // gate/up epilogue
     void* h_hi;
@@ -56,6 +60,10 @@ struct GemmParams {
 };
 
 constexpr int kThreads = 192;
+// Split-K of the down GEMM: only for at most this many routed rows, and at
+// least this many 128-byte K blocks per split.
+constexpr int kSplitMaxRows = 64;
+constexpr int kSplitMinBlocks = 8;
 constexpr int kABytes = kTileM * 128;   // one A plane per stage: 128 rows x 128 B
 constexpr int kBBytes = kTileN * 128;   // one B plane per stage: 256 rows x 128 B
 constexpr int kAccCols = kTileN;        // fp32 columns per accumulator
@@ -259,7 +267,10 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
     const uint32_t tmem_base = *tmem_slot;
 
     const int m_tiles = *p.num_mtiles;
-    const int total = m_tiles * p.n_tiles;
+    // Work items: tiles x K splits, the split fastest, so the splits of one
+    // tile (which share its activation rows) run side by side.
+    const int total = m_tiles * p.n_tiles * p.k_splits;
+    const int kb_per = p.kb_per;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -268,12 +279,14 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             uint32_t phase = 0;
             int issued = 0;
             for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-                const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+                const TileCoord tc = decode_tile(p.mtiles, t / p.k_splits, p.n_tiles);
                 const int mt = tc.mt, nt = tc.nt;
                 const MTile tile = p.mtiles[mt];
                 const int brow = tile.expert * p.b_rows_per_expert + nt * kTileN;
                 constexpr int kElems = kTf32x3 ? 32 : 64;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                const int kb0 = (t % p.k_splits) * kb_per;
+                const int kb1 = min(p.k_blocks, kb0 + kb_per);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, kDevErrTimeoutProducer)) {
                         *abort_flag = 1;
                         break;
@@ -319,7 +332,9 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * kAccCols;
                 bool ok = true;
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                const int kb0 = (t % p.k_splits) * kb_per;
+                const int kb1 = min(p.k_blocks, kb0 + kb_per);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(&full[stage], phase, p.err, kDevErrTimeoutMma)) {
                         *abort_flag = 1;
                         ok = false;
@@ -340,7 +355,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     for (int ks = 0; ks < 4; ++ks) {
                         // 32 bytes of K per instruction: +2 in the >>4 address field.
                         const uint64_t off = static_cast<uint64_t>(ks * 2);
-                        const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
+                        const uint32_t accum = (kb != kb0 || ks != 0) ? 1u : 0u;
                         if constexpr (kTf32x3) {
                             tc_mma<true>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
                             tc_mma<true>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
@@ -369,7 +384,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             // Exit decisions are warp-uniform: tcgen05.ld below is .sync.aligned.
             if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
-            const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
+            const TileCoord tc = decode_tile(p.mtiles, t / p.k_splits, p.n_tiles);
             const int mt = tc.mt, nt = tc.nt;
             const bool ready = mbar_wait(&tfull[acc], acc_phase, p.err, kDevErrTimeoutEpilogue);
             if (!__all_sync(0xffffffffu, ready)) {
@@ -675,6 +690,8 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
     g.h_hi = W.h_hi;
     g.h_lo = W.h_lo;
     g.ldh = L.ffp;
+    g.k_splits = 1;
+    g.kb_per = 0;   // set below, with k_blocks
     if (!down) {
         // gate/up: N = 2 * ffp per expert, K = d.
         g.n_tiles = 2 * L.ffp / kTileN;
@@ -686,6 +703,7 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         g.k_blocks = L.ffp / elems;
         g.b_rows_per_expert = L.d;
     }
+    g.kb_per = g.k_blocks;
     // CTA-pair tiles pay off when experts have at least 256 routed rows on
     // average; below that (decode-sized T) most of a 256-row tile would be
     // padding and the 1-CTA tiles spread the weight stream over twice as many
@@ -719,7 +737,19 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         return launch_pair<false, kEpiDown>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2, gp,
                                             clusters, s);
     }
-    int grid = max_mtiles * g.n_tiles;
+    // Decode-sized batches leave the down GEMM with few tiles (d / 256 per
+    // routed expert), too few to keep every SM streaming weights: split K
+    // until there are about two work items per SM.  The combine epilogue adds
+    // weight x partial into y, so the splits need no other reduction (their
+    // order of addition is not fixed, so such results are not bit-repeatable).
+    if (mode == 1 && routed_rows <= kSplitMaxRows) {
+        const int tiles = std::min(routed_rows, L.E) * g.n_tiles;
+        int ks = (2 * L.sm_count) / std::max(tiles, 1);
+        ks = std::max(1, std::min(ks, g.k_blocks / kSplitMinBlocks));
+        g.kb_per = (g.k_blocks + ks - 1) / ks;
+        g.k_splits = (g.k_blocks + g.kb_per - 1) / g.kb_per;
+    }
+    int grid = max_mtiles * g.n_tiles * g.k_splits;
     if (grid > L.sm_count) grid = L.sm_count;
     if (!down) {
         if (tf)

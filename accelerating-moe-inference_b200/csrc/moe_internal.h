@@ -197,6 +197,8 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
 cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
                           const NormRef& nr = {});
 int decode_max_supported_tokens();
+// What MOE_DECODE_AUTO resolves to for a precision (capi.cu).
+int auto_decode_max_tokens(int precision);
 
 // norm.cu: per-row LayerNorm statistics, the whole LayerNorm into y (d a
 // multiple of 128: norm_supported), and y += r over n floats (n a multiple

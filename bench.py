@@ -53,7 +53,7 @@ WORKLOADS = {
                     seed=1),
 }
 KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
-DECODE_T = (1, 8, 32, 64)
+DECODE_T = (1, 2, 4, 8, 16, 32, 64)
 FLUSH_BYTES = 256 << 20
 
 

@@ -80,6 +80,8 @@ typedef enum MoeGemmVariant {
     MOE_GEMM_CTA_PAIR = 2
 } MoeGemmVariant;
 
+#define MOE_DECODE_AUTO (-1)
+
 typedef struct MoeConfig {
     int32_t d_model;        /* hidden size; multiple of 64 */
     int32_t d_ff;           /* expert intermediate size (any; padded internally) */
@@ -90,7 +92,9 @@ typedef struct MoeConfig {
     float router_quantum;   /* PHI policy score quantum (reference 1e-3, include/config.h:22) */
     float router_tie_eps;   /* PHI policy tie margin (reference 2e-2, include/config.h:23) */
     int32_t decode_max_tokens; /* T <= this takes the weight-streaming decode kernels
-                                  (0..64; 0: never; default 16) */
+                                  (0..64; 0: never; MOE_DECODE_AUTO (-1, the
+                                  default): the measured crossover for the
+                                  precision -- 1 in BF16, 14 in FP32) */
     int32_t device;         /* CUDA device ordinal the handle lives on */
     int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
     int32_t gemm_variant;   /* MoeGemmVariant of the grouped expert GEMMs */
@@ -145,7 +149,9 @@ int moe_get_config(const MoeHandle* h, MoeConfig* cfg);
 /* Device bytes held by the handle (weights + workspace). */
 size_t moe_device_bytes(const MoeHandle* h);
 
-/* Change the decode threshold (MoeConfig.decode_max_tokens) of a handle. */
+/* Change the decode threshold (MoeConfig.decode_max_tokens) of a handle;
+ * MOE_DECODE_AUTO re-selects the precision's default.  moe_get_config
+ * reports the threshold in force. */
 int moe_set_decode_max_tokens(MoeHandle* h, int32_t max_tokens);
 
 /* y[T][d] = MoE(x[T][d]) on device buffers, enqueued on `stream`; no host

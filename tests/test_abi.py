@@ -51,6 +51,7 @@ def test_config_defaults_are_reference_constants():
     assert (c.d_model, c.d_ff, c.num_experts, c.top_k) == (4096, 448, 16, 2)
     assert c.router_policy == pkg.ROUTER_PHI_QUANTISED
     assert abs(c.router_quantum - 1e-3) < 1e-9 and abs(c.router_tie_eps - 2e-2) < 1e-9
+    assert c.decode_max_tokens == pkg.DECODE_AUTO == -1   # resolved per precision by a handle
 
 
 def test_invalid_config_is_rejected_before_any_device_work():

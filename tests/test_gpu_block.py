@@ -130,8 +130,8 @@ def test_block_forward_matches_reference_fixture(name, precision, gemm):
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
 @pytest.mark.parametrize("T", [1, 5, 16, 33, 300])
 def test_block_forward_decode_and_prefill_match_oracle(T, precision, orc):
-    """Both paths: T <= 16 runs the decode kernels (norm applied in the row
-    packing), larger T the grouped GEMMs."""
+    """Both paths: small T runs the decode kernels (norm applied in the row
+    packing; T <= 14 in FP32, T = 1 in BF16), larger T the grouped GEMMs."""
     pkg = load_pkg()
     layer = pkg.synthetic_layer(41, 512, 448, 8)
     layer.norm_weight, layer.norm_bias = pkg.synthetic_post_norm(41, 512)

@@ -195,6 +195,22 @@ def test_decode_path_matches_oracle(T, precision, orc):
 
 
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("T", [1, 2, 5, 8, 16, 32])
+def test_grouped_gemm_path_at_decode_sizes(T, precision, orc):
+    """The tcgen05 GEMMs at decode-sized T (decode kernels off), where the
+    down GEMM splits K across SMs and adds the partial sums into y."""
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(32, 512, 1536, 8)     # down K = 1536: 24 bf16 / 48 tf32 blocks
+    x = pkg.synthetic_tokens(32, T, 512)
+    y_ref, *_ = orc.moe_forward(x, layer, 2, oracle.POLICY_SOFTMAX)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision, decode_max_tokens=0) as m:
+        y = m.forward_host(x)
+    assert rel_l2(y, y_ref) <= TOL[precision]
+    if precision == 0:
+        assert ref_elementwise_failures(y, y_ref) == 0
+
+
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
 def test_decode_and_prefill_paths_agree(precision):
     pkg = load_pkg()
     layer, x = case_inputs(pkg, "c5mini")      # 64 experts, top-8, router bias
@@ -209,12 +225,19 @@ def test_decode_and_prefill_paths_agree(precision):
     assert rel_l2(y_dec, y_pre) <= TOL[precision]
 
 
-def test_decode_threshold_bounds():
+def test_decode_threshold_bounds_and_auto():
+    """MOE_DECODE_AUTO resolves per precision to the measured crossover with
+    the grouped GEMMs (1 in BF16, 14 in FP32); out-of-range values fail."""
     pkg = load_pkg()
     layer = pkg.synthetic_layer(1, 64, 64, 4)
     with pkg.MoeLayer(layer, top_k=2, policy=1) as m:
+        assert m.cfg.decode_max_tokens == 14
         with pytest.raises(pkg.MoeError):
             m.set_decode_max_tokens(65)
+        m.set_decode_max_tokens(5)
+        m.set_decode_max_tokens(pkg.DECODE_AUTO)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=1) as m:
+        assert m.cfg.decode_max_tokens == 1
 
 
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
