@@ -236,19 +236,29 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
         nr.w = L.norm_w;
         nr.b = L.norm_b;
     }
-    MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
+    const bool decode = T <= L.cfg.decode_max_tokens;
+    // A decode-sized batch is routed and dispatched (and y zeroed) by one
+    // single-CTA launch.
+    int kc = 0, stages = 0;
+    const bool small = route_small_geometry(L, T, block, &kc, &stages);
+    if (!small) MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
     prof_mark(L, 0, s);
     if (block)
         MOE_CUDA(launch_row_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, W.dev_err, s));
-    MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, nr));
+    if (small) {
+        MOE_CUDA(launch_route_small(L, x, T, nr, decode, y, s));
+    } else {
+        MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, nr));
+    }
     prof_mark(L, 1, s);
     // A batch that fits one router block is scanned inside the permute kernel.
     if (T > kRouteTokens) MOE_CUDA(launch_dispatch_scan(L, T, s));
     prof_mark(L, 2, s);
-    if (T <= L.cfg.decode_max_tokens) {
-        MOE_CUDA(launch_decode(L, x, T, y, s, nr));  // marks stages 3 and 4 between its kernels
+    if (decode) {
+        // marks stages 3 and 4 between its kernels
+        MOE_CUDA(launch_decode(L, x, T, y, s, nr, /*packed=*/small));
     } else {
-        MOE_CUDA(launch_dispatch_permute(L, x, T, s, nr));
+        if (!small) MOE_CUDA(launch_dispatch_permute(L, x, T, s, nr));
         prof_mark(L, 3, s);
         MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/false));
         prof_mark(L, 4, s);

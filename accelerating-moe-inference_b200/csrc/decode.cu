@@ -77,6 +77,13 @@ struct Vec<__nv_bfloat16> {
     }
 };
 
+// Programmatic dependent launch: these kernels are launched while their
+// predecessor on the stream may still be running, and wait here before
+// reading anything it wrote (a no-op for an ordinary launch).
+__device__ __forceinline__ void wait_predecessor() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -165,6 +172,7 @@ decode_gateup_kernel(const AT* __restrict__ a_rows, const WT* __restrict__ w13, 
                      int E, const int* __restrict__ counts, const int* __restrict__ eoff,
                      float* __restrict__ h) {
     __shared__ Active A;
+    wait_predecessor();
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const long long W = (long long)gridDim.x * kDecWarps;
@@ -219,6 +227,7 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
                    const int* __restrict__ row_token, const float* __restrict__ row_weight,
                    float* __restrict__ y) {
     __shared__ Active A;
+    wait_predecessor();
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const int nq = (d + 3) / 4;                    // column quads per expert
@@ -266,17 +275,34 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
     }
 }
 
+// One CTA per SM, launched with programmatic stream serialisation (the
+// kernel waits for its predecessor itself).  Profiling disables it so the
+// stage events stay between the kernels.
+template <typename Kern, typename... Args>
+cudaError_t launch_dependent(const Layer& L, Kern kern, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(L.sm_count);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L.profile ? 0 : 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <typename WT, typename AT, int TM>
 cudaError_t launch_t(Layer& L, float* y, cudaStream_t s, const WT* w13, const WT* w2) {
     const Workspace& W = L.ws;
-    decode_gateup_kernel<WT, AT, TM><<<L.sm_count, kDecThreads, 0, s>>>(
-        static_cast<const AT*>(W.a_hi), w13, L.d, L.ffp, L.E, W.counts, W.eoff, W.h_dec);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_dependent(L, decode_gateup_kernel<WT, AT, TM>, s,
+                                       static_cast<const AT*>(W.a_hi), w13, L.d, L.ffp, L.E,
+                                       (const int*)W.counts, (const int*)W.eoff, W.h_dec);
     if (err != cudaSuccess) return err;
     prof_mark(L, 4, s);
-    decode_down_kernel<WT, TM><<<L.sm_count, kDecThreads, 0, s>>>(
-        W.h_dec, w2, L.d, L.ffp, L.E, W.counts, W.eoff, W.row_token, W.row_weight, y);
-    return cudaGetLastError();
+    return launch_dependent(L, decode_down_kernel<WT, TM>, s, (const float*)W.h_dec, w2, L.d,
+                            L.ffp, L.E, (const int*)W.counts, (const int*)W.eoff,
+                            (const int*)W.row_token, (const float*)W.row_weight, y);
 }
 
 template <typename WT, typename AT>
@@ -296,12 +322,15 @@ cudaError_t launch_w(Layer& L, int T, float* y, cudaStream_t s, const WT* w13, c
 int decode_max_supported_tokens() { return kMaxDecodeTokens; }
 
 cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
-                          const NormRef& nr) {
+                          const NormRef& nr, bool packed) {
     if (T > kMaxDecodeTokens || !L.ws.h_dec) return cudaErrorInvalidValue;
     // Pack the routed token rows (fp32 as is in FP32 precision, bf16 in BF16),
-    // normalised on the way when nr is active.
-    cudaError_t err = launch_dispatch_permute_raw(L, x, T, s, nr);
-    if (err != cudaSuccess) return err;
+    // normalised on the way when nr is active -- unless the small-batch
+    // router already did.
+    if (!packed) {
+        cudaError_t err = launch_dispatch_permute_raw(L, x, T, s, nr);
+        if (err != cudaSuccess) return err;
+    }
     prof_mark(L, 3, s);
     if (L.cfg.precision == MOE_PREC_BF16)
         return launch_w<__nv_bfloat16, __nv_bfloat16>(

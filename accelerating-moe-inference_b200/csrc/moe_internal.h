@@ -168,6 +168,13 @@ inline void prof_mark(Layer& L, int i, cudaStream_t s) {
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
                           float* wts, int* blockhist, cudaStream_t s, const NormRef& nr = {});
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
+// Batches of at most 4 tokens: router, selection, layout and the routed rows
+// in one single-CTA launch (rows in the decode kernels' format if `decode`,
+// else the GEMMs'), which also zeroes y [T][d].  route_small_geometry says
+// whether it applies.
+bool route_small_geometry(const Layer& L, int T, bool norm, int* kc, int* stages);
+cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
+                               bool decode, float* y, cudaStream_t s);
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s,
                                     const NormRef& nr = {});
 // The same placement with the rows copied in the decode kernels' format:
@@ -194,8 +201,9 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
                                     int mode);
 
 // decode.cu: T <= decode_max_supported_tokens() (64)
+// packed: the routed rows are already in the decode format (launch_route_small).
 cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
-                          const NormRef& nr = {});
+                          const NormRef& nr = {}, bool packed = false);
 int decode_max_supported_tokens();
 // What MOE_DECODE_AUTO resolves to for a precision (capi.cu).
 int auto_decode_max_tokens(int precision);

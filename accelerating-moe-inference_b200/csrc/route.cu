@@ -20,7 +20,9 @@
 //                     format (bf16, or tf32 hi + lo planes).
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cfloat>
+#include <type_traits>
 #include <climits>
 #include <cmath>
 
@@ -59,6 +61,66 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Softmax ordering key: NaN sorts below every number (as -inf).
 __device__ __forceinline__ float route_key(float v) { return v != v ? -INFINITY : v; }
+
+// Expert selection for one token's logits l[0..E): warp-collective (every
+// lane calls it); the k selected experts and combine weights are valid on
+// lane 0.
+//   PHI_QUANTISED (src/layer.cu:47-70): quantise, then two hysteresis scans;
+//     the scan is order-dependent, so one lane runs it serially.
+//   SOFTMAX_TOPK: k rounds of a warp-wide argmax over (key, index), larger
+//     key first, exact ties to the lower index; weights are the softmax of
+//     the chosen logits in double, renormalised over the k.
+__device__ __forceinline__ void select_experts(const float* l, int E, int k, int policy,
+                                               float quantum, float tie_eps, int lane,
+                                               int (&sel)[kMaxTopK], float (&wsel)[kMaxTopK]) {
+    if (policy == MOE_ROUTER_PHI_QUANTISED) {
+        if (lane == 0) {
+            for (int s = 0; s < 2; ++s) {
+                const int excluded = s == 0 ? -1 : sel[0];
+                int best = -1;
+                float best_value = -INFINITY;
+                for (int e = 0; e < E; ++e) {
+                    if (e == excluded) continue;
+                    const float score = l[e];
+                    const float rounded =
+                        floorf(__fadd_rn(__fdiv_rn(fabsf(score), quantum), 0.5f)) * quantum;
+                    const float v = score < 0.0f ? -rounded : rounded;
+                    if (best < 0 || v > __fadd_rn(best_value, tie_eps)) {
+                        best = e;
+                        best_value = v;
+                    }
+                }
+                sel[s] = best;
+                wsel[s] = 0.5f;
+            }
+        }
+        return;
+    }
+    unsigned taken = 0;  // bit i: expert lane + 32 i already chosen
+    for (int s = 0; s < k; ++s) {
+        float bk = -INFINITY;
+        int bi = INT_MAX;
+        for (int i = 0, e = lane; e < E; ++i, e += 32) {
+            if (taken & (1u << i)) continue;
+            const float kv = route_key(l[e]);
+            if (bi == INT_MAX || kv > bk) { bk = kv; bi = e; }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ok = __shfl_xor_sync(0xffffffffu, bk, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ok > bk || (ok == bk && oi < bi)) { bk = ok; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        sel[s] = bi;
+    }
+    if (lane == 0) {
+        const double m = (double)l[sel[0]];
+        double p[kMaxTopK], sum = 0.0;
+        for (int s = 0; s < k; ++s) { p[s] = exp((double)l[sel[s]] - m); sum += p[s]; }
+        for (int s = 0; s < k; ++s) wsel[s] = (float)(p[s] / sum);
+    }
+}
 
 // Thread layout: el = tid % 8 is the expert lane, tt = tid / 8 the token
 // (0..31).  Thread (tt, el) owns the chains of experts el, el + 8, ...,
@@ -211,60 +273,9 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     for (int q = 0; q < 4; ++q) {
         const int tk = warp * 4 + q;
         if (tk >= n_tok) break;
-        const float* l = lg + tk * (E + 1);
         int sel[kMaxTopK];
         float wsel[kMaxTopK];
-        if (policy == MOE_ROUTER_PHI_QUANTISED) {
-            // src/layer.cu:47-70: quantise, then two hysteresis scans.  The
-            // scan is order-dependent, so one lane runs it serially.
-            if (lane == 0) {
-                for (int s = 0; s < 2; ++s) {
-                    const int excluded = s == 0 ? -1 : sel[0];
-                    int best = -1;
-                    float best_value = -INFINITY;
-                    for (int e = 0; e < E; ++e) {
-                        if (e == excluded) continue;
-                        const float score = l[e];
-                        const float rounded =
-                            floorf(__fadd_rn(__fdiv_rn(fabsf(score), quantum), 0.5f)) * quantum;
-                        const float v = score < 0.0f ? -rounded : rounded;
-                        if (best < 0 || v > __fadd_rn(best_value, tie_eps)) {
-                            best = e;
-                            best_value = v;
-                        }
-                    }
-                    sel[s] = best;
-                    wsel[s] = 0.5f;
-                }
-            }
-        } else {
-            // Softmax top-k: k rounds of a warp-wide argmax over
-            // (key, index), larger key first, exact ties to the lower index.
-            unsigned taken = 0;  // bit i: expert lane + 32 i already chosen
-            for (int s = 0; s < k; ++s) {
-                float bk = -INFINITY;
-                int bi = INT_MAX;
-                for (int i = 0, e = lane; e < E; ++i, e += 32) {
-                    if (taken & (1u << i)) continue;
-                    const float kv = route_key(l[e]);
-                    if (bi == INT_MAX || kv > bk) { bk = kv; bi = e; }
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) {
-                    const float ok = __shfl_xor_sync(0xffffffffu, bk, off);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                    if (ok > bk || (ok == bk && oi < bi)) { bk = ok; bi = oi; }
-                }
-                if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-                sel[s] = bi;
-            }
-            if (lane == 0) {
-                const double m = (double)l[sel[0]];
-                double p[kMaxTopK], sum = 0.0;
-                for (int s = 0; s < k; ++s) { p[s] = exp((double)l[sel[s]] - m); sum += p[s]; }
-                for (int s = 0; s < k; ++s) wsel[s] = (float)(p[s] / sum);
-            }
-        }
+        select_experts(lg + tk * (E + 1), E, k, policy, quantum, tie_eps, lane, sel, wsel);
         if (lane == 0) {
             const int t = t0 + tk;
             for (int s = 0; s < k; ++s) {
@@ -423,10 +434,6 @@ __device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_o
                     pt.pad[1] = pt.pad[2] = 0;
                     ptiles[np + i] = pt;
                 }
-                for (int r = off + c; r < off + mc * kTileM; ++r) {
-                    row_token[r] = -1;
-                    row_weight[r] = 0.0f;
-                }
                 nm += mc;
                 np += qc;
             }
@@ -440,6 +447,14 @@ __device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_o
         }
     }
     __syncthreads();
+    if (write) {
+        // Padding rows of every expert block (token -1, weight 0), all threads.
+        for (int e = 0; e < E; ++e)
+            for (int r = s_off[e] + cnt[e] + threadIdx.x; r < s_off[e + 1]; r += blockDim.x) {
+                row_token[r] = -1;
+                row_weight[r] = 0.0f;
+            }
+    }
 }
 
 template <int kMode>  // 0: bf16 plane, 1: tf32 hi + lo planes, 2: fp32 as is (decode)
@@ -569,8 +584,247 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
     }
 }
 
+// ------------------------------------------------------------ small batches
+// A decode-sized batch (T <= 4) is routed and dispatched by one CTA in one
+// launch.  Warp 0's lane 0 streams K chunks of the router weights and of the
+// token rows (and the post-attention norm's weight and bias) into a ring of
+// shared-memory stages with 1-D bulk copies, one per row, each stage
+// completing on its `full` mbarrier.  Every (token, expert) pair has a thread
+// in warps 1.. that runs its logit's fused-multiply-add chain out of the ring
+// (with the norm applied in registers), so the chains -- 4.5 cycles per FMA,
+// d of them -- and not the loads set the kernel's length.  Warp t then
+// selects token t's experts, the whole CTA builds the single-block layout,
+// and the routed rows are written in the format the next stage reads.
+constexpr int kSmallMaxTokens = 4;
+constexpr int kSmallChainThreads = 256;
+constexpr int kSmallThreads = 32 + kSmallChainThreads;
+constexpr int kSmallMaxStages = 8;
+
+struct SmallGeom {
+    int kc;       // K columns per stage
+    int stages;
+    int rows;     // E router rows, T token rows, then norm weight and bias rows
+    int ld;       // padded row stride in floats: kc + 4 (LDS.128 of 8 rows conflict-free)
+};
+
+// Columns 4v .. 4v+3 of packed row `row` in the format of kMode.
+template <int kMode>
+__device__ __forceinline__ void store_row4(void* a_hi, void* a_lo, size_t row, int nv, int v,
+                                           float4 f) {
+    if constexpr (kMode == 0) {
+        __nv_bfloat162 lo2 = __floats2bfloat162_rn(f.x, f.y);
+        __nv_bfloat162 hi2 = __floats2bfloat162_rn(f.z, f.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&lo2);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi2);
+        reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
+    } else if constexpr (kMode == 2) {
+        reinterpret_cast<float4*>(a_hi)[row * nv + v] = f;
+    } else {
+        float4 h, l;
+        h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+        h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+        h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+        h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+        reinterpret_cast<float4*>(a_hi)[row * nv + v] = h;
+        reinterpret_cast<float4*>(a_lo)[row * nv + v] = l;
+    }
+}
+
+// kMode: 0 bf16 plane, 1 tf32 hi + lo planes, 2 fp32 as is.  KC: K columns
+// per stage (the chain loop is fully unrolled over it); kNorm: apply the
+// post-attention LayerNorm.
+template <int kMode, int KC, bool kNorm>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
+                    const float* __restrict__ bias, int T, int d, int E, int k, int policy,
+                    float quantum, float tie_eps, NormRef nr, SmallGeom gm,
+                    float* __restrict__ logits_out, int* __restrict__ idx_out,
+                    float* __restrict__ w_out, ScanOut so, int* __restrict__ row_token,
+                    float* __restrict__ row_weight, void* __restrict__ a_hi,
+                    void* __restrict__ a_lo, float* __restrict__ y, int* err) {
+    extern __shared__ __align__(16) float ring[];
+    __shared__ uint64_t full[kSmallMaxStages], empty[kSmallMaxStages];
+    __shared__ float lg[kSmallMaxTokens * (kMaxExperts + 1)];
+    __shared__ int hist[kMaxExperts];
+    __shared__ int s_base[kMaxExperts + 1];
+    __shared__ int s_sel[kSmallMaxTokens * kMaxTopK];
+    __shared__ float s_w[kSmallMaxTokens * kMaxTopK];
+    __shared__ int s_dest[kSmallMaxTokens * kMaxTopK];
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nchunks = d / KC;
+    const int chain_warps = (blockDim.x >> 5) - 1;
+    constexpr bool norm = kNorm;
+    const int rows_used = E + T + (norm ? 2 : 0);
+    if (tid == 0) {
+        for (int st = 0; st < gm.stages; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], chain_warps);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    for (int e = tid; e < E; e += blockDim.x) hist[e] = 0;
+    // The expert GEMMs / decode kernels add into y: start it at zero here
+    // rather than in a launch of its own.
+    for (int i = tid; i < T * d / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(y)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    __syncthreads();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ loads
+            const uint32_t bytes = (uint32_t)rows_used * KC * 4;
+            for (int g = 0; g < nchunks; ++g) {
+                const int st = g % gm.stages;
+                if (g >= gm.stages &&
+                    !mbar_wait(&empty[st], ((g / gm.stages) - 1) & 1, err, kDevErrTimeoutProducer)) {
+                    abort_flag = 1;
+                    break;
+                }
+                if (abort_flag) break;
+                mbar_arrive_expect_tx(&full[st], bytes);
+                float* sb = ring + (size_t)st * gm.rows * gm.ld;
+                const size_t c0 = (size_t)g * KC;
+                for (int r = 0; r < rows_used; ++r) {
+                    const float* src = r < E ? wg + (size_t)r * d + c0
+                                     : r < E + T ? x + (size_t)(r - E) * d + c0
+                                     : (r == E + T ? nr.w : nr.b) + c0;
+                    bulk_load(sb + (size_t)r * gm.ld, src, KC * 4, &full[st]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------- chains
+        const int ci = tid - 32;
+        const bool active = ci < T * E;
+        const int t = active ? ci / E : 0, e = active ? ci % E : 0;
+        float m = 0.0f, iv = 0.0f;
+        if (norm && active) {
+            m = nr.mean[t];
+            iv = nr.inv[t];
+        }
+        float acc = 0.0f;
+        for (int g = 0; g < nchunks; ++g) {
+            const int st = g % gm.stages;
+            if (!mbar_wait(&full[st], (g / gm.stages) & 1, err, kDevErrTimeoutMma)) {
+                abort_flag = 1;
+                break;
+            }
+            const float* sb = ring + (size_t)st * gm.rows * gm.ld;
+            const float* xr = sb + (size_t)(E + t) * gm.ld;
+            const float* wr = sb + (size_t)e * gm.ld;
+            const float* nw = sb + (size_t)(E + T) * gm.ld;
+            const float* nb = nw + gm.ld;
+            if (active) {
+                // Two register groups alternate: the next 16 columns' loads
+                // are issued before the current group's dependent FMAs.
+                float4 xa[4], wa[4], xb[4], wb[4];
+                auto load = [&](float4 (&xv)[4], float4 (&wv)[4], int kk) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float4 xq = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
+                        if constexpr (kNorm)
+                            xq = layer_norm_out4(xq, m, iv,
+                                                 *reinterpret_cast<const float4*>(nw + kk + 4 * q),
+                                                 *reinterpret_cast<const float4*>(nb + kk + 4 * q));
+                        xv[q] = xq;
+                        wv[q] = *reinterpret_cast<const float4*>(wr + kk + 4 * q);
+                    }
+                };
+                auto chain = [&](const float4 (&xv)[4], const float4 (&wv)[4]) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        acc = __fmaf_rn(xv[q].x, wv[q].x, acc);
+                        acc = __fmaf_rn(xv[q].y, wv[q].y, acc);
+                        acc = __fmaf_rn(xv[q].z, wv[q].z, acc);
+                        acc = __fmaf_rn(xv[q].w, wv[q].w, acc);
+                    }
+                };
+                load(xa, wa, 0);
+#pragma unroll
+                for (int kk = 0; kk < KC; kk += 32) {
+                    load(xb, wb, kk + 16);
+                    chain(xa, wa);
+                    if (kk + 32 < KC) load(xa, wa, kk + 32);
+                    chain(xb, wb);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+        if (active) {
+            float v = acc;
+            if (bias) v = __fadd_rn(v, bias[e]);
+            lg[t * (E + 1) + e] = v;
+            if (logits_out) logits_out[(size_t)t * E + e] = v;
+        }
+    }
+    __syncthreads();
+    if (abort_flag) return;   // err is set; outputs are left as they were
+
+    // ---------------------------------------------------- selection: warp t, token t
+    if (warp < T) {
+        const int t = warp;
+        int sel[kMaxTopK];
+        float wsel[kMaxTopK];
+        select_experts(lg + t * (E + 1), E, k, policy, quantum, tie_eps, lane, sel, wsel);
+        if (lane == 0) {
+            for (int s2 = 0; s2 < k; ++s2) {
+                idx_out[(size_t)t * k + s2] = sel[s2];
+                w_out[(size_t)t * k + s2] = wsel[s2];
+                s_sel[t * k + s2] = sel[s2];
+                s_w[t * k + s2] = wsel[s2];
+                atomicAdd(&hist[sel[s2]], 1);
+            }
+        }
+    }
+    __syncthreads();
+    single_block_layout(hist, E, s_base, true, so.counts, so.eoff, so.mtiles, so.num_mtiles,
+                        so.ptiles, so.num_ptiles, row_token, row_weight);
+    // Stable placement: within an expert, tokens in ascending order.
+    if (tid < T * k) {
+        const int t = tid / k, e = s_sel[tid];
+        int rank = 0;
+        for (int t2 = 0; t2 < t; ++t2)
+            for (int s2 = 0; s2 < k; ++s2) rank += s_sel[t2 * k + s2] == e;
+        const int pos = s_base[e] + rank;
+        s_dest[tid] = pos;
+        row_token[pos] = t;
+        row_weight[pos] = s_w[tid];
+    }
+    __syncthreads();
+    // The routed rows, normalised if the norm is active, in the next stage's
+    // format: each token row is read once (16 loads in flight per thread, so
+    // a batch takes about one round trip) and written to its k packed rows.
+    const int nv = d / 4;
+    constexpr int kU = 16;
+    for (int i0 = tid; i0 < T * nv; i0 += kU * blockDim.x) {
+        float4 fv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int i = i0 + u * blockDim.x;
+            if (i < T * nv) {
+                fv[u] = reinterpret_cast<const float4*>(x + (size_t)(i / nv) * d)[i % nv];
+                if (norm) fv[u] = nr.apply4(fv[u], i / nv, i % nv);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int i = i0 + u * blockDim.x;
+            if (i >= T * nv) break;
+            const int t = i / nv, v = i % nv;
+            for (int s2 = 0; s2 < k; ++s2)
+                store_row4<kMode>(a_hi, a_lo, (size_t)s_dest[t * k + s2], nv, v, fv[u]);
+        }
+    }
+}
+
 // T fits one router block: the permute kernel does the scan as well.
 bool single_block(int T) { return T <= kRouteTokens; }
+
 
 // Token blocks x column splits: enough CTAs (about 4 per SM) to keep tens of
 // MB of row loads in flight.
@@ -628,6 +882,69 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
     if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
     if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
     return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
+}
+
+bool route_small_geometry(const Layer& L, int T, bool norm, int* kc_out, int* stages_out) {
+    if (T < 1 || T > kSmallMaxTokens || T * L.E_route > kSmallChainThreads || L.E != L.E_route)
+        return false;
+    const int rows = L.E_route + T + (norm ? 2 : 0);
+    for (int kc : {512, 256, 128, 64}) {
+        if (L.d % kc) continue;
+        const size_t stage = (size_t)rows * (kc + 4) * 4;
+        const int stages = (int)std::min<size_t>(kSmallMaxStages, (190u << 10) / stage);
+        if (stages >= 3) {
+            *kc_out = kc;
+            *stages_out = stages;
+            return true;
+        }
+    }
+    return false;
+}
+
+cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
+                               bool decode, float* y, cudaStream_t s) {
+    const Workspace& W = L.ws;
+    const bool norm = nr.mean != nullptr;
+    SmallGeom gm;
+    if (!route_small_geometry(L, T, norm, &gm.kc, &gm.stages)) return cudaErrorInvalidValue;
+    gm.rows = L.E_route + T + (norm ? 2 : 0);
+    gm.ld = gm.kc + 4;
+    const size_t smem = (size_t)gm.stages * gm.rows * gm.ld * 4;
+    ScanOut so;
+    so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
+    so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
+    // All chain warps are launched whatever T x E is: the tail (layout and
+    // row copies) uses every thread.
+    const int threads = kSmallThreads;
+    // Row format: the decode kernels read fp32 (FP32) or bf16 (BF16) rows,
+    // the grouped GEMMs bf16 or tf32 hi + lo.
+    const int mode = three_pass(L) ? (decode ? 2 : 1) : 0;
+    auto launch = [&](auto kern) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        kern<<<1, threads, smem, s>>>(x, L.wg, L.bias, T, L.d, L.E_route, L.k, L.cfg.router_policy,
+                                      L.cfg.router_quantum, L.cfg.router_tie_eps, nr, gm, W.logits,
+                                      W.idx, W.wts, so, W.row_token, W.row_weight, W.a_hi, W.a_lo,
+                                      y, W.dev_err);
+        return cudaGetLastError();
+    };
+    auto by_kc = [&](auto mode_c, auto norm_c) {
+        constexpr int M = decltype(mode_c)::value;
+        constexpr bool N = decltype(norm_c)::value;
+        if (gm.kc == 512) return launch(router_small_kernel<M, 512, N>);
+        if (gm.kc == 256) return launch(router_small_kernel<M, 256, N>);
+        if (gm.kc == 128) return launch(router_small_kernel<M, 128, N>);
+        return launch(router_small_kernel<M, 64, N>);
+    };
+    using T0 = std::integral_constant<int, 0>;
+    using T1 = std::integral_constant<int, 1>;
+    using T2 = std::integral_constant<int, 2>;
+    using NF = std::false_type;
+    using NT = std::true_type;
+    if (mode == 0) return norm ? by_kc(T0{}, NT{}) : by_kc(T0{}, NF{});
+    if (mode == 1) return norm ? by_kc(T1{}, NT{}) : by_kc(T1{}, NF{});
+    return norm ? by_kc(T2{}, NT{}) : by_kc(T2{}, NF{});
 }
 
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s) {

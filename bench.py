@@ -419,7 +419,21 @@ def main():
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
-    layer.profile(True)
+    # Timed passes run with the stage timers off (their events would sit
+    # between the kernels and keep dependent launches from overlapping); a
+    # separate short profiled pass gives the per-stage breakdown.
+    layer.profile(False)
+
+    def profiled_stages(fn, n):
+        layer.profile(True)
+        st_p = np.zeros(len(pkg.PROFILE_STAGES))
+        for _ in range(n):
+            fn()
+            st_p += layer.stage_ms()
+            flush.zero_()
+        torch.cuda.synchronize()
+        layer.profile(False)
+        return st_p / n
 
     def step():
         layer.forward_device(x.data_ptr(), y.data_ptr(), T, sp)
@@ -438,17 +452,16 @@ def main():
         dist.barrier()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    stage_sum = np.zeros(len(pkg.PROFILE_STAGES))
     for i in range(args.steps):
         ev[i][0].record(stream)
         step()
         ev[i][1].record(stream)
-        stage_sum += layer.stage_ms()
         flush.zero_()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    stages = profiled_stages(step, max(3, args.steps // 5))
 
     # ---- decode: the same layer at T in DECODE_T, HBM GB/s
     decode = {}
@@ -463,17 +476,17 @@ def main():
                 flush.zero_()
             torch.cuda.synchronize()
             tot, n = 0.0, max(5, args.steps)
-            st_d = np.zeros(len(pkg.PROFILE_STAGES))
             for _ in range(n):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
                 layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)
                 b.record(stream)
-                st_d += layer.stage_ms()
                 flush.zero_()
                 b.synchronize()
                 tot += a.elapsed_time(b)
             ms_d = tot / n
+            st_d = profiled_stages(
+                lambda: layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp), 5)
             active = int((layer.expert_counts() > 0).sum())
             wbytes = 2 if args.precision == "bf16" else 4
             alg = active * 3 * d * ff * wbytes + E * d * 4 + 2 * td * d * 4
@@ -482,7 +495,7 @@ def main():
             decode[str(td)] = {"ms": ms_d, "tokens_per_s": td / (ms_d / 1e3),
                                "experts_streamed": active, "algorithmic_bytes": alg,
                                "hbm_gbs": gbs, "frac_of_hbm": gbs / hbm, "path": path,
-                               "stages_ms": {nm: float(v) / n
+                               "stages_ms": {nm: float(v)
                                              for nm, v in zip(pkg.PROFILE_STAGES, st_d)}}
 
     # ---- the decoder layer's MoE half: y = x + MoE(layer_norm(x)), the norm
@@ -500,17 +513,16 @@ def main():
                 fn()
                 flush.zero_()
             torch.cuda.synchronize()
-            tot, st_b = 0.0, np.zeros(len(pkg.PROFILE_STAGES))
+            tot = 0.0
             for _ in range(n):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
                 fn()
                 b.record(stream)
-                st_b += layer.stage_ms()
                 flush.zero_()
                 b.synchronize()
                 tot += a.elapsed_time(b)
-            return tot / n, st_b / n
+            return tot / n, profiled_stages(fn, 3)
 
         nb_steps = max(5, args.steps // 2)
         for tb in sorted({T, 1}):
@@ -557,7 +569,7 @@ def main():
 
     if rank == 0:
         hbm, bf16_peak, bf16_sust, src = _peaks()
-        st = stage_sum / args.steps
+        st = stages
         gu_ms, dn_ms = st[3], st[4]
         gu_flops = 4.0 * T * k * d * ff
         dn_flops = 2.0 * T * k * d * ff

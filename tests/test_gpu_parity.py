@@ -194,6 +194,31 @@ def test_decode_path_matches_oracle(T, precision, orc):
         assert ref_elementwise_failures(y, y_ref) == 0
 
 
+@pytest.mark.parametrize("name,tag,policy", CASE_POL)
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_small_batch_route_and_dispatch(name, tag, policy, T, precision):
+    """Batches of at most 4 tokens are routed and dispatched by one
+    single-CTA kernel: its routing (read back through the dispatch layout)
+    equals the golden indices of the same tokens, bit for bit, and y is
+    within the precision's bound."""
+    pkg = load_pkg()
+    layer, x = case_inputs(pkg, name)
+    g = np.load(GOLDEN_DIR / f"{name}.npz")
+    k = CASES[name]["k"]
+    idx = g[f"{tag}_idx"][:T]
+    for dmt in (64, 0):                       # rows for the decode kernels, then the GEMMs
+        with pkg.MoeLayer(layer, top_k=k, policy=policy, precision=precision,
+                          decode_max_tokens=dmt) as m:
+            y = m.forward_host(x[:T])
+            counts = m.expert_counts()
+            tok, wt, eoff = m.dispatch_layout(rows_cap=128 * (layer.E + 1))
+        assert np.array_equal(counts, np.bincount(idx.ravel(), minlength=layer.E))
+        for e in range(layer.E):
+            assert np.array_equal(tok[eoff[e]:eoff[e] + counts[e]], np.nonzero((idx == e).any(1))[0])
+        assert rel_l2(y, g[f"{tag}_y"][:T]) <= TOL[precision]
+
+
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
 @pytest.mark.parametrize("T", [1, 2, 5, 8, 16, 32])
 def test_grouped_gemm_path_at_decode_sizes(T, precision, orc):
