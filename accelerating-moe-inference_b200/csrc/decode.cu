@@ -77,13 +77,6 @@ struct Vec<__nv_bfloat16> {
     }
 };
 
-// Programmatic dependent launch: these kernels are launched while their
-// predecessor on the stream may still be running, and wait here before
-// reading anything it wrote (a no-op for an ordinary launch).
-__device__ __forceinline__ void wait_predecessor() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -172,7 +165,7 @@ decode_gateup_kernel(const AT* __restrict__ a_rows, const WT* __restrict__ w13, 
                      int E, const int* __restrict__ counts, const int* __restrict__ eoff,
                      float* __restrict__ h) {
     __shared__ Active A;
-    wait_predecessor();
+    wait_predecessor_grid();
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const long long W = (long long)gridDim.x * kDecWarps;
@@ -227,7 +220,7 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
                    const int* __restrict__ row_token, const float* __restrict__ row_weight,
                    float* __restrict__ y) {
     __shared__ Active A;
-    wait_predecessor();
+    wait_predecessor_grid();
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const int nq = (d + 3) / 4;                    // column quads per expert

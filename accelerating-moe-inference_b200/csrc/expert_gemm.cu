@@ -265,6 +265,8 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything below reads what the previous kernel on the stream wrote.
+    wait_predecessor_grid();
 
     const int m_tiles = *p.num_mtiles;
     // Work items: tiles x K splits, the split fastest, so the splits of one
@@ -487,6 +489,8 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
     cluster_sync();                     // barriers of both CTAs initialised
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Everything below reads what the previous kernel on the stream wrote.
+    wait_predecessor_grid();
 
     const int p_tiles = *p.num_mtiles;  // pair tiles (num_ptiles)
     const int total = p_tiles * p.n_tiles;
@@ -631,7 +635,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
 template <bool kTf32x3, int kEpi>
 cudaError_t launch_pair(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                         const CUtensorMap& b_lo, const GemmParams& p, int clusters,
-                        cudaStream_t s) {
+                        bool pdl, cudaStream_t s) {
     using C = PairCfg<kTf32x3>;
     auto kern = expert_gemm_pair_kernel<kTf32x3, kEpi>;
     cudaError_t err =
@@ -642,13 +646,15 @@ cudaError_t launch_pair(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const 
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, a_hi, a_lo, b_hi, b_lo, p);
 }
 
@@ -661,8 +667,19 @@ cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMa
     cudaError_t err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (err != cudaSuccess) return err;
-    kern<<<grid, kThreads, C::kSmemBytes, s>>>(a_hi, a_lo, b_hi, b_lo, p);
-    return cudaGetLastError();
+    // Dependent launch: the kernel waits for its predecessor itself, after
+    // its prologue (barriers, TMEM); the stage timers turn it off.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L.profile ? 0 : 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a_hi, a_lo, b_hi, b_lo, p);
 }
 
 }  // namespace
@@ -720,22 +737,22 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         if (!down) {
             if (tf)
                 return launch_pair<true, kEpiGateUp>(W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi2, L.tm_w13_lo2,
-                                                     gp, clusters, s);
+                                                     gp, clusters, !L.profile, s);
             return launch_pair<false, kEpiGateUp>(W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi2, L.tm_w13_hi2,
-                                                  gp, clusters, s);
+                                                  gp, clusters, !L.profile, s);
         }
         if (mode == 2) {
             if (tf)
                 return launch_pair<true, kEpiDownStore>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2,
-                                                        L.tm_w2_lo2, gp, clusters, s);
+                                                        L.tm_w2_lo2, gp, clusters, !L.profile, s);
             return launch_pair<false, kEpiDownStore>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2,
-                                                     gp, clusters, s);
+                                                     gp, clusters, !L.profile, s);
         }
         if (tf)
             return launch_pair<true, kEpiDown>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2, L.tm_w2_lo2, gp,
-                                               clusters, s);
+                                               clusters, !L.profile, s);
         return launch_pair<false, kEpiDown>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2, gp,
-                                            clusters, s);
+                                            clusters, !L.profile, s);
     }
     // Decode-sized batches leave the down GEMM with few tiles (d / 256 per
     // routed expert), too few to keep every SM streaming weights: split K

@@ -36,6 +36,13 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
     return t;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation waits here for its predecessor on the stream to complete and
+// its writes to be visible (a no-op for an ordinary launch).
+__device__ __forceinline__ void wait_predecessor_grid() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

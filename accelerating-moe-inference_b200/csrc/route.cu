@@ -655,6 +655,9 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nchunks = d / KC;
     const int chain_warps = (blockDim.x >> 5) - 1;
+    // Dependent launch: nothing the previous kernel touches (x, y, the
+    // workspace) is read or written before it has completed.
+    wait_predecessor_grid();
     constexpr bool norm = kNorm;
     const int rows_used = E + T + (norm ? 2 : 0);
     if (tid == 0) {
@@ -923,11 +926,20 @@ cudaError_t launch_route_small(const Layer& L, const float* x, int T, const Norm
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
         if (e != cudaSuccess) return e;
-        kern<<<1, threads, smem, s>>>(x, L.wg, L.bias, T, L.d, L.E_route, L.k, L.cfg.router_policy,
-                                      L.cfg.router_quantum, L.cfg.router_tie_eps, nr, gm, W.logits,
-                                      W.idx, W.wts, so, W.row_token, W.row_weight, W.a_hi, W.a_lo,
-                                      y, W.dev_err);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1);
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = L.profile ? 0 : 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, kern, x, L.wg, (const float*)L.bias, T, L.d, L.E_route,
+                                  L.k, L.cfg.router_policy, L.cfg.router_quantum,
+                                  L.cfg.router_tie_eps, nr, gm, W.logits, W.idx, W.wts, so,
+                                  W.row_token, W.row_weight, W.a_hi, W.a_lo, y, W.dev_err);
     };
     auto by_kc = [&](auto mode_c, auto norm_c) {
         constexpr int M = decltype(mode_c)::value;
