@@ -47,7 +47,8 @@ EXPORTED_SYMBOLS = (
     "moe_block_forward_host", "moe_layer_norm_device",
     "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
 )
-PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm")
+PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm",
+                  "ep_exchange_in", "ep_exchange_out", "ep_combine")
 
 
 class MoeError(RuntimeError):

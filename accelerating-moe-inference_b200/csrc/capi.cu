@@ -228,7 +228,7 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
     Workspace& W = L.ws;
     L.last_stream = s;
     L.last_T = T;
-    for (bool& r : L.prof_ran) r = false;
+    L.prof_n = 0;
     NormRef nr;
     if (block) {
         nr.mean = W.row_mean;
@@ -265,7 +265,7 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
         MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/true));
     }
     if (block) MOE_CUDA(launch_residual_add(L, y, x, (size_t)T * L.d, s));
-    prof_mark(L, kProfileStages, s);
+    prof_mark(L, kProfEnd, s);
     return MOE_OK;
 }
 
@@ -663,13 +663,14 @@ int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n) {
     DeviceGuard guard(h->L.cfg.device);
     Layer& L = h->L;
     if (!L.prof_ev[0]) return fail(MOE_ERR_INVALID, "profiling was never enabled");
-    int last = -1;
-    for (int i = 0; i < kProfileStages; ++i)
-        if (L.prof_ran[i]) last = i;
-    if (last >= 0) MOE_CUDA(cudaEventSynchronize(L.prof_ev[last + 1]));
-    for (int i = 0; i < n && i < kProfileStages; ++i) {
-        stage_ms[i] = 0.0f;
-        if (L.prof_ran[i]) MOE_CUDA(cudaEventElapsedTime(&stage_ms[i], L.prof_ev[i], L.prof_ev[i + 1]));
+    for (int i = 0; i < n && i < kProfileStages; ++i) stage_ms[i] = 0.0f;
+    if (L.prof_n > 0) MOE_CUDA(cudaEventSynchronize(L.prof_ev[L.prof_n - 1]));
+    for (int j = 0; j + 1 < L.prof_n; ++j) {
+        const int st = L.prof_stage[j];
+        if (st < 0 || st >= n || st >= kProfileStages) continue;
+        float ms = 0.0f;
+        MOE_CUDA(cudaEventElapsedTime(&ms, L.prof_ev[j], L.prof_ev[j + 1]));
+        stage_ms[st] += ms;
     }
     return kProfileStages;
 }

@@ -260,15 +260,19 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     };
     cudaError_t ce;
     ncclResult_t nr;
+    L.prof_n = 0;
 
     // 1-2: route and pack locally (compact, expert-sorted).
+    prof_mark(L, 0, s);
     if (T > 0) {
         if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s)) != cudaSuccess)
             return cuda_err(ce, "router");
+        prof_mark(L, 1, s);
         if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
                                       W.counts, S.send_eoff, nullptr, nullptr, nullptr, nullptr,
                                       nullptr, nullptr, s)) != cudaSuccess)
             return cuda_err(ce, "dispatch scan");
+        prof_mark(L, 2, s);
         if ((ce = launch_dispatch_permute_to(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w,
                                              S.send_rows, s)) != cudaSuccess)
             return cuda_err(ce, "dispatch permute");
@@ -277,6 +281,7 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
             return cuda_err(ce, "counts");
     }
     // 3: counts exchange.
+    prof_mark(L, 5, s);
     if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
     for (int j = 0; j < G; ++j) {
         g_nccl.Send(W.counts + j * El, El, ncclInt32, j, S.comm, s);
@@ -308,6 +313,7 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     }
     if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "dispatch exchange");
     // 5-6: arrange and run the local experts.
+    prof_mark(L, 2, s);
     if (R > 0) {
         if ((ce = launch_scan_generic(S.cnt_scan, G, El, kTileM, W.counts, W.eoff, W.mtiles,
                                       W.num_mtiles, W.ptiles, W.num_ptiles, W.row_token,
@@ -324,12 +330,15 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
                                                              S.cnt_scan, W.eoff, W.row_token,
                                                              W.row_weight, W.a_hi, W.a_lo);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
+        prof_mark(L, 3, s);
         if ((ce = launch_expert_gemm_rows(L, R, nullptr, s, 0)) != cudaSuccess)
             return cuda_err(ce, "gate/up GEMM");
+        prof_mark(L, 4, s);
         if ((ce = launch_expert_gemm_rows(L, R, S.ret_send, s, 2)) != cudaSuccess)
             return cuda_err(ce, "down GEMM");
     }
     // 7: return exchange (same element type as the dispatch).
+    prof_mark(L, 6, s);
     if ((nr = g_nccl.GroupStart()) != ncclSuccess) return nccl_fail(nr, "ncclGroupStart");
     for (int j = 0; j < G; ++j) {
         if (recv_rows[j])
@@ -341,6 +350,7 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     }
     if ((nr = g_nccl.GroupEnd()) != ncclSuccess) return nccl_fail(nr, "combine exchange");
     // 8: weighted combine into y.
+    prof_mark(L, 7, s);
     if (T > 0) {
         if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * d, s)) != cudaSuccess)
             return cuda_err(ce, "y memset");
@@ -353,6 +363,7 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
                                                                     S.send_w, y);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
+    prof_mark(L, kProfEnd, s);
     return MOE_OK;
 }
 

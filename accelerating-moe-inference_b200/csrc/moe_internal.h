@@ -38,7 +38,9 @@ constexpr int kTileN = 256;        // GEMM tile columns
 constexpr int kFfBlock = 128;      // d_ff padding granule (half of kTileN)
 constexpr int kMaxExperts = 256;
 constexpr int kMaxTopK = 8;
-constexpr int kProfileStages = 5;
+constexpr int kProfileStages = 8;
+constexpr int kProfileMarks = 24;  // stage boundaries one forward may record
+constexpr int kProfEnd = -1;       // the mark closing the last stage
 
 // One 128-row slice of an expert's packed block.  m-tiles are listed expert
 // by expert; mstart / mcount locate the expert's own run in that list.  The
@@ -149,17 +151,21 @@ struct Layer {
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;
     int last_T = 0;
-    // Stage timers (moe_profile_enable): event i marks the start of stage i,
-    // event kProfileStages the end of the last one.
+    // Stage timers (moe_profile_enable): the marks of the last forward, in
+    // stream order; mark j's event starts stage prof_stage[j] (kProfEnd
+    // closes the last), which lasts until mark j + 1.  A stage may recur; its
+    // intervals add up.
     bool profile = false;
-    cudaEvent_t prof_ev[kProfileStages + 1] = {};
-    bool prof_ran[kProfileStages] = {};
+    cudaEvent_t prof_ev[kProfileMarks] = {};
+    int prof_stage[kProfileMarks] = {};
+    int prof_n = 0;
 };
 
-// Record the boundary before stage `i` (no-op unless profiling).
+// Start stage `i` (kProfEnd: close the last one); no-op unless profiling.
 inline void prof_mark(Layer& L, int i, cudaStream_t s) {
-    if (L.profile) cudaEventRecord(L.prof_ev[i], s);
-    if (L.profile && i < kProfileStages) L.prof_ran[i] = true;
+    if (!L.profile || L.prof_n >= kProfileMarks) return;
+    cudaEventRecord(L.prof_ev[L.prof_n], s);
+    L.prof_stage[L.prof_n++] = i;
 }
 
 // ------------------------------------------------------------ launchers

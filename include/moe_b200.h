@@ -242,13 +242,18 @@ int moe_dispatch_layout(MoeHandle* h, int32_t* row_token, float* row_weight, int
 /* Per-stage device timers, the counterpart of the reference's APS_PROFILE
  * stage timers (src/model.cu:1584-1622, 2052-2058).  When enabled, forward
  * records a CUDA event on its stream at each stage boundary (no host
- * synchronisation).  moe_profile_read synchronises on the last event and
+ * synchronisation; dependent launches are turned off so the events sit
+ * between the kernels).  moe_profile_read synchronises on the last event and
  * writes the milliseconds of each stage of the last forward:
- *   [0] router  [1] dispatch scan  [2] dispatch permute
+ *   [0] router (batches of <= 4 tokens: router, layout and row packing)
+ *   [1] dispatch scan  [2] dispatch permute (expert parallel: also the
+ *       arrival scan and arrangement)
  *   [3] gate/up grouped GEMM (decode path: decode gate/up kernel)
  *   [4] down grouped GEMM (decode path: decode down kernel)
- * Stages a forward did not run read 0.  Returns the number of stages (5). */
-#define MOE_PROFILE_STAGES 5
+ *   [5] expert parallel: counts exchange, host plan, payload exchange
+ *   [6] expert parallel: return exchange  [7] expert parallel: combine
+ * Stages a forward did not run read 0.  Returns the number of stages (8). */
+#define MOE_PROFILE_STAGES 8
 int moe_profile_enable(MoeHandle* h, int enable);
 int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n);
 

@@ -312,3 +312,28 @@ def test_bounded_wait_times_out_and_device_stays_usable():
     g = np.load(GOLDEN_DIR / "c1.npz")
     with pkg.MoeLayer(layer, top_k=2, policy=0) as m:
         assert rel_l2(m.forward_host(x), g["phi_y"]) <= 1e-3
+
+
+@pytest.mark.parametrize("T", [1, 300])
+def test_stage_timers_cover_the_forward(T):
+    """moe_profile_*: every stage a forward runs reads > 0, the others 0, and
+    together they account for the forward's device time."""
+    import torch
+    pkg = load_pkg()
+    layer = pkg.synthetic_layer(26, 512, 768, 8)
+    x = torch.from_numpy(pkg.synthetic_tokens(26, T, 512)).cuda()
+    y = torch.empty_like(x)
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=1) as m:
+        m.profile(True)
+        s = torch.cuda.current_stream()
+        m.forward_device(x.data_ptr(), y.data_ptr(), T, s.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        m.forward_device(x.data_ptr(), y.data_ptr(), T, s.cuda_stream)
+        b.record(s)
+        b.synchronize()
+        st = dict(zip(pkg.PROFILE_STAGES, m.stage_ms()))
+    assert all(v >= 0 for v in st.values())
+    assert st["router"] > 0 and st["gateup_gemm"] > 0 and st["down_gemm"] > 0
+    assert st["ep_exchange_in"] == st["ep_exchange_out"] == st["ep_combine"] == 0
+    assert sum(st.values()) <= a.elapsed_time(b) * 1.05 + 0.01
