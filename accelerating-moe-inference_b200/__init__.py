@@ -30,6 +30,9 @@ ROUTER_PHI_QUANTISED = 0
 ROUTER_SOFTMAX_TOPK = 1
 PREC_FP32 = 0
 PREC_BF16 = 1
+# MoeConfig.ep_transport (expert parallelism): fused NVLink peer stores, or NCCL send/recv.
+EP_TRANSPORT_P2P = 0
+EP_TRANSPORT_NCCL = 1
 # MoeConfig.decode_max_tokens: the measured decode-kernel threshold of the precision.
 DECODE_AUTO = -1
 GEMM_AUTO = 0
@@ -64,7 +67,7 @@ class MoeConfig(ctypes.Structure):
                 ("router_quantum", ctypes.c_float), ("router_tie_eps", ctypes.c_float),
                 ("decode_max_tokens", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("max_tokens", ctypes.c_int32), ("gemm_variant", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 4)]
+                ("ep_transport", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
 
 
 _f32p = ctypes.POINTER(ctypes.c_float)

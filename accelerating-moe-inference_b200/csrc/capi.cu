@@ -202,6 +202,8 @@ int validate_config(const MoeConfig& c) {
     if (c.max_tokens < 0) return fail(MOE_ERR_INVALID, "max_tokens < 0");
     if (c.gemm_variant < MOE_GEMM_AUTO || c.gemm_variant > MOE_GEMM_CTA_PAIR)
         return fail(MOE_ERR_INVALID, "unknown gemm_variant");
+    if (c.ep_transport != MOE_EP_TRANSPORT_P2P && c.ep_transport != MOE_EP_TRANSPORT_NCCL)
+        return fail(MOE_ERR_INVALID, "unknown ep_transport");
     return MOE_OK;
 }
 

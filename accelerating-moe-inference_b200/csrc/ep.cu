@@ -1,9 +1,33 @@
 // Expert parallelism: one process and one B200 per rank, experts split
-// contiguously across the ranks, NCCL point-to-point over NVLink for the
-// dispatch and combine exchanges.  The reference has no multi-GPU path; this
+// contiguously across the ranks.  The reference has no multi-GPU path; this
 // is the layer's scale-out.
 //
-// Forward on rank r with T local tokens (every rank runs it collectively):
+// Fused transport (the default, MOE_EP_TRANSPORT_P2P): every rank allocates a
+// receive buffer and a return buffer with one fixed segment per source rank
+// ([G][cap] rows, cap = the most rows one source can send: max_tokens x
+// min(top_k, experts per rank)) plus count and flag words, and maps every
+// other rank's through CUDA IPC (handles exchanged once, with an NCCL
+// all-gather).  Then, with no host synchronisation and no NCCL call:
+//   1. router; compact dispatch scan (granule 1);
+//   2. the dispatch permute stores each routed row straight into the owning
+//      rank's receive buffer over NVLink (at this rank's segment, in compact
+//      order) and records where it went;
+//   3. a signal kernel writes this rank's per-expert counts into each rank's
+//      count words and raises its dispatch flag there (system-scope fence,
+//      release store of the step's epoch);
+//   4. a wait kernel spins (bounded) until every source's flag shows the
+//      epoch; the arrival scan, arrangement and both GEMMs follow, the down
+//      GEMM's epilogue storing each result straight into the source rank's
+//      return buffer;
+//   5. signal and wait again for the returns; the combine reads the return
+//      buffer (local memory) and adds weight x row into y.
+// Buffers are never rewritten before their reader is done, by the data
+// dependencies alone: a rank pushes step e + 1 only after its step-e combine,
+// which needed every rank's step-e results, which those ranks computed after
+// arranging (copying out) their step-e arrivals.
+//
+// NCCL transport (MOE_EP_TRANSPORT_NCCL), the baseline; forward on rank r
+// with T local tokens (every rank runs it collectively):
 //   1. router over all E experts (router weights are replicated);
 //   2. compact dispatch (granule 1): rows sorted by global expert, then token,
 //      so the rows for rank j are one contiguous run; fp32 rows in FP32
@@ -25,6 +49,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -47,6 +72,8 @@ struct NcclApi {
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     bool ok = false;
 };
@@ -78,6 +105,7 @@ bool load_nccl(std::string* err) {
     MOE_SYM(Recv, "ncclRecv")
     MOE_SYM(GroupStart, "ncclGroupStart")
     MOE_SYM(GroupEnd, "ncclGroupEnd")
+    MOE_SYM(AllGather, "ncclAllGather")
     MOE_SYM(GetErrorString, "ncclGetErrorString")
 #undef MOE_SYM
     g_nccl.ok = true;
@@ -108,15 +136,39 @@ struct EpState {
     int* cnt_scan = nullptr;    // [G][E_local] device (scan in place)
     int* h_counts = nullptr;    // pinned [E]
     int* h_cnt_recv = nullptr;  // pinned [G][E_local]
+    // Fused (P2P) transport.
+    int transport = MOE_EP_TRANSPORT_P2P;
+    int cap_src = 0;             // rows of one source segment
+    uint32_t epoch = 0;          // forward steps run
+    void* p2p_recv = nullptr;    // [G][cap_src] rows, written by the sources
+    void* p2p_ret = nullptr;     // [G][cap_src] result rows, written by the expert ranks
+    int* p2p_cnt = nullptr;      // [G][E_local], written by the sources
+    unsigned* p2p_flag = nullptr;  // [2][G]: dispatch flag of source s, return flag of rank j
+    int* send_slot = nullptr;    // [T*k] compact row -> destination * cap_src + row
+    void** d_peer_recv = nullptr;  // [G] every rank's p2p_recv (own included), device array
+    void** d_peer_ret = nullptr;
+    int** d_peer_cnt = nullptr;
+    unsigned** d_peer_flag = nullptr;
+    std::vector<void*> ipc_opened;  // mappings of the other ranks' buffers
 };
 
 namespace {
 
 void ep_free_buffers(EpState& S) {
+    for (void* p : S.ipc_opened) cudaIpcCloseMemHandle(p);
+    S.ipc_opened.clear();
     for (void* p : {S.send_rows, (void*)S.send_tok, (void*)S.send_w, (void*)S.send_eoff,
                     S.recv_rows, (void*)S.ret_send, (void*)S.ret_recv, (void*)S.cnt_recv,
-                    (void*)S.cnt_scan})
+                    (void*)S.cnt_scan, S.p2p_recv, S.p2p_ret, (void*)S.p2p_cnt,
+                    (void*)S.p2p_flag, (void*)S.send_slot, (void*)S.d_peer_recv,
+                    (void*)S.d_peer_ret, (void*)S.d_peer_cnt, (void*)S.d_peer_flag})
         if (p) cudaFree(p);
+    S.p2p_recv = S.p2p_ret = nullptr;
+    S.p2p_cnt = S.send_slot = nullptr;
+    S.p2p_flag = nullptr;
+    S.d_peer_recv = S.d_peer_ret = nullptr;
+    S.d_peer_cnt = nullptr;
+    S.d_peer_flag = nullptr;
     if (S.h_counts) cudaFreeHost(S.h_counts);
     if (S.h_cnt_recv) cudaFreeHost(S.h_cnt_recv);
     S.send_rows = S.recv_rows = nullptr;
@@ -162,9 +214,15 @@ int ep_ensure(Layer& L, int T) {
 
 // One warp per received row: find its (source, local expert) run, place it in
 // the expert's GEMM block and convert it to the operand format.
+// cap_src > 0 (fused transport): source s's rows sit at rows
+// [s * cap_src, ...) of recv, and row_token gets the return slot
+// s * cap_src + q; else the sources' runs are contiguous and row_token gets
+// the arrival row.  rows is a bound: rows past the received total exit.
+// Received rows and counts were written by other GPUs: they are read through
+// L2 only.
 template <bool kTf32x3>
 __global__ void __launch_bounds__(256)
-ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
+ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El, int cap_src,
                   const int* __restrict__ cnt, const int* __restrict__ base,
                   const int* __restrict__ eoff, int* __restrict__ row_token,
                   float* __restrict__ row_weight, void* __restrict__ a_hi,
@@ -179,7 +237,7 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
             int r = 0;
             for (int e = 0; e < El; ++e) {
                 run_off[s * (El + 1) + e] = r;
-                r += cnt[s * El + e];
+                r += __ldcg(cnt + s * El + e);
             }
             run_off[s * (El + 1) + El] = r;
             off += r;
@@ -189,23 +247,24 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * 8 + warp;
-    if (i >= rows) return;
+    if (i >= rows || i >= src_off[G]) return;
     int s = 0;
     while (s + 1 < G && src_off[s + 1] <= i) ++s;
     const int q = i - src_off[s];
     int e = 0;
     while (e + 1 < El && run_off[s * (El + 1) + e + 1] <= q) ++e;
     const int prow = eoff[e] + base[s * El + e] + (q - run_off[s * (El + 1) + e]);
+    const size_t src_row = cap_src > 0 ? (size_t)s * cap_src + q : (size_t)i;
     if (lane == 0) {
-        row_token[prow] = i;
+        row_token[prow] = (int)src_row;
         row_weight[prow] = 1.0f;
     }
     if constexpr (kTf32x3) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + (size_t)i * d);
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + src_row * d);
         float4* hi = reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow * d);
         float4* lo = reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow * d);
         for (int v = lane; v < d / 4; v += 32) {
-            const float4 f = src[v];
+            const float4 f = __ldcg(src + v);
             float4 h, l;
             h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
             h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
@@ -215,30 +274,33 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
             lo[v] = l;
         }
     } else {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + (size_t)i * d);
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + src_row * d);
         uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow * d);
-        for (int v = lane; v < d / 8; v += 32) dst[v] = src[v];
+        for (int v = lane; v < d / 8; v += 32) dst[v] = __ldcg(src + v);
     }
 }
 
 // y[token] += weight * returned row, one compact row per warp.  Returned rows
-// are fp32 (FP32 precision) or bf16 (BF16 precision).
+// are fp32 (FP32 precision) or bf16 (BF16 precision); compact row j's is row
+// slot[j] of ret (fused transport: written by another GPU, read through L2
+// only), else row j.
 template <bool kF32>
 __global__ void __launch_bounds__(256)
 ep_combine_kernel(const void* __restrict__ ret, int rows, int d, const int* __restrict__ tok,
-                  const float* __restrict__ w, float* __restrict__ y) {
+                  const float* __restrict__ w, const int* __restrict__ slot, float* __restrict__ y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int j = blockIdx.x * 8 + warp;
     if (j >= rows) return;
     const float wt = w[j];
+    const size_t rj = slot ? (size_t)slot[j] : (size_t)j;
     float* dst = y + (size_t)tok[j] * d;
     for (int v = lane; v < d / 4; v += 32) {
         float4 r;
         if constexpr (kF32) {
-            r = reinterpret_cast<const float4*>(static_cast<const float*>(ret) + (size_t)j * d)[v];
+            r = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(ret) + rj * d) + v);
         } else {
-            const uint2 u = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(ret) +
-                                                          (size_t)j * d)[v];
+            const uint2 u = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(ret) +
+                                                                 rj * d) + v);
             r = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
                             __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
         }
@@ -247,7 +309,7 @@ ep_combine_kernel(const void* __restrict__ ret, int rows, int d, const int* __re
     }
 }
 
-int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     EpState& S = *L.ep;
     int rc = ep_ensure(L, T);
     if (rc) return rc;
@@ -322,11 +384,11 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
         const int grid = (R + 7) / 8;
         if (three_pass(L))
-            ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, S.cnt_recv,
+            ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, 0, S.cnt_recv,
                                                             S.cnt_scan, W.eoff, W.row_token,
                                                             W.row_weight, W.a_hi, W.a_lo);
         else
-            ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, S.cnt_recv,
+            ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, 0, S.cnt_recv,
                                                              S.cnt_scan, W.eoff, W.row_token,
                                                              W.row_weight, W.a_hi, W.a_lo);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
@@ -357,14 +419,264 @@ int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         const int rows = T * L.k;
         if (three_pass(L))
             ep_combine_kernel<true><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
-                                                                   S.send_w, y);
+                                                                   S.send_w, nullptr, y);
         else
             ep_combine_kernel<false><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
-                                                                    S.send_w, y);
+                                                                    S.send_w, nullptr, y);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
     prof_mark(L, kProfEnd, s);
     return MOE_OK;
+}
+
+// ------------------------------------------------------------ fused transport
+constexpr unsigned long long kPeerWaitNs = 5000000000ull;   // 5 s
+
+// Thread j: for rank j, copy this rank's counts for j's experts into j's
+// count words (dispatch only), then -- after a system-scope fence that orders
+// this step's earlier writes to j (the previous kernel's row stores
+// included) -- raise flag [which][this rank] in j's flag words to `epoch`.
+__global__ void ep_signal_kernel(int* const* peer_cnt, const int* __restrict__ counts,
+                                 unsigned* const* peer_flag, int G, int El, int rank, int which,
+                                 unsigned epoch) {
+    const int j = threadIdx.x;
+    if (j >= G) return;
+    if (peer_cnt)
+        for (int e = 0; e < El; ++e) peer_cnt[j][rank * El + e] = counts[j * El + e];
+    __threadfence_system();
+    st_release_sys(peer_flag[j] + which * G + rank, epoch);
+}
+
+// Wait until every rank's flag [which][s] shows `epoch` (bounded: on a
+// timeout the error flag is set).  Then copy the n count words the sources
+// wrote (read through L2) to cnt_a and cnt_b, each clamped to a segment's
+// capacity -- or zeros after a timeout, so a failed step moves no rows.
+__global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned epoch,
+                               const int* cnt_src, int* __restrict__ cnt_a, int* __restrict__ cnt_b,
+                               int n, int cap, int* err) {
+    __shared__ int timed_out;
+    if (threadIdx.x == 0) timed_out = 0;
+    __syncthreads();
+    const int sidx = threadIdx.x;
+    if (sidx < G) {
+        const unsigned* f = flag + which * G + sidx;
+        if (ld_acquire_sys(f) < epoch) {
+            const unsigned long long t0 = global_timer_ns();
+            while (ld_acquire_sys(f) < epoch) {
+                if (global_timer_ns() - t0 > kPeerWaitNs) {
+                    atomicOr(err, kDevErrTimeoutPeer);
+                    timed_out = 1;
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int c = timed_out ? 0 : min(max(__ldcg(cnt_src + i), 0), cap);
+        cnt_a[i] = c;
+        cnt_b[i] = c;
+    }
+}
+
+// Collective (every rank of the group, once, at creation): allocate the
+// buffers other ranks write into, export them through CUDA IPC, all-gather
+// the handles over NCCL and map every other rank's.
+int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
+    EpState& S = *L.ep;
+    const int G = S.world, El = S.e_local;
+    S.cap_T = capT;
+    S.cap_src = capT * std::min(L.k, El);
+    S.row_bytes = (size_t)L.d * elem_bytes(L);
+    const size_t rows_local = (size_t)capT * L.k;
+    const size_t seg_bytes = (size_t)G * S.cap_src * S.row_bytes;
+    cudaError_t e = cudaSuccess;
+    auto A = [&](void** p, size_t b) {
+        if (e == cudaSuccess) e = cudaMalloc(p, b ? b : 256);
+    };
+    A((void**)&S.send_tok, rows_local * sizeof(int));
+    A((void**)&S.send_w, rows_local * sizeof(float));
+    A((void**)&S.send_slot, rows_local * sizeof(int));
+    A((void**)&S.send_eoff, (L.E_route + 1) * sizeof(int));
+    A((void**)&S.cnt_recv, (size_t)G * El * sizeof(int));
+    A((void**)&S.cnt_scan, (size_t)G * El * sizeof(int));
+    A(&S.p2p_recv, seg_bytes);
+    A(&S.p2p_ret, seg_bytes);
+    A((void**)&S.p2p_cnt, (size_t)G * El * sizeof(int));
+    A((void**)&S.p2p_flag, 2 * G * sizeof(unsigned));
+    A((void**)&S.d_peer_recv, G * sizeof(void*));
+    A((void**)&S.d_peer_ret, G * sizeof(void*));
+    A((void**)&S.d_peer_cnt, G * sizeof(int*));
+    A((void**)&S.d_peer_flag, G * sizeof(unsigned*));
+    if (e == cudaSuccess) e = cudaMemset(S.p2p_flag, 0, 2 * G * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(S.p2p_cnt, 0, (size_t)G * El * sizeof(int));
+    if (e != cudaSuccess)
+        return report_error(MOE_ERR_OOM, std::string("expert-parallel buffers: ") +
+                                             cudaGetErrorString(e));
+    // Handles of this rank's four shared buffers, all-gathered.
+    constexpr int kBufs = 4;
+    void* mine[kBufs] = {S.p2p_recv, S.p2p_ret, S.p2p_cnt, S.p2p_flag};
+    std::vector<cudaIpcMemHandle_t> h_all((size_t)G * kBufs), h_mine(kBufs);
+    for (int i = 0; i < kBufs && e == cudaSuccess; ++i) e = cudaIpcGetMemHandle(&h_mine[i], mine[i]);
+    void* d_hbuf = nullptr;
+    const size_t hb = kBufs * sizeof(cudaIpcMemHandle_t);
+    if (e == cudaSuccess) e = cudaMalloc(&d_hbuf, hb * (G + 1));
+    if (e == cudaSuccess) e = cudaMemcpy(d_hbuf, h_mine.data(), hb, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        if (d_hbuf) cudaFree(d_hbuf);
+        return report_error(MOE_ERR_CUDA, std::string("IPC export: ") + cudaGetErrorString(e));
+    }
+    ncclResult_t nr = g_nccl.AllGather(d_hbuf, static_cast<char*>(d_hbuf) + hb, hb, ncclUint8,
+                                       S.comm, s);
+    if (nr != ncclSuccess) {
+        cudaFree(d_hbuf);
+        return nccl_fail(nr, "IPC handle all-gather");
+    }
+    e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(h_all.data(), static_cast<char*>(d_hbuf) + hb, hb * G, cudaMemcpyDeviceToHost);
+    cudaFree(d_hbuf);
+    std::vector<void*> ptr((size_t)G * kBufs);
+    for (int j = 0; j < G && e == cudaSuccess; ++j)
+        for (int i = 0; i < kBufs && e == cudaSuccess; ++i) {
+            if (j == S.rank) {
+                ptr[(size_t)j * kBufs + i] = mine[i];
+            } else {
+                void* p = nullptr;
+                e = cudaIpcOpenMemHandle(&p, h_all[(size_t)j * kBufs + i],
+                                         cudaIpcMemLazyEnablePeerAccess);
+                if (e == cudaSuccess) {
+                    S.ipc_opened.push_back(p);
+                    ptr[(size_t)j * kBufs + i] = p;
+                }
+            }
+        }
+    if (e != cudaSuccess)
+        return report_error(MOE_ERR_CUDA, std::string("IPC mapping of a peer's buffers: ") +
+                                              cudaGetErrorString(e));
+    std::vector<void*> col(G);
+    void** dst[kBufs] = {S.d_peer_recv, S.d_peer_ret, reinterpret_cast<void**>(S.d_peer_cnt),
+                         reinterpret_cast<void**>(S.d_peer_flag)};
+    for (int i = 0; i < kBufs && e == cudaSuccess; ++i) {
+        for (int j = 0; j < G; ++j) col[j] = ptr[(size_t)j * kBufs + i];
+        e = cudaMemcpy(dst[i], col.data(), G * sizeof(void*), cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) return report_error(MOE_ERR_CUDA, cudaGetErrorString(e));
+    // The receiving side runs the grouped GEMMs on up to world * T tokens' rows.
+    return ensure_workspace(L, capT * G);
+}
+
+int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+    EpState& S = *L.ep;
+    if (T > S.cap_T)
+        return report_error(MOE_ERR_INVALID,
+                            "T exceeds the expert-parallel capacity fixed at creation (max_tokens)");
+    Workspace& W = L.ws;
+    const int G = S.world, El = S.e_local, Eg = L.E_route;
+    const unsigned epoch = ++S.epoch;
+    auto cuda_err = [](cudaError_t e, const char* what) {
+        return report_error(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    cudaError_t ce;
+    L.prof_n = 0;
+    // 1-2: route; compact dispatch straight into the expert ranks' buffers.
+    prof_mark(L, 0, s);
+    if (T > 0) {
+        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s)) != cudaSuccess)
+            return cuda_err(ce, "router");
+        prof_mark(L, 1, s);
+        if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
+                                      W.counts, S.send_eoff, nullptr, nullptr, nullptr, nullptr,
+                                      nullptr, nullptr, s)) != cudaSuccess)
+            return cuda_err(ce, "dispatch scan");
+        prof_mark(L, 5, s);
+        PeerDst pd;
+        pd.bases = S.d_peer_recv;
+        pd.cap = S.cap_src;
+        pd.rank = S.rank;
+        pd.e_local = El;
+        pd.eoff = S.send_eoff;
+        pd.slot = S.send_slot;
+        if ((ce = launch_dispatch_push(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w, pd, s)) !=
+            cudaSuccess)
+            return cuda_err(ce, "dispatch push");
+    } else {
+        prof_mark(L, 5, s);
+        if ((ce = cudaMemsetAsync(W.counts, 0, Eg * sizeof(int), s)) != cudaSuccess)
+            return cuda_err(ce, "counts");
+    }
+    // 3-4: counts and flags to every rank; wait for every source's.
+    const int sig_threads = (G + 31) / 32 * 32;
+    ep_signal_kernel<<<1, sig_threads, 0, s>>>(S.d_peer_cnt, W.counts, S.d_peer_flag, G, El,
+                                               S.rank, 0, epoch);
+    ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 0, epoch, S.p2p_cnt,
+                                                            S.cnt_recv, S.cnt_scan, G * El,
+                                                            S.cap_src, W.dev_err);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "dispatch signal");
+    prof_mark(L, 2, s);
+    // Arrival scan and arrangement; the received total is known on the
+    // device only, so the launches are sized by bounds.
+    if ((ce = launch_scan_generic(S.cnt_scan, G, El, kTileM, W.counts, W.eoff, W.mtiles,
+                                  W.num_mtiles, W.ptiles, W.num_ptiles, W.row_token,
+                                  W.row_weight, s)) != cudaSuccess)
+        return cuda_err(ce, "arrival scan");
+    const int R_bound = G * S.cap_src;
+    const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
+    const int grid = (R_bound + 7) / 8;
+    if (three_pass(L))
+        ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.p2p_recv, R_bound, L.d, G, El, S.cap_src,
+                                                        S.cnt_recv, S.cnt_scan, W.eoff, W.row_token,
+                                                        W.row_weight, W.a_hi, W.a_lo);
+    else
+        ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.p2p_recv, R_bound, L.d, G, El, S.cap_src,
+                                                         S.cnt_recv, S.cnt_scan, W.eoff, W.row_token,
+                                                         W.row_weight, W.a_hi, W.a_lo);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
+    // 5-6: the local experts; the down GEMM stores each result in its
+    // source rank's return buffer.  The expected received count (T * k,
+    // this rank's own routed rows) sizes the GEMM launch; any count is run
+    // correctly.
+    const int R_est = std::max(T, 1) * L.k;
+    prof_mark(L, 3, s);
+    if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 0)) != cudaSuccess)
+        return cuda_err(ce, "gate/up GEMM");
+    prof_mark(L, 4, s);
+    PeerDst ret;
+    ret.bases = S.d_peer_ret;
+    ret.cap = S.cap_src;
+    ret.rank = S.rank;
+    if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 2, &ret)) != cudaSuccess)
+        return cuda_err(ce, "down GEMM");
+    // 7: return flags; wait for every expert rank's.
+    prof_mark(L, 6, s);
+    ep_signal_kernel<<<1, sig_threads, 0, s>>>(nullptr, nullptr, S.d_peer_flag, G, El, S.rank, 1,
+                                               epoch);
+    ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 1, epoch, nullptr,
+                                                            nullptr, nullptr, 0, 0, W.dev_err);
+    if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "return signal");
+    // 8: weighted combine into y.
+    prof_mark(L, 7, s);
+    if (T > 0) {
+        if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s)) != cudaSuccess)
+            return cuda_err(ce, "y memset");
+        const int rows = T * L.k;
+        if (three_pass(L))
+            ep_combine_kernel<true><<<(rows + 7) / 8, 256, 0, s>>>(S.p2p_ret, rows, L.d, S.send_tok,
+                                                                   S.send_w, S.send_slot, y);
+        else
+            ep_combine_kernel<false><<<(rows + 7) / 8, 256, 0, s>>>(S.p2p_ret, rows, L.d,
+                                                                    S.send_tok, S.send_w,
+                                                                    S.send_slot, y);
+        if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
+    }
+    prof_mark(L, kProfEnd, s);
+    return MOE_OK;
+}
+
+int ep_forward(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
+    if (L.ep->transport == MOE_EP_TRANSPORT_NCCL) return ep_forward_nccl(L, x, y, T, s);
+    return ep_forward_p2p(L, x, y, T, s);
 }
 
 struct DeviceGuardEp {
@@ -452,6 +764,16 @@ static int ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_
         S->comm = nullptr;
         moe_destroy(h);
         return rc;
+    }
+    S->transport = cfg->ep_transport;
+    if (S->transport == MOE_EP_TRANSPORT_P2P) {
+        // Fixed capacity: the buffers are mapped by every rank once.
+        const int capT = cfg->max_tokens > 0 ? cfg->max_tokens : 4096;
+        rc = ep_p2p_setup(h->L, capT, h->own_stream);
+        if (rc) {
+            moe_destroy(h);
+            return rc;
+        }
     }
     *out = h;
     return MOE_OK;

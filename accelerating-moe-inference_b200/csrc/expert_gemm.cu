@@ -56,6 +56,12 @@ struct GemmParams {
     const float* row_weight;
     float* y;          // Down: [T][d] accumulated; DownStore: [rows][d], row row_token[prow]
     int d;
+    // DownStore to peers (expert parallel, fused return): row_token[prow] is
+    // the slot source * peer_cap + row; the result goes to
+    // peer_out[source] at row peer_rank * peer_cap + row.
+    void* const* peer_out;
+    int peer_cap;
+    int peer_rank;
     int* err;
 };
 
@@ -158,6 +164,15 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
         // that sent it, at the row it arrived in -- fp32 in FP32
         // precision, bf16 in BF16 precision (half the return bytes).
         const int dst = valid ? p.row_token[prow] : 0;
+        // Start of the result row: local (p.y) or in the source rank's
+        // return buffer over NVLink.
+        constexpr size_t kEs = kTf32x3 ? 4 : 2;
+        char* rowp;
+        if (p.peer_out)
+            rowp = static_cast<char*>(p.peer_out[dst / p.peer_cap]) +
+                   ((size_t)p.peer_rank * p.peer_cap + dst % p.peer_cap) * p.d * kEs;
+        else
+            rowp = reinterpret_cast<char*>(p.y) + static_cast<size_t>(dst) * p.d * kEs;
 #pragma unroll 1
         for (int c = 0; c < kTileN; c += 32) {
             uint32_t v[32];
@@ -166,14 +181,13 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
             const int col = nt * kTileN + c;
             if (valid && col < p.d) {
                 if constexpr (kTf32x3) {
-                    float4* out = reinterpret_cast<float4*>(p.y + static_cast<size_t>(dst) * p.d + col);
+                    float4* out = reinterpret_cast<float4*>(rowp) + col / 4;
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
                         out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
                                                  __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
                 } else {
-                    uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.y) +
-                                                          static_cast<size_t>(dst) * p.d + col);
+                    uint4* out = reinterpret_cast<uint4*>(rowp) + col / 8;
 #pragma unroll
                     for (int j = 0; j < 32; j += 8) {
                         uint32_t w4[4];
@@ -689,7 +703,7 @@ cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, 
 }
 
 cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
-                                    int mode) {
+                                    int mode, const PeerDst* peer) {
     const bool down = mode != 0;
     const Workspace& W = L.ws;
     const bool tf = three_pass(L);
@@ -707,6 +721,14 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
     g.h_hi = W.h_hi;
     g.h_lo = W.h_lo;
     g.ldh = L.ffp;
+    g.peer_out = nullptr;
+    g.peer_cap = 1;
+    g.peer_rank = 0;
+    if (mode == 2 && peer) {
+        g.peer_out = peer->bases;
+        g.peer_cap = peer->cap;
+        g.peer_rank = peer->rank;
+    }
     g.k_splits = 1;
     g.kb_per = 0;   // set below, with k_blocks
     if (!down) {

@@ -24,6 +24,7 @@ enum DeviceError : int {
     kDevErrTimeoutDrain = 8,
     kDevErrTimeoutSelftest = 16,
     kDevErrTimeoutNorm = 32,
+    kDevErrTimeoutPeer = 64,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -41,6 +42,17 @@ __device__ __forceinline__ unsigned long long global_timer_ns() {
 // its writes to be visible (a no-op for an ordinary launch).
 __device__ __forceinline__ void wait_predecessor_grid() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// System-scope acquire load / release store of a flag word another GPU
+// writes or reads (expert-parallel completion flags in peer memory).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // ---------------------------------------------------------------- mbarrier

@@ -264,7 +264,8 @@ def run_ep(args, wl, pkg, world, rank, local):
         rank, world, obj[0], d=d, ff=ff, E=E, wg=wg.data_ptr(), w1=[ptr(t) for t in w1],
         w3=[ptr(t) for t in w3], w2=[ptr(t) for t in w2], device_pointers=True, top_k=k,
         policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec, device=local, max_tokens=T,
-        gemm_variant=_gemm_variant(args, pkg))
+        gemm_variant=_gemm_variant(args, pkg),
+        ep_transport=pkg.EP_TRANSPORT_NCCL if args.ep_transport == "nccl" else pkg.EP_TRANSPORT_P2P)
     del w1, w3, w2
     torch.cuda.empty_cache()
     xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
@@ -339,8 +340,10 @@ def run_ep(args, wl, pkg, world, rank, local):
                        "experts": E, "top_k": k, "router": "softmax_topk_renorm",
                        "precision": args.precision, "seed": wl["seed"],
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU, "
-                                      "NCCL send/recv dispatch and combine)"},
+                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU, " + (
+                           "NCCL send/recv dispatch and combine)" if args.ep_transport == "nccl"
+                           else "fused dispatch/combine: NVLink peer stores from the permute "
+                                "kernel and the down-GEMM epilogue)")},
             "roofline": {"kernel": "whole expert-parallel step (exchanges included)",
                          "bound": "tensor", "achieved": achieved, "peak": bf16_sust,
                          "unit": "TFLOP/s", "frac": achieved / bf16_sust,
@@ -373,6 +376,9 @@ def main():
     ap.add_argument("--gemm", choices=["auto", "ctapair", "single"], default="auto",
                     help="grouped-GEMM tiling: auto (2-CTA 256x256 tiles for prefill, 1-CTA "
                          "128x256 for decode-sized T), or force one")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange: fused NVLink peer stores (default) or NCCL "
+                         "send/recv")
     ap.add_argument("--parallelism", choices=["ep", "dp"], default="ep",
                     help="N > 1: expert parallel (default) or token-sharded replicas")
     ap.add_argument("--no-block", action="store_true",

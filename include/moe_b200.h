@@ -82,6 +82,18 @@ typedef enum MoeGemmVariant {
 
 #define MOE_DECODE_AUTO (-1)
 
+/* Expert-parallel exchange.
+ * P2P (default): fused -- the dispatch permute writes routed rows straight
+ *   into the owning rank's receive buffer over NVLink and the down GEMM's
+ *   epilogue writes results straight back; completion is signalled with
+ *   flags in peer memory.  Needs all ranks on one node (CUDA IPC).
+ * NCCL: separate grouped ncclSend / ncclRecv exchanges after the dispatch
+ *   and after the down GEMM, with a host read of the counts in between. */
+typedef enum MoeEpTransport {
+    MOE_EP_TRANSPORT_P2P = 0,
+    MOE_EP_TRANSPORT_NCCL = 1
+} MoeEpTransport;
+
 typedef struct MoeConfig {
     int32_t d_model;        /* hidden size; multiple of 64 */
     int32_t d_ff;           /* expert intermediate size (any; padded internally) */
@@ -98,7 +110,8 @@ typedef struct MoeConfig {
     int32_t device;         /* CUDA device ordinal the handle lives on */
     int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
     int32_t gemm_variant;   /* MoeGemmVariant of the grouped expert GEMMs */
-    int32_t reserved[4];
+    int32_t ep_transport;   /* MoeEpTransport (expert-parallel handles only) */
+    int32_t reserved[3];
 } MoeConfig;
 
 /* Host fp32 weights of one layer (the tensors PhiMoE loads by name,

@@ -7,7 +7,9 @@ payload all-to-all, the experts on each rank's slice, the return all-to-all
 and the weighted combine.  The result must equal the single-process oracle.
 
 GPU (2 B200s, skipped with fewer): moe_ep_forward_device itself against the
-oracle, per rank.
+oracle, per rank, with both transports: the fused one (dispatch permute and
+down-GEMM epilogue storing rows into the other GPU's buffers over NVLink,
+flags in peer memory) and NCCL send/recv.
 """
 import os
 import socket
@@ -128,7 +130,7 @@ def test_ep_plan_offsets_and_rejection():
         pkg.ep_plan(np.array([1, -1], np.int32), np.array([[0], [0]], np.int32), 2, 1)
 
 
-def _gpu_rank(rank, world, idbytes, q, precision):
+def _gpu_rank(rank, world, idbytes, q, precision, transport):
     try:
         import torch
         sys.path.insert(0, str(ROOT / "tests"))
@@ -140,7 +142,8 @@ def _gpu_rank(rank, world, idbytes, q, precision):
         m = pkg.MoeLayer.expert_parallel(rank, world, idbytes, d=D, ff=FF, E=E, wg=layer.wg,
                                          w1=layer.w1, w3=layer.w3, w2=layer.w2,
                                          bias=layer.router_bias, top_k=K, policy=1,
-                                         precision=precision, device=rank)
+                                         precision=precision, device=rank,
+                                         ep_transport=transport, max_tokens=64)
         xd = torch.from_numpy(x).cuda()
         yd = torch.empty_like(xd)
         ys = []
@@ -157,8 +160,9 @@ def _gpu_rank(rank, world, idbytes, q, precision):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("transport", [0, 1], ids=["p2p", "nccl"])
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
-def test_ep_forward_on_two_gpus(precision):
+def test_ep_forward_on_two_gpus(precision, transport):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -167,7 +171,8 @@ def test_ep_forward_on_two_gpus(precision):
     idbytes = pkg.ep_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, idbytes, q, precision)) for r in range(2)]
+    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, idbytes, q, precision, transport))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)
