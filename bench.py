@@ -51,7 +51,24 @@ WORKLOADS = {
     # 14336) with 2 experts, ~2 GB on the device (weights > L2).
     "c2small": dict(workload="c2small-2expert-profile", T=2048, d=4096, ff=14336, E=2, k=2,
                     seed=1),
+    # fine-grained experts, top-8, router logits ~N(0, 1)
+    # (router weights N(0, 1/d)) plus the Zipf-like bias 0.5 ln(1/rank).
+    "c5": dict(workload="c5-finegrained-ep", T=16384, d=2048, ff=1408, E=64, k=8, seed=3,
+               zipf=True),
 }
+
+
+def _router_weights(wl, gen, dev):
+    """Router weights and bias of a workload, drawn on the device."""
+    import torch
+    E, d = wl["E"], wl["d"]
+    std = (1.0 / d ** 0.5) if wl.get("zipf") else 0.02
+    wg = torch.randn(E, d, generator=gen, device=dev).mul_(std)
+    bias = None
+    if wl.get("zipf"):
+        r = torch.arange(1, E + 1, dtype=torch.float64)
+        bias = (0.5 * torch.log(1.0 / r)).to(torch.float32).to(dev)
+    return wg, bias
 KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
 DECODE_T = (1, 2, 4, 8, 16, 32, 64)  # BASELINE config 3
 FLUSH_BYTES = 256 << 20
@@ -248,7 +265,7 @@ def run_ep(args, wl, pkg, world, rank, local):
     dist.broadcast_object_list(obj, src=0)
     gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
     rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
-    wg = rnd(E, d)
+    wg, rbias = _router_weights(wl, gen, dev)
     w1, w3, w2 = [], [], []
     El = E // world
     for e in range(E):
@@ -263,6 +280,7 @@ def run_ep(args, wl, pkg, world, rank, local):
     layer = pkg.MoeLayer.expert_parallel(
         rank, world, obj[0], d=d, ff=ff, E=E, wg=wg.data_ptr(), w1=[ptr(t) for t in w1],
         w3=[ptr(t) for t in w3], w2=[ptr(t) for t in w2], device_pointers=True, top_k=k,
+        bias=rbias.data_ptr() if rbias is not None else None,
         policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec, device=local, max_tokens=T,
         gemm_variant=_gemm_variant(args, pkg),
         ep_transport=pkg.EP_TRANSPORT_NCCL if args.ep_transport == "nccl" else pkg.EP_TRANSPORT_P2P)
@@ -337,7 +355,8 @@ def run_ep(args, wl, pkg, world, rank, local):
             "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
             "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
             "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
-                       "experts": E, "top_k": k, "router": "softmax_topk_renorm",
+                       "experts": E, "top_k": k,
+                       "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
                        "precision": args.precision, "seed": wl["seed"],
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
                        "parallelism": f"ep{world} (expert parallel, {El} experts per GPU, " + (
@@ -421,13 +440,14 @@ def main():
     gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
     dev = torch.device("cuda", local)
     rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
-    wg = rnd(E, d)
+    wg, rbias = _router_weights(wl, gen, dev)
     w1 = [rnd(ff, d) for _ in range(E)]
     w3 = [rnd(ff, d) for _ in range(E)]
     w2 = [rnd(d, ff) for _ in range(E)]
     layer = pkg.MoeLayer.from_device_pointers(
         d, ff, E, wg.data_ptr(), [t.data_ptr() for t in w1], [t.data_ptr() for t in w3],
-        [t.data_ptr() for t in w2], top_k=k, policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec,
+        [t.data_ptr() for t in w2], rbias.data_ptr() if rbias is not None else None, top_k=k,
+        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec,
         device=local, max_tokens=T, decode_max_tokens=args.decode_max_tokens,
         gemm_variant=_gemm_variant(args, pkg))
     host_layer = None
@@ -605,7 +625,8 @@ def main():
             "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
             "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
             "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
-                       "experts": E, "top_k": k, "router": "softmax_topk_renorm",
+                       "experts": E, "top_k": k,
+                       "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
                        "precision": args.precision, "seed": wl["seed"], "gemm": args.gemm,
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
                        "parallelism": f"dp{world} (token-sharded replicas, all experts per GPU)"},
