@@ -150,6 +150,10 @@ struct EpState {
     int** d_peer_cnt = nullptr;
     unsigned** d_peer_flag = nullptr;
     std::vector<void*> ipc_opened;  // mappings of the other ranks' buffers
+    // Round-robin placement: rank r holds experts r, r + G, r + 2G, ...;
+    // eperm[e] = (e % G) * E_local + e / G is expert e's dispatch position
+    // (rank-major, so each rank's experts are one contiguous run).
+    int* eperm = nullptr;
 };
 
 namespace {
@@ -327,7 +331,8 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 1-2: route and pack locally (compact, expert-sorted).
     prof_mark(L, 0, s);
     if (T > 0) {
-        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s)) != cudaSuccess)
+        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, NormRef{},
+                                S.eperm)) != cudaSuccess)
             return cuda_err(ce, "router");
         prof_mark(L, 1, s);
         if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
@@ -583,7 +588,8 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 1-2: route; compact dispatch straight into the expert ranks' buffers.
     prof_mark(L, 0, s);
     if (T > 0) {
-        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s)) != cudaSuccess)
+        if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, NormRef{},
+                                S.eperm)) != cudaSuccess)
             return cuda_err(ce, "router");
         prof_mark(L, 1, s);
         if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
@@ -695,6 +701,7 @@ struct DeviceGuardEp {
 void ep_destroy(Layer& L) {
     if (!L.ep) return;
     ep_free_buffers(*L.ep);
+    if (L.ep->eperm) cudaFree(L.ep->eperm);
     if (L.ep->comm && g_nccl.ok) g_nccl.CommDestroy(L.ep->comm);
     delete L.ep;
     L.ep = nullptr;
@@ -747,8 +754,27 @@ static int ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_
         return report_error(MOE_ERR_INVALID, "num_experts must be a multiple of the group size");
     if (!load_nccl(&err)) return report_error(MOE_ERR_NCCL, err);
     const int El = cfg->num_experts / world;
+    // Round-robin placement (balances a skewed router, e.g. BASELINE config
+    // 5's Zipf-like bias): dispatch position i holds expert
+    // (i % El) * world + i / El, so this rank's slice [rank * El, ...) is
+    // experts rank, rank + world, ...  The router weights keep the experts'
+    // own order.
+    const int Eg = cfg->num_experts;
+    std::vector<const float*> w1p(Eg), w2p(Eg), w3p(Eg);
+    std::vector<int> eperm(Eg);
+    for (int i = 0; i < Eg; ++i) {
+        const int e = (i % El) * world + i / El;
+        w1p[i] = w->w1[e];
+        w2p[i] = w->w2[e];
+        w3p[i] = w->w3[e];
+        eperm[e] = i;
+    }
+    MoeWeightsHost wp = *w;
+    wp.w1 = w1p.data();
+    wp.w2 = w2p.data();
+    wp.w3 = w3p.data();
     MoeHandle* h = nullptr;
-    int rc = create_slice(cfg, w, device_ptrs, rank * El, El, &h);
+    int rc = create_slice(cfg, &wp, device_ptrs, rank * El, El, &h);
     if (rc) return rc;
     DeviceGuardEp guard(cfg->device);
     auto* S = new EpState();
@@ -756,6 +782,14 @@ static int ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_
     S->world = world;
     S->e_local = El;
     h->L.ep = S;
+    cudaError_t ce = cudaMalloc(&S->eperm, Eg * sizeof(int));
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(S->eperm, eperm.data(), Eg * sizeof(int), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        rc = report_error(MOE_ERR_CUDA, std::string("expert placement: ") + cudaGetErrorString(ce));
+        moe_destroy(h);
+        return rc;
+    }
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof id);
     ncclResult_t r = g_nccl.CommInitRank(&S->comm, world, id, rank);

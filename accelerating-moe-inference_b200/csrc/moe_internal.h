@@ -182,9 +182,12 @@ inline void prof_mark(Layer& L, int i, cudaStream_t s) {
 
 // ------------------------------------------------------------ launchers
 // route.cu
-// nr active: x is normalised on load (the post-attention LayerNorm).
+// nr active: x is normalised on load (the post-attention LayerNorm).  eperm
+// (expert parallelism): idx and the histogram get eperm[expert], the
+// expert's dispatch position, instead of the expert itself.
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
-                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr = {});
+                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr = {},
+                          const int* eperm = nullptr);
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
 // Batches of at most 4 tokens: router, selection, layout and the routed rows
 // in one single-CTA launch (rows in the decode kernels' format if `decode`,

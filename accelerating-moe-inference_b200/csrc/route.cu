@@ -132,7 +132,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
               const float* __restrict__ bias, int T, int d, int E, int k, int policy,
               float quantum, float tie_eps, float* __restrict__ logits_out,
               int* __restrict__ idx_out, float* __restrict__ w_out,
-              int* __restrict__ blockhist, NormRef nr) {
+              int* __restrict__ blockhist, NormRef nr, const int* __restrict__ eperm) {
     constexpr int kStages = 4;
     constexpr int kLd = KC + 4;              // padded row stride (floats)
     constexpr int kXs = kRouteTokens * kLd;  // x floats per stage
@@ -279,9 +279,12 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         if (lane == 0) {
             const int t = t0 + tk;
             for (int s = 0; s < k; ++s) {
-                idx_out[(size_t)t * k + s] = sel[s];
+                // Expert parallelism: the dispatch position of the expert
+                // (placement), selection having used its own index.
+                const int e = eperm ? eperm[sel[s]] : sel[s];
+                idx_out[(size_t)t * k + s] = e;
                 w_out[(size_t)t * k + s] = wsel[s];
-                atomicAdd(&hist[sel[s]], 1);
+                atomicAdd(&hist[e], 1);
             }
         }
     }
@@ -861,7 +864,8 @@ dim3 permute_grid(const Layer& L, int T) {
 
 template <int EJ, int KC>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
-                            float* wts, int* blockhist, cudaStream_t s, const NormRef& nr) {
+                            float* wts, int* blockhist, cudaStream_t s, const NormRef& nr,
+                            const int* eperm) {
     const int E = L.E_route;
     const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4) + 2 * KC) +
                                          2 * kRouteTokens + kRouteTokens * (E + 1)) +
@@ -877,34 +881,36 @@ cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits
     const int tok = T < kRouteTokens ? (T + 3) / 4 * 4 : kRouteTokens;
     kern<<<nblk, 8 * tok, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
                                             L.cfg.router_policy, L.cfg.router_quantum,
-                                            L.cfg.router_tie_eps, logits, idx, wts, blockhist, nr);
+                                            L.cfg.router_tie_eps, logits, idx, wts, blockhist, nr,
+                                            eperm);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, int* idx,
-                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr) {
+                          float* wts, int* blockhist, cudaStream_t s, const NormRef& nr,
+                          const int* eperm) {
     // K chunk per pipeline stage: as wide as shared memory allows, so each
     // SM keeps 100-200 KB of x / wg loads in flight (the dot-product chains
     // themselves are serial and cannot be split).
     const int ej = (L.E_route + 7) / 8;
     if (L.d % 256 == 0) {
-        if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s, nr);
-        if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+        if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
     }
     if (L.d % 128 == 0) {
-        if (ej <= 1) return launch_router_t<1, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
-        if (ej <= 2) return launch_router_t<2, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
-        if (ej <= 4) return launch_router_t<4, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
-        if (ej <= 8) return launch_router_t<8, 128>(L, x, T, logits, idx, wts, blockhist, s, nr);
+        if (ej <= 1) return launch_router_t<1, 128>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+        if (ej <= 2) return launch_router_t<2, 128>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+        if (ej <= 4) return launch_router_t<4, 128>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+        if (ej <= 8) return launch_router_t<8, 128>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
     }
-    if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
-    if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
-    if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
-    if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s, nr);
-    if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
-    return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s, nr);
+    if (ej <= 1) return launch_router_t<1, 64>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    if (ej <= 2) return launch_router_t<2, 64>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    if (ej <= 4) return launch_router_t<4, 64>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    if (ej <= 8) return launch_router_t<8, 64>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    if (ej <= 16) return launch_router_t<16, 32>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    return launch_router_t<32, 32>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
 }
 
 bool route_small_geometry(const Layer& L, int T, bool norm, int* kc_out, int* stages_out) {

@@ -109,13 +109,46 @@ def _traffic_from_profile(workload: str, precision: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled every
+    10 ms from construction to stop() by an NVML polling thread (read-only
+    queries); nvidia-smi every 100 ms if NVML is unavailable."""
     Q = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits.
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40}
 
     def __init__(self, uuid: str):
+        import threading
         self.uuid = uuid
+        self.p = None
+        self.samples, self.mask, self.mx = [], 0, None
+        self._stop = threading.Event()
+        self.t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(
+                            h, pynvml.NVML_CLOCK_SM)))
+                        self.mask |= int(reasons(h))
+                    except Exception:  # noqa: BLE001 -- a failed query skips a sample
+                        pass
+                    self._stop.wait(0.01)
+
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:  # noqa: BLE001 -- no NVML: fall back to nvidia-smi
+            self.t = None
         self.f = tempfile.TemporaryFile(mode="w+")
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
@@ -125,6 +158,13 @@ class ClockSampler:
             self.p = None
 
     def stop(self):
+        if self.t is not None:
+            self._stop.set()
+            self.t.join()
+            reasons = sorted(n for n, b in self.BITS.items() if self.mask & b)
+            return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                    "sm_max_mhz": self.mx, "samples": len(self.samples), "reasons": reasons,
+                    "source": "NVML, 10 ms"}
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.p.terminate()
@@ -145,7 +185,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "samples": len(sm), "reasons": sorted(reasons), "source": "nvidia-smi, 100 ms"}
 
 
 def cpu_reference_tokens_per_s(host_layer, x_host, threads: int):

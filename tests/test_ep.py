@@ -55,12 +55,15 @@ def _gloo_rank(rank, world, port, q):
         layer = _layer(pkg)
         x = _tokens(pkg, rank)
         T = x.shape[0]
+        # 1-2: route and pack compactly, sorted by dispatch position then
+        # token.  Round-robin placement: rank r holds experts r, r + G, ...;
+        # expert e's dispatch position is (e % G) * El + e // G.
         El = E // world
-        # 1-2: route and pack compactly, sorted by global expert then token.
+        pos = lambda e: (e % world) * El + e // world  # noqa: E731
         logits = orc.router_logits(x, layer.wg, layer.router_bias)
         idx, w = orc.route(logits, K, oracle.POLICY_SOFTMAX)
-        counts = np.bincount(idx.ravel(), minlength=E).astype(np.int32)
-        order = sorted(((int(idx[t, s]), t, s) for t in range(T) for s in range(K)))
+        counts = np.bincount([pos(int(e)) for e in idx.ravel()], minlength=E).astype(np.int32)
+        order = sorted(((pos(int(idx[t, s])), t, s) for t in range(T) for s in range(K)))
         send_rows = np.stack([x[t] for (_, t, _) in order])
         send_tok = np.array([t for (_, t, _) in order])
         send_w = np.array([w[t, s] for (_, t, s) in order], np.float32)
@@ -81,7 +84,7 @@ def _gloo_rank(rank, world, port, q):
             for el in range(El):
                 n = int(counts_in[src, el])
                 if n:
-                    e = rank * El + el
+                    e = el * world + rank
                     out[base:base + n] = orc.expert_ffn(recv[base:base + n], layer.w1[e],
                                                         layer.w3[e], layer.w2[e])
                 base += n
