@@ -363,7 +363,8 @@ class MoeLayer:
         """Collective: this rank's member of an expert-parallel group
         (moe_ep_create / moe_ep_create_from_device).  Weights are numpy arrays
         (host) or integer device addresses (device_pointers=True) for all E
-        experts; only this rank's slice is read."""
+        experts in their own order; only this rank's experts (rank,
+        rank + world, ...: round-robin placement) are read."""
         L = load_library()
         cfg = default_config(d_model=d, d_ff=ff, num_experts=E, top_k=top_k, router_policy=policy,
                              precision=precision, device=device, max_tokens=max_tokens, **cfg_kw)

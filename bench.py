@@ -309,7 +309,7 @@ def run_ep(args, wl, pkg, world, rank, local):
     w1, w3, w2 = [], [], []
     El = E // world
     for e in range(E):
-        mine = rank * El <= e < (rank + 1) * El
+        mine = e % world == rank   # round-robin placement: rank r holds r, r + N, ...
         a, b, c = rnd(ff, d), rnd(ff, d), rnd(d, ff)   # every rank draws the same stream
         w1.append(a if mine else None)
         w3.append(b if mine else None)
@@ -399,7 +399,7 @@ def run_ep(args, wl, pkg, world, rank, local):
                        "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
                        "precision": args.precision, "seed": wl["seed"],
                        "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU, " + (
+                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU placed round-robin, " + (
                            "NCCL send/recv dispatch and combine)" if args.ep_transport == "nccl"
                            else "fused dispatch/combine: NVLink peer stores from the permute "
                                 "kernel and the down-GEMM epilogue)")},

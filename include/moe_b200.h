@@ -272,14 +272,18 @@ int moe_profile_read(MoeHandle* h, float* stage_ms, int32_t n);
 
 /* ---------------------------------------------------------------------
  * Expert parallelism (no counterpart in the reference, which runs on one
- * GPU): one process and one GPU per rank, experts split contiguously
- * (rank r holds experts [r*E/G, (r+1)*E/G)), router weights replicated,
- * NCCL point-to-point exchanges over NVLink for dispatch and combine.
- * NCCL is loaded at run time (libnccl.so.2); MOE_ERR_NCCL if it is absent.
+ * GPU): one process and one GPU per rank, experts placed round-robin
+ * (rank r holds experts r, r + G, r + 2G, ...; a skewed router's hot
+ * experts land on different ranks), router weights replicated.  Expert e's
+ * dispatch position is (e % G) * (E / G) + e / G, so each rank's experts
+ * form one contiguous run of positions.  Dispatch and combine cross NVLink
+ * as peer stores (MOE_EP_TRANSPORT_P2P) or NCCL point-to-point exchanges
+ * (MOE_EP_TRANSPORT_NCCL).  NCCL is loaded at run time (libnccl.so.2);
+ * MOE_ERR_NCCL if it is absent.
  * --------------------------------------------------------------------- */
 
 /* The exchange plan of one forward, host only (no GPU needed): from this
- * rank's routed rows per global expert `counts` [world * e_local] and the
+ * rank's routed rows per dispatch position `counts` [world * e_local] and the
  * rows each source sends it for its local experts `counts_in`
  * [world][e_local], the rows sent to / received from each rank and their
  * offsets in the (expert-sorted) send and (source-major) receive buffers.
@@ -293,9 +297,10 @@ int moe_ep_unique_id(void* id_out);
 
 /* Collective over the group: every rank calls it with the same global
  * config (num_experts a multiple of `world`) and the same id.  `weights`
- * holds pointers for all E experts; only this rank's slice is read (host
- * pointers here, device pointers on cfg->device for the _from_device
- * variant). */
+ * holds pointers for all E experts, in the experts' own order; only this
+ * rank's experts (r, r + G, ...) are read, so the others may be any
+ * non-null placeholder (host pointers here, device pointers on cfg->device
+ * for the _from_device variant). */
 int moe_ep_create(const MoeConfig* cfg, const MoeWeightsHost* weights, int rank, int world,
                   const void* nccl_id, MoeHandle** out);
 int moe_ep_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* weights, int rank,
