@@ -49,6 +49,10 @@ EXPORTED_SYMBOLS = (
     "moe_selftest_wait_timeout", "moe_set_post_norm", "moe_block_forward_device",
     "moe_block_forward_host", "moe_layer_norm_device",
     "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
+    "moe_set_post_rms_norm", "moe_decoder_config_init", "moe_decoder_create",
+    "moe_decoder_create_from_device", "moe_decoder_destroy", "moe_decoder_device_bytes",
+    "moe_decoder_prefill", "moe_decoder_decode_step", "moe_decoder_generate",
+    "moe_decoder_last_timing",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm",
                   "ep_exchange_in", "ep_exchange_out", "ep_combine")
@@ -78,6 +82,27 @@ class MoeWeightsHost(ctypes.Structure):
     _fields_ = [("router_weight", _f32p), ("router_bias", _f32p),
                 ("w1", ctypes.POINTER(_f32p)), ("w3", ctypes.POINTER(_f32p)),
                 ("w2", ctypes.POINTER(_f32p))]
+
+
+class MoeDecoderConfig(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int32), ("d_model", ctypes.c_int32),
+                ("n_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("vocab", ctypes.c_int32), ("num_experts", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("d_ff", ctypes.c_int32),
+                ("rms_eps", ctypes.c_float), ("rope_base", ctypes.c_float),
+                ("precision", ctypes.c_int32), ("max_batch", ctypes.c_int32),
+                ("max_seq", ctypes.c_int32), ("device", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 4)]
+
+
+_f32pp = ctypes.POINTER(_f32p)
+
+
+class MoeDecoderWeightsC(ctypes.Structure):
+    _fields_ = [("embed", _f32p), ("final_norm", _f32p), ("attn_norm", _f32pp),
+                ("wq", _f32pp), ("wk", _f32pp), ("wv", _f32pp), ("wo", _f32pp),
+                ("ffn_norm", _f32pp), ("router", _f32pp), ("w1", _f32pp), ("w3", _f32pp),
+                ("w2", _f32pp)]
 
 
 _lib = None
@@ -132,6 +157,22 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_ep_forward_device.argtypes = [vp, vp, vp, ctypes.c_int32, vp]
     L.moe_dispatch_noalloc.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        vp, vp, ctypes.c_int32, vp, vp, vp]
+    L.moe_set_post_rms_norm.argtypes = [vp, vp, ctypes.c_float]
+    dcp = ctypes.POINTER(MoeDecoderConfig)
+    dwp = ctypes.POINTER(MoeDecoderWeightsC)
+    L.moe_decoder_config_init.argtypes = [dcp]
+    L.moe_decoder_config_init.restype = None
+    L.moe_decoder_create.argtypes = [dcp, dwp, ctypes.POINTER(vp)]
+    L.moe_decoder_create_from_device.argtypes = [dcp, dwp, ctypes.POINTER(vp)]
+    L.moe_decoder_destroy.argtypes = [vp]
+    L.moe_decoder_destroy.restype = None
+    L.moe_decoder_device_bytes.argtypes = [vp]
+    L.moe_decoder_device_bytes.restype = ctypes.c_size_t
+    L.moe_decoder_prefill.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p, _i32p]
+    L.moe_decoder_decode_step.argtypes = [vp, _i32p, _f32p, _i32p]
+    L.moe_decoder_generate.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_int32, _f32p, _i32p]
+    L.moe_decoder_last_timing.argtypes = [vp, _f32p, _f32p]
     if path is None:
         _lib = L
     return L
@@ -438,6 +479,13 @@ class MoeLayer:
             raise ValueError(f"post-norm weight and bias must have shape ({self.d},)")
         _check(load_library().moe_set_post_norm(self._h, _fp(w), _fp(b), eps))
 
+    def set_post_rms_norm(self, weight: np.ndarray, eps: float = 1e-5):
+        """Attach an RMSNorm as the block's input norm (moe_set_post_rms_norm)."""
+        w = np.ascontiguousarray(weight, np.float32)
+        if w.shape != (self.d,):
+            raise ValueError(f"rms-norm weight must have shape ({self.d},)")
+        _check(load_library().moe_set_post_rms_norm(self._h, w.ctypes.data, eps))
+
     def block_forward_host(self, attn: np.ndarray) -> np.ndarray:
         attn = np.ascontiguousarray(attn, np.float32)
         T, d = attn.shape
@@ -500,6 +548,213 @@ class MoeLayer:
     def close(self):
         if self._h:
             load_library().moe_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+# ---------------------------------------------------------------------------
+# Toy MoE decoder: moe_decoder_* in include/moe_b200.h.
+
+@dataclass
+class DecoderWeights:
+    """fp32 weights of the toy MoE decoder, nn.Linear layout ([out][in])."""
+    embed: np.ndarray                   # [vocab][d]; tied output head
+    final_norm: np.ndarray              # [d]
+    attn_norm: list                     # L x [d]
+    wq: list                            # L x [d][d]
+    wk: list
+    wv: list
+    wo: list
+    ffn_norm: list                      # L x [d]
+    moe: list                           # L x LayerWeights (router + experts)
+
+    @property
+    def n_layers(self) -> int:
+        return len(self.wq)
+
+    @property
+    def d(self) -> int:
+        return self.embed.shape[1]
+
+    @property
+    def vocab(self) -> int:
+        return self.embed.shape[0]
+
+
+def synthetic_decoder(seed: int, n_layers: int, d: int, vocab: int, E: int, ff: int,
+                      std: float = 0.02, norm_jitter: float = 0.0) -> DecoderWeights:
+    """Seeded N(0, std) weights (numpy PCG64), drawn in a fixed order:
+    embedding, then per layer wq, wk, wv, wo and the MoE layer (router, then
+    per expert w1, w3, w2, from its own seeded stream).  Norm weights are 1
+    (plus N(0, norm_jitter) when norm_jitter > 0, stream offset by 0x4e4f)."""
+    g = np.random.Generator(np.random.PCG64([seed, 0xDEC]))
+
+    def normal(shape):
+        return (g.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+    gn = np.random.Generator(np.random.PCG64([seed, 0x4E4F]))
+
+    def norm_w():
+        w = np.ones(d, np.float32)
+        if norm_jitter > 0:
+            w = (w + norm_jitter * gn.standard_normal(d)).astype(np.float32)
+        return w
+
+    embed = normal((vocab, d))
+    wq, wk, wv, wo, an, fn, moe = [], [], [], [], [], [], []
+    for l in range(n_layers):
+        wq.append(normal((d, d)))
+        wk.append(normal((d, d)))
+        wv.append(normal((d, d)))
+        wo.append(normal((d, d)))
+        an.append(norm_w())
+        fn.append(norm_w())
+        moe.append(synthetic_layer(seed * 1000 + 7 + l, d, ff, E, std))
+    return DecoderWeights(embed, norm_w(), an, wq, wk, wv, wo, fn, moe)
+
+
+def synthetic_prompt(seed: int, B: int, S: int, vocab: int) -> np.ndarray:
+    """Seeded uniform token ids [B][S] (numpy PCG64, stream offset by 0x1d5)."""
+    g = np.random.Generator(np.random.PCG64([seed, 0x1D5]))
+    return g.integers(0, vocab, size=(B, S), dtype=np.int32)
+
+
+def decoder_config(**kw) -> MoeDecoderConfig:
+    c = MoeDecoderConfig()
+    load_library().moe_decoder_config_init(ctypes.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+class MoeDecoder:
+    """The toy MoE decoder on one GPU (moe_decoder_*): prefill, KV-cached
+    decode steps and greedy generation, mirroring PhiTinyMoEModel's generate
+    and generate_decode (include/model.h:8-30)."""
+
+    def __init__(self, weights: Optional[DecoderWeights] = None, *, n_heads: int, head_dim: int,
+                 top_k: int = 2, precision: int = PREC_BF16, max_batch: int = 16,
+                 max_seq: int = 640, device: int = 0, rms_eps: float = 1e-5,
+                 rope_base: float = 10000.0, device_pointers: Optional[dict] = None,
+                 dims: Optional[dict] = None):
+        """Host numpy weights, or device_pointers: a dict of integer device
+        addresses with the DecoderWeights field names (per-layer entries as
+        lists; 'router', 'w1', 'w3', 'w2' flattened layer-major) plus dims
+        {n_layers, d, vocab, E, ff}."""
+        L = load_library()
+        if device_pointers is None:
+            w = weights
+            dm = dict(n_layers=w.n_layers, d=w.d, vocab=w.vocab, E=w.moe[0].E, ff=w.moe[0].ff)
+        else:
+            dm = dims
+        self.cfg = decoder_config(n_layers=dm["n_layers"], d_model=dm["d"], n_heads=n_heads,
+                                  head_dim=head_dim, vocab=dm["vocab"], num_experts=dm["E"],
+                                  top_k=top_k, d_ff=dm["ff"], rms_eps=rms_eps,
+                                  rope_base=rope_base, precision=precision,
+                                  max_batch=max_batch, max_seq=max_seq, device=device)
+        nl, E = dm["n_layers"], dm["E"]
+        P = lambda n: _f32p * n  # noqa: E731
+        if device_pointers is None:
+            keep = []
+
+            def hp(a):
+                a = np.ascontiguousarray(a, np.float32)
+                keep.append(a)
+                return _fp(a)
+
+            def arr(lst):
+                return P(len(lst))(*[hp(a) for a in lst])
+            cw = MoeDecoderWeightsC(
+                hp(w.embed), hp(w.final_norm), arr(w.attn_norm), arr(w.wq), arr(w.wk), arr(w.wv),
+                arr(w.wo), arr(w.ffn_norm), arr([m.wg for m in w.moe]),
+                arr([a for m in w.moe for a in m.w1]), arr([a for m in w.moe for a in m.w3]),
+                arr([a for m in w.moe for a in m.w2]))
+            fn = L.moe_decoder_create
+        else:
+            dp = device_pointers
+            keep = None
+            cast = lambda v: ctypes.cast(ctypes.c_void_p(v), _f32p)  # noqa: E731
+
+            def arr(lst):
+                return P(len(lst))(*[cast(v) for v in lst])
+            cw = MoeDecoderWeightsC(
+                cast(dp["embed"]), cast(dp["final_norm"]), arr(dp["attn_norm"]), arr(dp["wq"]),
+                arr(dp["wk"]), arr(dp["wv"]), arr(dp["wo"]), arr(dp["ffn_norm"]),
+                arr(dp["router"]), arr(dp["w1"]), arr(dp["w3"]), arr(dp["w2"]))
+            fn = L.moe_decoder_create_from_device
+        h = ctypes.c_void_p()
+        _check(fn(ctypes.byref(self.cfg), ctypes.byref(cw), ctypes.byref(h)))
+        del keep
+        self._h = h
+        self.vocab = dm["vocab"]
+        self.E = E
+        self.n_layers = nl
+
+    def device_bytes(self) -> int:
+        return load_library().moe_decoder_device_bytes(self._h)
+
+    def prefill(self, tokens: np.ndarray):
+        """Last-position logits [B][vocab] and greedy next ids [B]."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        B, S = tok.shape
+        logits = np.empty((B, self.vocab), np.float32)
+        ids = np.empty(B, np.int32)
+        self._B = 0
+        _check(load_library().moe_decoder_prefill(self._h, tok.ctypes.data_as(_i32p), B, S,
+                                                   _fp(logits), ids.ctypes.data_as(_i32p)))
+        self._B = B
+        return logits, ids
+
+    def decode_step(self, tokens: np.ndarray):
+        """tokens [B] at the next position of every sequence of the last
+        prefill; logits [B][vocab] and greedy next ids [B]."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        B = tok.shape[0]
+        if getattr(self, "_B", 0) and B != self._B:
+            raise ValueError(f"decode_step needs one token per sequence ({self._B}), got {B}")
+        logits = np.empty((B, self.vocab), np.float32)
+        ids = np.empty(B, np.int32)
+        _check(load_library().moe_decoder_decode_step(self._h, tok.ctypes.data_as(_i32p),
+                                                       _fp(logits), ids.ctypes.data_as(_i32p)))
+        return logits, ids
+
+    def generate(self, prompt: np.ndarray, max_new_tokens: int, eos_id: int = -1,
+                 want_logits: bool = True, logits_out: Optional[np.ndarray] = None):
+        """Greedy ids [B][n] (-1 after eos) and, if wanted, logits [B][n][vocab]."""
+        tok = np.ascontiguousarray(prompt, np.int32)
+        B, S = tok.shape
+        ids = np.empty((B, max_new_tokens), np.int32)
+        logits = None
+        if want_logits:
+            logits = logits_out if logits_out is not None else np.empty(
+                (B, max_new_tokens, self.vocab), np.float32)
+        self._B = 0
+        _check(load_library().moe_decoder_generate(
+            self._h, tok.ctypes.data_as(_i32p), B, S, max_new_tokens, eos_id,
+            _fp(logits) if logits is not None else None, ids.ctypes.data_as(_i32p)))
+        self._B = B
+        return ids, logits
+
+    def last_timing(self):
+        """(prefill_ms, decode_ms) of the last generate, CUDA events."""
+        a, b = ctypes.c_float(), ctypes.c_float()
+        _check(load_library().moe_decoder_last_timing(self._h, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load_library().moe_decoder_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -245,7 +245,9 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
     const bool small = route_small_geometry(L, T, block, &kc, &stages);
     if (!small) MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
     prof_mark(L, 0, s);
-    if (block)
+    if (block && L.norm_rms)
+        MOE_CUDA(launch_rms_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, s));
+    else if (block)
         MOE_CUDA(launch_row_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, W.dev_err, s));
     if (small) {
         MOE_CUDA(launch_route_small(L, x, T, nr, decode, y, s));
@@ -791,6 +793,28 @@ int moe_set_post_norm(MoeHandle* h, const float* weight, const float* bias, floa
     MOE_CUDA(cudaMemcpy(L.norm_w, weight, bytes, cudaMemcpyHostToDevice));
     MOE_CUDA(cudaMemcpy(L.norm_b, bias, bytes, cudaMemcpyHostToDevice));
     L.norm_eps = eps;
+    L.norm_rms = false;
+    return MOE_OK;
+}
+
+int moe_set_post_rms_norm(MoeHandle* h, const float* weight, float eps) {
+    using namespace moe;
+    if (!h || !weight) return fail(MOE_ERR_INVALID, "null argument");
+    if (!(eps >= 0.0f)) return fail(MOE_ERR_INVALID, "eps must be >= 0");
+    if (!norm_supported(h->L.d))
+        return fail(MOE_ERR_UNSUPPORTED, "the fused norm needs d_model a multiple of 128");
+    DeviceGuard guard(h->L.cfg.device);
+    Layer& L = h->L;
+    const size_t bytes = sizeof(float) * L.d;
+    if (!L.norm_w) {
+        MOE_CUDA(dalloc(&L.norm_w, bytes, &L.weight_bytes));
+        MOE_CUDA(dalloc(&L.norm_b, bytes, &L.weight_bytes));
+    }
+    MOE_CUDA(cudaDeviceSynchronize());   // no forward may still read the old values
+    MOE_CUDA(cudaMemcpy(L.norm_w, weight, bytes, cudaMemcpyDefault));
+    MOE_CUDA(cudaMemset(L.norm_b, 0, bytes));
+    L.norm_eps = eps;
+    L.norm_rms = true;
     return MOE_OK;
 }
 

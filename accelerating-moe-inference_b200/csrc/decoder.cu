@@ -1,0 +1,1168 @@
+// Toy MoE decoder: whole-model greedy generation around
+// the MoE layers -- the counterpart of the reference's PhiTinyMoEModel
+// (include/model.h:8-30; generate src/model.cu:1575-2058, generate_decode
+// src/model.cu:2061-2104).
+//
+// Per layer, on the decoder's stream:
+//   rms_pack        x -> rms_norm(x) in the GEMM's A format (bf16, or tf32
+//                   hi + lo), and the projection's output zeroed
+//   qkv GEMM        the tcgen05 grouped GEMM with one group and an identity
+//                   row map (combine epilogue, weight 1): qkv = A . Wqkv^T
+//   rope_kv         rotate-half RoPE on q and k (tensor_ops::apply_rope,
+//                   src/tensor.cu:191-210); k and v into the KV cache
+//   attention       causal softmax(q k^T / sqrt(hd)) v per (sequence, head),
+//                   output straight into the A format
+//   o GEMM          x += A . Wo^T (the combine epilogue adds into the
+//                   residual stream itself)
+//   MoE block       x' = x + MoE(rms_norm(x)) (moe_block_forward_device with
+//                   the RMSNorm attached; norm applied inside the router and
+//                   the dispatch)
+// then rms_pack of each sequence's last row, the output-head GEMM against the
+// (tied) embedding matrix, and a greedy argmax.
+//
+// The reference's generate_decode re-runs the whole prefix for every new
+// token; here a KV cache [layer][sequence][head][position][head_dim] (fp32)
+// keeps keys and values, so a decode step processes one row per sequence.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "moe_internal.h"
+#include "ptx.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kDecErrToken = 1 << 12;   // a token id outside [0, vocab)
+
+// ------------------------------------------------------------ A-format stores
+// Columns c .. c+3 of row `row` of a [rows][ld] A operand: bf16 (kTf = false)
+// or the tf32 hi and lo planes of the 3xTF32 path.
+template <bool kTf>
+__device__ __forceinline__ void store_a4(void* a_hi, void* a_lo, size_t row, int ld, int c,
+                                         float4 f) {
+    if constexpr (kTf) {
+        float4 h, l;
+        h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+        h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+        h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+        h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+        *reinterpret_cast<float4*>(static_cast<float*>(a_hi) + row * ld + c) = h;
+        *reinterpret_cast<float4*>(static_cast<float*>(a_lo) + row * ld + c) = l;
+    } else {
+        __nv_bfloat162 lo2 = __floats2bfloat162_rn(f.x, f.y);
+        __nv_bfloat162 hi2 = __floats2bfloat162_rn(f.z, f.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&lo2);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi2);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a_hi) + row * ld + c) = packed;
+    }
+}
+
+template <bool kTf>
+__device__ __forceinline__ void store_a1(void* a_hi, void* a_lo, size_t row, int ld, int c,
+                                         float f) {
+    if constexpr (kTf) {
+        const float h = to_tf32(f);
+        static_cast<float*>(a_hi)[row * ld + c] = h;
+        static_cast<float*>(a_lo)[row * ld + c] = to_tf32(f - h);
+    } else {
+        static_cast<__nv_bfloat16*>(a_hi)[row * ld + c] = __float2bfloat16_rn(f);
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ------------------------------------------------------------ embedding
+// x[r] = embed[tok[r]]: one block per row.  An id outside [0, vocab) gives a
+// zero row and sets kDecErrToken.
+__global__ void __launch_bounds__(256)
+embed_gather_kernel(const int* __restrict__ tok, const float* __restrict__ embed, int vocab,
+                    int d, float* __restrict__ x, int* __restrict__ err) {
+    const int r = blockIdx.x;
+    const int t = tok[r];
+    const bool ok = t >= 0 && t < vocab;
+    if (!ok && threadIdx.x == 0) atomicOr(err, kDecErrToken);
+    const float4* src = reinterpret_cast<const float4*>(embed + (size_t)(ok ? t : 0) * d);
+    float4* dst = reinterpret_cast<float4*>(x + (size_t)r * d);
+    for (int v = threadIdx.x; v < d / 4; v += blockDim.x)
+        dst[v] = ok ? __ldg(src + v) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+}
+
+// ------------------------------------------------------------ RMSNorm -> A
+// One warp per packed row r < rows_pad.  Row r < T is row src0 + r * stride
+// of x, written as (x * inv) * w with inv = 1 / sqrt(sum x^2 / d + eps) (the
+// same arithmetic as the MoE block's norm); rows past T are zero.  The grid
+// also zeroes the n4 float4 at `zero` -- the output the following GEMM adds
+// into -- so that no separate memset sits between this kernel and the GEMM.
+template <bool kTf>
+__global__ void __launch_bounds__(256)
+rms_pack_kernel(const float* __restrict__ x, int src0, int stride, int T, int rows_pad, int d,
+                float eps, const float* __restrict__ w, void* __restrict__ a_hi,
+                void* __restrict__ a_lo, float4* __restrict__ zero, size_t zero_n4) {
+    const size_t gtid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t gthreads = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = gtid; i < zero_n4; i += gthreads) zero[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows_pad) return;
+    if (r >= T) {
+        for (int c = lane * 4; c < d; c += 128)
+            store_a4<kTf>(a_hi, a_lo, r, d, c, make_float4(0.0f, 0.0f, 0.0f, 0.0f));
+        return;
+    }
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(src0 + (size_t)r * stride) * d);
+    float ss = 0.0f;
+    for (int v = lane; v < d / 4; v += 32) {
+        const float4 a = __ldg(xr + v);
+        ss = __fmaf_rn(a.x, a.x, ss);
+        ss = __fmaf_rn(a.y, a.y, ss);
+        ss = __fmaf_rn(a.z, a.z, ss);
+        ss = __fmaf_rn(a.w, a.w, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (int v = lane; v < d / 4; v += 32) {
+        const float4 a = __ldg(xr + v), g = __ldg(w4 + v);
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(a.x, inv), g.x);
+        o.y = __fmul_rn(__fmul_rn(a.y, inv), g.y);
+        o.z = __fmul_rn(__fmul_rn(a.z, inv), g.z);
+        o.w = __fmul_rn(__fmul_rn(a.w, inv), g.w);
+        store_a4<kTf>(a_hi, a_lo, r, d, 4 * v, o);
+    }
+}
+
+// ------------------------------------------------------------ tile list
+// The grouped GEMM's tile list for a dense projection over T rows: one group
+// (expert 0), rows 0..T-1 in order, row r's output row r with weight 1;
+// rows T..rows_pad-1 are padding (token -1, weight 0).  Same fields as the
+// dispatch scan writes for an expert block.
+__global__ void dense_tiles_kernel(int T, int rows_pad, MTile* __restrict__ mtiles,
+                                   int* __restrict__ num_mtiles, MTile* __restrict__ ptiles,
+                                   int* __restrict__ num_ptiles, int* __restrict__ row_token,
+                                   float* __restrict__ row_weight) {
+    const int mc = (T + kTileM - 1) / kTileM;
+    const int qc = (mc + 1) / 2;
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows_pad; r += gridDim.x * blockDim.x) {
+        row_token[r] = r < T ? r : -1;
+        row_weight[r] = r < T ? 1.0f : 0.0f;
+    }
+    if (blockIdx.x != 0) return;
+    for (int i = threadIdx.x; i < mc; i += blockDim.x) {
+        MTile mt;
+        mt.expert = 0; mt.row0 = i * kTileM; mt.rows = min(kTileM, T - i * kTileM);
+        mt.mstart = 0; mt.mcount = mc; mt.pad[0] = mt.pad[1] = mt.pad[2] = 0;
+        mtiles[i] = mt;
+    }
+    for (int i = threadIdx.x; i < qc; i += blockDim.x) {
+        MTile pt;
+        pt.expert = 0; pt.row0 = 2 * i * kTileM; pt.rows = min(kTileM, T - 2 * i * kTileM);
+        pt.mstart = 0; pt.mcount = qc;
+        pt.pad[0] = max(0, min(kTileM, T - (2 * i + 1) * kTileM));
+        pt.pad[1] = pt.pad[2] = 0;
+        ptiles[i] = pt;
+    }
+    if (threadIdx.x == 0) {
+        *num_mtiles = mc;
+        *num_ptiles = qc;
+    }
+}
+
+// ------------------------------------------------------------ RoPE + cache
+// Row r of qkv [T][3d] is token r % rps of sequence r / rps, at position
+// pos0 + r % rps.  q and k are rotated in the reference's rotate-half form
+// (tensor_ops::apply_rope, src/tensor.cu:191-210): for j < hd/2,
+//   x_j' = x_j cos - x_{j+hd/2} sin,  x_{j+hd/2}' = x_{j+hd/2} cos + x_j sin
+// with (cos, sin) of position p and pair j from the table [max_seq][hd/2][2].
+// q stays in qkv (rotated); k and v go to the cache at their position.
+template <int HD>
+__global__ void __launch_bounds__(256)
+rope_kv_kernel(float* __restrict__ qkv, int rps, int pos0, int H, const float2* __restrict__ rope,
+               float* __restrict__ kc, float* __restrict__ vc, int max_seq) {
+    constexpr int kHalf = HD / 2;
+    const int r = blockIdx.x;
+    const int b = r / rps, pos = pos0 + r % rps;
+    const int d = H * HD;
+    float* q = qkv + (size_t)r * 3 * d;
+    const float* k = q + d;
+    const float* v = q + 2 * d;
+    for (int i = threadIdx.x; i < H * kHalf; i += blockDim.x) {
+        const int h = i / kHalf, j = i % kHalf;
+        const float2 cs = __ldg(rope + (size_t)pos * kHalf + j);
+        const float q0 = q[h * HD + j], q1 = q[h * HD + j + kHalf];
+        q[h * HD + j] = q0 * cs.x - q1 * cs.y;
+        q[h * HD + j + kHalf] = q1 * cs.x + q0 * cs.y;
+        const float k0 = k[h * HD + j], k1 = k[h * HD + j + kHalf];
+        float* kd = kc + (((size_t)b * H + h) * max_seq + pos) * HD;
+        kd[j] = k0 * cs.x - k1 * cs.y;
+        kd[j + kHalf] = k1 * cs.x + k0 * cs.y;
+    }
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const int h = i / HD, c = i % HD;
+        vc[(((size_t)b * H + h) * max_seq + pos) * HD + c] = v[i];
+    }
+}
+
+// ------------------------------------------------------------ attention
+// Prefill: causal attention of the S queries of one sequence and head over
+// keys 0..S-1, a 64-query block per CTA, keys in blocks of 64 with an online
+// softmax.  256 threads: thread (ti, tj) = (tid / 16, tid % 16) scores
+// queries ti + 16a against keys tj + 16b (a, b < 4) and accumulates the
+// output of queries ti + 16a in dims 4 tj + 64 u .. +3.  Rows are padded to
+// hd + 4 floats so the float4 shared loads of 16 different rows fall in
+// different banks.  Output: row b*S + q of the A operand, cols h*hd..
+constexpr int kAttBQ = 64;
+constexpr int kAttBK = 64;
+
+template <int HD>
+struct AttnSmem {
+    static constexpr int kLd = HD + 4;
+    static constexpr int kLdP = kAttBK + 4;
+    static constexpr size_t kBytes =
+        sizeof(float) * ((size_t)kAttBQ * kLd + 2 * (size_t)kAttBK * kLd + (size_t)kAttBQ * kLdP);
+};
+
+template <int HD, bool kTf>
+__global__ void __launch_bounds__(256)
+attn_prefill_kernel(const float* __restrict__ qkv, int S, int H, const float* __restrict__ kc,
+                    const float* __restrict__ vc, int max_seq, float scale,
+                    void* __restrict__ a_hi, void* __restrict__ a_lo) {
+    using Sm = AttnSmem<HD>;
+    constexpr int kLd = Sm::kLd, kLdP = Sm::kLdP;
+    constexpr int kU = HD / 64;   // 64-dim slices per thread row
+    extern __shared__ __align__(16) float sm[];
+    float* sQ = sm;
+    float* sK = sQ + kAttBQ * kLd;
+    float* sV = sK + kAttBK * kLd;
+    float* sP = sV + kAttBK * kLd;
+    const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
+    const int q0 = qb * kAttBQ;
+    const int d = H * HD;
+    const float* kbase = kc + ((size_t)b * H + h) * max_seq * HD;
+    const float* vbase = vc + ((size_t)b * H + h) * max_seq * HD;
+
+    for (int i = tid; i < kAttBQ * HD / 4; i += 256) {
+        const int r = i / (HD / 4), c4 = i % (HD / 4);
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (q0 + r < S) {
+            v = *reinterpret_cast<const float4*>(qkv + ((size_t)b * S + q0 + r) * 3 * d + h * HD + 4 * c4);
+            v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+        }
+        *reinterpret_cast<float4*>(sQ + r * kLd + 4 * c4) = v;
+    }
+    float m[4], l[4], o[4][4 * kU];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        m[a] = -INFINITY;
+        l[a] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4 * kU; ++c) o[a][c] = 0.0f;
+    }
+    const int last_q = min(q0 + kAttBQ, S) - 1;
+    for (int k0 = 0; k0 <= last_q; k0 += kAttBK) {
+        __syncthreads();   // the previous block's sK / sV / sP reads are done
+        for (int i = tid; i < kAttBK * HD / 4; i += 256) {
+            const int r = i / (HD / 4), c4 = i % (HD / 4);
+            float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
+            if (k0 + r < S) {
+                kv = *reinterpret_cast<const float4*>(kbase + (size_t)(k0 + r) * HD + 4 * c4);
+                vv = *reinterpret_cast<const float4*>(vbase + (size_t)(k0 + r) * HD + 4 * c4);
+            }
+            *reinterpret_cast<float4*>(sK + r * kLd + 4 * c4) = kv;
+            *reinterpret_cast<float4*>(sV + r * kLd + 4 * c4) = vv;
+        }
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) s[a][bb] = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < HD; c += 4) {
+            float4 qv[4], kv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+                qv[a] = *reinterpret_cast<const float4*>(sQ + (ti + 16 * a) * kLd + c);
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb)
+                kv[bb] = *reinterpret_cast<const float4*>(sK + (tj + 16 * bb) * kLd + c);
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int bb = 0; bb < 4; ++bb) {
+                    s[a][bb] = fmaf(qv[a].x, kv[bb].x, s[a][bb]);
+                    s[a][bb] = fmaf(qv[a].y, kv[bb].y, s[a][bb]);
+                    s[a][bb] = fmaf(qv[a].z, kv[bb].z, s[a][bb]);
+                    s[a][bb] = fmaf(qv[a].w, kv[bb].w, s[a][bb]);
+                }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const int qpos = q0 + ti + 16 * a;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                const int kpos = k0 + tj + 16 * bb;
+                if (kpos > qpos || kpos >= S) s[a][bb] = -INFINITY;
+                mt = fmaxf(mt, s[a][bb]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1)
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+            const float mn = fmaxf(m[a], mt);
+            // Every visited block holds at least one key at or before each
+            // valid query (key k0 <= q0); rows past S may be all -inf.
+            const float corr = mn == -INFINITY ? 1.0f : expf(m[a] - mn);
+            m[a] = mn;
+            float ps = 0.0f;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                const float p = s[a][bb] == -INFINITY ? 0.0f : expf(s[a][bb] - mn);
+                sP[(ti + 16 * a) * kLdP + tj + 16 * bb] = p;
+                ps += p;
+            }
+            l[a] = l[a] * corr + ps;
+#pragma unroll
+            for (int c = 0; c < 4 * kU; ++c) o[a][c] *= corr;
+        }
+        __syncthreads();
+        const int nk = min(kAttBK, last_q + 1 - k0);
+#pragma unroll 2
+        for (int j = 0; j < nk; ++j) {
+            float4 vv[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u)
+                vv[u] = *reinterpret_cast<const float4*>(sV + j * kLd + 4 * tj + 64 * u);
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+                const float p = sP[(ti + 16 * a) * kLdP + j];
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    o[a][4 * u + 0] = fmaf(p, vv[u].x, o[a][4 * u + 0]);
+                    o[a][4 * u + 1] = fmaf(p, vv[u].y, o[a][4 * u + 1]);
+                    o[a][4 * u + 2] = fmaf(p, vv[u].z, o[a][4 * u + 2]);
+                    o[a][4 * u + 3] = fmaf(p, vv[u].w, o[a][4 * u + 3]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        float lt = l[a];
+#pragma unroll
+        for (int off = 1; off < 16; off <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+        const int q = q0 + ti + 16 * a;
+        if (q >= S) continue;
+        const float il = 1.0f / lt;
+        const size_t row = (size_t)b * S + q;
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            store_a4<kTf>(a_hi, a_lo, row, d, h * HD + 4 * tj + 64 * u,
+                          make_float4(o[a][4 * u] * il, o[a][4 * u + 1] * il,
+                                      o[a][4 * u + 2] * il, o[a][4 * u + 3] * il));
+    }
+}
+
+// Decode: one query per (sequence, head) at position pos over keys 0..pos.
+// 128 threads; warps score keys round-robin (one warp-wide dot each), the
+// block takes the softmax over the scores in shared memory, and thread t
+// accumulates dim t % hd over the keys j = t / hd (mod 128 / hd).
+constexpr int kDecThreads = 128;
+
+template <int HD, bool kTf>
+__global__ void __launch_bounds__(kDecThreads)
+attn_decode_kernel(const float* __restrict__ qkv, int pos, int H, const float* __restrict__ kc,
+                   const float* __restrict__ vc, int max_seq, float scale,
+                   void* __restrict__ a_hi, void* __restrict__ a_lo) {
+    constexpr int kPer = HD / 32;             // q values per lane
+    constexpr int kParts = kDecThreads / HD;  // key classes of the value pass
+    extern __shared__ __align__(16) float sS[];   // [max_seq] scores, then probabilities
+    __shared__ float red[kDecThreads / 32];
+    __shared__ float part[kDecThreads];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int d = H * HD;
+    const int n = pos + 1;
+    const float* q = qkv + (size_t)b * 3 * d + h * HD;
+    const float* kbase = kc + ((size_t)b * H + h) * max_seq * HD;
+    const float* vbase = vc + ((size_t)b * H + h) * max_seq * HD;
+    float qv[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) qv[i] = q[lane * kPer + i] * scale;
+    for (int j = warp; j < n; j += kDecThreads / 32) {
+        const float* kr = kbase + (size_t)j * HD + lane * kPer;
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) acc = fmaf(qv[i], kr[i], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) sS[j] = acc;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = tid; j < n; j += kDecThreads) mx = fmaxf(mx, sS[j]);
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < kDecThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = tid; j < n; j += kDecThreads) {
+        const float p = expf(sS[j] - mx);
+        sS[j] = p;
+        sum += p;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kDecThreads / 32; ++w) sum += red[w];
+    const int c = tid % HD, cls = tid / HD;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int j = cls;
+    for (; j + 3 * kParts < n; j += 4 * kParts) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            acc[u] = fmaf(sS[j + u * kParts], vbase[(size_t)(j + u * kParts) * HD + c], acc[u]);
+    }
+    for (; j < n; j += kParts) acc[0] = fmaf(sS[j], vbase[(size_t)j * HD + c], acc[0]);
+    part[tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    __syncthreads();
+    if (tid < HD) {
+        float v = part[tid];
+#pragma unroll
+        for (int p = 1; p < kParts; ++p) v += part[tid + p * HD];
+        store_a1<kTf>(a_hi, a_lo, b, d, h * HD + tid, v / sum);
+    }
+}
+
+// ------------------------------------------------------------ argmax
+// Greedy choice per row of logits [B][V], as generate_decode picks it
+// (src/model.cu:2081-2089): the first index holding the maximum, scanning
+// with a strict '>' from index 0 -- so NaNs are never chosen, except that a
+// NaN at index 0 yields 0.  Writes the id to ids[b] and, if `seq_out`, to
+// seq_out[b * seq_ld + step] (-1 once the sequence has emitted eos).
+__global__ void __launch_bounds__(1024)
+argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ ids,
+              int* __restrict__ seq_out, int seq_ld, int step, int eos, int* __restrict__ done) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* row = logits + (size_t)b * V;
+    float best = -INFINITY;
+    int bi = -1;
+    for (int v = tid; v < V; v += blockDim.x) {
+        const float x = row[v];
+        if (x > best || (bi < 0 && x == best)) { best = x; bi = v; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+        best = lane < (int)(blockDim.x >> 5) ? sv[lane] : -INFINITY;
+        bi = lane < (int)(blockDim.x >> 5) ? si[lane] : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            int id = bi < 0 || row[0] != row[0] ? 0 : bi;
+            if (done) {
+                if (done[b]) id = -1;
+                else if (id == eos) done[b] = 1;
+            }
+            ids[b] = id < 0 ? 0 : id;
+            if (seq_out) seq_out[(size_t)b * seq_ld + step] = id;
+        }
+    }
+}
+
+// ------------------------------------------------------------ dense projection
+// y [rows][N] (+)= A [rows][K] . W[N][K]^T on the expert GEMM: a Layer with
+// one expert whose "down" weights are W (d = N, ffp = K), reading the shared
+// A operand and tile list of the decoder.
+struct Dense {
+    Layer L;
+};
+
+void free_dense(Dense& D) {
+    if (D.L.w2_hi) cudaFree(D.L.w2_hi);
+    if (D.L.w2_lo) cudaFree(D.L.w2_lo);
+    D.L.w2_hi = D.L.w2_lo = nullptr;
+}
+
+}  // namespace
+}  // namespace moe
+
+// ============================================================ the model
+struct MoeDecoder {
+    MoeDecoderConfig cfg{};
+    int d = 0, H = 0, HD = 0, V = 0, nl = 0;
+    int max_rows = 0;         // max_batch * max_seq
+    int a_rows = 0;           // A operand rows (max_rows rounded up to 256)
+    std::vector<float*> attn_norm;
+    std::vector<moe::Dense> qkv, wo;
+    std::vector<MoeHandle*> moe;
+    moe::Dense head;
+    float* embed = nullptr;
+    float* final_norm = nullptr;
+    float2* rope = nullptr;   // [max_seq][head_dim / 2] (cos, sin)
+    float* kc = nullptr;      // [n_layers][max_batch][H][max_seq][head_dim]
+    float* vc = nullptr;
+    float* x = nullptr;       // [max_rows][d] residual stream (ping)
+    float* x2 = nullptr;      // (pong)
+    float* qkvbuf = nullptr;  // [max_rows][3d]
+    float* logits = nullptr;  // [max_batch][vocab]
+    float* gen_logits = nullptr;   // [max_batch][gen_cap][vocab] (generate)
+    size_t gen_cap = 0;
+    int* tok = nullptr;       // [max_rows]
+    int* next = nullptr;      // [max_batch]
+    int* seq_ids = nullptr;   // [max_batch][max_seq] generated ids
+    int* done = nullptr;      // [max_batch]
+    void* a_hi = nullptr;
+    void* a_lo = nullptr;
+    CUtensorMap tm_a_hi{}, tm_a_lo{};
+    moe::MTile* mtiles = nullptr;
+    moe::MTile* ptiles = nullptr;
+    int* num_mtiles = nullptr;
+    int* num_ptiles = nullptr;
+    int* row_token = nullptr;
+    float* row_weight = nullptr;
+    int* dev_err = nullptr;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[3] = {};
+    float t_prefill = 0.0f, t_decode = 0.0f;
+    int B = 0, pos = 0;       // sequences of the current batch, next position
+    size_t bytes = 0;
+};
+
+namespace moe {
+namespace {
+
+#define DEC_CUDA(call)                                                                 \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess)                                                         \
+            return report_error(MOE_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+#define DEC_RC(call)              \
+    do {                          \
+        int rc_ = (call);         \
+        if (rc_) return rc_;      \
+    } while (0)
+
+struct DecDeviceGuard {
+    int prev = -1;
+    explicit DecDeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DecDeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+cudaError_t dec_alloc(MoeDecoder& m, T** p, size_t bytes) {
+    *p = nullptr;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes ? bytes : 256);
+    if (e == cudaSuccess) m.bytes += bytes;
+    return e;
+}
+
+int round_up(int v, int g) { return (v + g - 1) / g * g; }
+
+// W = the listed fp32 row blocks stacked ([sum rows][K]), host or device
+// pointers, converted into the projection's weight planes.
+int make_dense(MoeDecoder& m, Dense& D, const float* const* parts, const int* part_rows,
+               int nparts, int K) {
+    Layer& L = D.L;
+    int N = 0;
+    for (int i = 0; i < nparts; ++i) N += part_rows[i];
+    L.cfg.precision = m.cfg.precision;
+    L.cfg.device = m.cfg.device;
+    L.d = N;
+    L.ff = K;
+    L.ffp = K;
+    L.E = 1;
+    L.E_route = 1;
+    L.k = 1;
+    L.sm_count = m.sm_count;
+    L.gemm_variant = MOE_GEMM_AUTO;
+    L.profile = false;
+    const bool tf = three_pass(L);
+    const size_t eb = elem_bytes(L);
+    DEC_CUDA(dec_alloc(m, &L.w2_hi, eb * N * K));
+    if (tf) DEC_CUDA(dec_alloc(m, &L.w2_lo, (size_t)4 * N * K));
+    float* stage = nullptr;
+    DEC_CUDA(cudaMalloc(&stage, sizeof(float) * (size_t)N * K));
+    size_t off = 0;
+    int rc = MOE_OK;
+    for (int i = 0; i < nparts && !rc; ++i) {
+        const size_t n = (size_t)part_rows[i] * K;
+        cudaError_t e = cudaMemcpyAsync(stage + off, parts[i], sizeof(float) * n, cudaMemcpyDefault,
+                                        m.stream);
+        if (e != cudaSuccess) rc = report_error(MOE_ERR_CUDA, std::string("weight copy: ") + cudaGetErrorString(e));
+        off += n;
+    }
+    if (!rc) {
+        cudaError_t e = convert_down(L, 0, stage, m.stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(m.stream);
+        if (e != cudaSuccess) rc = report_error(MOE_ERR_CUDA, std::string("weight conversion: ") + cudaGetErrorString(e));
+    }
+    cudaFree(stage);
+    if (rc) return rc;
+    const uint32_t box_k = tf ? 32 : 64;
+    std::string err;
+    const bool bf = !tf;
+    if (!make_tmap_2d(&L.tm_w2_hi, L.w2_hi, bf, K, N, box_k, kTileN, &err) ||
+        !make_tmap_2d(&L.tm_w2_hi2, L.w2_hi, bf, K, N, box_k, kTileN / 2, &err))
+        return report_error(MOE_ERR_CUDA, err);
+    if (tf) {
+        if (!make_tmap_2d(&L.tm_w2_lo, L.w2_lo, false, K, N, box_k, kTileN, &err) ||
+            !make_tmap_2d(&L.tm_w2_lo2, L.w2_lo, false, K, N, box_k, kTileN / 2, &err))
+            return report_error(MOE_ERR_CUDA, err);
+    } else {
+        L.tm_w2_lo = L.tm_w2_hi;
+        L.tm_w2_lo2 = L.tm_w2_hi2;
+    }
+    Workspace& W = L.ws;
+    W.mtiles = m.mtiles;
+    W.num_mtiles = m.num_mtiles;
+    W.ptiles = m.ptiles;
+    W.num_ptiles = m.num_ptiles;
+    W.row_token = m.row_token;
+    W.row_weight = m.row_weight;
+    W.h_hi = m.a_hi;
+    W.h_lo = m.a_lo;
+    W.tm_h_hi = m.tm_a_hi;
+    W.tm_h_lo = m.tm_a_lo;
+    W.dev_err = m.dev_err;
+    W.cap_rows = m.a_rows;
+    return MOE_OK;
+}
+
+bool tf_mode(const MoeDecoder& m) { return m.cfg.precision == MOE_PREC_FP32; }
+
+float* layer_kc(MoeDecoder& m, int l) {
+    return m.kc + (size_t)l * m.cfg.max_batch * m.H * m.cfg.max_seq * m.HD;
+}
+float* layer_vc(MoeDecoder& m, int l) {
+    return m.vc + (size_t)l * m.cfg.max_batch * m.H * m.cfg.max_seq * m.HD;
+}
+
+cudaError_t launch_tiles(MoeDecoder& m, int T) {
+    const int rows_pad = round_up(T, 2 * kTileM);
+    dense_tiles_kernel<<<std::min((rows_pad + 255) / 256, 4 * m.sm_count), 256, 0, m.stream>>>(
+        T, rows_pad, m.mtiles, m.num_mtiles, m.ptiles, m.num_ptiles, m.row_token, m.row_weight);
+    return cudaGetLastError();
+}
+
+// rms_norm(rows src0 + r * stride of x, r < T) -> A, zeroing `zero` [zero_n] floats.
+cudaError_t launch_rms_pack(MoeDecoder& m, const float* x, int src0, int stride, int T,
+                            const float* w, float* zero, size_t zero_n) {
+    const int rows_pad = round_up(T, 2 * kTileM);
+    const int grid = (rows_pad + 7) / 8;
+    const float eps = m.cfg.rms_eps;
+    if (tf_mode(m))
+        rms_pack_kernel<true><<<grid, 256, 0, m.stream>>>(x, src0, stride, T, rows_pad, m.d, eps, w,
+                                                          m.a_hi, m.a_lo,
+                                                          reinterpret_cast<float4*>(zero), zero_n / 4);
+    else
+        rms_pack_kernel<false><<<grid, 256, 0, m.stream>>>(x, src0, stride, T, rows_pad, m.d, eps,
+                                                           w, m.a_hi, m.a_lo,
+                                                           reinterpret_cast<float4*>(zero), zero_n / 4);
+    return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, int pos, bool prefill) {
+    const float scale = 1.0f / sqrtf((float)HD);
+    if (prefill) {
+        const size_t smem = AttnSmem<HD>::kBytes;
+        dim3 grid((S + kAttBQ - 1) / kAttBQ, m.H, B);
+        if (tf_mode(m)) {
+            auto k = attn_prefill_kernel<HD, true>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, 256, smem, m.stream>>>(m.qkvbuf, S, m.H, layer_kc(m, l), layer_vc(m, l),
+                                             m.cfg.max_seq, scale, m.a_hi, m.a_lo);
+        } else {
+            auto k = attn_prefill_kernel<HD, false>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, 256, smem, m.stream>>>(m.qkvbuf, S, m.H, layer_kc(m, l), layer_vc(m, l),
+                                             m.cfg.max_seq, scale, m.a_hi, m.a_lo);
+        }
+    } else {
+        const size_t smem = sizeof(float) * (size_t)m.cfg.max_seq;
+        dim3 grid(m.H, B);
+        if (tf_mode(m)) {
+            auto k = attn_decode_kernel<HD, true>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, kDecThreads, smem, m.stream>>>(m.qkvbuf, pos, m.H, layer_kc(m, l),
+                                                     layer_vc(m, l), m.cfg.max_seq, scale, m.a_hi, m.a_lo);
+        } else {
+            auto k = attn_decode_kernel<HD, false>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, kDecThreads, smem, m.stream>>>(m.qkvbuf, pos, m.H, layer_kc(m, l),
+                                                     layer_vc(m, l), m.cfg.max_seq, scale, m.a_hi, m.a_lo);
+        }
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_kv(MoeDecoder& m, int l, int T, int rps, int pos0) {
+    if (m.HD == 128)
+        rope_kv_kernel<128><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, pos0, m.H, m.rope, layer_kc(m, l),
+                                                     layer_vc(m, l), m.cfg.max_seq);
+    else
+        rope_kv_kernel<64><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, pos0, m.H, m.rope, layer_kc(m, l),
+                                                    layer_vc(m, l), m.cfg.max_seq);
+    return cudaGetLastError();
+}
+
+// One decoder layer over T rows: B sequences of rps rows each, the first at
+// position pos0 (prefill: rps = S, pos0 = 0; decode: rps = 1, pos0 = pos).
+int run_layer(MoeDecoder& m, int l, int B, int T, int rps, int pos0, bool prefill) {
+    DEC_CUDA(launch_rms_pack(m, m.x, 0, 1, T, m.attn_norm[l], m.qkvbuf, (size_t)T * 3 * m.d));
+    DEC_CUDA(launch_expert_gemm_rows(m.qkv[l].L, T, m.qkvbuf, m.stream, 1));
+    DEC_CUDA(launch_rope_kv(m, l, T, rps, pos0));
+    if (m.HD == 128)
+        DEC_CUDA(launch_attention_t<128>(m, l, B, rps, pos0, prefill));
+    else
+        DEC_CUDA(launch_attention_t<64>(m, l, B, rps, pos0, prefill));
+    DEC_CUDA(launch_expert_gemm_rows(m.wo[l].L, T, m.x, m.stream, 1));
+    DEC_RC(moe_block_forward_device(m.moe[l], m.x, m.x2, T, m.stream));
+    std::swap(m.x, m.x2);
+    return MOE_OK;
+}
+
+// Final norm of row src0 + b * stride (b < B), the output head into
+// m.logits, and the greedy ids (into seq_ids[b][step] when step >= 0).
+int run_head(MoeDecoder& m, int B, int src0, int stride, int step, int eos) {
+    DEC_CUDA(launch_tiles(m, B));
+    DEC_CUDA(launch_rms_pack(m, m.x, src0, stride, B, m.final_norm, m.logits, (size_t)B * m.V));
+    DEC_CUDA(launch_expert_gemm_rows(m.head.L, B, m.logits, m.stream, 1));
+    argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, step >= 0 ? m.seq_ids : nullptr,
+                                            m.cfg.max_seq, step, eos, step >= 0 ? m.done : nullptr);
+    DEC_CUDA(cudaGetLastError());
+    return MOE_OK;
+}
+
+// Prefill of B sequences of S tokens from m.tok.
+int run_prefill(MoeDecoder& m, int B, int S, int step, int eos) {
+    const int T = B * S;
+    DEC_CUDA(launch_tiles(m, T));
+    embed_gather_kernel<<<T, 256, 0, m.stream>>>(m.tok, m.embed, m.V, m.d, m.x, m.dev_err);
+    DEC_CUDA(cudaGetLastError());
+    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, T, S, 0, true));
+    DEC_RC(run_head(m, B, S - 1, S, step, eos));
+    m.B = B;
+    m.pos = S;
+    return MOE_OK;
+}
+
+// One decode step: token ids from `tok` (device, [B]) at position m.pos.
+int run_decode(MoeDecoder& m, const int* tok, int step, int eos) {
+    const int B = m.B;
+    DEC_CUDA(launch_tiles(m, B));
+    embed_gather_kernel<<<B, 256, 0, m.stream>>>(tok, m.embed, m.V, m.d, m.x, m.dev_err);
+    DEC_CUDA(cudaGetLastError());
+    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, B, 1, m.pos, false));
+    DEC_RC(run_head(m, B, 0, 1, step, eos));
+    ++m.pos;
+    return MOE_OK;
+}
+
+int check_dev_err(MoeDecoder& m) {
+    int flag = 0;
+    DEC_CUDA(cudaMemcpy(&flag, m.dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!flag) return MOE_OK;
+    cudaMemset(m.dev_err, 0, sizeof(int));
+    if (flag & kDecErrToken) return report_error(MOE_ERR_INVALID, "a token id is outside [0, vocab)");
+    char buf[96];
+    std::snprintf(buf, sizeof buf, "a device-side wait timed out (flags 0x%x)", flag);
+    return report_error(MOE_ERR_TIMEOUT, buf);
+}
+
+int validate(const MoeDecoderConfig& c) {
+    auto bad = [](int code, const char* msg) { return report_error(code, msg); };
+    if (c.n_layers < 1) return bad(MOE_ERR_INVALID, "n_layers must be >= 1");
+    if (c.head_dim != 64 && c.head_dim != 128) return bad(MOE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (c.n_heads < 1 || c.d_model != c.n_heads * c.head_dim)
+        return bad(MOE_ERR_UNSUPPORTED, "d_model must equal n_heads * head_dim");
+    if (c.d_model % 128 != 0) return bad(MOE_ERR_UNSUPPORTED, "d_model must be a multiple of 128");
+    if (c.vocab < 32 || c.vocab % 32 != 0) return bad(MOE_ERR_UNSUPPORTED, "vocab must be a positive multiple of 32");
+    if (c.max_batch < 1 || c.max_seq < 1) return bad(MOE_ERR_INVALID, "max_batch and max_seq must be >= 1");
+    if ((size_t)c.max_seq * 4 > 200 * 1024) return bad(MOE_ERR_UNSUPPORTED, "max_seq must be <= 51200");
+    if ((long long)c.max_batch * c.max_seq > (1 << 22)) return bad(MOE_ERR_UNSUPPORTED, "max_batch * max_seq too large");
+    if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16) return bad(MOE_ERR_INVALID, "unknown precision");
+    if (!(c.rms_eps >= 0.0f) || !(c.rope_base > 0.0f)) return bad(MOE_ERR_INVALID, "rms_eps >= 0 and rope_base > 0 required");
+    return MOE_OK;
+}
+
+void destroy(MoeDecoder* m) {
+    if (!m) return;
+    DecDeviceGuard guard(m->cfg.device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (MoeHandle* h : m->moe) moe_destroy(h);
+    for (auto& D : m->qkv) free_dense(D);
+    for (auto& D : m->wo) free_dense(D);
+    free_dense(m->head);
+    for (float* p : m->attn_norm) cudaFree(p);
+    void* bufs[] = {m->embed, m->final_norm, m->rope, m->kc, m->vc, m->x, m->x2, m->qkvbuf,
+                    m->logits, m->gen_logits, m->tok, m->next, m->seq_ids, m->done, m->a_hi,
+                    m->a_lo, m->mtiles, m->ptiles, m->num_mtiles, m->num_ptiles, m->row_token,
+                    m->row_weight, m->dev_err};
+    for (void* p : bufs)
+        if (p) cudaFree(p);
+    for (cudaEvent_t e : m->ev)
+        if (e) cudaEventDestroy(e);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int create(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w, bool device_ptrs,
+           MoeDecoder** out) {
+    if (!cfg || !w || !out) return report_error(MOE_ERR_INVALID, "null argument");
+    *out = nullptr;
+    DEC_RC(validate(*cfg));
+    if (!w->embed || !w->final_norm || !w->attn_norm || !w->wq || !w->wk || !w->wv || !w->wo ||
+        !w->ffn_norm || !w->router || !w->w1 || !w->w3 || !w->w2)
+        return report_error(MOE_ERR_INVALID, "missing weight pointers");
+    int ndev = 0;
+    DEC_CUDA(cudaGetDeviceCount(&ndev));
+    if (cfg->device < 0 || cfg->device >= ndev) return report_error(MOE_ERR_INVALID, "no such device");
+    DecDeviceGuard guard(cfg->device);
+    int major = 0, minor = 0;
+    DEC_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, cfg->device));
+    DEC_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, cfg->device));
+    if (major != 10 || minor != 0)
+        return report_error(MOE_ERR_UNSUPPORTED, "libmoe_b200 is built for sm_100a (B200) only");
+    std::unique_ptr<MoeDecoder, void (*)(MoeDecoder*)> m(new MoeDecoder(), destroy);
+    MoeDecoder& M = *m;
+    M.cfg = *cfg;
+    M.d = cfg->d_model;
+    M.H = cfg->n_heads;
+    M.HD = cfg->head_dim;
+    M.V = cfg->vocab;
+    M.nl = cfg->n_layers;
+    M.max_rows = cfg->max_batch * cfg->max_seq;
+    M.a_rows = round_up(std::max(M.max_rows, cfg->max_batch), 2 * kTileM);
+    DEC_CUDA(cudaDeviceGetAttribute(&M.sm_count, cudaDevAttrMultiProcessorCount, cfg->device));
+    DEC_CUDA(cudaStreamCreateWithFlags(&M.stream, cudaStreamNonBlocking));
+    for (auto& e : M.ev) DEC_CUDA(cudaEventCreate(&e));
+    const size_t d = M.d, V = M.V, rows = M.max_rows, B = cfg->max_batch, S = cfg->max_seq;
+    const bool tf = tf_mode(M);
+    const size_t eb = tf ? 4 : 2;
+    // Activations, caches, A operand and tile list.
+    DEC_CUDA(dec_alloc(M, &M.x, sizeof(float) * rows * d));
+    DEC_CUDA(dec_alloc(M, &M.x2, sizeof(float) * rows * d));
+    DEC_CUDA(dec_alloc(M, &M.qkvbuf, sizeof(float) * rows * 3 * d));
+    DEC_CUDA(dec_alloc(M, &M.logits, sizeof(float) * B * V));
+    DEC_CUDA(dec_alloc(M, &M.tok, sizeof(int) * rows));
+    DEC_CUDA(dec_alloc(M, &M.next, sizeof(int) * B));
+    DEC_CUDA(dec_alloc(M, &M.seq_ids, sizeof(int) * B * S));
+    DEC_CUDA(dec_alloc(M, &M.done, sizeof(int) * B));
+    const size_t cache = (size_t)M.nl * B * M.H * S * M.HD;
+    DEC_CUDA(dec_alloc(M, &M.kc, sizeof(float) * cache));
+    DEC_CUDA(dec_alloc(M, &M.vc, sizeof(float) * cache));
+    DEC_CUDA(dec_alloc(M, &M.a_hi, eb * (size_t)M.a_rows * d));
+    if (tf) DEC_CUDA(dec_alloc(M, &M.a_lo, (size_t)4 * M.a_rows * d));
+    const int max_mt = M.a_rows / kTileM + 2;
+    DEC_CUDA(dec_alloc(M, &M.mtiles, sizeof(MTile) * max_mt));
+    DEC_CUDA(dec_alloc(M, &M.ptiles, sizeof(MTile) * max_mt));
+    DEC_CUDA(dec_alloc(M, &M.num_mtiles, sizeof(int)));
+    DEC_CUDA(dec_alloc(M, &M.num_ptiles, sizeof(int)));
+    DEC_CUDA(dec_alloc(M, &M.row_token, sizeof(int) * M.a_rows));
+    DEC_CUDA(dec_alloc(M, &M.row_weight, sizeof(float) * M.a_rows));
+    DEC_CUDA(dec_alloc(M, &M.dev_err, sizeof(int)));
+    DEC_CUDA(cudaMemset(M.dev_err, 0, sizeof(int)));
+    DEC_CUDA(cudaMemset(M.a_hi, 0, eb * (size_t)M.a_rows * d));
+    if (tf) DEC_CUDA(cudaMemset(M.a_lo, 0, (size_t)4 * M.a_rows * d));
+    {
+        std::string err;
+        const uint32_t box_k = tf ? 32 : 64;
+        if (!make_tmap_2d(&M.tm_a_hi, M.a_hi, !tf, d, M.a_rows, box_k, kTileM, &err))
+            return report_error(MOE_ERR_CUDA, err);
+        if (tf) {
+            if (!make_tmap_2d(&M.tm_a_lo, M.a_lo, false, d, M.a_rows, box_k, kTileM, &err))
+                return report_error(MOE_ERR_CUDA, err);
+        } else {
+            M.tm_a_lo = M.tm_a_hi;
+        }
+    }
+    // RoPE table, in double: (cos, sin) of p * base^(-2j / hd).
+    {
+        const int half = M.HD / 2;
+        std::vector<float2> tab((size_t)S * half);
+        for (size_t p = 0; p < S; ++p)
+            for (int j = 0; j < half; ++j) {
+                const double inv = std::pow((double)cfg->rope_base, -2.0 * j / (double)M.HD);
+                const double a = (double)p * inv;
+                tab[p * half + j] = make_float2((float)std::cos(a), (float)std::sin(a));
+            }
+        DEC_CUDA(dec_alloc(M, &M.rope, sizeof(float2) * tab.size()));
+        DEC_CUDA(cudaMemcpy(M.rope, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice));
+    }
+    // Embedding (gather copy and output head) and norms.
+    DEC_CUDA(dec_alloc(M, &M.embed, sizeof(float) * V * d));
+    DEC_CUDA(cudaMemcpy(M.embed, w->embed, sizeof(float) * V * d, cudaMemcpyDefault));
+    DEC_CUDA(dec_alloc(M, &M.final_norm, sizeof(float) * d));
+    DEC_CUDA(cudaMemcpy(M.final_norm, w->final_norm, sizeof(float) * d, cudaMemcpyDefault));
+    {
+        const float* parts[1] = {M.embed};
+        const int prow[1] = {M.V};
+        DEC_RC(make_dense(M, M.head, parts, prow, 1, M.d));
+    }
+    M.attn_norm.assign(M.nl, nullptr);
+    M.qkv.resize(M.nl);
+    M.wo.resize(M.nl);
+    M.moe.assign(M.nl, nullptr);
+    const int E = cfg->num_experts;
+    for (int l = 0; l < M.nl; ++l) {
+        if (!w->attn_norm[l] || !w->wq[l] || !w->wk[l] || !w->wv[l] || !w->wo[l] ||
+            !w->ffn_norm[l] || !w->router[l])
+            return report_error(MOE_ERR_INVALID, "null layer weight");
+        DEC_CUDA(dec_alloc(M, &M.attn_norm[l], sizeof(float) * d));
+        DEC_CUDA(cudaMemcpy(M.attn_norm[l], w->attn_norm[l], sizeof(float) * d, cudaMemcpyDefault));
+        const float* qkv_parts[3] = {w->wq[l], w->wk[l], w->wv[l]};
+        const int qkv_rows[3] = {M.d, M.d, M.d};
+        DEC_RC(make_dense(M, M.qkv[l], qkv_parts, qkv_rows, 3, M.d));
+        const float* o_parts[1] = {w->wo[l]};
+        const int o_rows[1] = {M.d};
+        DEC_RC(make_dense(M, M.wo[l], o_parts, o_rows, 1, M.d));
+        MoeConfig mc;
+        moe_config_init(&mc);
+        mc.d_model = M.d;
+        mc.d_ff = cfg->d_ff;
+        mc.num_experts = E;
+        mc.top_k = cfg->top_k;
+        mc.router_policy = MOE_ROUTER_SOFTMAX_TOPK;
+        mc.precision = cfg->precision;
+        mc.device = cfg->device;
+        mc.max_tokens = M.max_rows;
+        MoeWeightsHost mw{};
+        mw.router_weight = w->router[l];
+        mw.router_bias = nullptr;
+        mw.w1 = w->w1 + (size_t)l * E;
+        mw.w3 = w->w3 + (size_t)l * E;
+        mw.w2 = w->w2 + (size_t)l * E;
+        DEC_RC(device_ptrs ? moe_create_from_device(&mc, &mw, &M.moe[l])
+                           : moe_create(&mc, &mw, &M.moe[l]));
+        DEC_RC(moe_set_post_rms_norm(M.moe[l], w->ffn_norm[l], cfg->rms_eps));
+        M.bytes += moe_device_bytes(M.moe[l]);
+    }
+    DEC_CUDA(cudaDeviceSynchronize());
+    *out = m.release();
+    return MOE_OK;
+}
+
+int copy_tokens(MoeDecoder& m, const int32_t* tokens, size_t n) {
+    DEC_CUDA(cudaMemcpyAsync(m.tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m.stream));
+    return MOE_OK;
+}
+
+int prefill_impl(MoeDecoder& m, const int32_t* tokens, int B, int S, float* logits,
+                 int32_t* next_ids);
+int decode_step_impl(MoeDecoder& m, const int32_t* tokens, float* logits, int32_t* next_ids);
+int generate_impl(MoeDecoder& m, const int32_t* prompt, int B, int S, int max_new_tokens,
+                  int eos_id, float* logits, int32_t* ids);
+
+}  // namespace
+}  // namespace moe
+
+extern "C" {
+
+void moe_decoder_config_init(MoeDecoderConfig* c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof *c);
+    c->n_layers = 8;
+    c->d_model = 2048;
+    c->n_heads = 16;
+    c->head_dim = 128;
+    c->vocab = 32000;
+    c->num_experts = 16;
+    c->top_k = 2;
+    c->d_ff = 5632;
+    c->rms_eps = 1.0e-5f;
+    c->rope_base = 10000.0f;
+    c->precision = MOE_PREC_BF16;
+    c->max_batch = 16;
+    c->max_seq = 640;
+    c->device = 0;
+}
+
+int moe_decoder_create(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w, MoeDecoder** out) {
+    return moe::create(cfg, w, false, out);
+}
+
+int moe_decoder_create_from_device(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w,
+                                   MoeDecoder** out) {
+    return moe::create(cfg, w, true, out);
+}
+
+void moe_decoder_destroy(MoeDecoder* m) { moe::destroy(m); }
+
+size_t moe_decoder_device_bytes(const MoeDecoder* m) { return m ? m->bytes : 0; }
+
+int moe_decoder_prefill(MoeDecoder* m, const int32_t* tokens, int32_t B, int32_t S, float* logits,
+                        int32_t* next_ids) {
+    using namespace moe;
+    if (!m || !tokens) return report_error(MOE_ERR_INVALID, "null argument");
+    if (B < 1 || B > m->cfg.max_batch || S < 1 || S > m->cfg.max_seq)
+        return report_error(MOE_ERR_INVALID, "need 1 <= B <= max_batch and 1 <= S <= max_seq");
+    DecDeviceGuard guard(m->cfg.device);
+    m->B = 0;   // until this call succeeds there is no batch to decode
+    const int rc = prefill_impl(*m, tokens, B, S, logits, next_ids);
+    if (rc) m->B = 0;
+    return rc;
+}
+
+int moe_decoder_decode_step(MoeDecoder* m, const int32_t* tokens, float* logits, int32_t* next_ids) {
+    using namespace moe;
+    if (!m || !tokens) return report_error(MOE_ERR_INVALID, "null argument");
+    if (m->B < 1) return report_error(MOE_ERR_INVALID, "decode step before a prefill");
+    if (m->pos >= m->cfg.max_seq) return report_error(MOE_ERR_INVALID, "the sequences reached max_seq");
+    DecDeviceGuard guard(m->cfg.device);
+    const int rc = decode_step_impl(*m, tokens, logits, next_ids);
+    if (rc) m->B = 0;   // the caches may be half-written: a new prefill is needed
+    return rc;
+}
+
+int moe_decoder_generate(MoeDecoder* m, const int32_t* prompt, int32_t B, int32_t S,
+                         int32_t max_new_tokens, int32_t eos_id, float* logits, int32_t* ids) {
+    using namespace moe;
+    if (!m || !prompt || !ids) return report_error(MOE_ERR_INVALID, "null argument");
+    if (max_new_tokens < 1) return report_error(MOE_ERR_INVALID, "max_new_tokens must be positive");
+    if (B < 1 || B > m->cfg.max_batch || S < 1)
+        return report_error(MOE_ERR_INVALID, "need 1 <= B <= max_batch and S >= 1");
+    if ((long long)S + max_new_tokens - 1 > m->cfg.max_seq)
+        return report_error(MOE_ERR_INVALID, "prompt + max_new_tokens - 1 exceeds max_seq");
+    DecDeviceGuard guard(m->cfg.device);
+    m->B = 0;
+    const int rc = generate_impl(*m, prompt, B, S, max_new_tokens, eos_id, logits, ids);
+    if (rc) m->B = 0;
+    return rc;
+}
+
+int moe_decoder_last_timing(const MoeDecoder* m, float* prefill_ms, float* decode_ms) {
+    using namespace moe;
+    if (!m) return report_error(MOE_ERR_INVALID, "null decoder");
+    if (prefill_ms) *prefill_ms = m->t_prefill;
+    if (decode_ms) *decode_ms = m->t_decode;
+    return MOE_OK;
+}
+
+}  // extern "C"
+
+namespace moe {
+namespace {
+
+int prefill_impl(MoeDecoder& M, const int32_t* tokens, int B, int S, float* logits,
+                 int32_t* next_ids) {
+    MoeDecoder* m = &M;
+    DEC_RC(copy_tokens(*m, tokens, (size_t)B * S));
+    DEC_RC(run_prefill(*m, B, S, -1, -1));
+    if (logits)
+        DEC_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * B * m->V, cudaMemcpyDeviceToHost, m->stream));
+    if (next_ids)
+        DEC_CUDA(cudaMemcpyAsync(next_ids, m->next, sizeof(int) * B, cudaMemcpyDeviceToHost, m->stream));
+    DEC_CUDA(cudaStreamSynchronize(m->stream));
+    return check_dev_err(*m);
+}
+
+int decode_step_impl(MoeDecoder& M, const int32_t* tokens, float* logits, int32_t* next_ids) {
+    MoeDecoder* m = &M;
+    DEC_RC(copy_tokens(*m, tokens, (size_t)m->B));
+    DEC_RC(run_decode(*m, m->tok, -1, -1));
+    if (logits)
+        DEC_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->B * m->V, cudaMemcpyDeviceToHost, m->stream));
+    if (next_ids)
+        DEC_CUDA(cudaMemcpyAsync(next_ids, m->next, sizeof(int) * m->B, cudaMemcpyDeviceToHost, m->stream));
+    DEC_CUDA(cudaStreamSynchronize(m->stream));
+    return check_dev_err(*m);
+}
+
+int generate_impl(MoeDecoder& M, const int32_t* prompt, int B, int S, int max_new_tokens,
+                  int eos_id, float* logits, int32_t* ids) {
+    MoeDecoder* m = &M;
+    const size_t V = m->V, n = max_new_tokens;
+    if (logits && m->gen_cap < (size_t)B * n) {
+        if (m->gen_logits) {
+            cudaFree(m->gen_logits);
+            m->bytes -= sizeof(float) * m->gen_cap * V;
+        }
+        m->gen_logits = nullptr;
+        m->gen_cap = 0;
+        DEC_CUDA(dec_alloc(*m, &m->gen_logits, sizeof(float) * B * n * V));
+        m->gen_cap = (size_t)B * n;
+    }
+    cudaStream_t s = m->stream;
+    DEC_RC(copy_tokens(*m, prompt, (size_t)B * S));
+    DEC_CUDA(cudaMemsetAsync(m->done, 0, sizeof(int) * B, s));
+    DEC_CUDA(cudaEventRecord(m->ev[0], s));
+    DEC_RC(run_prefill(*m, B, S, 0, eos_id));
+    if (logits)
+        DEC_CUDA(cudaMemcpy2DAsync(m->gen_logits, n * V * sizeof(float), m->logits, V * sizeof(float),
+                                   V * sizeof(float), B, cudaMemcpyDeviceToDevice, s));
+    DEC_CUDA(cudaEventRecord(m->ev[1], s));
+    for (int step = 1; step < max_new_tokens; ++step) {
+        DEC_RC(run_decode(*m, m->next, step, eos_id));
+        if (logits)
+            DEC_CUDA(cudaMemcpy2DAsync(m->gen_logits + (size_t)step * V, n * V * sizeof(float), m->logits,
+                                       V * sizeof(float), V * sizeof(float), B,
+                                       cudaMemcpyDeviceToDevice, s));
+    }
+    DEC_CUDA(cudaEventRecord(m->ev[2], s));
+    DEC_CUDA(cudaMemcpy2DAsync(ids, n * sizeof(int), m->seq_ids, m->cfg.max_seq * sizeof(int),
+                               n * sizeof(int), B, cudaMemcpyDeviceToHost, s));
+    if (logits)
+        DEC_CUDA(cudaMemcpyAsync(logits, m->gen_logits, sizeof(float) * B * n * V,
+                                 cudaMemcpyDeviceToHost, s));
+    DEC_CUDA(cudaStreamSynchronize(s));
+    DEC_CUDA(cudaEventElapsedTime(&m->t_prefill, m->ev[0], m->ev[1]));
+    DEC_CUDA(cudaEventElapsedTime(&m->t_decode, m->ev[1], m->ev[2]));
+    // generate_decode leaves a stopped sequence's later logits at zero.
+    if (logits)
+        for (int b = 0; b < B; ++b)
+            for (size_t t = 0; t < n; ++t)
+                if (ids[(size_t)b * n + t] < 0)
+                    std::memset(logits + ((size_t)b * n + t) * V, 0, sizeof(float) * V);
+    return check_dev_err(*m);
+}
+
+}  // namespace
+}  // namespace moe

@@ -159,6 +159,10 @@ struct Layer {
     float* norm_w = nullptr;
     float* norm_b = nullptr;
     float norm_eps = 0.0f;
+    // RMSNorm instead (moe_set_post_rms_norm): the statistics kernel writes
+    // mean 0 and norm_b holds zeros, so the LayerNorm apply expression
+    // fma((x - 0) * inv, w, 0) is exactly (x * inv) * w.
+    bool norm_rms = false;
     Workspace ws;
     size_t weight_bytes = 0;
     cudaStream_t last_stream = nullptr;
@@ -246,6 +250,10 @@ cudaError_t launch_layer_norm(const float* x, int T, int d, float eps, const flo
                               const float* b, float* y, cudaStream_t s);
 cudaError_t launch_residual_add(const Layer& L, float* y, const float* r, size_t n,
                                 cudaStream_t s);
+// RMSNorm statistics: mean[t] = 0, inv[t] = 1 / sqrt(sum_j x[t][j]^2 / d + eps)
+// (fp32 sum of squares; d a multiple of 4).
+cudaError_t launch_rms_stats(const float* x, int T, int d, float eps, float* mean, float* inv,
+                             cudaStream_t s);
 
 // weights.cu
 // Runs one bounded mbarrier wait that nothing completes (timeout self-test).

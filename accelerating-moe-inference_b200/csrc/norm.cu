@@ -308,6 +308,39 @@ cudaError_t launch_layer_norm(const float* x, int T, int d, float eps, const flo
     return launch_stats<true>(x, T, d, eps, nullptr, nullptr, w, b, y, nullptr, s);
 }
 
+namespace {
+// One warp per row: fp32 sum of squares (each lane walks its float4 columns,
+// then a butterfly), mean 0, inv = 1 / sqrt(ss / d + eps).
+__global__ void __launch_bounds__(256)
+rms_stats_kernel(const float* __restrict__ x, int T, int d, float eps, float* __restrict__ mean,
+                 float* __restrict__ inv) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= T) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * d);
+    float ss = 0.0f;
+    for (int v = lane; v < d / 4; v += 32) {
+        const float4 a = __ldg(xr + v);
+        ss = __fmaf_rn(a.x, a.x, ss);
+        ss = __fmaf_rn(a.y, a.y, ss);
+        ss = __fmaf_rn(a.z, a.z, ss);
+        ss = __fmaf_rn(a.w, a.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) {
+        mean[row] = 0.0f;
+        inv[row] = 1.0f / sqrtf(ss / (float)d + eps);
+    }
+}
+}  // namespace
+
+cudaError_t launch_rms_stats(const float* x, int T, int d, float eps, float* mean, float* inv,
+                             cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    rms_stats_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, T, d, eps, mean, inv);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_residual_add(const Layer& L, float* y, const float* r, size_t n,
                                 cudaStream_t s) {
     const size_t n4 = n / 4;

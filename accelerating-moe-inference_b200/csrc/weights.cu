@@ -57,7 +57,7 @@ __global__ void down_kernel(const float* __restrict__ w2, int ff, int ffp, int d
             const float h = to_tf32(v);
             static_cast<float*>(hi)[i] = h;
             static_cast<float*>(lo)[i] = to_tf32(v - h);
-            f32[i] = v;
+            if (f32) f32[i] = v;   // a dense projection keeps no decode copy
         }
     }
 }

@@ -70,6 +70,10 @@ def _router_weights(wl, gen, dev):
         bias = (0.5 * torch.log(1.0 / r)).to(torch.float32).to(dev)
     return wg, bias
 KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
+# the toy MoE decoder, end to end (prompt of 512 uniform
+# ids, 128 greedy tokens, batch 1 and 16).
+C4 = dict(workload="c4-toy-moe-decoder", n_layers=8, d=2048, heads=16, hd=128, vocab=32000,
+          E=16, k=2, ff=5632, prompt=512, new=128, batches=(1, 16), seed=2)
 DECODE_T = (1, 2, 4, 8, 16, 32, 64)
 FLUSH_BYTES = 256 << 20
 
@@ -289,6 +293,91 @@ def reference_arm(args, wl):
     return 0
 
 
+def run_decoder(args, pkg, dev, reps: int = 2):
+    """BASELINE config 4 through moe_decoder_generate: weights N(0, 0.02)
+    drawn on the device (seed 2), norms 1; per batch, prefill and decode
+    time from CUDA events on the decoder's stream and the host clock around
+    the whole call (prompt in, ids and logits [B][128][32000] out)."""
+    import numpy as np
+    import torch
+    c = C4
+    d, L, E, ff, V, k = c["d"], c["n_layers"], c["E"], c["ff"], c["vocab"], c["k"]
+    gen = torch.Generator(device="cuda").manual_seed(c["seed"])
+    rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
+    keep = []
+
+    def t(x):
+        keep.append(x)
+        return x.data_ptr()
+    ones = torch.ones(d, device=dev)
+    ptrs = {"embed": t(rnd(V, d)), "final_norm": ones.data_ptr(), "attn_norm": [], "wq": [],
+            "wk": [], "wv": [], "wo": [], "ffn_norm": [], "router": [], "w1": [], "w3": [],
+            "w2": []}
+    for _ in range(L):
+        for name in ("wq", "wk", "wv", "wo"):
+            ptrs[name].append(t(rnd(d, d)))
+        ptrs["attn_norm"].append(ones.data_ptr())
+        ptrs["ffn_norm"].append(ones.data_ptr())
+        ptrs["router"].append(t(rnd(E, d)))
+        for _e in range(E):
+            ptrs["w1"].append(t(rnd(ff, d)))
+            ptrs["w3"].append(t(rnd(ff, d)))
+            ptrs["w2"].append(t(rnd(d, ff)))
+    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
+    bmax = max(c["batches"])
+    m = pkg.MoeDecoder(n_heads=c["heads"], head_dim=c["hd"], top_k=k, precision=prec,
+                       max_batch=bmax, max_seq=c["prompt"] + c["new"], device=dev.index,
+                       device_pointers=ptrs, dims=dict(n_layers=L, d=d, vocab=V, E=E, ff=ff))
+    del keep, ptrs
+    torch.cuda.empty_cache()
+    prompt = pkg.synthetic_prompt(c["seed"], bmax, c["prompt"], V)
+    hbm = _peaks()[0]
+    wb = 2 if args.precision == "bf16" else 4
+    out = {}
+    for B in c["batches"]:
+        p = np.ascontiguousarray(prompt[:B])
+        lbuf = np.empty((B, c["new"], V), np.float32)
+        m.generate(p, c["new"], logits_out=lbuf)                      # warm-up
+        pre = dec = wall = 0.0
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            ids, _ = m.generate(p, c["new"], logits_out=lbuf)
+            wall += time.perf_counter() - t0
+            a, b = m.last_timing()
+            pre += a
+            dec += b
+        pre, dec, wall = pre / reps, dec / reps, wall / reps
+        steps = c["new"] - 1
+        # Bytes one decode step must read at least: dense projections and the
+        # output head, the experts a batch of B routes to (expected distinct
+        # experts under uniform routing), the router, the KV cache (fp32) at
+        # the mean position.
+        e_dist = E * (1.0 - (1.0 - k / E) ** B)
+        pos = c["prompt"] + steps / 2.0
+        step_bytes = (L * (4 * d * d * wb + e_dist * 3 * d * ff * wb + E * d * 4
+                           + 2 * B * pos * d * 4) + V * d * wb)
+        ms_step = dec / steps
+        out[str(B)] = {
+            "prefill_ms": pre, "prefill_tokens_per_s": B * c["prompt"] / (pre / 1e3),
+            "decode_ms_per_step": ms_step, "decode_tokens_per_s": B * steps / (dec / 1e3),
+            "decode_step_bytes": step_bytes,
+            "decode_hbm_gbs": step_bytes / (ms_step / 1e3) / 1e9,
+            "decode_frac_of_hbm": step_bytes / (ms_step / 1e3) / 1e9 / hbm,
+            "generate_wall_s": wall,
+            "e2e_new_tokens_per_s": B * c["new"] / wall,
+            "ids_valid": bool(((ids >= 0) & (ids < V)).all()),
+            "logits_finite": bool(np.isfinite(lbuf).all()),
+        }
+    m.close()
+    return {"workload": c["workload"], "n_layers": L, "d_model": d, "heads": c["heads"],
+            "head_dim": c["hd"], "vocab": V, "experts": E, "top_k": k, "d_ff": ff,
+            "prompt": c["prompt"], "new_tokens": c["new"], "precision": args.precision,
+            "seed": c["seed"], "by_batch": out,
+            "how": "moe_decoder_generate (KV-cached greedy decode); prefill/decode from CUDA "
+                   "events on the decoder's stream, e2e = host clock around the call; decode "
+                   "bytes use the expected distinct experts under uniform routing"}
+
+
 def run_ep(args, wl, pkg, world, rank, local):
     """N > 1, expert parallel: each rank holds E/N experts and its own T
     tokens; dispatch and combine are NCCL exchanges over NVLink (weak scaling:
@@ -443,6 +532,8 @@ def main():
     ap.add_argument("--no-block", action="store_true",
                     help="skip the decoder-layer block section (post-attention LayerNorm + "
                          "MoE + residual)")
+    ap.add_argument("--no-decoder", action="store_true",
+                    help="skip the toy MoE decoder section (BASELINE config 4)")
     ap.add_argument("--decode-max-tokens", type=int, default=None,
                     help="override the handle's decode threshold (0..64)")
     args = ap.parse_args()
@@ -622,6 +713,11 @@ def main():
                                       "gbs": ln_bytes / (ms_ln / 1e3) / 1e9,
                                       "frac_of_hbm": ln_bytes / (ms_ln / 1e3) / 1e9 / _peaks()[0]}
 
+    # ---- the toy MoE decoder, end to end
+    decoder = None
+    if not args.no_decoder and world == 1:
+        decoder = run_decoder(args, pkg, dev)
+
     # ---- e2e through the host-buffer C-ABI call (pinned buffers)
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -695,6 +791,7 @@ def main():
                       "what": "moe_block_forward_device: y = x + MoE(layer_norm(x)) "
                               "(PhiDecoderLayer's MoE half; norm statistics bit-exact with "
                               "tensor_ops::layer_norm, applied inside router and permute)"},
+            "decoder": decoder,
             "gpu_launches": KERNELS_PER_FORWARD * args.steps,
             "clocks": clocks,
             "output_finite": ok_y,

@@ -198,6 +198,13 @@ int moe_forward_host(MoeHandle* h, const float* x, float* y, int32_t T);
  * + attn, in the reference's order.  MOE_ERR_INVALID if no norm is attached.
  * y must not alias attn.  d_model must be a multiple of 128. */
 int moe_set_post_norm(MoeHandle* h, const float* weight, const float* bias, float eps);
+/* The same block with an RMSNorm in place of the LayerNorm (BASELINE
+ * config 4's decoder, which has no counterpart in the reference's Phi
+ * model): y = attn + MoE(rms_norm(attn)), rms_norm(x)_j = (x_j * inv) * w_j
+ * with inv = 1 / sqrt(sum_j x_j^2 / d_model + eps), the sum of squares in
+ * fp32.  weight is [d_model] fp32 (host or device pointer, copied).  Replaces an
+ * attached LayerNorm, and moe_set_post_norm replaces this. */
+int moe_set_post_rms_norm(MoeHandle* h, const float* weight, float eps);
 int moe_block_forward_device(MoeHandle* h, const float* attn, float* y, int32_t T, void* stream);
 int moe_block_forward_host(MoeHandle* h, const float* attn, float* y, int32_t T);
 
@@ -339,6 +346,105 @@ int moe_dispatch_noalloc(const int32_t* idx, const float* weights, int32_t T,
                          int32_t num_experts, int32_t top_k, int32_t* row_token,
                          float* row_weight, int32_t rows_cap, int32_t* expert_offsets,
                          int32_t* counts, void* stream);
+
+/* ---------------------------------------------------------------------
+ * Whole-model greedy generation with the MoE layers above: the toy MoE
+ * decoder of BASELINE config 4, the counterpart of the reference's
+ * PhiTinyMoEModel (include/model.h:8-30): generate (src/model.cu:1575-2058,
+ * last-position logits of a batch) and generate_decode (src/model.cu:
+ * 2061-2104, greedy argmax, first maximum wins, stop at EOS).
+ *
+ * Architecture: tied token embeddings; per layer x += o_proj(attn(rope(
+ * qkv_proj(rms_norm(x))))) then x += MoE(rms_norm(x)); a final rms_norm and
+ * the embedding matrix as the output head.  Multi-head attention (as many KV
+ * heads as query heads), causal, scaled by 1/sqrt(head_dim); rotary
+ * embedding in the reference's rotate-half form (tensor_ops::apply_rope,
+ * src/tensor.cu:191-210), its cos/sin table computed in double.  The MoE is
+ * the softmax / top-k / renormalise router with SwiGLU experts.  Unlike the
+ * reference's generate_decode, which re-runs the whole prefix per token, the
+ * decoder keeps a KV cache, so each new token costs one decode step.
+ *
+ * The projections and the output head run on the same tcgen05 grouped GEMM
+ * as the experts (one group, identity row map); precision as MoeConfig's.
+ * Constraints: d_model == n_heads * head_dim, d_model a multiple of 128,
+ * head_dim 64 or 128, vocab a multiple of 32; every sequence of a batch has
+ * the same length; max_batch * max_seq rows of activations are reserved.
+ * --------------------------------------------------------------------- */
+typedef struct MoeDecoderConfig {
+    int32_t n_layers;
+    int32_t d_model;
+    int32_t n_heads;
+    int32_t head_dim;
+    int32_t vocab;
+    int32_t num_experts;
+    int32_t top_k;
+    int32_t d_ff;
+    float rms_eps;       /* 1e-5 */
+    float rope_base;     /* 10000 */
+    int32_t precision;   /* MoePrecision */
+    int32_t max_batch;   /* sequences per call */
+    int32_t max_seq;     /* prompt + generated tokens per sequence */
+    int32_t device;
+    int32_t reserved[4];
+} MoeDecoderConfig;
+
+/* fp32 nn.Linear-layout weights ([out][in], row-major).  Per-layer entries
+ * are arrays of n_layers pointers; expert entries n_layers * num_experts
+ * pointers, layer-major.  Host pointers for moe_decoder_create, device
+ * pointers (on cfg->device) for moe_decoder_create_from_device; copied and
+ * converted, the caller keeps ownership. */
+typedef struct MoeDecoderWeights {
+    const float* embed;             /* [vocab][d_model]; also the output head */
+    const float* final_norm;        /* [d_model] */
+    const float* const* attn_norm;  /* [d_model] each */
+    const float* const* wq;         /* [d_model][d_model] each */
+    const float* const* wk;
+    const float* const* wv;
+    const float* const* wo;
+    const float* const* ffn_norm;   /* [d_model] each */
+    const float* const* router;     /* [num_experts][d_model] each */
+    const float* const* w1;         /* [d_ff][d_model] each */
+    const float* const* w3;         /* [d_ff][d_model] each */
+    const float* const* w2;         /* [d_model][d_ff] each */
+} MoeDecoderWeights;
+
+typedef struct MoeDecoder MoeDecoder;
+
+/* Defaults of BASELINE config 4 (8 layers, d 2048, 16 x 128 heads, vocab
+ * 32000, 16 experts top-2, d_ff 5632, eps 1e-5, RoPE base 10000), BF16,
+ * batch 16, 640 positions, device 0. */
+void moe_decoder_config_init(MoeDecoderConfig* cfg);
+int moe_decoder_create(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w,
+                       MoeDecoder** out);
+int moe_decoder_create_from_device(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w,
+                                   MoeDecoder** out);
+void moe_decoder_destroy(MoeDecoder* m);
+size_t moe_decoder_device_bytes(const MoeDecoder* m);
+
+/* Prefill (PhiTinyMoEModel::generate): tokens [B][S] (host int32) fill the
+ * KV cache from position 0 and give the last position's logits [B][vocab]
+ * and greedy next ids [B] (host; either may be NULL).  Synchronises. */
+int moe_decoder_prefill(MoeDecoder* m, const int32_t* tokens, int32_t B, int32_t S,
+                        float* logits, int32_t* next_ids);
+/* One decode step after a prefill or an earlier step: tokens [B] (host) go
+ * in at the next position of every sequence; logits [B][vocab] and the
+ * greedy next ids [B] come out (host; either may be NULL).  Synchronises.
+ * MOE_ERR_INVALID past max_seq. */
+int moe_decoder_decode_step(MoeDecoder* m, const int32_t* tokens, float* logits,
+                            int32_t* next_ids);
+/* Greedy generation (PhiTinyMoEModel::generate_decode): prefill the prompt
+ * [B][S], then max_new_tokens greedy tokens per sequence.  ids [B][n] (host)
+ * receive the generated tokens; logits [B][n][vocab] (host, may be NULL) the
+ * logits each token was chosen from.  A sequence that emits eos_id (pass -1
+ * for none) stops there: its later ids are -1 and its later logits 0.
+ * Decode steps keep the tokens on the device; one synchronisation at the
+ * end. */
+int moe_decoder_generate(MoeDecoder* m, const int32_t* prompt, int32_t B, int32_t S,
+                         int32_t max_new_tokens, int32_t eos_id, float* logits, int32_t* ids);
+/* Device time (CUDA events on the decoder's stream) of the last
+ * moe_decoder_generate: the prefill (through the first token's argmax) and
+ * all decode steps. */
+int moe_decoder_last_timing(const MoeDecoder* m, float* prefill_ms, float* decode_ms);
 
 #ifdef __cplusplus
 }

@@ -166,6 +166,8 @@ class Reference:
         L.ref_last_error.restype = ctypes.c_char_p
         L.ref_layer_norm.argtypes = [_f32p, _f32p, _f32p, ctypes.c_float, ctypes.c_int,
                                      ctypes.c_int, _f32p]
+        L.ref_apply_rope.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_float]
         L.ref_set_threads.argtypes = [ctypes.c_int]
         L.ref_set_threads.restype = ctypes.c_int
         self.E = L.ref_num_experts()
@@ -216,6 +218,15 @@ class Reference:
                                    _fp(y)) != 0:
             raise RuntimeError(self.lib.ref_last_error().decode())
         return y
+
+    def apply_rope(self, q, k, heads, head_dim, theta=10000.0):
+        """tensor_ops::apply_rope on copies of q [S][heads*hd] and k (same heads)."""
+        q = np.array(q, np.float32, copy=True, order="C")
+        k = np.array(k, np.float32, copy=True, order="C")
+        if self.lib.ref_apply_rope(_fp(q), _fp(k), q.shape[0], heads, heads, head_dim,
+                                   theta) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return q, k
 
     def matmul_transposed(self, a, b):
         a = np.ascontiguousarray(a, np.float32)

@@ -154,4 +154,24 @@ int ref_matmul_transposed(const float* a, const float* b, float* c, int m, int k
     }
 }
 
+// tensor_ops::apply_rope on raw buffers (src/tensor.cu:191-210): q [seq][q_heads *
+// head_dim] and k [seq][kv_heads * head_dim] rotated in place, position = row.
+int ref_apply_rope(float* q, float* k, int seq, int q_heads, int kv_heads, int head_dim,
+                   float theta) {
+    try {
+        const std::size_t S = static_cast<std::size_t>(seq), hd = static_cast<std::size_t>(head_dim);
+        Tensor qt({S, static_cast<std::size_t>(q_heads) * hd});
+        Tensor kt({S, static_cast<std::size_t>(kv_heads) * hd});
+        std::memcpy(qt.data(), q, sizeof(float) * qt.size());
+        std::memcpy(kt.data(), k, sizeof(float) * kt.size());
+        tensor_ops::apply_rope(qt, kt, S, static_cast<std::size_t>(q_heads),
+                               static_cast<std::size_t>(kv_heads), hd, theta);
+        std::memcpy(q, qt.data(), sizeof(float) * qt.size());
+        std::memcpy(k, kt.data(), sizeof(float) * kt.size());
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
 }  // extern "C"

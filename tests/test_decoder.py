@@ -1,0 +1,209 @@
+"""The toy MoE decoder -- moe_decoder_* against the CPU
+restatement in oracle/decoder_oracle.py.
+
+CPU tests pin the oracle: its RoPE against the reference's own
+tensor_ops::apply_rope (src/tensor.cu:191-210, compiled into oracle/_ref),
+its greedy loop against its own prefill, and its EOS rule (generate_decode,
+src/model.cu:2061-2104).  GPU tests run the decoder through the C ABI at a
+small shape (2 layers, d 256, vocab 1024, 8 experts top-2) and compare:
+  - prefill logits: relative L2 <= 1e-3 in FP32 (3xTF32), <= 3e-2 in BF16
+    (every activation rounded to bf16 before each GEMM);
+  - greedy ids: equal to the oracle's until the sequences diverge, and a
+    divergence only where the oracle's top-2 logit gap is below the
+    precision's noise margin (FP32 2e-3, BF16 5e-2); logits at the shared
+    prefix within the same bounds as prefill.
+"""
+import sys
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, load_oracle, load_pkg, rel_l2
+
+sys.path.insert(0, str(ROOT / "oracle"))
+
+SMALL = dict(n_layers=2, d=256, vocab=1024, E=8, ff=384)
+TOL = {0: 1e-3, 1: 3e-2}          # precision -> rel-L2 bound on logits
+MARGIN = {0: 2e-3, 1: 5e-2}       # precision -> top-2 gap a divergence may sit within
+
+
+def _weights(seed=2, **kw):
+    pkg = load_pkg()
+    shape = dict(SMALL, **kw)
+    return pkg.synthetic_decoder(seed, shape["n_layers"], shape["d"], shape["vocab"], shape["E"],
+                                 shape["ff"], norm_jitter=0.1)
+
+
+def _oracle(w, heads, hd):
+    load_oracle()
+    import decoder_oracle
+    return decoder_oracle.DecoderOracle(w, heads, hd)
+
+
+# ---------------------------------------------------------------- CPU
+def test_oracle_rope_matches_reference_apply_rope():
+    orc_mod = load_oracle()
+    if not orc_mod.Reference.available(8):
+        pytest.skip("reference library not built (reference sources absent)")
+    import decoder_oracle
+    ref = orc_mod.Reference(8)
+    g = np.random.default_rng(5)
+    S, H, hd = 48, 3, 64
+    q = g.standard_normal((S, H * hd)).astype(np.float32)
+    k = g.standard_normal((S, H * hd)).astype(np.float32)
+    rq, rk = ref.apply_rope(q, k, H, hd, 10000.0)
+    pos = np.arange(S)
+    oq = decoder_oracle.apply_rope(q.reshape(S, H, hd).astype(np.float64), pos, hd, 10000.0)
+    ok = decoder_oracle.apply_rope(k.reshape(S, H, hd).astype(np.float64), pos, hd, 10000.0)
+    # The reference forms each angle in float (pow, then position * inv), the
+    # restatement in double: they agree to the float rounding of the angle.
+    assert np.max(np.abs(oq.reshape(S, -1) - rq)) < 2e-5
+    assert np.max(np.abs(ok.reshape(S, -1) - rk)) < 2e-5
+
+
+def test_oracle_greedy_loop_restarts_from_the_prefix():
+    import decoder_oracle  # noqa: F401
+    w = _weights(n_layers=1, d=128, vocab=256, ff=128)
+    o = _oracle(w, 1, 128)
+    pkg = load_pkg()
+    prompt = pkg.synthetic_prompt(1, 2, 7, w.vocab)
+    ids, lg = o.generate(prompt, 3)
+    assert np.array_equal(lg[:, 0], o.last_logits(prompt))
+    assert np.array_equal(ids[:, 0], np.argmax(lg[:, 0], axis=1))
+    ext = np.concatenate([prompt, ids[:, :1]], axis=1)
+    assert np.allclose(lg[:, 1], o.last_logits(ext), rtol=0, atol=0)
+
+
+def test_oracle_stops_a_sequence_at_eos():
+    w = _weights(n_layers=1, d=128, vocab=256, ff=128)
+    o = _oracle(w, 1, 128)
+    pkg = load_pkg()
+    prompt = pkg.synthetic_prompt(3, 2, 5, w.vocab)
+    ids, _ = o.generate(prompt, 4)
+    eos = int(ids[0, 1])
+    ids2, lg2 = o.generate(prompt, 4, eos_id=eos)
+    stop = int(np.argmax(ids2[0] == eos))
+    assert np.all(ids2[0, stop + 1:] == -1) and np.all(lg2[0, stop + 1:] == 0)
+
+
+# ---------------------------------------------------------------- GPU
+def _decoder(w, heads, hd, precision, max_batch=4, max_seq=128):
+    pkg = load_pkg()
+    return pkg.MoeDecoder(w, n_heads=heads, head_dim=hd, precision=precision,
+                          max_batch=max_batch, max_seq=max_seq)
+
+
+def _check_greedy(ids, lg, ids_ref, lg_ref, precision):
+    import decoder_oracle
+    B, n = ids.shape
+    for b in range(B):
+        for t in range(n):
+            assert rel_l2(lg[b, t], lg_ref[b, t]) <= TOL[precision], (b, t)
+            if ids[b, t] != ids_ref[b, t]:
+                gap = decoder_oracle.top2_margin(lg_ref[b, t])
+                assert gap <= MARGIN[precision], (b, t, gap)
+                break   # the prefixes differ from here on
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("heads,hd", [(2, 128), (4, 64)], ids=["hd128", "hd64"])
+def test_decoder_prefill_matches_oracle(precision, heads, hd):
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, heads, hd)
+    prompt = pkg.synthetic_prompt(2, 2, 40, w.vocab)
+    ref = o.last_logits(prompt)
+    with _decoder(w, heads, hd, precision) as m:
+        lg, nxt = m.prefill(prompt)
+    assert rel_l2(lg, ref) <= TOL[precision], rel_l2(lg, ref)
+    import decoder_oracle
+    for b in range(2):
+        if nxt[b] != np.argmax(ref[b]):
+            assert decoder_oracle.top2_margin(ref[b]) <= MARGIN[precision]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_decoder_generate_matches_oracle(precision):
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, 2, 128)
+    prompt = pkg.synthetic_prompt(4, 3, 33, w.vocab)
+    ids_ref, lg_ref = o.generate(prompt, 6)
+    with _decoder(w, 2, 128, precision) as m:
+        ids, lg = m.generate(prompt, 6)
+        pre, dec = m.last_timing()
+    assert pre > 0 and dec > 0
+    _check_greedy(ids, lg, ids_ref, lg_ref, precision)
+
+
+@pytest.mark.gpu
+def test_decoder_large_prefill_takes_the_pair_gemm():
+    """B * S = 300 rows: the projections run the CTA-pair tiles (>= 256 rows)."""
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, 2, 128)
+    prompt = pkg.synthetic_prompt(5, 3, 100, w.vocab)
+    ref = o.last_logits(prompt)
+    with _decoder(w, 2, 128, 0) as m:
+        lg, _ = m.prefill(prompt)
+    assert rel_l2(lg, ref) <= TOL[0]
+
+
+@pytest.mark.gpu
+def test_decoder_step_api_matches_generate():
+    pkg = load_pkg()
+    w = _weights()
+    prompt = pkg.synthetic_prompt(6, 2, 20, w.vocab)
+    with _decoder(w, 2, 128, 0) as m:
+        ids, lg = m.generate(prompt, 4)
+        l0, n0 = m.prefill(prompt)
+        steps = [(l0, n0)]
+        for _ in range(3):
+            steps.append(m.decode_step(steps[-1][1]))
+    for t, (lt, nt) in enumerate(steps):
+        # Decode-sized projections split K with atomic adds: equal up to
+        # summation order.
+        assert rel_l2(lt, lg[:, t]) <= 1e-5
+        assert np.array_equal(nt, ids[:, t])
+
+
+@pytest.mark.gpu
+def test_decoder_eos_stops_a_sequence():
+    pkg = load_pkg()
+    w = _weights()
+    prompt = pkg.synthetic_prompt(7, 2, 16, w.vocab)
+    with _decoder(w, 2, 128, 0) as m:
+        ids, _ = m.generate(prompt, 5)
+        eos = int(ids[0, 1])
+        ids2, lg2 = m.generate(prompt, 5, eos_id=eos)
+    stop = int(np.argmax(ids2[0] == eos))
+    assert stop <= 1
+    assert np.all(ids2[0, stop + 1:] == -1) and np.all(lg2[0, stop + 1:] == 0)
+    assert np.array_equal(ids2[0, :stop + 1], ids[0, :stop + 1])
+
+
+@pytest.mark.gpu
+def test_decoder_rejects_bad_arguments():
+    pkg = load_pkg()
+    w = _weights()
+    with _decoder(w, 2, 128, 1, max_batch=2, max_seq=24) as m:
+        with pytest.raises(pkg.MoeError):
+            m.decode_step(np.zeros(2, np.int32))                     # before any prefill
+        with pytest.raises(pkg.MoeError):
+            m.prefill(pkg.synthetic_prompt(1, 3, 8, w.vocab))       # B > max_batch
+        with pytest.raises(pkg.MoeError):
+            m.generate(pkg.synthetic_prompt(1, 1, 20, w.vocab), 6)  # 20 + 6 - 1 > 24
+        bad = np.array([[1, 2, w.vocab]], np.int32)
+        with pytest.raises(pkg.MoeError) as ei:
+            m.prefill(bad)                                           # id out of range
+        assert "vocab" in str(ei.value)
+        with pytest.raises(pkg.MoeError):
+            m.decode_step(np.zeros(1, np.int32))                     # the failed prefill left no batch
+        m.prefill(pkg.synthetic_prompt(1, 2, 8, w.vocab))
+        with pytest.raises(ValueError):
+            m.decode_step(np.zeros(3, np.int32))                     # not the prefill's batch
+        # the decoder still works after the rejected calls
+        lg, _ = m.prefill(pkg.synthetic_prompt(1, 2, 8, w.vocab))
+        assert np.all(np.isfinite(lg))
