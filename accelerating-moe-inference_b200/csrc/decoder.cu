@@ -186,18 +186,19 @@ __global__ void dense_tiles_kernel(int T, int rows_pad, MTile* __restrict__ mtil
 
 // ------------------------------------------------------------ RoPE + cache
 // Row r of qkv [T][3d] is token r % rps of sequence r / rps, at position
-// pos0 + r % rps.  q and k are rotated in the reference's rotate-half form
+// pos0 (+ *pos_dev, a decode step's position kept on the device) + r % rps.  q and k are rotated in the reference's rotate-half form
 // (tensor_ops::apply_rope, src/tensor.cu:191-210): for j < hd/2,
 //   x_j' = x_j cos - x_{j+hd/2} sin,  x_{j+hd/2}' = x_{j+hd/2} cos + x_j sin
 // with (cos, sin) of position p and pair j from the table [max_seq][hd/2][2].
 // q stays in qkv (rotated); k and v go to the cache at their position.
 template <int HD>
 __global__ void __launch_bounds__(256)
-rope_kv_kernel(float* __restrict__ qkv, int rps, int pos0, int H, const float2* __restrict__ rope,
-               float* __restrict__ kc, float* __restrict__ vc, int max_seq) {
+rope_kv_kernel(float* __restrict__ qkv, int rps, int pos0, const int* __restrict__ pos_dev, int H,
+               const float2* __restrict__ rope, float* __restrict__ kc, float* __restrict__ vc,
+               int max_seq) {
     constexpr int kHalf = HD / 2;
     const int r = blockIdx.x;
-    const int b = r / rps, pos = pos0 + r % rps;
+    const int b = r / rps, pos = pos0 + (pos_dev ? *pos_dev : 0) + r % rps;
     const int d = H * HD;
     float* q = qkv + (size_t)r * 3 * d;
     const float* k = q + d;
@@ -380,79 +381,113 @@ attn_prefill_kernel(const float* __restrict__ qkv, int S, int H, const float* __
     }
 }
 
-// Decode: one query per (sequence, head) at position pos over keys 0..pos.
-// 128 threads; warps score keys round-robin (one warp-wide dot each), the
-// block takes the softmax over the scores in shared memory, and thread t
-// accumulates dim t % hd over the keys j = t / hd (mod 128 / hd).
+// Decode: one query per (sequence, head) at position *pos_dev (a device
+// counter, so a captured decode step replays at every position) over keys
+// 0..pos, split over the keys: a CTA per (64-key chunk, head, sequence)
+// writes its chunk's partial softmax -- running max m, sum l and the
+// unnormalised output o [hd] -- and attn_decode_combine_kernel merges the
+// chunks, o = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c.  The grid covers
+// max_seq keys; chunks past the position exit at once.
 constexpr int kDecThreads = 128;
+constexpr int kDecChunk = 64;
 
-template <int HD, bool kTf>
+template <int HD>
 __global__ void __launch_bounds__(kDecThreads)
-attn_decode_kernel(const float* __restrict__ qkv, int pos, int H, const float* __restrict__ kc,
-                   const float* __restrict__ vc, int max_seq, float scale,
-                   void* __restrict__ a_hi, void* __restrict__ a_lo) {
+attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, int H,
+                           const float* __restrict__ kc, const float* __restrict__ vc,
+                           int max_seq, float scale, float* __restrict__ part, int nch) {
     constexpr int kPer = HD / 32;             // q values per lane
     constexpr int kParts = kDecThreads / HD;  // key classes of the value pass
-    extern __shared__ __align__(16) float sS[];   // [max_seq] scores, then probabilities
-    __shared__ float red[kDecThreads / 32];
-    __shared__ float part[kDecThreads];
-    const int h = blockIdx.x, b = blockIdx.y;
+    constexpr int kWarps = kDecThreads / 32;
+    constexpr int kKeysPerWarp = kDecChunk / kWarps;
+    __shared__ float sp[kDecChunk];
+    __shared__ float sacc[kDecThreads];
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n = *pos_dev + 1;
+    const int k0 = c * kDecChunk;
+    if (k0 >= n) return;
+    const int nk = min(kDecChunk, n - k0);
     const int d = H * HD;
-    const int n = pos + 1;
     const float* q = qkv + (size_t)b * 3 * d + h * HD;
-    const float* kbase = kc + ((size_t)b * H + h) * max_seq * HD;
-    const float* vbase = vc + ((size_t)b * H + h) * max_seq * HD;
+    const float* kb = kc + (((size_t)b * H + h) * max_seq + k0) * HD;
+    const float* vb = vc + (((size_t)b * H + h) * max_seq + k0) * HD;
     float qv[kPer];
 #pragma unroll
     for (int i = 0; i < kPer; ++i) qv[i] = q[lane * kPer + i] * scale;
-    for (int j = warp; j < n; j += kDecThreads / 32) {
-        const float* kr = kbase + (size_t)j * HD + lane * kPer;
+    // Scores: warp w takes keys w, w + 4, ...; every K row load is issued
+    // before the reductions.
+    float dots[kKeysPerWarp];
+#pragma unroll
+    for (int i = 0; i < kKeysPerWarp; ++i) {
+        const int j = warp + kWarps * i;
         float acc = 0.0f;
+        if (j < nk) {
+            const float* kr = kb + (size_t)j * HD + lane * kPer;
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) acc = fmaf(qv[i], kr[i], acc);
-        acc = warp_sum(acc);
-        if (lane == 0) sS[j] = acc;
+            for (int e = 0; e < kPer; ++e) acc = fmaf(qv[e], __ldg(kr + e), acc);
+        }
+        dots[i] = acc;
+    }
+#pragma unroll
+    for (int i = 0; i < kKeysPerWarp; ++i) {
+        const float v = warp_sum(dots[i]);
+        const int j = warp + kWarps * i;
+        if (lane == 0 && j < nk) sp[j] = v;
     }
     __syncthreads();
-    float mx = -INFINITY;
-    for (int j = tid; j < n; j += kDecThreads) mx = fmaxf(mx, sS[j]);
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-#pragma unroll
-    for (int w = 1; w < kDecThreads / 32; ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-    float sum = 0.0f;
-    for (int j = tid; j < n; j += kDecThreads) {
-        const float p = expf(sS[j] - mx);
-        sS[j] = p;
-        sum += p;
+    float* out = part + (((size_t)b * H + h) * nch + c) * (HD + 2);
+    if (warp == 0) {
+        const float s0 = lane < nk ? sp[lane] : -INFINITY;
+        const float s1 = lane + 32 < nk ? sp[lane + 32] : -INFINITY;
+        const float mx = warp_max(fmaxf(s0, s1));
+        const float p0 = lane < nk ? expf(s0 - mx) : 0.0f;
+        const float p1 = lane + 32 < nk ? expf(s1 - mx) : 0.0f;
+        if (lane < nk) sp[lane] = p0;
+        if (lane + 32 < nk) sp[lane + 32] = p1;
+        const float l = warp_sum(p0 + p1);
+        if (lane == 0) {
+            out[HD] = mx;
+            out[HD + 1] = l;
+        }
     }
-    sum = warp_sum(sum);
-    if (lane == 0) red[warp] = sum;
     __syncthreads();
-    sum = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kDecThreads / 32; ++w) sum += red[w];
-    const int c = tid % HD, cls = tid / HD;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int col = tid % HD, cls = tid / HD;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     int j = cls;
-    for (; j + 3 * kParts < n; j += 4 * kParts) {
+    for (; j + 3 * kParts < nk; j += 4 * kParts) {
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-            acc[u] = fmaf(sS[j + u * kParts], vbase[(size_t)(j + u * kParts) * HD + c], acc[u]);
+            a[u] = fmaf(sp[j + u * kParts], __ldg(vb + (size_t)(j + u * kParts) * HD + col), a[u]);
     }
-    for (; j < n; j += kParts) acc[0] = fmaf(sS[j], vbase[(size_t)j * HD + c], acc[0]);
-    part[tid] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    for (; j < nk; j += kParts) a[0] = fmaf(sp[j], __ldg(vb + (size_t)j * HD + col), a[0]);
+    sacc[tid] = (a[0] + a[1]) + (a[2] + a[3]);
     __syncthreads();
     if (tid < HD) {
-        float v = part[tid];
+        float v = sacc[tid];
 #pragma unroll
-        for (int p = 1; p < kParts; ++p) v += part[tid + p * HD];
-        store_a1<kTf>(a_hi, a_lo, b, d, h * HD + tid, v / sum);
+        for (int p = 1; p < kParts; ++p) v += sacc[tid + p * HD];
+        out[tid] = v;
     }
+}
+
+template <int HD, bool kTf>
+__global__ void __launch_bounds__(HD)
+attn_decode_combine_kernel(const float* __restrict__ part, const int* __restrict__ pos_dev, int H,
+                           int nch, void* __restrict__ a_hi, void* __restrict__ a_lo) {
+    const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    const int used = (*pos_dev + kDecChunk) / kDecChunk;   // chunks holding keys 0..pos
+    const float* base = part + ((size_t)b * H + h) * nch * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < used; ++c) M = fmaxf(M, base[(size_t)c * (HD + 2) + HD]);
+    float L = 0.0f, o = 0.0f;
+    for (int c = 0; c < used; ++c) {
+        const float* pc = base + (size_t)c * (HD + 2);
+        const float w = expf(pc[HD] - M);
+        L = fmaf(w, pc[HD + 1], L);
+        o = fmaf(w, pc[t], o);
+    }
+    store_a1<kTf>(a_hi, a_lo, b, H * HD, h * HD + t, o / L);
 }
 
 // ------------------------------------------------------------ argmax
@@ -460,10 +495,12 @@ attn_decode_kernel(const float* __restrict__ qkv, int pos, int H, const float* _
 // (src/model.cu:2081-2089): the first index holding the maximum, scanning
 // with a strict '>' from index 0 -- so NaNs are never chosen, except that a
 // NaN at index 0 yields 0.  Writes the id to ids[b] and, if `seq_out`, to
-// seq_out[b * seq_ld + step] (-1 once the sequence has emitted eos).
+// seq_out[b * seq_ld + step] (-1 once the sequence has emitted eos); the
+// step is *step_dev when given (a captured decode step).
 __global__ void __launch_bounds__(1024)
 argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ ids,
-              int* __restrict__ seq_out, int seq_ld, int step, int eos, int* __restrict__ done) {
+              int* __restrict__ seq_out, int seq_ld, int step, const int* __restrict__ step_dev,
+              int eos, int* __restrict__ done) {
     __shared__ float sv[32];
     __shared__ int si[32];
     const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -498,9 +535,32 @@ argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ ids,
                 else if (id == eos) done[b] = 1;
             }
             ids[b] = id < 0 ? 0 : id;
-            if (seq_out) seq_out[(size_t)b * seq_ld + step] = id;
+            if (seq_out) seq_out[(size_t)b * seq_ld + (step_dev ? *step_dev : step)] = id;
         }
     }
+}
+
+// ------------------------------------------------------------ step counters
+// The decode position and generation step live on the device, so that one
+// captured decode step (a CUDA graph) serves every position.
+__global__ void set_counters_kernel(int* pos_dev, int* step_dev, int pos, int step) {
+    *pos_dev = pos;
+    *step_dev = step;
+}
+
+__global__ void advance_kernel(int* pos_dev, int* step_dev) {
+    ++*pos_dev;
+    ++*step_dev;
+}
+
+// gen[b][*step_dev][:] = logits[b][:] (generate's logits output, [B][n][V]).
+__global__ void __launch_bounds__(256)
+save_logits_kernel(const float4* __restrict__ logits, float4* __restrict__ gen,
+                   const int* __restrict__ step_dev, int V4, int n) {
+    const int b = blockIdx.y;
+    const size_t dst = ((size_t)b * n + *step_dev) * V4;
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V4; v += gridDim.x * blockDim.x)
+        gen[dst + v] = logits[(size_t)b * V4 + v];
 }
 
 // ------------------------------------------------------------ dense projection
@@ -555,6 +615,14 @@ struct MoeDecoder {
     int* row_token = nullptr;
     float* row_weight = nullptr;
     int* dev_err = nullptr;
+    float* attn_part = nullptr;   // decode attention partials [max_batch][H][chunks][hd + 2]
+    int* pos_dev = nullptr;   // next decode position
+    int* step_dev = nullptr;  // next generation step
+    // The captured decode step of generate, for (batch, eos, logits buffer,
+    // new tokens); re-captured when any of them changes.
+    cudaGraphExec_t step_graph = nullptr;
+    int g_B = -1, g_eos = 0, g_n = 0;
+    float* g_logits = nullptr;
     int sm_count = 148;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {};
@@ -705,7 +773,7 @@ cudaError_t launch_rms_pack(MoeDecoder& m, const float* x, int src0, int stride,
 }
 
 template <int HD>
-cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, int pos, bool prefill) {
+cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, bool prefill) {
     const float scale = 1.0f / sqrtf((float)HD);
     if (prefill) {
         const size_t smem = AttnSmem<HD>::kBytes;
@@ -724,45 +792,42 @@ cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, int pos, bool
                                              m.cfg.max_seq, scale, m.a_hi, m.a_lo);
         }
     } else {
-        const size_t smem = sizeof(float) * (size_t)m.cfg.max_seq;
-        dim3 grid(m.H, B);
-        if (tf_mode(m)) {
-            auto k = attn_decode_kernel<HD, true>;
-            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-            k<<<grid, kDecThreads, smem, m.stream>>>(m.qkvbuf, pos, m.H, layer_kc(m, l),
-                                                     layer_vc(m, l), m.cfg.max_seq, scale, m.a_hi, m.a_lo);
-        } else {
-            auto k = attn_decode_kernel<HD, false>;
-            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-            k<<<grid, kDecThreads, smem, m.stream>>>(m.qkvbuf, pos, m.H, layer_kc(m, l),
-                                                     layer_vc(m, l), m.cfg.max_seq, scale, m.a_hi, m.a_lo);
-        }
+        const int nch = (m.cfg.max_seq + kDecChunk - 1) / kDecChunk;
+        attn_decode_partial_kernel<HD><<<dim3(nch, m.H, B), kDecThreads, 0, m.stream>>>(
+            m.qkvbuf, m.pos_dev, m.H, layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale,
+            m.attn_part, nch);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        if (tf_mode(m))
+            attn_decode_combine_kernel<HD, true><<<dim3(m.H, B), HD, 0, m.stream>>>(
+                m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
+        else
+            attn_decode_combine_kernel<HD, false><<<dim3(m.H, B), HD, 0, m.stream>>>(
+                m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_rope_kv(MoeDecoder& m, int l, int T, int rps, int pos0) {
+cudaError_t launch_rope_kv(MoeDecoder& m, int l, int T, int rps, const int* pos_dev) {
     if (m.HD == 128)
-        rope_kv_kernel<128><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, pos0, m.H, m.rope, layer_kc(m, l),
-                                                     layer_vc(m, l), m.cfg.max_seq);
+        rope_kv_kernel<128><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, 0, pos_dev, m.H, m.rope,
+                                                     layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq);
     else
-        rope_kv_kernel<64><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, pos0, m.H, m.rope, layer_kc(m, l),
-                                                    layer_vc(m, l), m.cfg.max_seq);
+        rope_kv_kernel<64><<<T, 256, 0, m.stream>>>(m.qkvbuf, rps, 0, pos_dev, m.H, m.rope,
+                                                    layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq);
     return cudaGetLastError();
 }
 
-// One decoder layer over T rows: B sequences of rps rows each, the first at
-// position pos0 (prefill: rps = S, pos0 = 0; decode: rps = 1, pos0 = pos).
-int run_layer(MoeDecoder& m, int l, int B, int T, int rps, int pos0, bool prefill) {
+// One decoder layer over T rows: B sequences of rps rows each (prefill:
+// rps = S from position 0; decode: rps = 1 at the device position).
+int run_layer(MoeDecoder& m, int l, int B, int T, int rps, bool prefill) {
     DEC_CUDA(launch_rms_pack(m, m.x, 0, 1, T, m.attn_norm[l], m.qkvbuf, (size_t)T * 3 * m.d));
     DEC_CUDA(launch_expert_gemm_rows(m.qkv[l].L, T, m.qkvbuf, m.stream, 1));
-    DEC_CUDA(launch_rope_kv(m, l, T, rps, pos0));
+    DEC_CUDA(launch_rope_kv(m, l, T, rps, prefill ? nullptr : m.pos_dev));
     if (m.HD == 128)
-        DEC_CUDA(launch_attention_t<128>(m, l, B, rps, pos0, prefill));
+        DEC_CUDA(launch_attention_t<128>(m, l, B, rps, prefill));
     else
-        DEC_CUDA(launch_attention_t<64>(m, l, B, rps, pos0, prefill));
+        DEC_CUDA(launch_attention_t<64>(m, l, B, rps, prefill));
     DEC_CUDA(launch_expert_gemm_rows(m.wo[l].L, T, m.x, m.stream, 1));
     DEC_RC(moe_block_forward_device(m.moe[l], m.x, m.x2, T, m.stream));
     std::swap(m.x, m.x2);
@@ -770,39 +835,92 @@ int run_layer(MoeDecoder& m, int l, int B, int T, int rps, int pos0, bool prefil
 }
 
 // Final norm of row src0 + b * stride (b < B), the output head into
-// m.logits, and the greedy ids (into seq_ids[b][step] when step >= 0).
-int run_head(MoeDecoder& m, int B, int src0, int stride, int step, int eos) {
+// m.logits, and the greedy ids; with `record`, also into seq_ids[b][step]
+// (step = *step_dev when step_dev is given) with the EOS bookkeeping.  Leaves
+// the tile list at B rows.
+int run_head(MoeDecoder& m, int B, int src0, int stride, bool record, int step,
+             const int* step_dev, int eos) {
     DEC_CUDA(launch_tiles(m, B));
     DEC_CUDA(launch_rms_pack(m, m.x, src0, stride, B, m.final_norm, m.logits, (size_t)B * m.V));
     DEC_CUDA(launch_expert_gemm_rows(m.head.L, B, m.logits, m.stream, 1));
-    argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, step >= 0 ? m.seq_ids : nullptr,
-                                            m.cfg.max_seq, step, eos, step >= 0 ? m.done : nullptr);
+    argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, record ? m.seq_ids : nullptr,
+                                            m.cfg.max_seq, step, step_dev, eos,
+                                            record ? m.done : nullptr);
     DEC_CUDA(cudaGetLastError());
     return MOE_OK;
 }
 
-// Prefill of B sequences of S tokens from m.tok.
-int run_prefill(MoeDecoder& m, int B, int S, int step, int eos) {
+// Prefill of B sequences of S tokens from m.tok; the device counters then
+// point at position S, generation step 1.
+int run_prefill(MoeDecoder& m, int B, int S, bool record, int eos) {
     const int T = B * S;
     DEC_CUDA(launch_tiles(m, T));
     embed_gather_kernel<<<T, 256, 0, m.stream>>>(m.tok, m.embed, m.V, m.d, m.x, m.dev_err);
     DEC_CUDA(cudaGetLastError());
-    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, T, S, 0, true));
-    DEC_RC(run_head(m, B, S - 1, S, step, eos));
+    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, T, S, true));
+    DEC_RC(run_head(m, B, S - 1, S, record, 0, nullptr, eos));
+    set_counters_kernel<<<1, 1, 0, m.stream>>>(m.pos_dev, m.step_dev, S, 1);
+    DEC_CUDA(cudaGetLastError());
     m.B = B;
     m.pos = S;
     return MOE_OK;
 }
 
-// One decode step: token ids from `tok` (device, [B]) at position m.pos.
-int run_decode(MoeDecoder& m, const int* tok, int step, int eos) {
+// One decode step of the m.B sequences: token ids from `tok` (device, [B])
+// at the device position, which it advances.  Enqueues only -- the host's
+// m.pos is the caller's to advance -- so it can be captured as a graph.  With
+// `record`, the ids go to seq_ids at the device step and, if `save`, the
+// logits to save[b][step] ([B][n][V]).
+int run_decode(MoeDecoder& m, const int* tok, bool record, int eos, float* save, int n) {
     const int B = m.B;
-    DEC_CUDA(launch_tiles(m, B));
     embed_gather_kernel<<<B, 256, 0, m.stream>>>(tok, m.embed, m.V, m.d, m.x, m.dev_err);
     DEC_CUDA(cudaGetLastError());
-    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, B, 1, m.pos, false));
-    DEC_RC(run_head(m, B, 0, 1, step, eos));
-    ++m.pos;
+    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, B, 1, false));
+    DEC_RC(run_head(m, B, 0, 1, record, 0, m.step_dev, eos));
+    if (save) {
+        save_logits_kernel<<<dim3(std::max(1, std::min(m.V / 4 / 256, 64)), B), 256, 0, m.stream>>>(
+            reinterpret_cast<const float4*>(m.logits), reinterpret_cast<float4*>(save),
+            m.step_dev, m.V / 4, n);
+        DEC_CUDA(cudaGetLastError());
+    }
+    advance_kernel<<<1, 1, 0, m.stream>>>(m.pos_dev, m.step_dev);
+    DEC_CUDA(cudaGetLastError());
+    return MOE_OK;
+}
+
+void drop_graph(MoeDecoder& m) {
+    if (m.step_graph) cudaGraphExecDestroy(m.step_graph);
+    m.step_graph = nullptr;
+    m.g_B = -1;
+}
+
+// generate's decode step as a CUDA graph (captured once per batch / eos /
+// logits buffer / length), so that a step costs one launch instead of
+// about ten per layer.
+int step_graph(MoeDecoder& m, int eos, float* save, int n) {
+    if (m.step_graph && m.g_B == m.B && m.g_eos == eos && m.g_logits == save && m.g_n == n)
+        return MOE_OK;
+    drop_graph(m);
+    DEC_CUDA(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeRelaxed));
+    const int rc = run_decode(m, m.next, true, eos, save, n);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(m.stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess)
+        return report_error(MOE_ERR_CUDA, std::string("decode-step capture: ") + cudaGetErrorString(ce));
+    const cudaError_t ie = cudaGraphInstantiate(&m.step_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+        m.step_graph = nullptr;
+        return report_error(MOE_ERR_CUDA, std::string("decode-step graph: ") + cudaGetErrorString(ie));
+    }
+    m.g_B = m.B;
+    m.g_eos = eos;
+    m.g_logits = save;
+    m.g_n = n;
     return MOE_OK;
 }
 
@@ -826,7 +944,6 @@ int validate(const MoeDecoderConfig& c) {
     if (c.d_model % 128 != 0) return bad(MOE_ERR_UNSUPPORTED, "d_model must be a multiple of 128");
     if (c.vocab < 32 || c.vocab % 32 != 0) return bad(MOE_ERR_UNSUPPORTED, "vocab must be a positive multiple of 32");
     if (c.max_batch < 1 || c.max_seq < 1) return bad(MOE_ERR_INVALID, "max_batch and max_seq must be >= 1");
-    if ((size_t)c.max_seq * 4 > 200 * 1024) return bad(MOE_ERR_UNSUPPORTED, "max_seq must be <= 51200");
     if ((long long)c.max_batch * c.max_seq > (1 << 22)) return bad(MOE_ERR_UNSUPPORTED, "max_batch * max_seq too large");
     if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16) return bad(MOE_ERR_INVALID, "unknown precision");
     if (!(c.rms_eps >= 0.0f) || !(c.rope_base > 0.0f)) return bad(MOE_ERR_INVALID, "rms_eps >= 0 and rope_base > 0 required");
@@ -837,6 +954,7 @@ void destroy(MoeDecoder* m) {
     if (!m) return;
     DecDeviceGuard guard(m->cfg.device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    drop_graph(*m);
     for (MoeHandle* h : m->moe) moe_destroy(h);
     for (auto& D : m->qkv) free_dense(D);
     for (auto& D : m->wo) free_dense(D);
@@ -845,7 +963,7 @@ void destroy(MoeDecoder* m) {
     void* bufs[] = {m->embed, m->final_norm, m->rope, m->kc, m->vc, m->x, m->x2, m->qkvbuf,
                     m->logits, m->gen_logits, m->tok, m->next, m->seq_ids, m->done, m->a_hi,
                     m->a_lo, m->mtiles, m->ptiles, m->num_mtiles, m->num_ptiles, m->row_token,
-                    m->row_weight, m->dev_err};
+                    m->row_weight, m->dev_err, m->pos_dev, m->step_dev, m->attn_part};
     for (void* p : bufs)
         if (p) cudaFree(p);
     for (cudaEvent_t e : m->ev)
@@ -910,6 +1028,12 @@ int create(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w, bool device_
     DEC_CUDA(dec_alloc(M, &M.row_weight, sizeof(float) * M.a_rows));
     DEC_CUDA(dec_alloc(M, &M.dev_err, sizeof(int)));
     DEC_CUDA(cudaMemset(M.dev_err, 0, sizeof(int)));
+    DEC_CUDA(dec_alloc(M, &M.attn_part, sizeof(float) * B * M.H *
+                                            ((S + kDecChunk - 1) / kDecChunk) * (M.HD + 2)));
+    DEC_CUDA(dec_alloc(M, &M.pos_dev, sizeof(int)));
+    DEC_CUDA(dec_alloc(M, &M.step_dev, sizeof(int)));
+    DEC_CUDA(cudaMemset(M.pos_dev, 0, sizeof(int)));
+    DEC_CUDA(cudaMemset(M.step_dev, 0, sizeof(int)));
     DEC_CUDA(cudaMemset(M.a_hi, 0, eb * (size_t)M.a_rows * d));
     if (tf) DEC_CUDA(cudaMemset(M.a_lo, 0, (size_t)4 * M.a_rows * d));
     {
@@ -1095,7 +1219,7 @@ int prefill_impl(MoeDecoder& M, const int32_t* tokens, int B, int S, float* logi
                  int32_t* next_ids) {
     MoeDecoder* m = &M;
     DEC_RC(copy_tokens(*m, tokens, (size_t)B * S));
-    DEC_RC(run_prefill(*m, B, S, -1, -1));
+    DEC_RC(run_prefill(*m, B, S, false, -1));
     if (logits)
         DEC_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * B * m->V, cudaMemcpyDeviceToHost, m->stream));
     if (next_ids)
@@ -1107,7 +1231,8 @@ int prefill_impl(MoeDecoder& M, const int32_t* tokens, int B, int S, float* logi
 int decode_step_impl(MoeDecoder& M, const int32_t* tokens, float* logits, int32_t* next_ids) {
     MoeDecoder* m = &M;
     DEC_RC(copy_tokens(*m, tokens, (size_t)m->B));
-    DEC_RC(run_decode(*m, m->tok, -1, -1));
+    DEC_RC(run_decode(*m, m->tok, false, -1, nullptr, 0));
+    ++m->pos;
     if (logits)
         DEC_CUDA(cudaMemcpyAsync(logits, m->logits, sizeof(float) * m->B * m->V, cudaMemcpyDeviceToHost, m->stream));
     if (next_ids)
@@ -1121,6 +1246,7 @@ int generate_impl(MoeDecoder& M, const int32_t* prompt, int B, int S, int max_ne
     MoeDecoder* m = &M;
     const size_t V = m->V, n = max_new_tokens;
     if (logits && m->gen_cap < (size_t)B * n) {
+        drop_graph(*m);   // it writes into the old buffer
         if (m->gen_logits) {
             cudaFree(m->gen_logits);
             m->bytes -= sizeof(float) * m->gen_cap * V;
@@ -1134,17 +1260,18 @@ int generate_impl(MoeDecoder& M, const int32_t* prompt, int B, int S, int max_ne
     DEC_RC(copy_tokens(*m, prompt, (size_t)B * S));
     DEC_CUDA(cudaMemsetAsync(m->done, 0, sizeof(int) * B, s));
     DEC_CUDA(cudaEventRecord(m->ev[0], s));
-    DEC_RC(run_prefill(*m, B, S, 0, eos_id));
+    DEC_RC(run_prefill(*m, B, S, true, eos_id));
     if (logits)
         DEC_CUDA(cudaMemcpy2DAsync(m->gen_logits, n * V * sizeof(float), m->logits, V * sizeof(float),
                                    V * sizeof(float), B, cudaMemcpyDeviceToDevice, s));
     DEC_CUDA(cudaEventRecord(m->ev[1], s));
-    for (int step = 1; step < max_new_tokens; ++step) {
-        DEC_RC(run_decode(*m, m->next, step, eos_id));
-        if (logits)
-            DEC_CUDA(cudaMemcpy2DAsync(m->gen_logits + (size_t)step * V, n * V * sizeof(float), m->logits,
-                                       V * sizeof(float), V * sizeof(float), B,
-                                       cudaMemcpyDeviceToDevice, s));
+    if (max_new_tokens > 1) {
+        float* save = logits ? m->gen_logits : nullptr;
+        DEC_RC(step_graph(*m, eos_id, save, (int)n));
+        for (int step = 1; step < max_new_tokens; ++step) {
+            DEC_CUDA(cudaGraphLaunch(m->step_graph, s));
+            ++m->pos;
+        }
     }
     DEC_CUDA(cudaEventRecord(m->ev[2], s));
     DEC_CUDA(cudaMemcpy2DAsync(ids, n * sizeof(int), m->seq_ids, m->cfg.max_seq * sizeof(int),

@@ -207,3 +207,25 @@ def test_decoder_rejects_bad_arguments():
         # the decoder still works after the rejected calls
         lg, _ = m.prefill(pkg.synthetic_prompt(1, 2, 8, w.vocab))
         assert np.all(np.isfinite(lg))
+
+
+@pytest.mark.gpu
+def test_decoder_generate_reuses_and_recaptures_the_step_graph():
+    """generate captures its decode step as a CUDA graph per (batch, eos,
+    logits buffer, length): calls that change batch or length re-capture,
+    a repeated call replays; each must still match the oracle."""
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, 2, 128)
+    p3 = pkg.synthetic_prompt(8, 3, 12, w.vocab)
+    p1 = p3[:1]
+    with _decoder(w, 2, 128, 0) as m:
+        runs = [(p3, 4), (p1, 5), (p1, 5), (p3, 4)]
+        for prompt, n in runs:
+            ids, lg = m.generate(prompt, n)
+            ids_ref, lg_ref = o.generate(prompt, n)
+            _check_greedy(ids, lg, ids_ref, lg_ref, 0)
+        ids_nl, lg_nl = m.generate(p1, 5, want_logits=False)
+        assert lg_nl is None
+        ids_l, _ = m.generate(p1, 5)
+        assert np.array_equal(ids_nl, ids_l)
