@@ -407,53 +407,77 @@ dispatch_scan_kernel(int* __restrict__ blockhist, int nblk, int E, int granule,
 // memory (single-block dispatch: T fits one 32-token router block, so the
 // block histogram is the whole count and the scan is a prefix over experts).
 // Called by every thread of the CTA; writes the layout only if `write`.
+// Warp 0 scans 32 experts at a time with shuffles (expert e's lane writes
+// its own offsets and tiles); the padding rows are then spread over all
+// warps.
+__device__ __forceinline__ void store_tile(MTile* dst, int expert, int row0, int rows, int mstart,
+                                           int mcount, int second) {
+    int4* p = reinterpret_cast<int4*>(dst);
+    p[0] = make_int4(expert, row0, rows, mstart);
+    p[1] = make_int4(mcount, second, 0, 0);
+}
+
 __device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_off, bool write,
                                     int* __restrict__ counts, int* __restrict__ eoff,
                                     MTile* __restrict__ mtiles, int* __restrict__ num_mtiles,
                                     MTile* __restrict__ ptiles, int* __restrict__ num_ptiles,
                                     int* __restrict__ row_token, float* __restrict__ row_weight) {
-    if (threadIdx.x == 0) {
-        int off = 0, nm = 0, np = 0;
-        for (int e = 0; e < E; ++e) {
-            const int c = cnt[e];
-            s_off[e] = off;
-            if (write) {
-                counts[e] = c;
-                eoff[e] = off;
-                const int mc = (c + kTileM - 1) / kTileM;
-                const int qc = (mc + 1) / 2;
-                for (int i = 0; i < mc; ++i) {
-                    MTile mt;
-                    mt.expert = e; mt.row0 = off + i * kTileM; mt.rows = min(kTileM, c - i * kTileM);
-                    mt.mstart = nm; mt.mcount = mc; mt.pad[0] = mt.pad[1] = mt.pad[2] = 0;
-                    mtiles[nm + i] = mt;
+    static_assert(sizeof(MTile) == 32, "MTile is stored as two int4");
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int off = 0, nm = 0, np = 0;   // running totals of the experts before this group
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < E ? cnt[e] : 0;
+            const int mc = (c + kTileM - 1) / kTileM;
+            const int qc = (mc + 1) / 2;
+            int srow = mc * kTileM, smc = mc, sqc = qc;   // inclusive prefix sums
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, srow, o);
+                const int b = __shfl_up_sync(0xffffffffu, smc, o);
+                const int q = __shfl_up_sync(0xffffffffu, sqc, o);
+                if (lane >= o) {
+                    srow += a;
+                    smc += b;
+                    sqc += q;
                 }
-                for (int i = 0; i < qc; ++i) {
-                    MTile pt;
-                    pt.expert = e; pt.row0 = off + 2 * i * kTileM;
-                    pt.rows = min(kTileM, c - 2 * i * kTileM);
-                    pt.mstart = np; pt.mcount = qc;
-                    pt.pad[0] = max(0, min(kTileM, c - (2 * i + 1) * kTileM));
-                    pt.pad[1] = pt.pad[2] = 0;
-                    ptiles[np + i] = pt;
-                }
-                nm += mc;
-                np += qc;
             }
-            off += (c + kTileM - 1) / kTileM * kTileM;
+            const int my_off = off + srow - mc * kTileM;
+            const int my_m = nm + smc - mc, my_p = np + sqc - qc;
+            if (e < E) {
+                s_off[e] = my_off;
+                if (write) {
+                    counts[e] = c;
+                    eoff[e] = my_off;
+                    for (int i = 0; i < mc; ++i)
+                        store_tile(mtiles + my_m + i, e, my_off + i * kTileM,
+                                   min(kTileM, c - i * kTileM), my_m, mc, 0);
+                    for (int i = 0; i < qc; ++i)
+                        store_tile(ptiles + my_p + i, e, my_off + 2 * i * kTileM,
+                                   min(kTileM, c - 2 * i * kTileM), my_p, qc,
+                                   max(0, min(kTileM, c - (2 * i + 1) * kTileM)));
+                }
+            }
+            off += __shfl_sync(0xffffffffu, srow, 31);
+            nm += __shfl_sync(0xffffffffu, smc, 31);
+            np += __shfl_sync(0xffffffffu, sqc, 31);
         }
-        s_off[E] = off;
-        if (write) {
-            eoff[E] = off;
-            *num_mtiles = nm;
-            *num_ptiles = np;
+        if (lane == 0) {
+            s_off[E] = off;
+            if (write) {
+                eoff[E] = off;
+                *num_mtiles = nm;
+                *num_ptiles = np;
+            }
         }
     }
     __syncthreads();
     if (write) {
-        // Padding rows of every expert block (token -1, weight 0), all threads.
-        for (int e = 0; e < E; ++e)
-            for (int r = s_off[e] + cnt[e] + threadIdx.x; r < s_off[e + 1]; r += blockDim.x) {
+        // Padding rows of every expert block (token -1, weight 0).
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        for (int e = warp; e < E; e += nw)
+            for (int r = s_off[e] + cnt[e] + lane; r < s_off[e + 1]; r += 32) {
                 row_token[r] = -1;
                 row_weight[r] = 0.0f;
             }
@@ -698,8 +722,40 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         reinterpret_cast<float4*>(y)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     __syncthreads();
 
+    // When every K chunk has a stage of its own (nchunks <= stages), all
+    // threads fill the ring with plain 16-byte loads, 16 in flight each, and
+    // the chains run once the whole ring has landed: one SM's bulk copies
+    // deliver only a few bytes per cycle, many threads' loads far more.
+    const bool direct = nchunks <= gm.stages;
+    if (direct) {
+        constexpr int kV = KC / 4;     // float4 per row chunk
+        constexpr int kInFlight = 16;
+        const int nw = blockDim.x >> 5;
+        for (int r = warp; r < rows_used; r += nw) {
+            const float* src = r < E ? wg + (size_t)r * d
+                             : r < E + T ? x + (size_t)(r - E) * d
+                             : (r == E + T ? nr.w : nr.b);
+            for (int v0 = lane; v0 < d / 4; v0 += 32 * kInFlight) {
+                float4 f[kInFlight];
+#pragma unroll
+                for (int u = 0; u < kInFlight; ++u) {
+                    const int v = v0 + 32 * u;
+                    if (v < d / 4) f[u] = __ldg(reinterpret_cast<const float4*>(src) + v);
+                }
+#pragma unroll
+                for (int u = 0; u < kInFlight; ++u) {
+                    const int v = v0 + 32 * u;
+                    if (v < d / 4)
+                        *reinterpret_cast<float4*>(ring + (size_t)(v / kV) * gm.rows * gm.ld +
+                                                   (size_t)r * gm.ld + 4 * (v % kV)) = f[u];
+                }
+            }
+        }
+        __syncthreads();
+    }
+
     if (warp == 0) {
-        if (lane == 0) {
+        if (lane == 0 && !direct) {
             // ------------------------------------------------ loads
             const uint32_t bytes = (uint32_t)rows_used * KC * 4;
             for (int g = 0; g < nchunks; ++g) {
@@ -735,7 +791,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         float acc = 0.0f;
         for (int g = 0; g < nchunks; ++g) {
             const int st = g % gm.stages;
-            if (!mbar_wait(&full[st], (g / gm.stages) & 1, err, kDevErrTimeoutMma)) {
+            if (!direct && !mbar_wait(&full[st], (g / gm.stages) & 1, err, kDevErrTimeoutMma)) {
                 abort_flag = 1;
                 break;
             }
@@ -779,7 +835,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
+            if (lane == 0 && !direct) mbar_arrive(&empty[st]);
         }
         if (active) {
             float v = acc;
@@ -826,6 +882,23 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     // format: each token row is read once (16 loads in flight per thread, so
     // a batch takes about one round trip) and written to its k packed rows.
     const int nv = d / 4;
+    if (direct) {
+        // The token rows (and the norm's weight and bias) are still in the
+        // ring: chunk v / (KC / 4) of row E + t.
+        constexpr int kV = KC / 4;
+        for (int i = tid; i < T * nv; i += blockDim.x) {
+            const int t = i / nv, v = i % nv;
+            const float* sb = ring + (size_t)(v / kV) * gm.rows * gm.ld + 4 * (v % kV);
+            float4 f = *reinterpret_cast<const float4*>(sb + (size_t)(E + t) * gm.ld);
+            if constexpr (kNorm)
+                f = layer_norm_out4(f, nr.mean[t], nr.inv[t],
+                                    *reinterpret_cast<const float4*>(sb + (size_t)(E + T) * gm.ld),
+                                    *reinterpret_cast<const float4*>(sb + (size_t)(E + T + 1) * gm.ld));
+            for (int s2 = 0; s2 < k; ++s2)
+                store_row4<kMode>(a_hi, a_lo, (size_t)s_dest[t * k + s2], nv, v, f);
+        }
+        return;
+    }
     constexpr int kU = 16;
     for (int i0 = tid; i0 < T * nv; i0 += kU * blockDim.x) {
         float4 fv[kU];
