@@ -9,7 +9,8 @@
 //   qkv GEMM        the tcgen05 grouped GEMM with one group and an identity
 //                   row map (combine epilogue, weight 1): qkv = A . Wqkv^T
 //   rope_kv         rotate-half RoPE on q and k (tensor_ops::apply_rope,
-//                   src/tensor.cu:191-210); k and v into the KV cache
+//                   src/tensor.cu:191-210); k and v into the KV cache (a
+//                   decode step does this inside its attention kernel)
 //   attention       causal softmax(q k^T / sqrt(hd)) v per (sequence, head),
 //                   output straight into the A format
 //   o GEMM          x += A . Wo^T (the combine epilogue adds into the
@@ -391,11 +392,32 @@ attn_prefill_kernel(const float* __restrict__ qkv, int S, int H, const float* __
 constexpr int kDecThreads = 128;
 constexpr int kDecChunk = 64;
 
+// Rotate-half RoPE of one head vector held kPer values per lane (lane l has
+// dims l * kPer ..): the partner of dim j < hd/2 is j + hd/2, held by lane
+// l ^ 16.  Same expression as rope_kv_kernel.
+template <int HD>
+__device__ __forceinline__ void rope_lane(float (&v)[HD / 32], int lane,
+                                          const float2* __restrict__ cs_row) {
+    constexpr int kPer = HD / 32;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[i], 16);
+        const int j = (lane & 15) * kPer + i;
+        const float2 cs = __ldg(cs_row + j);
+        v[i] = lane < 16 ? v[i] * cs.x - other * cs.y : v[i] * cs.x + other * cs.y;
+    }
+}
+
+// The decode step's RoPE and KV-cache write are fused in: every CTA rotates
+// its query itself, and the CTA whose chunk holds the current position
+// rotates that position's key and writes key and value to the cache before
+// it scores.
 template <int HD>
 __global__ void __launch_bounds__(kDecThreads)
 attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, int H,
-                           const float* __restrict__ kc, const float* __restrict__ vc,
-                           int max_seq, float scale, float* __restrict__ part, int nch) {
+                           float* __restrict__ kc, float* __restrict__ vc, int max_seq,
+                           float scale, const float2* __restrict__ rope,
+                           float* __restrict__ part, int nch) {
     constexpr int kPer = HD / 32;             // q values per lane
     constexpr int kParts = kDecThreads / HD;  // key classes of the value pass
     constexpr int kWarps = kDecThreads / 32;
@@ -404,7 +426,8 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
     __shared__ float sacc[kDecThreads];
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n = *pos_dev + 1;
+    const int pos = *pos_dev;
+    const int n = pos + 1;
     const int k0 = c * kDecChunk;
     if (k0 >= n) return;
     const int nk = min(kDecChunk, n - k0);
@@ -412,9 +435,30 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
     const float* q = qkv + (size_t)b * 3 * d + h * HD;
     const float* kb = kc + (((size_t)b * H + h) * max_seq + k0) * HD;
     const float* vb = vc + (((size_t)b * H + h) * max_seq + k0) * HD;
+    const float2* cs_row = rope + (size_t)pos * (HD / 2);
     float qv[kPer];
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) qv[i] = q[lane * kPer + i] * scale;
+    for (int i = 0; i < kPer; ++i) qv[i] = q[lane * kPer + i];
+    rope_lane<HD>(qv, lane, cs_row);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) qv[i] *= scale;
+    if (pos < k0 + kDecChunk) {
+        // This chunk holds the new position: its key and value enter the cache.
+        if (warp == 0) {
+            float kv[kPer];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) kv[i] = q[d + lane * kPer + i];
+            rope_lane<HD>(kv, lane, cs_row);
+            float* kd = kc + (((size_t)b * H + h) * max_seq + pos) * HD;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) kd[lane * kPer + i] = kv[i];
+        } else if (warp == 1) {
+            float* vd = vc + (((size_t)b * H + h) * max_seq + pos) * HD;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) vd[lane * kPer + i] = q[2 * d + lane * kPer + i];
+        }
+        __syncthreads();
+    }
     // Scores: warp w takes keys w, w + 4, ...; every K row load is issued
     // before the reductions.
     float dots[kKeysPerWarp];
@@ -423,9 +467,10 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
         const int j = warp + kWarps * i;
         float acc = 0.0f;
         if (j < nk) {
+            // Plain loads: this kernel itself may have written row pos.
             const float* kr = kb + (size_t)j * HD + lane * kPer;
 #pragma unroll
-            for (int e = 0; e < kPer; ++e) acc = fmaf(qv[e], __ldg(kr + e), acc);
+            for (int e = 0; e < kPer; ++e) acc = fmaf(qv[e], kr[e], acc);
         }
         dots[i] = acc;
     }
@@ -458,9 +503,9 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
     for (; j + 3 * kParts < nk; j += 4 * kParts) {
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-            a[u] = fmaf(sp[j + u * kParts], __ldg(vb + (size_t)(j + u * kParts) * HD + col), a[u]);
+            a[u] = fmaf(sp[j + u * kParts], vb[(size_t)(j + u * kParts) * HD + col], a[u]);
     }
-    for (; j < nk; j += kParts) a[0] = fmaf(sp[j], __ldg(vb + (size_t)j * HD + col), a[0]);
+    for (; j < nk; j += kParts) a[0] = fmaf(sp[j], vb[(size_t)j * HD + col], a[0]);
     sacc[tid] = (a[0] + a[1]) + (a[2] + a[3]);
     __syncthreads();
     if (tid < HD) {
@@ -795,7 +840,7 @@ cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, bool prefill)
         const int nch = (m.cfg.max_seq + kDecChunk - 1) / kDecChunk;
         attn_decode_partial_kernel<HD><<<dim3(nch, m.H, B), kDecThreads, 0, m.stream>>>(
             m.qkvbuf, m.pos_dev, m.H, layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale,
-            m.attn_part, nch);
+            m.rope, m.attn_part, nch);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         if (tf_mode(m))
@@ -823,7 +868,8 @@ cudaError_t launch_rope_kv(MoeDecoder& m, int l, int T, int rps, const int* pos_
 int run_layer(MoeDecoder& m, int l, int B, int T, int rps, bool prefill) {
     DEC_CUDA(launch_rms_pack(m, m.x, 0, 1, T, m.attn_norm[l], m.qkvbuf, (size_t)T * 3 * m.d));
     DEC_CUDA(launch_expert_gemm_rows(m.qkv[l].L, T, m.qkvbuf, m.stream, 1));
-    DEC_CUDA(launch_rope_kv(m, l, T, rps, prefill ? nullptr : m.pos_dev));
+    // Decode rotates q and k inside the attention kernel (and writes the cache there).
+    if (prefill) DEC_CUDA(launch_rope_kv(m, l, T, rps, nullptr));
     if (m.HD == 128)
         DEC_CUDA(launch_attention_t<128>(m, l, B, rps, prefill));
     else

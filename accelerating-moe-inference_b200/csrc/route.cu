@@ -752,6 +752,20 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
             }
         }
         __syncthreads();
+        if constexpr (kNorm) {
+            // Every expert's chain reads the same normalised token row:
+            // normalise it once, in place, with the expression the chains
+            // would apply (bit-identical), instead of in each chain.
+            for (int i = tid; i < T * (d / 4); i += blockDim.x) {
+                const int t = i / (d / 4), v = i % (d / 4);
+                float* sb = ring + (size_t)(v / kV) * gm.rows * gm.ld + 4 * (v % kV);
+                float4* xp = reinterpret_cast<float4*>(sb + (size_t)(E + t) * gm.ld);
+                *xp = layer_norm_out4(*xp, nr.mean[t], nr.inv[t],
+                                      *reinterpret_cast<const float4*>(sb + (size_t)(E + T) * gm.ld),
+                                      *reinterpret_cast<const float4*>(sb + (size_t)(E + T + 1) * gm.ld));
+            }
+            __syncthreads();
+        }
     }
 
     if (warp == 0) {
@@ -804,35 +818,44 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
                 // Two register groups alternate: the next 16 columns' loads
                 // are issued before the current group's dependent FMAs.
                 float4 xa[4], wa[4], xb[4], wb[4];
-                auto load = [&](float4 (&xv)[4], float4 (&wv)[4], int kk) {
+                // kApply: the norm is applied here (ring path); the direct
+                // path normalised the token rows in shared memory already.
+                auto run = [&](auto apply_tag) {
+                    constexpr bool kApply = decltype(apply_tag)::value;
+                    auto load = [&](float4 (&xv)[4], float4 (&wv)[4], int kk) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float4 xq = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
-                        if constexpr (kNorm)
-                            xq = layer_norm_out4(xq, m, iv,
-                                                 *reinterpret_cast<const float4*>(nw + kk + 4 * q),
-                                                 *reinterpret_cast<const float4*>(nb + kk + 4 * q));
-                        xv[q] = xq;
-                        wv[q] = *reinterpret_cast<const float4*>(wr + kk + 4 * q);
+                        for (int q = 0; q < 4; ++q) {
+                            float4 xq = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
+                            if constexpr (kApply)
+                                xq = layer_norm_out4(xq, m, iv,
+                                                     *reinterpret_cast<const float4*>(nw + kk + 4 * q),
+                                                     *reinterpret_cast<const float4*>(nb + kk + 4 * q));
+                            xv[q] = xq;
+                            wv[q] = *reinterpret_cast<const float4*>(wr + kk + 4 * q);
+                        }
+                    };
+                    auto chain = [&](const float4 (&xv)[4], const float4 (&wv)[4]) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            acc = __fmaf_rn(xv[q].x, wv[q].x, acc);
+                            acc = __fmaf_rn(xv[q].y, wv[q].y, acc);
+                            acc = __fmaf_rn(xv[q].z, wv[q].z, acc);
+                            acc = __fmaf_rn(xv[q].w, wv[q].w, acc);
+                        }
+                    };
+                    load(xa, wa, 0);
+#pragma unroll
+                    for (int kk = 0; kk < KC; kk += 32) {
+                        load(xb, wb, kk + 16);
+                        chain(xa, wa);
+                        if (kk + 32 < KC) load(xa, wa, kk + 32);
+                        chain(xb, wb);
                     }
                 };
-                auto chain = [&](const float4 (&xv)[4], const float4 (&wv)[4]) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        acc = __fmaf_rn(xv[q].x, wv[q].x, acc);
-                        acc = __fmaf_rn(xv[q].y, wv[q].y, acc);
-                        acc = __fmaf_rn(xv[q].z, wv[q].z, acc);
-                        acc = __fmaf_rn(xv[q].w, wv[q].w, acc);
-                    }
-                };
-                load(xa, wa, 0);
-#pragma unroll
-                for (int kk = 0; kk < KC; kk += 32) {
-                    load(xb, wb, kk + 16);
-                    chain(xa, wa);
-                    if (kk + 32 < KC) load(xa, wa, kk + 32);
-                    chain(xb, wb);
-                }
+                if (kNorm && !direct)
+                    run(std::integral_constant<bool, kNorm>{});
+                else
+                    run(std::integral_constant<bool, false>{});
             }
             __syncwarp();
             if (lane == 0 && !direct) mbar_arrive(&empty[st]);
@@ -883,17 +906,13 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     // a batch takes about one round trip) and written to its k packed rows.
     const int nv = d / 4;
     if (direct) {
-        // The token rows (and the norm's weight and bias) are still in the
-        // ring: chunk v / (KC / 4) of row E + t.
+        // The token rows are still in the ring: chunk v / (KC / 4) of row E + t.
         constexpr int kV = KC / 4;
         for (int i = tid; i < T * nv; i += blockDim.x) {
             const int t = i / nv, v = i % nv;
             const float* sb = ring + (size_t)(v / kV) * gm.rows * gm.ld + 4 * (v % kV);
-            float4 f = *reinterpret_cast<const float4*>(sb + (size_t)(E + t) * gm.ld);
-            if constexpr (kNorm)
-                f = layer_norm_out4(f, nr.mean[t], nr.inv[t],
-                                    *reinterpret_cast<const float4*>(sb + (size_t)(E + T) * gm.ld),
-                                    *reinterpret_cast<const float4*>(sb + (size_t)(E + T + 1) * gm.ld));
+            // Already normalised in place when the norm is active.
+            const float4 f = *reinterpret_cast<const float4*>(sb + (size_t)(E + t) * gm.ld);
             for (int s2 = 0; s2 < k; ++s2)
                 store_row4<kMode>(a_hi, a_lo, (size_t)s_dest[t * k + s2], nv, v, f);
         }
@@ -992,8 +1011,11 @@ bool route_small_geometry(const Layer& L, int T, bool norm, int* kc_out, int* st
     const int rows = L.E_route + T + (norm ? 2 : 0);
     for (int kc : {512, 256, 128, 64}) {
         if (L.d % kc) continue;
+        // 218 KB of ring plus the kernel's ~7 KB of static shared memory stay
+        // under the 227 KB a CTA may hold; that keeps every K chunk resident
+        // (the direct-load path) up to T = 4 at d 4096 with 8 experts.
         const size_t stage = (size_t)rows * (kc + 4) * 4;
-        const int stages = (int)std::min<size_t>(kSmallMaxStages, (190u << 10) / stage);
+        const int stages = (int)std::min<size_t>(kSmallMaxStages, (218u << 10) / stage);
         if (stages >= 3) {
             *kc_out = kc;
             *stages_out = stages;

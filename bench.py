@@ -293,14 +293,16 @@ def reference_arm(args, wl):
     return 0
 
 
-def run_decoder(args, pkg, dev, reps: int = 2):
+def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=False):
     """BASELINE config 4 through moe_decoder_generate: weights N(0, 0.02)
     drawn on the device (seed 2), norms 1; per batch, prefill and decode
     time from CUDA events on the decoder's stream and the host clock around
     the whole call (prompt in, ids and logits [B][128][32000] out)."""
     import numpy as np
     import torch
-    c = C4
+    c = dict(C4)
+    if new_tokens:
+        c["new"] = new_tokens
     d, L, E, ff, V, k = c["d"], c["n_layers"], c["E"], c["ff"], c["vocab"], c["k"]
     gen = torch.Generator(device="cuda").manual_seed(c["seed"])
     rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
@@ -338,6 +340,13 @@ def run_decoder(args, pkg, dev, reps: int = 2):
         p = np.ascontiguousarray(prompt[:B])
         lbuf = np.empty((B, c["new"], V), np.float32)
         m.generate(p, c["new"], logits_out=lbuf)                      # warm-up
+        if profile_range:
+            # One generate inside cudaProfilerStart/Stop (ncu --profile-from-start off).
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            m.generate(p, c["new"], logits_out=lbuf)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
         pre = dec = wall = 0.0
         for _ in range(reps):
             t0 = time.perf_counter()
@@ -376,6 +385,27 @@ def run_decoder(args, pkg, dev, reps: int = 2):
             "how": "moe_decoder_generate (KV-cached greedy decode); prefill/decode from CUDA "
                    "events on the decoder's stream, e2e = host clock around the call; decode "
                    "bytes use the expected distinct experts under uniform routing"}
+
+
+def decoder_only(args):
+    """--workload c4: the toy MoE decoder alone on GPU 0; one JSON line whose
+    value is batch-16 decode tokens/s."""
+    import torch
+    torch.cuda.set_device(0)
+    pkg = _pkg()
+    dev = torch.device("cuda", 0)
+    dec = run_decoder(args, pkg, dev, reps=max(1, args.steps // 25),
+                      new_tokens=args.decoder_new_tokens, profile_range=args.profile_range)
+    b16 = dec["by_batch"][str(max(C4["batches"]))]
+    print(json.dumps({
+        "metric": "toy MoE decoder tokens/s (BASELINE config 4)", "value": b16["decode_tokens_per_s"],
+        "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
+        "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
+        "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights; uniform prompt ids)",
+        "config": {"workload": C4["workload"], "batch": max(C4["batches"]),
+                   "prompt": C4["prompt"], "new_tokens": dec["new_tokens"]},
+        "decoder": dec}))
+    return 0
 
 
 def run_ep(args, wl, pkg, world, rank, local):
@@ -518,7 +548,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c4"], default="c2",
+                    help="c2 (default, the headline layer), c2small, c5, or c4: only the toy "
+                         "MoE decoder (BASELINE config 4), one GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--gemm", choices=["auto", "ctapair", "single"], default="auto",
@@ -534,11 +566,18 @@ def main():
                          "MoE + residual)")
     ap.add_argument("--no-decoder", action="store_true",
                     help="skip the toy MoE decoder section (BASELINE config 4)")
+    ap.add_argument("--decoder-new-tokens", type=int, default=None,
+                    help="generated tokens per sequence in the decoder section (default 128)")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket one decoder generate per batch with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--decode-max-tokens", type=int, default=None,
                     help="override the handle's decode threshold (0..64)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if args.workload == "c4":
+        return decoder_only(args)
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return reference_arm(args, wl)
