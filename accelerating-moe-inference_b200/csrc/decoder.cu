@@ -382,6 +382,281 @@ attn_prefill_kernel(const float* __restrict__ qkv, int S, int H, const float* __
     }
 }
 
+// Prefill on the tensor cores (BF16 precision): one CTA per (128-query
+// block, head, sequence), 128 threads, thread r owning query row r (TMEM
+// lane r).  Two passes over the key blocks up to the diagonal, so the output
+// accumulator never needs rescaling:
+//   pass 1   S = Q K^T (tcgen05, M 128, N 128 keys, K = hd) -> each thread
+//            reads its row of S from TMEM and updates its running max m and
+//            sum l of e^(s - m);
+//   pass 2   S again; P = e^(s - m) / l written as bf16 into shared memory;
+//            O += P V (tcgen05, M 128, N = hd, K = 128 keys), O in TMEM.
+// Operands are staged by the threads themselves from the fp32 cache into the
+// K-major, 128-byte-swizzled layout the GEMMs' descriptors read (16-byte
+// chunk c of row r at chunk c ^ (r % 8)): Q and K as [rows][hd], V
+// transposed as [hd][keys] so that both MMAs read K-major operands.  q is
+// scaled by 1/sqrt(hd) before rounding to bf16, as the CUDA-core kernel
+// scales it.  Every wait is bounded; a CTA whose wait runs out drains its
+// MMAs, frees TMEM and leaves (error flag set).
+constexpr int kTcBQ = 128;   // queries per CTA
+constexpr int kTcBK = 128;   // keys per block
+
+template <int HD>
+struct TcAttn {
+    static constexpr int kQBytes = kTcBQ * HD * 2;      // [128][hd] bf16
+    static constexpr int kKBytes = kTcBK * HD * 2;
+    static constexpr int kVBytes = HD * kTcBK * 2;      // [hd][128 keys] bf16
+    static constexpr int kPBytes = kTcBQ * kTcBK * 2;
+    static constexpr int kQ = 0, kK = kQ + kQBytes, kV = kK + kKBytes, kP = kV + kVBytes;
+    static constexpr int kBar = kP + kPBytes;
+    static constexpr size_t kSmem = (size_t)kBar + 64 + 1024;   // barriers + alignment slack
+    static constexpr uint32_t kIdescS = mma_idesc(1u, kTcBQ, kTcBK);
+    static constexpr uint32_t kIdescO = mma_idesc(1u, kTcBQ, HD);
+};
+
+// Byte offset of element (row, col) of a [rows][w] bf16 K-major operand made
+// of w/64 column blocks of [rows][64], each 128-byte swizzled.
+__device__ __forceinline__ uint32_t sw128_off(int row, int col, int rows) {
+    const int blk = col >> 6, c = col & 63;
+    return (uint32_t)(blk * rows * 128 + row * 128 + ((((c >> 3) ^ (row & 7))) << 4) + (c & 7) * 2);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// One row of 64 fp32 (scaled) into 8 swizzled 16-byte chunks of a bf16 tile.
+__device__ __forceinline__ void stage_row64(uint8_t* tile, int row, int col0, int rows,
+                                            const float* __restrict__ src, float scale, bool zero) {
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (!zero) {
+            const float4 a = *reinterpret_cast<const float4*>(src + ch * 8);
+            const float4 b = *reinterpret_cast<const float4*>(src + ch * 8 + 4);
+            u.x = pack_bf16x2(a.x * scale, a.y * scale);
+            u.y = pack_bf16x2(a.z * scale, a.w * scale);
+            u.z = pack_bf16x2(b.x * scale, b.y * scale);
+            u.w = pack_bf16x2(b.z * scale, b.w * scale);
+        }
+        *reinterpret_cast<uint4*>(tile + sw128_off(row, col0 + ch * 8, rows)) = u;
+    }
+}
+
+__device__ __forceinline__ void fence_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128, 1)
+attn_prefill_tc_kernel(const float* __restrict__ qkv, int S, int H, const float* __restrict__ kc,
+                       const float* __restrict__ vc, int max_seq, float scale,
+                       void* __restrict__ a_out, int* __restrict__ err) {
+    using L = TcAttn<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+    uint8_t* sQ = sm + L::kQ;
+    uint8_t* sK = sm + L::kK;
+    uint8_t* sV = sm + L::kV;
+    uint8_t* sP = sm + L::kP;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);   // [0] S done, [1] O done, [2] drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 3);
+    int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int q0 = qb * kTcBQ;
+    const int d = H * HD;
+    const float* kbase = kc + ((size_t)b * H + h) * max_seq * HD;
+    const float* vbase = vc + ((size_t)b * H + h) * max_seq * HD;
+
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        mbar_init(&bar[2], 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    // Q tile: row tid = query q0 + tid.
+    {
+        const bool valid = q0 + tid < S;
+        const float* src = qkv + ((size_t)b * S + q0 + tid) * 3 * d + h * HD;
+#pragma unroll
+        for (int c0 = 0; c0 < HD; c0 += 64)
+            stage_row64(sQ, tid, c0, kTcBQ, src + c0, scale, !valid);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t t_s = tmem, t_o = tmem + kTcBK;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int qrow = q0 + tid;
+    const int last_q = min(q0 + kTcBQ, S) - 1;
+    const int nblk = last_q / kTcBK + 1;
+    uint32_t ph_s = 0, ph_o = 0;
+    int issued = 0;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+
+    // K block kb into sK (row j = key k0 + j); with_v: V transposed into sV.
+    auto stage_kv = [&](int kb, bool with_v) {
+        const int k0 = kb * kTcBK;
+        const bool kvalid = k0 + tid < S;
+        const float* ks = kbase + (size_t)(k0 + tid) * HD;
+#pragma unroll
+        for (int c0 = 0; c0 < HD; c0 += 64) stage_row64(sK, tid, c0, kTcBK, ks + c0, 1.0f, !kvalid);
+        if (with_v) {
+            // Thread t: keys 2 (t % 64), + 1 and dims [hd/2 * (t / 64), + hd/2).
+            const int kp = tid & 63, half = tid >> 6;
+            const int j0 = 2 * kp;
+            const bool v0 = k0 + j0 < S, v1 = k0 + j0 + 1 < S;
+            const float* r0 = vbase + (size_t)(k0 + j0) * HD;
+            const float* r1 = r0 + HD;
+#pragma unroll 4
+            for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += 4) {
+                const float4 a = v0 ? *reinterpret_cast<const float4*>(r0 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 e = v1 ? *reinterpret_cast<const float4*>(r1 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<uint32_t*>(sV + sw128_off(c + 0, j0, HD)) = pack_bf16x2(a.x, e.x);
+                *reinterpret_cast<uint32_t*>(sV + sw128_off(c + 1, j0, HD)) = pack_bf16x2(a.y, e.y);
+                *reinterpret_cast<uint32_t*>(sV + sw128_off(c + 2, j0, HD)) = pack_bf16x2(a.z, e.z);
+                *reinterpret_cast<uint32_t*>(sV + sw128_off(c + 3, j0, HD)) = pack_bf16x2(a.w, e.w);
+            }
+        }
+        fence_async_shared();
+        tc_fence_before();
+        __syncthreads();
+    };
+    // S = Q K^T into TMEM columns [0, 128), then wait for it.
+    auto mma_s = [&]() -> bool {
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t qa = smem_u32(sQ), ka = smem_u32(sK);
+#pragma unroll
+            for (int kb = 0; kb < HD / 64; ++kb)
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    tc_mma<false>(t_s, smem_desc_sw128(qa + kb * kTcBQ * 128) + 2 * ks,
+                                  smem_desc_sw128(ka + kb * kTcBK * 128) + 2 * ks, L::kIdescS,
+                                  (kb | ks) ? 1u : 0u);
+            tc_commit(&bar[0]);
+        }
+        ++issued;
+        const bool got = mbar_wait(&bar[0], ph_s, err, kDevErrTimeoutMma);
+        ph_s ^= 1u;
+        tc_fence_after();
+        return __syncthreads_and(got);
+    };
+    // This thread's row of S (128 columns) in 4 loads of 32, scaled/masked.
+    auto read_s = [&](int k0, float (&sv)[kTcBK]) {
+#pragma unroll
+        for (int c = 0; c < kTcBK; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_s + lane_base + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int key = k0 + c + j;
+                sv[c + j] = (key > qrow || key >= S) ? -INFINITY : __uint_as_float(r[j]);
+            }
+        }
+    };
+
+    // ---------------------------------------------------------- pass 1
+    for (int kb = 0; kb < nblk && ok; ++kb) {
+        stage_kv(kb, false);
+        if (!mma_s()) { ok = false; break; }
+        float sv[kTcBK];
+        read_s(kb * kTcBK, sv);
+        float mt = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kTcBK; ++j) mt = fmaxf(mt, sv[j]);
+        const float mn = fmaxf(m, mt);
+        float ps = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kTcBK; ++j) ps += sv[j] == -INFINITY ? 0.0f : expf(sv[j] - mn);
+        l = (m == -INFINITY ? 0.0f : l * expf(m - mn)) + ps;
+        m = mn;
+        tc_fence_before();
+        __syncthreads();   // every row of S read before the next block overwrites it
+    }
+    // ---------------------------------------------------------- pass 2
+    const float il = l > 0.0f ? 1.0f / l : 0.0f;
+    for (int kb = 0; kb < nblk && ok; ++kb) {
+        stage_kv(kb, true);
+        if (!mma_s()) { ok = false; break; }
+        float sv[kTcBK];
+        read_s(kb * kTcBK, sv);
+#pragma unroll
+        for (int c0 = 0; c0 < kTcBK; c0 += 8) {
+            float p[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                p[j] = sv[c0 + j] == -INFINITY ? 0.0f : expf(sv[c0 + j] - m) * il;
+            const uint4 u = make_uint4(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]),
+                                       pack_bf16x2(p[4], p[5]), pack_bf16x2(p[6], p[7]));
+            *reinterpret_cast<uint4*>(sP + sw128_off(tid, c0, kTcBQ)) = u;
+        }
+        fence_async_shared();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t pa = smem_u32(sP), va = smem_u32(sV);
+#pragma unroll
+            for (int kb2 = 0; kb2 < kTcBK / 64; ++kb2)
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    tc_mma<false>(t_o, smem_desc_sw128(pa + kb2 * kTcBQ * 128) + 2 * ks,
+                                  smem_desc_sw128(va + kb2 * HD * 128) + 2 * ks, L::kIdescO,
+                                  (kb | kb2 | ks) ? 1u : 0u);
+            tc_commit(&bar[1]);
+        }
+        ++issued;
+        const bool got = mbar_wait(&bar[1], ph_o, err, kDevErrTimeoutMma);
+        ph_o ^= 1u;
+        tc_fence_after();
+        if (!__syncthreads_and(got)) { ok = false; break; }
+    }
+    if (ok) {   // CTA-uniform: the TMEM loads are warp-collective, only the stores are per row
+        // O row -> the o projection's A operand (bf16), cols h * hd ..
+        __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(a_out) + ((size_t)b * S + qrow) * d + h * HD;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_o + lane_base + c, r);
+            tmem_ld_wait();
+            if (qrow < S) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                    const uint4 u = make_uint4(
+                        pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
+                        pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
+                        pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5])),
+                        pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7])));
+                    *reinterpret_cast<uint4*>(orow + c + j) = u;
+                }
+            }
+        }
+    }
+    if (!ok && tid == 0) {
+        // Let every MMA this CTA issued finish before TMEM is released.
+        tc_commit(&bar[2]);
+        mbar_wait(&bar[2], 0, err, kDevErrTimeoutDrain);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 // Decode: one query per (sequence, head) at position *pos_dev (a device
 // counter, so a captured decode step replays at every position) over keys
 // 0..pos, split over the keys: a CTA per (64-key chunk, head, sequence)
@@ -820,7 +1095,15 @@ cudaError_t launch_rms_pack(MoeDecoder& m, const float* x, int src0, int stride,
 template <int HD>
 cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, bool prefill) {
     const float scale = 1.0f / sqrtf((float)HD);
-    if (prefill) {
+    if (prefill && !tf_mode(m)) {
+        const size_t smem = TcAttn<HD>::kSmem;
+        auto k = attn_prefill_tc_kernel<HD>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<dim3((S + kTcBQ - 1) / kTcBQ, m.H, B), 128, smem, m.stream>>>(
+            m.qkvbuf, S, m.H, layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale, m.a_hi,
+            m.dev_err);
+    } else if (prefill) {
         const size_t smem = AttnSmem<HD>::kBytes;
         dim3 grid((S + kAttBQ - 1) / kAttBQ, m.H, B);
         if (tf_mode(m)) {

@@ -139,16 +139,23 @@ def test_decoder_generate_matches_oracle(precision):
 
 
 @pytest.mark.gpu
-def test_decoder_large_prefill_takes_the_pair_gemm():
-    """B * S = 300 rows: the projections run the CTA-pair tiles (>= 256 rows)."""
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("heads,hd", [(2, 128), (4, 64)], ids=["hd128", "hd64"])
+def test_decoder_long_prefill(precision, heads, hd):
+    """2 x 200 rows: the projections run the CTA-pair tiles (>= 256 rows) and
+    the prefill attention spans two query and two key blocks of 128 (the
+    tensor-core kernel in BF16), the causal diagonal crossing a block."""
     pkg = load_pkg()
     w = _weights()
-    o = _oracle(w, 2, 128)
-    prompt = pkg.synthetic_prompt(5, 3, 100, w.vocab)
+    o = _oracle(w, heads, hd)
+    prompt = pkg.synthetic_prompt(5, 2, 200, w.vocab)
     ref = o.last_logits(prompt)
-    with _decoder(w, 2, 128, 0) as m:
+    with _decoder(w, heads, hd, precision, max_seq=256) as m:
         lg, _ = m.prefill(prompt)
-    assert rel_l2(lg, ref) <= TOL[0]
+        ids, lgg = m.generate(prompt, 3)
+    assert rel_l2(lg, ref) <= TOL[precision], rel_l2(lg, ref)
+    ids_ref, lg_ref = o.generate(prompt, 3)
+    _check_greedy(ids, lgg, ids_ref, lg_ref, precision)
 
 
 @pytest.mark.gpu
