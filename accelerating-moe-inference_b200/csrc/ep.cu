@@ -144,11 +144,21 @@ struct EpState {
     void* p2p_ret = nullptr;     // [G][cap_src] result rows, written by the expert ranks
     int* p2p_cnt = nullptr;      // [G][E_local], written by the sources
     unsigned* p2p_flag = nullptr;  // [2][G]: dispatch flag of source s, return flag of rank j
-    int* send_slot = nullptr;    // [T*k] compact row -> destination * cap_src + row
+    int* send_slot = nullptr;    // unused by the deduplicated transport
+    // Deduplicated fused transport: one row per (token, destination rank).
+    int kmax = 1;                // selections one row can carry: min(top_k, E_local)
+    int2* p2p_meta = nullptr;    // [G][cap_src][kmax] {pos * 256 + local expert, weight bits}, x = -1 ends
+    int* dest_hist = nullptr;    // [blocks][G] tokens per destination per 32-token block (scanned in place)
+    int* dest_cnt = nullptr;     // [G] rows sent to each rank
+    int* dest_off = nullptr;     // [G + 1]
+    int* slot_dd = nullptr;      // [cap_T][G] row of token t at rank g (-1: none)
+    float* y_recv = nullptr;     // [G * cap_src][d] fp32: weighted sum of the local experts per received row
+    int* rows_recv = nullptr;    // [G] rows received from each source this step
     void** d_peer_recv = nullptr;  // [G] every rank's p2p_recv (own included), device array
     void** d_peer_ret = nullptr;
     int** d_peer_cnt = nullptr;
     unsigned** d_peer_flag = nullptr;
+    int2** d_peer_meta = nullptr;
     std::vector<void*> ipc_opened;  // mappings of the other ranks' buffers
     // Round-robin placement: rank r holds experts r, r + G, r + 2G, ...;
     // eperm[e] = (e % G) * E_local + e / G is expert e's dispatch position
@@ -165,8 +175,14 @@ void ep_free_buffers(EpState& S) {
                     S.recv_rows, (void*)S.ret_send, (void*)S.ret_recv, (void*)S.cnt_recv,
                     (void*)S.cnt_scan, S.p2p_recv, S.p2p_ret, (void*)S.p2p_cnt,
                     (void*)S.p2p_flag, (void*)S.send_slot, (void*)S.d_peer_recv,
-                    (void*)S.d_peer_ret, (void*)S.d_peer_cnt, (void*)S.d_peer_flag})
+                    (void*)S.d_peer_ret, (void*)S.d_peer_cnt, (void*)S.d_peer_flag,
+                    (void*)S.p2p_meta, (void*)S.dest_hist, (void*)S.dest_cnt, (void*)S.dest_off,
+                    (void*)S.slot_dd, (void*)S.y_recv, (void*)S.rows_recv, (void*)S.d_peer_meta})
         if (p) cudaFree(p);
+    S.p2p_meta = nullptr;
+    S.dest_hist = S.dest_cnt = S.dest_off = S.slot_dd = S.rows_recv = nullptr;
+    S.y_recv = nullptr;
+    S.d_peer_meta = nullptr;
     S.p2p_recv = S.p2p_ret = nullptr;
     S.p2p_cnt = S.send_slot = nullptr;
     S.p2p_flag = nullptr;
@@ -443,11 +459,12 @@ constexpr unsigned long long kPeerWaitNs = 5000000000ull;   // 5 s
 // included) -- raise flag [which][this rank] in j's flag words to `epoch`.
 __global__ void ep_signal_kernel(int* const* peer_cnt, const int* __restrict__ counts,
                                  unsigned* const* peer_flag, int G, int El, int rank, int which,
-                                 unsigned epoch) {
+                                 unsigned epoch, const int* __restrict__ rows = nullptr) {
     const int j = threadIdx.x;
     if (j >= G) return;
     if (peer_cnt)
         for (int e = 0; e < El; ++e) peer_cnt[j][rank * El + e] = counts[j * El + e];
+    if (peer_cnt && rows) peer_cnt[j][G * El + rank] = rows[j];   // rows this rank sends j
     __threadfence_system();
     st_release_sys(peer_flag[j] + which * G + rank, epoch);
 }
@@ -458,7 +475,7 @@ __global__ void ep_signal_kernel(int* const* peer_cnt, const int* __restrict__ c
 // capacity -- or zeros after a timeout, so a failed step moves no rows.
 __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned epoch,
                                const int* cnt_src, int* __restrict__ cnt_a, int* __restrict__ cnt_b,
-                               int n, int cap, int* err) {
+                               int n, int cap, int* err, int* __restrict__ rows_out = nullptr) {
     __shared__ int timed_out;
     if (threadIdx.x == 0) timed_out = 0;
     __syncthreads();
@@ -483,6 +500,238 @@ __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned 
         cnt_a[i] = c;
         cnt_b[i] = c;
     }
+    if (rows_out)   // the sources' row counts follow their n count words
+        for (int i = threadIdx.x; i < G; i += blockDim.x)
+            rows_out[i] = timed_out ? 0 : min(max(__ldcg(cnt_src + n + i), 0), cap);
+}
+
+// ------------------------------------------------------------ deduplicated transport
+// A token whose k experts fall on the same rank crosses NVLink once for that
+// rank: the source sends one row per (token, destination rank) with the
+// token's selections on that rank as metadata; the rank runs the row through
+// each of its experts, sums their weighted outputs into one fp32 row
+// (y_recv, the down GEMM's combine epilogue), and returns that single row;
+// the source adds its ranks' rows in ascending rank order.  Rows of one
+// source keep ascending token order, so each selection also carries its
+// position inside its expert's block from this source -- exactly the compact
+// dispatch scan's -- and the receiver places it without a scan of its own.
+
+// Per 32-token block: how many of its tokens send to each rank (G <= 32).
+__global__ void __launch_bounds__(256)
+ep_dest_hist_kernel(const int* __restrict__ idx, int T, int k, int El, int G,
+                    int* __restrict__ dest_hist) {
+    __shared__ unsigned s_mask[32];
+    const int t0 = blockIdx.x * kRouteTokens;
+    const int n_tok = min(kRouteTokens, T - t0);
+    if (threadIdx.x < 32) s_mask[threadIdx.x] = 0u;
+    __syncthreads();
+    const int i = threadIdx.x;
+    if (i < n_tok * k) {
+        const int e = idx[(size_t)t0 * k + i];
+        if (e >= 0 && e < El * G) atomicOr(&s_mask[e / El], 1u << (i / k));
+    }
+    __syncthreads();
+    if (threadIdx.x < G) dest_hist[(size_t)blockIdx.x * G + threadIdx.x] = __popc(s_mask[threadIdx.x]);
+}
+
+// Rows and metadata into the destination ranks' receive buffers.  ebase /
+// gbase: the scanned per-block bases of the expert positions and of the
+// destinations (relative to each one's start).  kMode 0: bf16 rows, 2: fp32.
+template <int kMode>
+__global__ void __launch_bounds__(256)
+ep_dedup_push_kernel(const float* __restrict__ x, int T, int d, int k, int El, int G, int kmax,
+                     const int* __restrict__ idx, const float* __restrict__ wts,
+                     const int* __restrict__ ebase, const int* __restrict__ gbase,
+                     void* const* __restrict__ peer_recv, int2* const* __restrict__ peer_meta,
+                     int cap, int rank, int* __restrict__ slot_dd) {
+    __shared__ unsigned s_emask[kMaxExperts];
+    __shared__ unsigned s_gmask[32];
+    __shared__ int s_list[kRouteTokens * 32];   // (token << 16) | (g << 11)... packed below
+    __shared__ int s_row[kRouteTokens * 32];
+    __shared__ int s_n;
+    const int Eg = El * G;
+    const int blk = blockIdx.x;
+    const int t0 = blk * kRouteTokens;
+    const int n_tok = min(kRouteTokens, T - t0);
+    for (int e = threadIdx.x; e < Eg; e += blockDim.x) s_emask[e] = 0u;
+    if (threadIdx.x < 32) s_gmask[threadIdx.x] = 0u;
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_tok * k; i += blockDim.x) {
+        const int e = idx[(size_t)t0 * k + i];
+        if (e >= 0 && e < Eg) {
+            atomicOr(&s_emask[e], 1u << (i / k));
+            atomicOr(&s_gmask[e / El], 1u << (i / k));
+        }
+    }
+    __syncthreads();
+    // One thread per (token, destination): its row index, metadata and slot.
+    for (int i = threadIdx.x; i < n_tok * G; i += blockDim.x) {
+        const int tl = i / G, g = i % G;
+        const unsigned below = (1u << tl) - 1u;
+        const int t = t0 + tl;
+        if (!((s_gmask[g] >> tl) & 1u)) {
+            slot_dd[(size_t)t * G + g] = -1;
+            continue;
+        }
+        const int r = gbase[(size_t)blk * G + g] + __popc(s_gmask[g] & below);
+        slot_dd[(size_t)t * G + g] = r;
+        int2* meta = peer_meta[g] + ((size_t)rank * cap + r) * kmax;
+        int j = 0;
+        for (int sl = 0; sl < k; ++sl) {
+            const int e = idx[(size_t)t * k + sl];
+            if (e < 0 || e >= Eg || e / El != g) continue;
+            const int pos = ebase[(size_t)blk * Eg + e] + __popc(s_emask[e] & below);
+            if (j < kmax) meta[j] = make_int2(pos * 256 + (e - g * El), __float_as_int(wts[(size_t)t * k + sl]));
+            ++j;
+        }
+        for (; j < kmax; ++j) meta[j] = make_int2(-1, 0);
+        const int n = atomicAdd(&s_n, 1);
+        s_list[n] = tl * 32 + g;
+        s_row[n] = r;
+    }
+    __syncthreads();
+    // Row copies, one warp per (token, destination).
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int p = warp; p < s_n; p += nw) {
+        const int tl = s_list[p] / 32, g = s_list[p] % 32;
+        const float4* src = reinterpret_cast<const float4*>(x + (size_t)(t0 + tl) * d);
+        const size_t row = (size_t)rank * cap + s_row[p];
+        if constexpr (kMode == 0) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peer_recv[g]) + row * d);
+            for (int v = lane; v < d / 8; v += 32) {
+                const float4 a = __ldg(src + 2 * v), b = __ldg(src + 2 * v + 1);
+                __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+                __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+                dst[v] = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
+                                    *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
+            }
+        } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(peer_recv[g]) + row * d);
+            for (int v = lane; v < d / 4; v += 32) dst[v] = __ldg(src + v);
+        }
+    }
+}
+
+// One warp per received row (source s, row r < rows_recv[s]): its metadata
+// places it in each of its local experts' GEMM blocks (row_token = the
+// received slot s * cap + r, row_weight = the routing weight), the row is
+// converted into each of those A rows, and its y_recv row is zeroed for the
+// down GEMM's combine epilogue.  Rows and metadata were written by other
+// GPUs: read through L2 only.
+template <bool kTf32x3>
+__global__ void __launch_bounds__(256)
+ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ meta,
+                     const int* __restrict__ rows_recv, int cap, int d, int G, int El, int kmax,
+                     const int* __restrict__ base, const int* __restrict__ eoff,
+                     int* __restrict__ row_token, float* __restrict__ row_weight,
+                     void* __restrict__ a_hi, void* __restrict__ a_lo, float* __restrict__ y_recv) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t i = (size_t)blockIdx.x * 8 + warp;
+    if (i >= (size_t)G * cap) return;
+    const int s = (int)(i / cap), r = (int)(i % cap);
+    if (r >= rows_recv[s]) return;
+    int prow[8];
+    int n = 0;
+    const int lim = eoff[El];
+    for (int j = 0; j < kmax && j < 8; ++j) {
+        const int2 m = __ldcg(meta + i * kmax + j);
+        if (m.x < 0) break;
+        const int e = m.x & 255, pos = m.x >> 8;
+        if (e >= El) break;
+        const int pr = eoff[e] + base[s * El + e] + pos;
+        if (pr >= lim) continue;   // inconsistent metadata: never expected, never written past the blocks
+        prow[n] = pr;
+        if (lane == 0) {
+            row_token[prow[n]] = (int)i;
+            row_weight[prow[n]] = __int_as_float(m.y);
+        }
+        ++n;
+    }
+    float4* yr = reinterpret_cast<float4*>(y_recv + i * d);
+    for (int v = lane; v < d / 4; v += 32) yr[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if constexpr (kTf32x3) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + i * d);
+        for (int v = lane; v < d / 4; v += 32) {
+            const float4 f = __ldcg(src + v);
+            float4 h, l;
+            h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+            h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+            h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+            h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+            for (int j = 0; j < n; ++j) {
+                reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow[j] * d)[v] = h;
+                reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow[j] * d)[v] = l;
+            }
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + i * d);
+        for (int v = lane; v < d / 8; v += 32) {
+            const uint4 u = __ldcg(src + v);
+            for (int j = 0; j < n; ++j)
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow[j] * d)[v] = u;
+        }
+    }
+}
+
+// One warp per received row: its summed expert output back to the source's
+// return buffer, row rank * cap + r (bf16 in BF16 precision, fp32 in FP32).
+template <bool kF32>
+__global__ void __launch_bounds__(256)
+ep_return_push_kernel(const float* __restrict__ y_recv, const int* __restrict__ rows_recv, int cap,
+                      int d, int G, int rank, void* const* __restrict__ peer_ret) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t i = (size_t)blockIdx.x * 8 + warp;
+    if (i >= (size_t)G * cap) return;
+    const int s = (int)(i / cap), r = (int)(i % cap);
+    if (r >= rows_recv[s]) return;
+    const float4* src = reinterpret_cast<const float4*>(y_recv + i * d);
+    const size_t row = (size_t)rank * cap + r;
+    if constexpr (kF32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(peer_ret[s]) + row * d);
+        for (int v = lane; v < d / 4; v += 32) dst[v] = src[v];
+    } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peer_ret[s]) + row * d);
+        for (int v = lane; v < d / 8; v += 32) {
+            const float4 a = src[2 * v], b = src[2 * v + 1];
+            __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
+            __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
+            dst[v] = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
+                                *reinterpret_cast<uint32_t*>(&p2), *reinterpret_cast<uint32_t*>(&p3));
+        }
+    }
+}
+
+// y[t] = sum over ranks g (ascending) of the row rank g returned for token t
+// (written by other GPUs: read through L2 only).  One warp per token; every
+// element of y[t] is written, so y needs no clearing.
+template <bool kF32>
+__global__ void __launch_bounds__(256)
+ep_dd_combine_kernel(const void* __restrict__ ret, const int* __restrict__ slot_dd, int T, int G,
+                     int cap, int d, float* __restrict__ y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    int rows[32];
+    for (int g = 0; g < G; ++g) rows[g] = slot_dd[(size_t)t * G + g];
+    float4* dst = reinterpret_cast<float4*>(y + (size_t)t * d);
+    for (int v = lane; v < d / 4; v += 32) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int g = 0; g < G; ++g) {
+            if (rows[g] < 0) continue;
+            const size_t rr = (size_t)g * cap + rows[g];
+            float4 f;
+            if constexpr (kF32) {
+                f = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(ret) + rr * d) + v);
+            } else {
+                const uint2 u = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(ret) + rr * d) + v);
+                f = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+            }
+            acc.x += f.x; acc.y += f.y; acc.z += f.z; acc.w += f.w;
+        }
+        dst[v] = acc;
+    }
 }
 
 // Collective (every rank of the group, once, at creation): allocate the
@@ -491,11 +740,14 @@ __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned 
 int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     EpState& S = *L.ep;
     const int G = S.world, El = S.e_local;
+    if (G > 32) return report_error(MOE_ERR_UNSUPPORTED, "the fused transport supports up to 32 ranks");
     S.cap_T = capT;
-    S.cap_src = capT * std::min(L.k, El);
+    S.cap_src = capT;   // one row per (token, destination)
+    S.kmax = std::min(L.k, El);
     S.row_bytes = (size_t)L.d * elem_bytes(L);
     const size_t rows_local = (size_t)capT * L.k;
     const size_t seg_bytes = (size_t)G * S.cap_src * S.row_bytes;
+    const int nblk = (capT + kRouteTokens - 1) / kRouteTokens;
     cudaError_t e = cudaSuccess;
     auto A = [&](void** p, size_t b) {
         if (e == cudaSuccess) e = cudaMalloc(p, b ? b : 256);
@@ -508,20 +760,29 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     A((void**)&S.cnt_scan, (size_t)G * El * sizeof(int));
     A(&S.p2p_recv, seg_bytes);
     A(&S.p2p_ret, seg_bytes);
-    A((void**)&S.p2p_cnt, (size_t)G * El * sizeof(int));
+    // Count words: [G][El] per-expert rows from each source, then [G] rows.
+    A((void**)&S.p2p_cnt, (size_t)G * (El + 1) * sizeof(int));
     A((void**)&S.p2p_flag, 2 * G * sizeof(unsigned));
+    A((void**)&S.p2p_meta, (size_t)G * S.cap_src * S.kmax * sizeof(int2));
+    A((void**)&S.dest_hist, (size_t)nblk * G * sizeof(int));
+    A((void**)&S.dest_cnt, G * sizeof(int));
+    A((void**)&S.dest_off, (G + 1) * sizeof(int));
+    A((void**)&S.slot_dd, (size_t)capT * G * sizeof(int));
+    A((void**)&S.y_recv, (size_t)G * S.cap_src * L.d * sizeof(float));
+    A((void**)&S.rows_recv, G * sizeof(int));
     A((void**)&S.d_peer_recv, G * sizeof(void*));
     A((void**)&S.d_peer_ret, G * sizeof(void*));
     A((void**)&S.d_peer_cnt, G * sizeof(int*));
     A((void**)&S.d_peer_flag, G * sizeof(unsigned*));
+    A((void**)&S.d_peer_meta, G * sizeof(int2*));
     if (e == cudaSuccess) e = cudaMemset(S.p2p_flag, 0, 2 * G * sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(S.p2p_cnt, 0, (size_t)G * El * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(S.p2p_cnt, 0, (size_t)G * (El + 1) * sizeof(int));
     if (e != cudaSuccess)
         return report_error(MOE_ERR_OOM, std::string("expert-parallel buffers: ") +
                                              cudaGetErrorString(e));
-    // Handles of this rank's four shared buffers, all-gathered.
-    constexpr int kBufs = 4;
-    void* mine[kBufs] = {S.p2p_recv, S.p2p_ret, S.p2p_cnt, S.p2p_flag};
+    // Handles of this rank's five shared buffers, all-gathered.
+    constexpr int kBufs = 5;
+    void* mine[kBufs] = {S.p2p_recv, S.p2p_ret, S.p2p_cnt, S.p2p_flag, S.p2p_meta};
     std::vector<cudaIpcMemHandle_t> h_all((size_t)G * kBufs), h_mine(kBufs);
     for (int i = 0; i < kBufs && e == cudaSuccess; ++i) e = cudaIpcGetMemHandle(&h_mine[i], mine[i]);
     void* d_hbuf = nullptr;
@@ -562,7 +823,8 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
                                               cudaGetErrorString(e));
     std::vector<void*> col(G);
     void** dst[kBufs] = {S.d_peer_recv, S.d_peer_ret, reinterpret_cast<void**>(S.d_peer_cnt),
-                         reinterpret_cast<void**>(S.d_peer_flag)};
+                         reinterpret_cast<void**>(S.d_peer_flag),
+                         reinterpret_cast<void**>(S.d_peer_meta)};
     for (int i = 0; i < kBufs && e == cudaSuccess; ++i) {
         for (int j = 0; j < G; ++j) col[j] = ptr[(size_t)j * kBufs + i];
         e = cudaMemcpy(dst[i], col.data(), G * sizeof(void*), cudaMemcpyHostToDevice);
@@ -585,95 +847,104 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     };
     cudaError_t ce;
     L.prof_n = 0;
-    // 1-2: route; compact dispatch straight into the expert ranks' buffers.
+    // 1-2: route; per (token, destination rank) one row and its selections
+    // straight into the destination's receive buffer.
+    const int nblk = (T + kRouteTokens - 1) / kRouteTokens;
     prof_mark(L, 0, s);
     if (T > 0) {
         if ((ce = launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, NormRef{},
                                 S.eperm)) != cudaSuccess)
             return cuda_err(ce, "router");
         prof_mark(L, 1, s);
-        if ((ce = launch_scan_generic(W.blockhist, (T + kRouteTokens - 1) / kRouteTokens, Eg, 1,
-                                      W.counts, S.send_eoff, nullptr, nullptr, nullptr, nullptr,
-                                      nullptr, nullptr, s)) != cudaSuccess)
+        // Expert positions (compact): per-expert counts to the ranks, and each
+        // selection's position inside its expert's block from this source.
+        if ((ce = launch_scan_generic(W.blockhist, nblk, Eg, 1, W.counts, S.send_eoff, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, s)) != cudaSuccess)
             return cuda_err(ce, "dispatch scan");
+        ep_dest_hist_kernel<<<nblk, 256, 0, s>>>(W.idx, T, L.k, El, G, S.dest_hist);
+        if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "destination histogram");
+        if ((ce = launch_scan_generic(S.dest_hist, nblk, G, 1, S.dest_cnt, S.dest_off, nullptr,
+                                      nullptr, nullptr, nullptr, nullptr, nullptr, s)) != cudaSuccess)
+            return cuda_err(ce, "destination scan");
         prof_mark(L, 5, s);
-        PeerDst pd;
-        pd.bases = S.d_peer_recv;
-        pd.cap = S.cap_src;
-        pd.rank = S.rank;
-        pd.e_local = El;
-        pd.eoff = S.send_eoff;
-        pd.slot = S.send_slot;
-        if ((ce = launch_dispatch_push(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w, pd, s)) !=
-            cudaSuccess)
-            return cuda_err(ce, "dispatch push");
+        if (three_pass(L))
+            ep_dedup_push_kernel<2><<<nblk, 256, 0, s>>>(x, T, L.d, L.k, El, G, S.kmax, W.idx,
+                                                         W.wts, W.blockhist, S.dest_hist,
+                                                         S.d_peer_recv, S.d_peer_meta, S.cap_src,
+                                                         S.rank, S.slot_dd);
+        else
+            ep_dedup_push_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.k, El, G, S.kmax, W.idx,
+                                                         W.wts, W.blockhist, S.dest_hist,
+                                                         S.d_peer_recv, S.d_peer_meta, S.cap_src,
+                                                         S.rank, S.slot_dd);
+        if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "dispatch push");
     } else {
         prof_mark(L, 5, s);
-        if ((ce = cudaMemsetAsync(W.counts, 0, Eg * sizeof(int), s)) != cudaSuccess)
+        if ((ce = cudaMemsetAsync(W.counts, 0, Eg * sizeof(int), s)) != cudaSuccess ||
+            (ce = cudaMemsetAsync(S.dest_cnt, 0, G * sizeof(int), s)) != cudaSuccess)
             return cuda_err(ce, "counts");
     }
-    // 3-4: counts and flags to every rank; wait for every source's.
+    // 3-4: counts, row counts and flags to every rank; wait for every source's.
     const int sig_threads = (G + 31) / 32 * 32;
     ep_signal_kernel<<<1, sig_threads, 0, s>>>(S.d_peer_cnt, W.counts, S.d_peer_flag, G, El,
-                                               S.rank, 0, epoch);
+                                               S.rank, 0, epoch, S.dest_cnt);
     ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 0, epoch, S.p2p_cnt,
                                                             S.cnt_recv, S.cnt_scan, G * El,
-                                                            S.cap_src, W.dev_err);
+                                                            S.cap_src, W.dev_err, S.rows_recv);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "dispatch signal");
     prof_mark(L, 2, s);
-    // Arrival scan and arrangement; the received total is known on the
-    // device only, so the launches are sized by bounds.
+    // Arrival scan (per-source bases inside each local expert's block) and
+    // arrangement: each received row into each of its experts' GEMM rows.
     if ((ce = launch_scan_generic(S.cnt_scan, G, El, kTileM, W.counts, W.eoff, W.mtiles,
                                   W.num_mtiles, W.ptiles, W.num_ptiles, W.row_token,
                                   W.row_weight, s)) != cudaSuccess)
         return cuda_err(ce, "arrival scan");
-    const int R_bound = G * S.cap_src;
-    const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
-    const int grid = (R_bound + 7) / 8;
+    const size_t R_bound = (size_t)G * S.cap_src;
+    const int grid = (int)((R_bound + 7) / 8);
     if (three_pass(L))
-        ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.p2p_recv, R_bound, L.d, G, El, S.cap_src,
-                                                        S.cnt_recv, S.cnt_scan, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo);
+        ep_dd_arrange_kernel<true><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
+                                                        S.cap_src, L.d, G, El, S.kmax, S.cnt_scan,
+                                                        W.eoff, W.row_token, W.row_weight, W.a_hi,
+                                                        W.a_lo, S.y_recv);
     else
-        ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.p2p_recv, R_bound, L.d, G, El, S.cap_src,
-                                                         S.cnt_recv, S.cnt_scan, W.eoff, W.row_token,
-                                                         W.row_weight, W.a_hi, W.a_lo);
+        ep_dd_arrange_kernel<false><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
+                                                         S.cap_src, L.d, G, El, S.kmax,
+                                                         S.cnt_scan, W.eoff, W.row_token,
+                                                         W.row_weight, W.a_hi, W.a_lo, S.y_recv);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
-    // 5-6: the local experts; the down GEMM stores each result in its
-    // source rank's return buffer.  The expected received count (T * k,
-    // this rank's own routed rows) sizes the GEMM launch; any count is run
-    // correctly.
+    // 5-6: the local experts; the down GEMM's combine epilogue adds each
+    // expert's weighted output into its received row's y_recv row.  The
+    // expected routed rows (T * k, this rank's own) size the GEMM launch; any
+    // count is run correctly.
     const int R_est = std::max(T, 1) * L.k;
     prof_mark(L, 3, s);
     if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 0)) != cudaSuccess)
         return cuda_err(ce, "gate/up GEMM");
     prof_mark(L, 4, s);
-    PeerDst ret;
-    ret.bases = S.d_peer_ret;
-    ret.cap = S.cap_src;
-    ret.rank = S.rank;
-    if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 2, &ret)) != cudaSuccess)
+    if ((ce = launch_expert_gemm_rows(L, R_est, S.y_recv, s, 1)) != cudaSuccess)
         return cuda_err(ce, "down GEMM");
-    // 7: return flags; wait for every expert rank's.
+    // 7: one summed row per received row back to its source; return flags.
     prof_mark(L, 6, s);
+    if (three_pass(L))
+        ep_return_push_kernel<true><<<grid, 256, 0, s>>>(S.y_recv, S.rows_recv, S.cap_src, L.d, G,
+                                                         S.rank, S.d_peer_ret);
+    else
+        ep_return_push_kernel<false><<<grid, 256, 0, s>>>(S.y_recv, S.rows_recv, S.cap_src, L.d, G,
+                                                          S.rank, S.d_peer_ret);
     ep_signal_kernel<<<1, sig_threads, 0, s>>>(nullptr, nullptr, S.d_peer_flag, G, El, S.rank, 1,
                                                epoch);
     ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 1, epoch, nullptr,
                                                             nullptr, nullptr, 0, 0, W.dev_err);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "return signal");
-    // 8: weighted combine into y.
+    // 8: y[t] = sum of its ranks' rows, ascending rank.
     prof_mark(L, 7, s);
     if (T > 0) {
-        if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s)) != cudaSuccess)
-            return cuda_err(ce, "y memset");
-        const int rows = T * L.k;
         if (three_pass(L))
-            ep_combine_kernel<true><<<(rows + 7) / 8, 256, 0, s>>>(S.p2p_ret, rows, L.d, S.send_tok,
-                                                                   S.send_w, S.send_slot, y);
+            ep_dd_combine_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(S.p2p_ret, S.slot_dd, T, G,
+                                                                   S.cap_src, L.d, y);
         else
-            ep_combine_kernel<false><<<(rows + 7) / 8, 256, 0, s>>>(S.p2p_ret, rows, L.d,
-                                                                    S.send_tok, S.send_w,
-                                                                    S.send_slot, y);
+            ep_dd_combine_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(S.p2p_ret, S.slot_dd, T, G,
+                                                                    S.cap_src, L.d, y);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
     prof_mark(L, kProfEnd, s);
