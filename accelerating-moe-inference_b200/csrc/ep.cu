@@ -144,7 +144,6 @@ struct EpState {
     void* p2p_ret = nullptr;     // [G][cap_src] result rows, written by the expert ranks
     int* p2p_cnt = nullptr;      // [G][E_local], written by the sources
     unsigned* p2p_flag = nullptr;  // [2][G]: dispatch flag of source s, return flag of rank j
-    int* send_slot = nullptr;    // unused by the deduplicated transport
     // Deduplicated fused transport: one row per (token, destination rank).
     int kmax = 1;                // selections one row can carry: min(top_k, E_local)
     int2* p2p_meta = nullptr;    // [G][cap_src][kmax] {pos * 256 + local expert, weight bits}, x = -1 ends
@@ -174,7 +173,7 @@ void ep_free_buffers(EpState& S) {
     for (void* p : {S.send_rows, (void*)S.send_tok, (void*)S.send_w, (void*)S.send_eoff,
                     S.recv_rows, (void*)S.ret_send, (void*)S.ret_recv, (void*)S.cnt_recv,
                     (void*)S.cnt_scan, S.p2p_recv, S.p2p_ret, (void*)S.p2p_cnt,
-                    (void*)S.p2p_flag, (void*)S.send_slot, (void*)S.d_peer_recv,
+                    (void*)S.p2p_flag, (void*)S.d_peer_recv,
                     (void*)S.d_peer_ret, (void*)S.d_peer_cnt, (void*)S.d_peer_flag,
                     (void*)S.p2p_meta, (void*)S.dest_hist, (void*)S.dest_cnt, (void*)S.dest_off,
                     (void*)S.slot_dd, (void*)S.y_recv, (void*)S.rows_recv, (void*)S.d_peer_meta})
@@ -184,7 +183,7 @@ void ep_free_buffers(EpState& S) {
     S.y_recv = nullptr;
     S.d_peer_meta = nullptr;
     S.p2p_recv = S.p2p_ret = nullptr;
-    S.p2p_cnt = S.send_slot = nullptr;
+    S.p2p_cnt = nullptr;
     S.p2p_flag = nullptr;
     S.d_peer_recv = S.d_peer_ret = nullptr;
     S.d_peer_cnt = nullptr;
@@ -754,7 +753,6 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     };
     A((void**)&S.send_tok, rows_local * sizeof(int));
     A((void**)&S.send_w, rows_local * sizeof(float));
-    A((void**)&S.send_slot, rows_local * sizeof(int));
     A((void**)&S.send_eoff, (L.E_route + 1) * sizeof(int));
     A((void**)&S.cnt_recv, (size_t)G * El * sizeof(int));
     A((void**)&S.cnt_scan, (size_t)G * El * sizeof(int));

@@ -56,12 +56,6 @@ struct GemmParams {
     const float* row_weight;
     float* y;          // Down: [T][d] accumulated; DownStore: [rows][d], row row_token[prow]
     int d;
-    // DownStore to peers (expert parallel, fused return): row_token[prow] is
-    // the slot source * peer_cap + row; the result goes to
-    // peer_out[source] at row peer_rank * peer_cap + row.
-    void* const* peer_out;
-    int peer_cap;
-    int peer_rank;
     int* err;
 };
 
@@ -160,19 +154,12 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
             }
         }
     } else if constexpr (kEpi == kEpiDownStore) {
-        // Expert parallelism: each row's result goes back to the rank
-        // that sent it, at the row it arrived in -- fp32 in FP32
-        // precision, bf16 in BF16 precision (half the return bytes).
+        // Expert parallelism (NCCL transport): each row's result is stored
+        // at the row it arrived in -- fp32 in FP32 precision, bf16 in BF16
+        // precision (half the return bytes).
         const int dst = valid ? p.row_token[prow] : 0;
-        // Start of the result row: local (p.y) or in the source rank's
-        // return buffer over NVLink.
         constexpr size_t kEs = kTf32x3 ? 4 : 2;
-        char* rowp;
-        if (p.peer_out)
-            rowp = static_cast<char*>(p.peer_out[dst / p.peer_cap]) +
-                   ((size_t)p.peer_rank * p.peer_cap + dst % p.peer_cap) * p.d * kEs;
-        else
-            rowp = reinterpret_cast<char*>(p.y) + static_cast<size_t>(dst) * p.d * kEs;
+        char* rowp = reinterpret_cast<char*>(p.y) + static_cast<size_t>(dst) * p.d * kEs;
 #pragma unroll 1
         for (int c = 0; c < kTileN; c += 32) {
             uint32_t v[32];
@@ -703,7 +690,7 @@ cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, 
 }
 
 cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
-                                    int mode, const PeerDst* peer) {
+                                    int mode) {
     const bool down = mode != 0;
     const Workspace& W = L.ws;
     const bool tf = three_pass(L);
@@ -721,14 +708,6 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
     g.h_hi = W.h_hi;
     g.h_lo = W.h_lo;
     g.ldh = L.ffp;
-    g.peer_out = nullptr;
-    g.peer_cap = 1;
-    g.peer_rank = 0;
-    if (mode == 2 && peer) {
-        g.peer_out = peer->bases;
-        g.peer_cap = peer->cap;
-        g.peer_rank = peer->rank;
-    }
     g.k_splits = 1;
     g.kb_per = 0;   // set below, with k_blocks
     if (!down) {

@@ -118,18 +118,6 @@ struct NormRef {
 #endif
 };
 
-// Expert-parallel fused dispatch: the dispatch permute stores each routed
-// row straight into the receive buffer of the rank that holds its expert
-// (over NVLink), at this rank's segment of that buffer.
-struct PeerDst {
-    void* const* bases = nullptr;  // [G] the ranks' receive buffers, [G][cap] rows each
-    int cap = 0;                   // rows of one source segment
-    int rank = 0;                  // this rank: its segment in every buffer
-    int e_local = 1;               // experts per rank
-    const int* eoff = nullptr;     // compact per-expert row offsets [E + 1]
-    int* slot = nullptr;           // out: compact row -> destination * cap + row in segment
-};
-
 struct EpState;  // expert-parallel group (ep.cu)
 
 struct Layer {
@@ -210,11 +198,6 @@ cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, c
 cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
                                        const int* eoff, int* row_token, float* row_weight,
                                        void* rows, cudaStream_t s);
-// The same placement, each row stored into its expert's rank's receive
-// buffer (fp32 in FP32 precision, bf16 in BF16), its return slot recorded.
-cudaError_t launch_dispatch_push(const Layer& L, const float* x, int T, int E, const int* eoff,
-                                 int* row_token, float* row_weight, const PeerDst& pd,
-                                 cudaStream_t s);
 // The scan on any [nblk][E] count matrix, expert blocks rounded to `granule`
 // rows; mtiles == nullptr gives a compact layout with no tiles or padding.
 cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
@@ -226,11 +209,10 @@ cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* co
 // down == true:  down GEMM with the weighted-combine epilogue into y.
 cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down);
 // The same over `routed_rows` packed rows; mode 0 gate/up, 1 down with the
-// combine epilogue, 2 down storing each row's result at y[row_token[row]]
-// or, with `peer`, at peer->bases[slot / cap] row rank * cap + slot % cap
-// (slot = row_token[row]).
+// combine epilogue (y[row_token[row]] += row_weight[row] * result), 2 down
+// storing each row's result at y[row_token[row]] (bf16 in BF16 precision).
 cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
-                                    int mode, const PeerDst* peer = nullptr);
+                                    int mode);
 
 // decode.cu: T <= decode_max_supported_tokens() (64)
 // packed: the routed rows are already in the decode format (launch_route_small).

@@ -223,19 +223,24 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         // group's dependent FMAs, which the loads then overlap.  Lanes whose
         // expert index is past E run chains on unused rows that are never
         // stored.
-        float4 xa[4], wa[EJ][4], xb[4], wb[EJ][4];
-        auto load_group = [&](float4 (&xv)[4], float4 (&wv)[EJ][4], int kk) {
+        // Group width: 16 columns for 1-2 chains per thread, 8 for 4, 4 for
+        // 8 or more, so that both register sets (4 kQ (1 + EJ) floats each)
+        // stay in registers whatever the expert count.
+        constexpr int kQ = EJ >= 8 ? 1 : (EJ >= 4 ? 2 : 4);   // float4 per row per group
+        constexpr int kGw = 4 * kQ;                            // columns per group
+        float4 xa[kQ], wa[EJ][kQ], xb[kQ], wb[EJ][kQ];
+        auto load_group = [&](float4 (&xv)[kQ], float4 (&wv)[EJ][kQ], int kk) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) xv[q] = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
+            for (int q = 0; q < kQ; ++q) xv[q] = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
 #pragma unroll
             for (int j = 0; j < EJ; ++j)
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+                for (int q = 0; q < kQ; ++q)
                     wv[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 4 * q);
         };
-        auto chain_group = [&](const float4 (&xv)[4], const float4 (&wv)[EJ][4]) {
+        auto chain_group = [&](const float4 (&xv)[kQ], const float4 (&wv)[EJ][kQ]) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+            for (int q = 0; q < kQ; ++q)
 #pragma unroll
                 for (int j = 0; j < EJ; ++j) {
                     acc[j] = __fmaf_rn(xv[q].x, wv[j][q].x, acc[j]);
@@ -246,10 +251,10 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         };
         load_group(xa, wa, 0);
 #pragma unroll
-        for (int kk = 0; kk < KC; kk += 32) {
-            load_group(xb, wb, kk + 16);
+        for (int kk = 0; kk < KC; kk += 2 * kGw) {
+            load_group(xb, wb, kk + kGw);
             chain_group(xa, wa);
-            if (kk + 32 < KC) load_group(xa, wa, kk + 32);
+            if (kk + 2 * kGw < KC) load_group(xa, wa, kk + 2 * kGw);
             chain_group(xb, wb);
         }
     }
@@ -485,20 +490,18 @@ __device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_o
 }
 
 // kMode: 0 bf16 plane, 1 tf32 hi + lo planes, 2 fp32 as is (decode).
-// kPeer: rows go to the receive buffers of pd (modes 0 and 2 only).
-template <int kMode, bool kPeer = false>
+template <int kMode>
 __global__ void __launch_bounds__(256)
 dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                         const int* __restrict__ idx, const float* __restrict__ wts,
                         const int* __restrict__ blockbase, const int* __restrict__ eoff,
                         int* __restrict__ row_token, float* __restrict__ row_weight,
                         void* __restrict__ a_hi, void* __restrict__ a_lo, ScanOut so,
-                        NormRef nr, PeerDst pd = {}) {
+                        NormRef nr) {
     __shared__ unsigned s_mask[kMaxExperts];
     __shared__ int s_base[kMaxExperts + 1];
     __shared__ int s_dest[kRouteTokens * kMaxTopK];
     __shared__ float s_nmean[kRouteTokens], s_ninv[kRouteTokens];
-    __shared__ char* s_row[kPeer ? kRouteTokens * kMaxTopK : 1];   // destination row starts
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kRouteTokens;
     const int n_tok = min(kRouteTokens, T - t0);
@@ -534,14 +537,6 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
         if (blockIdx.y == 0) {
             row_token[pos] = t0 + my_t;
             row_weight[pos] = wts[(size_t)(t0 + my_t) * k + (tid % k)];
-        }
-        if constexpr (kPeer) {
-            const int j = my_e / pd.e_local;
-            const int q = pos - pd.eoff[j * pd.e_local];
-            const size_t row_bytes = (size_t)d * (kMode == 0 ? 2 : 4);
-            s_row[tid] = static_cast<char*>(pd.bases[j]) +
-                         ((size_t)pd.rank * pd.cap + q) * row_bytes;
-            if (blockIdx.y == 0) pd.slot[pos] = j * pd.cap + q;
         }
     }
     __syncthreads();
@@ -598,24 +593,15 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                 packed.x = *reinterpret_cast<uint32_t*>(&lo2);
                 packed.y = *reinterpret_cast<uint32_t*>(&hi2);
                 for (int s = 0; s < k; ++s) {
-                    if constexpr (kPeer) {
-                        reinterpret_cast<uint2*>(s_row[t * k + s])[v] = packed;
-                    } else {
-                        const size_t row = (size_t)s_dest[t * k + s];
-                        reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
-                    }
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
                 }
             } else if constexpr (kMode == 2) {
                 for (int s = 0; s < k; ++s) {
-                    if constexpr (kPeer) {
-                        reinterpret_cast<float4*>(s_row[t * k + s])[v] = f[u];
-                    } else {
-                        const size_t row = (size_t)s_dest[t * k + s];
-                        reinterpret_cast<float4*>(a_hi)[row * nv + v] = f[u];
-                    }
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<float4*>(a_hi)[row * nv + v] = f[u];
                 }
             } else {
-                static_assert(!kPeer, "peer rows are bf16 or fp32");
                 float4 h, l;
                 h.x = to_tf32(f[u].x); l.x = to_tf32(f[u].x - h.x);
                 h.y = to_tf32(f[u].y); l.y = to_tf32(f[u].y - h.y);
@@ -1131,24 +1117,6 @@ cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, in
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
                                                         row_weight, rows, nullptr, ScanOut{}, NormRef{});
-    return cudaGetLastError();
-}
-
-cudaError_t launch_dispatch_push(const Layer& L, const float* x, int T, int E, const int* eoff,
-                                 int* row_token, float* row_weight, const PeerDst& pd,
-                                 cudaStream_t s) {
-    const Workspace& W = L.ws;
-    const dim3 grid = permute_grid(L, T);
-    if (three_pass(L))
-        dispatch_permute_kernel<2, true><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
-                                                              W.blockhist, eoff, row_token,
-                                                              row_weight, nullptr, nullptr,
-                                                              ScanOut{}, NormRef{}, pd);
-    else
-        dispatch_permute_kernel<0, true><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
-                                                              W.blockhist, eoff, row_token,
-                                                              row_weight, nullptr, nullptr,
-                                                              ScanOut{}, NormRef{}, pd);
     return cudaGetLastError();
 }
 
