@@ -126,8 +126,13 @@ __device__ __forceinline__ void select_experts(const float* l, int E, int k, int
 // (0..31).  Thread (tt, el) owns the chains of experts el, el + 8, ...,
 // el + 8 (EJ - 1) for token tt.  Per 4-wide k step a warp reads 4 distinct x
 // rows and 8 distinct weight rows out of shared memory.
-template <int EJ, int KC>
-__global__ void __launch_bounds__(kRouterThreads)
+// kBlk (E a multiple of 32): 2E threads, thread (tq = tid % 8, eq = tid / 8)
+// owning the 16 chains of tokens tq + 8a and experts eq + (E/4) b (a, b < 4):
+// 4 x and 4 weight float4 per 4-wide k step for 64 FMAs instead of 9 for 32,
+// each load's rows consecutive (bank-conflict free).  Every chain is still
+// one serial fused multiply-add per k, ascending.
+template <int EJ, int KC, bool kBlk = false>
+__global__ void __launch_bounds__(kBlk ? 512 : kRouterThreads)
 router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
               const float* __restrict__ bias, int T, int d, int E, int k, int policy,
               float quantum, float tie_eps, float* __restrict__ logits_out,
@@ -136,10 +141,10 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     constexpr int kStages = 4;
     constexpr int kLd = KC + 4;              // padded row stride (floats)
     constexpr int kXs = kRouteTokens * kLd;  // x floats per stage
-    constexpr int kWs = 8 * EJ * kLd;        // wg floats per stage
+    const int kWs = (kBlk ? E : 8 * EJ) * kLd;   // wg floats per stage
     extern __shared__ __align__(16) float rsm[];
     float* xs = rsm;                       // [kStages][32][kLd]
-    float* ws = rsm + kStages * kXs;       // [kStages][8*EJ][kLd]
+    float* ws = rsm + kStages * kXs;       // [kStages][wg rows][kLd]
     float* nws = ws + kStages * kWs;       // [kStages][2][KC] norm weight, bias chunks
     float* nst = nws + kStages * 2 * KC;   // [2][32] norm mean, inverse std of the tokens
     float* lg = nst + 2 * kRouteTokens;    // [32][E + 1]
@@ -159,9 +164,11 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     }
 
     // Stage loader: x chunk is 32 rows x KC floats, wg chunk E rows x KC.
+    // Token rows this CTA stages (kBlk: all 32, the rows past T zero-filled).
+    const int x_rows = kBlk ? kRouteTokens : (int)(blockDim.x / 8);
     auto load_chunk = [&](int chunk, int stage) {
         const int kbase = chunk * KC;
-        const int kXv = (blockDim.x / 8) * KC / 4;   // float4 per x chunk (tokens this CTA runs)
+        const int kXv = x_rows * KC / 4;   // float4 per x chunk
         for (int v = tid; v < kXv; v += blockDim.x) {
             const int r = v / (KC / 4), c = (v % (KC / 4)) * 4;
             const bool ok = r < n_tok;
@@ -182,9 +189,10 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         }
     };
 
-    float acc[EJ];
+    constexpr int kAcc = kBlk ? 16 : EJ;
+    float acc[kAcc];
 #pragma unroll
-    for (int j = 0; j < EJ; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < kAcc; ++j) acc[j] = 0.0f;
 
     for (int s = 0; s < kStages - 1; ++s) {
         if (s < nchunks) load_chunk(s, s);
@@ -202,7 +210,7 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
             // Post-attention LayerNorm: normalise the landed x chunk in place,
             // once per element, before the chains read it (the norm's weight
             // and bias chunk landed with it).
-            const int kXv = (blockDim.x / 8) * KC / 4;
+            const int kXv = x_rows * KC / 4;
             const float* nw = nws + st * 2 * KC;
             for (int v = tid; v < kXv; v += blockDim.x) {
                 const int r = v / (KC / 4), cc = (v % (KC / 4)) * 4;
@@ -215,68 +223,118 @@ router_kernel(const float* __restrict__ x, const float* __restrict__ wg,
             }
             __syncthreads();
         }
-        const float* xr = xs + st * kXs + tt * kLd;
-        const float* wr = ws + st * kWs + el * kLd;
-        // Fully unrolled over the chunk, every shared-memory offset an
-        // immediate.  Two register sets alternate (ping-pong, no copies): the
-        // loads of the next 16-wide group are issued before the current
-        // group's dependent FMAs, which the loads then overlap.  Lanes whose
-        // expert index is past E run chains on unused rows that are never
-        // stored.
-        // Group width: 16 columns for 1-2 chains per thread, 8 for 4, 4 for
-        // 8 or more, so that both register sets (4 kQ (1 + EJ) floats each)
-        // stay in registers whatever the expert count.
-        constexpr int kQ = EJ >= 8 ? 1 : (EJ >= 4 ? 2 : 4);   // float4 per row per group
-        constexpr int kGw = 4 * kQ;                            // columns per group
-        float4 xa[kQ], wa[EJ][kQ], xb[kQ], wb[EJ][kQ];
-        auto load_group = [&](float4 (&xv)[kQ], float4 (&wv)[EJ][kQ], int kk) {
+        if constexpr (kBlk) {
+            const int tq = tid & 7, eq = tid >> 3, es = E / 4;
+            const float* xr = xs + st * kXs + tq * kLd;
+            const float* wr = ws + st * kWs + eq * kLd;
+            float4 xa[4], wa[4], xb[4], wb[4];
+            auto load_q = [&](float4 (&xv)[4], float4 (&wv)[4], int kk) {
 #pragma unroll
-            for (int q = 0; q < kQ; ++q) xv[q] = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
+                for (int a = 0; a < 4; ++a) xv[a] = *reinterpret_cast<const float4*>(xr + 8 * a * kLd + kk);
 #pragma unroll
-            for (int j = 0; j < EJ; ++j)
+                for (int b = 0; b < 4; ++b)
+                    wv[b] = *reinterpret_cast<const float4*>(wr + (size_t)es * b * kLd + kk);
+            };
+            auto chain_q = [&](const float4 (&xv)[4], const float4 (&wv)[4]) {
 #pragma unroll
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        float& c = acc[a * 4 + b];
+                        c = __fmaf_rn(xv[a].x, wv[b].x, c);
+                        c = __fmaf_rn(xv[a].y, wv[b].y, c);
+                        c = __fmaf_rn(xv[a].z, wv[b].z, c);
+                        c = __fmaf_rn(xv[a].w, wv[b].w, c);
+                    }
+            };
+            load_q(xa, wa, 0);
+#pragma unroll
+            for (int kk = 0; kk < KC; kk += 8) {
+                load_q(xb, wb, kk + 4);
+                chain_q(xa, wa);
+                if (kk + 8 < KC) load_q(xa, wa, kk + 8);
+                chain_q(xb, wb);
+            }
+        } else {
+            const float* xr = xs + st * kXs + tt * kLd;
+            const float* wr = ws + st * kWs + el * kLd;
+            // Fully unrolled over the chunk, every shared-memory offset an
+            // immediate.  Two register sets alternate (ping-pong, no copies): the
+            // loads of the next 16-wide group are issued before the current
+            // group's dependent FMAs, which the loads then overlap.  Lanes whose
+            // expert index is past E run chains on unused rows that are never
+            // stored.
+            // Group width: 16 columns for 1-2 chains per thread, 8 for 4, 4 for
+            // 8 or more, so that both register sets (4 kQ (1 + EJ) floats each)
+            // stay in registers whatever the expert count.
+            constexpr int kQ = EJ >= 8 ? 1 : (EJ >= 4 ? 2 : 4);   // float4 per row per group
+            constexpr int kGw = 4 * kQ;                            // columns per group
+            float4 xa[kQ], wa[EJ][kQ], xb[kQ], wb[EJ][kQ];
+            auto load_group = [&](float4 (&xv)[kQ], float4 (&wv)[EJ][kQ], int kk) {
+    #pragma unroll
+                for (int q = 0; q < kQ; ++q) xv[q] = *reinterpret_cast<const float4*>(xr + kk + 4 * q);
+    #pragma unroll
+                for (int j = 0; j < EJ; ++j)
+    #pragma unroll
+                    for (int q = 0; q < kQ; ++q)
+                        wv[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 4 * q);
+            };
+            auto chain_group = [&](const float4 (&xv)[kQ], const float4 (&wv)[EJ][kQ]) {
+    #pragma unroll
                 for (int q = 0; q < kQ; ++q)
-                    wv[j][q] = *reinterpret_cast<const float4*>(wr + 8 * j * kLd + kk + 4 * q);
-        };
-        auto chain_group = [&](const float4 (&xv)[kQ], const float4 (&wv)[EJ][kQ]) {
-#pragma unroll
-            for (int q = 0; q < kQ; ++q)
-#pragma unroll
-                for (int j = 0; j < EJ; ++j) {
-                    acc[j] = __fmaf_rn(xv[q].x, wv[j][q].x, acc[j]);
-                    acc[j] = __fmaf_rn(xv[q].y, wv[j][q].y, acc[j]);
-                    acc[j] = __fmaf_rn(xv[q].z, wv[j][q].z, acc[j]);
-                    acc[j] = __fmaf_rn(xv[q].w, wv[j][q].w, acc[j]);
-                }
-        };
-        load_group(xa, wa, 0);
-#pragma unroll
-        for (int kk = 0; kk < KC; kk += 2 * kGw) {
-            load_group(xb, wb, kk + kGw);
-            chain_group(xa, wa);
-            if (kk + 2 * kGw < KC) load_group(xa, wa, kk + 2 * kGw);
-            chain_group(xb, wb);
+    #pragma unroll
+                    for (int j = 0; j < EJ; ++j) {
+                        acc[j] = __fmaf_rn(xv[q].x, wv[j][q].x, acc[j]);
+                        acc[j] = __fmaf_rn(xv[q].y, wv[j][q].y, acc[j]);
+                        acc[j] = __fmaf_rn(xv[q].z, wv[j][q].z, acc[j]);
+                        acc[j] = __fmaf_rn(xv[q].w, wv[j][q].w, acc[j]);
+                    }
+            };
+            load_group(xa, wa, 0);
+    #pragma unroll
+            for (int kk = 0; kk < KC; kk += 2 * kGw) {
+                load_group(xb, wb, kk + kGw);
+                chain_group(xa, wa);
+                if (kk + 2 * kGw < KC) load_group(xa, wa, kk + 2 * kGw);
+                chain_group(xb, wb);
+            }
         }
     }
     cp_async_wait<0>();
 
     for (int e = tid; e < E; e += blockDim.x) hist[e] = 0;
+    if constexpr (kBlk) {
+        const int tq = tid & 7, eq = tid >> 3;
 #pragma unroll
-    for (int j = 0; j < EJ; ++j) {
-        const int e = el + 8 * j;
-        if (e < E) {
-            float v = acc[j];
-            if (bias) v = __fadd_rn(v, bias[e]);
-            lg[tt * (E + 1) + e] = v;
-            if (logits_out && tt < n_tok) logits_out[(size_t)(t0 + tt) * E + e] = v;
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int t = tq + 8 * a, e = eq + (E / 4) * b;
+                float v = acc[a * 4 + b];
+                if (bias) v = __fadd_rn(v, bias[e]);
+                lg[t * (E + 1) + e] = v;
+                if (logits_out && t < n_tok) logits_out[(size_t)(t0 + t) * E + e] = v;
+            }
+    } else {
+#pragma unroll
+        for (int j = 0; j < EJ; ++j) {
+            const int e = el + 8 * j;
+            if (e < E) {
+                float v = acc[j];
+                if (bias) v = __fadd_rn(v, bias[e]);
+                lg[tt * (E + 1) + e] = v;
+                if (logits_out && tt < n_tok) logits_out[(size_t)(t0 + tt) * E + e] = v;
+            }
         }
     }
     __syncthreads();
 
-    // Selection: warp w handles tokens 4w .. 4w+3.
+    // Selection: warp w handles tokens per * w .. per * w + per - 1 (4 per
+    // warp with 8 warps; kBlk: 32 / warps).
     const int warp = tid >> 5, lane = tid & 31;
-    for (int q = 0; q < 4; ++q) {
-        const int tk = warp * 4 + q;
+    const int per = kBlk ? kRouteTokens / (int)(blockDim.x >> 5) : 4;
+    for (int q = 0; q < per; ++q) {
+        const int tk = warp * per + q;
         if (tk >= n_tok) break;
         int sel[kMaxTopK];
         float wsel[kMaxTopK];
@@ -940,15 +998,16 @@ dim3 permute_grid(const Layer& L, int T) {
     return dim3(nblk, splits);
 }
 
-template <int EJ, int KC>
+template <int EJ, int KC, bool kBlk = false>
 cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits, int* idx,
                             float* wts, int* blockhist, cudaStream_t s, const NormRef& nr,
                             const int* eperm) {
     const int E = L.E_route;
-    const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + 8 * EJ * (KC + 4) + 2 * KC) +
+    const int wrows = kBlk ? E : 8 * EJ;
+    const size_t smem = sizeof(float) * (4 * (kRouteTokens * (KC + 4) + wrows * (KC + 4) + 2 * KC) +
                                          2 * kRouteTokens + kRouteTokens * (E + 1)) +
                         sizeof(int) * E;
-    auto kern = router_kernel<EJ, KC>;
+    auto kern = router_kernel<EJ, KC, kBlk>;
     cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)smem);
     if (err != cudaSuccess) return err;
@@ -957,7 +1016,7 @@ cudaError_t launch_router_t(const Layer& L, const float* x, int T, float* logits
     // (8 threads per token, whole warps): at decode sizes the dependent FMA
     // chain is the critical path and idle warps would only take issue slots.
     const int tok = T < kRouteTokens ? (T + 3) / 4 * 4 : kRouteTokens;
-    kern<<<nblk, 8 * tok, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
+    kern<<<nblk, kBlk ? 2 * E : 8 * tok, smem, s>>>(x, L.wg, L.bias, T, L.d, E, L.k,
                                             L.cfg.router_policy, L.cfg.router_quantum,
                                             L.cfg.router_tie_eps, logits, idx, wts, blockhist, nr,
                                             eperm);
@@ -973,6 +1032,14 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
     // SM keeps 100-200 KB of x / wg loads in flight (the dot-product chains
     // themselves are serial and cannot be split).
     const int ej = (L.E_route + 7) / 8;
+    // Expert counts that are multiples of 32: the 4 x 4 register-blocked
+    // chains (K chunk sized so two CTAs fit an SM up to 64 experts).
+    if (L.E_route % 32 == 0) {
+        if (L.E_route <= 128 && L.d % 64 == 0)
+            return launch_router_t<1, 64, true>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+        if (L.E_route <= 256 && L.d % 32 == 0)
+            return launch_router_t<1, 32, true>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
+    }
     if (L.d % 256 == 0) {
         if (ej <= 1) return launch_router_t<1, 256>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
         if (ej <= 2) return launch_router_t<2, 256>(L, x, T, logits, idx, wts, blockhist, s, nr, eperm);
