@@ -83,10 +83,12 @@ typedef enum MoeGemmVariant {
 #define MOE_DECODE_AUTO (-1)
 
 /* Expert-parallel exchange.
- * P2P (default): fused -- the dispatch permute writes routed rows straight
- *   into the owning rank's receive buffer over NVLink and the down GEMM's
- *   epilogue writes results straight back; completion is signalled with
- *   flags in peer memory.  Needs all ranks on one node (CUDA IPC).
+ * P2P (default): fused and deduplicated -- each token row is stored once
+ *   into the receive buffer of every rank holding any of its experts (over
+ *   NVLink, with its selections on that rank as metadata); that rank sums
+ *   the weighted outputs of its experts for the row and stores one row back;
+ *   completion is signalled with flags in peer memory.  Needs all ranks on
+ *   one node (CUDA IPC) and at most 32 ranks.
  * NCCL: separate grouped ncclSend / ncclRecv exchanges after the dispatch
  *   and after the down GEMM, with a host read of the counts in between. */
 typedef enum MoeEpTransport {
