@@ -236,3 +236,27 @@ def test_decoder_generate_reuses_and_recaptures_the_step_graph():
         assert lg_nl is None
         ids_l, _ = m.generate(p1, 5)
         assert np.array_equal(ids_nl, ids_l)
+
+
+def test_decoder_config_is_validated_before_any_device_work():
+    """moe_decoder_create rejects shapes it cannot run before it looks at the
+    weights or a device (no GPU needed)."""
+    import ctypes
+    pkg = load_pkg()
+    L = pkg.load_library()
+    bad = [(dict(head_dim=96), -2, "head_dim"),
+           (dict(n_heads=3), -2, "n_heads"),
+           (dict(vocab=250), -2, "vocab"),
+           (dict(max_batch=0), -1, "max_batch"),
+           (dict(precision=7), -1, "precision")]
+    for kw, code, word in bad:
+        cfg = pkg.decoder_config(n_layers=1, d_model=128, n_heads=1, head_dim=128, vocab=256,
+                                 num_experts=8, top_k=2, d_ff=128, max_batch=2, max_seq=16)
+        for k, v in kw.items():
+            setattr(cfg, k, v)
+        h = ctypes.c_void_p()
+        cw = pkg.MoeDecoderWeightsC()          # all null: never reached
+        rc = L.moe_decoder_create(ctypes.byref(cfg), ctypes.byref(cw), ctypes.byref(h))
+        assert rc == code, (kw, rc)
+        assert word in L.moe_last_error().decode()
+        assert not h.value
