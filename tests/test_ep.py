@@ -6,10 +6,15 @@ the experts: local routing, counts exchange, compact expert-sorted packing,
 payload all-to-all, the experts on each rank's slice, the return all-to-all
 and the weighted combine.  The result must equal the single-process oracle.
 
+CPU (gloo): the deduplicated fused transport's layout restated the same way
+(one row per token and destination rank, selections as metadata, the
+expert-rank sum, one returned row), which must also equal the oracle and
+place every selection in exactly one GEMM row.
+
 GPU (2 B200s, skipped with fewer): moe_ep_forward_device itself against the
-oracle, per rank, with both transports: the fused one (dispatch permute and
-down-GEMM epilogue storing rows into the other GPU's buffers over NVLink,
-flags in peer memory) and NCCL send/recv.
+oracle, per rank, with both transports: the fused one (rows and metadata
+stored into the other GPU's buffers over NVLink, flags in peer memory) and
+NCCL send/recv.
 """
 import os
 import socket
@@ -100,6 +105,136 @@ def _gloo_rank(rank, world, port, q):
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e), -1, -1))
+
+
+K_DD = 4   # top-4 of 8 experts on 2 ranks: most tokens have several experts on one rank
+
+
+def _gloo_dedup_rank(rank, world, port, q):
+    """The deduplicated fused transport's layout, restated on gloo: one row
+    per (token, destination rank) carrying its selections on that rank as
+    (local expert, position inside the expert's block from this source,
+    weight); the receiver places each selection at eoff[e] + base[source][e]
+    + position, sums the row's weighted expert outputs, and returns one row;
+    the source adds its ranks' rows in ascending rank order."""
+    try:
+        import torch
+        import torch.distributed as dist
+        sys.path.insert(0, str(ROOT / "tests"))
+        from conftest import load_oracle as lo, load_pkg as lp
+        pkg, oracle = lp(), lo()
+        orc = oracle.Oracle()
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        layer = _layer(pkg)
+        x = _tokens(pkg, rank)
+        T = x.shape[0]
+        El = E // world
+        kmax = min(K_DD, El)
+        pos_of = lambda e: (e % world) * El + e // world  # noqa: E731
+        logits = orc.router_logits(x, layer.wg, layer.router_bias)
+        idx, w = orc.route(logits, K_DD, oracle.POLICY_SOFTMAX)
+        P = np.vectorize(pos_of)(idx)                      # dispatch positions [T][K]
+        # Source side: positions inside each expert's block (ascending token),
+        # per-expert counts, rows per destination and their metadata.
+        seen = np.zeros(E, np.int64)
+        pin = np.zeros_like(P)
+        for t in range(T):
+            for s_ in range(K_DD):
+                pin[t, s_] = seen[P[t, s_]]
+                seen[P[t, s_]] += 1
+        counts = seen.astype(np.int32)
+        rows, metas, slot = [[] for _ in range(world)], [[] for _ in range(world)], {}
+        for t in range(T):
+            for g in range(world):
+                sel = [(int(P[t, s_]) - g * El, int(pin[t, s_]), float(w[t, s_]))
+                       for s_ in range(K_DD) if P[t, s_] // El == g]
+                if not sel:
+                    continue
+                assert len(sel) <= kmax
+                slot[(t, g)] = len(rows[g])
+                rows[g].append(x[t])
+                metas[g].append(sel + [(-1, 0, 0.0)] * (kmax - len(sel)))
+        n_send = [len(r) for r in rows]
+        # Exchange counts, row counts, rows and metadata.
+        cin = torch.empty(world * El, dtype=torch.int32)
+        dist.all_to_all_single(cin, torch.from_numpy(counts))
+        counts_in = cin.numpy().reshape(world, El)
+        nin = torch.empty(world, dtype=torch.int64)
+        dist.all_to_all_single(nin, torch.tensor(n_send, dtype=torch.int64))
+        n_recv = [int(v) for v in nin]
+        send = np.concatenate([np.asarray(r, np.float32).reshape(-1, D) for r in rows])
+        recv = torch.empty(sum(n_recv), D)
+        dist.all_to_all_single(recv, torch.from_numpy(send), n_recv, n_send)
+        mi = np.concatenate([np.asarray([[(e, p_) for e, p_, _ in m] for m in metas[g]],
+                                        np.int64).reshape(-1, kmax * 2) for g in range(world)])
+        mw = np.concatenate([np.asarray([[w_ for _, _, w_ in m] for m in metas[g]],
+                                        np.float32).reshape(-1, kmax) for g in range(world)])
+        rmi = torch.empty(sum(n_recv), kmax * 2, dtype=torch.int64)
+        rmw = torch.empty(sum(n_recv), kmax)
+        dist.all_to_all_single(rmi, torch.from_numpy(mi), n_recv, n_send)
+        dist.all_to_all_single(rmw, torch.from_numpy(mw), n_recv, n_send)
+        recv, rmi, rmw = recv.numpy(), rmi.numpy().reshape(-1, kmax, 2), rmw.numpy()
+        # Receiver side: arrival scan and arrangement.
+        total = counts_in.sum(axis=0)
+        eoff = np.concatenate([[0], np.cumsum(total)])
+        base = np.cumsum(counts_in, axis=0) - counts_in          # [source][local expert]
+        A = np.full((int(eoff[-1]), D), np.nan, np.float32)
+        owner = np.full(int(eoff[-1]), -1, np.int64)
+        wt = np.zeros(int(eoff[-1]), np.float64)
+        src_of = np.repeat(np.arange(world), n_recv)
+        for i in range(len(recv)):
+            sidx = int(src_of[i])
+            for j in range(kmax):
+                e, p_ = int(rmi[i, j, 0]), int(rmi[i, j, 1])
+                if e < 0:
+                    break
+                prow = int(eoff[e] + base[sidx, e] + p_)
+                assert owner[prow] == -1, "two selections placed in one row"
+                owner[prow], wt[prow] = i, float(rmw[i, j])
+                A[prow] = recv[i]
+        assert (owner >= 0).all(), "a row of an expert block left unplaced"
+        y_recv = np.zeros((len(recv), D), np.float64)
+        for e in range(El):
+            lo_, hi_ = int(eoff[e]), int(eoff[e + 1])
+            if hi_ > lo_:
+                ge = e * world + rank
+                out = orc.expert_ffn(A[lo_:hi_], layer.w1[ge], layer.w3[ge], layer.w2[ge])
+                np.add.at(y_recv, owner[lo_:hi_], wt[lo_:hi_, None] * out.astype(np.float64))
+        # Return one row per received row; combine in ascending rank order.
+        back = torch.empty(sum(n_send), D, dtype=torch.float64)
+        dist.all_to_all_single(back, torch.from_numpy(y_recv), n_send, n_recv)
+        back = back.numpy()
+        seg = np.concatenate([[0], np.cumsum(n_send)])
+        y = np.zeros((T, D), np.float64)
+        for t in range(T):
+            for g in range(world):
+                if (t, g) in slot:
+                    y[t] += back[seg[g] + slot[(t, g)]]
+        y_ref, *_ = orc.moe_forward(x, layer, K_DD, oracle.POLICY_SOFTMAX)
+        q.put((rank, rel_l2(y, y_ref), T * K_DD, sum(n_send)))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), -1, -1))
+
+
+def test_ep_dedup_layout_on_gloo_matches_oracle():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_dedup_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    res.sort()
+    for rank, err, selections, rows_sent in res:
+        assert isinstance(err, float), err
+        assert err <= 1e-6, (rank, err)
+        # Deduplication: at most one row per (token, rank), fewer rows than selections.
+        assert rows_sent < selections
 
 
 def test_ep_dataflow_on_gloo_matches_oracle():
