@@ -20,9 +20,11 @@ CPU restatement of whole-model greedy generation:
                stops at EOS
 Norms, projections, RoPE and attention run in float64 numpy; the MoE in the
 oracle's fp32 reference arithmetic.  No reference code computes this
-architecture end to end, so beyond the MoE (pinned) and RoPE (checked against
-the reference's apply_rope in tests/test_decoder.py) the dense parts are
-float64 restatements.
+architecture end to end: the MoE is pinned (moe_oracle.c), and the attention
+block -- projections, RoPE, causal softmax -- is checked against the
+reference's own PhiAttention::forward built with plain multi-head attention
+(oracle/_ref/libref_attn.so, tests/test_decoder.py); RMSNorm, the embedding
+and the tied head are float64 restatements.
 """
 from __future__ import annotations
 
@@ -53,6 +55,31 @@ def apply_rope(x: np.ndarray, positions: np.ndarray, head_dim: int, base: float)
     return np.concatenate([x0 * c - x1 * s, x1 * c + x0 * s], axis=-1)
 
 
+def self_attention(xn: np.ndarray, wq, wk, wv, wo, B: int, S: int, H: int, hd: int,
+                   base: float) -> np.ndarray:
+    """Multi-head causal self-attention of B sequences of S rows each
+    (xn [B*S][d], positions 0..S-1): q, k, v projections, rotate-half RoPE,
+    softmax(q k^T / sqrt(hd)) over keys <= the query, the o projection.
+    float64."""
+    T = B * S
+    xn = np.asarray(xn, np.float64)
+    pos = np.tile(np.arange(S), B)
+    q = (xn @ np.asarray(wq, np.float64).T).reshape(T, H, hd)
+    k = (xn @ np.asarray(wk, np.float64).T).reshape(T, H, hd)
+    v = (xn @ np.asarray(wv, np.float64).T).reshape(T, H, hd)
+    q = apply_rope(q, pos, hd, base).reshape(B, S, H, hd)
+    k = apply_rope(k, pos, hd, base).reshape(B, S, H, hd)
+    v = v.reshape(B, S, H, hd)
+    sc = np.einsum("bqhc,bkhc->bhqk", q, k) / np.sqrt(hd)
+    mask = np.triu(np.ones((S, S), bool), 1)
+    sc = np.where(mask[None, None], -np.inf, sc)
+    sc = sc - sc.max(axis=-1, keepdims=True)
+    p = np.exp(sc)
+    p /= p.sum(axis=-1, keepdims=True)
+    o = np.einsum("bhqk,bkhc->bqhc", p, v).reshape(T, H * hd)
+    return o @ np.asarray(wo, np.float64).T
+
+
 class DecoderOracle:
     """The toy decoder's forward and greedy generation on the CPU.
 
@@ -76,23 +103,10 @@ class DecoderOracle:
         d, H, hd = w.d, self.H, self.hd
         T = B * S
         x = w.embed[tok.reshape(-1)].astype(np.float64)            # [T][d]
-        pos = np.tile(np.arange(S), B)
-        mask = np.triu(np.ones((S, S), bool), 1)
         for l in range(w.n_layers):
             xn = rms_norm(x, w.attn_norm[l], self.eps)
-            q = (xn @ w.wq[l].T.astype(np.float64)).reshape(T, H, hd)
-            k = (xn @ w.wk[l].T.astype(np.float64)).reshape(T, H, hd)
-            v = (xn @ w.wv[l].T.astype(np.float64)).reshape(T, H, hd)
-            q = apply_rope(q, pos, hd, self.base).reshape(B, S, H, hd)
-            k = apply_rope(k, pos, hd, self.base).reshape(B, S, H, hd)
-            v = v.reshape(B, S, H, hd)
-            sc = np.einsum("bqhc,bkhc->bhqk", q, k) / np.sqrt(hd)
-            sc = np.where(mask[None, None], -np.inf, sc)
-            sc = sc - sc.max(axis=-1, keepdims=True)
-            p = np.exp(sc)
-            p /= p.sum(axis=-1, keepdims=True)
-            o = np.einsum("bhqk,bkhc->bqhc", p, v).reshape(T, d)
-            x = x + o @ w.wo[l].T.astype(np.float64)
+            x = x + self_attention(xn, w.wq[l], w.wk[l], w.wv[l], w.wo[l], B, S, H, hd,
+                                   self.base)
             xm = rms_norm(x, w.ffn_norm[l], self.eps).astype(np.float32)
             y, *_ = self.orc.moe_forward(xm, w.moe[l], self.k, POLICY_SOFTMAX,
                                          nthreads=self.nthreads)

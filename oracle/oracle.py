@@ -236,3 +236,34 @@ class Reference:
                                           b.shape[0]) != 0:
             raise RuntimeError(self.lib.ref_last_error().decode())
         return c
+
+
+class ReferenceAttention:
+    """The reference's own PhiAttention::forward (src/layer.cu:110-147), built
+    with plain multi-head attention (2 heads of 128, no effective sliding
+    window) into _ref/libref_attn.so."""
+
+    PATH = HERE / "_ref" / "libref_attn.so"
+
+    def __init__(self):
+        if not self.PATH.exists():
+            raise FileNotFoundError(f"{self.PATH} not built (reference sources absent at build time)")
+        self.lib = ctypes.CDLL(str(self.PATH))
+        L = self.lib
+        L.ref_attention.argtypes = [ctypes.c_char_p, ctypes.c_int, _f32p, ctypes.c_int,
+                                    ctypes.c_int, _f32p, ctypes.c_int]
+        L.ref_attention_heads.restype = ctypes.c_int
+        L.ref_last_error.restype = ctypes.c_char_p
+        self.heads = L.ref_attention_heads()
+
+    @classmethod
+    def available(cls) -> bool:
+        return cls.PATH.exists()
+
+    def forward(self, model_bin, layer, x, out_cols):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty((x.shape[0], out_cols), np.float32)
+        if self.lib.ref_attention(str(model_bin).encode(), layer, _fp(x), x.shape[0], x.shape[1],
+                                  _fp(y), out_cols) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return y

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <exception>
 #include <fstream>
+#include <stdexcept>
 #include <string>
 #include <unordered_map>
 #include <utility>
@@ -173,5 +174,27 @@ int ref_apply_rope(float* q, float* k, int seq, int q_heads, int kv_heads, int h
         return fail(e);
     }
 }
+
+// PhiAttention::forward (src/layer.cu:110-147) of layer `layer` of a
+// model.bin: x [S][d] -> y [S][heads * head_dim projected by o_proj], with the
+// heads, head_dim, sliding window and RoPE base of this build's config.h.
+int ref_attention(const char* model_bin, int layer, const float* x, int S, int d, float* y,
+                  int y_cols) {
+    try {
+        ModelLoader loader(model_bin);
+        PhiAttention att(loader, static_cast<std::size_t>(layer));
+        Tensor xt({static_cast<std::size_t>(S), static_cast<std::size_t>(d)}), yt;
+        std::memcpy(xt.data(), x, sizeof(float) * xt.size());
+        att.forward(xt, yt);
+        if (yt.size() != static_cast<std::size_t>(S) * static_cast<std::size_t>(y_cols))
+            throw std::invalid_argument("ref_attention: unexpected output size");
+        std::memcpy(y, yt.data(), sizeof(float) * yt.size());
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
+int ref_attention_heads() { return static_cast<int>(apss26::NUM_ATTENTION_HEADS); }
 
 }  // extern "C"

@@ -3,7 +3,9 @@ restatement in oracle/decoder_oracle.py.
 
 CPU tests pin the oracle: its RoPE against the reference's own
 tensor_ops::apply_rope (src/tensor.cu:191-210, compiled into oracle/_ref),
-its greedy loop against its own prefill, and its EOS rule (generate_decode,
+its attention block against the reference's PhiAttention::forward
+(src/layer.cu:110-147, built with plain multi-head attention), its greedy
+loop against its own prefill, and its EOS rule (generate_decode,
 src/model.cu:2061-2104).  GPU tests run the decoder through the C ABI at a
 small shape (2 layers, d 256, vocab 1024, 8 experts top-2) and compare:
   - prefill logits: relative L2 <= 1e-3 in FP32 (3xTF32), <= 3e-2 in BF16
@@ -59,6 +61,49 @@ def test_oracle_rope_matches_reference_apply_rope():
     # restatement in double: they agree to the float rounding of the angle.
     assert np.max(np.abs(oq.reshape(S, -1) - rq)) < 2e-5
     assert np.max(np.abs(ok.reshape(S, -1) - rk)) < 2e-5
+
+
+def _write_tensors(path, entries):
+    """fp32 tensors in the ModelLoader format (src/model_loader.cu:14-30)."""
+    import struct
+    metas = [(n.encode(), a.shape, a.nbytes) for n, a in entries]
+    hsize = 4 + sum(4 + len(nb) + 4 + 4 * len(sh) + 16 for nb, sh, _ in metas)
+    header, off = bytearray(struct.pack("<I", len(entries))), hsize
+    for nb, sh, nbytes in metas:
+        header += struct.pack("<I", len(nb)) + nb + struct.pack("<I", len(sh))
+        header += struct.pack(f"<{len(sh)}I", *sh) + struct.pack("<QQ", off, nbytes)
+        off += nbytes
+    with open(path, "wb") as f:
+        f.write(header)
+        for _, a in entries:
+            f.write(np.ascontiguousarray(a, np.float32).tobytes())
+
+
+def test_oracle_attention_matches_reference_phi_attention(tmp_path):
+    """The restatement's attention block (projections, rotate-half RoPE,
+    causal softmax scaled by 1/sqrt(hd), o projection) against the
+    reference's own PhiAttention::forward built with plain multi-head
+    attention; zero biases, since config 4 has none."""
+    orc_mod = load_oracle()
+    if not orc_mod.ReferenceAttention.available():
+        pytest.skip("reference attention library not built (reference sources absent)")
+    import decoder_oracle
+    ref = orc_mod.ReferenceAttention()
+    H, hd = ref.heads, 128
+    d = H * hd
+    g = np.random.default_rng(7)
+    w = {n: (0.05 * g.standard_normal((d, d))).astype(np.float32) for n in ("q", "k", "v", "o")}
+    entries = []
+    for n in ("q", "k", "v", "o"):
+        entries.append((f"model.layers.0.self_attn.{n}_proj.weight", w[n]))
+        entries.append((f"model.layers.0.self_attn.{n}_proj.bias", np.zeros(d, np.float32)))
+    path = tmp_path / "attn.bin"
+    _write_tensors(path, entries)
+    for S in (1, 17, 40):
+        x = g.standard_normal((S, d)).astype(np.float32)
+        y_ref = ref.forward(path, 0, x, d)
+        y = decoder_oracle.self_attention(x, w["q"], w["k"], w["v"], w["o"], 1, S, H, hd, 10000.0)
+        assert rel_l2(y, y_ref) <= 1e-5, (S, rel_l2(y, y_ref))
 
 
 def test_oracle_greedy_loop_restarts_from_the_prefix():
