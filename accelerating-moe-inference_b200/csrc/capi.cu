@@ -2,11 +2,11 @@
 // weight upload, workspace management and the forward orchestration.
 //
 // forward on device buffers, all on the caller's stream, no host sync:
-//   router_kernel -> dispatch_scan -> dispatch_permute -> memset(y)
-//   -> gate/up grouped GEMM (SwiGLU epilogue) -> down grouped GEMM (combine
-//   epilogue)
+//   router_kernel -> dispatch_scan -> dispatch_permute
+//   -> gate/up grouped GEMM (SwiGLU epilogue) -> down grouped GEMM (each
+//   routed row's output at its selection slot) -> ordered combine into y
 // or, for T <= decode_max_tokens, router -> scan -> the weight-streaming
-// decode kernels.
+// decode kernels -> ordered combine.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -86,7 +86,8 @@ void free_workspace(Workspace& W) {
     free_ptr(W.logits); free_ptr(W.idx); free_ptr(W.wts); free_ptr(W.blockhist);
     free_ptr(W.counts); free_ptr(W.eoff); free_ptr(W.mtiles); free_ptr(W.num_mtiles);
     free_ptr(W.ptiles); free_ptr(W.num_ptiles);
-    free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.a_hi); free_ptr(W.a_lo);
+    free_ptr(W.row_token); free_ptr(W.row_weight); free_ptr(W.row_slot); free_ptr(W.part);
+    free_ptr(W.a_hi); free_ptr(W.a_lo);
     free_ptr(W.h_hi); free_ptr(W.h_lo); free_ptr(W.x_stage); free_ptr(W.y_stage);
     free_ptr(W.dev_err); free_ptr(W.h_dec); free_ptr(W.dec_counter);
     free_ptr(W.row_mean); free_ptr(W.row_inv);
@@ -121,6 +122,17 @@ int ensure_workspace(Layer& L, int T) {
     MOE_CUDA(dalloc(&W.num_ptiles, sizeof(int), &bytes));
     MOE_CUDA(dalloc(&W.row_token, sizeof(int) * cap_rows, &bytes));
     MOE_CUDA(dalloc(&W.row_weight, sizeof(float) * cap_rows, &bytes));
+    MOE_CUDA(dalloc(&W.row_slot, sizeof(int) * cap_rows, &bytes));
+    // Expert output rows for the ordered combine: one per selection slot, or
+    // per (slot, K split) at decode sizes -- the down GEMM splits K only for
+    // at most kSplitMaxRows routed rows, into at most k_blocks / kSplitMinBlocks
+    // parts, and the decode kernel into decode_chunks() parts for T <= 64.
+    {
+        const size_t gemm_splits = (size_t)L.ffp / 32 / kSplitMinBlocks + 1;
+        const size_t dec_rows = (size_t)decode_max_supported_tokens() * k * decode_chunks(L);
+        W.part_rows = std::max({(size_t)capT * k, (size_t)kSplitMaxRows * gemm_splits, dec_rows});
+        MOE_CUDA(dalloc(&W.part, sizeof(float) * W.part_rows * L.d, &bytes));
+    }
     MOE_CUDA(dalloc(&W.a_hi, eb * cap_rows * L.d, &bytes));
     MOE_CUDA(dalloc(&W.h_hi, eb * cap_rows * L.ffp, &bytes));
     if (tf) {
@@ -239,18 +251,16 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
         nr.b = L.norm_b;
     }
     const bool decode = T <= L.cfg.decode_max_tokens;
-    // A decode-sized batch is routed and dispatched (and y zeroed) by one
-    // single-CTA launch.
+    // A decode-sized batch is routed and dispatched by one single-CTA launch.
     int kc = 0, stages = 0;
     const bool small = route_small_geometry(L, T, block, &kc, &stages);
-    if (!small) MOE_CUDA(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * L.d, s));
     prof_mark(L, 0, s);
     if (block && L.norm_rms)
         MOE_CUDA(launch_rms_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, s));
     else if (block)
         MOE_CUDA(launch_row_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, W.dev_err, s));
     if (small) {
-        MOE_CUDA(launch_route_small(L, x, T, nr, decode, y, s));
+        MOE_CUDA(launch_route_small(L, x, T, nr, decode, s));
     } else {
         MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, nr));
     }
@@ -258,17 +268,20 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
     // A batch that fits one router block is scanned inside the permute kernel.
     if (T > kRouteTokens) MOE_CUDA(launch_dispatch_scan(L, T, s));
     prof_mark(L, 2, s);
+    int nsplit = 1;
     if (decode) {
         // marks stages 3 and 4 between its kernels
-        MOE_CUDA(launch_decode(L, x, T, y, s, nr, /*packed=*/small));
+        MOE_CUDA(launch_decode(L, x, T, &nsplit, s, nr, /*packed=*/small));
     } else {
         if (!small) MOE_CUDA(launch_dispatch_permute(L, x, T, s, nr));
         prof_mark(L, 3, s);
-        MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/false));
+        MOE_CUDA(launch_expert_gemm_rows(L, T * L.k, nullptr, s, 0));
         prof_mark(L, 4, s);
-        MOE_CUDA(launch_expert_gemm(L, T, y, s, /*down=*/true));
+        MOE_CUDA(launch_expert_gemm_rows(L, T * L.k, nullptr, s, 3,
+                                         (size_t)T * L.k * L.d, &nsplit));
     }
-    if (block) MOE_CUDA(launch_residual_add(L, y, x, (size_t)T * L.d, s));
+    // The combine (and the block's residual, y = moe + x) counts as down time.
+    MOE_CUDA(launch_combine(L, T, nsplit, block ? x : nullptr, y, s));
     prof_mark(L, kProfEnd, s);
     return MOE_OK;
 }

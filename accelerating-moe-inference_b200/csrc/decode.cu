@@ -16,10 +16,11 @@
 //   through L1 (they are tiny and shared by every warp).  Warp reductions
 //   give the dots; SwiGLU is applied and H (fp32, one row per routed token,
 //   unpadded) is written.
-// decode_down: work items are (active expert, 4 output columns, 1024-wide K
+// decode_down: work items are (active expert, 4 output columns, 2048-wide K
 //   chunk of the padded d_ff), again in equal contiguous ranges per warp.
-//   Each partial dot is scaled by the routing weight and added into y, so the
-//   split-K sum and the combine are one reduction.
+//   Each partial dot is stored, unweighted, at part[chunk][slot of the row];
+//   the ordered combine (combine.cu) adds the chunks in order and the
+//   experts in ascending order, so the result is bit-reproducible.
 // No shared-memory staging and no block-wide synchronisation: warps are
 // independent, and the ranges balance the bytes each warp streams to within
 // one step.
@@ -34,7 +35,6 @@ namespace {
 constexpr int kDecThreads = 512;            // 16 warps per CTA
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kMaxDecodeTokens = 64;
-constexpr int kDownChunk = 2048;            // K chunk of the down projection
 
 // Weights are read exactly once: bypass L1 so the stream does not evict the
 // token rows every warp re-reads from it.
@@ -217,8 +217,8 @@ template <typename WT, int TM>
 __global__ void __launch_bounds__(kDecThreads, 1)
 decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d, int ffp,
                    int E, const int* __restrict__ counts, const int* __restrict__ eoff,
-                   const int* __restrict__ row_token, const float* __restrict__ row_weight,
-                   float* __restrict__ y) {
+                   const int* __restrict__ row_slot, float* __restrict__ part,
+                   size_t split_stride) {
     __shared__ Active A;
     wait_predecessor_grid();
     build_active(A, counts, E);
@@ -257,11 +257,12 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
             for (int m = 0; m < TM; ++m) {
                 if (m >= gm) break;
                 const int prow = r0 + g0 + m;
+                float* dst = part + (size_t)(k0 / kDownChunk) * split_stride +
+                             (size_t)row_slot[prow] * d + n0;
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const float v = warp_sum(acc[r][m]);
-                    if (lane == r && n0 + r < d)
-                        atomicAdd(y + (size_t)row_token[prow] * d + n0 + r, row_weight[prow] * v);
+                    if (lane == r && n0 + r < d) dst[r] = v;
                 }
             }
         }
@@ -286,7 +287,7 @@ cudaError_t launch_dependent(const Layer& L, Kern kern, cudaStream_t s, Args... 
 }
 
 template <typename WT, typename AT, int TM>
-cudaError_t launch_t(Layer& L, float* y, cudaStream_t s, const WT* w13, const WT* w2) {
+cudaError_t launch_t(Layer& L, size_t stride, cudaStream_t s, const WT* w13, const WT* w2) {
     const Workspace& W = L.ws;
     cudaError_t err = launch_dependent(L, decode_gateup_kernel<WT, AT, TM>, s,
                                        static_cast<const AT*>(W.a_hi), w13, L.d, L.ffp, L.E,
@@ -295,18 +296,19 @@ cudaError_t launch_t(Layer& L, float* y, cudaStream_t s, const WT* w13, const WT
     prof_mark(L, 4, s);
     return launch_dependent(L, decode_down_kernel<WT, TM>, s, (const float*)W.h_dec, w2, L.d,
                             L.ffp, L.E, (const int*)W.counts, (const int*)W.eoff,
-                            (const int*)W.row_token, (const float*)W.row_weight, y);
+                            (const int*)W.row_slot, W.part, stride);
 }
 
 template <typename WT, typename AT>
-cudaError_t launch_w(Layer& L, int T, float* y, cudaStream_t s, const WT* w13, const WT* w2) {
+cudaError_t launch_w(Layer& L, int T, cudaStream_t s, const WT* w13, const WT* w2) {
     // Token rows per pass over the weights: up to 4 (the weights of a pass
     // are re-read from L1/L2 for further passes).
     const int tm = T >= 4 ? 4 : (T >= 2 ? 2 : 1);
+    const size_t stride = (size_t)T * L.k * L.d;
     switch (tm) {
-        case 4: return launch_t<WT, AT, 4>(L, y, s, w13, w2);
-        case 2: return launch_t<WT, AT, 2>(L, y, s, w13, w2);
-        default: return launch_t<WT, AT, 1>(L, y, s, w13, w2);
+        case 4: return launch_t<WT, AT, 4>(L, stride, s, w13, w2);
+        case 2: return launch_t<WT, AT, 2>(L, stride, s, w13, w2);
+        default: return launch_t<WT, AT, 1>(L, stride, s, w13, w2);
     }
 }
 
@@ -314,9 +316,12 @@ cudaError_t launch_w(Layer& L, int T, float* y, cudaStream_t s, const WT* w13, c
 
 int decode_max_supported_tokens() { return kMaxDecodeTokens; }
 
-cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
+int decode_chunks(const Layer& L) { return (L.ffp + kDownChunk - 1) / kDownChunk; }
+
+cudaError_t launch_decode(Layer& L, const float* x, int T, int* nsplit, cudaStream_t s,
                           const NormRef& nr, bool packed) {
     if (T > kMaxDecodeTokens || !L.ws.h_dec) return cudaErrorInvalidValue;
+    *nsplit = decode_chunks(L);
     // Pack the routed token rows (fp32 as is in FP32 precision, bf16 in BF16),
     // normalised on the way when nr is active -- unless the small-batch
     // router already did.
@@ -327,9 +332,9 @@ cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_
     prof_mark(L, 3, s);
     if (L.cfg.precision == MOE_PREC_BF16)
         return launch_w<__nv_bfloat16, __nv_bfloat16>(
-            L, T, y, s, static_cast<const __nv_bfloat16*>(L.w13_hi),
+            L, T, s, static_cast<const __nv_bfloat16*>(L.w13_hi),
             static_cast<const __nv_bfloat16*>(L.w2_hi));
-    return launch_w<float, float>(L, T, y, s, L.w13_f32, L.w2_f32);
+    return launch_w<float, float>(L, T, s, L.w13_f32, L.w2_f32);
 }
 
 }  // namespace moe

@@ -1,37 +1,42 @@
-// Expert parallelism: one process and one B200 per rank, experts split
-// contiguously across the ranks.  The reference has no multi-GPU path; this
-// is the layer's scale-out.
+// Expert parallelism: one process and one B200 per rank; rank r holds experts
+// r, r + G, r + 2G, ... (round-robin placement).  The reference has no
+// multi-GPU path; this is the layer's scale-out.
 //
-// Fused transport (the default, MOE_EP_TRANSPORT_P2P): every rank allocates a
-// receive buffer and a return buffer with one fixed segment per source rank
-// ([G][cap] rows, cap = the most rows one source can send: max_tokens x
-// min(top_k, experts per rank)) plus count and flag words, and maps every
-// other rank's through CUDA IPC (handles exchanged once, with an NCCL
-// all-gather).  Then, with no host synchronisation and no NCCL call:
-//   1. router; compact dispatch scan (granule 1);
-//   2. the dispatch permute stores each routed row straight into the owning
-//      rank's receive buffer over NVLink (at this rank's segment, in compact
-//      order) and records where it went;
-//   3. a signal kernel writes this rank's per-expert counts into each rank's
-//      count words and raises its dispatch flag there (system-scope fence,
-//      release store of the step's epoch);
+// Fused, deduplicated transport (the default, MOE_EP_TRANSPORT_P2P): every
+// rank allocates a receive buffer and a return buffer with one fixed segment
+// per source rank ([G][cap] rows, cap = max_tokens: one row per token per
+// source), a metadata buffer and count and flag words, and maps every other
+// rank's through CUDA IPC (handles exchanged once, with an NCCL all-gather).
+// Then, with no host synchronisation and no NCCL call:
+//   1. router; compact scans of the expert positions and of the
+//      destinations;
+//   2. the push kernel stores one row per (token, destination rank) straight
+//      into the destination's receive buffer over NVLink, with the token's
+//      selections on that rank as metadata;
+//   3. a signal kernel writes this rank's counts into each rank's count
+//      words and raises its dispatch flag there (system-scope fence, release
+//      store of the step's epoch);
 //   4. a wait kernel spins (bounded) until every source's flag shows the
-//      epoch; the arrival scan, arrangement and both GEMMs follow, the down
-//      GEMM's epilogue storing each result straight into the source rank's
-//      return buffer;
-//   5. signal and wait again for the returns; the combine reads the return
-//      buffer (local memory) and adds weight x row into y.
+//      epoch; the arrival scan and the arrangement place each received row
+//      in each of its experts' GEMM rows; both GEMMs run, the down GEMM
+//      storing each expert's output at its (received row, selection) slot;
+//   5. the return push adds each received row's expert outputs in ascending
+//      expert order (the reference's fma combine) and stores the one summed
+//      row into the source's return buffer; signal and wait again;
+//   6. the combine adds the rows a token's ranks returned, in ascending rank
+//      order.  Every sum has a fixed order, so a step is bit-reproducible.
 // Buffers are never rewritten before their reader is done, by the data
 // dependencies alone: a rank pushes step e + 1 only after its step-e combine,
 // which needed every rank's step-e results, which those ranks computed after
-// arranging (copying out) their step-e arrivals.
+// arranging (copying out) their step-e arrivals.  No load of another GPU's
+// memory uses TMA; the peer traffic is plain stores.
 //
 // NCCL transport (MOE_EP_TRANSPORT_NCCL), the baseline; forward on rank r
 // with T local tokens (every rank runs it collectively):
 //   1. router over all E experts (router weights are replicated);
-//   2. compact dispatch (granule 1): rows sorted by global expert, then token,
-//      so the rows for rank j are one contiguous run; fp32 rows in FP32
-//      precision, bf16 rows in BF16 precision;
+//   2. compact dispatch (granule 1): rows sorted by dispatch position, then
+//      token, so the rows for rank j are one contiguous run; fp32 rows in
+//      FP32 precision, bf16 rows in BF16 precision;
 //   3. counts exchange: each rank sends rank j its E/G per-expert counts for
 //      j's experts; one small device-to-host copy gives the split sizes;
 //   4. payload exchange (grouped ncclSend / ncclRecv, self included);
@@ -44,7 +49,8 @@
 //      bf16 in BF16 precision) at the row it arrived in;
 //   7. return exchange (the reverse splits), so each rank gets its own rows
 //      back in its compact dispatch order;
-//   8. combine: y[token] += routing weight * returned row.
+//   8. combine: y[token] = its k returned rows, weighted, in ascending expert
+//      order.
 #include <cuda_bf16.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -128,6 +134,7 @@ struct EpState {
     void* send_rows = nullptr;  // [T*k][d] compact, expert-sorted
     int* send_tok = nullptr;    // compact row -> local token
     float* send_w = nullptr;    // compact row -> routing weight
+    int* send_slot = nullptr;   // selection slot t * k + s -> compact row
     int* send_eoff = nullptr;   // [E+1] compact offsets
     void* recv_rows = nullptr;  // [G*T*k][d]
     float* ret_send = nullptr;  // [G*T*k][d] results (dispatch element type), by arrival row
@@ -151,7 +158,6 @@ struct EpState {
     int* dest_cnt = nullptr;     // [G] rows sent to each rank
     int* dest_off = nullptr;     // [G + 1]
     int* slot_dd = nullptr;      // [cap_T][G] row of token t at rank g (-1: none)
-    float* y_recv = nullptr;     // [G * cap_src][d] fp32: weighted sum of the local experts per received row
     int* rows_recv = nullptr;    // [G] rows received from each source this step
     void** d_peer_recv = nullptr;  // [G] every rank's p2p_recv (own included), device array
     void** d_peer_ret = nullptr;
@@ -176,11 +182,12 @@ void ep_free_buffers(EpState& S) {
                     (void*)S.p2p_flag, (void*)S.d_peer_recv,
                     (void*)S.d_peer_ret, (void*)S.d_peer_cnt, (void*)S.d_peer_flag,
                     (void*)S.p2p_meta, (void*)S.dest_hist, (void*)S.dest_cnt, (void*)S.dest_off,
-                    (void*)S.slot_dd, (void*)S.y_recv, (void*)S.rows_recv, (void*)S.d_peer_meta})
+                    (void*)S.slot_dd, (void*)S.send_slot, (void*)S.rows_recv,
+                    (void*)S.d_peer_meta})
         if (p) cudaFree(p);
     S.p2p_meta = nullptr;
     S.dest_hist = S.dest_cnt = S.dest_off = S.slot_dd = S.rows_recv = nullptr;
-    S.y_recv = nullptr;
+    S.send_slot = nullptr;
     S.d_peer_meta = nullptr;
     S.p2p_recv = S.p2p_ret = nullptr;
     S.p2p_cnt = nullptr;
@@ -212,6 +219,7 @@ int ep_ensure(Layer& L, int T) {
     A(&S.send_rows, rows_local * S.row_bytes);
     A((void**)&S.send_tok, rows_local * sizeof(int));
     A((void**)&S.send_w, rows_local * sizeof(float));
+    A((void**)&S.send_slot, rows_local * sizeof(int));
     A((void**)&S.send_eoff, (L.E_route + 1) * sizeof(int));
     A(&S.recv_rows, rows_recv * S.row_bytes);
     A((void**)&S.ret_send, rows_recv * L.d * sizeof(float));
@@ -299,32 +307,54 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
     }
 }
 
-// y[token] += weight * returned row, one compact row per warp.  Returned rows
-// are fp32 (FP32 precision) or bf16 (BF16 precision); compact row j's is row
-// slot[j] of ret (fused transport: written by another GPU, read through L2
-// only), else row j.
+// y[t] = token t's k returned rows (fp32 in FP32 precision, bf16 in BF16),
+// each times its routing weight, added with the reference's fma in ascending
+// expert order from 0.  Slot s's row is ret[slot_row[t * k + s]].  idx holds
+// dispatch positions; under the round-robin placement position p is expert
+// (p % El) * G + p / El.  One warp per token; every element of y[t] is
+// written.
 template <bool kF32>
 __global__ void __launch_bounds__(256)
-ep_combine_kernel(const void* __restrict__ ret, int rows, int d, const int* __restrict__ tok,
-                  const float* __restrict__ w, const int* __restrict__ slot, float* __restrict__ y) {
+ep_combine_kernel(const void* __restrict__ ret, int T, int k, int d, int G, int El,
+                  const int* __restrict__ idx, const float* __restrict__ w,
+                  const int* __restrict__ slot_row, float* __restrict__ y) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = blockIdx.x * 8 + warp;
-    if (j >= rows) return;
-    const float wt = w[j];
-    const size_t rj = slot ? (size_t)slot[j] : (size_t)j;
-    float* dst = y + (size_t)tok[j] * d;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    int key = 0, row = 0;
+    float wv = 0.0f;
+    if (lane < k) {
+        const int p = idx[(size_t)t * k + lane];
+        key = (p % El) * G + p / El;
+        wv = w[(size_t)t * k + lane];
+        row = slot_row[(size_t)t * k + lane];
+    }
+    int ord[kMaxTopK];
+    float ow[kMaxTopK];
+    slot_order_keys<kMaxTopK>(key, wv, k, lane, ord, ow);
+    int rows[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) rows[r] = __shfl_sync(0xffffffffu, row, ord[r]);
+    float4* dst = reinterpret_cast<float4*>(y + (size_t)t * d);
     for (int v = lane; v < d / 4; v += 32) {
-        float4 r;
-        if constexpr (kF32) {
-            r = __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(ret) + rj * d) + v);
-        } else {
-            const uint2 u = __ldcg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(ret) +
-                                                                 rj * d) + v);
-            r = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                            __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int r = 0; r < k; ++r) {
+            const size_t rj = (size_t)rows[r];
+            float4 f;
+            if constexpr (kF32) {
+                f = reinterpret_cast<const float4*>(static_cast<const float*>(ret) + rj * d)[v];
+            } else {
+                const uint2 u = reinterpret_cast<const uint2*>(
+                    static_cast<const __nv_bfloat16*>(ret) + rj * d)[v];
+                f = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+            }
+            acc.x = __fmaf_rn(ow[r], f.x, acc.x);
+            acc.y = __fmaf_rn(ow[r], f.y, acc.y);
+            acc.z = __fmaf_rn(ow[r], f.z, acc.z);
+            acc.w = __fmaf_rn(ow[r], f.w, acc.w);
         }
-        atomicAdd(reinterpret_cast<float4*>(dst) + v,
-                  make_float4(wt * r.x, wt * r.y, wt * r.z, wt * r.w));
+        dst[v] = acc;
     }
 }
 
@@ -356,7 +386,7 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
             return cuda_err(ce, "dispatch scan");
         prof_mark(L, 2, s);
         if ((ce = launch_dispatch_permute_to(L, x, T, Eg, S.send_eoff, S.send_tok, S.send_w,
-                                             S.send_rows, s)) != cudaSuccess)
+                                             S.send_slot, S.send_rows, s)) != cudaSuccess)
             return cuda_err(ce, "dispatch permute");
     } else {
         if ((ce = cudaMemsetAsync(W.counts, 0, Eg * sizeof(int), s)) != cudaSuccess)
@@ -434,15 +464,12 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 8: weighted combine into y.
     prof_mark(L, 7, s);
     if (T > 0) {
-        if ((ce = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * d, s)) != cudaSuccess)
-            return cuda_err(ce, "y memset");
-        const int rows = T * L.k;
         if (three_pass(L))
-            ep_combine_kernel<true><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
-                                                                   S.send_w, nullptr, y);
+            ep_combine_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(S.ret_recv, T, L.k, L.d, G, El,
+                                                                W.idx, W.wts, S.send_slot, y);
         else
-            ep_combine_kernel<false><<<(rows + 7) / 8, 256, 0, s>>>(S.ret_recv, rows, L.d, S.send_tok,
-                                                                    S.send_w, nullptr, y);
+            ep_combine_kernel<false><<<(T + 7) / 8, 256, 0, s>>>(S.ret_recv, T, L.k, L.d, G, El,
+                                                                 W.idx, W.wts, S.send_slot, y);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
     prof_mark(L, kProfEnd, s);
@@ -508,8 +535,8 @@ __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned 
 // A token whose k experts fall on the same rank crosses NVLink once for that
 // rank: the source sends one row per (token, destination rank) with the
 // token's selections on that rank as metadata; the rank runs the row through
-// each of its experts, sums their weighted outputs into one fp32 row
-// (y_recv, the down GEMM's combine epilogue), and returns that single row;
+// each of its experts, sums their weighted outputs into one fp32 row in
+// ascending expert order (the return push), and returns that single row;
 // the source adds its ranks' rows in ascending rank order.  Rows of one
 // source keep ascending token order, so each selection also carries its
 // position inside its expert's block from this source -- exactly the compact
@@ -612,43 +639,64 @@ ep_dedup_push_kernel(const float* __restrict__ x, int T, int d, int k, int El, i
     }
 }
 
+// The selections received row i (source s) carries, from its metadata, in
+// metadata order: local expert, routing weight and GEMM row of each.  An
+// entry whose row would fall outside the expert blocks (inconsistent
+// metadata: never expected) is dropped, by the arrangement and the return
+// push alike.  Metadata was written by another GPU: read through L2 only.
+struct DdSelections {
+    int n;
+    int e[kMaxTopK];
+    float w[kMaxTopK];
+    int prow[kMaxTopK];
+};
+
+__device__ __forceinline__ void dd_selections(const int2* __restrict__ meta, size_t i, int kmax,
+                                              int s, int El, const int* __restrict__ base,
+                                              const int* __restrict__ eoff, DdSelections& out) {
+    out.n = 0;
+    const int lim = eoff[El];
+    for (int j = 0; j < kmax && j < kMaxTopK; ++j) {
+        const int2 m = __ldcg(meta + i * kmax + j);
+        if (m.x < 0) break;
+        const int e = m.x & 255, pos = m.x >> 8;
+        if (e >= El) break;
+        const int pr = eoff[e] + base[s * El + e] + pos;
+        if (pr >= lim) continue;
+        out.e[out.n] = e;
+        out.w[out.n] = __int_as_float(m.y);
+        out.prow[out.n] = pr;
+        ++out.n;
+    }
+}
+
 // One warp per received row (source s, row r < rows_recv[s]): its metadata
-// places it in each of its local experts' GEMM blocks (row_token = the
-// received slot s * cap + r, row_weight = the routing weight), the row is
-// converted into each of those A rows, and its y_recv row is zeroed for the
-// down GEMM's combine epilogue.  Rows and metadata were written by other
-// GPUs: read through L2 only.
+// places it in each of its local experts' GEMM rows (row_token = the
+// received slot i = s * cap + r, row_weight = the routing weight, row_slot =
+// i * kmax + j for its j-th placed selection, where the down GEMM stores that
+// expert's output), and the row is converted into each of those A rows.
+// Rows were written by other GPUs: read through L2 only.
 template <bool kTf32x3>
 __global__ void __launch_bounds__(256)
 ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ meta,
                      const int* __restrict__ rows_recv, int cap, int d, int G, int El, int kmax,
                      const int* __restrict__ base, const int* __restrict__ eoff,
                      int* __restrict__ row_token, float* __restrict__ row_weight,
-                     void* __restrict__ a_hi, void* __restrict__ a_lo, float* __restrict__ y_recv) {
+                     int* __restrict__ row_slot, void* __restrict__ a_hi,
+                     void* __restrict__ a_lo) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t i = (size_t)blockIdx.x * 8 + warp;
     if (i >= (size_t)G * cap) return;
     const int s = (int)(i / cap), r = (int)(i % cap);
     if (r >= rows_recv[s]) return;
-    int prow[8];
-    int n = 0;
-    const int lim = eoff[El];
-    for (int j = 0; j < kmax && j < 8; ++j) {
-        const int2 m = __ldcg(meta + i * kmax + j);
-        if (m.x < 0) break;
-        const int e = m.x & 255, pos = m.x >> 8;
-        if (e >= El) break;
-        const int pr = eoff[e] + base[s * El + e] + pos;
-        if (pr >= lim) continue;   // inconsistent metadata: never expected, never written past the blocks
-        prow[n] = pr;
-        if (lane == 0) {
-            row_token[prow[n]] = (int)i;
-            row_weight[prow[n]] = __int_as_float(m.y);
-        }
-        ++n;
+    DdSelections sel;
+    dd_selections(meta, i, kmax, s, El, base, eoff, sel);
+    const int n = sel.n;
+    if (lane < n) {
+        row_token[sel.prow[lane]] = (int)i;
+        row_weight[sel.prow[lane]] = sel.w[lane];
+        row_slot[sel.prow[lane]] = (int)(i * kmax) + lane;
     }
-    float4* yr = reinterpret_cast<float4*>(y_recv + i * d);
-    for (int v = lane; v < d / 4; v += 32) yr[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if constexpr (kTf32x3) {
         const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + i * d);
         for (int v = lane; v < d / 4; v += 32) {
@@ -659,8 +707,8 @@ ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ met
             h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
             h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
             for (int j = 0; j < n; ++j) {
-                reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow[j] * d)[v] = h;
-                reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow[j] * d)[v] = l;
+                reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)sel.prow[j] * d)[v] = h;
+                reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)sel.prow[j] * d)[v] = l;
             }
         }
     } else {
@@ -668,31 +716,63 @@ ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ met
         for (int v = lane; v < d / 8; v += 32) {
             const uint4 u = __ldcg(src + v);
             for (int j = 0; j < n; ++j)
-                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow[j] * d)[v] = u;
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)sel.prow[j] * d)[v] = u;
         }
     }
 }
 
-// One warp per received row: its summed expert output back to the source's
-// return buffer, row rank * cap + r (bf16 in BF16 precision, fp32 in FP32).
+// One warp per received row i: the outputs of its experts (part row
+// i * kmax + j for its j-th placed selection, unweighted fp32) are added with
+// the reference's fma in ascending expert order from 0, and the one summed
+// row goes back to the source's return buffer, row rank * cap + r (bf16 in
+// BF16 precision, fp32 in FP32).  Local expert order is global expert order
+// on one rank (rank + G * local).
 template <bool kF32>
 __global__ void __launch_bounds__(256)
-ep_return_push_kernel(const float* __restrict__ y_recv, const int* __restrict__ rows_recv, int cap,
-                      int d, int G, int rank, void* const* __restrict__ peer_ret) {
+ep_return_push_kernel(const float* __restrict__ part, const int2* __restrict__ meta,
+                      const int* __restrict__ rows_recv, int cap, int d, int G, int El, int kmax,
+                      const int* __restrict__ base, const int* __restrict__ eoff, int rank,
+                      void* const* __restrict__ peer_ret) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t i = (size_t)blockIdx.x * 8 + warp;
     if (i >= (size_t)G * cap) return;
     const int s = (int)(i / cap), r = (int)(i % cap);
     if (r >= rows_recv[s]) return;
-    const float4* src = reinterpret_cast<const float4*>(y_recv + i * d);
+    DdSelections sel;
+    dd_selections(meta, i, kmax, s, El, base, eoff, sel);
+    // Placed index j of each selection, by ascending expert (insertion sort;
+    // experts are distinct within a token).
+    int ord[kMaxTopK];
+    for (int j = 0; j < sel.n; ++j) {
+        int q = j;
+        while (q > 0 && sel.e[ord[q - 1]] > sel.e[j]) {
+            ord[q] = ord[q - 1];
+            --q;
+        }
+        ord[q] = j;
+    }
+    const float4* src = reinterpret_cast<const float4*>(part) + i * kmax * (d / 4);
     const size_t row = (size_t)rank * cap + r;
+    auto sum4 = [&](int v) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int q = 0; q < sel.n; ++q) {
+            const int j = ord[q];
+            const float4 f = __ldcs(src + (size_t)j * (d / 4) + v);
+            const float w = sel.w[j];
+            acc.x = __fmaf_rn(w, f.x, acc.x);
+            acc.y = __fmaf_rn(w, f.y, acc.y);
+            acc.z = __fmaf_rn(w, f.z, acc.z);
+            acc.w = __fmaf_rn(w, f.w, acc.w);
+        }
+        return acc;
+    };
     if constexpr (kF32) {
         float4* dst = reinterpret_cast<float4*>(static_cast<float*>(peer_ret[s]) + row * d);
-        for (int v = lane; v < d / 4; v += 32) dst[v] = src[v];
+        for (int v = lane; v < d / 4; v += 32) dst[v] = sum4(v);
     } else {
         uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(peer_ret[s]) + row * d);
         for (int v = lane; v < d / 8; v += 32) {
-            const float4 a = src[2 * v], b = src[2 * v + 1];
+            const float4 a = sum4(2 * v), b = sum4(2 * v + 1);
             __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y), p1 = __floats2bfloat162_rn(a.z, a.w);
             __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y), p3 = __floats2bfloat162_rn(b.z, b.w);
             dst[v] = make_uint4(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1),
@@ -766,7 +846,6 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     A((void**)&S.dest_cnt, G * sizeof(int));
     A((void**)&S.dest_off, (G + 1) * sizeof(int));
     A((void**)&S.slot_dd, (size_t)capT * G * sizeof(int));
-    A((void**)&S.y_recv, (size_t)G * S.cap_src * L.d * sizeof(float));
     A((void**)&S.rows_recv, G * sizeof(int));
     A((void**)&S.d_peer_recv, G * sizeof(void*));
     A((void**)&S.d_peer_ret, G * sizeof(void*));
@@ -902,33 +981,38 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     if (three_pass(L))
         ep_dd_arrange_kernel<true><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
                                                         S.cap_src, L.d, G, El, S.kmax, S.cnt_scan,
-                                                        W.eoff, W.row_token, W.row_weight, W.a_hi,
-                                                        W.a_lo, S.y_recv);
+                                                        W.eoff, W.row_token, W.row_weight,
+                                                        W.row_slot, W.a_hi, W.a_lo);
     else
         ep_dd_arrange_kernel<false><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
                                                          S.cap_src, L.d, G, El, S.kmax,
                                                          S.cnt_scan, W.eoff, W.row_token,
-                                                         W.row_weight, W.a_hi, W.a_lo, S.y_recv);
+                                                         W.row_weight, W.row_slot, W.a_hi,
+                                                         W.a_lo);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
-    // 5-6: the local experts; the down GEMM's combine epilogue adds each
-    // expert's weighted output into its received row's y_recv row.  The
-    // expected routed rows (T * k, this rank's own) size the GEMM launch; any
-    // count is run correctly.
+    // 5-6: the local experts; the down GEMM stores each expert's output at
+    // its (received row, selection) slot, K whole.  The expected routed rows
+    // (T * k, this rank's own) size the GEMM launch; any count is run
+    // correctly.
     const int R_est = std::max(T, 1) * L.k;
     prof_mark(L, 3, s);
     if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 0)) != cudaSuccess)
         return cuda_err(ce, "gate/up GEMM");
     prof_mark(L, 4, s);
-    if ((ce = launch_expert_gemm_rows(L, R_est, S.y_recv, s, 1)) != cudaSuccess)
+    if ((ce = launch_expert_gemm_rows(L, R_est, nullptr, s, 3)) != cudaSuccess)
         return cuda_err(ce, "down GEMM");
     // 7: one summed row per received row back to its source; return flags.
     prof_mark(L, 6, s);
     if (three_pass(L))
-        ep_return_push_kernel<true><<<grid, 256, 0, s>>>(S.y_recv, S.rows_recv, S.cap_src, L.d, G,
-                                                         S.rank, S.d_peer_ret);
+        ep_return_push_kernel<true><<<grid, 256, 0, s>>>(W.part, S.p2p_meta, S.rows_recv,
+                                                         S.cap_src, L.d, G, El, S.kmax,
+                                                         S.cnt_scan, W.eoff, S.rank,
+                                                         S.d_peer_ret);
     else
-        ep_return_push_kernel<false><<<grid, 256, 0, s>>>(S.y_recv, S.rows_recv, S.cap_src, L.d, G,
-                                                          S.rank, S.d_peer_ret);
+        ep_return_push_kernel<false><<<grid, 256, 0, s>>>(W.part, S.p2p_meta, S.rows_recv,
+                                                          S.cap_src, L.d, G, El, S.kmax,
+                                                          S.cnt_scan, W.eoff, S.rank,
+                                                          S.d_peer_ret);
     ep_signal_kernel<<<1, sig_threads, 0, s>>>(nullptr, nullptr, S.d_peer_flag, G, El, S.rank, 1,
                                                epoch);
     ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 1, epoch, nullptr,

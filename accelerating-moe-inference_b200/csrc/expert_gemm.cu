@@ -7,14 +7,15 @@
 //           applied in the epilogue straight out of TMEM.  Replaces
 //           gemm_grouped<true,true> (src/model.cu:618-643) and
 //           PhiMLP::forward's w1/w3/silu/mul (src/layer.cu:32-41).
-// down:     y[token(r)] += weight(r) * (H[r] . w2[e])
-//           The weighted un-permute/combine is the epilogue: each row's
-//           fp32 result is scaled by its routing weight and added into the
-//           token's output row with a vector reduction.  Replaces
-//           gemm_grouped_combine<1,2> (src/model.cu:645-667, 417-449) and the
-//           combine loop src/layer.cu:100-101.  With top-2 the two adds into a
-//           zeroed row commute, so y is deterministic; with k > 2 the order
-//           of the k adds is not fixed.
+// down:     out[r] = H[r] . w2[e], stored unweighted at the row's selection
+//           slot (part[split][row_slot[r]]) for the ordered combine
+//           (combine.cu), which adds a token's k rows in ascending expert
+//           order with the reference's fma -- the combine of
+//           gemm_grouped_combine<1,2> (src/model.cu:645-667, 417-449) and of
+//           src/layer.cu:100-101, independent of the tile schedule.  Two
+//           other epilogues serve the decoder's dense projections (add
+//           weight * out into y[row_token[r]]) and the NCCL expert-parallel
+//           transport (store out at y[row_token[r]]).
 //
 // One persistent CTA per SM, 6 warps:
 //   warp 0      TMA producer (one thread): A and B K-blocks into a ring of
@@ -37,7 +38,7 @@
 namespace moe {
 namespace {
 
-enum Epi { kEpiGateUp = 0, kEpiDown = 1, kEpiDownStore = 2 };
+enum Epi { kEpiGateUp = 0, kEpiDown = 1, kEpiDownStore = 2, kEpiDownSlot = 3 };
 
 struct GemmParams {
     const MTile* mtiles;
@@ -55,15 +56,14 @@ struct GemmParams {
     const int* row_token;
     const float* row_weight;
     float* y;          // Down: [T][d] accumulated; DownStore: [rows][d], row row_token[prow]
+    const int* row_slot;   // DownSlot: packed row -> selection slot
+    float* part;           // DownSlot: [k_splits][slots][d]
+    size_t split_stride;   // DownSlot: floats between the splits' planes
     int d;
     int* err;
 };
 
 constexpr int kThreads = 192;
-// Split-K of the down GEMM: only for at most this many routed rows, and at
-// least this many 128-byte K blocks per split.
-constexpr int kSplitMaxRows = 64;
-constexpr int kSplitMinBlocks = 8;
 constexpr int kABytes = kTileM * 128;   // one A plane per stage: 128 rows x 128 B
 constexpr int kBBytes = kTileN * 128;   // one B plane per stage: 256 rows x 128 B
 constexpr int kAccCols = kTileN;        // fp32 columns per accumulator
@@ -104,7 +104,7 @@ __device__ __forceinline__ TileCoord decode_tile(const MTile* __restrict__ mtile
 // warp-collective, so every lane runs the loads.
 template <bool kTf32x3, int kEpi>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbase, bool valid,
-                                              size_t prow, int nt) {
+                                              size_t prow, int nt, int split) {
     if constexpr (kEpi == kEpiGateUp) {
 #pragma unroll 1
         for (int c = 0; c < kTileN / 2; c += 32) {
@@ -151,6 +151,24 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
                         dst[j / 8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     }
                 }
+            }
+        }
+    } else if constexpr (kEpi == kEpiDownSlot) {
+        // The row's result, unweighted and in fp32, at its selection slot.
+        const int slot = valid ? p.row_slot[prow] : 0;
+        float* rowp = p.part + (size_t)split * p.split_stride + (size_t)slot * p.d;
+#pragma unroll 1
+        for (int c = 0; c < kTileN; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tbase + c, v);
+            tmem_ld_wait();
+            const int col = nt * kTileN + c;
+            if (valid && col < p.d) {
+                float4* out = reinterpret_cast<float4*>(rowp + col);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    out[j / 4] = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                             __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
             }
         }
     } else if constexpr (kEpi == kEpiDownStore) {
@@ -400,7 +418,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             const size_t prow = static_cast<size_t>(tile.row0 + row_in_tile);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kAccCols);
-            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, nt);
+            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, nt, t % p.k_splits);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -616,7 +634,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             const size_t prow = static_cast<size_t>(tile.row0 + (int)crank * kTileM + row_in_tile);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kAccCols);
-            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, tc.nt);
+            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, tc.nt, 0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
@@ -683,14 +701,39 @@ cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMa
     return cudaLaunchKernelEx(&cfg, kern, a_hi, a_lo, b_hi, b_lo, p);
 }
 
-}  // namespace
-
-cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down) {
-    return launch_expert_gemm_rows(L, T * L.k, y, s, down ? 1 : 0);
+// One template instantiation per (precision, epilogue) for each tile shape.
+template <bool kTf, int kEpi>
+cudaError_t dispatch_shape(const Layer& L, bool pair, const GemmParams& g, int clusters,
+                           int grid, cudaStream_t s) {
+    const Workspace& W = L.ws;
+    const bool gu = kEpi == kEpiGateUp;
+    const CUtensorMap& a_hi = gu ? W.tm_a_hi : W.tm_h_hi;
+    const CUtensorMap& a_lo = kTf ? (gu ? W.tm_a_lo : W.tm_h_lo) : a_hi;
+    if (pair) {
+        const CUtensorMap& b_hi = gu ? L.tm_w13_hi2 : L.tm_w2_hi2;
+        const CUtensorMap& b_lo = kTf ? (gu ? L.tm_w13_lo2 : L.tm_w2_lo2) : b_hi;
+        return launch_pair<kTf, kEpi>(a_hi, a_lo, b_hi, b_lo, g, clusters, !L.profile, s);
+    }
+    const CUtensorMap& b_hi = gu ? L.tm_w13_hi : L.tm_w2_hi;
+    const CUtensorMap& b_lo = kTf ? (gu ? L.tm_w13_lo : L.tm_w2_lo) : b_hi;
+    return launch_one<kTf, kEpi>(L, a_hi, a_lo, b_hi, b_lo, g, grid, s);
 }
 
+template <bool kTf>
+cudaError_t dispatch_mode(const Layer& L, int mode, bool pair, const GemmParams& g, int clusters,
+                          int grid, cudaStream_t s) {
+    switch (mode) {
+        case 0: return dispatch_shape<kTf, kEpiGateUp>(L, pair, g, clusters, grid, s);
+        case 1: return dispatch_shape<kTf, kEpiDown>(L, pair, g, clusters, grid, s);
+        case 2: return dispatch_shape<kTf, kEpiDownStore>(L, pair, g, clusters, grid, s);
+        default: return dispatch_shape<kTf, kEpiDownSlot>(L, pair, g, clusters, grid, s);
+    }
+}
+
+}  // namespace
+
 cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
-                                    int mode) {
+                                    int mode, size_t split_stride, int* nsplit) {
     const bool down = mode != 0;
     const Workspace& W = L.ws;
     const bool tf = three_pass(L);
@@ -704,12 +747,14 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
     g.row_token = W.row_token;
     g.row_weight = W.row_weight;
     g.y = y;
+    g.row_slot = W.row_slot;
+    g.part = W.part;
+    g.split_stride = split_stride;
     g.d = L.d;
     g.h_hi = W.h_hi;
     g.h_lo = W.h_lo;
     g.ldh = L.ffp;
     g.k_splits = 1;
-    g.kb_per = 0;   // set below, with k_blocks
     if (!down) {
         // gate/up: N = 2 * ffp per expert, K = d.
         g.n_tiles = 2 * L.ffp / kTileN;
@@ -722,6 +767,7 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         g.b_rows_per_expert = L.d;
     }
     g.kb_per = g.k_blocks;
+    if (nsplit) *nsplit = 1;
     // CTA-pair tiles pay off when experts have at least 256 routed rows on
     // average; below that (decode-sized T) most of a 256-row tile would be
     // padding and the 1-CTA tiles spread the weight stream over twice as many
@@ -730,64 +776,31 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
                       (L.gemm_variant == MOE_GEMM_AUTO && routed_rows >= 2 * kTileM * L.E);
     if (pair) {
         // CTA-pair tiles: 256 rows x 256 columns per 2-SM cluster.
-        GemmParams gp = g;
-        gp.mtiles = W.ptiles;
-        gp.num_mtiles = W.num_ptiles;
+        g.mtiles = W.ptiles;
+        g.num_mtiles = W.num_ptiles;
         int clusters = ((routed_rows + 2 * kTileM - 1) / (2 * kTileM) + L.E) * g.n_tiles;
         if (clusters > L.sm_count / 2) clusters = L.sm_count / 2;
-        if (!down) {
-            if (tf)
-                return launch_pair<true, kEpiGateUp>(W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi2, L.tm_w13_lo2,
-                                                     gp, clusters, !L.profile, s);
-            return launch_pair<false, kEpiGateUp>(W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi2, L.tm_w13_hi2,
-                                                  gp, clusters, !L.profile, s);
-        }
-        if (mode == 2) {
-            if (tf)
-                return launch_pair<true, kEpiDownStore>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2,
-                                                        L.tm_w2_lo2, gp, clusters, !L.profile, s);
-            return launch_pair<false, kEpiDownStore>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2,
-                                                     gp, clusters, !L.profile, s);
-        }
-        if (tf)
-            return launch_pair<true, kEpiDown>(W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi2, L.tm_w2_lo2, gp,
-                                               clusters, !L.profile, s);
-        return launch_pair<false, kEpiDown>(W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi2, L.tm_w2_hi2, gp,
-                                            clusters, !L.profile, s);
+        return tf ? dispatch_mode<true>(L, mode, true, g, clusters, 0, s)
+                  : dispatch_mode<false>(L, mode, true, g, clusters, 0, s);
     }
     // Decode-sized batches leave the down GEMM with few tiles (d / 256 per
     // routed expert), too few to keep every SM streaming weights: split K
-    // until there are about two work items per SM.  The combine epilogue adds
-    // weight x partial into y, so the splits need no other reduction (their
-    // order of addition is not fixed, so such results are not bit-repeatable).
-    if (mode == 1 && routed_rows <= kSplitMaxRows) {
+    // until there are about two work items per SM.  Each split's partial
+    // goes to its own plane (slot epilogue; the ordered combine adds the
+    // planes in split order) or is added into y (dense projections).
+    const bool can_split = mode == 1 || (mode == 3 && split_stride > 0);
+    if (can_split && routed_rows <= kSplitMaxRows) {
         const int tiles = std::min(routed_rows, L.E) * g.n_tiles;
         int ks = (2 * L.sm_count) / std::max(tiles, 1);
         ks = std::max(1, std::min(ks, g.k_blocks / kSplitMinBlocks));
         g.kb_per = (g.k_blocks + ks - 1) / ks;
         g.k_splits = (g.k_blocks + g.kb_per - 1) / g.kb_per;
+        if (nsplit) *nsplit = g.k_splits;
     }
     int grid = max_mtiles * g.n_tiles * g.k_splits;
     if (grid > L.sm_count) grid = L.sm_count;
-    if (!down) {
-        if (tf)
-            return launch_one<true, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_lo, L.tm_w13_hi, L.tm_w13_lo,
-                                                g, grid, s);
-        return launch_one<false, kEpiGateUp>(L, W.tm_a_hi, W.tm_a_hi, L.tm_w13_hi, L.tm_w13_hi, g,
-                                             grid, s);
-    }
-    if (mode == 2) {
-        if (tf)
-            return launch_one<true, kEpiDownStore>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo,
-                                                   g, grid, s);
-        return launch_one<false, kEpiDownStore>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi,
-                                                g, grid, s);
-    }
-    if (tf)
-        return launch_one<true, kEpiDown>(L, W.tm_h_hi, W.tm_h_lo, L.tm_w2_hi, L.tm_w2_lo, g, grid,
-                                          s);
-    return launch_one<false, kEpiDown>(L, W.tm_h_hi, W.tm_h_hi, L.tm_w2_hi, L.tm_w2_hi, g, grid,
-                                       s);
+    return tf ? dispatch_mode<true>(L, mode, false, g, 0, grid, s)
+              : dispatch_mode<false>(L, mode, false, g, 0, grid, s);
 }
 
 }  // namespace moe

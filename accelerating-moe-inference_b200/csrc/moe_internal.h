@@ -41,6 +41,12 @@ constexpr int kMaxTopK = 8;
 constexpr int kProfileStages = 8;
 constexpr int kProfileMarks = 24;  // stage boundaries one forward may record
 constexpr int kProfEnd = -1;       // the mark closing the last stage
+// Split-K of the down GEMM (single-CTA tiles): only for at most this many
+// routed rows, with at least this many 128-byte K blocks per split.
+constexpr int kSplitMaxRows = 64;
+constexpr int kSplitMinBlocks = 8;
+// K chunk of the decode down kernel (its split-K granule).
+constexpr int kDownChunk = 2048;
 
 // One 128-row slice of an expert's packed block.  m-tiles are listed expert
 // by expert; mstart / mcount locate the expert's own run in that list.  The
@@ -71,6 +77,12 @@ struct Workspace {
     int* num_ptiles = nullptr;
     int* row_token = nullptr;
     float* row_weight = nullptr;
+    // Packed row -> selection slot t * k + s (the ordered combine's index).
+    int* row_slot = nullptr;
+    // Expert output rows, unweighted, one per selection slot and K split:
+    // [splits][T * k][d] fp32, read by the ordered combine (combine.cu).
+    float* part = nullptr;
+    size_t part_rows = 0;
     void* a_hi = nullptr;
     void* a_lo = nullptr;
     void* h_hi = nullptr;
@@ -87,6 +99,43 @@ struct Workspace {
 };
 
 #ifdef __CUDACC__
+// A token's k selections ordered by ascending key (the expert index): ord[r]
+// is the slot of rank r and ow[r] its weight.  Warp-collective (k and KMAX
+// warp-uniform, k <= KMAX <= 32); lane s < k supplies slot s's key and
+// weight, other lanes' values are ignored.  Equal keys keep slot order.
+template <int KMAX>
+__device__ __forceinline__ void slot_order_keys(int key, float wv, int k, int lane,
+                                                int (&ord)[KMAX], float (&ow)[KMAX]) {
+    if (lane >= k) key = 0x7fffffff;
+    int rank = 0;
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+        if (j >= k) break;
+        const int kj = __shfl_sync(0xffffffffu, key, j);
+        rank += (kj < key) || (kj == key && j < lane);
+    }
+#pragma unroll
+    for (int r = 0; r < KMAX; ++r) {
+        const unsigned m = __ballot_sync(0xffffffffu, lane < k && rank == r);
+        const int s = m ? __ffs(m) - 1 : 0;
+        ord[r] = s;
+        ow[r] = __shfl_sync(0xffffffffu, wv, s);
+    }
+}
+
+// The same with the keys and weights read from idx[0..k) / w[0..k).
+template <int KMAX>
+__device__ __forceinline__ void slot_order(const int* idx, const float* w, int k, int lane,
+                                           int (&ord)[KMAX], float (&ow)[KMAX]) {
+    int key = 0;
+    float wv = 0.0f;
+    if (lane < k) {
+        key = idx[lane];
+        wv = w[lane];
+    }
+    slot_order_keys<KMAX>(key, wv, k, lane, ord, ow);
+}
+
 // Output expression of tensor_ops::layer_norm (src/tensor.cu:187) as GCC
 // contracts it: fma((x - mean) * inv, w, b), four columns at a time.
 __device__ __forceinline__ float4 layer_norm_out4(float4 x, float m, float iv, float4 w,
@@ -183,21 +232,21 @@ cudaError_t launch_router(const Layer& L, const float* x, int T, float* logits, 
 cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
 // Batches of at most 4 tokens: router, selection, layout and the routed rows
 // in one single-CTA launch (rows in the decode kernels' format if `decode`,
-// else the GEMMs'), which also zeroes y [T][d].  route_small_geometry says
-// whether it applies.
+// else the GEMMs').  route_small_geometry says whether it applies.
 bool route_small_geometry(const Layer& L, int T, bool norm, int* kc, int* stages);
 cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
-                               bool decode, float* y, cudaStream_t s);
+                               bool decode, cudaStream_t s);
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s,
                                     const NormRef& nr = {});
 // The same placement with the rows copied in the decode kernels' format:
 // fp32 as is (FP32 precision) or bf16 (BF16 precision).
 cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, cudaStream_t s,
                                         const NormRef& nr = {});
-// Placement into explicit outputs, routing over E experts with offsets eoff.
+// Placement into explicit outputs, routing over E experts with offsets eoff;
+// slot_row[t * k + s] receives the row of token t's s-th selection.
 cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
                                        const int* eoff, int* row_token, float* row_weight,
-                                       void* rows, cudaStream_t s);
+                                       int* slot_row, void* rows, cudaStream_t s);
 // The scan on any [nblk][E] count matrix, expert blocks rounded to `granule`
 // rows; mtiles == nullptr gives a compact layout with no tiles or padding.
 cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* counts, int* eoff,
@@ -205,19 +254,32 @@ cudaError_t launch_scan_generic(int* hist, int nblk, int E, int granule, int* co
                                 int* row_token, float* row_weight, cudaStream_t s);
 
 // expert_gemm.cu
-// down == false: gate/up GEMM with the SwiGLU epilogue into H;
-// down == true:  down GEMM with the weighted-combine epilogue into y.
-cudaError_t launch_expert_gemm(const Layer& L, int T, float* y, cudaStream_t s, bool down);
-// The same over `routed_rows` packed rows; mode 0 gate/up, 1 down with the
-// combine epilogue (y[row_token[row]] += row_weight[row] * result), 2 down
-// storing each row's result at y[row_token[row]] (bf16 in BF16 precision).
+// Grouped GEMMs over `routed_rows` packed rows.  mode:
+//   0 gate/up with the SwiGLU epilogue into H;
+//   1 down, adding into y: y[row_token[row]] += row_weight[row] * result
+//     (the dense projections of the decoder: one contribution per element
+//     unless K is split);
+//   2 down storing each row's result at y[row_token[row]] (bf16 in BF16
+//     precision; the NCCL expert-parallel transport);
+//   3 down storing each row's unweighted result at
+//     part[split][row_slot[row]] for the ordered combine.
+// split_stride (floats between the K splits' part planes; mode 3 only): 0
+// keeps K whole.  *nsplit receives the number of K splits (may be null).
 cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, cudaStream_t s,
-                                    int mode);
+                                    int mode, size_t split_stride = 0, int* nsplit = nullptr);
+
+// combine.cu: y[t] = the ordered combine of token t's k expert rows in
+// part ([nsplit][T * k][d]) with weights wts, plus resid[t] when non-null.
+cudaError_t launch_combine(const Layer& L, int T, int nsplit, const float* resid, float* y,
+                           cudaStream_t s);
 
 // decode.cu: T <= decode_max_supported_tokens() (64)
 // packed: the routed rows are already in the decode format (launch_route_small).
-cudaError_t launch_decode(Layer& L, const float* x, int T, float* y, cudaStream_t s,
+// The down kernel stores each slot's partial dots per K chunk into part;
+// *nsplit receives the number of chunks for the ordered combine.
+cudaError_t launch_decode(Layer& L, const float* x, int T, int* nsplit, cudaStream_t s,
                           const NormRef& nr = {}, bool packed = false);
+int decode_chunks(const Layer& L);
 int decode_max_supported_tokens();
 // What MOE_DECODE_AUTO resolves to for a precision (capi.cu).
 int auto_decode_max_tokens(int precision);

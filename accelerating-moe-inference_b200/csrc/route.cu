@@ -43,6 +43,10 @@ struct ScanOut {
     int* num_mtiles = nullptr;
     MTile* ptiles = nullptr;
     int* num_ptiles = nullptr;
+    // Selection slot maps (written whenever non-null, scan or not): packed
+    // row -> slot t * k + s, and slot -> packed row.
+    int* row_slot = nullptr;
+    int* slot_row = nullptr;
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
@@ -593,8 +597,11 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
         const int pos = s_base[my_e] + rank;
         s_dest[tid] = pos;
         if (blockIdx.y == 0) {
+            const int slot = (t0 + my_t) * k + (tid % k);
             row_token[pos] = t0 + my_t;
-            row_weight[pos] = wts[(size_t)(t0 + my_t) * k + (tid % k)];
+            row_weight[pos] = wts[slot];
+            if (so.row_slot) so.row_slot[pos] = slot;
+            if (so.slot_row) so.slot_row[slot] = pos;
         }
     }
     __syncthreads();
@@ -733,7 +740,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
                     float* __restrict__ logits_out, int* __restrict__ idx_out,
                     float* __restrict__ w_out, ScanOut so, int* __restrict__ row_token,
                     float* __restrict__ row_weight, void* __restrict__ a_hi,
-                    void* __restrict__ a_lo, float* __restrict__ y, int* err) {
+                    void* __restrict__ a_lo, int* err) {
     extern __shared__ __align__(16) float ring[];
     __shared__ uint64_t full[kSmallMaxStages], empty[kSmallMaxStages];
     __shared__ float lg[kSmallMaxTokens * (kMaxExperts + 1)];
@@ -746,7 +753,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nchunks = d / KC;
     const int chain_warps = (blockDim.x >> 5) - 1;
-    // Dependent launch: nothing the previous kernel touches (x, y, the
+    // Dependent launch: nothing the previous kernel touches (x, the
     // workspace) is read or written before it has completed.
     wait_predecessor_grid();
     constexpr bool norm = kNorm;
@@ -760,10 +767,6 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         fence_mbar_init();
     }
     for (int e = tid; e < E; e += blockDim.x) hist[e] = 0;
-    // The expert GEMMs / decode kernels add into y: start it at zero here
-    // rather than in a launch of its own.
-    for (int i = tid; i < T * d / 4; i += blockDim.x)
-        reinterpret_cast<float4*>(y)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     __syncthreads();
 
     // When every K chunk has a stage of its own (nchunks <= stages), all
@@ -943,6 +946,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         s_dest[tid] = pos;
         row_token[pos] = t;
         row_weight[pos] = s_w[tid];
+        so.row_slot[pos] = tid;
     }
     __syncthreads();
     // The routed rows, normalised if the norm is active, in the next stage's
@@ -1079,7 +1083,7 @@ bool route_small_geometry(const Layer& L, int T, bool norm, int* kc_out, int* st
 }
 
 cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
-                               bool decode, float* y, cudaStream_t s) {
+                               bool decode, cudaStream_t s) {
     const Workspace& W = L.ws;
     const bool norm = nr.mean != nullptr;
     SmallGeom gm;
@@ -1090,6 +1094,7 @@ cudaError_t launch_route_small(const Layer& L, const float* x, int T, const Norm
     ScanOut so;
     so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
     so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
+    so.row_slot = W.row_slot;
     // All chain warps are launched whatever T x E is: the tail (layout and
     // row copies) uses every thread.
     const int threads = kSmallThreads;
@@ -1113,7 +1118,7 @@ cudaError_t launch_route_small(const Layer& L, const float* x, int T, const Norm
         return cudaLaunchKernelEx(&cfg, kern, x, L.wg, (const float*)L.bias, T, L.d, L.E_route,
                                   L.k, L.cfg.router_policy, L.cfg.router_quantum,
                                   L.cfg.router_tie_eps, nr, gm, W.logits, W.idx, W.wts, so,
-                                  W.row_token, W.row_weight, W.a_hi, W.a_lo, y, W.dev_err);
+                                  W.row_token, W.row_weight, W.a_hi, W.a_lo, W.dev_err);
     };
     auto by_kc = [&](auto mode_c, auto norm_c) {
         constexpr int M = decltype(mode_c)::value;
@@ -1160,6 +1165,7 @@ cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, c
         so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
         so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
     }
+    so.row_slot = W.row_slot;
     if (three_pass(L))
         dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,
@@ -1173,17 +1179,19 @@ cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, c
 
 cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, int E,
                                        const int* eoff, int* row_token, float* row_weight,
-                                       void* rows, cudaStream_t s) {
+                                       int* slot_row, void* rows, cudaStream_t s) {
     const Workspace& W = L.ws;
     const dim3 grid = permute_grid(L, T);
+    ScanOut so;
+    so.slot_row = slot_row;
     if (three_pass(L))
         dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, ScanOut{}, NormRef{});
+                                                        row_weight, rows, nullptr, so, NormRef{});
     else
         dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
                                                         W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, ScanOut{}, NormRef{});
+                                                        row_weight, rows, nullptr, so, NormRef{});
     return cudaGetLastError();
 }
 
@@ -1196,6 +1204,7 @@ cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaS
         so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;
         so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
     }
+    so.row_slot = W.row_slot;
     if (three_pass(L))
         dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
                                                         W.blockhist, W.eoff, W.row_token,

@@ -11,10 +11,10 @@ CPU (gloo): the deduplicated fused transport's layout restated the same way
 expert-rank sum, one returned row), which must also equal the oracle and
 place every selection in exactly one GEMM row.
 
-GPU (2 B200s, skipped with fewer): moe_ep_forward_device itself against the
-oracle, per rank, with both transports: the fused one (rows and metadata
-stored into the other GPU's buffers over NVLink, flags in peer memory) and
-NCCL send/recv.
+GPU (2, 4 and 8 B200s, each skipped with fewer): moe_ep_forward_device
+itself against the oracle, per rank, with both transports: the fused one
+(rows and metadata stored into the other GPUs' buffers over NVLink, flags in
+peer memory) and NCCL send/recv; two steps must agree bit for bit.
 """
 import os
 import socket
@@ -268,7 +268,7 @@ def test_ep_plan_offsets_and_rejection():
         pkg.ep_plan(np.array([1, -1], np.int32), np.array([[0], [0]], np.int32), 2, 1)
 
 
-def _gpu_rank(rank, world, idbytes, q, precision, transport):
+def _gpu_rank(rank, world, idbytes, q, precision, transport, k=K):
     try:
         import torch
         sys.path.insert(0, str(ROOT / "tests"))
@@ -279,7 +279,7 @@ def _gpu_rank(rank, world, idbytes, q, precision, transport):
         x = _tokens(pkg, rank)
         m = pkg.MoeLayer.expert_parallel(rank, world, idbytes, d=D, ff=FF, E=E, wg=layer.wg,
                                          w1=layer.w1, w3=layer.w3, w2=layer.w2,
-                                         bias=layer.router_bias, top_k=K, policy=1,
+                                         bias=layer.router_bias, top_k=k, policy=1,
                                          precision=precision, device=rank,
                                          ep_transport=transport, max_tokens=64)
         xd = torch.from_numpy(x).cuda()
@@ -290,33 +290,42 @@ def _gpu_rank(rank, world, idbytes, q, precision, transport):
                                 torch.cuda.current_stream().cuda_stream)
             torch.cuda.synchronize()
             ys.append(yd.cpu().numpy().copy())
-        y_ref, *_ = oracle.Oracle().moe_forward(x, layer, K, oracle.POLICY_SOFTMAX)
+        y_ref, *_ = oracle.Oracle().moe_forward(x, layer, k, oracle.POLICY_SOFTMAX)
         m.close()
-        q.put((rank, rel_l2(ys[0], y_ref), rel_l2(ys[1], y_ref)))
+        same = bool(np.array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32)))
+        q.put((rank, rel_l2(ys[0], y_ref), rel_l2(ys[1], y_ref), same))
     except Exception as e:
-        q.put((rank, repr(e), None))
+        q.put((rank, repr(e), None, None))
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("k", [2, 4])
 @pytest.mark.parametrize("transport", [0, 1], ids=["p2p", "nccl"])
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
-def test_ep_forward_on_two_gpus(precision, transport):
+def test_ep_forward_on_gpus(precision, transport, k, world):
+    """Each rank's y against the oracle, twice (the epochs advance), and the
+    two steps bit-identical: the expert-rank sums and the combine run in a
+    fixed order whatever the arrival order.  Top-4 of 8 experts puts up to 4
+    of a token's experts on one rank at 2 GPUs."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     pkg = load_pkg()
     idbytes = pkg.ep_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, idbytes, q, precision, transport))
-             for r in range(2)]
+    procs = [ctx.Process(target=_gpu_rank, args=(r, world, idbytes, q, precision, transport, k))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=300) for _ in procs)
     for p in procs:
         p.join(timeout=60)
     tol = 1e-3 if precision == 0 else 2e-2
-    for rank, e1, e2 in res:
+    for rank, e1, e2, same in res:
         assert isinstance(e1, float), e1
         assert e1 <= tol and e2 <= tol, (rank, e1, e2)
+        assert same, f"rank {rank}: two identical steps differ"
+
