@@ -30,6 +30,8 @@ ROUTER_PHI_QUANTISED = 0
 ROUTER_SOFTMAX_TOPK = 1
 PREC_FP32 = 0
 PREC_BF16 = 1
+# fp32-faithful through three bf16 MMAs on bf16 hi / lo operand planes.
+PREC_FP32_BF16X3 = 2
 # MoeConfig.ep_transport (expert parallelism): fused NVLink peer stores, or NCCL send/recv.
 EP_TRANSPORT_P2P = 0
 EP_TRANSPORT_NCCL = 1
@@ -49,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "moe_selftest_wait_timeout", "moe_set_post_norm", "moe_block_forward_device",
     "moe_block_forward_host", "moe_layer_norm_device",
     "moe_ep_plan", "moe_ep_unique_id", "moe_ep_create", "moe_ep_create_from_device", "moe_ep_forward_device",
+    "moe_ep_check",
     "moe_set_post_rms_norm", "moe_decoder_config_init", "moe_decoder_create",
     "moe_decoder_create_from_device", "moe_decoder_destroy", "moe_decoder_device_bytes",
     "moe_decoder_prefill", "moe_decoder_decode_step", "moe_decoder_generate",
@@ -71,7 +74,8 @@ class MoeConfig(ctypes.Structure):
                 ("router_quantum", ctypes.c_float), ("router_tie_eps", ctypes.c_float),
                 ("decode_max_tokens", ctypes.c_int32), ("device", ctypes.c_int32),
                 ("max_tokens", ctypes.c_int32), ("gemm_variant", ctypes.c_int32),
-                ("ep_transport", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+                ("ep_transport", ctypes.c_int32), ("ep_wait_ms", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 2)]
 
 
 _f32p = ctypes.POINTER(ctypes.c_float)
@@ -155,6 +159,7 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
                                 ctypes.c_int, ctypes.c_int, vp, ctypes.POINTER(vp)]
     L.moe_ep_create_from_device.argtypes = L.moe_ep_create.argtypes
     L.moe_ep_forward_device.argtypes = [vp, vp, vp, ctypes.c_int32, vp]
+    L.moe_ep_check.argtypes = [vp]
     L.moe_dispatch_noalloc.argtypes = [vp, vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        vp, vp, ctypes.c_int32, vp, vp, vp]
     L.moe_set_post_rms_norm.argtypes = [vp, vp, ctypes.c_float]
@@ -288,31 +293,13 @@ def synthetic_post_norm(seed: int, d: int):
     return w, b
 
 
-def write_model_bin(path, layers: Sequence[LayerWeights]) -> None:
-    """Write layers in the ModelLoader format (src/model_loader.cu:14-30):
+def write_tensors(path, entries) -> None:
+    """Named fp32 tensors in the ModelLoader format (src/model_loader.cu:14-30):
     u32 count; per entry u32 name_len, name, u32 ndim, u32 dims[ndim],
-    u64 offset, u64 bytes; then the fp32 payloads."""
-    entries = []
-    for li, L in enumerate(layers):
-        if L.norm_weight is not None:
-            pn = f"model.layers.{li}.post_attention_layernorm"
-            entries.append((f"{pn}.weight", L.norm_weight))
-            entries.append((f"{pn}.bias", L.norm_bias))
-        base = f"model.layers.{li}.block_sparse_moe"
-        entries.append((f"{base}.gate.weight", L.wg))
-        if L.router_bias is not None:
-            entries.append((f"{base}.gate.bias", L.router_bias))
-        for e in range(L.E):
-            entries.append((f"{base}.experts.{e}.w1.weight", L.w1[e]))
-            entries.append((f"{base}.experts.{e}.w2.weight", L.w2[e]))
-            entries.append((f"{base}.experts.{e}.w3.weight", L.w3[e]))
-    header = bytearray(struct.pack("<I", len(entries)))
-    # First pass: header size, so payload offsets are known.
-    metas = []
-    for name, arr in entries:
-        nb = name.encode()
-        metas.append((nb, arr.shape, arr.nbytes))
+    u64 offset, u64 bytes; then the payloads.  entries: (name, array) pairs."""
+    metas = [(n.encode(), np.shape(a), np.asarray(a, np.float32).nbytes) for n, a in entries]
     hsize = 4 + sum(4 + len(nb) + 4 + 4 * len(sh) + 16 for nb, sh, _ in metas)
+    header = bytearray(struct.pack("<I", len(entries)))
     off = hsize
     for (nb, sh, nbytes) in metas:
         header += struct.pack("<I", len(nb)) + nb + struct.pack("<I", len(sh))
@@ -324,6 +311,33 @@ def write_model_bin(path, layers: Sequence[LayerWeights]) -> None:
         f.write(header)
         for _, arr in entries:
             f.write(np.ascontiguousarray(arr, np.float32).tobytes())
+
+
+def layer_entries(L: LayerWeights, li: int = 0):
+    """The (name, array) entries of one MoE layer (src/layer.cu:73-77) and
+    its post_attention_layernorm when present."""
+    entries = []
+    if L.norm_weight is not None:
+        pn = f"model.layers.{li}.post_attention_layernorm"
+        entries.append((f"{pn}.weight", L.norm_weight))
+        entries.append((f"{pn}.bias", L.norm_bias))
+    base = f"model.layers.{li}.block_sparse_moe"
+    entries.append((f"{base}.gate.weight", L.wg))
+    if L.router_bias is not None:
+        entries.append((f"{base}.gate.bias", L.router_bias))
+    for e in range(L.E):
+        entries.append((f"{base}.experts.{e}.w1.weight", L.w1[e]))
+        entries.append((f"{base}.experts.{e}.w2.weight", L.w2[e]))
+        entries.append((f"{base}.experts.{e}.w3.weight", L.w3[e]))
+    return entries
+
+
+def write_model_bin(path, layers: Sequence[LayerWeights]) -> None:
+    """Write MoE layers in the ModelLoader format (write_tensors)."""
+    entries = []
+    for li, L in enumerate(layers):
+        entries += layer_entries(L, li)
+    write_tensors(path, entries)
 
 
 # ------------------------------------------------------------------ layer
@@ -431,6 +445,11 @@ class MoeLayer:
         self.cfg = MoeConfig()
         _check(L.moe_get_config(h, ctypes.byref(self.cfg)))
         return self
+
+    def ep_check(self):
+        """moe_ep_check: wait for the last expert-parallel forward and raise
+        MoeError (MOE_ERR_TIMEOUT) if a peer wait of this group ran out."""
+        _check(load_library().moe_ep_check(self._h))
 
     def ep_forward_device(self, x_ptr: int, y_ptr: int, T: int, stream: int = 0):
         _check(load_library().moe_ep_forward_device(self._h, ctypes.c_void_p(x_ptr),

@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <array>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -107,8 +108,8 @@ int ensure_workspace(Layer& L, int T) {
     const int nblk = (capT + kRouteTokens - 1) / kRouteTokens;
     const int cap_mtiles = (int)((size_t)capT * k / kTileM) + L.E + 1;
     const size_t cap_rows = (size_t)cap_mtiles * kTileM;
-    const size_t eb = elem_bytes(L);
-    const bool tf = three_pass(L);
+    const size_t eb = plane_bytes(L);
+    const bool two = split_planes(L);
     size_t bytes = 0;
     MOE_CUDA(dalloc(&W.logits, sizeof(float) * capT * E, &bytes));
     MOE_CUDA(dalloc(&W.idx, sizeof(int) * capT * k, &bytes));
@@ -133,11 +134,14 @@ int ensure_workspace(Layer& L, int T) {
         W.part_rows = std::max({(size_t)capT * k, (size_t)kSplitMaxRows * gemm_splits, dec_rows});
         MOE_CUDA(dalloc(&W.part, sizeof(float) * W.part_rows * L.d, &bytes));
     }
-    MOE_CUDA(dalloc(&W.a_hi, eb * cap_rows * L.d, &bytes));
+    // A holds the dispatched rows in the GEMM operand format or, for the
+    // decode kernels, as fp32 rows in the fp32-faithful precisions (at the
+    // same padded row positions).
+    MOE_CUDA(dalloc(&W.a_hi, (fp32_faithful(L) ? 4 : eb) * cap_rows * L.d, &bytes));
     MOE_CUDA(dalloc(&W.h_hi, eb * cap_rows * L.ffp, &bytes));
-    if (tf) {
-        MOE_CUDA(dalloc(&W.a_lo, 4 * cap_rows * L.d, &bytes));
-        MOE_CUDA(dalloc(&W.h_lo, 4 * cap_rows * L.ffp, &bytes));
+    if (two) {
+        MOE_CUDA(dalloc(&W.a_lo, eb * cap_rows * L.d, &bytes));
+        MOE_CUDA(dalloc(&W.h_lo, eb * cap_rows * L.ffp, &bytes));
     }
     MOE_CUDA(dalloc(&W.h_dec, sizeof(float) * (size_t)decode_max_supported_tokens() * k * L.ffp,
                     &bytes));
@@ -152,15 +156,15 @@ int ensure_workspace(Layer& L, int T) {
     W.cap_rows = (int)cap_rows;
     W.cap_mtiles = cap_mtiles;
     W.bytes = bytes;
-    const bool bf = !tf;
-    const uint32_t box_k = tf ? 32 : 64;
+    const bool bf = planes_bf16(L);
+    const uint32_t box_k = kblock_elems(L);
     std::string err;
     if (!make_tmap_2d(&W.tm_a_hi, W.a_hi, bf, L.d, cap_rows, box_k, kTileM, &err) ||
         !make_tmap_2d(&W.tm_h_hi, W.h_hi, bf, L.ffp, cap_rows, box_k, kTileM, &err))
         return fail(MOE_ERR_CUDA, err);
-    if (tf) {
-        if (!make_tmap_2d(&W.tm_a_lo, W.a_lo, false, L.d, cap_rows, box_k, kTileM, &err) ||
-            !make_tmap_2d(&W.tm_h_lo, W.h_lo, false, L.ffp, cap_rows, box_k, kTileM, &err))
+    if (two) {
+        if (!make_tmap_2d(&W.tm_a_lo, W.a_lo, bf, L.d, cap_rows, box_k, kTileM, &err) ||
+            !make_tmap_2d(&W.tm_h_lo, W.h_lo, bf, L.ffp, cap_rows, box_k, kTileM, &err))
             return fail(MOE_ERR_CUDA, err);
     } else {
         W.tm_a_lo = W.tm_a_hi;
@@ -207,7 +211,8 @@ int validate_config(const MoeConfig& c) {
         return fail(MOE_ERR_INVALID, "the PHI_QUANTISED router selects exactly 2 experts");
     if (c.router_policy == MOE_ROUTER_PHI_QUANTISED && !(c.router_quantum > 0.0f))
         return fail(MOE_ERR_INVALID, "router_quantum must be positive");
-    if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16)
+    if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16 &&
+        c.precision != MOE_PREC_FP32_BF16X3)
         return fail(MOE_ERR_INVALID, "unknown precision");
     if (c.decode_max_tokens < -1 || c.decode_max_tokens > decode_max_supported_tokens())
         return fail(MOE_ERR_INVALID, "decode_max_tokens must be in -1..64");
@@ -216,6 +221,7 @@ int validate_config(const MoeConfig& c) {
         return fail(MOE_ERR_INVALID, "unknown gemm_variant");
     if (c.ep_transport != MOE_EP_TRANSPORT_P2P && c.ep_transport != MOE_EP_TRANSPORT_NCCL)
         return fail(MOE_ERR_INVALID, "unknown ep_transport");
+    if (c.ep_wait_ms < 0) return fail(MOE_ERR_INVALID, "ep_wait_ms < 0");
     return MOE_OK;
 }
 
@@ -421,16 +427,17 @@ int create_impl(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs,
 // Build a handle that routes over cfg->num_experts experts and holds experts
 // [e_first, e_first + e_count) (all of them unless expert-parallel).
 int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, int e_first,
-                 int e_count, MoeHandle** out) {
+                 int e_count, MoeHandle** out, ExpertReader* reader) {
     if (!cfg || !w || !out) return fail(MOE_ERR_INVALID, "null argument");
     *out = nullptr;
     int rc = validate_config(*cfg);
     if (rc) return rc;
-    if (!w->router_weight || !w->w1 || !w->w2 || !w->w3)
+    if (reader && device_ptrs) return fail(MOE_ERR_INVALID, "an expert reader supplies host weights");
+    if (!w->router_weight || (!reader && (!w->w1 || !w->w2 || !w->w3)))
         return fail(MOE_ERR_INVALID, "missing weight pointers");
     if (e_first < 0 || e_count < 1 || e_first + e_count > cfg->num_experts)
         return fail(MOE_ERR_INVALID, "bad expert slice");
-    for (int e = e_first; e < e_first + e_count; ++e)
+    for (int e = e_first; !reader && e < e_first + e_count; ++e)
         if (!w->w1[e] || !w->w2[e] || !w->w3[e]) return fail(MOE_ERR_INVALID, "null expert weight");
     int ndev = 0;
     MOE_CUDA(cudaGetDeviceCount(&ndev));
@@ -464,8 +471,8 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
     cudaStream_t s = h->own_stream;
 
     const size_t d = L.d, E = L.E, ffp = L.ffp, ff = L.ff;
-    const bool tf = three_pass(L);
-    const size_t eb = elem_bytes(L);
+    const bool two = split_planes(L);
+    const size_t eb = plane_bytes(L);
     size_t& wb = L.weight_bytes;
     auto cleanup_and_fail = [&](int code) {
         moe_destroy(h.release());
@@ -486,9 +493,11 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
     }
     MOE_CUDA_C(dalloc(&L.w13_hi, eb * E * 2 * ffp * d, &wb));
     MOE_CUDA_C(dalloc(&L.w2_hi, eb * E * d * ffp, &wb));
-    if (tf) {
-        MOE_CUDA_C(dalloc(&L.w13_lo, 4 * E * 2 * ffp * d, &wb));
-        MOE_CUDA_C(dalloc(&L.w2_lo, 4 * E * d * ffp, &wb));
+    if (two) {
+        MOE_CUDA_C(dalloc(&L.w13_lo, eb * E * 2 * ffp * d, &wb));
+        MOE_CUDA_C(dalloc(&L.w2_lo, eb * E * d * ffp, &wb));
+    }
+    if (fp32_faithful(L)) {
         MOE_CUDA_C(dalloc(&L.w13_f32, 4 * E * 2 * ffp * d, &wb));
         MOE_CUDA_C(dalloc(&L.w2_f32, 4 * E * d * ffp, &wb));
     }
@@ -501,31 +510,62 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
         }
         MOE_CUDA_C(cudaStreamSynchronize(s));
     } else {
-        float *st1 = nullptr, *st3 = nullptr, *st2 = nullptr;
-        MOE_CUDA_C(dalloc(&st1, sizeof(float) * ff * d, nullptr));
-        MOE_CUDA_C(dalloc(&st3, sizeof(float) * ff * d, nullptr));
-        MOE_CUDA_C(dalloc(&st2, sizeof(float) * ff * d, nullptr));
+        // Device staging for one expert's three fp32 tensors; with a reader,
+        // two pinned host buffers in turn: tensor i is read into buffer
+        // i % 2 while the copy of tensor i - 1 runs (event-gated reuse).
+        struct Staging {
+            float* dev[3] = {};
+            float* pin[2] = {};
+            cudaEvent_t ev[2] = {};
+            ~Staging() {
+                for (float* p : dev) if (p) cudaFree(p);
+                for (float* p : pin) if (p) cudaFreeHost(p);
+                for (cudaEvent_t e : ev) if (e) cudaEventDestroy(e);
+            }
+        } st;
+        const size_t n = ff * d;
+        for (float*& p : st.dev) MOE_CUDA_C(dalloc(&p, sizeof(float) * n, nullptr));
+        if (reader)
+            for (int i = 0; i < 2; ++i) {
+                MOE_CUDA_C(cudaHostAlloc(reinterpret_cast<void**>(&st.pin[i]), sizeof(float) * n, 0));
+                MOE_CUDA_C(cudaEventCreateWithFlags(&st.ev[i], cudaEventDisableTiming));
+            }
+        long long issued = 0;
         for (int e = 0; e < L.E; ++e) {
-            MOE_CUDA_C(cudaMemcpyAsync(st1, w->w1[e_first + e], sizeof(float) * ff * d, kind, s));
-            MOE_CUDA_C(cudaMemcpyAsync(st3, w->w3[e_first + e], sizeof(float) * ff * d, kind, s));
-            MOE_CUDA_C(cudaMemcpyAsync(st2, w->w2[e_first + e], sizeof(float) * ff * d, kind, s));
-            MOE_CUDA_C(convert_gateup(L, e, st1, st3, s));
-            MOE_CUDA_C(convert_down(L, e, st2, s));
-            MOE_CUDA_C(cudaStreamSynchronize(s));
+            const float* host[3] = {reader ? nullptr : w->w1[e_first + e],
+                                    reader ? nullptr : w->w3[e_first + e],
+                                    reader ? nullptr : w->w2[e_first + e]};
+            for (int which = 0; which < 3; ++which) {
+                const float* src = host[which];
+                if (reader) {
+                    const int b = static_cast<int>(issued & 1);
+                    if (issued >= 2) MOE_CUDA_C(cudaEventSynchronize(st.ev[b]));
+                    const int rrc = reader->read(e_first + e, which, st.pin[b], n);
+                    if (rrc) {
+                        cudaStreamSynchronize(s);
+                        return cleanup_and_fail(rrc);
+                    }
+                    src = st.pin[b];
+                }
+                MOE_CUDA_C(cudaMemcpyAsync(st.dev[which], src, sizeof(float) * n, kind, s));
+                if (reader) MOE_CUDA_C(cudaEventRecord(st.ev[issued & 1], s));
+                ++issued;
+            }
+            MOE_CUDA_C(convert_gateup(L, e, st.dev[0], st.dev[1], s));
+            MOE_CUDA_C(convert_down(L, e, st.dev[2], s));
+            if (!reader) MOE_CUDA_C(cudaStreamSynchronize(s));
         }
-        cudaFree(st1);
-        cudaFree(st3);
-        cudaFree(st2);
+        MOE_CUDA_C(cudaStreamSynchronize(s));
     }
-    const uint32_t box_k = tf ? 32 : 64;
+    const uint32_t box_k = kblock_elems(L);
     std::string err;
-    const bool bf = !tf;
+    const bool bf = planes_bf16(L);
     if (!make_tmap_2d(&L.tm_w13_hi, L.w13_hi, bf, d, E * 2 * ffp, box_k, kTileN, &err) ||
         !make_tmap_2d(&L.tm_w2_hi, L.w2_hi, bf, ffp, E * d, box_k, kTileN, &err))
         return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
-    if (tf) {
-        if (!make_tmap_2d(&L.tm_w13_lo, L.w13_lo, false, d, E * 2 * ffp, box_k, kTileN, &err) ||
-            !make_tmap_2d(&L.tm_w2_lo, L.w2_lo, false, ffp, E * d, box_k, kTileN, &err))
+    if (two) {
+        if (!make_tmap_2d(&L.tm_w13_lo, L.w13_lo, bf, d, E * 2 * ffp, box_k, kTileN, &err) ||
+            !make_tmap_2d(&L.tm_w2_lo, L.w2_lo, bf, ffp, E * d, box_k, kTileN, &err))
             return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
     } else {
         L.tm_w13_lo = L.tm_w13_hi;
@@ -534,9 +574,9 @@ int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs
     if (!make_tmap_2d(&L.tm_w13_hi2, L.w13_hi, bf, d, E * 2 * ffp, box_k, kTileN / 2, &err) ||
         !make_tmap_2d(&L.tm_w2_hi2, L.w2_hi, bf, ffp, E * d, box_k, kTileN / 2, &err))
         return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
-    if (tf) {
-        if (!make_tmap_2d(&L.tm_w13_lo2, L.w13_lo, false, d, E * 2 * ffp, box_k, kTileN / 2, &err) ||
-            !make_tmap_2d(&L.tm_w2_lo2, L.w2_lo, false, ffp, E * d, box_k, kTileN / 2, &err))
+    if (two) {
+        if (!make_tmap_2d(&L.tm_w13_lo2, L.w13_lo, bf, d, E * 2 * ffp, box_k, kTileN / 2, &err) ||
+            !make_tmap_2d(&L.tm_w2_lo2, L.w2_lo, bf, ffp, E * d, box_k, kTileN / 2, &err))
             return cleanup_and_fail(fail(MOE_ERR_CUDA, err));
     } else {
         L.tm_w13_lo2 = L.tm_w13_hi2;
@@ -571,27 +611,44 @@ int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int lay
     if (cfg.d_model == 0) cfg.d_model = (int)gshape[1];
     if ((int)gshape[0] != cfg.num_experts || (int)gshape[1] != cfg.d_model)
         return fail(MOE_ERR_INVALID, "router weight shape does not match the config");
-    std::vector<std::vector<float>> w1(cfg.num_experts), w2(cfg.num_experts), w3(cfg.num_experts);
+    // Expert tensors: shapes checked from the index now, data streamed from
+    // the file one tensor at a time during the upload (ExpertReader).
+    std::vector<std::array<const BinEntry*, 3>> ent(cfg.num_experts);
     for (int e = 0; e < cfg.num_experts; ++e) {
         const std::string pre = base + ".experts." + std::to_string(e);
-        std::vector<uint64_t> s1, s2, s3;
-        if ((rc = load_tensor(path, index, pre + ".w1.weight", &w1[e], &s1)) ||
-            (rc = load_tensor(path, index, pre + ".w2.weight", &w2[e], &s2)) ||
-            (rc = load_tensor(path, index, pre + ".w3.weight", &w3[e], &s3)))
-            return rc;
+        const char* names[3] = {".w1.weight", ".w3.weight", ".w2.weight"};
+        for (int which = 0; which < 3; ++which) {
+            auto it = index.find(pre + names[which]);
+            if (it == index.end()) return fail(MOE_ERR_IO, "missing tensor: " + pre + names[which]);
+            ent[e][which] = &it->second;
+        }
+        const auto& s1 = ent[e][0]->shape;
+        const auto& s3 = ent[e][1]->shape;
+        const auto& s2 = ent[e][2]->shape;
         if (s1.size() != 2 || s2.size() != 2 || s3.size() != 2)
             return fail(MOE_ERR_IO, "expert weight is not 2-D");
         if (cfg.d_ff == 0) cfg.d_ff = (int)s1[0];
         if ((int)s1[0] != cfg.d_ff || (int)s1[1] != cfg.d_model || s3 != s1 ||
             (int)s2[0] != cfg.d_model || (int)s2[1] != cfg.d_ff)
             return fail(MOE_ERR_INVALID, "expert weight shapes do not match the config");
+        for (int which = 0; which < 3; ++which)
+            if (ent[e][which]->bytes != (uint64_t)cfg.d_ff * cfg.d_model * sizeof(float))
+                return fail(MOE_ERR_IO, "tensor is not float32: " + pre + names[which]);
     }
-    std::vector<const float*> p1(cfg.num_experts), p2(cfg.num_experts), p3(cfg.num_experts);
-    for (int e = 0; e < cfg.num_experts; ++e) {
-        p1[e] = w1[e].data();
-        p2[e] = w2[e].data();
-        p3[e] = w3[e].data();
-    }
+    struct FileReader : ExpertReader {
+        std::ifstream f;
+        const std::vector<std::array<const BinEntry*, 3>>* ent = nullptr;
+        int read(int e, int which, float* dst, size_t n) override {
+            const BinEntry* be = (*ent)[e][which];
+            f.seekg(static_cast<std::streamoff>(be->offset));
+            if (!f.read(reinterpret_cast<char*>(dst), static_cast<std::streamsize>(n * 4)))
+                return fail(MOE_ERR_IO, "truncated expert tensor of expert " + std::to_string(e));
+            return MOE_OK;
+        }
+    } reader;
+    reader.f.open(path, std::ios::binary);
+    if (!reader.f) return fail(MOE_ERR_IO, std::string("cannot reopen model: ") + path);
+    reader.ent = &ent;
     std::vector<float> bias;
     MoeWeightsHost wh{};
     wh.router_weight = gate.data();
@@ -601,9 +658,6 @@ int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int lay
         if ((int)bias.size() != cfg.num_experts) return fail(MOE_ERR_IO, "router bias shape");
         wh.router_bias = bias.data();
     }
-    wh.w1 = p1.data();
-    wh.w2 = p2.data();
-    wh.w3 = p3.data();
     // The decoder layer's post-attention LayerNorm, when the file has it.
     const std::string pn = "model.layers." + std::to_string(layer_idx) + ".post_attention_layernorm";
     std::vector<float> nw, nb;
@@ -614,7 +668,7 @@ int moe_create_from_model_bin(const MoeConfig* cfg_in, const char* path, int lay
         if ((int)nw.size() != cfg.d_model || (int)nb.size() != cfg.d_model)
             return fail(MOE_ERR_IO, "post_attention_layernorm shape");
     }
-    rc = moe_create(&cfg, &wh, out);
+    rc = create_slice(&cfg, &wh, false, 0, cfg.num_experts, out, &reader);
     if (rc || nw.empty()) return rc;
     rc = moe_set_post_norm(*out, nw.data(), nb.data(), 1.0e-5f);
     if (rc) {

@@ -1007,10 +1007,10 @@ int make_dense(MoeDecoder& m, Dense& D, const float* const* parts, const int* pa
     L.sm_count = m.sm_count;
     L.gemm_variant = MOE_GEMM_AUTO;
     L.profile = false;
-    const bool tf = three_pass(L);
-    const size_t eb = elem_bytes(L);
+    const bool tf = split_planes(L);   // 3xTF32 (the decoder's precisions: FP32, BF16)
+    const size_t eb = plane_bytes(L);
     DEC_CUDA(dec_alloc(m, &L.w2_hi, eb * N * K));
-    if (tf) DEC_CUDA(dec_alloc(m, &L.w2_lo, (size_t)4 * N * K));
+    if (tf) DEC_CUDA(dec_alloc(m, &L.w2_lo, eb * N * K));
     float* stage = nullptr;
     DEC_CUDA(cudaMalloc(&stage, sizeof(float) * (size_t)N * K));
     size_t off = 0;
@@ -1274,6 +1274,8 @@ int validate(const MoeDecoderConfig& c) {
     if (c.vocab < 32 || c.vocab % 32 != 0) return bad(MOE_ERR_UNSUPPORTED, "vocab must be a positive multiple of 32");
     if (c.max_batch < 1 || c.max_seq < 1) return bad(MOE_ERR_INVALID, "max_batch and max_seq must be >= 1");
     if ((long long)c.max_batch * c.max_seq > (1 << 22)) return bad(MOE_ERR_UNSUPPORTED, "max_batch * max_seq too large");
+    if (c.precision == MOE_PREC_FP32_BF16X3)
+        return bad(MOE_ERR_UNSUPPORTED, "the decoder runs in FP32 (3xTF32) or BF16 precision");
     if (c.precision != MOE_PREC_FP32 && c.precision != MOE_PREC_BF16) return bad(MOE_ERR_INVALID, "unknown precision");
     if (!(c.rms_eps >= 0.0f) || !(c.rope_base > 0.0f)) return bad(MOE_ERR_INVALID, "rms_eps >= 0 and rope_base > 0 required");
     return MOE_OK;

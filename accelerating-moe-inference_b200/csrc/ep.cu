@@ -169,6 +169,16 @@ struct EpState {
     // eperm[e] = (e % G) * E_local + e / G is expert e's dispatch position
     // (rank-major, so each rank's experts are one contiguous run).
     int* eperm = nullptr;
+    // Failure of the fused transport: poison (device word) is set by a wait
+    // that ran out and stops this rank's peer stores and flags; each forward
+    // ends with a copy of the device error flags into h_err (pinned) and
+    // err_ev; failed (host) is set once a completed copy shows a flag.
+    unsigned long long wait_ns = 0;
+    int* poison = nullptr;
+    int* h_err = nullptr;
+    cudaEvent_t err_ev = nullptr;
+    bool err_recorded = false;
+    bool failed = false;
 };
 
 namespace {
@@ -192,6 +202,13 @@ void ep_free_buffers(EpState& S) {
     S.p2p_recv = S.p2p_ret = nullptr;
     S.p2p_cnt = nullptr;
     S.p2p_flag = nullptr;
+    if (S.poison) cudaFree(S.poison);
+    if (S.h_err) cudaFreeHost(S.h_err);
+    if (S.err_ev) cudaEventDestroy(S.err_ev);
+    S.poison = nullptr;
+    S.h_err = nullptr;
+    S.err_ev = nullptr;
+    S.err_recorded = false;
     S.d_peer_recv = S.d_peer_ret = nullptr;
     S.d_peer_cnt = nullptr;
     S.d_peer_flag = nullptr;
@@ -211,7 +228,7 @@ int ep_ensure(Layer& L, int T) {
     const int capT = T > 64 ? T : 64;
     const size_t rows_local = (size_t)capT * L.k;
     const size_t rows_recv = rows_local * S.world;
-    S.row_bytes = (size_t)L.d * elem_bytes(L);
+    S.row_bytes = (size_t)L.d * wire_bytes(L);
     cudaError_t e = cudaSuccess;
     auto A = [&](void** p, size_t b) {
         if (e == cudaSuccess) e = cudaMalloc(p, b ? b : 256);
@@ -247,7 +264,48 @@ int ep_ensure(Layer& L, int T) {
 // the arrival row.  rows is a bound: rows past the received total exit.
 // Received rows and counts were written by other GPUs: they are read through
 // L2 only.
-template <bool kTf32x3>
+// One received row (fp32 on the wire for kFmt kActTf32x2 / kActBf16x2, bf16
+// for kActBf16) into each of the n GEMM rows prow[0..n) of the operand
+// planes, one warp, columns lane-strided.  Rows written by other GPUs are
+// read through L2 only.
+template <int kFmt>
+__device__ __forceinline__ void convert_row(const void* src_row, int d, const int* prow, int n,
+                                            void* a_hi, void* a_lo, int lane) {
+    if constexpr (kFmt == kActBf16) {
+        const uint4* src = static_cast<const uint4*>(src_row);
+        for (int v = lane; v < d / 8; v += 32) {
+            const uint4 u = __ldcg(src + v);
+            for (int j = 0; j < n; ++j)
+                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow[j] * d)[v] = u;
+        }
+    } else {
+        const float4* src = static_cast<const float4*>(src_row);
+        for (int v = lane; v < d / 4; v += 32) {
+            const float4 f = __ldcg(src + v);
+            if constexpr (kFmt == kActTf32x2) {
+                float4 h, l;
+                h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
+                h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
+                h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
+                h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
+                for (int j = 0; j < n; ++j) {
+                    reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow[j] * d)[v] = h;
+                    reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow[j] * d)[v] = l;
+                }
+            } else {
+                uint2 hp, lp;
+                split_bf16x2(f.x, f.y, hp.x, lp.x);
+                split_bf16x2(f.z, f.w, hp.y, lp.y);
+                for (int j = 0; j < n; ++j) {
+                    reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow[j] * d)[v] = hp;
+                    reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a_lo) + (size_t)prow[j] * d)[v] = lp;
+                }
+            }
+        }
+    }
+}
+
+template <int kFmt>
 __global__ void __launch_bounds__(256)
 ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El, int cap_src,
                   const int* __restrict__ cnt, const int* __restrict__ base,
@@ -286,25 +344,9 @@ ep_arrange_kernel(const void* __restrict__ recv, int rows, int d, int G, int El,
         row_token[prow] = (int)src_row;
         row_weight[prow] = 1.0f;
     }
-    if constexpr (kTf32x3) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + src_row * d);
-        float4* hi = reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)prow * d);
-        float4* lo = reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)prow * d);
-        for (int v = lane; v < d / 4; v += 32) {
-            const float4 f = __ldcg(src + v);
-            float4 h, l;
-            h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
-            h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
-            h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
-            h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
-            hi[v] = h;
-            lo[v] = l;
-        }
-    } else {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + src_row * d);
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)prow * d);
-        for (int v = lane; v < d / 8; v += 32) dst[v] = __ldcg(src + v);
-    }
+    const size_t wb = kFmt == kActBf16 ? 2 : 4;
+    convert_row<kFmt>(static_cast<const char*>(recv) + src_row * d * wb, d, &prow, 1, a_hi, a_lo,
+                      lane);
 }
 
 // y[t] = token t's k returned rows (fp32 in FP32 precision, bf16 in BF16),
@@ -364,7 +406,7 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     if (rc) return rc;
     Workspace& W = L.ws;
     const int G = S.world, El = S.e_local, Eg = L.E_route;
-    const ncclDataType_t dt = three_pass(L) ? ncclFloat32 : ncclBfloat16;
+    const ncclDataType_t dt = fp32_faithful(L) ? ncclFloat32 : ncclBfloat16;
     const size_t d = L.d;
     auto cuda_err = [](cudaError_t e, const char* what) {
         return report_error(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -433,14 +475,15 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
             return cuda_err(ce, "arrival scan");
         const size_t smem = sizeof(int) * ((G + 1) + (size_t)G * (El + 1));
         const int grid = (R + 7) / 8;
-        if (three_pass(L))
-            ep_arrange_kernel<true><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, 0, S.cnt_recv,
-                                                            S.cnt_scan, W.eoff, W.row_token,
-                                                            W.row_weight, W.a_hi, W.a_lo);
-        else
-            ep_arrange_kernel<false><<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, 0, S.cnt_recv,
-                                                             S.cnt_scan, W.eoff, W.row_token,
-                                                             W.row_weight, W.a_hi, W.a_lo);
+        auto run = [&](auto kern) {
+            kern<<<grid, 256, smem, s>>>(S.recv_rows, R, L.d, G, El, 0, S.cnt_recv, S.cnt_scan,
+                                         W.eoff, W.row_token, W.row_weight, W.a_hi, W.a_lo);
+        };
+        switch (act_format(L, false)) {
+            case kActTf32x2: run(ep_arrange_kernel<kActTf32x2>); break;
+            case kActBf16x2: run(ep_arrange_kernel<kActBf16x2>); break;
+            default: run(ep_arrange_kernel<kActBf16>); break;
+        }
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
         prof_mark(L, 3, s);
         if ((ce = launch_expert_gemm_rows(L, R, nullptr, s, 0)) != cudaSuccess)
@@ -464,7 +507,7 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 8: weighted combine into y.
     prof_mark(L, 7, s);
     if (T > 0) {
-        if (three_pass(L))
+        if (fp32_faithful(L))
             ep_combine_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(S.ret_recv, T, L.k, L.d, G, El,
                                                                 W.idx, W.wts, S.send_slot, y);
         else
@@ -477,7 +520,7 @@ int ep_forward_nccl(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------ fused transport
-constexpr unsigned long long kPeerWaitNs = 5000000000ull;   // 5 s
+constexpr unsigned long long kPeerWaitNs = 5000000000ull;   // 5 s: the default peer-wait bound
 
 // Thread j: for rank j, copy this rank's counts for j's experts into j's
 // count words (dispatch only), then -- after a system-scope fence that orders
@@ -485,9 +528,12 @@ constexpr unsigned long long kPeerWaitNs = 5000000000ull;   // 5 s
 // included) -- raise flag [which][this rank] in j's flag words to `epoch`.
 __global__ void ep_signal_kernel(int* const* peer_cnt, const int* __restrict__ counts,
                                  unsigned* const* peer_flag, int G, int El, int rank, int which,
-                                 unsigned epoch, const int* __restrict__ rows = nullptr) {
+                                 unsigned epoch, const int* poison,
+                                 const int* __restrict__ rows = nullptr) {
     const int j = threadIdx.x;
-    if (j >= G) return;
+    // A failed rank raises no flags: its peers' waits run out instead of
+    // proceeding on a step it did not complete.
+    if (j >= G || *reinterpret_cast<const volatile int*>(poison)) return;
     if (peer_cnt)
         for (int e = 0; e < El; ++e) peer_cnt[j][rank * El + e] = counts[j * El + e];
     if (peer_cnt && rows) peer_cnt[j][G * El + rank] = rows[j];   // rows this rank sends j
@@ -501,17 +547,19 @@ __global__ void ep_signal_kernel(int* const* peer_cnt, const int* __restrict__ c
 // capacity -- or zeros after a timeout, so a failed step moves no rows.
 __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned epoch,
                                const int* cnt_src, int* __restrict__ cnt_a, int* __restrict__ cnt_b,
-                               int n, int cap, int* err, int* __restrict__ rows_out = nullptr) {
+                               int n, int cap, int* err, int* poison, unsigned long long budget_ns,
+                               int* __restrict__ rows_out = nullptr) {
     __shared__ int timed_out;
-    if (threadIdx.x == 0) timed_out = 0;
+    // A rank that failed in an earlier step waits for nothing.
+    if (threadIdx.x == 0) timed_out = *reinterpret_cast<volatile int*>(poison);
     __syncthreads();
     const int sidx = threadIdx.x;
-    if (sidx < G) {
+    if (sidx < G && !timed_out) {
         const unsigned* f = flag + which * G + sidx;
         if (ld_acquire_sys(f) < epoch) {
             const unsigned long long t0 = global_timer_ns();
             while (ld_acquire_sys(f) < epoch) {
-                if (global_timer_ns() - t0 > kPeerWaitNs) {
+                if (global_timer_ns() - t0 > budget_ns) {
                     atomicOr(err, kDevErrTimeoutPeer);
                     timed_out = 1;
                     break;
@@ -521,6 +569,7 @@ __global__ void ep_wait_kernel(const unsigned* flag, int G, int which, unsigned 
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0 && timed_out) *reinterpret_cast<volatile int*>(poison) = 1;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int c = timed_out ? 0 : min(max(__ldcg(cnt_src + i), 0), cap);
         cnt_a[i] = c;
@@ -569,7 +618,9 @@ ep_dedup_push_kernel(const float* __restrict__ x, int T, int d, int k, int El, i
                      const int* __restrict__ idx, const float* __restrict__ wts,
                      const int* __restrict__ ebase, const int* __restrict__ gbase,
                      void* const* __restrict__ peer_recv, int2* const* __restrict__ peer_meta,
-                     int cap, int rank, int* __restrict__ slot_dd) {
+                     int cap, int rank, int* __restrict__ slot_dd, const int* poison) {
+    // A failed rank stores nothing into other GPUs' buffers.
+    if (*reinterpret_cast<const volatile int*>(poison)) return;
     __shared__ unsigned s_emask[kMaxExperts];
     __shared__ unsigned s_gmask[32];
     __shared__ int s_list[kRouteTokens * 32];   // (token << 16) | (g << 11)... packed below
@@ -676,7 +727,7 @@ __device__ __forceinline__ void dd_selections(const int2* __restrict__ meta, siz
 // i * kmax + j for its j-th placed selection, where the down GEMM stores that
 // expert's output), and the row is converted into each of those A rows.
 // Rows were written by other GPUs: read through L2 only.
-template <bool kTf32x3>
+template <int kFmt>
 __global__ void __launch_bounds__(256)
 ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ meta,
                      const int* __restrict__ rows_recv, int cap, int d, int G, int El, int kmax,
@@ -697,28 +748,9 @@ ep_dd_arrange_kernel(const void* __restrict__ recv, const int2* __restrict__ met
         row_weight[sel.prow[lane]] = sel.w[lane];
         row_slot[sel.prow[lane]] = (int)(i * kmax) + lane;
     }
-    if constexpr (kTf32x3) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(recv) + i * d);
-        for (int v = lane; v < d / 4; v += 32) {
-            const float4 f = __ldcg(src + v);
-            float4 h, l;
-            h.x = to_tf32(f.x); l.x = to_tf32(f.x - h.x);
-            h.y = to_tf32(f.y); l.y = to_tf32(f.y - h.y);
-            h.z = to_tf32(f.z); l.z = to_tf32(f.z - h.z);
-            h.w = to_tf32(f.w); l.w = to_tf32(f.w - h.w);
-            for (int j = 0; j < n; ++j) {
-                reinterpret_cast<float4*>(static_cast<float*>(a_hi) + (size_t)sel.prow[j] * d)[v] = h;
-                reinterpret_cast<float4*>(static_cast<float*>(a_lo) + (size_t)sel.prow[j] * d)[v] = l;
-            }
-        }
-    } else {
-        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(recv) + i * d);
-        for (int v = lane; v < d / 8; v += 32) {
-            const uint4 u = __ldcg(src + v);
-            for (int j = 0; j < n; ++j)
-                reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a_hi) + (size_t)sel.prow[j] * d)[v] = u;
-        }
-    }
+    const size_t wb = kFmt == kActBf16 ? 2 : 4;
+    convert_row<kFmt>(static_cast<const char*>(recv) + i * d * wb, d, sel.prow, n, a_hi, a_lo,
+                      lane);
 }
 
 // One warp per received row i: the outputs of its experts (part row
@@ -732,10 +764,10 @@ __global__ void __launch_bounds__(256)
 ep_return_push_kernel(const float* __restrict__ part, const int2* __restrict__ meta,
                       const int* __restrict__ rows_recv, int cap, int d, int G, int El, int kmax,
                       const int* __restrict__ base, const int* __restrict__ eoff, int rank,
-                      void* const* __restrict__ peer_ret) {
+                      void* const* __restrict__ peer_ret, const int* poison) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t i = (size_t)blockIdx.x * 8 + warp;
-    if (i >= (size_t)G * cap) return;
+    if (i >= (size_t)G * cap || *reinterpret_cast<const volatile int*>(poison)) return;
     const int s = (int)(i / cap), r = (int)(i % cap);
     if (r >= rows_recv[s]) return;
     DdSelections sel;
@@ -823,7 +855,7 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     S.cap_T = capT;
     S.cap_src = capT;   // one row per (token, destination)
     S.kmax = std::min(L.k, El);
-    S.row_bytes = (size_t)L.d * elem_bytes(L);
+    S.row_bytes = (size_t)L.d * wire_bytes(L);
     const size_t rows_local = (size_t)capT * L.k;
     const size_t seg_bytes = (size_t)G * S.cap_src * S.row_bytes;
     const int nblk = (capT + kRouteTokens - 1) / kRouteTokens;
@@ -847,11 +879,15 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     A((void**)&S.dest_off, (G + 1) * sizeof(int));
     A((void**)&S.slot_dd, (size_t)capT * G * sizeof(int));
     A((void**)&S.rows_recv, G * sizeof(int));
+    A((void**)&S.poison, sizeof(int));
     A((void**)&S.d_peer_recv, G * sizeof(void*));
     A((void**)&S.d_peer_ret, G * sizeof(void*));
     A((void**)&S.d_peer_cnt, G * sizeof(int*));
     A((void**)&S.d_peer_flag, G * sizeof(unsigned*));
     A((void**)&S.d_peer_meta, G * sizeof(int2*));
+    if (e == cudaSuccess) e = cudaMemset(S.poison, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&S.h_err, sizeof(int), 0);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&S.err_ev, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMemset(S.p2p_flag, 0, 2 * G * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(S.p2p_cnt, 0, (size_t)G * (El + 1) * sizeof(int));
     if (e != cudaSuccess)
@@ -911,11 +947,32 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     return ensure_workspace(L, capT * G);
 }
 
+// MOE_ERR_TIMEOUT once the group has failed: a completed copy of the device
+// error flags (taken at the end of every fused forward) shows a flag.  With
+// wait, the last forward's copy is waited for first.
+int ep_failure(EpState& S, bool wait) {
+    if (!S.failed && S.err_recorded) {
+        const cudaError_t q = wait ? cudaEventSynchronize(S.err_ev) : cudaEventQuery(S.err_ev);
+        if (q == cudaSuccess) {
+            if (*reinterpret_cast<volatile int*>(S.h_err) != 0) S.failed = true;
+        } else if (q != cudaErrorNotReady) {
+            return report_error(MOE_ERR_CUDA, std::string("expert-parallel status: ") +
+                                                  cudaGetErrorString(q));
+        }
+    }
+    if (S.failed)
+        return report_error(MOE_ERR_TIMEOUT,
+                            "an expert-parallel peer wait timed out (a rank missed a step or "
+                            "stopped); the group is failed: destroy and recreate it on every rank");
+    return MOE_OK;
+}
+
 int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     EpState& S = *L.ep;
     if (T > S.cap_T)
         return report_error(MOE_ERR_INVALID,
                             "T exceeds the expert-parallel capacity fixed at creation (max_tokens)");
+    if (int rc = ep_failure(S, false)) return rc;
     Workspace& W = L.ws;
     const int G = S.world, El = S.e_local, Eg = L.E_route;
     const unsigned epoch = ++S.epoch;
@@ -944,16 +1001,16 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
                                       nullptr, nullptr, nullptr, nullptr, nullptr, s)) != cudaSuccess)
             return cuda_err(ce, "destination scan");
         prof_mark(L, 5, s);
-        if (three_pass(L))
+        if (fp32_faithful(L))
             ep_dedup_push_kernel<2><<<nblk, 256, 0, s>>>(x, T, L.d, L.k, El, G, S.kmax, W.idx,
                                                          W.wts, W.blockhist, S.dest_hist,
                                                          S.d_peer_recv, S.d_peer_meta, S.cap_src,
-                                                         S.rank, S.slot_dd);
+                                                         S.rank, S.slot_dd, S.poison);
         else
             ep_dedup_push_kernel<0><<<nblk, 256, 0, s>>>(x, T, L.d, L.k, El, G, S.kmax, W.idx,
                                                          W.wts, W.blockhist, S.dest_hist,
                                                          S.d_peer_recv, S.d_peer_meta, S.cap_src,
-                                                         S.rank, S.slot_dd);
+                                                         S.rank, S.slot_dd, S.poison);
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "dispatch push");
     } else {
         prof_mark(L, 5, s);
@@ -964,10 +1021,11 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
     // 3-4: counts, row counts and flags to every rank; wait for every source's.
     const int sig_threads = (G + 31) / 32 * 32;
     ep_signal_kernel<<<1, sig_threads, 0, s>>>(S.d_peer_cnt, W.counts, S.d_peer_flag, G, El,
-                                               S.rank, 0, epoch, S.dest_cnt);
+                                               S.rank, 0, epoch, S.poison, S.dest_cnt);
     ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 0, epoch, S.p2p_cnt,
                                                             S.cnt_recv, S.cnt_scan, G * El,
-                                                            S.cap_src, W.dev_err, S.rows_recv);
+                                                            S.cap_src, W.dev_err, S.poison,
+                                                            S.wait_ns, S.rows_recv);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "dispatch signal");
     prof_mark(L, 2, s);
     // Arrival scan (per-source bases inside each local expert's block) and
@@ -978,17 +1036,18 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         return cuda_err(ce, "arrival scan");
     const size_t R_bound = (size_t)G * S.cap_src;
     const int grid = (int)((R_bound + 7) / 8);
-    if (three_pass(L))
-        ep_dd_arrange_kernel<true><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
-                                                        S.cap_src, L.d, G, El, S.kmax, S.cnt_scan,
-                                                        W.eoff, W.row_token, W.row_weight,
-                                                        W.row_slot, W.a_hi, W.a_lo);
-    else
-        ep_dd_arrange_kernel<false><<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv,
-                                                         S.cap_src, L.d, G, El, S.kmax,
-                                                         S.cnt_scan, W.eoff, W.row_token,
-                                                         W.row_weight, W.row_slot, W.a_hi,
-                                                         W.a_lo);
+    {
+        auto run = [&](auto kern) {
+            kern<<<grid, 256, 0, s>>>(S.p2p_recv, S.p2p_meta, S.rows_recv, S.cap_src, L.d, G, El,
+                                      S.kmax, S.cnt_scan, W.eoff, W.row_token, W.row_weight,
+                                      W.row_slot, W.a_hi, W.a_lo);
+        };
+        switch (act_format(L, false)) {
+            case kActTf32x2: run(ep_dd_arrange_kernel<kActTf32x2>); break;
+            case kActBf16x2: run(ep_dd_arrange_kernel<kActBf16x2>); break;
+            default: run(ep_dd_arrange_kernel<kActBf16>); break;
+        }
+    }
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "arrange");
     // 5-6: the local experts; the down GEMM stores each expert's output at
     // its (received row, selection) slot, K whole.  The expected routed rows
@@ -1003,25 +1062,26 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         return cuda_err(ce, "down GEMM");
     // 7: one summed row per received row back to its source; return flags.
     prof_mark(L, 6, s);
-    if (three_pass(L))
+    if (fp32_faithful(L))
         ep_return_push_kernel<true><<<grid, 256, 0, s>>>(W.part, S.p2p_meta, S.rows_recv,
                                                          S.cap_src, L.d, G, El, S.kmax,
                                                          S.cnt_scan, W.eoff, S.rank,
-                                                         S.d_peer_ret);
+                                                         S.d_peer_ret, S.poison);
     else
         ep_return_push_kernel<false><<<grid, 256, 0, s>>>(W.part, S.p2p_meta, S.rows_recv,
                                                           S.cap_src, L.d, G, El, S.kmax,
                                                           S.cnt_scan, W.eoff, S.rank,
-                                                          S.d_peer_ret);
+                                                          S.d_peer_ret, S.poison);
     ep_signal_kernel<<<1, sig_threads, 0, s>>>(nullptr, nullptr, S.d_peer_flag, G, El, S.rank, 1,
-                                               epoch);
+                                               epoch, S.poison);
     ep_wait_kernel<<<1, std::max(sig_threads, 128), 0, s>>>(S.p2p_flag, G, 1, epoch, nullptr,
-                                                            nullptr, nullptr, 0, 0, W.dev_err);
+                                                            nullptr, nullptr, 0, 0, W.dev_err,
+                                                            S.poison, S.wait_ns);
     if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "return signal");
     // 8: y[t] = sum of its ranks' rows, ascending rank.
     prof_mark(L, 7, s);
     if (T > 0) {
-        if (three_pass(L))
+        if (fp32_faithful(L))
             ep_dd_combine_kernel<true><<<(T + 7) / 8, 256, 0, s>>>(S.p2p_ret, S.slot_dd, T, G,
                                                                    S.cap_src, L.d, y);
         else
@@ -1030,6 +1090,13 @@ int ep_forward_p2p(Layer& L, const float* x, float* y, int T, cudaStream_t s) {
         if ((ce = cudaGetLastError()) != cudaSuccess) return cuda_err(ce, "combine");
     }
     prof_mark(L, kProfEnd, s);
+    // The step's device error flags, read back without blocking; the next
+    // forward (or moe_ep_check) looks at them once the copy has completed.
+    if ((ce = cudaMemcpyAsync(S.h_err, W.dev_err, sizeof(int), cudaMemcpyDeviceToHost, s)) !=
+            cudaSuccess ||
+        (ce = cudaEventRecord(S.err_ev, s)) != cudaSuccess)
+        return cuda_err(ce, "status copy");
+    S.err_recorded = true;
     return MOE_OK;
 }
 
@@ -1153,6 +1220,8 @@ static int ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_
         return rc;
     }
     S->transport = cfg->ep_transport;
+    S->wait_ns = (cfg->ep_wait_ms > 0 ? (unsigned long long)cfg->ep_wait_ms * 1000000ull
+                                      : kPeerWaitNs);
     if (S->transport == MOE_EP_TRANSPORT_P2P) {
         // Fixed capacity: the buffers are mapped by every rank once.
         const int capT = cfg->max_tokens > 0 ? cfg->max_tokens : 4096;
@@ -1174,6 +1243,14 @@ int moe_ep_create(const MoeConfig* cfg, const MoeWeightsHost* w, int rank, int w
 int moe_ep_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* w, int rank, int world,
                               const void* nccl_id, MoeHandle** out) {
     return ep_create(cfg, w, true, rank, world, nccl_id, out);
+}
+
+int moe_ep_check(MoeHandle* h) {
+    using namespace moe;
+    if (!h || !h->L.ep) return report_error(MOE_ERR_INVALID, "not an expert-parallel handle");
+    if (h->L.ep->transport == MOE_EP_TRANSPORT_NCCL) return MOE_OK;
+    DeviceGuardEp guard(h->L.cfg.device);
+    return ep_failure(*h->L.ep, true);
 }
 
 int moe_ep_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream) {

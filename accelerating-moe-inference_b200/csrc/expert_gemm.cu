@@ -25,9 +25,11 @@
 //               256-column fp32 accumulators in TMEM; tcgen05.commit releases
 //               smem stages and hands finished accumulators to the epilogue.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, one row per thread.
-// Precision: BF16 (kind::f16, 64 bf16 per 128-byte K-block, 4 stages) or
-// FP32 as 3xTF32 (kind::tf32 on hi/lo planes: hi*hi + hi*lo + lo*hi, 32 fp32
-// per K-block, 2 stages).  Both use 128-byte-swizzled K-major tiles.
+// Precision (GemmPrec): BF16 (kind::f16, 64 bf16 per 128-byte K-block, 4
+// stages); FP32 as 3xTF32 (kind::tf32 on hi/lo planes: lo*hi + hi*lo + hi*hi,
+// 32 fp32 per K-block, 2 stages); FP32_BF16X3 (kind::f16 on bf16 hi/lo
+// planes, the same three products at the bf16 rate, 64 per K-block, 2
+// stages).  All use 128-byte-swizzled K-major tiles.
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -69,14 +71,17 @@ constexpr int kBBytes = kTileN * 128;   // one B plane per stage: 256 rows x 128
 constexpr int kAccCols = kTileN;        // fp32 columns per accumulator
 constexpr int kTmemCols = 2 * kAccCols;
 
-template <bool kTf32x3>
+// kP: GemmPrec.  Two-plane schemes issue three MMAs per K step.
+template <int kP>
 struct Cfg {
-    static constexpr int kPlanes = kTf32x3 ? 2 : 1;
+    static constexpr int kPlanes = kP == kGemmBf16 ? 1 : 2;
+    static constexpr bool kTfKind = kP == kGemm3xTf32;
+    static constexpr int kElems = kTfKind ? 32 : 64;   // K elements per 128-byte block
     static constexpr int kStageBytes = kPlanes * (kABytes + kBBytes);
-    static constexpr int kStages = kTf32x3 ? 2 : 4;
+    static constexpr int kStages = kPlanes == 2 ? 2 : 4;
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
-    static constexpr uint32_t kIdesc = mma_idesc(kTf32x3 ? 2u : 1u, kTileM, kTileN);
+    static constexpr uint32_t kIdesc = mma_idesc(kTfKind ? 2u : 1u, kTileM, kTileN);
 };
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
@@ -102,7 +107,7 @@ __device__ __forceinline__ TileCoord decode_tile(const MTile* __restrict__ mtile
 // One accumulator tile out of TMEM for the calling warp's 32 rows: lane i
 // holds row (lane quarter base + i); `valid` rows are written.  tcgen05.ld is
 // warp-collective, so every lane runs the loads.
-template <bool kTf32x3, int kEpi>
+template <int kP, int kEpi>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbase, bool valid,
                                               size_t prow, int nt, int split) {
     if constexpr (kEpi == kEpiGateUp) {
@@ -114,7 +119,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
             tmem_ld_wait();
             const int col = nt * (kTileN / 2) + c;
             if (valid) {
-                if constexpr (kTf32x3) {
+                if constexpr (kP == kGemm3xTf32) {
                     float4* dh = reinterpret_cast<float4*>(
                         static_cast<float*>(p.h_hi) + prow * p.ldh + col);
                     float4* dl = reinterpret_cast<float4*>(
@@ -132,6 +137,24 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
                         hv.w = to_tf32(h3); lv.w = to_tf32(h3 - hv.w);
                         dh[j / 4] = hv;
                         dl[j / 4] = lv;
+                    }
+                } else if constexpr (kP == kGemmBf16x3) {
+                    const size_t off = prow * p.ldh + col;
+                    uint4* dh = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.h_hi) + off);
+                    uint4* dl = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.h_lo) + off);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        uint32_t hw[4], lw[4];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float a = silu_f(__uint_as_float(g[j + 2 * i])) *
+                                            __uint_as_float(u[j + 2 * i]);
+                            const float b = silu_f(__uint_as_float(g[j + 2 * i + 1])) *
+                                            __uint_as_float(u[j + 2 * i + 1]);
+                            split_bf16x2(a, b, hw[i], lw[i]);
+                        }
+                        dh[j / 8] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                        dl[j / 8] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                     }
                 } else {
                     uint4* dst = reinterpret_cast<uint4*>(
@@ -176,7 +199,8 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
         // at the row it arrived in -- fp32 in FP32 precision, bf16 in BF16
         // precision (half the return bytes).
         const int dst = valid ? p.row_token[prow] : 0;
-        constexpr size_t kEs = kTf32x3 ? 4 : 2;
+        constexpr bool kF32 = kP != kGemmBf16;   // fp32-faithful precisions return fp32
+        constexpr size_t kEs = kF32 ? 4 : 2;
         char* rowp = reinterpret_cast<char*>(p.y) + static_cast<size_t>(dst) * p.d * kEs;
 #pragma unroll 1
         for (int c = 0; c < kTileN; c += 32) {
@@ -185,7 +209,7 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
             tmem_ld_wait();
             const int col = nt * kTileN + c;
             if (valid && col < p.d) {
-                if constexpr (kTf32x3) {
+                if constexpr (kF32) {
                     float4* out = reinterpret_cast<float4*>(rowp) + col / 4;
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
@@ -236,13 +260,13 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, uint32_t tbas
     }
 }
 
-template <bool kTf32x3, int kEpi>
+template <int kP, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
 expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                    const __grid_constant__ CUtensorMap tmA_lo,
                    const __grid_constant__ CUtensorMap tmB_hi,
                    const __grid_constant__ CUtensorMap tmB_lo, const GemmParams p) {
-    using C = Cfg<kTf32x3>;
+    using C = Cfg<kP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -271,7 +295,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
         fence_mbar_init();
         tma_prefetch_desc(&tmA_hi);
         tma_prefetch_desc(&tmB_hi);
-        if constexpr (kTf32x3) {
+        if constexpr (C::kPlanes == 2) {
             tma_prefetch_desc(&tmA_lo);
             tma_prefetch_desc(&tmB_lo);
         }
@@ -304,7 +328,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                 const int mt = tc.mt, nt = tc.nt;
                 const MTile tile = p.mtiles[mt];
                 const int brow = tile.expert * p.b_rows_per_expert + nt * kTileN;
-                constexpr int kElems = kTf32x3 ? 32 : 64;
+                constexpr int kElems = C::kElems;
                 const int kb0 = (t % p.k_splits) * kb_per;
                 const int kb1 = min(p.k_blocks, kb0 + kb_per);
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -316,7 +340,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
                     const int kx = kb * kElems;
                     tma_load_2d(sbase, &tmA_hi, &full[stage], kx, tile.row0);
-                    if constexpr (kTf32x3) {
+                    if constexpr (C::kPlanes == 2) {
                         tma_load_2d(sbase + kABytes, &tmA_lo, &full[stage], kx, tile.row0);
                         tma_load_2d(sbase + 2 * kABytes, &tmB_hi, &full[stage], kx, brow);
                         tma_load_2d(sbase + 2 * kABytes + kBBytes, &tmB_lo, &full[stage], kx, brow);
@@ -365,7 +389,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     const uint32_t sbase = smem_u32(smem + stage * C::kStageBytes);
                     const uint64_t a_hi = smem_desc_sw128(sbase);
                     uint64_t a_lo = 0, b_hi, b_lo = 0;
-                    if constexpr (kTf32x3) {
+                    if constexpr (C::kPlanes == 2) {
                         a_lo = smem_desc_sw128(sbase + kABytes);
                         b_hi = smem_desc_sw128(sbase + 2 * kABytes);
                         b_lo = smem_desc_sw128(sbase + 2 * kABytes + kBBytes);
@@ -377,10 +401,11 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                         // 32 bytes of K per instruction: +2 in the >>4 address field.
                         const uint64_t off = static_cast<uint64_t>(ks * 2);
                         const uint32_t accum = (kb != kb0 || ks != 0) ? 1u : 0u;
-                        if constexpr (kTf32x3) {
-                            tc_mma<true>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
-                            tc_mma<true>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
-                            tc_mma<true>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
+                        if constexpr (C::kPlanes == 2) {
+                            // Small products first: lo*hi, hi*lo, then hi*hi.
+                            tc_mma<C::kTfKind>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
+                            tc_mma<C::kTfKind>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
+                            tc_mma<C::kTfKind>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
                         } else {
                             tc_mma<false>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, accum);
                         }
@@ -418,7 +443,7 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             const size_t prow = static_cast<size_t>(tile.row0 + row_in_tile);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kAccCols);
-            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, nt, t % p.k_splits);
+            epilogue_rows<kP, kEpi>(p, tbase, valid, prow, nt, t % p.k_splits);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -446,25 +471,27 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
 //   empty[s]   both CTAs; the leader's commit arrives on both;
 //   tfull[a]   both CTAs; the leader's commit arrives on both;
 //   tempty[a]  leader only; 4 epilogue warps x 2 CTAs arrive.
-template <bool kTf32x3>
+template <int kP>
 struct PairCfg {
-    static constexpr int kPlanes = kTf32x3 ? 2 : 1;
+    static constexpr int kPlanes = kP == kGemmBf16 ? 1 : 2;
+    static constexpr bool kTfKind = kP == kGemm3xTf32;
+    static constexpr int kElems = kTfKind ? 32 : 64;
     static constexpr int kHalfA = kTileM * 128;          // 128 rows of A
     static constexpr int kHalfB = (kTileN / 2) * 128;    // 128 rows of B
     static constexpr int kStageBytes = kPlanes * (kHalfA + kHalfB);
-    static constexpr int kStages = kTf32x3 ? 3 : 6;
+    static constexpr int kStages = kPlanes == 2 ? 3 : 6;
     static constexpr int kBarOffset = kStages * kStageBytes;
     static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
-    static constexpr uint32_t kIdesc = mma_idesc(kTf32x3 ? 2u : 1u, 2 * kTileM, kTileN);
+    static constexpr uint32_t kIdesc = mma_idesc(kTfKind ? 2u : 1u, 2 * kTileM, kTileN);
 };
 
-template <bool kTf32x3, int kEpi>
+template <int kP, int kEpi>
 __global__ void __launch_bounds__(kThreads, 1)
 expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                         const __grid_constant__ CUtensorMap tmA_lo,
                         const __grid_constant__ CUtensorMap tmB_hi,
                         const __grid_constant__ CUtensorMap tmB_lo, const GemmParams p) {
-    using C = PairCfg<kTf32x3>;
+    using C = PairCfg<kP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -495,7 +522,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
         fence_mbar_init();
         tma_prefetch_desc(&tmA_hi);
         tma_prefetch_desc(&tmB_hi);
-        if constexpr (kTf32x3) {
+        if constexpr (C::kPlanes == 2) {
             tma_prefetch_desc(&tmA_lo);
             tma_prefetch_desc(&tmB_lo);
         }
@@ -523,7 +550,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             int stage = 0;
             uint32_t phase = 0;
             int issued = 0;
-            constexpr int kElems = kTf32x3 ? 32 : 64;
+            constexpr int kElems = C::kElems;
             for (int t = cid; t < total && !*abort_flag; t += nclusters) {
                 const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
                 const MTile tile = p.mtiles[tc.mt];
@@ -540,7 +567,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     const uint32_t fb = full0 + stage * 8;
                     const int kx = kb * kElems;
                     tma_load_2d_pair(sbase, &tmA_hi, fb, kx, arow);
-                    if constexpr (kTf32x3) {
+                    if constexpr (C::kPlanes == 2) {
                         tma_load_2d_pair(sbase + C::kHalfA, &tmA_lo, fb, kx, arow);
                         tma_load_2d_pair(sbase + 2 * C::kHalfA, &tmB_hi, fb, kx, brow);
                         tma_load_2d_pair(sbase + 2 * C::kHalfA + C::kHalfB, &tmB_lo, fb, kx, brow);
@@ -585,7 +612,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     const uint32_t sbase = smem_u32(smem + stage * C::kStageBytes);
                     const uint64_t a_hi = smem_desc_sw128(sbase);
                     uint64_t a_lo = 0, b_hi, b_lo = 0;
-                    if constexpr (kTf32x3) {
+                    if constexpr (C::kPlanes == 2) {
                         a_lo = smem_desc_sw128(sbase + C::kHalfA);
                         b_hi = smem_desc_sw128(sbase + 2 * C::kHalfA);
                         b_lo = smem_desc_sw128(sbase + 2 * C::kHalfA + C::kHalfB);
@@ -596,10 +623,10 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     for (int ks = 0; ks < 4; ++ks) {
                         const uint64_t off = static_cast<uint64_t>(ks * 2);
                         const uint32_t accum = (kb | ks) != 0 ? 1u : 0u;
-                        if constexpr (kTf32x3) {
-                            tc_mma_pair<true>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
-                            tc_mma_pair<true>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
-                            tc_mma_pair<true>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
+                        if constexpr (C::kPlanes == 2) {
+                            tc_mma_pair<C::kTfKind>(d_tmem, a_lo + off, b_hi + off, C::kIdesc, accum);
+                            tc_mma_pair<C::kTfKind>(d_tmem, a_hi + off, b_lo + off, C::kIdesc, 1u);
+                            tc_mma_pair<C::kTfKind>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, 1u);
                         } else {
                             tc_mma_pair<false>(d_tmem, a_hi + off, b_hi + off, C::kIdesc, accum);
                         }
@@ -634,7 +661,7 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             const size_t prow = static_cast<size_t>(tile.row0 + (int)crank * kTileM + row_in_tile);
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                                    static_cast<uint32_t>(acc * kAccCols);
-            epilogue_rows<kTf32x3, kEpi>(p, tbase, valid, prow, tc.nt, 0);
+            epilogue_rows<kP, kEpi>(p, tbase, valid, prow, tc.nt, 0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty0 + acc * 8);
@@ -651,12 +678,12 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
     }
 }
 
-template <bool kTf32x3, int kEpi>
+template <int kP, int kEpi>
 cudaError_t launch_pair(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
                         const CUtensorMap& b_lo, const GemmParams& p, int clusters,
                         bool pdl, cudaStream_t s) {
-    using C = PairCfg<kTf32x3>;
-    auto kern = expert_gemm_pair_kernel<kTf32x3, kEpi>;
+    using C = PairCfg<kP>;
+    auto kern = expert_gemm_pair_kernel<kP, kEpi>;
     cudaError_t err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (err != cudaSuccess) return err;
@@ -677,12 +704,12 @@ cudaError_t launch_pair(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const 
     return cudaLaunchKernelEx(&cfg, kern, a_hi, a_lo, b_hi, b_lo, p);
 }
 
-template <bool kTf32x3, int kEpi>
+template <int kP, int kEpi>
 cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                        const CUtensorMap& b_hi, const CUtensorMap& b_lo, const GemmParams& p,
                        int grid, cudaStream_t s) {
-    using C = Cfg<kTf32x3>;
-    auto kern = expert_gemm_kernel<kTf32x3, kEpi>;
+    using C = Cfg<kP>;
+    auto kern = expert_gemm_kernel<kP, kEpi>;
     cudaError_t err =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     if (err != cudaSuccess) return err;
@@ -702,31 +729,41 @@ cudaError_t launch_one(const Layer& L, const CUtensorMap& a_hi, const CUtensorMa
 }
 
 // One template instantiation per (precision, epilogue) for each tile shape.
-template <bool kTf, int kEpi>
+template <int kP, int kEpi>
 cudaError_t dispatch_shape(const Layer& L, bool pair, const GemmParams& g, int clusters,
                            int grid, cudaStream_t s) {
     const Workspace& W = L.ws;
+    constexpr bool two = kP != kGemmBf16;
     const bool gu = kEpi == kEpiGateUp;
     const CUtensorMap& a_hi = gu ? W.tm_a_hi : W.tm_h_hi;
-    const CUtensorMap& a_lo = kTf ? (gu ? W.tm_a_lo : W.tm_h_lo) : a_hi;
+    const CUtensorMap& a_lo = two ? (gu ? W.tm_a_lo : W.tm_h_lo) : a_hi;
     if (pair) {
         const CUtensorMap& b_hi = gu ? L.tm_w13_hi2 : L.tm_w2_hi2;
-        const CUtensorMap& b_lo = kTf ? (gu ? L.tm_w13_lo2 : L.tm_w2_lo2) : b_hi;
-        return launch_pair<kTf, kEpi>(a_hi, a_lo, b_hi, b_lo, g, clusters, !L.profile, s);
+        const CUtensorMap& b_lo = two ? (gu ? L.tm_w13_lo2 : L.tm_w2_lo2) : b_hi;
+        return launch_pair<kP, kEpi>(a_hi, a_lo, b_hi, b_lo, g, clusters, !L.profile, s);
     }
     const CUtensorMap& b_hi = gu ? L.tm_w13_hi : L.tm_w2_hi;
-    const CUtensorMap& b_lo = kTf ? (gu ? L.tm_w13_lo : L.tm_w2_lo) : b_hi;
-    return launch_one<kTf, kEpi>(L, a_hi, a_lo, b_hi, b_lo, g, grid, s);
+    const CUtensorMap& b_lo = two ? (gu ? L.tm_w13_lo : L.tm_w2_lo) : b_hi;
+    return launch_one<kP, kEpi>(L, a_hi, a_lo, b_hi, b_lo, g, grid, s);
 }
 
-template <bool kTf>
+template <int kP>
 cudaError_t dispatch_mode(const Layer& L, int mode, bool pair, const GemmParams& g, int clusters,
                           int grid, cudaStream_t s) {
     switch (mode) {
-        case 0: return dispatch_shape<kTf, kEpiGateUp>(L, pair, g, clusters, grid, s);
-        case 1: return dispatch_shape<kTf, kEpiDown>(L, pair, g, clusters, grid, s);
-        case 2: return dispatch_shape<kTf, kEpiDownStore>(L, pair, g, clusters, grid, s);
-        default: return dispatch_shape<kTf, kEpiDownSlot>(L, pair, g, clusters, grid, s);
+        case 0: return dispatch_shape<kP, kEpiGateUp>(L, pair, g, clusters, grid, s);
+        case 1: return dispatch_shape<kP, kEpiDown>(L, pair, g, clusters, grid, s);
+        case 2: return dispatch_shape<kP, kEpiDownStore>(L, pair, g, clusters, grid, s);
+        default: return dispatch_shape<kP, kEpiDownSlot>(L, pair, g, clusters, grid, s);
+    }
+}
+
+cudaError_t dispatch_prec(const Layer& L, int mode, bool pair, const GemmParams& g,
+                          int clusters, int grid, cudaStream_t s) {
+    switch (gemm_prec(L)) {
+        case kGemm3xTf32: return dispatch_mode<kGemm3xTf32>(L, mode, pair, g, clusters, grid, s);
+        case kGemmBf16x3: return dispatch_mode<kGemmBf16x3>(L, mode, pair, g, clusters, grid, s);
+        default: return dispatch_mode<kGemmBf16>(L, mode, pair, g, clusters, grid, s);
     }
 }
 
@@ -736,8 +773,7 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
                                     int mode, size_t split_stride, int* nsplit) {
     const bool down = mode != 0;
     const Workspace& W = L.ws;
-    const bool tf = three_pass(L);
-    const int elems = tf ? 32 : 64;
+    const int elems = kblock_elems(L);
     const int max_mtiles = (routed_rows + kTileM - 1) / kTileM + L.E;
 
     GemmParams g{};
@@ -780,8 +816,7 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
         g.num_mtiles = W.num_ptiles;
         int clusters = ((routed_rows + 2 * kTileM - 1) / (2 * kTileM) + L.E) * g.n_tiles;
         if (clusters > L.sm_count / 2) clusters = L.sm_count / 2;
-        return tf ? dispatch_mode<true>(L, mode, true, g, clusters, 0, s)
-                  : dispatch_mode<false>(L, mode, true, g, clusters, 0, s);
+        return dispatch_prec(L, mode, true, g, clusters, 0, s);
     }
     // Decode-sized batches leave the down GEMM with few tiles (d / 256 per
     // routed expert), too few to keep every SM streaming weights: split K
@@ -799,8 +834,7 @@ cudaError_t launch_expert_gemm_rows(const Layer& L, int routed_rows, float* y, c
     }
     int grid = max_mtiles * g.n_tiles * g.k_splits;
     if (grid > L.sm_count) grid = L.sm_count;
-    return tf ? dispatch_mode<true>(L, mode, false, g, 0, grid, s)
-              : dispatch_mode<false>(L, mode, false, g, 0, grid, s);
+    return dispatch_prec(L, mode, false, g, 0, grid, s);
 }
 
 }  // namespace moe

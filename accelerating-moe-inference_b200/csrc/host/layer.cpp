@@ -1,6 +1,10 @@
 // MoE layer classes of the drop-in (include/layer.h) over the C ABI.
 #include "layer.h"
 
+#include <algorithm>
+#include <cmath>
+#include <limits>
+#include <vector>
 #include <stdexcept>
 #include <string>
 
@@ -191,4 +195,102 @@ void PhiMoEBlock::forward_device(const float* attn_dev, float* y_dev, std::size_
     const int rc = moe_block_forward_device(h_.get(), attn_dev, y_dev, static_cast<int32_t>(rows),
                                             stream);
     if (rc != MOE_OK) throw_status(rc, "PhiMoEBlock::forward_device");
+}
+
+// ---------------------------------------------------------------- PhiAttention
+namespace {
+
+std::string attn_name(std::size_t layer_idx, const char* proj, const char* what) {
+    return "model.layers." + std::to_string(layer_idx) + ".self_attn." + proj + "." + what;
+}
+
+}  // namespace
+
+PhiAttention::PhiAttention(const ModelLoader& loader, std::size_t layer_idx)
+    : PhiAttention(loader, layer_idx, PhiAttentionGeometry{}) {}
+
+PhiAttention::PhiAttention(const ModelLoader& loader, std::size_t layer_idx,
+                           const PhiAttentionGeometry& g)
+    : q_proj_(loader, attn_name(layer_idx, "q_proj", "weight"), attn_name(layer_idx, "q_proj", "bias")),
+      k_proj_(loader, attn_name(layer_idx, "k_proj", "weight"), attn_name(layer_idx, "k_proj", "bias")),
+      v_proj_(loader, attn_name(layer_idx, "v_proj", "weight"), attn_name(layer_idx, "v_proj", "bias")),
+      o_proj_(loader, attn_name(layer_idx, "o_proj", "weight"), attn_name(layer_idx, "o_proj", "bias")),
+      g_(g) {
+    if (g_.heads == 0 || g_.kv_heads == 0 || g_.heads % g_.kv_heads || g_.head_dim % 2)
+        throw std::invalid_argument("PhiAttention geometry");
+}
+
+// Causal attention with the reference's arithmetic per score (a
+// d-ascending fused multiply-add chain, scaled by 1/sqrt(head_dim) in
+// float), its max-subtracted exp in double, its running denominator and its
+// probability-times-value chain; scores are computed once per (query, key)
+// rather than three times, with the same values.
+void PhiAttention::forward(const Tensor& x, Tensor& y) const {
+    const std::size_t S = x.size(0);
+    const std::size_t H = g_.heads, KVH = g_.kv_heads, hd = g_.head_dim;
+    Tensor q, k, v;
+    q_proj_.forward(x, q);
+    k_proj_.forward(x, k);
+    v_proj_.forward(x, v);
+    if (q.size(1) != H * hd || k.size(1) != KVH * hd || v.size(1) != KVH * hd)
+        throw std::invalid_argument("PhiAttention: projection widths do not match the geometry");
+    tensor_ops::apply_rope(q, k, S, H, KVH, hd, g_.rope_theta);
+    Tensor out({S, H * hd});
+    const std::size_t group = H / KVH;
+    const float scale = std::sqrt(static_cast<float>(hd));
+    const float* Q = q.data();
+    const float* K = k.data();
+    const float* V = v.data();
+    float* O = out.data();
+    const std::size_t qw = H * hd, kw = KVH * hd;
+#pragma omp parallel for
+    for (long long w = 0; w < static_cast<long long>(S * H); ++w) {
+        const std::size_t qi = static_cast<std::size_t>(w) / H, qh = static_cast<std::size_t>(w) % H;
+        const std::size_t kh = qh / group;
+        const std::size_t k0 = qi + 1 > g_.sliding_window ? qi + 1 - g_.sliding_window : 0;
+        std::vector<float> sc(qi + 1 - k0);
+        float maxv = -std::numeric_limits<float>::infinity();
+        for (std::size_t ki = k0; ki <= qi; ++ki) {
+            const float* qr = Q + qi * qw + qh * hd;
+            const float* kr = K + ki * kw + kh * hd;
+            float s = 0.0f;
+            for (std::size_t d = 0; d < hd; ++d) s = std::fma(qr[d], kr[d], s);
+            sc[ki - k0] = s / scale;
+            maxv = std::max(maxv, sc[ki - k0]);
+        }
+        float denom = 0.0f;
+        for (float& s : sc) {
+            s = static_cast<float>(std::exp(static_cast<double>(s - maxv)));
+            denom += s;
+        }
+        for (std::size_t d = 0; d < hd; ++d) {
+            float value = 0.0f;
+            for (std::size_t ki = k0; ki <= qi; ++ki)
+                value = std::fma(sc[ki - k0] / denom, V[ki * kw + kh * hd + d], value);
+            O[qi * qw + qh * hd + d] = value;
+        }
+    }
+    o_proj_.forward(out, y);
+}
+
+// ---------------------------------------------------------------- PhiDecoderLayer
+PhiDecoderLayer::PhiDecoderLayer(const ModelLoader& loader, std::size_t layer_idx)
+    : PhiDecoderLayer(loader, layer_idx, PhiAttentionGeometry{}, reference_config()) {}
+
+PhiDecoderLayer::PhiDecoderLayer(const ModelLoader& loader, std::size_t layer_idx,
+                                 const PhiAttentionGeometry& g, const MoeConfig& moe_cfg)
+    : input_norm_weight_(loader.load("model.layers." + std::to_string(layer_idx) +
+                                     ".input_layernorm.weight")),
+      input_norm_bias_(loader.load("model.layers." + std::to_string(layer_idx) +
+                                   ".input_layernorm.bias")),
+      attention_(loader, layer_idx, g),
+      moe_(loader, layer_idx, moe_cfg),
+      eps_(g.norm_eps) {}
+
+void PhiDecoderLayer::forward(const Tensor& x, Tensor& y) const {
+    Tensor normed(x.shape()), attn;
+    tensor_ops::layer_norm(x, input_norm_weight_, input_norm_bias_, eps_, normed);
+    attention_.forward(normed, attn);
+    tensor_ops::add_inplace(attn, x);
+    moe_.forward(attn, y);
 }

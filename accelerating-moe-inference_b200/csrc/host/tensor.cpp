@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <limits>
 #include <stdexcept>
 #include <string>
 
@@ -144,6 +145,74 @@ void matmul_transposed(const Tensor& a, const Tensor& b, Tensor& c) {
             for (std::size_t p = 0; p < k; ++p) s = std::fma(A[i * k + p], B[j * k + p], s);
             C[i * n + j] = s;
         }
+}
+
+// c[i][j] = sum_p a[i][p] * b[p][j], a p-ascending fused multiply-add chain
+// per output, as matmul_transposed.
+void matmul(const Tensor& a, const Tensor& b, Tensor& c) {
+    if (a.ndim() != 2 || b.ndim() != 2 || c.ndim() != 2)
+        throw std::invalid_argument("matmul shape");
+    const std::size_t m = a.size(0), k = a.size(1), n = b.size(1);
+    if (b.size(0) != k || c.size(0) != m || c.size(1) != n)
+        throw std::invalid_argument("matmul shape");
+    const float* A = a.data();
+    const float* B = b.data();
+    float* C = c.data();
+#pragma omp parallel for
+    for (long long i = 0; i < static_cast<long long>(m); ++i)
+        for (std::size_t j = 0; j < n; ++j) {
+            float s = 0.0f;
+            for (std::size_t p = 0; p < k; ++p) s = std::fma(A[i * k + p], B[p * n + j], s);
+            C[i * n + j] = s;
+        }
+}
+
+void softmax_last_dim(const Tensor& x, Tensor& y) {
+    if (x.ndim() == 0 || y.size() != x.size()) throw std::invalid_argument("softmax shape");
+    const std::size_t h = x.size(x.ndim() - 1), rows = x.size() / h;
+    const float* X = x.data();
+    float* Y = y.data();
+    for (std::size_t r = 0; r < rows; ++r) {
+        const float* xr = X + r * h;
+        float* yr = Y + r * h;
+        float m = -std::numeric_limits<float>::infinity();
+        for (std::size_t j = 0; j < h; ++j) m = std::max(m, xr[j]);
+        double sum = 0.0;
+        for (std::size_t j = 0; j < h; ++j) sum += std::exp(static_cast<double>(xr[j] - m));
+        for (std::size_t j = 0; j < h; ++j)
+            yr[j] = static_cast<float>(std::exp(static_cast<double>(xr[j] - m)) / sum);
+    }
+}
+
+// Pair (j, j + head_dim / 2) of every head of row s turns by the angle
+// s * theta^(-2j / head_dim), computed in float as the reference does.
+void apply_rope(Tensor& q, Tensor& k, std::size_t seq_len, std::size_t q_heads,
+                std::size_t kv_heads, std::size_t head_dim, float theta) {
+    if (head_dim % 2 || q.ndim() != 2 || k.ndim() != 2 || q.size(0) < seq_len ||
+        k.size(0) < seq_len || q.size(1) != q_heads * head_dim || k.size(1) != kv_heads * head_dim)
+        throw std::invalid_argument("apply_rope shape");
+    const std::size_t half = head_dim / 2;
+    auto rotate = [&](Tensor& t, std::size_t heads, std::size_t s) {
+        float* row = t.data() + s * t.size(1);
+        for (std::size_t j = 0; j < half; ++j) {
+            const float inv = std::pow(theta, -2.0f * static_cast<float>(j) /
+                                                  static_cast<float>(head_dim));
+            const float ang = static_cast<float>(s) * inv;
+            const float c = std::cos(ang), sn = std::sin(ang);
+            for (std::size_t hh = 0; hh < heads; ++hh) {
+                float* p = row + hh * head_dim;
+                const float x0 = p[j], x1 = p[j + half];
+                // (x0 * c - x1 * sn, x1 * c + x0 * sn), each contracted to one
+                // fma around the second product's rounding.
+                p[j] = std::fma(x0, c, -(x1 * sn));
+                p[j + half] = std::fma(x1, c, x0 * sn);
+            }
+        }
+    };
+    for (std::size_t s = 0; s < seq_len; ++s) {
+        rotate(q, q_heads, s);
+        rotate(k, kv_heads, s);
+    }
 }
 
 void layer_norm(const Tensor& x, const Tensor& weight, const Tensor& bias, float eps, Tensor& y) {

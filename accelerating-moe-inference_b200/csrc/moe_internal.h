@@ -10,9 +10,9 @@
 //             are zero.
 //   down      w2 [E][d][ffp], padding columns zero.
 //   BF16 precision stores these once in bf16.  FP32 precision stores a tf32
-//   "hi" plane and an fp32 "lo" plane (w = hi + lo exactly, hi has its low 13
-//   mantissa bits clear) for the 3xTF32 tensor-core path, plus the plain fp32
-//   weights for the decode path.
+//   "hi" plane and a tf32 "lo" plane (the remainder) for the 3xTF32
+//   tensor-core path, FP32_BF16X3 a bf16 "hi" plane and a bf16 "lo" plane;
+//   both also keep the plain fp32 weights for the decode path.
 // Workspace per forward (capacity grows, never shrinks):
 //   logits [T][E], idx/wts [T][k], blockhist [nblk][E], counts [E],
 //   eoff [E+1] (packed-row offset of each expert, multiples of 128),
@@ -310,9 +310,18 @@ cudaError_t convert_down(const Layer& L, int e, const float* w2_dev, cudaStream_
 int report_error(int code, const std::string& msg);
 // Grow the workspace to T tokens (capi.cu).
 int ensure_workspace(Layer& L, int T);
+// Supplies one expert tensor on the host during handle construction
+// (which: 0 w1, 1 w3, 2 w2; n floats into dst); a non-zero return is an
+// MoeStatus with moe_last_error set.  Lets a loader stream the experts from
+// a file one tensor at a time instead of holding the layer in host memory.
+struct ExpertReader {
+    virtual ~ExpertReader() = default;
+    virtual int read(int e, int which, float* dst, size_t n) = 0;
+};
 // Handle construction for experts [e_first, e_first + e_count) (capi.cu).
+// With a reader (host weights only), w's expert pointers are not used.
 int create_slice(const MoeConfig* cfg, const MoeWeightsHost* w, bool device_ptrs, int e_first,
-                 int e_count, MoeHandle** out);
+                 int e_count, MoeHandle** out, ExpertReader* reader = nullptr);
 // Expert-parallel teardown (ep.cu).
 void ep_destroy(Layer& L);
 
@@ -333,7 +342,34 @@ struct MoeHandle {
 
 namespace moe {
 
-inline size_t elem_bytes(const Layer& L) { return L.cfg.precision == MOE_PREC_BF16 ? 2 : 4; }
-inline bool three_pass(const Layer& L) { return L.cfg.precision == MOE_PREC_FP32; }
+// Tensor-core operand scheme of the grouped GEMMs: one bf16 plane; tf32 hi +
+// lo planes (fp32 storage) with three tf32 MMAs; bf16 hi + lo planes with
+// three bf16 MMAs.
+enum GemmPrec : int { kGemmBf16 = 0, kGemm3xTf32 = 1, kGemmBf16x3 = 2 };
+inline int gemm_prec(const Layer& L) {
+    return L.cfg.precision == MOE_PREC_BF16 ? kGemmBf16
+         : L.cfg.precision == MOE_PREC_FP32 ? kGemm3xTf32 : kGemmBf16x3;
+}
+// fp32-faithful precisions: decode streams fp32 weights, expert-parallel rows
+// travel in fp32.
+inline bool fp32_faithful(const Layer& L) { return L.cfg.precision != MOE_PREC_BF16; }
+// GEMM operands in two planes (hi and lo).
+inline bool split_planes(const Layer& L) { return gemm_prec(L) != kGemmBf16; }
+// Bytes of one element of one operand plane, and whether the planes are bf16.
+inline size_t plane_bytes(const Layer& L) { return gemm_prec(L) == kGemm3xTf32 ? 4 : 2; }
+inline bool planes_bf16(const Layer& L) { return gemm_prec(L) != kGemm3xTf32; }
+// Bytes per element of an expert-parallel row on the wire.
+inline size_t wire_bytes(const Layer& L) { return fp32_faithful(L) ? 4 : 2; }
+// Elements of one 128-byte K block of an operand plane.
+inline int kblock_elems(const Layer& L) { return gemm_prec(L) == kGemm3xTf32 ? 32 : 64; }
+
+// Format of the packed activation rows: the GEMM operand planes of each
+// precision, or (decode kernels) the rows as the decode kernels read them.
+enum ActFormat : int { kActBf16 = 0, kActTf32x2 = 1, kActF32 = 2, kActBf16x2 = 3 };
+inline int act_format(const Layer& L, bool decode) {
+    if (decode) return fp32_faithful(L) ? kActF32 : kActBf16;
+    const int g = gemm_prec(L);
+    return g == kGemmBf16 ? kActBf16 : g == kGemm3xTf32 ? kActTf32x2 : kActBf16x2;
+}
 
 }  // namespace moe

@@ -11,10 +11,11 @@
 //
 // This file therefore keeps that scratch in a fixed, file-scope device array
 // (kScratchBytes, 1 MiB on every GPU that loads the library, held until the
-// process exits) and never allocates.  The three passes are the same
-// counting sort as the forward path's dispatch (histogram per 32-token block,
-// one-block exclusive scan per expert, stable placement in ascending token
-// order), written as separate kernels here so the forward path is untouched.
+// process exits) and never allocates.  The passes are the same counting sort
+// as the forward path's dispatch (histogram per 32-token block, exclusive
+// scan per expert over the blocks, padded expert offsets, stable placement in
+// ascending token order), written as separate kernels here so the forward
+// path is untouched.
 //
 // Contract:
 //   - the first call on a device looks up the array's device address with
@@ -58,71 +59,99 @@ noalloc_count_kernel(const int* __restrict__ idx, int T, int E, int k, int* __re
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)blockIdx.x * E + e] = h[e];
 }
 
-// One block: per-expert exclusive scan over the blocks (in place), counts,
-// expert offsets padded to 128 rows, and the padding rows' token -1 / 0.
-__global__ void __launch_bounds__(kMaxExperts)
-noalloc_scan_kernel(int* __restrict__ hist, int nblk, int E, int* __restrict__ counts,
-                    int* __restrict__ eoff, int* __restrict__ row_token,
-                    float* __restrict__ row_weight) {
-    __shared__ int s_cnt[kMaxExperts];
-    __shared__ int s_off[kMaxExperts + 1];
-    const int e = threadIdx.x;
-    if (e < E) {
-        int run = 0;
-        for (int b = 0; b < nblk; ++b) {
-            const int c = hist[(size_t)b * E + e];
-            hist[(size_t)b * E + e] = run;
-            run += c;
-        }
-        s_cnt[e] = run;
-        counts[e] = run;
-    }
+constexpr int kScanThreads = 1024;
+
+// One CTA per expert: exclusive scan of the expert's per-block counts over
+// the blocks, in place, 1024 blocks per round (warp shuffles, then the warp
+// totals); the expert's total goes to counts.
+__global__ void __launch_bounds__(kScanThreads)
+noalloc_scan_kernel(int* __restrict__ hist, int nblk, int E, int* __restrict__ counts) {
+    __shared__ int s_warp[kScanThreads / 32];
+    __shared__ int s_carry;
+    const int e = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) s_carry = 0;
     __syncthreads();
-    if (e == 0) {
+    for (int b0 = 0; b0 < nblk; b0 += kScanThreads) {
+        const int b = b0 + tid;
+        const int c = b < nblk ? hist[(size_t)b * E + e] : 0;
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) s_warp[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int w = s_warp[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += v;
+            }
+            s_warp[lane] = w;   // inclusive over warps
+        }
+        __syncthreads();
+        const int carry = s_carry;
+        const int before = (warp ? s_warp[warp - 1] : 0) + incl - c;
+        if (b < nblk) hist[(size_t)b * E + e] = carry + before;
+        __syncthreads();
+        if (tid == 0) s_carry = carry + s_warp[kScanThreads / 32 - 1];
+        __syncthreads();
+    }
+    if (tid == 0) counts[e] = s_carry;
+}
+
+// One CTA: expert offsets padded to 128 rows from the counts, and the
+// padding rows' token -1 / weight 0.
+__global__ void __launch_bounds__(256)
+noalloc_offsets_kernel(const int* __restrict__ counts, int E, int* __restrict__ eoff,
+                       int* __restrict__ row_token, float* __restrict__ row_weight) {
+    __shared__ int s_off[kMaxExperts + 1];
+    if (threadIdx.x == 0) {
         int off = 0;
         for (int x = 0; x < E; ++x) {
             s_off[x] = off;
             eoff[x] = off;
-            off += (s_cnt[x] + kTileM - 1) / kTileM * kTileM;
+            off += (counts[x] + kTileM - 1) / kTileM * kTileM;
         }
         s_off[E] = off;
         eoff[E] = off;
     }
     __syncthreads();
-    if (e < E) {
-        for (int r = s_off[e] + s_cnt[e]; r < s_off[e + 1]; ++r) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = warp; e < E; e += blockDim.x >> 5)
+        for (int r = s_off[e] + counts[e] + lane; r < s_off[e + 1]; r += 32) {
             row_token[r] = -1;
             row_weight[r] = 0.0f;
         }
-    }
 }
 
-// Stable placement: within an expert, rows are in ascending token order.
+// Stable placement: within an expert, entries in ascending (token, slot)
+// order.  An entry's rank inside its block counts the block's earlier
+// entries with the same expert, so an expert that a token lists twice gets
+// two rows, in slot order.
 __global__ void __launch_bounds__(256)
 noalloc_place_kernel(const int* __restrict__ idx, const float* __restrict__ wts, int T, int E,
                      int k, const int* __restrict__ hist, const int* __restrict__ eoff,
                      int* __restrict__ row_token, float* __restrict__ row_weight) {
-    __shared__ unsigned s_mask[kMaxExperts];
-    __shared__ int s_base[kMaxExperts];
+    __shared__ int s_e[kRouteTokens * kMaxTopK];
     const int t0 = blockIdx.x * kRouteTokens;
-    const int n_tok = min(kRouteTokens, T - t0);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        s_mask[e] = 0u;
-        s_base[e] = eoff[e] + hist[(size_t)blockIdx.x * E + e];
-    }
-    __syncthreads();
+    const int n = min(kRouteTokens, T - t0) * k;
     const int i = threadIdx.x;
-    int e = -1, t = 0;
-    if (i < n_tok * k) {
-        t = i / k;
+    int e = -1;
+    if (i < n) {
         e = idx[(size_t)t0 * k + i];
-        if (e >= 0 && e < E) atomicOr(&s_mask[e], 1u << t);
-        else e = -1;
+        if (e < 0 || e >= E) e = -1;
+        s_e[i] = e;
     }
     __syncthreads();
     if (e >= 0) {
-        const int pos = s_base[e] + __popc(s_mask[e] & ((1u << t) - 1u));
-        row_token[pos] = t0 + t;
+        int rank = 0;
+        for (int j = 0; j < i; ++j) rank += s_e[j] == e;
+        const int pos = eoff[e] + hist[(size_t)blockIdx.x * E + e] + rank;
+        row_token[pos] = t0 + i / k;
         row_weight[pos] = wts[(size_t)t0 * k + i];
     }
 }
@@ -153,8 +182,7 @@ extern "C" int moe_dispatch_noalloc(const int32_t* idx, const float* weights, in
         return set_error(MOE_ERR_INVALID,
                          "moe_dispatch_noalloc: rows_cap must be at least "
                          "(T * top_k / 128 + num_experts + 1) * 128");
-    if (T == 0) return MOE_OK;
-    if (!idx || !weights || !row_token || !row_weight || !expert_offsets || !counts)
+    if (!row_token || !row_weight || !expert_offsets || !counts || (T > 0 && (!idx || !weights)))
         return set_error(MOE_ERR_INVALID, "moe_dispatch_noalloc: null pointer argument");
 
     int dev = -1;
@@ -177,11 +205,15 @@ extern "C" int moe_dispatch_noalloc(const int32_t* idx, const float* weights, in
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int nb = (int)nblk;
-    noalloc_count_kernel<<<nb, 256, 0, s>>>(idx, T, num_experts, top_k, scratch);
-    noalloc_scan_kernel<<<1, kMaxExperts, 0, s>>>(scratch, nb, num_experts, counts,
-                                                  expert_offsets, row_token, row_weight);
-    noalloc_place_kernel<<<nb, 256, 0, s>>>(idx, weights, T, num_experts, top_k, scratch,
-                                            expert_offsets, row_token, row_weight);
+    // T == 0 runs only the last two kernels, which write zero counts and
+    // offsets.
+    if (nb > 0) noalloc_count_kernel<<<nb, 256, 0, s>>>(idx, T, num_experts, top_k, scratch);
+    noalloc_scan_kernel<<<num_experts, kScanThreads, 0, s>>>(scratch, nb, num_experts, counts);
+    noalloc_offsets_kernel<<<1, 256, 0, s>>>(counts, num_experts, expert_offsets, row_token,
+                                             row_weight);
+    if (nb > 0)
+        noalloc_place_kernel<<<nb, 256, 0, s>>>(idx, weights, T, num_experts, top_k, scratch,
+                                                expert_offsets, row_token, row_weight);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(MOE_ERR_CUDA, cudaGetErrorString(e));
     return MOE_OK;

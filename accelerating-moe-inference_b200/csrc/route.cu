@@ -551,7 +551,8 @@ __device__ void single_block_layout(const int* __restrict__ cnt, int E, int* s_o
     }
 }
 
-// kMode: 0 bf16 plane, 1 tf32 hi + lo planes, 2 fp32 as is (decode).
+// kMode: ActFormat -- bf16 plane, tf32 hi + lo planes, fp32 as is (decode),
+// or bf16 hi + lo planes.
 template <int kMode>
 __global__ void __launch_bounds__(256)
 dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
@@ -661,10 +662,19 @@ dispatch_permute_kernel(const float* __restrict__ x, int T, int d, int E, int k,
                     const size_t row = (size_t)s_dest[t * k + s];
                     reinterpret_cast<uint2*>(a_hi)[row * nv + v] = packed;
                 }
-            } else if constexpr (kMode == 2) {
+            } else if constexpr (kMode == kActF32) {
                 for (int s = 0; s < k; ++s) {
                     const size_t row = (size_t)s_dest[t * k + s];
                     reinterpret_cast<float4*>(a_hi)[row * nv + v] = f[u];
+                }
+            } else if constexpr (kMode == kActBf16x2) {
+                uint2 hp, lp;
+                split_bf16x2(f[u].x, f[u].y, hp.x, lp.x);
+                split_bf16x2(f[u].z, f[u].w, hp.y, lp.y);
+                for (int s = 0; s < k; ++s) {
+                    const size_t row = (size_t)s_dest[t * k + s];
+                    reinterpret_cast<uint2*>(a_hi)[row * nv + v] = hp;
+                    reinterpret_cast<uint2*>(a_lo)[row * nv + v] = lp;
                 }
             } else {
                 float4 h, l;
@@ -705,11 +715,17 @@ struct SmallGeom {
     int ld;       // padded row stride in floats: kc + 4 (LDS.128 of 8 rows conflict-free)
 };
 
-// Columns 4v .. 4v+3 of packed row `row` in the format of kMode.
+// Columns 4v .. 4v+3 of packed row `row` in the format of kMode (ActFormat).
 template <int kMode>
 __device__ __forceinline__ void store_row4(void* a_hi, void* a_lo, size_t row, int nv, int v,
                                            float4 f) {
-    if constexpr (kMode == 0) {
+    if constexpr (kMode == kActBf16x2) {
+        uint2 hp, lp;
+        split_bf16x2(f.x, f.y, hp.x, lp.x);
+        split_bf16x2(f.z, f.w, hp.y, lp.y);
+        reinterpret_cast<uint2*>(a_hi)[row * nv + v] = hp;
+        reinterpret_cast<uint2*>(a_lo)[row * nv + v] = lp;
+    } else if constexpr (kMode == 0) {
         __nv_bfloat162 lo2 = __floats2bfloat162_rn(f.x, f.y);
         __nv_bfloat162 hi2 = __floats2bfloat162_rn(f.z, f.w);
         uint2 packed;
@@ -729,7 +745,7 @@ __device__ __forceinline__ void store_row4(void* a_hi, void* a_lo, size_t row, i
     }
 }
 
-// kMode: 0 bf16 plane, 1 tf32 hi + lo planes, 2 fp32 as is.  KC: K columns
+// kMode: ActFormat of the routed rows.  KC: K columns
 // per stage (the chain loop is fully unrolled over it); kNorm: apply the
 // post-attention LayerNorm.
 template <int kMode, int KC, bool kNorm>
@@ -1098,9 +1114,9 @@ cudaError_t launch_route_small(const Layer& L, const float* x, int T, const Norm
     // All chain warps are launched whatever T x E is: the tail (layout and
     // row copies) uses every thread.
     const int threads = kSmallThreads;
-    // Row format: the decode kernels read fp32 (FP32) or bf16 (BF16) rows,
-    // the grouped GEMMs bf16 or tf32 hi + lo.
-    const int mode = three_pass(L) ? (decode ? 2 : 1) : 0;
+    // Row format: the decode kernels read fp32 (fp32-faithful) or bf16 (BF16)
+    // rows, the grouped GEMMs their operand planes.
+    const int mode = act_format(L, decode);
     auto launch = [&](auto kern) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
@@ -1128,13 +1144,15 @@ cudaError_t launch_route_small(const Layer& L, const float* x, int T, const Norm
         if (gm.kc == 128) return launch(router_small_kernel<M, 128, N>);
         return launch(router_small_kernel<M, 64, N>);
     };
-    using T0 = std::integral_constant<int, 0>;
-    using T1 = std::integral_constant<int, 1>;
-    using T2 = std::integral_constant<int, 2>;
+    using T0 = std::integral_constant<int, kActBf16>;
+    using T1 = std::integral_constant<int, kActTf32x2>;
+    using T2 = std::integral_constant<int, kActF32>;
+    using T3 = std::integral_constant<int, kActBf16x2>;
     using NF = std::false_type;
     using NT = std::true_type;
-    if (mode == 0) return norm ? by_kc(T0{}, NT{}) : by_kc(T0{}, NF{});
-    if (mode == 1) return norm ? by_kc(T1{}, NT{}) : by_kc(T1{}, NF{});
+    if (mode == kActBf16) return norm ? by_kc(T0{}, NT{}) : by_kc(T0{}, NF{});
+    if (mode == kActTf32x2) return norm ? by_kc(T1{}, NT{}) : by_kc(T1{}, NF{});
+    if (mode == kActBf16x2) return norm ? by_kc(T3{}, NT{}) : by_kc(T3{}, NF{});
     return norm ? by_kc(T2{}, NT{}) : by_kc(T2{}, NF{});
 }
 
@@ -1166,14 +1184,16 @@ cudaError_t launch_dispatch_permute_raw(const Layer& L, const float* x, int T, c
         so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
     }
     so.row_slot = W.row_slot;
-    if (three_pass(L))
-        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, nullptr, so, nr);
+    if (fp32_faithful(L))
+        dispatch_permute_kernel<kActF32><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx,
+                                                              W.wts, W.blockhist, W.eoff,
+                                                              W.row_token, W.row_weight, W.a_hi,
+                                                              nullptr, so, nr);
     else
-        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, nullptr, so, nr);
+        dispatch_permute_kernel<kActBf16><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx,
+                                                               W.wts, W.blockhist, W.eoff,
+                                                               W.row_token, W.row_weight, W.a_hi,
+                                                               nullptr, so, nr);
     return cudaGetLastError();
 }
 
@@ -1184,14 +1204,17 @@ cudaError_t launch_dispatch_permute_to(const Layer& L, const float* x, int T, in
     const dim3 grid = permute_grid(L, T);
     ScanOut so;
     so.slot_row = slot_row;
-    if (three_pass(L))
-        dispatch_permute_kernel<2><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
-                                                        W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, so, NormRef{});
+    // Rows on the wire: fp32 in the fp32-faithful precisions, else bf16.
+    if (fp32_faithful(L))
+        dispatch_permute_kernel<kActF32><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
+                                                              W.blockhist, eoff, row_token,
+                                                              row_weight, rows, nullptr, so,
+                                                              NormRef{});
     else
-        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
-                                                        W.blockhist, eoff, row_token,
-                                                        row_weight, rows, nullptr, so, NormRef{});
+        dispatch_permute_kernel<kActBf16><<<grid, 256, 0, s>>>(x, T, L.d, E, L.k, W.idx, W.wts,
+                                                               W.blockhist, eoff, row_token,
+                                                               row_weight, rows, nullptr, so,
+                                                               NormRef{});
     return cudaGetLastError();
 }
 
@@ -1205,14 +1228,15 @@ cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaS
         so.num_mtiles = W.num_mtiles; so.ptiles = W.ptiles; so.num_ptiles = W.num_ptiles;
     }
     so.row_slot = W.row_slot;
-    if (three_pass(L))
-        dispatch_permute_kernel<1><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo, so, nr);
-    else
-        dispatch_permute_kernel<0><<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts,
-                                                        W.blockhist, W.eoff, W.row_token,
-                                                        W.row_weight, W.a_hi, W.a_lo, so, nr);
+    auto run = [&](auto kern) {
+        kern<<<grid, 256, 0, s>>>(x, T, L.d, L.E_route, L.k, W.idx, W.wts, W.blockhist, W.eoff,
+                                  W.row_token, W.row_weight, W.a_hi, W.a_lo, so, nr);
+    };
+    switch (act_format(L, false)) {
+        case kActTf32x2: run(dispatch_permute_kernel<kActTf32x2>); break;
+        case kActBf16x2: run(dispatch_permute_kernel<kActBf16x2>); break;
+        default: run(dispatch_permute_kernel<kActBf16>); break;
+    }
     return cudaGetLastError();
 }
 

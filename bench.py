@@ -2,7 +2,7 @@
 """MoE-layer benchmark on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--precision bf16|fp32] [--workload c2]
+                    [--precision bf16x3|3xtf32|bf16] [--workload c2|c2small|c5|c4]
 
 Workload: a Mixtral-shaped MoE FFN layer in prefill,
 T=4096 tokens per GPU, d_model=4096, d_ff=14336, 8 experts, top-2 softmax
@@ -11,24 +11,39 @@ activations -- synthetic, drawn on the GPU by a seeded torch generator.
 
 One step = one forward of the layer over the step's T tokens: router,
 dispatch (histogram / scan / permute), gate/up grouped GEMM with the SwiGLU
-epilogue, down grouped GEMM with the weighted-combine epilogue.
+epilogue, down grouped GEMM (each routed row's output at its selection
+slot), ordered combine.
+
+The headline precision is fp32-faithful, as BASELINE config 2's fp32 weights
+and the reference's fp32 arithmetic ask: bf16x3 (every fp32 operand split
+into bf16 hi + lo, three bf16 MMAs into fp32; rel-L2 <= 1e-3).  The BF16
+weight mode (rel-L2 <= 2e-2) is measured in the same run and reported under
+roofline.modes.
 
   value       tokens/s over all ranks, x resident in HBM, CUDA events around
               each step on the launching stream; L2 is flushed (256 MiB
               write) between steps, outside the events.
   e2e         tokens/s through moe_forward_host (the reference-facing
               host-buffer call): pinned host x -> device -> layer -> host y,
-              timed around the synchronous call.
+              host clock around the synchronous call.
   roofline    the gate/up GEMM (2/3 of the layer's FLOPs): algorithmic FLOPs
-              4*T*k*d*ff per launch / its live CUDA-event duration, against
-              the measured dense bf16 peak in MEASURED_PEAKS.json.
+              4*T*k*d*ff per launch / its time (the step time of the timed,
+              unprofiled steps times the GEMM's share of a profiled step),
+              against the measured burst dense bf16 peak in
+              MEASURED_PEAKS.json.  Also holds each precision mode's numbers
+              (modes), the config-3 decode HBM fractions (decode) and the
+              config-4 decoder's (decoder).
   cpu_baseline  the reference's own PhiMoE::forward (src/layer.cu:80-103,
               compiled from its sources into oracle/_ref) on this host's
               cores, on a bounded sample of the same layer.
 
-N > 1 (torchrun): expert parallel -- each rank holds E/N experts and its own
-T tokens; dispatch and combine are NCCL send/recv exchanges over NVLink
-(weak scaling).  --parallelism dp runs token-sharded replicas instead.
+N > 1 (torchrun): expert parallel -- each rank holds E/N experts (round-robin
+placement) and its own T tokens; the default transport deduplicates: one row
+per (token, destination rank) stored into the destination's buffer over
+NVLink by the push kernel, the rank's expert outputs summed there in
+ascending expert order and one row stored back (--ep-transport nccl: NCCL
+send/recv exchanges instead); weak scaling.  --parallelism dp runs
+token-sharded replicas instead.
 """
 from __future__ import annotations
 
@@ -56,6 +71,17 @@ WORKLOADS = {
     "c5": dict(workload="c5-finegrained-ep", T=16384, d=2048, ff=1408, E=64, k=8, seed=3,
                zipf=True),
 }
+# Precision modes: the MoeConfig precision, the dtype string, and how many
+# bf16-rate tensor-core passes one algorithmic FLOP costs (bf16x3: three bf16
+# MMAs; 3xTF32: three tf32 MMAs at half the bf16 rate).
+PRECISIONS = {
+    "bf16x3": dict(prec=2, dtype="fp32 (bf16x3 tensor cores: hi*hi + hi*lo + lo*hi)", passes=3),
+    "3xtf32": dict(prec=0, dtype="fp32 (3xTF32 tensor cores)", passes=6),
+    "bf16": dict(prec=1, dtype="bf16", passes=1),
+}
+ROUTER_NOTE = ("the reference's PhiMoE routes with its quantised top-2 rule (scores rounded to "
+               "1e-3, tie margin 2e-2, weights 0.5/0.5); this repo's line routes with "
+               "BASELINE's softmax top-k renormalised -- the expert FLOPs per token are the same")
 
 
 def _router_weights(wl, gen, dev):
@@ -69,7 +95,10 @@ def _router_weights(wl, gen, dev):
         r = torch.arange(1, E + 1, dtype=torch.float64)
         bias = (0.5 * torch.log(1.0 / r)).to(torch.float32).to(dev)
     return wg, bias
-KERNELS_PER_FORWARD = 5   # router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM
+
+
+# router, dispatch_scan, dispatch_permute, gate/up GEMM, down GEMM, combine
+KERNELS_PER_FORWARD = 6
 # the toy MoE decoder, end to end (prompt of 512 uniform
 # ids, 128 greedy tokens, batch 1 and 16).
 C4 = dict(workload="c4-toy-moe-decoder", n_layers=8, d=2048, heads=16, hd=128, vocab=32000,
@@ -110,6 +139,21 @@ def _traffic_from_profile(workload: str, precision: str):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
     return float(m.group(1)) if m else None
+
+
+def _config(wl, args, world):
+    """The config object of both arms' lines (the reference arm emits the same)."""
+    par = f"dp{world} (token-sharded replicas, all experts per GPU)"
+    if world > 1 and args.parallelism == "ep":
+        par = (f"ep{world} (expert parallel, {wl['E'] // world} experts per GPU placed "
+               "round-robin, " + ("NCCL send/recv dispatch and combine)" if args.ep_transport == "nccl"
+                                  else "deduplicated NVLink peer-store dispatch and return)"))
+    return {"workload": wl["workload"], "T_per_gpu": wl["T"], "d_model": wl["d"], "d_ff": wl["ff"],
+            "experts": wl["E"], "top_k": wl["k"],
+            "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
+            "precision": args.precision, "seed": wl["seed"],
+            "l2": "flushed between steps (256 MiB write, outside the timed events)",
+            "parallelism": par}
 
 
 class ClockSampler:
@@ -192,36 +236,62 @@ class ClockSampler:
                 "samples": len(sm), "reasons": sorted(reasons), "source": "nvidia-smi, 100 ms"}
 
 
+
+def _ref_layer(wl):
+    """The workload's layer on the host for the reference CPU code (seeded
+    torch CPU generator, N(0, 0.02) weights)."""
+    import torch
+    pkg = _pkg()
+    g = torch.Generator().manual_seed(wl["seed"])
+    d, ff, E = wl["d"], wl["ff"], wl["E"]
+    mk = lambda *s: (torch.randn(*s, generator=g) * 0.02).numpy()  # noqa: E731
+    layer = pkg.LayerWeights(mk(E, d), [mk(ff, d) for _ in range(E)],
+                             [mk(ff, d) for _ in range(E)], [mk(d, ff) for _ in range(E)])
+    x = torch.randn(wl["T"], d, generator=g).numpy()
+    return layer, x
+
+
+def _load_reference(host_layer, threads):
+    """The reference's PhiMoE (oracle/_ref) loaded with this layer through a
+    RAM-backed model.bin; (None, 0) when it was not built."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # checker / baseline only
+    pkg = _pkg()
+    if not oracle.Reference.available(host_layer.E):
+        return None, 0
+    ref = oracle.Reference(host_layer.E)
+    cores = ref.set_threads(threads)
+    fd = os.memfd_create("moe_model_bin", 0)
+    path = f"/proc/self/fd/{fd}"
+    try:
+        pkg.write_model_bin(path, [host_layer])
+        ref.load(path, 0)
+    finally:
+        os.close(fd)
+    return ref, cores
+
+
+def _ref_sample(cores, T):
+    # The reference parallelises each expert's matmuls over that expert's
+    # rows (OpenMP), so a sample of 4 tokens per core gives every core about
+    # one row per expert at top-2 of 8 experts; fewer tokens leave cores idle.
+    return int(min(T, max(8, 4 * cores)))
+
+
 def cpu_reference_tokens_per_s(host_layer, x_host, threads: int):
     """Time the reference's own PhiMoE::forward on a bounded token sample.
     Returns (tokens/s, kind, tokens in the sample, threads used)."""
     sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
     import oracle  # checker / baseline only
-    pkg = _pkg()
-    E = host_layer.E
-    if oracle.Reference.available(E):
-        ref = oracle.Reference(E)
-        cores = ref.set_threads(threads)
-        fd = os.memfd_create("moe_model_bin", 0)
-        path = f"/proc/self/fd/{fd}"
-        try:
-            pkg.write_model_bin(path, [host_layer])
-            ref.load(path, 0)
-        finally:
-            os.close(fd)
-        run = ref.forward
-        kind = "reference"
+    ref, cores = _load_reference(host_layer, threads)
+    if ref is not None:
+        run, kind = ref.forward, "reference"
     else:
         orc = oracle.Oracle()
         cores = threads
         run = lambda xs: orc.moe_forward(xs, host_layer, 2, oracle.POLICY_PHI, nthreads=threads)[0]  # noqa: E731
         kind = "port"
-        ref = None
-    # The reference parallelises each expert's matmul over its rows, so the
-    # sample carries ~4 tokens per core (about one row per core per expert
-    # at top-2 of 8); the per-token work is fixed, so its time is bounded.
-    n = int(min(len(x_host), max(8, 4 * cores)))
+    n = _ref_sample(cores, len(x_host))
     t = time.perf_counter()
     run(x_host[:n])
     dt = time.perf_counter() - t
@@ -231,44 +301,24 @@ def cpu_reference_tokens_per_s(host_layer, x_host, threads: int):
 
 
 def reference_arm(args, wl):
-    """bench.py --impl reference: the reference's own CPU MoE layer (rank 0)."""
+    """bench.py --impl reference: the reference's own CPU MoE layer (rank 0
+    only; other ranks exit without work)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    import numpy as np
-    import torch
-    pkg = _pkg()
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle
-    g = torch.Generator().manual_seed(wl["seed"])
-    d, ff, E = wl["d"], wl["ff"], wl["E"]
-    std = 0.02
-    mk = lambda *s: (torch.randn(*s, generator=g) * std).numpy()  # noqa: E731
-    layer = pkg.LayerWeights(mk(E, d), [mk(ff, d) for _ in range(E)],
-                             [mk(ff, d) for _ in range(E)], [mk(d, ff) for _ in range(E)])
-    x = torch.randn(wl["T"], d, generator=g).numpy()
+    layer, x = _ref_layer(wl)
     threads = len(os.sched_getaffinity(0))
-    if not oracle.Reference.available(E):
+    ref, cores = _load_reference(layer, threads)
+    if ref is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "oracle/_ref was not built (reference sources absent at build time)"}))
         return 0
-    ref = oracle.Reference(E)
-    cores = ref.set_threads(threads)
-    fd = os.memfd_create("moe_model_bin", 0)
-    try:
-        pkg.write_model_bin(f"/proc/self/fd/{fd}", [layer])
-        ref.load(f"/proc/self/fd/{fd}", 0)
-    finally:
-        os.close(fd)
-    # Size each step so the whole run stays within ~3 minutes.
-    n0 = max(1, min(wl["T"], cores))
-    t = time.perf_counter()
-    ref.forward(x[:n0])
-    rate = n0 / (time.perf_counter() - t)
-    per_step = 150.0 / max(1, args.steps + args.warmup)
-    n = int(max(1, min(wl["T"], rate * per_step)))
+    n = _ref_sample(cores, wl["T"])
+    # Warm-up steps run one token (they only page the code and the first
+    # experts in); each timed step runs the n-token sample.
     for _ in range(args.warmup):
-        ref.forward(x[:n])
+        ref.forward(x[:1])
     times = []
     for _ in range(args.steps):
         t = time.perf_counter()
@@ -277,14 +327,15 @@ def reference_arm(args, wl):
     ref.close()
     ms = 1e3 * sum(times) / len(times)
     value = n / (ms / 1e3)
-    sample = (f"{n} of the workload's {wl['T']} tokens per step through the reference's "
-              f"PhiMoE::forward (its quantised top-2 router; same per-token work)")
+    sample = (f"{n} of the workload's {wl['T']} tokens per timed step ({n // max(cores, 1)} per "
+              f"core) through the reference's PhiMoE::forward, {cores} OpenMP threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded torch CPU generator, N(0,0.02) weights, N(0,1) x)",
-        "config": {k: wl[k] for k in ("workload", "T", "d", "ff", "E", "k", "seed")},
+        "config": _config(wl, args, world),
+        "router_difference": ROUTER_NOTE,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores,
                          "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -325,7 +376,9 @@ def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=Fa
             ptrs["w1"].append(t(rnd(ff, d)))
             ptrs["w3"].append(t(rnd(ff, d)))
             ptrs["w2"].append(t(rnd(d, ff)))
-    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
+    # BASELINE config 4 names no precision: bf16, or 3xTF32 when that is the headline.
+    dprec = "3xtf32" if args.precision == "3xtf32" else "bf16"
+    prec = pkg.PREC_FP32 if dprec == "3xtf32" else pkg.PREC_BF16
     bmax = max(c["batches"])
     m = pkg.MoeDecoder(n_heads=c["heads"], head_dim=c["hd"], top_k=k, precision=prec,
                        max_batch=bmax, max_seq=c["prompt"] + c["new"], device=dev.index,
@@ -334,7 +387,7 @@ def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=Fa
     torch.cuda.empty_cache()
     prompt = pkg.synthetic_prompt(c["seed"], bmax, c["prompt"], V)
     hbm = _peaks()[0]
-    wb = 2 if args.precision == "bf16" else 4
+    wb = 4 if dprec == "3xtf32" else 2
     out = {}
     for B in c["batches"]:
         p = np.ascontiguousarray(prompt[:B])
@@ -380,7 +433,7 @@ def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=Fa
     m.close()
     return {"workload": c["workload"], "n_layers": L, "d_model": d, "heads": c["heads"],
             "head_dim": c["hd"], "vocab": V, "experts": E, "top_k": k, "d_ff": ff,
-            "prompt": c["prompt"], "new_tokens": c["new"], "precision": args.precision,
+            "prompt": c["prompt"], "new_tokens": c["new"], "precision": dprec,
             "seed": c["seed"], "by_batch": out,
             "how": "moe_decoder_generate (KV-cached greedy decode); prefill/decode from CUDA "
                    "events on the decoder's stream, e2e = host clock around the call; decode "
@@ -400,7 +453,7 @@ def decoder_only(args):
     print(json.dumps({
         "metric": "toy MoE decoder tokens/s (BASELINE config 4)", "value": b16["decode_tokens_per_s"],
         "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
-        "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
+        "dtype": dec["precision"],
         "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights; uniform prompt ids)",
         "config": {"workload": C4["workload"], "batch": max(C4["batches"]),
                    "prompt": C4["prompt"], "new_tokens": dec["new_tokens"]},
@@ -408,17 +461,24 @@ def decoder_only(args):
     return 0
 
 
+def _ep_transport(args, pkg):
+    return pkg.EP_TRANSPORT_NCCL if args.ep_transport == "nccl" else pkg.EP_TRANSPORT_P2P
+
+
 def run_ep(args, wl, pkg, world, rank, local):
-    """N > 1, expert parallel: each rank holds E/N experts and its own T
-    tokens; dispatch and combine are NCCL exchanges over NVLink (weak scaling:
-    tokens per GPU fixed)."""
-    import numpy as np
+    """N > 1, expert parallel: each rank holds E/N experts (round-robin) and
+    its own T tokens (weak scaling: tokens per GPU fixed).  Default
+    transport: the deduplicated fused one -- one row per (token, destination
+    rank) stored into the destination's receive buffer over NVLink, the
+    rank's expert outputs summed there in ascending expert order, one row
+    stored back, flags in peer memory, no NCCL call per step; --ep-transport
+    nccl: NCCL send/recv exchanges."""
     import torch
     import torch.distributed as dist
     T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
     if E % world:
         raise SystemExit(f"{E} experts do not split over {world} GPUs")
-    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
+    mode = PRECISIONS[args.precision]
     dev = torch.device("cuda", local)
     obj = [pkg.ep_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
@@ -440,9 +500,8 @@ def run_ep(args, wl, pkg, world, rank, local):
         rank, world, obj[0], d=d, ff=ff, E=E, wg=wg.data_ptr(), w1=[ptr(t) for t in w1],
         w3=[ptr(t) for t in w3], w2=[ptr(t) for t in w2], device_pointers=True, top_k=k,
         bias=rbias.data_ptr() if rbias is not None else None,
-        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec, device=local, max_tokens=T,
-        gemm_variant=_gemm_variant(args, pkg),
-        ep_transport=pkg.EP_TRANSPORT_NCCL if args.ep_transport == "nccl" else pkg.EP_TRANSPORT_P2P)
+        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=mode["prec"], device=local, max_tokens=T,
+        gemm_variant=_gemm_variant(args, pkg), ep_transport=_ep_transport(args, pkg))
     del w1, w3, w2
     torch.cuda.empty_cache()
     xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
@@ -504,50 +563,292 @@ def run_ep(args, wl, pkg, world, rank, local):
     ms = float(t[0]) / args.steps
     e2e_ms = float(t[1])
     if rank == 0:
-        hbm, bf16_peak, bf16_sust, src = _peaks()
+        hbm, bf16_peak, _, src = _peaks()
         flops = 6.0 * T * k * d * ff          # expert FLOPs per rank (average routed rows)
         achieved = flops / (ms / 1e3) / 1e12
         print(json.dumps({
             "metric": METRIC, "value": world * T / (ms / 1e3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
+            "dtype": mode["dtype"],
             "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
-            "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
-                       "experts": E, "top_k": k,
-                       "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
-                       "precision": args.precision, "seed": wl["seed"],
-                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                       "parallelism": f"ep{world} (expert parallel, {El} experts per GPU placed round-robin, " + (
-                           "NCCL send/recv dispatch and combine)" if args.ep_transport == "nccl"
-                           else "fused dispatch/combine: NVLink peer stores from the permute "
-                                "kernel and the down-GEMM epilogue)")},
-            "roofline": {"kernel": "whole expert-parallel step (exchanges included)",
-                         "bound": "tensor", "achieved": achieved, "peak": bf16_sust,
-                         "unit": "TFLOP/s", "frac": achieved / bf16_sust,
-                         "frac_of_burst_peak": achieved / bf16_peak, "traffic": None,
-                         "peak_source": f"{src} bf16 dense, sustained (burst {bf16_peak})"},
-            "stages_ms_rank0": {nm: float(v) for nm, v in zip(pkg.PROFILE_STAGES, ep_stages)},
-            "expert_load": {"rows_max_rank": rows_max, "rows_mean_rank": rows_mean,
-                            "imbalance": rows_max / max(rows_mean, 1.0)},
+            "config": _config(wl, args, world),
+            "roofline": {"kernel": "whole expert-parallel step (exchanges included), per GPU",
+                         "bound": "tensor", "achieved": achieved, "peak": bf16_peak,
+                         "unit": "TFLOP/s", "frac": achieved / bf16_peak,
+                         "frac_of_mode_ceiling": achieved * mode["passes"] / bf16_peak,
+                         "traffic": None, "peak_source": f"{src} dense bf16, burst",
+                         "stages_ms_rank0": {nm: round(float(v), 4) for nm, v in
+                                             zip(pkg.PROFILE_STAGES, ep_stages)},
+                         "expert_load": {"rows_max_rank": rows_max, "rows_mean_rank": rows_mean,
+                                         "imbalance": rows_max / max(rows_mean, 1.0)}},
             "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * d * 4, "d2h_bytes_per_step": T * d * 4,
                     "how": "pinned host x -> device -> moe_ep_forward_device -> pinned host y, "
                            "CUDA events, max over ranks"},
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 9 * args.steps,
             "clocks": clocks,
         }))
     layer.close()
     return 0
 
 
+def _timed(fn, n, warmup, flush, stream):
+    """Mean device ms of fn over n calls (CUDA events on `stream`, L2
+    flushed between calls outside the events), after `warmup` calls."""
+    import torch
+    for _ in range(warmup):
+        fn()
+        flush.zero_()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        flush.zero_()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / n
+
+
+def _stages(layer, fn, n, flush):
+    """Per-stage device ms of fn averaged over n profiled calls (the stage
+    events sit between the kernels and turn dependent launches off, so only
+    their shares are applied to the timed, unprofiled steps)."""
+    import numpy as np
+    import torch
+    pkg = _pkg()
+    layer.profile(True)
+    st = np.zeros(len(pkg.PROFILE_STAGES))
+    for _ in range(n):
+        fn()
+        st += layer.stage_ms()
+        flush.zero_()
+    torch.cuda.synchronize()
+    layer.profile(False)
+    return st / n
+
+
+def measure_mode(args, wl, pkg, name, wptrs, x, y, flush, stream, decode_T, host_e2e):
+    """One precision mode on this GPU: the timed prefill steps, the stage
+    shares, the config-3 decode sweep and (headline mode) the host-buffer
+    e2e.  Returns (numbers, layer handle)."""
+    import numpy as np
+    import torch
+    mode = PRECISIONS[name]
+    T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
+    layer = pkg.MoeLayer.from_device_pointers(
+        d, ff, E, wptrs["wg"], wptrs["w1"], wptrs["w3"], wptrs["w2"], wptrs["bias"], top_k=k,
+        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=mode["prec"], device=x.device.index,
+        max_tokens=T, decode_max_tokens=args.decode_max_tokens,
+        gemm_variant=_gemm_variant(args, pkg))
+    layer.profile(False)
+    sp = stream.cuda_stream
+
+    def step():
+        layer.forward_device(x.data_ptr(), y.data_ptr(), T, sp)
+
+    ms = _timed(step, args.steps, args.warmup, flush, stream)
+    st = _stages(layer, step, max(3, args.steps // 5), flush)
+    share = dict(zip(pkg.PROFILE_STAGES, st / max(st.sum(), 1e-9)))
+    _, bf16_peak, _, _ = _peaks()
+    gu_ms = ms * share["gateup_gemm"]
+    dn_ms = ms * share["down_gemm"]
+    gu_tf = 4.0 * T * k * d * ff / (gu_ms / 1e3) / 1e12
+    layer_tf = 6.0 * T * k * d * ff / (ms / 1e3) / 1e12
+    out = {"tokens_per_s": T / (ms / 1e3), "ms_per_step": ms,
+           "gateup_ms": gu_ms, "down_ms": dn_ms,
+           "gateup_tflops": gu_tf, "gateup_frac": gu_tf / bf16_peak,
+           "layer_tflops": layer_tf, "layer_frac": layer_tf / bf16_peak,
+           "tc_passes": mode["passes"],
+           "stage_share": {n: round(float(v), 4) for n, v in share.items() if v > 0}}
+    if host_e2e:
+        import ctypes
+        xh = x.cpu().pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        xn, yn = xh.numpy(), yh.numpy()
+        lib = pkg.load_library()
+        fp = ctypes.POINTER(ctypes.c_float)
+        xp, yp = xn.ctypes.data_as(fp), yn.ctypes.data_as(fp)
+        for _ in range(args.warmup):
+            pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
+        n = max(3, args.steps // 2)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
+        out["e2e_tokens_per_s"] = T / ((time.perf_counter() - t0) / n)
+        out["output_finite"] = bool(np.isfinite(yn).all())
+    dec = {}
+    hbm = _peaks()[0]
+    wbytes = 2 if name == "bf16" else 4
+    for td in decode_T:
+        xt, yt = x[:td], y[:td]
+        fn = lambda: layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)  # noqa: E731
+        ms_d = _timed(fn, max(5, args.steps), args.warmup, flush, stream)
+        active = int((layer.expert_counts() > 0).sum())
+        alg = active * 3 * d * ff * wbytes + E * d * 4 + 2 * td * d * 4
+        gbs = alg / (ms_d / 1e3) / 1e9
+        dec[str(td)] = {"ms": round(ms_d, 4), "gbs": round(gbs, 1), "frac": round(gbs / hbm, 3),
+                        "path": "decode" if td <= layer.cfg.decode_max_tokens else "gemm"}
+    out["decode"] = dec
+    return out, layer
+
+
+def run_single(args, wl, pkg, world, rank, local):
+    """N = 1 (or token-sharded replicas): the headline precision and the other
+    modes on this GPU, the decoder-layer block, the toy decoder, the CPU
+    baseline."""
+    import torch
+    import torch.distributed as dist
+    T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
+    rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
+    wg, rbias = _router_weights(wl, gen, dev)
+    w1 = [rnd(ff, d) for _ in range(E)]
+    w3 = [rnd(ff, d) for _ in range(E)]
+    w2 = [rnd(d, ff) for _ in range(E)]
+    wptrs = {"wg": wg.data_ptr(), "w1": [t.data_ptr() for t in w1],
+             "w3": [t.data_ptr() for t in w3], "w2": [t.data_ptr() for t in w2],
+             "bias": rbias.data_ptr() if rbias is not None else None}
+    host_layer = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_layer = pkg.LayerWeights(wg.cpu().numpy(), [t.cpu().numpy() for t in w1],
+                                      [t.cpu().numpy() for t in w3], [t.cpu().numpy() for t in w2])
+    xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
+    x = torch.randn(T, d, generator=xgen, device=dev)
+    y = torch.empty_like(x)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    decode_T = [] if args.no_decode else [t for t in DECODE_T if t <= T]
+    names = [args.precision] + [m for m in args.modes.split(",") if m and m != args.precision]
+    if world > 1:
+        dist.barrier()
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+    time.sleep(0.3)
+    modes, head_layer = {}, None
+    for i, nm in enumerate(names):
+        res, layer = measure_mode(args, wl, pkg, nm, wptrs, x, y, flush, stream, decode_T,
+                                  host_e2e=(i == 0))
+        modes[nm] = res
+        if i == 0:
+            head_layer = layer
+        else:
+            layer.close()
+    del w1, w3, w2
+    torch.cuda.empty_cache()
+    head = modes[args.precision]
+
+    # The decoder layer's MoE half: y = x + MoE(layer_norm(x)), the norm
+    # fused into the router and the dispatch permute, the residual into the
+    # ordered combine; and the standalone bit-exact LayerNorm.
+    block = {}
+    sp = stream.cuda_stream
+    if not args.no_block:
+        nw, nb = pkg.synthetic_post_norm(wl["seed"], d)
+        head_layer.set_post_norm(nw, nb)
+        wd, bd = torch.from_numpy(nw).to(dev), torch.from_numpy(nb).to(dev)
+        yb = torch.empty_like(x)
+        nb_steps = max(5, args.steps // 2)
+        for tb in sorted({T, 1}):
+            ms_b = _timed(lambda: head_layer.block_forward_device(x.data_ptr(), yb.data_ptr(), tb,
+                                                                  sp), nb_steps, args.warmup,
+                          flush, stream)
+            block[str(tb)] = {"ms": round(ms_b, 4), "tokens_per_s": tb / (ms_b / 1e3)}
+        block[str(T)]["overhead_ms_vs_moe_forward"] = block[str(T)]["ms"] - head["ms_per_step"]
+        ms_ln = _timed(lambda: pkg.layer_norm_device(x.data_ptr(), wd.data_ptr(), bd.data_ptr(),
+                                                     1e-5, T, d, yb.data_ptr(), sp), nb_steps,
+                       args.warmup, flush, stream)
+        ln_bytes = 2 * T * d * 4
+        block["layer_norm_device"] = {"T": T, "ms": round(ms_ln, 4),
+                                      "frac_of_hbm": ln_bytes / (ms_ln / 1e3) / 1e9 / _peaks()[0]}
+    head_layer.close()
+
+    decoder = None
+    if not args.no_decoder and world == 1:
+        decoder = run_decoder(args, pkg, dev)
+    clocks = sampler.stop()
+
+    ms, e2e_tps = head["ms_per_step"], head["e2e_tokens_per_s"]
+    if world > 1:
+        t = torch.tensor([ms, T / e2e_tps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_s = float(t[0]), float(t[1])
+        e2e_tps = T / e2e_s
+    if rank != 0:
+        return 0
+    hbm, bf16_peak, _, src = _peaks()
+    mode = PRECISIONS[args.precision]
+    roofline = {
+        "kernel": f"gate/up grouped GEMM (tcgen05, SwiGLU epilogue), {args.precision}",
+        "bound": "tensor", "achieved": head["gateup_tflops"], "peak": bf16_peak,
+        "unit": "TFLOP/s", "frac": head["gateup_frac"],
+        "frac_of_mode_ceiling": head["gateup_frac"] * mode["passes"],
+        "traffic": _traffic_from_profile(wl["workload"], args.precision),
+        "peak_source": f"{src} dense bf16, burst (the GEMM runs ~1-10 ms per step)",
+        "how": "achieved = 4*T*k*d*ff / (timed step ms x the GEMM's share of a profiled step); "
+               "frac counts algorithmic FLOPs once (fp32-faithful modes: ceiling 1/passes)",
+        "modes": {nm: {key: (round(v, 4) if isinstance(v, float) else v)
+                       for key, v in r.items() if key not in ("decode", "stage_share")}
+                  for nm, r in modes.items()},
+        "decode": {"hbm_peak_gbs": hbm,
+                   "bytes": "routed experts x 3 x d x d_ff x weight bytes + router + x/y",
+                   **{nm: {t: [v["path"], v["ms"], v["frac"]] for t, v in r["decode"].items()}
+                      for nm, r in modes.items() if r["decode"]}},
+    }
+    if decoder is not None:
+        roofline["decoder"] = {
+            f"batch{b}": {"decode_ms_per_step": round(v["decode_ms_per_step"], 4),
+                          "decode_tokens_per_s": round(v["decode_tokens_per_s"], 1),
+                          "decode_frac_of_hbm": round(v["decode_frac_of_hbm"], 3),
+                          "prefill_ms": round(v["prefill_ms"], 3)}
+            for b, v in decoder["by_batch"].items()}
+    line = {
+        "metric": METRIC, "value": world * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": mode["dtype"],
+        "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
+        "config": _config(wl, args, world),
+        "stages_share": head["stage_share"],
+        "block": block,
+        "decoder": decoder,
+        "gpu_launches": KERNELS_PER_FORWARD * args.steps,
+        "output_finite": head.get("output_finite"),
+        "e2e": {"value": world * e2e_tps, "unit": "tokens/s", "h2d_bytes_per_step": T * d * 4,
+                "d2h_bytes_per_step": T * d * 4,
+                "how": "moe_forward_host on pinned host buffers, host clock around the "
+                       "synchronous call"},
+        "clocks": clocks,
+        "roofline": roofline,
+    }
+    if host_layer is not None:
+        xs = x[: min(T, 1024)].cpu().numpy()
+        tps, kind, n, cores = cpu_reference_tokens_per_s(host_layer, xs,
+                                                         len(os.sched_getaffinity(0)))
+        line["cpu_baseline"] = {
+            "value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{n} tokens of this layer through PhiMoE::forward (fp32, "
+                      f"its quantised top-2 router), {cores} OpenMP threads"}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--precision", choices=sorted(PRECISIONS), default="bf16x3",
+                    help="headline precision: bf16x3 (fp32-faithful, default), 3xtf32 "
+                         "(fp32-faithful) or bf16")
+    ap.add_argument("--modes", default="bf16",
+                    help="other precisions measured on one GPU besides the headline, "
+                         "comma-separated (reported under roofline.modes)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c4"], default="c2",
                     help="c2 (default, the headline layer), c2small, c5, or c4: only the toy "
                          "MoE decoder (BASELINE config 4), one GPU")
@@ -557,8 +858,8 @@ def main():
                     help="grouped-GEMM tiling: auto (2-CTA 256x256 tiles for prefill, 1-CTA "
                          "128x256 for decode-sized T), or force one")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
-                    help="expert-parallel exchange: fused NVLink peer stores (default) or NCCL "
-                         "send/recv")
+                    help="expert-parallel exchange: the deduplicated NVLink peer-store "
+                         "transport (default) or NCCL send/recv")
     ap.add_argument("--parallelism", choices=["ep", "dp"], default="ep",
                     help="N > 1: expert parallel (default) or token-sharded replicas")
     ap.add_argument("--no-block", action="store_true",
@@ -576,13 +877,15 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    for m in args.modes.split(","):
+        if m and m not in PRECISIONS:
+            ap.error(f"unknown mode {m}")
     if args.workload == "c4":
         return decoder_only(args)
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         return reference_arm(args, wl)
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -600,255 +903,12 @@ def main():
     pkg = _pkg()
     if world > 1 and args.parallelism == "ep":
         rc = run_ep(args, wl, pkg, world, rank, local)
-        dist.barrier()
-        dist.destroy_process_group()
-        return rc
-    prec = pkg.PREC_BF16 if args.precision == "bf16" else pkg.PREC_FP32
-    T, d, ff, E, k = wl["T"], wl["d"], wl["ff"], wl["E"], wl["k"]
-
-    # ---- synthetic layer, drawn on the device (same weights on every rank)
-    gen = torch.Generator(device="cuda").manual_seed(wl["seed"])
-    dev = torch.device("cuda", local)
-    rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
-    wg, rbias = _router_weights(wl, gen, dev)
-    w1 = [rnd(ff, d) for _ in range(E)]
-    w3 = [rnd(ff, d) for _ in range(E)]
-    w2 = [rnd(d, ff) for _ in range(E)]
-    layer = pkg.MoeLayer.from_device_pointers(
-        d, ff, E, wg.data_ptr(), [t.data_ptr() for t in w1], [t.data_ptr() for t in w3],
-        [t.data_ptr() for t in w2], rbias.data_ptr() if rbias is not None else None, top_k=k,
-        policy=pkg.ROUTER_SOFTMAX_TOPK, precision=prec,
-        device=local, max_tokens=T, decode_max_tokens=args.decode_max_tokens,
-        gemm_variant=_gemm_variant(args, pkg))
-    host_layer = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        host_layer = pkg.LayerWeights(wg.cpu().numpy(), [t.cpu().numpy() for t in w1],
-                                      [t.cpu().numpy() for t in w3], [t.cpu().numpy() for t in w2])
-    del w1, w3, w2
-    torch.cuda.empty_cache()
-    xgen = torch.Generator(device="cuda").manual_seed(wl["seed"] * 1000 + 17 + rank)
-    x = torch.randn(T, d, generator=xgen, device=dev)
-    y = torch.empty_like(x)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-    # Timed passes run with the stage timers off (their events would sit
-    # between the kernels and keep dependent launches from overlapping); a
-    # separate short profiled pass gives the per-stage breakdown.
-    layer.profile(False)
-
-    def profiled_stages(fn, n):
-        layer.profile(True)
-        st_p = np.zeros(len(pkg.PROFILE_STAGES))
-        for _ in range(n):
-            fn()
-            st_p += layer.stage_ms()
-            flush.zero_()
-        torch.cuda.synchronize()
-        layer.profile(False)
-        return st_p / n
-
-    def step():
-        layer.forward_device(x.data_ptr(), y.data_ptr(), T, sp)
-
-    for _ in range(args.warmup):
-        step()
-        flush.zero_()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    uuid = str(torch.cuda.get_device_properties(local).uuid)
-    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-    time.sleep(0.3)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
-    for i in range(args.steps):
-        ev[i][0].record(stream)
-        step()
-        ev[i][1].record(stream)
-        flush.zero_()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    total_ms = sum(a.elapsed_time(b) for a, b in ev)
-    stages = profiled_stages(step, max(3, args.steps // 5))
-
-    # ---- decode: the same layer at T in DECODE_T, HBM GB/s
-    decode = {}
-    if not args.no_decode:
-        hbm = _peaks()[0]
-        dec_T = [t for t in DECODE_T if t <= T]
-        for td in dec_T:
-            xt = x[:td]
-            yt = y[:td]
-            for _ in range(args.warmup):
-                layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)
-                flush.zero_()
-            torch.cuda.synchronize()
-            tot, n = 0.0, max(5, args.steps)
-            for _ in range(n):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp)
-                b.record(stream)
-                flush.zero_()
-                b.synchronize()
-                tot += a.elapsed_time(b)
-            ms_d = tot / n
-            st_d = profiled_stages(
-                lambda: layer.forward_device(xt.data_ptr(), yt.data_ptr(), td, sp), 5)
-            active = int((layer.expert_counts() > 0).sum())
-            wbytes = 2 if args.precision == "bf16" else 4
-            alg = active * 3 * d * ff * wbytes + E * d * 4 + 2 * td * d * 4
-            gbs = alg / (ms_d / 1e3) / 1e9
-            path = "decode kernels" if td <= layer.cfg.decode_max_tokens else "grouped GEMM"
-            decode[str(td)] = {"ms": ms_d, "tokens_per_s": td / (ms_d / 1e3),
-                               "experts_streamed": active, "algorithmic_bytes": alg,
-                               "hbm_gbs": gbs, "frac_of_hbm": gbs / hbm, "path": path,
-                               "stages_ms": {nm: float(v)
-                                             for nm, v in zip(pkg.PROFILE_STAGES, st_d)}}
-
-    # ---- the decoder layer's MoE half: y = x + MoE(layer_norm(x)), the norm
-    # fused into the router and the dispatch permute, the residual after the
-    # combine; and the standalone bit-exact LayerNorm (read x, write y).
-    block = {}
-    if not args.no_block:
-        nw, nb = pkg.synthetic_post_norm(wl["seed"], d)
-        layer.set_post_norm(nw, nb)
-        wd, bd = torch.from_numpy(nw).to(dev), torch.from_numpy(nb).to(dev)
-        yb = torch.empty_like(x)
-
-        def timed(fn, n):
-            for _ in range(args.warmup):
-                fn()
-                flush.zero_()
-            torch.cuda.synchronize()
-            tot = 0.0
-            for _ in range(n):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                fn()
-                b.record(stream)
-                flush.zero_()
-                b.synchronize()
-                tot += a.elapsed_time(b)
-            return tot / n, profiled_stages(fn, 3)
-
-        nb_steps = max(5, args.steps // 2)
-        for tb in sorted({T, 1}):
-            ms_b, st_b = timed(lambda: layer.block_forward_device(x.data_ptr(), yb.data_ptr(), tb,
-                                                                  sp), nb_steps)
-            block[str(tb)] = {"ms": ms_b, "tokens_per_s": tb / (ms_b / 1e3),
-                              "stages_ms": {nm: float(v)
-                                            for nm, v in zip(pkg.PROFILE_STAGES, st_b)}}
-        block[str(T)]["overhead_ms_vs_moe_forward"] = block[str(T)]["ms"] - total_ms / args.steps
-        ms_ln, _ = timed(lambda: pkg.layer_norm_device(x.data_ptr(), wd.data_ptr(), bd.data_ptr(),
-                                                       1e-5, T, d, yb.data_ptr(), sp), nb_steps)
-        ln_bytes = 2 * T * d * 4
-        block["layer_norm_device"] = {"T": T, "ms": ms_ln, "algorithmic_bytes": ln_bytes,
-                                      "gbs": ln_bytes / (ms_ln / 1e3) / 1e9,
-                                      "frac_of_hbm": ln_bytes / (ms_ln / 1e3) / 1e9 / _peaks()[0]}
-
-    # ---- the toy MoE decoder, end to end
-    decoder = None
-    if not args.no_decoder and world == 1:
-        decoder = run_decoder(args, pkg, dev)
-
-    # ---- e2e through the host-buffer C-ABI call (pinned buffers)
-    xh = x.cpu().pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
-    xn, yn = xh.numpy(), yh.numpy()
-    import ctypes
-    lib = pkg.load_library()
-    fp = ctypes.POINTER(ctypes.c_float)
-    xp, yp = xn.ctypes.data_as(fp), yn.ctypes.data_as(fp)
-    for _ in range(args.warmup):
-        pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
-    e2e_steps = max(3, args.steps // 2)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        pkg._check(lib.moe_forward_host(layer._h, xp, yp, T))
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    clocks = sampler.stop()
-    ok_y = bool(torch.isfinite(torch.from_numpy(yn)).all())
-
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_s = float(t[0]), float(t[1])
-    ms = total_ms / args.steps
-    value = world * T / (ms / 1e3)
-    e2e = world * T / e2e_s
-
-    if rank == 0:
-        hbm, bf16_peak, bf16_sust, src = _peaks()
-        st = stages
-        gu_ms, dn_ms = st[3], st[4]
-        gu_flops = 4.0 * T * k * d * ff
-        dn_flops = 2.0 * T * k * d * ff
-        achieved = gu_flops / (gu_ms / 1e3) / 1e12
-        traffic = _traffic_from_profile(wl["workload"], args.precision)
-        line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16" if args.precision == "bf16" else "fp32 (3xTF32 tensor cores)",
-            "data": "synthetic (seeded torch CUDA generator: N(0,0.02) weights, N(0,1) x)",
-            "config": {"workload": wl["workload"], "T_per_gpu": T, "d_model": d, "d_ff": ff,
-                       "experts": E, "top_k": k,
-                       "router": "softmax_topk_renorm" + (" + zipf bias" if wl.get("zipf") else ""),
-                       "precision": args.precision, "seed": wl["seed"], "gemm": args.gemm,
-                       "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                       "parallelism": f"dp{world} (token-sharded replicas, all experts per GPU)"},
-            # The GEMMs run back to back inside a multi-millisecond step under
-            # the 1 kW power cap, so the denominator is the measured sustained
-            # bf16 rate; the burst fraction is reported beside it.
-            "roofline": {"kernel": "gate/up grouped GEMM (tcgen05, SwiGLU epilogue)",
-                         "bound": "tensor", "achieved": achieved, "peak": bf16_sust,
-                         "unit": "TFLOP/s", "frac": achieved / bf16_sust,
-                         "frac_of_burst_peak": achieved / bf16_peak,
-                         "traffic": traffic,
-                         "peak_source": f"{src} bf16 dense, sustained (burst {bf16_peak})"},
-            "expert_gemm": {"tflops": (gu_flops + dn_flops) / ((gu_ms + dn_ms) / 1e3) / 1e12,
-                            "frac_of_sustained_peak": (gu_flops + dn_flops) / ((gu_ms + dn_ms) / 1e3)
-                            / 1e12 / bf16_sust,
-                            "frac_of_burst_peak": (gu_flops + dn_flops) / ((gu_ms + dn_ms) / 1e3)
-                            / 1e12 / bf16_peak},
-            "stages_ms": {n: float(v) for n, v in zip(pkg.PROFILE_STAGES, st)},
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * d * 4,
-                    "d2h_bytes_per_step": T * d * 4,
-                    "how": "moe_forward_host on pinned host buffers, host clock around the "
-                           "synchronous call"},
-            "decode": {"hbm_peak_gbs": _peaks()[0], "by_T": decode,
-                       "bytes": "routed experts x 3 x d x d_ff x weight bytes + router + x/y"},
-            "block": {"by_T": block,
-                      "what": "moe_block_forward_device: y = x + MoE(layer_norm(x)) "
-                              "(PhiDecoderLayer's MoE half; norm statistics bit-exact with "
-                              "tensor_ops::layer_norm, applied inside router and permute)"},
-            "decoder": decoder,
-            "gpu_launches": KERNELS_PER_FORWARD * args.steps,
-            "clocks": clocks,
-            "output_finite": ok_y,
-        }
-        if host_layer is not None:
-            xs = x[: min(T, 1024)].cpu().numpy()
-            tps, kind, n, cores = cpu_reference_tokens_per_s(host_layer, xs,
-                                                             len(os.sched_getaffinity(0)))
-            line["cpu_baseline"] = {
-                "value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
-                "sample": f"{n} tokens of this layer through PhiMoE::forward (fp32, "
-                          f"its quantised top-2 router), {cores} OpenMP threads"}
-        print(json.dumps(line))
-    layer.close()
+    else:
+        rc = run_single(args, wl, pkg, world, rank, local)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return rc
 
 
 if __name__ == "__main__":

@@ -15,8 +15,10 @@
 //   PhiMoEBlock  the MoE half of PhiDecoderLayer::forward (src/layer.cu:
 //            157-161): post-attention LayerNorm, PhiMoE, residual add, on the
 //            GPU with the norm fused into the MoE's input
-// PhiAttention and PhiDecoderLayer's attention half are not part of this
-// library's path and are not declared here.
+//   PhiAttention  src/layer.cu:105-147 on the host, with the reference's
+//            arithmetic (the attention is not on this library's GPU path)
+//   PhiDecoderLayer  src/layer.cu:149-162: input LayerNorm and attention on
+//            the host, then PhiMoEBlock on the GPU
 //
 // Layers share their device handle between copies; a handle runs one forward
 // at a time, so copies must not run forward concurrently.
@@ -97,4 +99,45 @@ public:
 private:
     std::shared_ptr<MoeHandle> h_;
     MoeConfig cfg_{};
+};
+
+// Attention geometry.  The defaults are the reference's constants
+// (include/config.h:10-19: 16 query heads, 4 KV heads of 128, sliding window
+// 2047, RoPE base 1e4, LayerNorm eps 1e-5), which its PhiAttention compiles
+// in; the overloads below take another geometry.
+struct PhiAttentionGeometry {
+    std::size_t heads = 16;
+    std::size_t kv_heads = 4;
+    std::size_t head_dim = 128;
+    std::size_t sliding_window = 2047;
+    float rope_theta = 10000.0f;
+    float norm_eps = 1.0e-5f;
+};
+
+class PhiAttention {
+public:
+    PhiAttention(const ModelLoader& loader, std::size_t layer_idx);
+    PhiAttention(const ModelLoader& loader, std::size_t layer_idx, const PhiAttentionGeometry& g);
+    void forward(const Tensor& x, Tensor& y) const;
+
+private:
+    Linear q_proj_, k_proj_, v_proj_, o_proj_;
+    PhiAttentionGeometry g_;
+};
+
+// y = h + PhiMoE(layer_norm(h)), h = x + attention(layer_norm(x)) -- the
+// reference's PhiDecoderLayer::forward with its MoE half (post-attention
+// LayerNorm, router, experts, combine, residual) on the GPU.
+class PhiDecoderLayer {
+public:
+    PhiDecoderLayer(const ModelLoader& loader, std::size_t layer_idx);
+    PhiDecoderLayer(const ModelLoader& loader, std::size_t layer_idx,
+                    const PhiAttentionGeometry& g, const MoeConfig& moe_cfg);
+    void forward(const Tensor& x, Tensor& y) const;
+
+private:
+    Tensor input_norm_weight_, input_norm_bias_;
+    PhiAttention attention_;
+    PhiMoEBlock moe_;
+    float eps_;
 };

@@ -61,10 +61,18 @@ typedef enum MoeRouterPolicy {
  *   fp32 weights through CUDA cores.  Relative L2 error vs the reference
  *   <= 1e-3.
  * BF16: weights and activations rounded to bf16 (RNE), fp32 accumulation.
- *   Relative L2 error vs the reference <= 2e-2. */
+ *   Relative L2 error vs the reference <= 2e-2.
+ * FP32_BF16X3: fp32-faithful at bf16 tensor-core rate.  Every fp32 operand x
+ *   is split into bf16 parts hi = bf16(x) and lo = bf16(x - hi) (16
+ *   significant bits together), and three bf16 MMAs (hi*hi + hi*lo + lo*hi)
+ *   accumulate into the fp32 TMEM accumulator; the dropped lo*lo term and the
+ *   split's remainder are about 2^-16 of each product.  Decode streams the
+ *   fp32 weights as in FP32.  Relative L2 error vs the reference <= 1e-3.
+ *   Not available to the toy decoder (moe_decoder_*). */
 typedef enum MoePrecision {
     MOE_PREC_FP32 = 0,
-    MOE_PREC_BF16 = 1
+    MOE_PREC_BF16 = 1,
+    MOE_PREC_FP32_BF16X3 = 2
 } MoePrecision;
 
 /* Tiling of the tcgen05 grouped expert GEMMs.
@@ -113,7 +121,9 @@ typedef struct MoeConfig {
     int32_t max_tokens;     /* workspace is pre-sized for this many tokens; grows on demand */
     int32_t gemm_variant;   /* MoeGemmVariant of the grouped expert GEMMs */
     int32_t ep_transport;   /* MoeEpTransport (expert-parallel handles only) */
-    int32_t reserved[3];
+    int32_t ep_wait_ms;     /* bound on each peer wait of the fused expert-parallel
+                               transport, in ms (0: the default, 5000) */
+    int32_t reserved[2];
 } MoeConfig;
 
 /* Host fp32 weights of one layer (the tensors PhiMoE loads by name,
@@ -321,6 +331,20 @@ int moe_ep_create_from_device(const MoeConfig* cfg, const MoeWeightsHost* weight
  * moe_destroy releases the group's communicator. */
 int moe_ep_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, void* stream);
 
+/* Failure of the fused transport.  Every peer wait is bounded
+ * (MoeConfig.ep_wait_ms).  A rank whose wait runs out marks itself failed on
+ * the device: from then on its kernels store nothing into other GPUs'
+ * buffers and raise no flags, and its own waits end at once, so no rank
+ * hangs and no late peer's rows are mixed into a later step; the other ranks'
+ * waits then run out too.  moe_ep_forward_device enqueues without host
+ * synchronisation, so it reports the failure of an earlier step
+ * (MOE_ERR_TIMEOUT) once that step has completed on the GPU; moe_ep_check
+ * waits for the last forward and reports it at once.  After MOE_ERR_TIMEOUT
+ * the handle stays failed: every later forward returns MOE_ERR_TIMEOUT
+ * without launching anything, and the group must be destroyed and created
+ * again (on every rank).  The NCCL transport reports through NCCL. */
+int moe_ep_check(MoeHandle* h);
+
 /* Dispatch that allocates nothing.  No counterpart in the reference: it
  * exists for callers that cannot call cudaMalloc -- code running inside a
  * stream capture that must not touch the allocator, frameworks that own all
@@ -333,7 +357,9 @@ int moe_ep_forward_device(MoeHandle* h, const float* x, float* y, int32_t T, voi
  * ascending order inside each block, row_token = -1 and row_weight = 0 on
  * padding rows, expert_offsets [E+1], counts [E].  All outputs are device
  * buffers; rows_cap must be >= (T * top_k / 128 + num_experts + 1) * 128.
- * Expert indices outside [0, num_experts) are not placed.
+ * Expert indices outside [0, num_experts) are not placed; an expert that one
+ * token lists twice gets two rows, in slot order (the router never does
+ * this).  T == 0 writes zero counts and offsets.
  *
  * Its only scratch is a fixed 1 MiB array in the library's device memory
  * (MOE_NOALLOC_SCRATCH_BYTES, present on every GPU that loads the library

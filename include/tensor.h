@@ -65,6 +65,7 @@ private:
 // reference's arithmetic: matmul_transposed is a k-ascending fused
 // multiply-add chain per output, silu uses a double-precision exp.
 namespace tensor_ops {
+void matmul(const Tensor& a, const Tensor& b, Tensor& c);              // [M,K] x [K,N]
 void matmul_transposed(const Tensor& a, const Tensor& b, Tensor& c);   // [M,K] x [N,K]
 void add_inplace(Tensor& a, const Tensor& b);
 void add_bias_inplace(Tensor& a, const Tensor& bias);
@@ -73,4 +74,12 @@ void silu(const Tensor& x, Tensor& y);
 // src/tensor.cu:174-189, with the reference build's arithmetic: serial
 // j-ascending sums, unfused variance terms, fused output expression.
 void layer_norm(const Tensor& x, const Tensor& weight, const Tensor& bias, float eps, Tensor& y);
+// Softmax over the last dimension (declared by the reference, include/
+// tensor.h:67, with no definition there): max-subtracted, exp in double.
+void softmax_last_dim(const Tensor& x, Tensor& y);
+// Rotary embedding in rotate-half form, in place, position = row
+// (src/tensor.cu:191-210): q [seq][q_heads * head_dim], k [seq][kv_heads *
+// head_dim].
+void apply_rope(Tensor& q, Tensor& k, std::size_t seq_len, std::size_t q_heads,
+                std::size_t kv_heads, std::size_t head_dim, float theta);
 }

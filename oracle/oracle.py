@@ -253,8 +253,14 @@ class ReferenceAttention:
         L.ref_attention.argtypes = [ctypes.c_char_p, ctypes.c_int, _f32p, ctypes.c_int,
                                     ctypes.c_int, _f32p, ctypes.c_int]
         L.ref_attention_heads.restype = ctypes.c_int
+        L.ref_decoder_layer.argtypes = [ctypes.c_char_p, ctypes.c_int, _f32p, ctypes.c_int,
+                                        ctypes.c_int, _f32p]
+        L.ref_apply_rope.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_float]
+        L.ref_num_experts.restype = ctypes.c_int
         L.ref_last_error.restype = ctypes.c_char_p
         self.heads = L.ref_attention_heads()
+        self.num_experts = L.ref_num_experts()
 
     @classmethod
     def available(cls) -> bool:
@@ -267,3 +273,21 @@ class ReferenceAttention:
                                   _fp(y), out_cols) != 0:
             raise RuntimeError(self.lib.ref_last_error().decode())
         return y
+
+    def decoder_layer(self, model_bin, layer, x):
+        """The reference's PhiDecoderLayer::forward (src/layer.cu:152-162)."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty_like(x)
+        if self.lib.ref_decoder_layer(str(model_bin).encode(), layer, _fp(x), x.shape[0],
+                                      x.shape[1], _fp(y)) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return y
+
+    def apply_rope(self, q, k, heads, kv_heads, head_dim, theta=10000.0):
+        """The reference's tensor_ops::apply_rope on copies of q and k."""
+        q = np.array(q, np.float32, order="C")
+        k = np.array(k, np.float32, order="C")
+        if self.lib.ref_apply_rope(_fp(q), _fp(k), q.shape[0], heads, kv_heads, head_dim,
+                                   theta) != 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return q, k

@@ -197,4 +197,22 @@ int ref_attention(const char* model_bin, int layer, const float* x, int S, int d
 
 int ref_attention_heads() { return static_cast<int>(apss26::NUM_ATTENTION_HEADS); }
 
+// PhiDecoderLayer::forward (src/layer.cu:152-162) of layer `layer` of a
+// model.bin: x [S][d] -> y [S][d] (input LayerNorm, attention, residual,
+// post-attention LayerNorm, PhiMoE, residual), with this build's config.h.
+int ref_decoder_layer(const char* model_bin, int layer, const float* x, int S, int d, float* y) {
+    try {
+        ModelLoader loader(model_bin);
+        PhiDecoderLayer dl(loader, static_cast<std::size_t>(layer));
+        Tensor xt({static_cast<std::size_t>(S), static_cast<std::size_t>(d)}), yt;
+        std::memcpy(xt.data(), x, sizeof(float) * xt.size());
+        dl.forward(xt, yt);
+        if (yt.size() != xt.size()) throw std::invalid_argument("ref_decoder_layer: output size");
+        std::memcpy(y, yt.data(), sizeof(float) * yt.size());
+        return 0;
+    } catch (const std::exception& e) {
+        return fail(e);
+    }
+}
+
 }  // extern "C"

@@ -11,10 +11,19 @@
 //       tensor_ops::layer_norm with post_attention_layernorm -> <out_prefix>.ln.bin
 //   test_phimoe block <model.bin> <x.bin> <T> <d> <out_prefix>
 //       PhiMoEBlock(loader, 0).forward(attn, y)          -> <out_prefix>.block.bin
+//   test_phimoe rope <q.bin> <k.bin> <S> <heads> <kv_heads> <head_dim> <out_prefix>   no GPU
+//       tensor_ops::apply_rope (base 1e4)                -> <out_prefix>.q.bin / .k.bin
+//   test_phimoe attention <model.bin> <x.bin> <S> <d> <heads> <kv_heads> <out_prefix>   no GPU
+//       PhiAttention(loader, 0, geometry: head_dim 128, no effective window)
+//                                                        -> <out_prefix>.attn.bin
+//   test_phimoe decoder <model.bin> <x.bin> <S> <d> <heads> <kv_heads> <out_prefix>
+//       PhiDecoderLayer(loader, 0, same geometry, the reference's MoE
+//       configuration with sizes from the file)           -> <out_prefix>.dec.bin
 #include "layer.h"
 #include "model_loader.h"
 #include "tensor.h"
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -84,6 +93,26 @@ static int errors(const std::string& dir) {
     CHECK(throws<std::invalid_argument>([&] { tensor_ops::matmul_transposed(bad, b, c); },
                                         "matmul_transposed shape"),
           "matmul shape");
+    // matmul: [M,K] x [K,N]
+    Tensor bt({4, 3}), c2({2, 3});
+    for (size_t p = 0; p < 4; ++p)
+        for (size_t j = 0; j < 3; ++j) bt.at(p, j) = b.at(j, p);
+    tensor_ops::matmul(a, bt, c2);
+    CHECK(std::memcmp(c.data(), c2.data(), c.size() * 4) == 0, "matmul == matmul_transposed");
+    CHECK(throws<std::invalid_argument>([&] { tensor_ops::matmul(a, b, c2); }, "matmul shape"),
+          "matmul inner size");
+    // softmax_last_dim: rows sum to 1, order kept, max-subtracted (large inputs finite)
+    Tensor sx({2, 3}), sy({2, 3});
+    const float vals[6] = {1.0f, 2.0f, 3.0f, 1000.0f, 1001.0f, 999.0f};
+    std::memcpy(sx.data(), vals, sizeof vals);
+    tensor_ops::softmax_last_dim(sx, sy);
+    CHECK(std::abs(sy.at(0, 0) + sy.at(0, 1) + sy.at(0, 2) - 1.0f) < 1e-6f, "softmax sums to 1");
+    CHECK(sy.at(1, 1) > sy.at(1, 0) && sy.at(1, 0) > sy.at(1, 2), "softmax order");
+    CHECK(std::abs(sy.at(0, 2) - sy.at(1, 1)) < 1e-6f, "softmax shift invariance");
+    Tensor q1({1, 4}), k1({1, 4});
+    CHECK(throws<std::invalid_argument>(
+              [&] { tensor_ops::apply_rope(q1, k1, 1, 1, 1, 3, 10000.0f); }, "apply_rope shape"),
+          "apply_rope odd head_dim");
     std::printf("%s\n", failures ? "errors: FAILED" : "errors: ok");
     return failures ? 1 : 0;
 }
@@ -169,6 +198,55 @@ static int block(const std::string& model, const std::string& xpath, size_t T, s
     return failures ? 1 : 0;
 }
 
+static Tensor read_mat(const std::string& path, size_t rows, size_t cols) { return read_x(path, rows, cols); }
+
+static PhiAttentionGeometry test_geometry(size_t heads, size_t kv_heads) {
+    PhiAttentionGeometry g;
+    g.heads = heads;
+    g.kv_heads = kv_heads;
+    g.head_dim = 128;
+    g.sliding_window = 1000000;   // beyond any test sequence
+    return g;
+}
+
+static int rope(const std::string& qp, const std::string& kp, size_t S, size_t H, size_t KVH,
+                size_t hd, const std::string& out) {
+    Tensor q = read_mat(qp, S, H * hd), k = read_mat(kp, S, KVH * hd);
+    tensor_ops::apply_rope(q, k, S, H, KVH, hd, 10000.0f);
+    write_file(out + ".q.bin", q.data(), q.size() * 4);
+    write_file(out + ".k.bin", k.data(), k.size() * 4);
+    std::printf("rope: ok\n");
+    return 0;
+}
+
+static int attention(const std::string& model, const std::string& xpath, size_t S, size_t d,
+                     size_t H, size_t KVH, const std::string& out) {
+    ModelLoader loader(model);
+    PhiAttention att(loader, 0, test_geometry(H, KVH));
+    const Tensor x = read_x(xpath, S, d);
+    Tensor y;
+    att.forward(x, y);
+    write_file(out + ".attn.bin", y.data(), y.size() * 4);
+    std::printf("attention: ok\n");
+    return 0;
+}
+
+static int decoder(const std::string& model, const std::string& xpath, size_t S, size_t d,
+                   size_t H, size_t KVH, const std::string& out) {
+    ModelLoader loader(model);
+    MoeConfig cfg;
+    moe_config_init(&cfg);              // the reference's router and precision
+    cfg.d_model = cfg.d_ff = cfg.num_experts = 0;   // sizes from the file
+    PhiDecoderLayer layer(loader, 0, test_geometry(H, KVH), cfg);
+    const Tensor x = read_x(xpath, S, d);
+    Tensor y;
+    layer.forward(x, y);
+    CHECK(y.ndim() == 2 && y.size(0) == S && y.size(1) == d, "PhiDecoderLayer output shape");
+    write_file(out + ".dec.bin", y.data(), y.size() * 4);
+    std::printf("%s\n", failures ? "decoder: FAILED" : "decoder: ok");
+    return failures ? 1 : 0;
+}
+
 int main(int argc, char** argv) {
     try {
         if (argc >= 3 && std::string(argv[1]) == "errors") return errors(argv[2]);
@@ -178,6 +256,15 @@ int main(int argc, char** argv) {
             return layernorm(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
         if (argc >= 7 && std::string(argv[1]) == "block")
             return block(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]), argv[6]);
+        if (argc >= 9 && std::string(argv[1]) == "rope")
+            return rope(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]),
+                        std::stoul(argv[6]), std::stoul(argv[7]), argv[8]);
+        if (argc >= 9 && std::string(argv[1]) == "attention")
+            return attention(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]),
+                             std::stoul(argv[6]), std::stoul(argv[7]), argv[8]);
+        if (argc >= 9 && std::string(argv[1]) == "decoder")
+            return decoder(argv[2], argv[3], std::stoul(argv[4]), std::stoul(argv[5]),
+                           std::stoul(argv[6]), std::stoul(argv[7]), argv[8]);
     } catch (const std::exception& e) {
         std::fprintf(stderr, "uncaught: %s\n", e.what());
         return 2;

@@ -84,3 +84,91 @@ def test_phimoe_block_matches_reference(test_bin, tmp_path):
     assert r.returncode == 0, r.stdout + r.stderr
     y = np.fromfile(tmp_path / "out.block.bin", np.float32).reshape(T, d)
     assert rel_l2(y, g["block_phi_y"]) <= 1e-3
+
+
+# ------------------------------------------------------------ decoder layer
+# The reference's PhiAttention / PhiDecoderLayer compiled from its sources
+# with plain multi-head attention (oracle/_ref/libref_attn.so: 2 heads and 2
+# KV heads of 128, 16 experts, no effective sliding window).
+def _ref_attn():
+    orc_mod = load_oracle()
+    if not orc_mod.ReferenceAttention.available():
+        pytest.skip("reference attention library not built (reference sources absent)")
+    return orc_mod.ReferenceAttention()
+
+
+def _decoder_model(pkg, tmp_path, ref, S=17, ff=64, seed=31):
+    """One decoder layer of the reference's format: input and post-attention
+    LayerNorms, q/k/v/o projections with biases, and an MoE of the
+    reference build's expert count; returns (model path, x, d)."""
+    H, hd = ref.heads, 128
+    d = H * hd
+    g = np.random.default_rng(seed)
+    ent = []
+    for n in ("input_layernorm", "post_attention_layernorm"):
+        ent.append((f"model.layers.0.{n}.weight", (1.0 + 0.1 * g.standard_normal(d)).astype(np.float32)))
+        ent.append((f"model.layers.0.{n}.bias", (0.1 * g.standard_normal(d)).astype(np.float32)))
+    for n in ("q", "k", "v", "o"):
+        ent.append((f"model.layers.0.self_attn.{n}_proj.weight",
+                    (0.05 * g.standard_normal((d, d))).astype(np.float32)))
+        ent.append((f"model.layers.0.self_attn.{n}_proj.bias",
+                    (0.02 * g.standard_normal(d)).astype(np.float32)))
+    layer = pkg.synthetic_layer(seed, d, ff, ref.num_experts)
+    ent += pkg.layer_entries(layer, 0)
+    model = tmp_path / "dec.bin"
+    pkg.write_tensors(model, ent)
+    x = g.standard_normal((S, d)).astype(np.float32)
+    xp = tmp_path / "x.bin"
+    x.tofile(xp)
+    return model, xp, x, d, H
+
+
+def test_apply_rope_matches_reference_bits(test_bin, tmp_path):
+    """tensor_ops::apply_rope of the drop-in gives the reference's bits."""
+    ref = _ref_attn()
+    g = np.random.default_rng(3)
+    S, H, KVH, hd = 37, 4, 2, 128
+    q = g.standard_normal((S, H * hd)).astype(np.float32)
+    k = g.standard_normal((S, KVH * hd)).astype(np.float32)
+    q.tofile(tmp_path / "q.bin")
+    k.tofile(tmp_path / "k.bin")
+    r = subprocess.run([str(test_bin), "rope", str(tmp_path / "q.bin"), str(tmp_path / "k.bin"),
+                        str(S), str(H), str(KVH), str(hd), str(tmp_path / "out")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    q_ref, k_ref = ref.apply_rope(q, k, H, KVH, hd)
+    qo = np.fromfile(tmp_path / "out.q.bin", np.float32).reshape(q.shape)
+    ko = np.fromfile(tmp_path / "out.k.bin", np.float32).reshape(k.shape)
+    assert np.array_equal(qo.view(np.uint32), q_ref.view(np.uint32))
+    assert np.array_equal(ko.view(np.uint32), k_ref.view(np.uint32))
+
+
+def test_phi_attention_matches_reference(test_bin, tmp_path):
+    """PhiAttention(loader, 0) on the host against the reference's own
+    PhiAttention::forward on the same model.bin (biases included)."""
+    ref = _ref_attn()
+    pkg = load_pkg()
+    model, xp, x, d, H = _decoder_model(pkg, tmp_path, ref)
+    r = subprocess.run([str(test_bin), "attention", str(model), str(xp), str(x.shape[0]), str(d),
+                        str(H), str(H), str(tmp_path / "out")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    y = np.fromfile(tmp_path / "out.attn.bin", np.float32).reshape(x.shape)
+    y_ref = ref.forward(model, 0, x, d)
+    assert rel_l2(y, y_ref) <= 1e-6, rel_l2(y, y_ref)
+
+
+@pytest.mark.gpu
+def test_phi_decoder_layer_matches_reference(test_bin, tmp_path):
+    """PhiDecoderLayer(loader, 0) -- LayerNorm and attention on the host, the
+    MoE half (post-attention LayerNorm, quantised top-2 router, experts,
+    combine, residual) on the GPU -- against the reference's own
+    PhiDecoderLayer::forward (src/layer.cu:152-162) on the same model.bin."""
+    ref = _ref_attn()
+    pkg = load_pkg()
+    model, xp, x, d, H = _decoder_model(pkg, tmp_path, ref)
+    r = subprocess.run([str(test_bin), "decoder", str(model), str(xp), str(x.shape[0]), str(d),
+                        str(H), str(H), str(tmp_path / "out")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    y = np.fromfile(tmp_path / "out.dec.bin", np.float32).reshape(x.shape)
+    y_ref = ref.decoder_layer(model, 0, x)
+    assert rel_l2(y, y_ref) <= 1e-3, rel_l2(y, y_ref)
