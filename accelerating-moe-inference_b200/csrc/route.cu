@@ -769,9 +769,10 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nchunks = d / KC;
     const int chain_warps = (blockDim.x >> 5) - 1;
-    // Dependent launch: nothing the previous kernel touches (x, the
-    // workspace) is read or written before it has completed.
-    wait_predecessor_grid();
+    // Dependent launch: nothing the previous kernel may write (x, the norm
+    // statistics, the workspace) is read or written before it has completed;
+    // the layer's constants (router rows, the norm's weight and bias) are
+    // loaded before that wait, so their latency overlaps the previous kernel.
     constexpr bool norm = kNorm;
     const int rows_used = E + T + (norm ? 2 : 0);
     if (tid == 0) {
@@ -794,23 +795,30 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         constexpr int kV = KC / 4;     // float4 per row chunk
         constexpr int kInFlight = 16;
         const int nw = blockDim.x >> 5;
-        for (int r = warp; r < rows_used; r += nw) {
-            const float* src = r < E ? wg + (size_t)r * d
-                             : r < E + T ? x + (size_t)(r - E) * d
-                             : (r == E + T ? nr.w : nr.b);
-            for (int v0 = lane; v0 < d / 4; v0 += 32 * kInFlight) {
-                float4 f[kInFlight];
+        // Pass 0: the constant rows (router, norm weight and bias); pass 1,
+        // after the wait for the previous kernel: the token rows.
+        for (int pass = 0; pass < 2; ++pass) {
+            if (pass == 1) wait_predecessor_grid();
+            for (int r = warp; r < rows_used; r += nw) {
+                const bool token_row = r >= E && r < E + T;
+                if (token_row != (pass == 1)) continue;
+                const float* src = r < E ? wg + (size_t)r * d
+                                 : token_row ? x + (size_t)(r - E) * d
+                                 : (r == E + T ? nr.w : nr.b);
+                for (int v0 = lane; v0 < d / 4; v0 += 32 * kInFlight) {
+                    float4 f[kInFlight];
 #pragma unroll
-                for (int u = 0; u < kInFlight; ++u) {
-                    const int v = v0 + 32 * u;
-                    if (v < d / 4) f[u] = __ldg(reinterpret_cast<const float4*>(src) + v);
-                }
+                    for (int u = 0; u < kInFlight; ++u) {
+                        const int v = v0 + 32 * u;
+                        if (v < d / 4) f[u] = __ldg(reinterpret_cast<const float4*>(src) + v);
+                    }
 #pragma unroll
-                for (int u = 0; u < kInFlight; ++u) {
-                    const int v = v0 + 32 * u;
-                    if (v < d / 4)
-                        *reinterpret_cast<float4*>(ring + (size_t)(v / kV) * gm.rows * gm.ld +
-                                                   (size_t)r * gm.ld + 4 * (v % kV)) = f[u];
+                    for (int u = 0; u < kInFlight; ++u) {
+                        const int v = v0 + 32 * u;
+                        if (v < d / 4)
+                            *reinterpret_cast<float4*>(ring + (size_t)(v / kV) * gm.rows * gm.ld +
+                                                       (size_t)r * gm.ld + 4 * (v % kV)) = f[u];
+                    }
                 }
             }
         }
@@ -831,6 +839,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         }
     }
 
+    if (!direct) wait_predecessor_grid();
     if (warp == 0) {
         if (lane == 0 && !direct) {
             // ------------------------------------------------ loads
