@@ -23,9 +23,10 @@ namespace {
 constexpr int kCombineThreads = 256;
 constexpr int kCombineWarps = kCombineThreads / 32;
 
-// kU float4 columns per lane per unit: 4 for large batches (several loads in
-// flight per lane), 1 for decode-sized ones (more warps on fewer tokens).
-template <int KMAX, int kU>
+// kU float4 columns per lane per unit (more for large batches); the k * nsplit
+// partial rows a column needs are loaded kB at a time, all in flight, then
+// consumed in the fixed order: slot by ascending expert, split by split.
+template <int KMAX, int kU, int kB>
 __global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(const float* __restrict__ part, int nsplit, size_t split_stride,
                const int* __restrict__ idx, const float* __restrict__ wts, int T, int k, int d,
@@ -39,43 +40,65 @@ combine_kernel(const float* __restrict__ part, int nsplit, size_t split_stride,
     int ord[KMAX];
     float ow[KMAX];
     slot_order<KMAX>(idx + (size_t)t * k, wts + (size_t)t * k, k, lane, ord, ow);
+    // Lane r holds the r-th slot (ascending expert): its row offset and weight.
     const int nv = d / 4;
-    const float4* base = reinterpret_cast<const float4*>(part) + (size_t)t * k * nv;
+    size_t my_off = 0;
+    float my_w = 0.0f;
+#pragma unroll
+    for (int r = 0; r < KMAX; ++r)
+        if (lane == r) {
+            my_off = ((size_t)t * k + ord[r]) * nv;
+            my_w = ow[r];
+        }
+    const float4* base = reinterpret_cast<const float4*>(part);
     const size_t sstride = split_stride / 4;
     const int v0 = chunk * 32 * kU + lane;
-    float4 acc[kU];
+    const int total = k * nsplit;
+    float4 acc[kU], v[kU];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) acc[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int u = 0; u < kU; ++u) {
+        acc[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        v[u] = acc[u];
+    }
+    for (int b0 = 0; b0 < total; b0 += kB) {
+        float4 q[kB][kU];
 #pragma unroll
-    for (int r = 0; r < KMAX; ++r) {
-        if (r >= k) break;
-        const float4* src = base + (size_t)ord[r] * nv;
-        float4 v[kU];
+        for (int j = 0; j < kB; ++j) {
+            const int i = b0 + j;
+            const int r = i / nsplit, sp = i - r * nsplit;
+            const size_t off = __shfl_sync(0xffffffffu, my_off, r < 32 ? r : 0);
+            if (i < total) {
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int c = v0 + 32 * u;
-            if (c < nv) v[u] = __ldcs(src + c);
-        }
-        for (int sp = 1; sp < nsplit; ++sp) {
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int c = v0 + 32 * u;
-                if (c < nv) {
-                    const float4 q = __ldcs(src + sp * sstride + c);
-                    v[u].x = __fadd_rn(v[u].x, q.x);
-                    v[u].y = __fadd_rn(v[u].y, q.y);
-                    v[u].z = __fadd_rn(v[u].z, q.z);
-                    v[u].w = __fadd_rn(v[u].w, q.w);
+                for (int u = 0; u < kU; ++u) {
+                    const int c = v0 + 32 * u;
+                    if (c < nv) q[j][u] = __ldcs(base + off + sp * sstride + c);
                 }
             }
         }
-        const float w = ow[r];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            acc[u].x = __fmaf_rn(w, v[u].x, acc[u].x);
-            acc[u].y = __fmaf_rn(w, v[u].y, acc[u].y);
-            acc[u].z = __fmaf_rn(w, v[u].z, acc[u].z);
-            acc[u].w = __fmaf_rn(w, v[u].w, acc[u].w);
+        for (int j = 0; j < kB; ++j) {
+            const int i = b0 + j;
+            const int r = i / nsplit, sp = i - r * nsplit;
+            const float w = __shfl_sync(0xffffffffu, my_w, r < 32 ? r : 0);
+            if (i < total) {
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    if (sp == 0) {
+                        v[u] = q[j][u];
+                    } else {
+                        v[u].x = __fadd_rn(v[u].x, q[j][u].x);
+                        v[u].y = __fadd_rn(v[u].y, q[j][u].y);
+                        v[u].z = __fadd_rn(v[u].z, q[j][u].z);
+                        v[u].w = __fadd_rn(v[u].w, q[j][u].w);
+                    }
+                    if (sp == nsplit - 1) {
+                        acc[u].x = __fmaf_rn(w, v[u].x, acc[u].x);
+                        acc[u].y = __fmaf_rn(w, v[u].y, acc[u].y);
+                        acc[u].z = __fmaf_rn(w, v[u].z, acc[u].z);
+                        acc[u].w = __fmaf_rn(w, v[u].w, acc[u].w);
+                    }
+                }
+            }
         }
     }
     float4* yr = reinterpret_cast<float4*>(y) + (size_t)t * nv;
@@ -96,7 +119,7 @@ combine_kernel(const float* __restrict__ part, int nsplit, size_t split_stride,
     }
 }
 
-template <int KMAX, int kU>
+template <int KMAX, int kU, int kB>
 cudaError_t launch_t(const Layer& L, int T, int nsplit, size_t split_stride, const float* resid,
                      float* y, cudaStream_t s) {
     const int units = (L.d / 4 + 32 * kU - 1) / (32 * kU);
@@ -110,7 +133,7 @@ cudaError_t launch_t(const Layer& L, int T, int nsplit, size_t split_stride, con
     attr[0].val.programmaticStreamSerializationAllowed = L.profile ? 0 : 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, combine_kernel<KMAX, kU>, (const float*)L.ws.part, nsplit,
+    return cudaLaunchKernelEx(&cfg, combine_kernel<KMAX, kU, kB>, (const float*)L.ws.part, nsplit,
                               split_stride, (const int*)L.ws.idx, (const float*)L.ws.wts, T, L.k,
                               L.d, units, resid, y);
 }
@@ -123,12 +146,15 @@ cudaError_t launch_combine(const Layer& L, int T, int nsplit, const float* resid
     const size_t stride = (size_t)T * L.k * L.d;
     // Decode-sized batches: one float4 per lane per unit, so a token's row is
     // spread over d / 128 warps.
+    // Large batches (one split): 4 columns per lane, all k slots' loads in
+    // flight (k <= 2) or 2 columns and 8 slots (k <= 8).
     const bool small = (long long)T * (L.d / 512) < 8LL * L.sm_count;
-    if (L.k <= 2)
-        return small ? launch_t<2, 1>(L, T, nsplit, stride, resid, y, s)
-                     : launch_t<2, 4>(L, T, nsplit, stride, resid, y, s);
-    return small ? launch_t<kMaxTopK, 1>(L, T, nsplit, stride, resid, y, s)
-                 : launch_t<kMaxTopK, 4>(L, T, nsplit, stride, resid, y, s);
+    if (small) {
+        if (L.k <= 2) return launch_t<2, 1, 16>(L, T, nsplit, stride, resid, y, s);
+        return launch_t<kMaxTopK, 1, 16>(L, T, nsplit, stride, resid, y, s);
+    }
+    if (L.k <= 2) return launch_t<2, 4, 2>(L, T, nsplit, stride, resid, y, s);
+    return launch_t<kMaxTopK, 2, 8>(L, T, nsplit, stride, resid, y, s);
 }
 
 }  // namespace moe
