@@ -776,10 +776,9 @@ int forward_host_impl(MoeHandle* h, const float* x, float* y, int32_t T, bool bl
     // Rows are independent, so large batches run as a pipeline of chunks: the
     // copy-in of chunk c + 1 and the copy-out of chunk c - 1 overlap chunk c's
     // compute (and each other: the link is full duplex).  Chunks stay at
-    // least 2048 tokens in BF16 so the grouped GEMMs keep their weight reuse;
-    // the fp32-faithful GEMMs do three MMAs per weight byte, so 1024-token
-    // chunks stay compute-bound and shorten the exposed first and last copy.
-    int nch = T / (fp32_faithful(L) ? 1024 : 2048);
+    // least 2048 tokens so the grouped GEMMs keep their weight reuse (at
+    // config 2, 1024-token chunks made the fp32-faithful e2e slower).
+    int nch = T / 2048;
     if (nch > MoeHandle::kMaxChunks) nch = MoeHandle::kMaxChunks;
     if (nch < 2 || !h->h2d_stream) nch = 1;
     if (nch == 1) {

@@ -66,6 +66,10 @@ WORKLOADS = {
     # 14336) with 2 experts, ~2 GB on the device (weights > L2).
     "c2small": dict(workload="c2small-2expert-profile", T=2048, d=4096, ff=14336, E=2, k=2,
                     seed=1),
+    # A quarter of config 2 for DRAM-traffic captures: 2 of its 8 experts with
+    # its 1024 routed rows per expert, so a launch's traffic times 4 is
+    # config 2's (~3 GB on the device).
+    "c2slice": dict(workload="c2slice-2of8-experts", T=1024, d=4096, ff=14336, E=2, k=2, seed=1),
     # fine-grained experts, top-8, router logits ~N(0, 1)
     # (router weights N(0, 1/d)) plus the Zipf-like bias 0.5 ln(1/rank).
     "c5": dict(workload="c5-finegrained-ep", T=16384, d=2048, ff=1408, E=64, k=8, seed=3,
@@ -723,7 +727,8 @@ def run_single(args, wl, pkg, world, rank, local):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     decode_T = [] if args.no_decode else [t for t in DECODE_T if t <= T]
-    names = [args.precision] + [m for m in args.modes.split(",") if m and m != args.precision]
+    names = [args.precision] + [m for m in args.modes.split(",")
+                                if m and m != "none" and m != args.precision]
     if world > 1:
         dist.barrier()
     uuid = str(torch.cuda.get_device_properties(local).uuid)
@@ -848,7 +853,7 @@ def main():
                          "(fp32-faithful) or bf16")
     ap.add_argument("--modes", default="bf16",
                     help="other precisions measured on one GPU besides the headline, "
-                         "comma-separated (reported under roofline.modes)")
+                         "comma-separated (reported under roofline.modes), or none")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c4"], default="c2",
                     help="c2 (default, the headline layer), c2small, c5, or c4: only the toy "
                          "MoE decoder (BASELINE config 4), one GPU")
@@ -878,7 +883,7 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     for m in args.modes.split(","):
-        if m and m not in PRECISIONS:
+        if m and m != "none" and m not in PRECISIONS:
             ap.error(f"unknown mode {m}")
     if args.workload == "c4":
         return decoder_only(args)

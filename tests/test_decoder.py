@@ -7,7 +7,9 @@ its attention block against the reference's PhiAttention::forward
 (src/layer.cu:110-147, built with plain multi-head attention), its greedy
 loop against its own prefill, and its EOS rule (generate_decode,
 src/model.cu:2061-2104).  GPU tests run the decoder through the C ABI at a
-small shape (2 layers, d 256, vocab 1024, 8 experts top-2) and compare:
+small shape (2 layers, d 256, vocab 1024, 8 experts top-2) and, for 2 layers,
+at config 4's own layer shapes (d 2048, 16 heads, 16 experts of 5632,
+vocab 32000), and compare:
   - prefill logits: relative L2 <= 1e-3 in FP32 (3xTF32), <= 3e-2 in BF16
     (every activation rounded to bf16 before each GEMM);
   - greedy ids: equal to the oracle's until the sequences diverge, and a
@@ -305,3 +307,30 @@ def test_decoder_config_is_validated_before_any_device_work():
         assert rc == code, (kw, rc)
         assert word in L.moe_last_error().decode()
         assert not h.value
+
+
+@pytest.fixture(scope="module")
+def config4_case():
+    """Config-4 layer shapes, 2 layers: weights (drawn once, ~40 s on the host)
+    and the oracle's prefill logits and 3 greedy tokens for 2 prompts of 64."""
+    pkg = load_pkg()
+    w = _weights(seed=4, n_layers=2, d=2048, vocab=32000, E=16, ff=5632)
+    o = _oracle(w, 16, 128)
+    prompt = pkg.synthetic_prompt(8, 2, 64, w.vocab)
+    ids_ref, lg_ref = o.generate(prompt, 3)
+    return w, prompt, ids_ref, lg_ref
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+def test_decoder_at_config4_shapes(config4_case, precision):
+    """The decoder at BASELINE config 4's layer shapes -- d 2048, 16 heads of
+    128, 16 experts top-2 with d_ff 5632, vocabulary 32000 -- for 2 layers:
+    prefill logits and 3 greedy tokens of 2 sequences of 64 against the
+    oracle, within the same bounds as the small shape."""
+    w, prompt, ids_ref, lg_ref = config4_case
+    with _decoder(w, 16, 128, precision, max_batch=2, max_seq=80) as m:
+        lg, _ = m.prefill(prompt)
+        ids, lgg = m.generate(prompt, 3)
+    assert rel_l2(lg, lg_ref[:, 0]) <= TOL[precision], rel_l2(lg, lg_ref[:, 0])
+    _check_greedy(ids, lgg, ids_ref, lg_ref, precision)
