@@ -323,6 +323,14 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             int stage = 0;
             uint32_t phase = 0;
             int issued = 0;
+            // Activation rows are re-read by every N tile of their expert over
+            // the whole expert's run, while the weights stream past: keep the
+            // activations in L2 (evict_last; 6% fewer DRAM reads for bf16x3
+            // gate/up at config-2 shapes).  Weights keep the default policy --
+            // evict_first doubled their reads, since the M tiles sharing a
+            // weight tile do not read it at the same instant.
+            const uint64_t pol_a = l2_policy_evict_last();
+            const uint64_t pol_b = 0;
             for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
                 const TileCoord tc = decode_tile(p.mtiles, t / p.k_splits, p.n_tiles);
                 const int mt = tc.mt, nt = tc.nt;
@@ -339,13 +347,17 @@ expert_gemm_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     uint8_t* sbase = smem + stage * C::kStageBytes;
                     mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
                     const int kx = kb * kElems;
-                    tma_load_2d(sbase, &tmA_hi, &full[stage], kx, tile.row0);
+                    auto ld = [&](uint8_t* dst, const CUtensorMap* tm, int y, uint64_t pol) {
+                        if (pol) tma_load_2d_hint(dst, tm, &full[stage], kx, y, pol);
+                        else tma_load_2d(dst, tm, &full[stage], kx, y);
+                    };
+                    ld(sbase, &tmA_hi, tile.row0, pol_a);
                     if constexpr (C::kPlanes == 2) {
-                        tma_load_2d(sbase + kABytes, &tmA_lo, &full[stage], kx, tile.row0);
-                        tma_load_2d(sbase + 2 * kABytes, &tmB_hi, &full[stage], kx, brow);
-                        tma_load_2d(sbase + 2 * kABytes + kBBytes, &tmB_lo, &full[stage], kx, brow);
+                        ld(sbase + kABytes, &tmA_lo, tile.row0, pol_a);
+                        ld(sbase + 2 * kABytes, &tmB_hi, brow, pol_b);
+                        ld(sbase + 2 * kABytes + kBBytes, &tmB_lo, brow, pol_b);
                     } else {
-                        tma_load_2d(sbase + kABytes, &tmB_hi, &full[stage], kx, brow);
+                        ld(sbase + kABytes, &tmB_hi, brow, pol_b);
                     }
                     ++issued;
                     if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
@@ -551,6 +563,14 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
             uint32_t phase = 0;
             int issued = 0;
             constexpr int kElems = C::kElems;
+            // Activation rows are re-read by every N tile of their expert over
+            // the whole expert's run, while the weights stream past: keep the
+            // activations in L2 (evict_last; 6% fewer DRAM reads for bf16x3
+            // gate/up at config-2 shapes).  Weights keep the default policy --
+            // evict_first doubled their reads, since the M tiles sharing a
+            // weight tile do not read it at the same instant.
+            const uint64_t pol_a = l2_policy_evict_last();
+            const uint64_t pol_b = 0;
             for (int t = cid; t < total && !*abort_flag; t += nclusters) {
                 const TileCoord tc = decode_tile(p.mtiles, t, p.n_tiles);
                 const MTile tile = p.mtiles[tc.mt];
@@ -566,13 +586,17 @@ expert_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::kStageBytes);
                     const uint32_t fb = full0 + stage * 8;
                     const int kx = kb * kElems;
-                    tma_load_2d_pair(sbase, &tmA_hi, fb, kx, arow);
+                    auto ld = [&](uint8_t* dst, const CUtensorMap* tm, int y, uint64_t pol) {
+                        if (pol) tma_load_2d_pair_hint(dst, tm, fb, kx, y, pol);
+                        else tma_load_2d_pair(dst, tm, fb, kx, y);
+                    };
+                    ld(sbase, &tmA_hi, arow, pol_a);
                     if constexpr (C::kPlanes == 2) {
-                        tma_load_2d_pair(sbase + C::kHalfA, &tmA_lo, fb, kx, arow);
-                        tma_load_2d_pair(sbase + 2 * C::kHalfA, &tmB_hi, fb, kx, brow);
-                        tma_load_2d_pair(sbase + 2 * C::kHalfA + C::kHalfB, &tmB_lo, fb, kx, brow);
+                        ld(sbase + C::kHalfA, &tmA_lo, arow, pol_a);
+                        ld(sbase + 2 * C::kHalfA, &tmB_hi, brow, pol_b);
+                        ld(sbase + 2 * C::kHalfA + C::kHalfB, &tmB_lo, brow, pol_b);
                     } else {
-                        tma_load_2d_pair(sbase + C::kHalfA, &tmB_hi, fb, kx, brow);
+                        ld(sbase + C::kHalfA, &tmB_hi, brow, pol_b);
                     }
                     ++issued;
                     if (++stage == C::kStages) { stage = 0; phase ^= 1u; }
