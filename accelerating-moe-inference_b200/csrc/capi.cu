@@ -260,13 +260,16 @@ int forward_impl(Layer& L, const float* x, float* y, int T, cudaStream_t s, bool
     // A decode-sized batch is routed and dispatched by one single-CTA launch.
     int kc = 0, stages = 0;
     const bool small = route_small_geometry(L, T, block, &kc, &stages);
+    // The small-batch router computes RMSNorm statistics itself when every
+    // K chunk is resident in its shared memory (one launch fewer per block).
+    const bool rms_inline = small && block && L.norm_rms && route_small_resident(L, kc, stages);
     prof_mark(L, 0, s);
-    if (block && L.norm_rms)
+    if (block && L.norm_rms && !rms_inline)
         MOE_CUDA(launch_rms_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, s));
-    else if (block)
+    else if (block && !L.norm_rms)
         MOE_CUDA(launch_row_stats(x, T, L.d, L.norm_eps, W.row_mean, W.row_inv, W.dev_err, s));
     if (small) {
-        MOE_CUDA(launch_route_small(L, x, T, nr, decode, s));
+        MOE_CUDA(launch_route_small(L, x, T, nr, decode, s, rms_inline));
     } else {
         MOE_CUDA(launch_router(L, x, T, W.logits, W.idx, W.wts, W.blockhist, s, nr));
     }

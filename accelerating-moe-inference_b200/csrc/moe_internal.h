@@ -234,8 +234,12 @@ cudaError_t launch_dispatch_scan(const Layer& L, int T, cudaStream_t s);
 // in one single-CTA launch (rows in the decode kernels' format if `decode`,
 // else the GEMMs').  route_small_geometry says whether it applies.
 bool route_small_geometry(const Layer& L, int T, bool norm, int* kc, int* stages);
+// Every K chunk of the geometry has a stage of its own (the direct-load path).
+bool route_small_resident(const Layer& L, int kc, int stages);
+// rms_inline: the RMSNorm statistics are computed in the kernel (needs the
+// resident geometry) instead of read from the workspace.
 cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
-                               bool decode, cudaStream_t s);
+                               bool decode, cudaStream_t s, bool rms_inline = false);
 cudaError_t launch_dispatch_permute(const Layer& L, const float* x, int T, cudaStream_t s,
                                     const NormRef& nr = {});
 // The same placement with the rows copied in the decode kernels' format:

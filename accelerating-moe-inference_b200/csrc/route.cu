@@ -713,6 +713,13 @@ struct SmallGeom {
     int stages;
     int rows;     // E router rows, T token rows, then norm weight and bias rows
     int ld;       // padded row stride in floats: kc + 4 (LDS.128 of 8 rows conflict-free)
+    // RMSNorm statistics computed here from the token rows in shared memory
+    // (every K chunk resident) instead of by rms_stats_kernel beforehand:
+    // the same sum order and expression, written to stat_mean / stat_inv.
+    int rms_inline;
+    float rms_eps;
+    float* stat_mean;
+    float* stat_inv;
 };
 
 // Columns 4v .. 4v+3 of packed row `row` in the format of kMode (ActFormat).
@@ -824,6 +831,35 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         }
         __syncthreads();
         if constexpr (kNorm) {
+            __shared__ float s_mean[kSmallMaxTokens], s_inv[kSmallMaxTokens];
+            if (gm.rms_inline) {
+                // Warp t: token t's sum of squares in rms_stats_kernel's order
+                // (lane-strided float4 fma chain, then the xor-shuffle tree).
+                if (warp < T) {
+                    float ss = 0.0f;
+                    for (int v = lane; v < d / 4; v += 32) {
+                        const float4 a = *reinterpret_cast<const float4*>(
+                            ring + (size_t)(v / kV) * gm.rows * gm.ld + (size_t)(E + warp) * gm.ld +
+                            4 * (v % kV));
+                        ss = __fmaf_rn(a.x, a.x, ss);
+                        ss = __fmaf_rn(a.y, a.y, ss);
+                        ss = __fmaf_rn(a.z, a.z, ss);
+                        ss = __fmaf_rn(a.w, a.w, ss);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                    if (lane == 0) {
+                        s_mean[warp] = 0.0f;
+                        s_inv[warp] = 1.0f / sqrtf(ss / (float)d + gm.rms_eps);
+                        gm.stat_mean[warp] = 0.0f;
+                        gm.stat_inv[warp] = s_inv[warp];
+                    }
+                }
+            } else if (tid < T) {
+                s_mean[tid] = nr.mean[tid];
+                s_inv[tid] = nr.inv[tid];
+            }
+            __syncthreads();
             // Every expert's chain reads the same normalised token row:
             // normalise it once, in place, with the expression the chains
             // would apply (bit-identical), instead of in each chain.
@@ -831,7 +867,7 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
                 const int t = i / (d / 4), v = i % (d / 4);
                 float* sb = ring + (size_t)(v / kV) * gm.rows * gm.ld + 4 * (v % kV);
                 float4* xp = reinterpret_cast<float4*>(sb + (size_t)(E + t) * gm.ld);
-                *xp = layer_norm_out4(*xp, nr.mean[t], nr.inv[t],
+                *xp = layer_norm_out4(*xp, s_mean[t], s_inv[t],
                                       *reinterpret_cast<const float4*>(sb + (size_t)(E + T) * gm.ld),
                                       *reinterpret_cast<const float4*>(sb + (size_t)(E + T + 1) * gm.ld));
             }
@@ -1107,14 +1143,21 @@ bool route_small_geometry(const Layer& L, int T, bool norm, int* kc_out, int* st
     return false;
 }
 
+bool route_small_resident(const Layer& L, int kc, int stages) { return L.d / kc <= stages; }
+
 cudaError_t launch_route_small(const Layer& L, const float* x, int T, const NormRef& nr,
-                               bool decode, cudaStream_t s) {
+                               bool decode, cudaStream_t s, bool rms_inline) {
     const Workspace& W = L.ws;
     const bool norm = nr.mean != nullptr;
     SmallGeom gm;
     if (!route_small_geometry(L, T, norm, &gm.kc, &gm.stages)) return cudaErrorInvalidValue;
     gm.rows = L.E_route + T + (norm ? 2 : 0);
     gm.ld = gm.kc + 4;
+    gm.rms_inline = rms_inline && norm && route_small_resident(L, gm.kc, gm.stages);
+    if (rms_inline && !gm.rms_inline) return cudaErrorInvalidValue;
+    gm.rms_eps = L.norm_eps;
+    gm.stat_mean = W.row_mean;
+    gm.stat_inv = W.row_inv;
     const size_t smem = (size_t)gm.stages * gm.rows * gm.ld * 4;
     ScanOut so;
     so.counts = W.counts; so.eoff = W.eoff; so.mtiles = W.mtiles;

@@ -145,6 +145,32 @@ def test_block_forward_decode_and_prefill_match_oracle(T, precision, orc):
 
 
 @pytest.mark.parametrize("precision", [0, 1, 2], ids=["fp32", "bf16", "bf16x3"])
+@pytest.mark.parametrize("T", [1, 3, 4, 33, 300])
+def test_rms_block_forward_matches_oracle(T, precision, orc):
+    """y = x + MoE(rms_norm(x)) (moe_set_post_rms_norm, the decoder's MoE
+    block): up to 4 tokens the small-batch router computes the RMS
+    statistics itself, larger batches take them from rms_stats_kernel.
+    Against the oracle MoE on the float64 RMS-normalised rows (as fp32)."""
+    pkg = load_pkg()
+    d = 512
+    layer = pkg.synthetic_layer(43, d, 448, 8)
+    w = (1.0 + 0.1 * np.random.default_rng(43).standard_normal(d)).astype(np.float32)
+    x = (pkg.synthetic_tokens(43, T, d) * 1.5 + 0.1).astype(np.float32)
+    x64 = x.astype(np.float64)
+    inv = 1.0 / np.sqrt((x64 * x64).mean(axis=1, keepdims=True) + EPS)
+    xn = (x64 * inv * w.astype(np.float64)).astype(np.float32)
+    y_moe, _, _, _ = orc.moe_forward(xn, layer, 2, oracle.POLICY_SOFTMAX)
+    y_ref = y_moe.astype(np.float64) + x64
+    with pkg.MoeLayer(layer, top_k=2, policy=1, precision=precision,
+                      decode_max_tokens=64) as m:
+        m.set_post_rms_norm(w, EPS)
+        y = m.block_forward_host(x)
+        y2 = m.block_forward_host(x)
+    assert rel_l2(y, y_ref) <= TOL[precision], rel_l2(y, y_ref)
+    assert np.array_equal(bits(y), bits(y2))
+
+
+@pytest.mark.parametrize("precision", [0, 1, 2], ids=["fp32", "bf16", "bf16x3"])
 @pytest.mark.parametrize("T", [3, 200])
 def test_fused_block_equals_unfused_composition(T, precision):
     """layer_norm_device -> forward_device -> + attn (torch) gives the same
