@@ -32,6 +32,7 @@ combine_kernel(const float* __restrict__ part, int nsplit, size_t split_stride,
                const int* __restrict__ idx, const float* __restrict__ wts, int T, int k, int d,
                int units_per_token, const float* resid, float* y) {
     wait_predecessor_grid();
+    launch_dependents();
     const int lane = threadIdx.x & 31;
     const long long unit = (long long)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
     if (unit >= (long long)T * units_per_token) return;

@@ -90,16 +90,44 @@ struct Active {
     int coff[kMaxExperts];
 };
 
+// Warp 0 builds it: each lane loads a run of consecutive experts' counts at
+// once (no chain of dependent global loads before the first weight load),
+// and two warp scans give the row offsets and the active list's positions,
+// so the list stays in ascending expert order.
 __device__ void build_active(Active& a, const int* __restrict__ counts, int E) {
-    if (threadIdx.x == 0) {
-        int n = 0, off = 0;
-        for (int e = 0; e < E; ++e) {
-            const int c = counts[e];
-            a.coff[e] = off;
-            off += c;
-            if (c > 0) a.act[n++] = e;
+    if (threadIdx.x < 32) {
+        constexpr int kPer = kMaxExperts / 32;
+        const int lane = threadIdx.x;
+        const int per = (E + 31) / 32;
+        const int e0 = lane * per;
+        int c[kPer];
+        int sum = 0, nact = 0;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            c[i] = (i < per && e0 + i < E) ? counts[e0 + i] : 0;
+            sum += c[i];
+            nact += c[i] > 0 ? 1 : 0;
         }
-        a.n = n;
+        int s = sum, n = nact;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ts = __shfl_up_sync(0xffffffffu, s, o);
+            const int tn = __shfl_up_sync(0xffffffffu, n, o);
+            if (lane >= o) {
+                s += ts;
+                n += tn;
+            }
+        }
+        int off = s - sum, pos = n - nact;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            if (i < per && e0 + i < E) {
+                a.coff[e0 + i] = off;
+                off += c[i];
+                if (c[i] > 0) a.act[pos++] = e0 + i;
+            }
+        }
+        if (lane == 31) a.n = n;
     }
     __syncthreads();
 }
@@ -166,6 +194,7 @@ decode_gateup_kernel(const AT* __restrict__ a_rows, const WT* __restrict__ w13, 
                      float* __restrict__ h) {
     __shared__ Active A;
     wait_predecessor_grid();
+    launch_dependents();
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const long long W = (long long)gridDim.x * kDecWarps;
@@ -220,7 +249,12 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
                    const int* __restrict__ row_slot, float* __restrict__ part,
                    size_t split_stride) {
     __shared__ Active A;
-    wait_predecessor_grid();
+    // The routing (counts) comes from the kernel before decode_gateup, and a
+    // dependent launch of this kernel happens only once every decode_gateup
+    // CTA has passed its own wait (launch_dependents follows it), so counts
+    // are final here already: the active list is built, and each warp's first
+    // work item's weight rows are prefetched into L2, while decode_gateup is
+    // still streaming.  h (decode_gateup's output) is read after the wait.
     build_active(A, counts, E);
     const int lane = threadIdx.x & 31;
     const int nq = (d + 3) / 4;                    // column quads per expert
@@ -228,6 +262,19 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
     const long long W = (long long)gridDim.x * kDecWarps;
     const long long gw = (long long)blockIdx.x * kDecWarps + (threadIdx.x >> 5);
     const long long total = (long long)A.n * nq * nk;
+    {
+        const long long it = total * gw / W;
+        if (lane < 4 && it < total * (gw + 1) / W) {
+            const int e = A.act[(int)(it / ((long long)nq * nk))];
+            const int rem = (int)(it % ((long long)nq * nk));
+            const int n = min((rem / nk) * 4 + lane, d - 1);
+            const int k0 = (rem % nk) * kDownChunk;
+            const int k1 = min(ffp, k0 + kDownChunk);
+            prefetch_l2_bulk(w2 + ((size_t)e * d + n) * ffp + k0, (uint32_t)((k1 - k0) * sizeof(WT)));
+        }
+    }
+    wait_predecessor_grid();
+    launch_dependents();
     for (long long it = total * gw / W; it < total * (gw + 1) / W; ++it) {
         const int ai = (int)(it / ((long long)nq * nk));
         const int rem = (int)(it % ((long long)nq * nk));

@@ -116,6 +116,9 @@ __global__ void __launch_bounds__(256)
 rms_pack_kernel(const float* __restrict__ x, int src0, int stride, int T, int rows_pad, int d,
                 float eps, const float* __restrict__ w, void* __restrict__ a_hi,
                 void* __restrict__ a_lo, float4* __restrict__ zero, size_t zero_n4) {
+    // Dependent launch: x and the buffers below belong to earlier kernels.
+    wait_predecessor_grid();
+    launch_dependents();
     const size_t gtid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t gthreads = (size_t)gridDim.x * blockDim.x;
     for (size_t i = gtid; i < zero_n4; i += gthreads) zero[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -701,6 +704,22 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
     __shared__ float sacc[kDecThreads];
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Dependent launch.  The position counter and the cached keys and values
+    // before it were written by earlier decode steps, which completed before
+    // the previous kernel started (it is launched only after the one before
+    // it has passed its own wait): prefetch this chunk's cached rows into L2
+    // now, while the q/k/v projection (the previous kernel) still runs.
+    {
+        const int pos0 = *pos_dev;
+        const int kk0 = c * kDecChunk;
+        if (tid < 2 && kk0 < pos0) {
+            const int rows = min(kDecChunk, pos0 - kk0);
+            const float* src = (tid == 0 ? kc : vc) + (((size_t)b * H + h) * max_seq + kk0) * HD;
+            prefetch_l2_bulk(src, (uint32_t)(rows * HD * sizeof(float)));
+        }
+    }
+    wait_predecessor_grid();   // q/k/v of this step
+    launch_dependents();
     const int pos = *pos_dev;
     const int n = pos + 1;
     const int k0 = c * kDecChunk;
@@ -742,10 +761,22 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
         const int j = warp + kWarps * i;
         float acc = 0.0f;
         if (j < nk) {
-            // Plain loads: this kernel itself may have written row pos.
+            // Plain (coherent) vector loads: this kernel itself may have
+            // written row pos.
             const float* kr = kb + (size_t)j * HD + lane * kPer;
+            float kv[kPer];
+            if constexpr (kPer == 4) {
+                const float4 f = *reinterpret_cast<const float4*>(kr);
+                kv[0] = f.x; kv[1] = f.y; kv[2] = f.z; kv[3] = f.w;
+            } else {
 #pragma unroll
-            for (int e = 0; e < kPer; ++e) acc = fmaf(qv[e], kr[e], acc);
+                for (int e = 0; e < kPer; e += 2) {
+                    const float2 f = *reinterpret_cast<const float2*>(kr + e);
+                    kv[e] = f.x; kv[e + 1] = f.y;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < kPer; ++e) acc = fmaf(qv[e], kv[e], acc);
         }
         dots[i] = acc;
     }
@@ -772,15 +803,23 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
         }
     }
     __syncthreads();
+    // Values: thread (class, column) takes keys class, class + kParts, ...;
+    // all of its V loads are issued before the first FMA (one memory round
+    // trip per chunk instead of one per group of keys).
     const int col = tid % HD, cls = tid / HD;
-    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    int j = cls;
-    for (; j + 3 * kParts < nk; j += 4 * kParts) {
+    constexpr int kKeysPerThread = kDecChunk / kParts;
+    float vv[kKeysPerThread];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-            a[u] = fmaf(sp[j + u * kParts], vb[(size_t)(j + u * kParts) * HD + col], a[u]);
+    for (int i = 0; i < kKeysPerThread; ++i) {
+        const int j = cls + i * kParts;
+        vv[i] = j < nk ? vb[(size_t)j * HD + col] : 0.0f;
     }
-    for (; j < nk; j += kParts) a[0] = fmaf(sp[j], vb[(size_t)j * HD + col], a[0]);
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < kKeysPerThread; ++i) {
+        const int j = cls + i * kParts;
+        if (j < nk) a[i & 3] = fmaf(sp[j], vv[i], a[i & 3]);
+    }
     sacc[tid] = (a[0] + a[1]) + (a[2] + a[3]);
     __syncthreads();
     if (tid < HD) {
@@ -796,6 +835,8 @@ __global__ void __launch_bounds__(HD)
 attn_decode_combine_kernel(const float* __restrict__ part, const int* __restrict__ pos_dev, int H,
                            int nch, void* __restrict__ a_hi, void* __restrict__ a_lo) {
     const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    wait_predecessor_grid();   // dependent launch: the partials
+    launch_dependents();
     const int used = (*pos_dev + kDecChunk) / kDecChunk;   // chunks holding keys 0..pos
     const float* base = part + ((size_t)b * H + h) * nch * (HD + 2);
     float M = -INFINITY;
@@ -881,6 +922,122 @@ save_logits_kernel(const float4* __restrict__ logits, float4* __restrict__ gen,
     const size_t dst = ((size_t)b * n + *step_dev) * V4;
     for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V4; v += gridDim.x * blockDim.x)
         gen[dst + v] = logits[(size_t)b * V4 + v];
+}
+
+// ------------------------------------------------------------ dense GEMV
+// Decode-sized dense projections (q/k/v, o, the output head at T <= 4 rows,
+// BF16): y[t][n] (+)= W[n] . A[t] for t < T, W bf16 [N][K], A the bf16
+// operand rows; `accumulate` adds into y (the o projection into the residual
+// stream), else y is overwritten.  These are weight-streaming bound; 128-row tensor-core tiles would be
+// 1-4 rows full and spread the N x K stream over few CTAs, so instead every
+// warp of one CTA per SM owns an equal contiguous range of weight rows and
+// streams them once with 128-bit loads, two rows at a time, all of a row
+// pair's loads in flight.  Launched as a dependent grid: the weights do not
+// depend on the previous kernel, so each warp starts an L2 prefetch of its
+// first rows before it waits for that kernel; the activations and y are
+// read after the wait.  Each y element is one warp's sum (no atomics).
+constexpr int kGemvThreads = 512;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kGemvMaxRows = 4;
+constexpr uint32_t kGemvPrefetchBytes = 16384;   // per warp
+constexpr int kGemvVecs = 8;                     // 16-byte loads per row per lane per pass
+
+__device__ __forceinline__ uint4 gemv_stream_load(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& r, float (&v)[8]) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+template <int TM>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+dense_gemv_kernel(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restrict__ A,
+                  int N, int K, int T, int accumulate, float* __restrict__ y) {
+    const int lane = threadIdx.x & 31;
+    const long long nw = (long long)gridDim.x * kGemvWarps;
+    const long long gw = (long long)blockIdx.x * kGemvWarps + (threadIdx.x >> 5);
+    const int r0 = (int)((long long)N * gw / nw), r1 = (int)((long long)N * (gw + 1) / nw);
+    if (lane == 0 && r1 > r0) {
+        const size_t bytes = (size_t)(r1 - r0) * K * sizeof(__nv_bfloat16);
+        prefetch_l2_bulk(W + (size_t)r0 * K,
+                         (uint32_t)(bytes < kGemvPrefetchBytes ? bytes : kGemvPrefetchBytes));
+    }
+    wait_predecessor_grid();
+    launch_dependents();
+    // The T activation rows, staged once per CTA through L2 (written by the
+    // previous kernel) into shared memory, where every warp reads them.
+    extern __shared__ __align__(16) uint4 s_a[];
+    const int kv = K / 8;
+    for (int i = threadIdx.x; i < T * kv; i += blockDim.x)
+        s_a[i] = __ldcg(reinterpret_cast<const uint4*>(A) + i);
+    __syncthreads();
+    for (int r = r0; r < r1; r += 2) {
+        const bool two = r + 1 < r1;
+        const __nv_bfloat16* w0 = W + (size_t)r * K;
+        const __nv_bfloat16* w1 = two ? w0 + K : w0;
+        // This warp's outputs (through L2: the previous kernel may have just
+        // written them), loaded now so their latency overlaps the stream.
+        float yv[2][TM];
+#pragma unroll
+        for (int m = 0; m < TM; ++m) {
+            yv[0][m] = (accumulate && lane == 0 && m < T) ? __ldcg(y + (size_t)m * N + r) : 0.0f;
+            yv[1][m] = (accumulate && lane == 0 && m < T && two) ? __ldcg(y + (size_t)m * N + r + 1)
+                                                                 : 0.0f;
+        }
+        float acc[2][TM];
+#pragma unroll
+        for (int m = 0; m < TM; ++m) acc[0][m] = acc[1][m] = 0.0f;
+        for (int k0 = lane * 8; k0 < K; k0 += 32 * 8 * kGemvVecs) {
+            uint4 raw[kGemvVecs][2];
+#pragma unroll
+            for (int u = 0; u < kGemvVecs; ++u) {
+                const int kk = k0 + u * 256;
+                if (kk < K) {
+                    raw[u][0] = gemv_stream_load(w0 + kk);
+                    raw[u][1] = gemv_stream_load(w1 + kk);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvVecs; ++u) {
+                const int kk = k0 + u * 256;
+                if (kk >= K) break;
+                float wv0[8], wv1[8];
+                bf16x8_to_f32(raw[u][0], wv0);
+                bf16x8_to_f32(raw[u][1], wv1);
+#pragma unroll
+                for (int m = 0; m < TM; ++m) {
+                    if (m >= T) break;
+                    float av[8];
+                    bf16x8_to_f32(s_a[m * kv + kk / 8], av);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        acc[0][m] = fmaf(wv0[q], av[q], acc[0][m]);
+                        acc[1][m] = fmaf(wv1[q], av[q], acc[1][m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < TM; ++m) {
+            if (m >= T) break;
+            const float v0 = warp_sum(acc[0][m]);
+            const float v1 = warp_sum(acc[1][m]);
+            if (lane == 0) {
+                y[(size_t)m * N + r] = yv[0][m] + v0;
+                if (two) y[(size_t)m * N + r + 1] = yv[1][m] + v1;
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------ dense projection
@@ -1075,21 +1232,62 @@ cudaError_t launch_tiles(MoeDecoder& m, int T) {
     return cudaGetLastError();
 }
 
-// rms_norm(rows src0 + r * stride of x, r < T) -> A, zeroing `zero` [zero_n] floats.
+// A kernel launched as a dependent grid of the previous one on m.stream (it
+// calls wait_predecessor_grid() before touching earlier kernels' data).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(MoeDecoder& m, dim3 grid, dim3 block, size_t smem, void (*kern)(KArgs...),
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = m.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// The dense projections of T rows run as the GEMV (BF16, T <= 4, the
+// activation rows fit the default shared memory) instead of the grouped GEMM.
+bool use_gemv(const MoeDecoder& m, int T) {
+    return T >= 1 && T <= kGemvMaxRows && !tf_mode(m) && m.d % 8 == 0 &&
+           (size_t)T * m.d * sizeof(__nv_bfloat16) <= 48 * 1024;
+}
+
+// y (+)= A . W^T for the first T rows of the shared A operand (y [T][N]):
+// the GEMV at decode-sized T (`accumulate` adds into y, else y is
+// overwritten), the grouped GEMM otherwise (which always adds, into a y the
+// caller zeroed unless it accumulates).
+cudaError_t launch_dense(MoeDecoder& m, const Dense& D, int T, float* y, bool accumulate) {
+    const Layer& L = D.L;
+    if (!use_gemv(m, T)) return launch_expert_gemm_rows(L, T, y, m.stream, 1);
+    const auto* W = static_cast<const __nv_bfloat16*>(L.w2_hi);
+    const auto* A = static_cast<const __nv_bfloat16*>(m.a_hi);
+    const size_t smem = (size_t)T * L.ffp * sizeof(__nv_bfloat16);
+    const int acc = accumulate ? 1 : 0;
+    const dim3 grid(m.sm_count), block(kGemvThreads);
+    if (T == 1) return launch_pdl(m, grid, block, smem, dense_gemv_kernel<1>, W, A, L.d, L.ffp, T, acc, y);
+    if (T == 2) return launch_pdl(m, grid, block, smem, dense_gemv_kernel<2>, W, A, L.d, L.ffp, T, acc, y);
+    return launch_pdl(m, grid, block, smem, dense_gemv_kernel<4>, W, A, L.d, L.ffp, T, acc, y);
+}
+
+// rms_norm(rows src0 + r * stride of x, r < T) -> A, zeroing `zero` [zero_n]
+// floats.  For the grouped GEMM, A's rows up to the next 256 are zeroed too;
+// the GEMV reads only the T rows.
 cudaError_t launch_rms_pack(MoeDecoder& m, const float* x, int src0, int stride, int T,
                             const float* w, float* zero, size_t zero_n) {
-    const int rows_pad = round_up(T, 2 * kTileM);
+    const int rows_pad = use_gemv(m, T) ? T : round_up(T, 2 * kTileM);
     const int grid = (rows_pad + 7) / 8;
     const float eps = m.cfg.rms_eps;
+    float4* z = reinterpret_cast<float4*>(zero);
     if (tf_mode(m))
-        rms_pack_kernel<true><<<grid, 256, 0, m.stream>>>(x, src0, stride, T, rows_pad, m.d, eps, w,
-                                                          m.a_hi, m.a_lo,
-                                                          reinterpret_cast<float4*>(zero), zero_n / 4);
-    else
-        rms_pack_kernel<false><<<grid, 256, 0, m.stream>>>(x, src0, stride, T, rows_pad, m.d, eps,
-                                                           w, m.a_hi, m.a_lo,
-                                                           reinterpret_cast<float4*>(zero), zero_n / 4);
-    return cudaGetLastError();
+        return launch_pdl(m, dim3(grid), dim3(256), 0, rms_pack_kernel<true>, x, src0, stride, T,
+                          rows_pad, m.d, eps, w, m.a_hi, m.a_lo, z, zero_n / 4);
+    return launch_pdl(m, dim3(grid), dim3(256), 0, rms_pack_kernel<false>, x, src0, stride, T,
+                      rows_pad, m.d, eps, w, m.a_hi, m.a_lo, z, zero_n / 4);
 }
 
 template <int HD>
@@ -1121,17 +1319,16 @@ cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, bool prefill)
         }
     } else {
         const int nch = (m.cfg.max_seq + kDecChunk - 1) / kDecChunk;
-        attn_decode_partial_kernel<HD><<<dim3(nch, m.H, B), kDecThreads, 0, m.stream>>>(
-            m.qkvbuf, m.pos_dev, m.H, layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale,
-            m.rope, m.attn_part, nch);
-        cudaError_t e = cudaGetLastError();
+        cudaError_t e = launch_pdl(m, dim3(nch, m.H, B), dim3(kDecThreads), 0,
+                                   attn_decode_partial_kernel<HD>, m.qkvbuf, m.pos_dev, m.H,
+                                   layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale, m.rope,
+                                   m.attn_part, nch);
         if (e != cudaSuccess) return e;
         if (tf_mode(m))
-            attn_decode_combine_kernel<HD, true><<<dim3(m.H, B), HD, 0, m.stream>>>(
-                m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
-        else
-            attn_decode_combine_kernel<HD, false><<<dim3(m.H, B), HD, 0, m.stream>>>(
-                m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
+            return launch_pdl(m, dim3(m.H, B), dim3(HD), 0, attn_decode_combine_kernel<HD, true>,
+                              m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
+        return launch_pdl(m, dim3(m.H, B), dim3(HD), 0, attn_decode_combine_kernel<HD, false>,
+                          m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
     }
     return cudaGetLastError();
 }
@@ -1149,15 +1346,18 @@ cudaError_t launch_rope_kv(MoeDecoder& m, int l, int T, int rps, const int* pos_
 // One decoder layer over T rows: B sequences of rps rows each (prefill:
 // rps = S from position 0; decode: rps = 1 at the device position).
 int run_layer(MoeDecoder& m, int l, int B, int T, int rps, bool prefill) {
-    DEC_CUDA(launch_rms_pack(m, m.x, 0, 1, T, m.attn_norm[l], m.qkvbuf, (size_t)T * 3 * m.d));
-    DEC_CUDA(launch_expert_gemm_rows(m.qkv[l].L, T, m.qkvbuf, m.stream, 1));
+    // The GEMV overwrites q/k/v; the grouped GEMM adds into a zeroed buffer.
+    const bool gemv = use_gemv(m, T);
+    DEC_CUDA(launch_rms_pack(m, m.x, 0, 1, T, m.attn_norm[l], gemv ? nullptr : m.qkvbuf,
+                             gemv ? 0 : (size_t)T * 3 * m.d));
+    DEC_CUDA(launch_dense(m, m.qkv[l], T, m.qkvbuf, false));
     // Decode rotates q and k inside the attention kernel (and writes the cache there).
     if (prefill) DEC_CUDA(launch_rope_kv(m, l, T, rps, nullptr));
     if (m.HD == 128)
         DEC_CUDA(launch_attention_t<128>(m, l, B, rps, prefill));
     else
         DEC_CUDA(launch_attention_t<64>(m, l, B, rps, prefill));
-    DEC_CUDA(launch_expert_gemm_rows(m.wo[l].L, T, m.x, m.stream, 1));
+    DEC_CUDA(launch_dense(m, m.wo[l], T, m.x, true));   // x += o . Wo^T
     DEC_RC(moe_block_forward_device(m.moe[l], m.x, m.x2, T, m.stream));
     std::swap(m.x, m.x2);
     return MOE_OK;
@@ -1169,9 +1369,11 @@ int run_layer(MoeDecoder& m, int l, int B, int T, int rps, bool prefill) {
 // the tile list at B rows.
 int run_head(MoeDecoder& m, int B, int src0, int stride, bool record, int step,
              const int* step_dev, int eos) {
-    DEC_CUDA(launch_tiles(m, B));
-    DEC_CUDA(launch_rms_pack(m, m.x, src0, stride, B, m.final_norm, m.logits, (size_t)B * m.V));
-    DEC_CUDA(launch_expert_gemm_rows(m.head.L, B, m.logits, m.stream, 1));
+    const bool gemv = use_gemv(m, B);
+    if (!gemv) DEC_CUDA(launch_tiles(m, B));
+    DEC_CUDA(launch_rms_pack(m, m.x, src0, stride, B, m.final_norm, gemv ? nullptr : m.logits,
+                             gemv ? 0 : (size_t)B * m.V));
+    DEC_CUDA(launch_dense(m, m.head, B, m.logits, false));
     argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, record ? m.seq_ids : nullptr,
                                             m.cfg.max_seq, step, step_dev, eos,
                                             record ? m.done : nullptr);

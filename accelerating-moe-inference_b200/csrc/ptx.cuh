@@ -45,6 +45,22 @@ __device__ __forceinline__ void wait_predecessor_grid() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Lets the next kernel on the stream (if launched as a dependent grid) be
+// scheduled before this one completes.  Called only after this kernel's own
+// wait_predecessor_grid(): once every CTA of this grid has passed it, all
+// earlier kernels on the stream have completed, so a dependent grid's
+// prologue may read their results; it reads this grid's only after its own
+// wait.
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Asynchronous prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes
+// a multiple of 16); nothing waits for it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // System-scope acquire load / release store of a flag word another GPU
 // writes or reads (expert-parallel completion flags in peer memory).
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {

@@ -805,7 +805,10 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         // Pass 0: the constant rows (router, norm weight and bias); pass 1,
         // after the wait for the previous kernel: the token rows.
         for (int pass = 0; pass < 2; ++pass) {
-            if (pass == 1) wait_predecessor_grid();
+            if (pass == 1) {
+                wait_predecessor_grid();
+                launch_dependents();
+            }
             for (int r = warp; r < rows_used; r += nw) {
                 const bool token_row = r >= E && r < E + T;
                 if (token_row != (pass == 1)) continue;
@@ -875,7 +878,10 @@ router_small_kernel(const float* __restrict__ x, const float* __restrict__ wg,
         }
     }
 
-    if (!direct) wait_predecessor_grid();
+    if (!direct) {
+        wait_predecessor_grid();
+        launch_dependents();
+    }
     if (warp == 0) {
         if (lane == 0 && !direct) {
             // ------------------------------------------------ loads

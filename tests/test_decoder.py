@@ -188,6 +188,23 @@ def test_decoder_generate_matches_oracle(precision):
 @pytest.mark.gpu
 @pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
 @pytest.mark.parametrize("heads,hd", [(2, 128), (4, 64)], ids=["hd128", "hd64"])
+def test_decoder_batch1_generate_matches_oracle(precision, heads, hd):
+    """One sequence: every dense projection runs at one row (in BF16 the
+    weight-streaming GEMV, one row per pass), the MoE block through the
+    small-batch router and the decode kernels."""
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, heads, hd)
+    prompt = pkg.synthetic_prompt(9, 1, 24, w.vocab)
+    ids_ref, lg_ref = o.generate(prompt, 6)
+    with _decoder(w, heads, hd, precision) as m:
+        ids, lg = m.generate(prompt, 6)
+    _check_greedy(ids, lg, ids_ref, lg_ref, precision)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", [0, 1], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("heads,hd", [(2, 128), (4, 64)], ids=["hd128", "hd64"])
 def test_decoder_long_prefill(precision, heads, hd):
     """2 x 200 rows: the projections run the CTA-pair tiles (>= 256 rows) and
     the prefill attention spans two query and two key blocks of 128 (the
