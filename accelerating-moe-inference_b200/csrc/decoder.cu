@@ -152,6 +152,68 @@ rms_pack_kernel(const float* __restrict__ x, int src0, int stride, int T, int ro
     }
 }
 
+// Decode-sized batches (the GEMV path): one CTA per row instead of one warp,
+// so every x and w load of the row is issued at once (one memory round trip
+// instead of a lane's serial walk), and a block reduction of the sum of
+// squares; same expression (x * inv) * w.  Rows past T are not written (the
+// GEMV reads only T rows).
+constexpr int kPackThreads = 256;
+constexpr int kPackMaxVec = 8;   // float4 per thread: d <= 8192
+
+template <bool kTf>
+__global__ void __launch_bounds__(kPackThreads)
+rms_pack_row_kernel(const float* __restrict__ x, int src0, int stride, int d, float eps,
+                    const float* __restrict__ w, void* __restrict__ a_hi,
+                    void* __restrict__ a_lo, float4* __restrict__ zero, size_t zero_n4) {
+    __shared__ float s_part[kPackThreads / 32];
+    wait_predecessor_grid();   // dependent launch: x and the buffers below
+    launch_dependents();
+    const int r = blockIdx.x, tid = threadIdx.x;
+    for (size_t i = (size_t)r * kPackThreads + tid; i < zero_n4; i += (size_t)gridDim.x * kPackThreads)
+        zero[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(src0 + (size_t)r * stride) * d);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const int nv = d / 4;
+    float4 a[kPackMaxVec], g[kPackMaxVec];
+#pragma unroll
+    for (int i = 0; i < kPackMaxVec; ++i) {
+        const int v = tid + i * kPackThreads;
+        if (v < nv) {
+            a[i] = __ldcg(xr + v);   // written by the previous kernel: through L2
+            g[i] = __ldg(w4 + v);
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPackMaxVec; ++i) {
+        if (tid + i * kPackThreads < nv) {
+            ss = __fmaf_rn(a[i].x, a[i].x, ss);
+            ss = __fmaf_rn(a[i].y, a[i].y, ss);
+            ss = __fmaf_rn(a[i].z, a[i].z, ss);
+            ss = __fmaf_rn(a[i].w, a[i].w, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) s_part[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPackThreads / 32; ++i) tot += s_part[i];
+    const float inv = 1.0f / sqrtf(tot / (float)d + eps);
+#pragma unroll
+    for (int i = 0; i < kPackMaxVec; ++i) {
+        const int v = tid + i * kPackThreads;
+        if (v < nv) {
+            float4 o;
+            o.x = __fmul_rn(__fmul_rn(a[i].x, inv), g[i].x);
+            o.y = __fmul_rn(__fmul_rn(a[i].y, inv), g[i].y);
+            o.z = __fmul_rn(__fmul_rn(a[i].z, inv), g[i].z);
+            o.w = __fmul_rn(__fmul_rn(a[i].w, inv), g[i].w);
+            store_a4<kTf>(a_hi, a_lo, r, d, 4 * v, o);
+        }
+    }
+}
+
 // ------------------------------------------------------------ tile list
 // The grouped GEMM's tile list for a dense projection over T rows: one group
 // (expert 0), rows 0..T-1 in order, row r's output row r with weight 1;
@@ -830,23 +892,50 @@ attn_decode_partial_kernel(const float* __restrict__ qkv, const int* __restrict_
     }
 }
 
+constexpr int kAttnStagedChunks = 2048;   // 16 KB of staged maxima and sums
+
+// Chunk maxima and sums are staged in shared memory (one load round trip),
+// then every chunk's output value of this thread's dimension is loaded 16
+// chunks at a time before it is used; the sums run in chunk order.
 template <int HD, bool kTf>
 __global__ void __launch_bounds__(HD)
 attn_decode_combine_kernel(const float* __restrict__ part, const int* __restrict__ pos_dev, int H,
                            int nch, void* __restrict__ a_hi, void* __restrict__ a_lo) {
+    extern __shared__ float s_ml[];   // [nch] maxima, then [nch] sums
     const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     wait_predecessor_grid();   // dependent launch: the partials
     launch_dependents();
     const int used = (*pos_dev + kDecChunk) / kDecChunk;   // chunks holding keys 0..pos
     const float* base = part + ((size_t)b * H + h) * nch * (HD + 2);
+    // Staged when the launch gave shared memory for them (nch <= kAttnStagedChunks).
+    const bool staged = nch <= kAttnStagedChunks;
+    if (staged) {
+        for (int c = t; c < used; c += HD) {
+            s_ml[c] = base[(size_t)c * (HD + 2) + HD];
+            s_ml[nch + c] = base[(size_t)c * (HD + 2) + HD + 1];
+        }
+        __syncthreads();
+    }
+    auto mval = [&](int c) { return staged ? s_ml[c] : base[(size_t)c * (HD + 2) + HD]; };
+    auto lval = [&](int c) { return staged ? s_ml[nch + c] : base[(size_t)c * (HD + 2) + HD + 1]; };
     float M = -INFINITY;
-    for (int c = 0; c < used; ++c) M = fmaxf(M, base[(size_t)c * (HD + 2) + HD]);
+    for (int c = 0; c < used; ++c) M = fmaxf(M, mval(c));
     float L = 0.0f, o = 0.0f;
-    for (int c = 0; c < used; ++c) {
-        const float* pc = base + (size_t)c * (HD + 2);
-        const float w = expf(pc[HD] - M);
-        L = fmaf(w, pc[HD + 1], L);
-        o = fmaf(w, pc[t], o);
+    constexpr int kU = 16;
+    for (int c0 = 0; c0 < used; c0 += kU) {
+        float pv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            pv[u] = c0 + u < used ? base[(size_t)(c0 + u) * (HD + 2) + t] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int c = c0 + u;
+            if (c < used) {
+                const float w = expf(mval(c) - M);
+                L = fmaf(w, lval(c), L);
+                o = fmaf(w, pv[u], o);
+            }
+        }
     }
     store_a1<kTf>(a_hi, a_lo, b, H * HD, h * HD + t, o / L);
 }
@@ -868,10 +957,38 @@ argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ ids,
     const float* row = logits + (size_t)b * V;
     float best = -INFINITY;
     int bi = -1;
-    for (int v = tid; v < V; v += blockDim.x) {
-        const float x = row[v];
+    // Each thread scans its indices in ascending order (groups of 4, 8 groups
+    // loaded at once when the row is 16-byte aligned, then the tail), keeping
+    // the first index of its maximum.
+    auto see = [&](float x, int v) {
         if (x > best || (bi < 0 && x == best)) { best = x; bi = v; }
+    };
+    int v_tail = 0;
+    if ((V & 3) == 0) {
+        constexpr int kU = 8;
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        const int nv = V / 4;
+        for (int v0 = tid; v0 < nv; v0 += kU * blockDim.x) {
+            float4 q[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int v = v0 + u * blockDim.x;
+                if (v < nv) q[u] = row4[v];
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int v = v0 + u * blockDim.x;
+                if (v < nv) {
+                    see(q[u].x, 4 * v);
+                    see(q[u].y, 4 * v + 1);
+                    see(q[u].z, 4 * v + 2);
+                    see(q[u].w, 4 * v + 3);
+                }
+            }
+        }
+        v_tail = V;
     }
+    for (int v = v_tail + tid; v < V; v += blockDim.x) see(row[v], v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
@@ -1279,10 +1396,13 @@ cudaError_t launch_dense(MoeDecoder& m, const Dense& D, int T, float* y, bool ac
 // the GEMV reads only the T rows.
 cudaError_t launch_rms_pack(MoeDecoder& m, const float* x, int src0, int stride, int T,
                             const float* w, float* zero, size_t zero_n) {
-    const int rows_pad = use_gemv(m, T) ? T : round_up(T, 2 * kTileM);
-    const int grid = (rows_pad + 7) / 8;
     const float eps = m.cfg.rms_eps;
     float4* z = reinterpret_cast<float4*>(zero);
+    if (use_gemv(m, T) && m.d <= 4 * kPackThreads * kPackMaxVec)
+        return launch_pdl(m, dim3(T), dim3(kPackThreads), 0, rms_pack_row_kernel<false>, x, src0,
+                          stride, m.d, eps, w, m.a_hi, m.a_lo, z, zero_n / 4);
+    const int rows_pad = use_gemv(m, T) ? T : round_up(T, 2 * kTileM);
+    const int grid = (rows_pad + 7) / 8;
     if (tf_mode(m))
         return launch_pdl(m, dim3(grid), dim3(256), 0, rms_pack_kernel<true>, x, src0, stride, T,
                           rows_pad, m.d, eps, w, m.a_hi, m.a_lo, z, zero_n / 4);
@@ -1324,10 +1444,11 @@ cudaError_t launch_attention_t(MoeDecoder& m, int l, int B, int S, bool prefill)
                                    layer_kc(m, l), layer_vc(m, l), m.cfg.max_seq, scale, m.rope,
                                    m.attn_part, nch);
         if (e != cudaSuccess) return e;
+        const size_t smem = nch <= kAttnStagedChunks ? 2 * sizeof(float) * (size_t)nch : 0;
         if (tf_mode(m))
-            return launch_pdl(m, dim3(m.H, B), dim3(HD), 0, attn_decode_combine_kernel<HD, true>,
+            return launch_pdl(m, dim3(m.H, B), dim3(HD), smem, attn_decode_combine_kernel<HD, true>,
                               m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
-        return launch_pdl(m, dim3(m.H, B), dim3(HD), 0, attn_decode_combine_kernel<HD, false>,
+        return launch_pdl(m, dim3(m.H, B), dim3(HD), smem, attn_decode_combine_kernel<HD, false>,
                           m.attn_part, m.pos_dev, m.H, nch, m.a_hi, m.a_lo);
     }
     return cudaGetLastError();

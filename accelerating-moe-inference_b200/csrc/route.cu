@@ -118,12 +118,21 @@ __device__ __forceinline__ void select_experts(const float* l, int E, int k, int
         if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         sel[s] = bi;
     }
-    if (lane == 0) {
-        const double m = (double)l[sel[0]];
-        double p[kMaxTopK], sum = 0.0;
-        for (int s = 0; s < k; ++s) { p[s] = exp((double)l[sel[s]] - m); sum += p[s]; }
-        for (int s = 0; s < k; ++s) wsel[s] = (float)(p[s] / sum);
-    }
+    // Lane s < k computes p_s = e^(l_s - l_0) and its weight p_s / sum at
+    // the same time (one exp and one divide of latency instead of k); every
+    // lane adds the p_s in ascending s, the order a serial loop would use.
+    float ls = 0.0f;
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+        if (s < k && lane == s) ls = l[sel[s]];
+    const double m = (double)l[sel[0]];
+    const double p = lane < k ? exp((double)ls - m) : 0.0;
+    double sum = 0.0;
+    for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, p, s);
+    const float w = (float)(p / sum);
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+        if (s < k) wsel[s] = __shfl_sync(0xffffffffu, w, s);
 }
 
 // Thread layout: el = tid % 8 is the expert lane, tt = tid / 8 the token
