@@ -55,7 +55,7 @@ EXPORTED_SYMBOLS = (
     "moe_set_post_rms_norm", "moe_decoder_config_init", "moe_decoder_create",
     "moe_decoder_create_from_device", "moe_decoder_destroy", "moe_decoder_device_bytes",
     "moe_decoder_prefill", "moe_decoder_decode_step", "moe_decoder_generate",
-    "moe_decoder_last_timing",
+    "moe_decoder_last_timing", "moe_decoder_set_fused_step", "moe_decoder_fused_step_active",
 )
 PROFILE_STAGES = ("router", "dispatch_scan", "dispatch_permute", "gateup_gemm", "down_gemm",
                   "ep_exchange_in", "ep_exchange_out", "ep_combine")
@@ -178,6 +178,8 @@ def load_library(path: Optional[Path] = None) -> ctypes.CDLL:
     L.moe_decoder_generate.argtypes = [vp, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        ctypes.c_int32, _f32p, _i32p]
     L.moe_decoder_last_timing.argtypes = [vp, _f32p, _f32p]
+    L.moe_decoder_set_fused_step.argtypes = [vp, ctypes.c_int32]
+    L.moe_decoder_fused_step_active.argtypes = [vp]
     if path is None:
         _lib = L
     return L
@@ -764,6 +766,15 @@ class MoeDecoder:
             _fp(logits) if logits is not None else None, ids.ctypes.data_as(_i32p)))
         self._B = B
         return ids, logits
+
+    def set_fused_step(self, enable: bool):
+        """Batch-1 decode steps as one cooperative launch (True, the default
+        where the configuration allows it) or as the kernel chain (False)."""
+        _check(load_library().moe_decoder_set_fused_step(self._h, 1 if enable else 0))
+
+    @property
+    def fused_step_active(self) -> bool:
+        return bool(load_library().moe_decoder_fused_step_active(self._h))
 
     def last_timing(self):
         """(prefill_ms, decode_ms) of the last generate, CUDA events."""

@@ -33,13 +33,12 @@
 #include <string>
 #include <vector>
 
+#include "decode_step.h"
 #include "moe_internal.h"
 #include "ptx.cuh"
 
 namespace moe {
 namespace {
-
-constexpr int kDecErrToken = 1 << 12;   // a token id outside [0, vocab)
 
 // ------------------------------------------------------------ A-format stores
 // Columns c .. c+3 of row `row` of a [rows][ld] A operand: bf16 (kTf = false)
@@ -1218,6 +1217,14 @@ struct MoeDecoder {
     int g_B = -1, g_eos = 0, g_n = 0;
     float* g_logits = nullptr;
     int sm_count = 148;
+    // The fused batch-1 decode step (decode_step.cu): available when the
+    // configuration fits it (step_ok), used while step_on is set (off by
+    // default: on B200 the kernel chain measured faster).
+    bool step_ok = false, step_on = false;
+    moe::StepLayer* step_layers = nullptr;   // [n_layers], device
+    float* step_ws = nullptr;                // xm, router logits, h, part
+    unsigned* step_sync = nullptr;           // grid-barrier words [3]
+    size_t step_smem = 0;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {};
     float t_prefill = 0.0f, t_decode = 0.0f;
@@ -1484,6 +1491,15 @@ int run_layer(MoeDecoder& m, int l, int B, int T, int rps, bool prefill) {
     return MOE_OK;
 }
 
+// Greedy ids of the B logits rows (see run_head).
+int launch_argmax(MoeDecoder& m, int B, bool record, int step, const int* step_dev, int eos) {
+    argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, record ? m.seq_ids : nullptr,
+                                            m.cfg.max_seq, step, step_dev, eos,
+                                            record ? m.done : nullptr);
+    DEC_CUDA(cudaGetLastError());
+    return MOE_OK;
+}
+
 // Final norm of row src0 + b * stride (b < B), the output head into
 // m.logits, and the greedy ids; with `record`, also into seq_ids[b][step]
 // (step = *step_dev when step_dev is given) with the EOS bookkeeping.  Leaves
@@ -1495,11 +1511,7 @@ int run_head(MoeDecoder& m, int B, int src0, int stride, bool record, int step,
     DEC_CUDA(launch_rms_pack(m, m.x, src0, stride, B, m.final_norm, gemv ? nullptr : m.logits,
                              gemv ? 0 : (size_t)B * m.V));
     DEC_CUDA(launch_dense(m, m.head, B, m.logits, false));
-    argmax_kernel<<<B, 1024, 0, m.stream>>>(m.logits, m.V, m.next, record ? m.seq_ids : nullptr,
-                                            m.cfg.max_seq, step, step_dev, eos,
-                                            record ? m.done : nullptr);
-    DEC_CUDA(cudaGetLastError());
-    return MOE_OK;
+    return launch_argmax(m, B, record, step, step_dev, eos);
 }
 
 // Prefill of B sequences of S tokens from m.tok; the device counters then
@@ -1518,6 +1530,8 @@ int run_prefill(MoeDecoder& m, int B, int S, bool record, int eos) {
     return MOE_OK;
 }
 
+StepArgs step_args(MoeDecoder& m, const int* tok);
+
 // One decode step of the m.B sequences: token ids from `tok` (device, [B])
 // at the device position, which it advances.  Enqueues only -- the host's
 // m.pos is the caller's to advance -- so it can be captured as a graph.  With
@@ -1525,10 +1539,17 @@ int run_prefill(MoeDecoder& m, int B, int S, bool record, int eos) {
 // logits to save[b][step] ([B][n][V]).
 int run_decode(MoeDecoder& m, const int* tok, bool record, int eos, float* save, int n) {
     const int B = m.B;
-    embed_gather_kernel<<<B, 256, 0, m.stream>>>(tok, m.embed, m.V, m.d, m.x, m.dev_err);
-    DEC_CUDA(cudaGetLastError());
-    for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, B, 1, false));
-    DEC_RC(run_head(m, B, 0, 1, record, 0, m.step_dev, eos));
+    if (B == 1 && m.step_ok && m.step_on) {
+        // One sequence: the whole layer stack and the output head in one
+        // cooperative launch, then the greedy id.
+        DEC_CUDA(launch_step_fused(step_args(m, tok), m.HD, m.sm_count, m.step_smem, m.stream));
+        DEC_RC(launch_argmax(m, 1, record, 0, m.step_dev, eos));
+    } else {
+        embed_gather_kernel<<<B, 256, 0, m.stream>>>(tok, m.embed, m.V, m.d, m.x, m.dev_err);
+        DEC_CUDA(cudaGetLastError());
+        for (int l = 0; l < m.nl; ++l) DEC_RC(run_layer(m, l, B, B, 1, false));
+        DEC_RC(run_head(m, B, 0, 1, record, 0, m.step_dev, eos));
+    }
     if (save) {
         save_logits_kernel<<<dim3(std::max(1, std::min(m.V / 4 / 256, 64)), B), 256, 0, m.stream>>>(
             reinterpret_cast<const float4*>(m.logits), reinterpret_cast<float4*>(save),
@@ -1581,6 +1602,8 @@ int check_dev_err(MoeDecoder& m) {
     DEC_CUDA(cudaMemcpy(&flag, m.dev_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (!flag) return MOE_OK;
     cudaMemset(m.dev_err, 0, sizeof(int));
+    // A fused step that gave up left its barrier words mid-step.
+    if (m.step_sync) cudaMemset(m.step_sync, 0, 4 * sizeof(unsigned));
     if (flag & kDecErrToken) return report_error(MOE_ERR_INVALID, "a token id is outside [0, vocab)");
     char buf[96];
     std::snprintf(buf, sizeof buf, "a device-side wait timed out (flags 0x%x)", flag);
@@ -1604,6 +1627,96 @@ int validate(const MoeDecoderConfig& c) {
     return MOE_OK;
 }
 
+// The fused batch-1 decode step: available in BF16 precision when one
+// 512-thread CTA per SM fits the step's shared memory, every router expert
+// has a CTA of its own (E <= SMs) and the MoE blocks use the RMSNorm with
+// dense bf16 operands of row stride d.  Builds the per-layer operand table
+// and the step's workspace.
+int setup_fused_step(MoeDecoder& m) {
+    if (tf_mode(m) || m.d > 8192 || m.d % 128 != 0) return MOE_OK;
+    const Layer& L0 = m.moe[0]->L;
+    if (L0.E > m.sm_count || L0.E > kMaxExperts || L0.k > kMaxTopK || L0.k < 1) return MOE_OK;
+    for (int l = 0; l < m.nl; ++l) {
+        const Layer& L = m.moe[l]->L;
+        if (!L.norm_rms || !L.norm_w || !L.norm_b || !L.w13_hi || !L.w2_hi || L.ep) return MOE_OK;
+        if (m.qkv[l].L.ffp != m.d || m.wo[l].L.ffp != m.d) return MOE_OK;
+    }
+    if (m.head.L.ffp != m.d) return MOE_OK;
+    int coop = 0;
+    DEC_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m.cfg.device));
+    if (!coop) return MOE_OK;
+    const int nch = (m.cfg.max_seq + kDecChunk - 1) / kDecChunk;
+    const size_t smem = step_fused_smem(m.d, m.H, nch);
+    if (smem > 200 * 1024 || step_fused_occupancy(m.HD, smem) < 1) {
+        cudaGetLastError();
+        return MOE_OK;
+    }
+    std::vector<StepLayer> tab(m.nl);
+    for (int l = 0; l < m.nl; ++l) {
+        const Layer& L = m.moe[l]->L;
+        StepLayer& t = tab[l];
+        t.attn_norm = m.attn_norm[l];
+        t.wqkv = static_cast<const __nv_bfloat16*>(m.qkv[l].L.w2_hi);
+        t.wo = static_cast<const __nv_bfloat16*>(m.wo[l].L.w2_hi);
+        t.kc = layer_kc(m, l);
+        t.vc = layer_vc(m, l);
+        t.wg = L.wg;
+        t.bias = L.bias;
+        t.ffn_norm = L.norm_w;
+        t.ffn_norm_b = L.norm_b;
+        t.ffn_eps = L.norm_eps;
+        t.w13 = static_cast<const __nv_bfloat16*>(L.w13_hi);
+        t.w2 = static_cast<const __nv_bfloat16*>(L.w2_hi);
+    }
+    DEC_CUDA(dec_alloc(m, &m.step_layers, sizeof(StepLayer) * m.nl));
+    DEC_CUDA(cudaMemcpy(m.step_layers, tab.data(), sizeof(StepLayer) * m.nl, cudaMemcpyHostToDevice));
+    const size_t nk = (L0.ffp + kDownChunk - 1) / kDownChunk;
+    const size_t ws = (size_t)m.d + 256 + (size_t)L0.k * L0.ffp + nk * L0.k * m.d;
+    DEC_CUDA(dec_alloc(m, &m.step_ws, sizeof(float) * ws));
+    DEC_CUDA(dec_alloc(m, &m.step_sync, 4 * sizeof(unsigned)));
+    DEC_CUDA(cudaMemset(m.step_sync, 0, 4 * sizeof(unsigned)));
+    m.step_smem = smem;
+    m.step_ok = true;   // available; off until moe_decoder_set_fused_step enables it
+    return MOE_OK;
+}
+
+// The step's operands for token ids `tok` (device, one id).
+StepArgs step_args(MoeDecoder& m, const int* tok) {
+    const Layer& L0 = m.moe[0]->L;
+    StepArgs a{};
+    a.layers = m.step_layers;
+    a.nl = m.nl;
+    a.d = m.d;
+    a.H = m.H;
+    a.E = L0.E;
+    a.k = L0.k;
+    a.ffp = L0.ffp;
+    a.V = m.V;
+    a.max_seq = m.cfg.max_seq;
+    a.nch = (m.cfg.max_seq + kDecChunk - 1) / kDecChunk;
+    a.policy = L0.cfg.router_policy;
+    a.quantum = L0.cfg.router_quantum;
+    a.tie_eps = L0.cfg.router_tie_eps;
+    a.eps = m.cfg.rms_eps;
+    a.scale = 1.0f / sqrtf((float)m.HD);
+    a.tok = tok;
+    a.embed = m.embed;
+    a.final_norm = m.final_norm;
+    a.head = static_cast<const __nv_bfloat16*>(m.head.L.w2_hi);
+    a.rope = m.rope;
+    a.pos_dev = m.pos_dev;
+    a.qkv = m.qkvbuf;
+    a.attn_part = m.attn_part;
+    a.xm = m.step_ws;
+    a.logits_e = a.xm + m.d;
+    a.h = a.logits_e + 256;
+    a.part = a.h + (size_t)L0.k * L0.ffp;
+    a.logits = m.logits;
+    a.sync = m.step_sync;
+    a.err = m.dev_err;
+    return a;
+}
+
 void destroy(MoeDecoder* m) {
     if (!m) return;
     DecDeviceGuard guard(m->cfg.device);
@@ -1617,7 +1730,8 @@ void destroy(MoeDecoder* m) {
     void* bufs[] = {m->embed, m->final_norm, m->rope, m->kc, m->vc, m->x, m->x2, m->qkvbuf,
                     m->logits, m->gen_logits, m->tok, m->next, m->seq_ids, m->done, m->a_hi,
                     m->a_lo, m->mtiles, m->ptiles, m->num_mtiles, m->num_ptiles, m->row_token,
-                    m->row_weight, m->dev_err, m->pos_dev, m->step_dev, m->attn_part};
+                    m->row_weight, m->dev_err, m->pos_dev, m->step_dev, m->attn_part,
+                    m->step_layers, m->step_ws, m->step_sync};
     for (void* p : bufs)
         if (p) cudaFree(p);
     for (cudaEvent_t e : m->ev)
@@ -1763,6 +1877,7 @@ int create(const MoeDecoderConfig* cfg, const MoeDecoderWeights* w, bool device_
         DEC_RC(moe_set_post_rms_norm(M.moe[l], w->ffn_norm[l], cfg->rms_eps));
         M.bytes += moe_device_bytes(M.moe[l]);
     }
+    DEC_RC(setup_fused_step(M));
     DEC_CUDA(cudaDeviceSynchronize());
     *out = m.release();
     return MOE_OK;
@@ -1863,6 +1978,24 @@ int moe_decoder_last_timing(const MoeDecoder* m, float* prefill_ms, float* decod
     if (decode_ms) *decode_ms = m->t_decode;
     return MOE_OK;
 }
+
+int moe_decoder_set_fused_step(MoeDecoder* m, int32_t enable) {
+    using namespace moe;
+    if (!m) return report_error(MOE_ERR_INVALID, "null decoder");
+    if (enable && !m->step_ok)
+        return report_error(MOE_ERR_UNSUPPORTED,
+                            "the fused decode step needs BF16 precision, experts <= SMs and "
+                            "d_model <= 8192");
+    if ((enable != 0) != m->step_on) {
+        DecDeviceGuard guard(m->cfg.device);
+        cudaStreamSynchronize(m->stream);
+        drop_graph(*m);   // the captured step holds the other path
+        m->step_on = enable != 0;
+    }
+    return MOE_OK;
+}
+
+int moe_decoder_fused_step_active(const MoeDecoder* m) { return m && m->step_ok && m->step_on ? 1 : 0; }
 
 }  // extern "C"
 

@@ -360,6 +360,10 @@ def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=Fa
     c = dict(C4)
     if new_tokens:
         c["new"] = new_tokens
+    if getattr(args, "decoder_layers", None):
+        c["n_layers"] = args.decoder_layers
+    if getattr(args, "decoder_batches", None):
+        c["batches"] = tuple(int(b) for b in args.decoder_batches.split(","))
     d, L, E, ff, V, k = c["d"], c["n_layers"], c["E"], c["ff"], c["vocab"], c["k"]
     gen = torch.Generator(device="cuda").manual_seed(c["seed"])
     rnd = lambda *s: torch.randn(*s, generator=gen, device=dev).mul_(0.02)  # noqa: E731
@@ -436,6 +440,20 @@ def run_decoder(args, pkg, dev, reps: int = 2, new_tokens=None, profile_range=Fa
             "ids_valid": bool(((ids >= 0) & (ids < V)).all()),
             "logits_finite": bool(np.isfinite(lbuf).all()),
         }
+        if B == 1:
+            # The fused batch-1 step (one cooperative launch per decode
+            # step; off by default), for comparison with the chain above.
+            try:
+                m.set_fused_step(True)
+            except pkg.MoeError:
+                pass
+            if m.fused_step_active:
+                m.generate(p, c["new"], logits_out=lbuf)
+                m.generate(p, c["new"], logits_out=lbuf)
+                fused = m.last_timing()[1] / steps
+                m.set_fused_step(False)
+                out[str(B)]["fused_decode_ms_per_step"] = fused
+                out[str(B)]["fused_decode_frac_of_hbm"] = step_bytes / (fused / 1e3) / 1e9 / hbm
     m.close()
     return {"workload": c["workload"], "n_layers": L, "d_model": d, "heads": c["heads"],
             "head_dim": c["hd"], "vocab": V, "experts": E, "top_k": k, "d_ff": ff,
@@ -455,7 +473,7 @@ def decoder_only(args):
     dev = torch.device("cuda", 0)
     dec = run_decoder(args, pkg, dev, reps=max(1, args.steps // 25),
                       new_tokens=args.decoder_new_tokens, profile_range=args.profile_range)
-    b16 = dec["by_batch"][str(max(C4["batches"]))]
+    b16 = dec["by_batch"][max(dec["by_batch"], key=int)]
     print(json.dumps({
         "metric": "toy MoE decoder tokens/s (BASELINE config 4)", "value": b16["decode_tokens_per_s"],
         "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True,
@@ -815,7 +833,9 @@ def run_single(args, wl, pkg, world, rank, local):
             f"batch{b}": {"decode_ms_per_step": round(v["decode_ms_per_step"], 4),
                           "decode_tokens_per_s": round(v["decode_tokens_per_s"], 1),
                           "decode_frac_of_hbm": round(v["decode_frac_of_hbm"], 3),
-                          "prefill_ms": round(v["prefill_ms"], 3)}
+                          "prefill_ms": round(v["prefill_ms"], 3),
+                          **({"fused_decode_frac_of_hbm": round(v["fused_decode_frac_of_hbm"], 3)}
+                             if "fused_decode_frac_of_hbm" in v else {})}
             for b, v in decoder["by_batch"].items()}
     line = {
         "metric": METRIC, "value": world * T / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
@@ -880,6 +900,10 @@ def main():
                     help="skip the toy MoE decoder section (BASELINE config 4)")
     ap.add_argument("--decoder-new-tokens", type=int, default=None,
                     help="generated tokens per sequence in the decoder section (default 128)")
+    ap.add_argument("--decoder-layers", type=int, default=None,
+                    help="decoder layers (default 8; fewer for a small profiling case)")
+    ap.add_argument("--decoder-batches", default=None,
+                    help="comma-separated decoder batch sizes (default 1,16)")
     ap.add_argument("--profile-range", action="store_true",
                     help="bracket one decoder generate per batch with cudaProfilerStart/Stop "
                          "(for ncu --profile-from-start off)")

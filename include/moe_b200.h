@@ -473,6 +473,19 @@ int moe_decoder_generate(MoeDecoder* m, const int32_t* prompt, int32_t B, int32_
  * moe_decoder_generate: the prefill (through the first token's argmax) and
  * all decode steps. */
 int moe_decoder_last_timing(const MoeDecoder* m, float* prefill_ms, float* decode_ms);
+/* Fused batch-1 decode step (no counterpart in the reference, whose
+ * generate_decode re-runs the whole prefix per token, src/model.cu:2061-2104):
+ * with one sequence in BF16 precision a decode step can run as ONE
+ * cooperative launch over every layer and the output head, grid-wide
+ * barriers between its phases, instead of about ten kernels per layer; its
+ * logits are bit-identical to the kernel chain's.  Off by default (at config
+ * 4 the chain measured 0.74 ms per step, the fused step 0.99 ms).
+ * enable = 1 selects the fused step, 0 the chain; MOE_ERR_UNSUPPORTED when
+ * enabling a configuration it does not cover (FP32 precision, more experts
+ * than SMs, d_model > 8192). */
+int moe_decoder_set_fused_step(MoeDecoder* m, int32_t enable);
+/* 1 if batch-1 decode steps run the fused step, else 0 (or a null m). */
+int moe_decoder_fused_step_active(const MoeDecoder* m);
 
 #ifdef __cplusplus
 }

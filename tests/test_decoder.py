@@ -351,3 +351,76 @@ def test_decoder_at_config4_shapes(config4_case, precision):
         ids, lgg = m.generate(prompt, 3)
     assert rel_l2(lg, lg_ref[:, 0]) <= TOL[precision], rel_l2(lg, lg_ref[:, 0])
     _check_greedy(ids, lgg, ids_ref, lg_ref, precision)
+
+
+# ---------------------------------------------------------------- fused batch-1 step
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,hd", [(2, 128), (4, 64)], ids=["hd128", "hd64"])
+def test_fused_batch1_step_is_bit_identical_to_the_kernel_chain(heads, hd):
+    """One sequence in BF16: with the fused step enabled the decode steps run
+    as one cooperative launch; the kernel chain (the default) must give the
+    same ids and bit-identical logits (every phase evaluates the chain's expressions in
+    the chain's order), and both follow the oracle."""
+    pkg = load_pkg()
+    w = _weights()
+    o = _oracle(w, heads, hd)
+    prompt = pkg.synthetic_prompt(11, 1, 30, w.vocab)
+    ids_ref, lg_ref = o.generate(prompt, 8)
+    with _decoder(w, heads, hd, 1) as m:
+        assert not m.fused_step_active
+        m.set_fused_step(True)
+        assert m.fused_step_active
+        ids_f, lg_f = m.generate(prompt, 8)
+        m.set_fused_step(False)
+        assert not m.fused_step_active
+        ids_c, lg_c = m.generate(prompt, 8)
+        m.set_fused_step(True)
+        ids_f2, lg_f2 = m.generate(prompt, 8)
+    assert np.array_equal(ids_f, ids_c)
+    assert np.array_equal(lg_f, lg_c)
+    assert np.array_equal(lg_f2, lg_f)
+    _check_greedy(ids_f, lg_f, ids_ref, lg_ref, 1)
+
+
+@pytest.mark.gpu
+def test_fused_step_serves_the_step_api_and_is_refused_in_fp32():
+    pkg = load_pkg()
+    w = _weights()
+    prompt = pkg.synthetic_prompt(12, 1, 20, w.vocab)
+    with _decoder(w, 2, 128, 1) as m:
+        m.set_fused_step(True)
+        ids, lg = m.generate(prompt, 4)
+        l0, n0 = m.prefill(prompt)
+        steps = [(l0, n0)]
+        for _ in range(3):
+            steps.append(m.decode_step(steps[-1][1]))
+    for t, (lt, nt) in enumerate(steps):
+        assert np.array_equal(lt, lg[:, t])
+        assert np.array_equal(nt, ids[:, t])
+    with _decoder(w, 2, 128, 0) as m:
+        assert not m.fused_step_active
+        with pytest.raises(pkg.MoeError) as ei:
+            m.set_fused_step(True)
+        assert "BF16" in str(ei.value)
+        m.set_fused_step(False)
+
+
+@pytest.mark.gpu
+def test_fused_batch1_step_at_config4_shapes(config4_case):
+    """Config-4 layer shapes (d 2048, 16 heads, 16 experts of 5632, vocab
+    32000), 2 layers, one sequence: the fused step against the kernel chain
+    (bit-identical) and against the oracle.  The prompt has 72 tokens: a
+    prefill of at most 64 rows splits the projections' K with atomic adds,
+    which would make the two runs' KV caches differ in the last bits."""
+    pkg = load_pkg()
+    w = config4_case[0]
+    prompt = pkg.synthetic_prompt(13, 1, 72, w.vocab)
+    ids_ref, lg_ref = _oracle(w, 16, 128).generate(prompt, 3)
+    with _decoder(w, 16, 128, 1, max_batch=1, max_seq=80) as m:
+        m.set_fused_step(True)
+        ids_f, lg_f = m.generate(prompt, 3)
+        m.set_fused_step(False)
+        ids_c, lg_c = m.generate(prompt, 3)
+    assert np.array_equal(ids_f, ids_c)
+    assert np.array_equal(lg_f, lg_c)
+    _check_greedy(ids_f, lg_f, ids_ref, lg_ref, 1)
