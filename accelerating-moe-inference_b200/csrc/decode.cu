@@ -140,10 +140,9 @@ __device__ __forceinline__ void stream_dots(const WT* const (&w)[R], const AT* c
                                             int gm, int k_begin, int k_end, int lane,
                                             float (&acc)[R][TM]) {
     constexpr int V = Vec<WT>::N;
-    // 16-byte loads in flight per lane: 16 over the R rows, fewer when more
-    // token rows share the registers.
-    constexpr int kLoads = V * TM >= 32 ? 4 : (V * TM >= 16 ? 8 : 16);
-    constexpr int kInFlight = kLoads / R > 0 ? kLoads / R : 1;
+    // 16-byte loads per weight row in flight per lane: more when fewer token
+    // rows share the registers.
+    constexpr int kInFlight = V * TM >= 32 ? 1 : (V * TM >= 16 ? 2 : 4);
     for (int k0 = k_begin + lane * V; k0 < k_end; k0 += 32 * V * kInFlight) {
         typename Vec<WT>::Raw raw[kInFlight][R];
 #pragma unroll
@@ -203,27 +202,17 @@ decode_gateup_kernel(const AT* __restrict__ a_rows, const WT* __restrict__ w13, 
     const long long total = (long long)A.n * ffp;          // (expert, column) pairs
     long long j = total * gw / W;
     const long long j_end = total * (gw + 1) / W;
-    // One column (its gate and up rows) per pass for a single token: all of
-    // a lane's 16 loads are in flight on it and warps differ by at most one
-    // column; two columns per pass when several tokens share the weights.
-    constexpr int kCols = TM == 1 ? 1 : 2;
-    constexpr int R = 2 * kCols;
     while (j < j_end) {
         const int ai = (int)(j / ffp);
         const int e = A.act[ai];
         const int c = (int)(j % ffp);
         // Two columns when both are in range and in the same expert.
-        const int nc = (kCols == 2 && j + 1 < j_end && c + 1 < ffp) ? 2 : 1;
+        const int nc = (j + 1 < j_end && c + 1 < ffp) ? 2 : 1;
         const size_t base = (size_t)e * 2 * ffp;
         const size_t rg0 = (size_t)(c / kFfBlock) * (2 * kFfBlock) + (c % kFfBlock);
         const size_t rg1 = (size_t)((c + nc - 1) / kFfBlock) * (2 * kFfBlock) + ((c + nc - 1) % kFfBlock);
-        const WT* w[R];
-        w[0] = w13 + (base + rg0) * d;
-        w[1] = w13 + (base + rg0 + kFfBlock) * d;
-        if constexpr (kCols == 2) {
-            w[2] = w13 + (base + rg1) * d;
-            w[3] = w13 + (base + rg1 + kFfBlock) * d;
-        }
+        const WT* const w[4] = {w13 + (base + rg0) * d, w13 + (base + rg0 + kFfBlock) * d,
+                                w13 + (base + rg1) * d, w13 + (base + rg1 + kFfBlock) * d};
         const int n_e = counts[e];
         const int r0 = eoff[e];
         for (int g0 = 0; g0 < n_e; g0 += TM) {
@@ -231,20 +220,21 @@ decode_gateup_kernel(const AT* __restrict__ a_rows, const WT* __restrict__ w13, 
             const AT* a[TM];
 #pragma unroll
             for (int m = 0; m < TM; ++m) a[m] = a_rows + (size_t)(r0 + g0 + min(m, gm - 1)) * d;
-            float acc[R][TM];
+            float acc[4][TM];
 #pragma unroll
-            for (int r = 0; r < R; ++r)
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
                 for (int m = 0; m < TM; ++m) acc[r][m] = 0.0f;
-            stream_dots<WT, AT, R, TM>(w, a, gm, 0, d, lane, acc);
+            stream_dots<WT, AT, 4, TM>(w, a, gm, 0, d, lane, acc);
 #pragma unroll
             for (int m = 0; m < TM; ++m) {
                 if (m >= gm) break;
-#pragma unroll
-                for (int cc = 0; cc < kCols; ++cc) {
-                    const float gv = warp_sum(acc[2 * cc][m]), uv = warp_sum(acc[2 * cc + 1][m]);
-                    if (lane == 0 && cc < nc)
-                        h[(size_t)(A.coff[e] + g0 + m) * ffp + c + cc] = gv / (1.0f + __expf(-gv)) * uv;
+                const float g0v = warp_sum(acc[0][m]), u0v = warp_sum(acc[1][m]);
+                const float g1v = warp_sum(acc[2][m]), u1v = warp_sum(acc[3][m]);
+                if (lane == 0) {
+                    float* hr = h + (size_t)(A.coff[e] + g0 + m) * ffp + c;
+                    hr[0] = g0v / (1.0f + __expf(-g0v)) * u0v;
+                    if (nc == 2) hr[1] = g1v / (1.0f + __expf(-g1v)) * u1v;
                 }
             }
         }
@@ -266,22 +256,18 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
     // work item's weight rows are prefetched into L2, while decode_gateup is
     // still streaming.  h (decode_gateup's output) is read after the wait.
     build_active(A, counts, E);
-    // Items: (expert, kCols output columns, K chunk); two columns for a
-    // single token (finer items: warps differ by less), four when several
-    // tokens share each weight load.
-    constexpr int kCols = TM == 1 ? 2 : 4;
     const int lane = threadIdx.x & 31;
-    const int nq = (d + kCols - 1) / kCols;        // column groups per expert
+    const int nq = (d + 3) / 4;                    // column quads per expert
     const int nk = (ffp + kDownChunk - 1) / kDownChunk;
     const long long W = (long long)gridDim.x * kDecWarps;
     const long long gw = (long long)blockIdx.x * kDecWarps + (threadIdx.x >> 5);
     const long long total = (long long)A.n * nq * nk;
     {
         const long long it = total * gw / W;
-        if (lane < kCols && it < total * (gw + 1) / W) {
+        if (lane < 4 && it < total * (gw + 1) / W) {
             const int e = A.act[(int)(it / ((long long)nq * nk))];
             const int rem = (int)(it % ((long long)nq * nk));
-            const int n = min((rem / nk) * kCols + lane, d - 1);
+            const int n = min((rem / nk) * 4 + lane, d - 1);
             const int k0 = (rem % nk) * kDownChunk;
             const int k1 = min(ffp, k0 + kDownChunk);
             prefetch_l2_bulk(w2 + ((size_t)e * d + n) * ffp + k0, (uint32_t)((k1 - k0) * sizeof(WT)));
@@ -293,12 +279,13 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
         const int ai = (int)(it / ((long long)nq * nk));
         const int rem = (int)(it % ((long long)nq * nk));
         const int e = A.act[ai];
-        const int n0 = (rem / nk) * kCols;
+        const int n0 = (rem / nk) * 4;
         const int k0 = (rem % nk) * kDownChunk;
         const int k1 = min(ffp, k0 + kDownChunk);
-        const WT* w[kCols];
-#pragma unroll
-        for (int r = 0; r < kCols; ++r) w[r] = w2 + ((size_t)e * d + min(n0 + r, d - 1)) * ffp;
+        const WT* const w[4] = {w2 + ((size_t)e * d + min(n0, d - 1)) * ffp,
+                                w2 + ((size_t)e * d + min(n0 + 1, d - 1)) * ffp,
+                                w2 + ((size_t)e * d + min(n0 + 2, d - 1)) * ffp,
+                                w2 + ((size_t)e * d + min(n0 + 3, d - 1)) * ffp};
         const int n_e = counts[e];
         const int r0 = eoff[e];
         for (int g0 = 0; g0 < n_e; g0 += TM) {
@@ -307,12 +294,12 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
 #pragma unroll
             for (int m = 0; m < TM; ++m)
                 a[m] = h + (size_t)(A.coff[e] + g0 + min(m, gm - 1)) * ffp;
-            float acc[kCols][TM];
+            float acc[4][TM];
 #pragma unroll
-            for (int r = 0; r < kCols; ++r)
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
                 for (int m = 0; m < TM; ++m) acc[r][m] = 0.0f;
-            stream_dots<WT, float, kCols, TM>(w, a, gm, k0, k1, lane, acc);
+            stream_dots<WT, float, 4, TM>(w, a, gm, k0, k1, lane, acc);
 #pragma unroll
             for (int m = 0; m < TM; ++m) {
                 if (m >= gm) break;
@@ -320,7 +307,7 @@ decode_down_kernel(const float* __restrict__ h, const WT* __restrict__ w2, int d
                 float* dst = part + (size_t)(k0 / kDownChunk) * split_stride +
                              (size_t)row_slot[prow] * d + n0;
 #pragma unroll
-                for (int r = 0; r < kCols; ++r) {
+                for (int r = 0; r < 4; ++r) {
                     const float v = warp_sum(acc[r][m]);
                     if (lane == r && n0 + r < d) dst[r] = v;
                 }
