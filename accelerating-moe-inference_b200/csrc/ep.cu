@@ -944,7 +944,20 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     }
     if (e != cudaSuccess) return report_error(MOE_ERR_CUDA, cudaGetErrorString(e));
     // The receiving side runs the grouped GEMMs on up to world * T tokens' rows.
-    return ensure_workspace(L, capT * G);
+    if (int rc = ensure_workspace(L, capT * G)) return rc;
+    // No rank leaves setup before every rank has mapped its peers' buffers:
+    // at 8 ranks the 35 IPC mappings per rank took long enough for ranks to
+    // leave seconds apart, and a first step that follows at once then ran out
+    // its bounded peer wait on the ranks that were early.
+    char* d_sync = nullptr;
+    e = cudaMalloc(&d_sync, 16 * (size_t)(G + 1));
+    if (e != cudaSuccess) return report_error(MOE_ERR_OOM, cudaGetErrorString(e));
+    nr = g_nccl.AllGather(d_sync, d_sync + 16, 16, ncclUint8, S.comm, s);
+    const cudaError_t se = nr == ncclSuccess ? cudaStreamSynchronize(s) : cudaSuccess;
+    cudaFree(d_sync);
+    if (nr != ncclSuccess) return nccl_fail(nr, "setup barrier");
+    if (se != cudaSuccess) return report_error(MOE_ERR_CUDA, cudaGetErrorString(se));
+    return MOE_OK;
 }
 
 // MOE_ERR_TIMEOUT once the group has failed: a completed copy of the device

@@ -281,7 +281,8 @@ def _gpu_rank(rank, world, idbytes, q, precision, transport, k=K):
                                          w1=layer.w1, w3=layer.w3, w2=layer.w2,
                                          bias=layer.router_bias, top_k=k, policy=1,
                                          precision=precision, device=rank,
-                                         ep_transport=transport, max_tokens=64)
+                                         ep_transport=transport,
+                                         max_tokens=T_LOCAL + 5 * (world - 1))
         xd = torch.from_numpy(x).cuda()
         yd = torch.empty_like(xd)
         ys = []
