@@ -945,10 +945,10 @@ int ep_p2p_setup(Layer& L, int capT, cudaStream_t s) {
     if (e != cudaSuccess) return report_error(MOE_ERR_CUDA, cudaGetErrorString(e));
     // The receiving side runs the grouped GEMMs on up to world * T tokens' rows.
     if (int rc = ensure_workspace(L, capT * G)) return rc;
-    // No rank leaves setup before every rank has mapped its peers' buffers:
-    // at 8 ranks the 35 IPC mappings per rank took long enough for ranks to
-    // leave seconds apart, and a first step that follows at once then ran out
-    // its bounded peer wait on the ranks that were early.
+    // No rank leaves setup before every rank has mapped its peers' buffers
+    // (5 per peer; ranks take different times over them), so a first step
+    // that follows creation at once does not spend its bounded peer wait on
+    // a rank still mapping.
     char* d_sync = nullptr;
     e = cudaMalloc(&d_sync, 16 * (size_t)(G + 1));
     if (e != cudaSuccess) return report_error(MOE_ERR_OOM, cudaGetErrorString(e));
